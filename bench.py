@@ -1,0 +1,378 @@
+"""Benchmark of the hot path: decode steps of the 64-layer FP8 model (BASELINE config 3 shape).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch 256]
+
+One step = one decode token for each of `--batch` rows through all 64 layers (48 gated-delta + 16
+attention) plus the lm_head group-of-32 maxima, rows at positions spread over [0, 511) of a
+512-position context, each advancing one position per step (a row reaching 511 restarts at 0 as a
+new sequence, as the reference's batched loop refills rows). N GPUs run tensor parallel (TP = N,
+heads and vocabulary sliced, row-parallel outputs summed): the total work is fixed, so scaling is
+"strong". Weights are seeded random FP8 of the real architecture; cache and recurrent-state contents
+are seeded random values (the bytes moved are the same as a real prompt's).
+
+The JSON line's `value` is tokens/s with the step inputs already on the device; `e2e` is the same
+through the reference-facing calls (B200Step(**host tensors) -> host hidden, B200Head.run_graph ->
+host maxima), host<->device copies included. `--impl reference` times the CPU oracle (the reference's
+CPU path restated) on this host's cores on a bounded sample: one 4-layer block per step at the same
+batch, scaled to 64 layers.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import platform
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+PACKAGE = "qwen38-27b-aws_b200"
+METRIC = "total tokens/s (64-layer decode step incl. lm_head maxima)"
+MAX_SEQ = 512
+LAYERS = 64
+
+
+def peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return float(json.loads(path.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """nvidia-smi samples during the timed region (clocks and throttle reasons)."""
+
+    FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def max_over_ranks(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ------------------------------------------------------------------------------------------------
+def run_ours(args, world, rank, local):
+    pkg = importlib.import_module(PACKAGE)
+    step_mod = importlib.import_module(f"{PACKAGE}.step")
+    ops = importlib.import_module(f"{PACKAGE}.ops")
+    device = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(device)
+    if world > 1:
+        torch.distributed.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=300))
+    cfg = pkg.config.full_config(num_blocks=LAYERS // 4)
+    B = args.batch
+
+    t0 = time.time()
+    step = step_mod.B200Step(cfg, lambda i: pkg.weights.synthetic_layer(cfg, i, seed=0, device=device), MAX_SEQ, B,
+                             tp_degree=world, rank=rank, device=device)
+    head = step_mod.B200Head(cfg, pkg.weights.synthetic_head(cfg, seed=0, device=device), B, tp_degree=world, rank=rank,
+                             device=device)
+    torch.cuda.synchronize()
+    build_s = time.time() - t0
+
+    # Seeded cache and state contents.
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1234 + rank)
+    for l in step.layers:
+        if l.kind == pkg.config.LINEAR:
+            l.mixer.state.normal_(0.0, 0.1, generator=gen)
+            l.mixer.conv_state.normal_(0.0, 1.0, generator=gen)
+        else:
+            l.mixer.k_cache.normal_(0.0, 1.0, generator=gen)
+            l.mixer.v_cache.normal_(0.0, 1.0, generator=gen)
+
+    # Step inputs for every warm-up and timed step, made up front (host and device copies).
+    total = args.warmup + args.steps
+    g_cpu = torch.Generator().manual_seed(99)
+    pos0 = torch.randint(0, MAX_SEQ - 1, (B,), generator=g_cpu)
+    positions = torch.stack([(pos0 + s) % (MAX_SEQ - 1) for s in range(total)]).to(torch.int32)
+    embeds = (torch.randn(total, B, cfg.hidden_size, generator=g_cpu) * 0.02).to(torch.bfloat16)
+    om_rot = lambda p: rotary(cfg, p)  # noqa: E731
+    cs = [om_rot(positions[s]) for s in range(total)]
+    host = [dict(inputs_embeds=embeds[s].reshape(B, 1, -1).pin_memory(), cos=cs[s][0].unsqueeze(1).pin_memory(),
+                 sin=cs[s][1].unsqueeze(1).pin_memory(), position=positions[s].pin_memory(),
+                 active=torch.ones(B).pin_memory()) for s in range(total)]
+    dev_inputs = [{k: v.to(device) for k, v in h.items()} for h in host]
+
+    def device_step(s):
+        d = dev_inputs[s]
+        step.load_decode_inputs(d["inputs_embeds"], d["cos"], d["sin"], d["position"], d["active"])
+        hidden = step.decode_device()
+        head.hidden.copy_(hidden)
+        return head.maxima_device()
+
+    # Warm-up (also captures the decode graph).
+    for s in range(args.warmup):
+        device_step(s)
+    torch.cuda.synchronize()
+
+    # L2 note: every step streams ~24 GB of weights and ~40 GB of state, far above the 126 MB L2.
+    sampler = ClockSampler(local)
+    sampler.start()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for s in range(args.warmup, total):
+        device_step(s)
+    end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    dev_ms = max_over_ranks(start.elapsed_time(end), world, device)
+    clocks = sampler.stop()
+
+    # End to end through the reference-facing calls, host tensors in and out.
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    e_start.record()
+    for s in range(args.warmup, total):
+        hidden = step(**host[s])
+        head.run_graph(hidden)
+    e_end.record()
+    torch.cuda.synchronize()
+    wall_e2e = time.perf_counter() - w0
+    e2e_ms = max_over_ranks(max(e_start.elapsed_time(e_end), wall_e2e * 1e3), world, device)
+    h2d = sum(v.numel() * v.element_size() for v in host[0].values()) + B * cfg.hidden_size * 2
+    d2h = B * cfg.hidden_size * 2 + B * (cfg.vocab_size // 32) * 4
+
+    # Roofline of the dominant kernel (gdn_decode): each launch moves the state tiles in and out,
+    # the conv state in and out, and reads its qkvz/ab rows and writes the e5m2 output.
+    gdn_ms = time_gdn_launches(step, ops, pkg, repeats=3)
+    hv = cfg.linear_num_value_heads // world
+    per_launch = (B * hv * cfg.linear_key_head_dim * cfg.linear_value_head_dim * 2 * 2
+                  + B * (cfg.linear_conv_dim // world) * 3 * 2 * 2
+                  + B * ((cfg.linear_conv_dim + cfg.linear_value_dim) // world + 2 * hv) * 2
+                  + B * (cfg.linear_value_dim // world))
+    peak, peak_kind = peaks()
+    achieved = per_launch / (gdn_ms * 1e-3) / 1e9
+
+    tokens = B * args.steps
+    line = {
+        "metric": METRIC,
+        "value": tokens / (dev_ms / 1e3),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": dev_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "fp8(e4m3 weights x e5m2 activations)+bf16",
+        "data": "synthetic (seeded random FP8 weights of the architecture, random cache/state contents)",
+        "config": {
+            "workload": "BASELINE config 3: 64-layer decode step, batch %d, 512-position context, rows at positions spread over [0,511)" % B,
+            "global_batch": B,
+            "seq_len": MAX_SEQ,
+            "parallelism": f"tp{world}",
+            "l2": "inputs larger than L2 (24 GB weights + ~40 GB state streamed per step)",
+        },
+        "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "roofline": {
+            "kernel": "gdn_decode",
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": peak,
+            "peak_kind": peak_kind,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": None,
+            "bytes_per_launch": per_launch,
+            "launch_ms": gdn_ms,
+        },
+        "clocks": clocks,
+        "gpu_launches": (step.kernels_per_decode_step() + 2) * args.steps,
+        "build_s": round(build_s, 1),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(cfg, pkg, B, samples=1)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del step, head
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def time_gdn_launches(step, ops, pkg, repeats: int) -> float:
+    """Average duration of the step's gdn_decode launches, each bracketed by CUDA events on the
+    launching stream, replayed eagerly over the 48 layers' own states right after the timed region."""
+    cfg, tp = step.cfg, step.tp
+    durations = []
+    stream = torch.cuda.current_stream()
+    for _ in range(repeats):
+        for l in step.layers:
+            if l.kind != pkg.config.LINEAR:
+                continue
+            m = l.mixer
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            ops.gdn_decode(step.proj, step.ab, m.conv_state, m.conv_w, m.a_log, m.dt_bias, m.norm_w, m.state,
+                           step.position, step.active, step.mix_gdn, batch=step.batch,
+                           num_k_heads=cfg.linear_num_key_heads // tp, num_v_heads=cfg.linear_num_value_heads // tp,
+                           head_k=cfg.linear_key_head_dim, head_v=cfg.linear_value_head_dim, eps=cfg.rms_norm_eps)
+            b.record(stream)
+            durations.append((a, b))
+    torch.cuda.synchronize()
+    times = [a.elapsed_time(b) for a, b in durations]
+    return sum(times) / len(times)
+
+
+def rotary(cfg, positions):
+    dim = cfg.rotary_dim
+    inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, dim, 2, dtype=torch.float32) / dim))
+    f = positions.float().unsqueeze(-1) * inv
+    return f.cos().repeat(1, 2).to(torch.bfloat16), f.sin().repeat(1, 2).to(torch.bfloat16)
+
+
+# ------------------------------------------------------------------------------------------------
+def cpu_block_step(cfg, pkg, batch: int):
+    """A CPU oracle for one full-width 4-layer block (the bounded sample), and a function running one
+    decode step of it."""
+    from oracle import cpu_model as om
+
+    w = {}
+    for i in range(4):
+        w |= pkg.weights.synthetic_layer(cfg, i, seed=0, device="cpu")
+    block = pkg.config.block_config(cfg, 4)
+    st = om.OracleStep(block, w, MAX_SEQ, batch)
+    gen = torch.Generator().manual_seed(5)
+    for kind, mixer, *_ in st.layers:
+        if kind == om.LINEAR:
+            mixer.recurrent_state.normal_(0.0, 0.1, generator=gen)
+        else:
+            mixer.k_cache.normal_(0.0, 1.0, generator=gen)
+            mixer.v_cache.normal_(0.0, 1.0, generator=gen)
+    pos = torch.randint(0, MAX_SEQ - 2, (batch,), generator=gen, dtype=torch.int32)
+    cos, sin = om.rotary(cfg, pos, torch.bfloat16)
+    x = (torch.randn(batch, 1, cfg.hidden_size, generator=gen) * 0.02).to(torch.bfloat16)
+    inputs = dict(cos=cos.unsqueeze(1), sin=sin.unsqueeze(1), position=pos, active=torch.ones(batch))
+    return lambda: st(inputs_embeds=x, **inputs)
+
+
+def cpu_baseline(cfg, pkg, batch: int, samples: int) -> dict:
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    run = cpu_block_step(cfg, pkg, batch)
+    run()  # dequantises and caches the block's weights
+    times = []
+    for _ in range(samples):
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+    per_block = sorted(times)[len(times) // 2]
+    step_s = per_block * (LAYERS // 4)
+    return {"value": batch / step_s, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"one full-width 4-layer block (3 gated-delta + 1 attention) decode at batch {batch}, "
+                      f"{per_block:.2f} s per block, scaled x{LAYERS // 4} to 64 layers; lm_head not included; "
+                      f"CPU {platform.processor() or platform.machine()}"}
+
+
+def run_reference(args, world, rank, local):
+    """The reference arm: the CPU oracle on this host's cores, rank 0 only."""
+    if rank != 0:
+        return
+    pkg = importlib.import_module(PACKAGE)
+    cfg = pkg.config.full_config(num_blocks=LAYERS // 4)
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    run = cpu_block_step(cfg, pkg, args.batch)
+    for _ in range(max(1, args.warmup)):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run()
+    per_block = (time.perf_counter() - t0) / args.steps
+    step_s = per_block * (LAYERS // 4)
+    value = args.batch / step_s
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp8 weights dequantised to bf16 (CPU)", "data": "synthetic", "impl": "reference",
+        "config": {"workload": "BASELINE config 3 decode step, batch %d; per step one 4-layer block timed, scaled x16" % args.batch,
+                   "global_batch": args.batch, "seq_len": MAX_SEQ, "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
+                         "sample": "one full-width 4-layer block per step at the same batch, scaled to 64 layers"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    world, rank, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}; launch N>1 with torch.distributed.run")
+    if args.impl == "reference":
+        run_reference(args, world, rank, local)
+    else:
+        run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,160 @@
+/*
+ * q38.h: C ABI of the B200 (sm_100a) kernels for the Qwen3.8 hybrid-decoder step.
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream (passed as an opaque
+ * pointer, 0 for the legacy default stream), launches asynchronously on that stream, allocates
+ * nothing, and returns an int status: Q38_OK (0) or a negative Q38_ERR_* code. q38_last_error()
+ * gives the message of the last failure on the calling host thread.
+ *
+ * Numbers and layouts:
+ *   bf16   : IEEE bfloat16, 2 bytes.
+ *   e5m2   : FP8 E5M2 byte, the format the reference rounds every FP8 linear's input to
+ *            (qwen38_inf2/model.py:85-87, :224).
+ *   e4m3   : FP8 E4M3 (OCP e4m3fn) byte, the weight format.
+ *   ue8m0  : one byte per 32 weights along K, value 2^(byte-127) (power-of-two group scale).
+ *   Weights are row-major [out_features, in_features] (K contiguous). Their scales are pre-tiled by
+ *   q38_sf_tile_bytes/host code into 512-byte blocks, one per (128 output rows, 128 K): byte
+ *   (r % 32) * 16 + (r / 32) * 4 + (g % 4) holds row r's scale for K group g.
+ *
+ * The reference's device path is NKI kernels called from PyTorch (qwen38_inf2/kernels.py); its
+ * CPU branches (qwen38_inf2/model.py) define the arithmetic these kernels reproduce. Each function
+ * below names the reference interface it replaces.
+ */
+#ifndef Q38_H
+#define Q38_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define Q38_OK 0
+#define Q38_ERR_ARG (-1)         /* bad pointer, size, alignment or unsupported shape */
+#define Q38_ERR_CUDA (-2)        /* a CUDA runtime/driver call failed */
+#define Q38_ERR_TIMEOUT (-3)     /* a bounded device wait gave up (set by kernels) */
+#define Q38_ERR_UNSUPPORTED (-4) /* not built for this device */
+#define Q38_ERR_DEVICE (-5)      /* a kernel recorded an error; see q38_device_status */
+
+typedef void* q38_stream_t; /* a cudaStream_t */
+
+/* Epilogues of q38_fp8_gemm. */
+#define Q38_EPI_BF16 0     /* y = bf16(acc) */
+#define Q38_EPI_RESIDUAL 1 /* y = bf16(residual + bf16(acc)); residual may alias y */
+
+/* ABI version, bumped on any signature change. */
+int q38_abi_version(void);
+
+/* Copies the last error message of this host thread into buf (NUL-terminated). Returns its length. */
+int q38_last_error(char* buf, size_t n);
+
+/* Reads (and with reset != 0 clears) the device error word that bounded waits set. Synchronises
+ * the current device. Returns Q38_OK, a kernel's Q38_ERR_* code, or Q38_ERR_CUDA. */
+int q38_device_status(int reset);
+
+/*
+ * y[t, f] = sum_k e5m2(x)[t, k] * e4m3(w)[f, k] * 2^(sf[f, k/32] - 127), fp32 accumulate, then the
+ * epilogue. Replaces FP8Linear.forward (qwen38_inf2/model.py:211-229) and the NKI kernel
+ * fp8_linear (qwen38_inf2/kernels.py:25-71, :175-196), whose CPU branch is
+ * F.linear(fp8_round(x), fp8_to_float(W).T.to(bf16)). x is already e5m2 here: the producer of x
+ * (norm, gated norm, attention, SiLU product) rounds it.
+ *
+ *   x        e5m2 [tokens, k]            (16-byte aligned, k % 16 == 0)
+ *   w        e4m3 [features, k]
+ *   w_sf     pre-tiled ue8m0 scales, ceil(features/128) * ceil(k/128) blocks of 512 bytes
+ *   y        bf16 [tokens, ldy]
+ *   residual bf16 [tokens, ldr] for Q38_EPI_RESIDUAL, else NULL
+ *   splits   K splits (>= 1). With splits > 1 the partial sums go through `workspace`, of at least
+ *            q38_fp8_gemm_workspace_bytes(tokens, features, splits) bytes, whose counter region
+ *            must be zero before the first call (the kernel leaves it zero again).
+ */
+size_t q38_fp8_gemm_workspace_bytes(int64_t tokens, int64_t features, int splits);
+int q38_fp8_gemm(const void* x, int64_t tokens, int64_t k, const void* w, const void* w_sf, int64_t features,
+                 int epilogue, void* y, int64_t ldy, const void* residual, int64_t ldr, int splits, void* workspace,
+                 size_t workspace_bytes, q38_stream_t stream);
+
+/* Bytes of the pre-tiled scale array of a [features, k] weight. */
+size_t q38_sf_tile_bytes(int64_t features, int64_t k);
+
+/*
+ * Decoder-layer input norms: h = bf16(rms_norm(x) * (1 + w)), written as bf16 (y_bf16, optional)
+ * and as e5m2 (y_e5m2, optional). Replaces rms_norm (qwen38_inf2/model.py:54-57) as used by
+ * DecoderLayer.forward (:918-930) and HeadStep.forward (:890-891), plus the e5m2 rounding of
+ * fp8_round (:85-87) at the next linear.
+ */
+int q38_rmsnorm_quant(const void* x, int64_t ldx, const void* w, int64_t rows, int64_t n, float eps, void* y_bf16,
+                      int64_t ldy, void* y_e5m2, int64_t ldq, q38_stream_t stream);
+
+/*
+ * MLP middle: h = e5m2(bf16(bf16(silu(g)) * u)) with g, u the bf16 gate and up projections
+ * [rows, n] at gu and gu + n (row stride ld). Replaces silu(gate_proj(x)) * up_proj(x)
+ * (qwen38_inf2/model.py:48-51, :259) and the NKI mlp_up epilogue (kernels.py:74-118).
+ */
+int q38_silu_mul_quant(const void* gu, int64_t ld, int64_t rows, int64_t n, void* y_e5m2, int64_t ldy,
+                       q38_stream_t stream);
+
+/*
+ * y[r, o] = bf16(sum_k x[r, k] * w[o, k]) for small bf16 weights [n_out, k] (the gated delta
+ * rule's in_proj_b / in_proj_a, which stay BF16: qwen38_inf2/model.py:294-296, :333-337).
+ */
+int q38_bf16_linear_small(const void* x, int64_t ldx, int64_t rows, int64_t k, const void* w, int64_t n_out,
+                          void* y, int64_t ldy, q38_stream_t stream);
+
+/*
+ * One decode token per row of the gated delta rule, everything between the input projections and
+ * out_proj: causal conv window (kernel 4) + SiLU, q/k L2 norms (q / sqrt(dk)), key heads repeated to
+ * value heads, beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias), the recurrent update
+ * S = S*e^g*keep; delta = (v - S^T k) * beta; S += k delta^T; o = S^T q, and the gated RMS norm
+ * times SiLU(z), rounded to e5m2 for out_proj. Replaces GatedDeltaNetStep.forward
+ * (qwen38_inf2/model.py:347-374 with _split :322-331, _gates :333-337, _finish :339-345).
+ *
+ *   qkvz        bf16 [batch, ld_qkvz]: conv_dim qkv columns then value_dim z columns
+ *   ab          bf16 [batch, ld_ab]: num_v_heads b columns then num_v_heads a columns
+ *   conv_state  bf16 [batch, conv_dim, conv_kernel - 1], updated in place
+ *   conv_weight bf16 [conv_dim, conv_kernel]
+ *   a_log, dt_bias bf16 [num_v_heads]; norm_weight bf16 [head_v]
+ *   state       bf16 [batch, num_v_heads, head_k, head_v], updated in place (rows with active 0
+ *               keep theirs bit for bit)
+ *   position    int32 [batch]; active float32 [batch]
+ *   out         e5m2 [batch, ld_out], num_v_heads * head_v columns
+ */
+int q38_gdn_decode(const void* qkvz, int64_t ld_qkvz, const void* ab, int64_t ld_ab, void* conv_state,
+                   const void* conv_weight, const void* a_log, const void* dt_bias, const void* norm_weight,
+                   void* state, const int32_t* position, const float* active, void* out, int64_t ld_out,
+                   int64_t batch, int num_k_heads, int num_v_heads, int head_k, int head_v, int conv_kernel,
+                   float eps, q38_stream_t stream);
+
+/*
+ * One decode token per row of gated full attention with a BF16 KV cache: q/k RMS norms (1 + w),
+ * partial rotary on the first rot_dim dims, softmax attention over cache positions < position plus
+ * the token's own key/value, times sigmoid(gate), rounded to e5m2 for o_proj; the token's key and
+ * value are written at `position` (rows with active 0 write at max_seq - 1, as the reference does).
+ * Replaces FullAttentionStep._project + forward (qwen38_inf2/model.py:565-577, :610-639) and the
+ * NKI decode_attention (kernels.py:437-465, :491-644).
+ *
+ *   qkv      bf16 [batch, ld_qkv]: per q head [query head_dim | gate head_dim], then num_kv_heads
+ *            keys, then num_kv_heads values
+ *   cos, sin bf16 [batch, rot_dim]
+ *   k_cache, v_cache bf16 [batch, num_kv_heads, max_seq, head_dim]
+ *   out      e5m2 [batch, ld_out], num_q_heads * head_dim columns
+ */
+int q38_attn_decode(const void* qkv, int64_t ld_qkv, const void* q_norm_w, const void* k_norm_w, const void* cos,
+                    const void* sin, void* k_cache, void* v_cache, int64_t max_seq, const int32_t* position,
+                    const float* active, void* out, int64_t ld_out, int64_t batch, int num_q_heads,
+                    int num_kv_heads, int head_dim, int rot_dim, float eps, q38_stream_t stream);
+
+/*
+ * lm_head candidates: maxima[r, j] = max over the `group` vocab rows v in group j of
+ * sum_k x[r, k] * w[v, k], fp32 (x bf16 [rows, k], w bf16 [vocab, k]). Replaces HeadStep.forward's
+ * logits and group maxima (qwen38_inf2/model.py:890-900) and the NKI lm_head_group_maxima
+ * (kernels.py:126-172). group must be 32.
+ */
+int q38_lm_head_groupmax(const void* x, int64_t rows, int64_t k, const void* w, int64_t vocab, int group,
+                         float* maxima, int64_t ld_max, q38_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* Q38_H */

@@ -1,0 +1,397 @@
+// Tensor-core GEMMs for sm_100a: the FP8 linear layers and the lm_head group-of-32 maxima.
+//
+// Layout ("swap AB"): the weight matrix W [features, K] is the MMA's A operand (M = 128 features
+// per tile) and the activations X [tokens, K] are its B operand (N = 128 or 256 tokens per tile),
+// so a decode batch of 8..256 rows fills the MMA's N side and every weight byte is read once per
+// token tile. D[feature, token] accumulates in TMEM (lane = feature, column = token).
+//
+// Roles in one CTA of 192 threads:
+//   warp 0      TMA producer: W tile [128 x 128 B], X tile [NTOK x 128 B] (both 128-byte swizzled)
+//               and, for FP8, the 512-byte scale block of the W tile, into a STAGES-deep ring.
+//   warp 1      MMA issuer: one thread copies the W scales to TMEM (tcgen05.cp) and issues the
+//               4 MMAs of each stage (K = 32 bytes each), then commits the stage back to warp 0.
+//   warps 2..5  epilogue: tcgen05.ld of their 32-lane quarter, then the epilogue below.
+//
+// FP8 path: tcgen05.mma kind::mxf8f6f4.block_scale, A = e4m3 weights with UE8M0 scales per 32 K
+// (exact dequantisation: the reference's weights are e4m3 * 2^s), B = e5m2 activations with scale
+// 1.0. BF16 path (lm_head): kind::f16 with BF16 A and B.
+//
+// Split K: with splits > 1 each CTA stores its fp32 partial tile in the workspace; the last CTA of
+// a tile (by an atomic counter) sums the partials in split order 0..S-1, so results do not depend
+// on which CTA finishes last, then resets the counter.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+
+#include "q38_common.cuh"
+
+namespace {
+
+using namespace q38;
+
+constexpr int BM = 128;          // features per tile (MMA M)
+constexpr int BK_BYTES = 128;    // K bytes per pipeline stage (one 128-byte swizzle row)
+constexpr int SF_BLOCK = 512;    // scale bytes per (128 rows, 128 K) block
+
+enum : int { EPI_BF16 = 0, EPI_RESIDUAL = 1, EPI_GROUPMAX = 2 };
+
+template <int NTOK, bool MX>
+struct Cfg {
+  static constexpr int A_BYTES = BM * BK_BYTES;
+  static constexpr int B_BYTES = NTOK * BK_BYTES;
+  static constexpr int SF_BYTES = MX ? SF_BLOCK : 0;
+  static constexpr int STAGES = NTOK == 256 ? 4 : 6;
+  static constexpr int TMEM_COLS = NTOK == 256 ? 512 : 256;
+  static constexpr int SFA_COL = NTOK;       // 4 columns per stage
+  static constexpr int SFB_COL = NTOK + 32;  // 8 columns of 1.0 scales for the activations
+  static constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES + SF_BYTES) + 256;
+};
+
+struct GemmArgs {
+  const uint8_t* sf;  // pre-tiled W scales (FP8 path)
+  int T, F, nkc;      // tokens, features, K stages
+  int splits, kc_per_split;
+  int epilogue;
+  __nv_bfloat16* y;
+  int64_t ldy;
+  const __nv_bfloat16* res;
+  int64_t ldr;
+  float* maxima;  // group maxima [T, ldm] (EPI_GROUPMAX)
+  int64_t ldm;
+  float* ws;              // split partials
+  unsigned int* counters; // one per output tile
+};
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Applies the epilogue to 16 consecutive tokens of one feature row.
+__device__ __forceinline__ void epilogue16(const GemmArgs& a, int row, int t0, const float (&v)[16], int lane) {
+  if (a.epilogue == EPI_GROUPMAX) {
+    // The warp's 32 lanes are 32 consecutive vocab rows: one group (F is a multiple of 32, so a
+    // group is either wholly inside or wholly past the vocabulary).
+    if ((row & ~31) >= a.F) return;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float m = row < a.F ? v[j] : -INFINITY;
+      m = warp_max(m);
+      const int t = t0 + j;
+      if (lane == 0 && t < a.T) a.maxima[static_cast<int64_t>(t) * a.ldm + (row >> 5)] = m;
+    }
+    return;
+  }
+  if (row >= a.F) return;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int t = t0 + j;
+    if (t < a.T) {
+      float out = bf16r(v[j]);
+      if (a.epilogue == EPI_RESIDUAL) out = __bfloat162float(a.res[static_cast<int64_t>(t) * a.ldr + row]) + out;
+      a.y[static_cast<int64_t>(t) * a.ldy + row] = __float2bfloat16_rn(out);
+    }
+  }
+}
+
+template <int NTOK, bool MX>
+__global__ void __launch_bounds__(192, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, GemmArgs a) {
+  using C = Cfg<NTOK, MX>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + C::STAGES * C::A_BYTES;
+  uint8_t* sSF = sB + C::STAGES * C::B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sSF + C::STAGES * C::SF_BYTES);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* accf = empty + C::STAGES;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accf + 1);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_holder + 1);  // [0] abort, [1] last CTA
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = blockIdx.x, nt = blockIdx.y, split = blockIdx.z;
+  const int m0 = mt * BM, n0 = nt * NTOK;
+  const int kc0 = split * a.kc_per_split;
+  const int kc1 = min(a.nkc, kc0 + a.kc_per_split);
+  const int nk = kc1 - kc0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accf, 1);
+    flags[0] = 0;
+    flags[1] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  if (MX && warp >= 2) {
+    // Activation scales are all 1.0 (UE8M0 127) in every lane quarter.
+    const int q = warp & 3;
+    tmem_st8_fill(tmem + (static_cast<uint32_t>(q * 32) << 16) + C::SFB_COL, 0x7f7f7f7fu);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmap_w);
+      prefetch_tmap(&tmap_x);
+      int issued = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (i / C::STAGES) & 1;
+        if (flags[0] || !mbar_wait(&empty[s], ph ^ 1)) {
+          flags[0] = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES + C::SF_BYTES);
+        const int kx = (kc0 + i) * (MX ? BK_BYTES : BK_BYTES / 2);  // element coordinate along K
+        tma_load_2d(sA + s * C::A_BYTES, &tmap_w, &full[s], kx, m0);
+        tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0);
+        if (MX) bulk_load(sSF + s * SF_BLOCK, a.sf + (static_cast<size_t>(mt) * a.nkc + kc0 + i) * SF_BLOCK, SF_BLOCK, &full[s]);
+        issued = i + 1;
+      }
+      // Never leave with copies in flight: wait (bounded) for the last load of every stage.
+      for (int i = max(0, issued - C::STAGES); i < issued; ++i) mbar_wait(&full[i % C::STAGES], (i / C::STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      uint32_t idesc;
+      if (MX) {
+        idesc = (0u << 7)                                  // A: E4M3
+                | (1u << 10)                               // B: E5M2
+                | (static_cast<uint32_t>(NTOK >> 3) << 17)  // N
+                | (1u << 23)                               // scales UE8M0
+                | (static_cast<uint32_t>(BM >> 4) << 24);   // M
+      } else {
+        idesc = (1u << 4)                                  // D: F32
+                | (1u << 7) | (1u << 10)                   // A, B: BF16
+                | (static_cast<uint32_t>(NTOK >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+      }
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (i / C::STAGES) & 1;
+        if (flags[0] || !mbar_wait(&full[s], ph)) {
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES);
+        const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
+        if (MX) {
+          const uint32_t sfa = tmem + C::SFA_COL + 4 * s;
+          tmem_cp_32x128b_x4(sfa, sdesc_rows16(smem_u32(sSF + s * SF_BLOCK)));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t id = idesc | (static_cast<uint32_t>(kk) << 29) | (static_cast<uint32_t>(kk) << 4);
+            mma_mxf8(tmem, sdesc_sw128(a_addr + kk * 32), sdesc_sw128(b_addr + kk * 32), id,
+                     sfa | (static_cast<uint32_t>(kk) << 30), (tmem + C::SFB_COL) | (static_cast<uint32_t>(kk) << 30),
+                     (i | kk) != 0);
+          }
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16(tmem, sdesc_sw128(a_addr + kk * 32), sdesc_sw128(b_addr + kk * 32), idesc, (i | kk) != 0);
+        }
+        tc_commit(&empty[s]);
+      }
+      tc_commit(accf);
+    }
+    __syncwarp();
+  } else {
+    // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its hardware lane quarter).
+    const int q = warp & 3;
+    const int row = m0 + q * 32 + lane;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const bool ok = mbar_wait(accf, 0);
+    tc_fence_after();
+    if (!ok || flags[0]) {
+      flags[0] = 1;
+    } else if (a.splits == 1) {
+      for (int c = 0; c < NTOK; c += 16) {
+        if (n0 + c >= a.T) break;
+        float v[16];
+        tmem_ld16(taddr + c, v);
+        epilogue16(a, row, n0 + c, v, lane);
+      }
+    } else {
+      const int tiles = gridDim.x * gridDim.y;
+      const int tile = nt * gridDim.x + mt;
+      float* part = a.ws + (static_cast<size_t>(split) * tiles + tile) * BM * NTOK + static_cast<size_t>(q * 32 + lane) * NTOK;
+      for (int c = 0; c < NTOK; c += 16) {
+        if (n0 + c >= a.T) break;
+        float v[16];
+        tmem_ld16(taddr + c, v);
+#pragma unroll
+        for (int j = 0; j < 16; j += 4) __stcg(reinterpret_cast<float4*>(part + c + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+      }
+      __threadfence();
+      epi_bar();
+      if (warp == 2 && lane == 0) {
+        const unsigned prev = atomicAdd(&a.counters[tile], 1u);
+        flags[1] = prev == static_cast<unsigned>(a.splits - 1);
+      }
+      epi_bar();
+      if (flags[1]) {
+        __threadfence();
+        const float* base = a.ws + static_cast<size_t>(tile) * BM * NTOK + static_cast<size_t>(q * 32 + lane) * NTOK;
+        const size_t split_stride = static_cast<size_t>(tiles) * BM * NTOK;
+        for (int c = 0; c < NTOK; c += 16) {
+          if (n0 + c >= a.T) break;
+          float v[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = 0.f;
+          for (int s = 0; s < a.splits; ++s) {
+            const float* p = base + s * split_stride + c;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+              const float4 f = __ldcg(reinterpret_cast<const float4*>(p + j));
+              v[j] += f.x;
+              v[j + 1] += f.y;
+              v[j + 2] += f.z;
+              v[j + 3] += f.w;
+            }
+          }
+          epilogue16(a, row, n0 + c, v, lane);
+        }
+        if (warp == 2 && lane == 0) a.counters[tile] = 0u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int NTOK, bool MX>
+int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, dim3 grid, cudaStream_t stream) {
+  using C = Cfg<NTOK, MX>;
+  // The shared-memory opt-in is per device; remember which devices have it.
+  static unsigned long long done_mask = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return q38host::cuda_status(e, "cudaGetDevice");
+  if (dev < 64 && !(done_mask & (1ull << dev))) {
+    e = cudaFuncSetAttribute(gemm_kernel<NTOK, MX>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM));
+    if (e != cudaSuccess) return q38host::cuda_status(e, "cudaFuncSetAttribute(gemm)");
+    done_mask |= 1ull << dev;
+  }
+  gemm_kernel<NTOK, MX><<<grid, 192, C::SMEM, stream>>>(tw, tx, a);
+  return q38host::cuda_status(cudaGetLastError(), "gemm launch");
+}
+
+int token_tile(int64_t tokens) { return tokens > 128 ? 256 : 128; }
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" size_t q38_sf_tile_bytes(int64_t features, int64_t k) {
+  if (features <= 0 || k <= 0) return 0;
+  return static_cast<size_t>(cdiv(features, BM) * cdiv(k, BK_BYTES)) * SF_BLOCK;
+}
+
+extern "C" size_t q38_fp8_gemm_workspace_bytes(int64_t tokens, int64_t features, int splits) {
+  if (tokens <= 0 || features <= 0 || splits <= 1) return 0;
+  const int ntok = token_tile(tokens);
+  const int64_t tiles = cdiv(features, BM) * cdiv(tokens, ntok);
+  const size_t counters = static_cast<size_t>((tiles * 4 + 255) / 256 * 256);
+  return counters + static_cast<size_t>(splits) * tiles * BM * ntok * sizeof(float);
+}
+
+extern "C" int q38_fp8_gemm(const void* x, int64_t tokens, int64_t k, const void* w, const void* w_sf,
+                            int64_t features, int epilogue, void* y, int64_t ldy, const void* residual, int64_t ldr,
+                            int splits, void* workspace, size_t workspace_bytes, q38_stream_t stream) {
+  using namespace q38host;
+  if (!x || !w || !w_sf || !y) return set_error("q38_fp8_gemm: null pointer"), Q38_ERR_ARG;
+  if (tokens <= 0 || k <= 0 || features <= 0 || tokens > (1 << 24) || features > (1 << 30) || k > (1 << 30))
+    return set_error("q38_fp8_gemm: bad sizes tokens=%lld k=%lld features=%lld", (long long)tokens, (long long)k,
+                     (long long)features),
+           Q38_ERR_ARG;
+  if (k % 16 != 0 || !aligned16(x) || !aligned16(w) || !aligned16(w_sf))
+    return set_error("q38_fp8_gemm: k must be a multiple of 16 and x, w, w_sf 16-byte aligned"), Q38_ERR_ARG;
+  if (epilogue != Q38_EPI_BF16 && epilogue != Q38_EPI_RESIDUAL)
+    return set_error("q38_fp8_gemm: unknown epilogue %d", epilogue), Q38_ERR_ARG;
+  if (epilogue == Q38_EPI_RESIDUAL && !residual) return set_error("q38_fp8_gemm: residual epilogue needs residual"), Q38_ERR_ARG;
+  if (ldy < features || (residual && ldr < features)) return set_error("q38_fp8_gemm: leading dimension too small"), Q38_ERR_ARG;
+  if (splits < 1) return set_error("q38_fp8_gemm: splits must be >= 1"), Q38_ERR_ARG;
+
+  const int ntok = token_tile(tokens);
+  const int nkc = static_cast<int>(cdiv(k, BK_BYTES));
+  int kc_per = static_cast<int>(cdiv(nkc, std::min(splits, nkc)));
+  splits = static_cast<int>(cdiv(nkc, kc_per));
+  GemmArgs a{};
+  a.sf = static_cast<const uint8_t*>(w_sf);
+  a.T = static_cast<int>(tokens);
+  a.F = static_cast<int>(features);
+  a.nkc = nkc;
+  a.splits = splits;
+  a.kc_per_split = kc_per;
+  a.epilogue = epilogue;
+  a.y = static_cast<__nv_bfloat16*>(y);
+  a.ldy = ldy;
+  a.res = static_cast<const __nv_bfloat16*>(residual);
+  a.ldr = ldr;
+  const int64_t tiles = cdiv(features, BM) * cdiv(tokens, ntok);
+  if (splits > 1) {
+    const size_t need = q38_fp8_gemm_workspace_bytes(tokens, features, splits);
+    if (!workspace || workspace_bytes < need || !aligned16(workspace))
+      return set_error("q38_fp8_gemm: split-K needs a 16-byte aligned workspace of %zu bytes", need), Q38_ERR_ARG;
+    const size_t counters = static_cast<size_t>((tiles * 4 + 255) / 256 * 256);
+    a.counters = static_cast<unsigned int*>(workspace);
+    a.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
+  }
+  CUtensorMap tw, tx;
+  int st = encode_tmap_2d(&tw, w, features, k, 1, BM, BK_BYTES);
+  if (st != Q38_OK) return st;
+  st = encode_tmap_2d(&tx, x, tokens, k, 1, ntok, BK_BYTES);
+  if (st != Q38_OK) return st;
+  dim3 grid(static_cast<unsigned>(cdiv(features, BM)), static_cast<unsigned>(cdiv(tokens, ntok)), static_cast<unsigned>(splits));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return ntok == 256 ? launch_gemm<256, true>(tw, tx, a, grid, s) : launch_gemm<128, true>(tw, tx, a, grid, s);
+}
+
+extern "C" int q38_lm_head_groupmax(const void* x, int64_t rows, int64_t k, const void* w, int64_t vocab, int group,
+                                    float* maxima, int64_t ld_max, q38_stream_t stream) {
+  using namespace q38host;
+  if (!x || !w || !maxima) return set_error("q38_lm_head_groupmax: null pointer"), Q38_ERR_ARG;
+  if (group != 32) return set_error("q38_lm_head_groupmax: group must be 32, got %d", group), Q38_ERR_ARG;
+  if (rows <= 0 || k <= 0 || vocab <= 0 || vocab % 32 != 0 || k % 8 != 0 || rows > (1 << 24) || vocab > (1 << 30))
+    return set_error("q38_lm_head_groupmax: bad sizes rows=%lld k=%lld vocab=%lld", (long long)rows, (long long)k,
+                     (long long)vocab),
+           Q38_ERR_ARG;
+  if (!aligned16(x) || !aligned16(w)) return set_error("q38_lm_head_groupmax: x and w must be 16-byte aligned"), Q38_ERR_ARG;
+  if (ld_max < vocab / 32) return set_error("q38_lm_head_groupmax: ld_max too small"), Q38_ERR_ARG;
+  const int ntok = token_tile(rows);
+  GemmArgs a{};
+  a.T = static_cast<int>(rows);
+  a.F = static_cast<int>(vocab);
+  a.nkc = static_cast<int>(cdiv(k, BK_BYTES / 2));
+  a.splits = 1;
+  a.kc_per_split = a.nkc;
+  a.epilogue = EPI_GROUPMAX;
+  a.maxima = maxima;
+  a.ldm = ld_max;
+  CUtensorMap tw, tx;
+  int st = encode_tmap_2d(&tw, w, vocab, k, 2, BM, BK_BYTES / 2);
+  if (st != Q38_OK) return st;
+  st = encode_tmap_2d(&tx, x, rows, k, 2, ntok, BK_BYTES / 2);
+  if (st != Q38_OK) return st;
+  dim3 grid(static_cast<unsigned>(cdiv(vocab, BM)), static_cast<unsigned>(cdiv(rows, ntok)), 1);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return ntok == 256 ? launch_gemm<256, false>(tw, tx, a, grid, s) : launch_gemm<128, false>(tw, tx, a, grid, s);
+}

@@ -1,0 +1,187 @@
+// Element-wise and row kernels around the FP8 GEMMs, each rounding where the reference rounds:
+//   q38_rmsnorm_quant      rms_norm (model.py:54-57) -> bf16, and e5m2 for the next FP8 linear
+//   q38_silu_mul_quant     silu(gate) * up in bf16 steps (model.py:48-51, :259) -> e5m2
+//   q38_bf16_linear_small  x @ W^T for the BF16 in_proj_b / in_proj_a (model.py:333-337)
+// All are HBM-bound; rows are read with 16-byte vector loads.
+#include "q38_common.cuh"
+
+namespace {
+
+using namespace q38;
+
+constexpr int kNormThreads = 256;
+
+union Pack8 {
+  uint4 u;
+  __nv_bfloat16 h[8];
+};
+
+// One CTA per row. Two passes over the row: sum of squares, then scale. The second read of the
+// row hits L1/L2.
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                                      const __nv_bfloat16* __restrict__ w, int n,
+                                                                      float eps, __nv_bfloat16* __restrict__ y,
+                                                                      int64_t ldy, uint8_t* __restrict__ q,
+                                                                      int64_t ldq) {
+  const int row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * ldx;
+  const int chunks = n / 8;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < chunks; c += kNormThreads) {
+    Pack8 p;
+    p.u = *reinterpret_cast<const uint4*>(xr + c * 8);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float f = __bfloat162float(p.h[i]);
+      ss += f * f;
+    }
+  }
+  __shared__ float red[kNormThreads / 32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) total += red[i];
+  const float r = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
+  for (int c = threadIdx.x; c < chunks; c += kNormThreads) {
+    Pack8 p, pw, out;
+    p.u = *reinterpret_cast<const uint4*>(xr + c * 8);
+    pw.u = *reinterpret_cast<const uint4*>(w + c * 8);
+    float h[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float scaled = __fmul_rn(__bfloat162float(p.h[i]), r);
+      h[i] = bf16r(__fmul_rn(scaled, __fadd_rn(1.0f, __bfloat162float(pw.h[i]))));
+      out.h[i] = __float2bfloat16_rn(h[i]);
+    }
+    if (y) *reinterpret_cast<uint4*>(y + row * ldy + c * 8) = out.u;
+    if (q) {
+      uint2 o;
+      o.x = pack4_e5m2(h[0], h[1], h[2], h[3]);
+      o.y = pack4_e5m2(h[4], h[5], h[6], h[7]);
+      *reinterpret_cast<uint2*>(q + row * ldq + c * 8) = o;
+    }
+  }
+}
+
+// Grid-stride over (row, 8-column chunk).
+__global__ void silu_mul_quant_kernel(const __nv_bfloat16* __restrict__ gu, int64_t ld, int rows, int n,
+                                      uint8_t* __restrict__ y, int64_t ldy) {
+  const int chunks = n / 8;
+  const int64_t total = static_cast<int64_t>(rows) * chunks;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(i / chunks);
+    const int c = static_cast<int>(i % chunks);
+    Pack8 g, u;
+    g.u = *reinterpret_cast<const uint4*>(gu + row * ld + c * 8);
+    u.u = *reinterpret_cast<const uint4*>(gu + row * ld + n + c * 8);
+    float h[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float gf = __bfloat162float(g.h[k]);
+      const float s = bf16r(sigmoidf_(gf));
+      const float t = bf16r(__fmul_rn(gf, s));
+      h[k] = bf16r(__fmul_rn(t, __bfloat162float(u.h[k])));
+    }
+    uint2 o;
+    o.x = pack4_e5m2(h[0], h[1], h[2], h[3]);
+    o.y = pack4_e5m2(h[4], h[5], h[6], h[7]);
+    *reinterpret_cast<uint2*>(y + row * ldy + c * 8) = o;
+  }
+}
+
+// CTA = 4 rows of x staged in shared memory; warps take output columns round-robin and stream
+// their weight rows with 16-byte loads.
+constexpr int kLinRows = 4;
+__global__ void __launch_bounds__(256) bf16_linear_small_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                                 int rows, int k, const __nv_bfloat16* __restrict__ w,
+                                                                 int n_out, __nv_bfloat16* __restrict__ y, int64_t ldy) {
+  extern __shared__ uint4 xs_raw[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(xs_raw);
+  const int r0 = blockIdx.x * kLinRows;
+  const int nr = min(kLinRows, rows - r0);
+  const int chunks = k / 8;
+  for (int i = threadIdx.x; i < kLinRows * chunks; i += blockDim.x) {
+    const int r = i / chunks, c = i % chunks;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < nr) v = *reinterpret_cast<const uint4*>(x + (r0 + r) * ldx + c * 8);
+    reinterpret_cast<uint4*>(xs)[i] = v;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int o = warp; o < n_out; o += blockDim.x / 32) {
+    float acc[kLinRows] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = lane; c < chunks; c += 32) {
+      Pack8 pw;
+      pw.u = *reinterpret_cast<const uint4*>(w + static_cast<int64_t>(o) * k + c * 8);
+#pragma unroll
+      for (int r = 0; r < kLinRows; ++r) {
+        Pack8 px;
+        px.u = reinterpret_cast<const uint4*>(xs)[r * chunks + c];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[r] += __bfloat162float(px.h[e]) * __bfloat162float(pw.h[e]);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kLinRows; ++r) {
+      const float s = warp_sum(acc[r]);
+      if (lane == 0 && r < nr) y[(r0 + r) * ldy + o] = __float2bfloat16_rn(s);
+    }
+  }
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" int q38_rmsnorm_quant(const void* x, int64_t ldx, const void* w, int64_t rows, int64_t n, float eps,
+                                 void* y_bf16, int64_t ldy, void* y_e5m2, int64_t ldq, q38_stream_t stream) {
+  using namespace q38host;
+  if (!x || !w || (!y_bf16 && !y_e5m2)) return set_error("q38_rmsnorm_quant: null pointer"), Q38_ERR_ARG;
+  if (rows <= 0 || n <= 0 || n % 8 != 0 || rows > (1 << 30) || ldx < n || (y_bf16 && ldy < n) || (y_e5m2 && ldq < n))
+    return set_error("q38_rmsnorm_quant: bad sizes"), Q38_ERR_ARG;
+  if (!al16(x) || !al16(w) || (y_bf16 && !al16(y_bf16)) || (y_e5m2 && reinterpret_cast<uintptr_t>(y_e5m2) % 8) ||
+      ldx % 8 || (y_bf16 && ldy % 8) || (y_e5m2 && ldq % 8))
+    return set_error("q38_rmsnorm_quant: misaligned pointer or leading dimension"), Q38_ERR_ARG;
+  rmsnorm_quant_kernel<<<static_cast<unsigned>(rows), kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w), static_cast<int>(n), eps,
+      static_cast<__nv_bfloat16*>(y_bf16), ldy, static_cast<uint8_t*>(y_e5m2), ldq);
+  return cuda_status(cudaGetLastError(), "rmsnorm_quant launch");
+}
+
+extern "C" int q38_silu_mul_quant(const void* gu, int64_t ld, int64_t rows, int64_t n, void* y_e5m2, int64_t ldy,
+                                  q38_stream_t stream) {
+  using namespace q38host;
+  if (!gu || !y_e5m2) return set_error("q38_silu_mul_quant: null pointer"), Q38_ERR_ARG;
+  if (rows <= 0 || n <= 0 || n % 8 || ld < 2 * n || ldy < n || ld % 8 || ldy % 8 || !al16(gu) ||
+      reinterpret_cast<uintptr_t>(y_e5m2) % 8)
+    return set_error("q38_silu_mul_quant: bad sizes or alignment"), Q38_ERR_ARG;
+  const int64_t work = rows * (n / 8);
+  const unsigned blocks = static_cast<unsigned>(std::min<int64_t>((work + 255) / 256, 148 * 16));
+  silu_mul_quant_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(gu), ld, static_cast<int>(rows), static_cast<int>(n),
+      static_cast<uint8_t*>(y_e5m2), ldy);
+  return cuda_status(cudaGetLastError(), "silu_mul_quant launch");
+}
+
+extern "C" int q38_bf16_linear_small(const void* x, int64_t ldx, int64_t rows, int64_t k, const void* w,
+                                     int64_t n_out, void* y, int64_t ldy, q38_stream_t stream) {
+  using namespace q38host;
+  if (!x || !w || !y) return set_error("q38_bf16_linear_small: null pointer"), Q38_ERR_ARG;
+  if (rows <= 0 || k <= 0 || n_out <= 0 || k % 8 || ldx % 8 || ldx < k || ldy < n_out || !al16(x) || !al16(w))
+    return set_error("q38_bf16_linear_small: bad sizes or alignment"), Q38_ERR_ARG;
+  const size_t smem = static_cast<size_t>(kLinRows) * k * sizeof(__nv_bfloat16);
+  if (smem > 200 * 1024) return set_error("q38_bf16_linear_small: k=%lld too large", (long long)k), Q38_ERR_ARG;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(bf16_linear_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem));
+    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(bf16_linear_small)");
+  }
+  const unsigned blocks = static_cast<unsigned>((rows + kLinRows - 1) / kLinRows);
+  bf16_linear_small_kernel<<<blocks, 256, smem, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, static_cast<int>(rows), static_cast<int>(k),
+      static_cast<const __nv_bfloat16*>(w), static_cast<int>(n_out), static_cast<__nv_bfloat16*>(y), ldy);
+  return cuda_status(cudaGetLastError(), "bf16_linear_small launch");
+}

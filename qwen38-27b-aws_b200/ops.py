@@ -1,0 +1,144 @@
+"""One wrapper per C-ABI call of include/q38.h, taking torch CUDA tensors.
+
+Each launches on the current torch stream and raises `_lib.Q38Error` on a bad status. Shapes and
+dtypes are checked here so a wrong call fails on the host with a message, not on the device.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib, codec
+
+BF16 = torch.bfloat16
+U8 = torch.uint8
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need(cond: bool, msg: str) -> None:
+    if not cond:
+        raise ValueError(msg)
+
+
+def _cuda(*ts) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("all tensors must be on a CUDA device")
+
+
+class DeviceLinear:
+    """An FP8 linear prepared for the GEMM kernel: e4m3 bytes [out, in] and tiled UE8M0 scales."""
+
+    def __init__(self, w, device):
+        self.q = w.q.to(device=device, dtype=U8).contiguous()
+        self.sf = codec.tile_scales(codec.scale_to_ue8m0(w.scale.to(device))).contiguous()
+        self.out_features, self.in_features = self.q.shape
+        _need(self.sf.numel() == _lib.load().q38_sf_tile_bytes(self.out_features, self.in_features), "scale tiling mismatch")
+
+    @property
+    def nbytes(self) -> int:
+        return self.q.numel() + self.sf.numel()
+
+
+def token_tile(tokens: int) -> int:
+    return 256 if tokens > 128 else 128
+
+
+def choose_splits(tokens: int, features: int, k: int, sms: int = 148) -> int:
+    """K splits that bring the grid near one CTA per SM for weight-streaming (few-token) GEMMs."""
+    tiles = -(-features // 128) * -(-tokens // token_tile(tokens))
+    kc = -(-k // 128)
+    if tiles >= sms // 2:
+        return 1
+    return max(1, min(kc // 4, sms // tiles))
+
+
+def gemm_workspace_bytes(tokens: int, features: int, splits: int) -> int:
+    return _lib.load().q38_fp8_gemm_workspace_bytes(tokens, features, splits)
+
+
+def fp8_gemm(x_e5m2: torch.Tensor, lin: DeviceLinear, y: torch.Tensor, residual: torch.Tensor | None = None,
+             splits: int = 1, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """y[:, :out] = bf16(e5m2(x) @ W^T) (+ residual, in bf16)."""
+    _cuda(x_e5m2, y, residual, workspace)
+    _need(x_e5m2.dtype == U8 and x_e5m2.dim() == 2 and x_e5m2.stride(1) == 1 and x_e5m2.stride(0) == x_e5m2.shape[1],
+          "x must be contiguous uint8 e5m2 [tokens, k]")
+    tokens, k = x_e5m2.shape
+    _need(k == lin.in_features, f"x has {k} columns, the weight {lin.in_features}")
+    _need(y.dtype == BF16 and y.dim() == 2 and y.stride(1) == 1 and y.shape[0] >= tokens, "y must be bf16 [tokens, >= out]")
+    epi = 0
+    ldr = 0
+    if residual is not None:
+        _need(residual.dtype == BF16 and residual.stride(1) == 1, "residual must be bf16 with unit column stride")
+        epi, ldr = 1, residual.stride(0)
+    ws_ptr, ws_bytes = None, 0
+    if splits > 1:
+        _need(workspace is not None, "split K needs a workspace")
+        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    _lib.call("q38_fp8_gemm", x_e5m2.data_ptr(), tokens, k, lin.q.data_ptr(), lin.sf.data_ptr(), lin.out_features, epi,
+              y.data_ptr(), y.stride(0), residual.data_ptr() if residual is not None else None, ldr, splits, ws_ptr,
+              ws_bytes, _stream())
+    return y
+
+
+def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, y_bf16: torch.Tensor | None = None,
+                  y_e5m2: torch.Tensor | None = None) -> None:
+    _cuda(x, w, y_bf16, y_e5m2)
+    rows, n = x.shape
+    _need(x.dtype == BF16 and w.dtype == BF16 and w.numel() == n, "rmsnorm_quant: bf16 x [rows, n], w [n]")
+    _lib.call("q38_rmsnorm_quant", x.data_ptr(), x.stride(0), w.data_ptr(), rows, n, eps,
+              y_bf16.data_ptr() if y_bf16 is not None else None, y_bf16.stride(0) if y_bf16 is not None else 0,
+              y_e5m2.data_ptr() if y_e5m2 is not None else None, y_e5m2.stride(0) if y_e5m2 is not None else 0,
+              _stream())
+
+
+def silu_mul_quant(gu: torch.Tensor, n: int, y_e5m2: torch.Tensor) -> None:
+    _cuda(gu, y_e5m2)
+    rows = gu.shape[0]
+    _lib.call("q38_silu_mul_quant", gu.data_ptr(), gu.stride(0), rows, n, y_e5m2.data_ptr(), y_e5m2.stride(0), _stream())
+
+
+def bf16_linear_small(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> None:
+    _cuda(x, w, y)
+    rows, k = x.shape
+    _need(w.dtype == BF16 and w.shape[1] == k and w.is_contiguous(), "w must be contiguous bf16 [n_out, k]")
+    _lib.call("q38_bf16_linear_small", x.data_ptr(), x.stride(0), rows, k, w.data_ptr(), w.shape[0], y.data_ptr(),
+              y.stride(0), _stream())
+
+
+def gdn_decode(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, state, position, active, out, *,
+               batch: int, num_k_heads: int, num_v_heads: int, head_k: int, head_v: int, eps: float) -> None:
+    _cuda(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, state, position, active, out)
+    _need(position.dtype == torch.int32 and active.dtype == torch.float32, "position int32, active float32")
+    _need(state.is_contiguous() and conv_state.is_contiguous(), "state buffers must be contiguous")
+    _lib.call("q38_gdn_decode", qkvz.data_ptr(), qkvz.stride(0), ab.data_ptr(), ab.stride(0), conv_state.data_ptr(),
+              conv_weight.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(), norm_weight.data_ptr(), state.data_ptr(),
+              position.data_ptr(), active.data_ptr(), out.data_ptr(), out.stride(0), batch, num_k_heads, num_v_heads,
+              head_k, head_v, conv_weight.shape[1], eps, _stream())
+
+
+def attn_decode(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, position, active, out, *, batch: int,
+                num_q_heads: int, num_kv_heads: int, head_dim: int, rot_dim: int, eps: float) -> None:
+    _cuda(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, position, active, out)
+    _need(cos.is_contiguous() and sin.is_contiguous() and cos.shape[-1] == rot_dim, "cos/sin [batch, rot] contiguous")
+    _need(k_cache.is_contiguous() and v_cache.is_contiguous(), "caches must be contiguous")
+    _lib.call("q38_attn_decode", qkv.data_ptr(), qkv.stride(0), q_norm_w.data_ptr(), k_norm_w.data_ptr(), cos.data_ptr(),
+              sin.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2], position.data_ptr(),
+              active.data_ptr(), out.data_ptr(), out.stride(0), batch, num_q_heads, num_kv_heads, head_dim, rot_dim, eps,
+              _stream())
+
+
+def lm_head_groupmax(x: torch.Tensor, w: torch.Tensor, maxima: torch.Tensor, group: int = 32) -> None:
+    _cuda(x, w, maxima)
+    rows, k = x.shape
+    _need(x.is_contiguous() and w.is_contiguous() and w.dtype == BF16 and x.dtype == BF16, "bf16 contiguous x, w")
+    _need(maxima.dtype == torch.float32 and maxima.stride(1) == 1, "maxima fp32")
+    _lib.call("q38_lm_head_groupmax", x.data_ptr(), rows, k, w.data_ptr(), w.shape[0], group, maxima.data_ptr(),
+              maxima.stride(0), _stream())
+
+
+def device_status(reset: bool = True) -> int:
+    return _lib.load().q38_device_status(1 if reset else 0)

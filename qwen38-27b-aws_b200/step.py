@@ -1,0 +1,309 @@
+"""The drop-in step objects: `B200Step` and `B200Head`.
+
+`B200Step(**inputs)` has the call of the reference's `NeuronStep.__call__(inputs_embeds, **inputs)`
+(qwen38_inf2/neuron.py:273-280) and `SimulatedCoresStep.__call__` (cpu_sim.py:83-85): host tensors
+in, the hidden state ``[rows, tokens, hidden]`` back on the host, routed by which inputs are present
+exactly as `Qwen38Step.forward` routes them (model.py:983-995):
+
+* decode: inputs_embeds [B, 1, H], cos/sin [B, 1, rot], position int32 [B], active float32 [B];
+* prefill: inputs_embeds [1, C, H], cos/sin [1, C, rot], slot/start/n_valid int32 [1] (not built yet);
+* save_slot / restore_slot int32 [1]: copy one row's recurrent states, return inputs_embeds.
+
+`B200Head.run_graph(hidden=...)` is the reference's lm_head graph call (generate.py:194):
+hidden [B, 1, H] -> group-of-32 maxima [B, V / 32] float32 on the host.
+
+One process drives one GPU. With tp_degree > 1 every rank makes the same calls with the same inputs
+(torch.distributed, NCCL), holds its slice of heads, and the row-parallel outputs are summed across
+ranks after o_proj / out_proj / down_proj (model.py:259, :374, :639).
+
+The decode step is captured once into a CUDA graph and replayed: ~9 kernels per layer, all on one
+stream, with every buffer allocated up front. Nothing here falls back to PyTorch math: the layer
+arithmetic is the C-ABI kernels (ops.py) or it fails.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import ops, weights as W
+from .config import FULL, LINEAR, TextConfig
+
+BF16 = torch.bfloat16
+
+
+@dataclass
+class _GDN:
+    qkvz: ops.DeviceLinear
+    ab: torch.Tensor
+    conv_w: torch.Tensor
+    a_log: torch.Tensor
+    dt_bias: torch.Tensor
+    norm_w: torch.Tensor
+    out: ops.DeviceLinear
+    conv_state: torch.Tensor
+    state: torch.Tensor
+
+
+@dataclass
+class _Attn:
+    qkv: ops.DeviceLinear
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+    o: ops.DeviceLinear
+    k_cache: torch.Tensor
+    v_cache: torch.Tensor
+
+
+@dataclass
+class _Layer:
+    kind: str
+    ln_in: torch.Tensor
+    ln_post: torch.Tensor
+    mixer: object
+    gate_up: ops.DeviceLinear
+    down: ops.DeviceLinear
+
+
+class B200Step:
+    """The decoder layers of one rank on one B200, called like the reference's NeuronStep."""
+
+    def __init__(self, cfg: TextConfig, layer_weights, max_seq_len: int, batch_size: int, tp_degree: int = 1,
+                 rank: int = 0, device: torch.device | str | None = None, saved_states: bool = False,
+                 use_graph: bool = True, process_group=None):
+        """`layer_weights(i)` returns layer i's unsharded weights (weights.synthetic_layer names), or
+        `layer_weights` is a dict holding them all."""
+        cfg.validate_tp(tp_degree)
+        self.cfg, self.tp, self.rank = cfg, tp_degree, rank
+        self.max_seq, self.batch = max_seq_len, batch_size
+        self.device = torch.device(device or f"cuda:{torch.cuda.current_device()}")
+        self.group = process_group
+        self.use_graph = use_graph
+        self.saved = saved_states
+        get = layer_weights if callable(layer_weights) else (lambda i: layer_weights)
+        with torch.cuda.device(self.device):
+            self.layers = [self._prepare(i, W.shard_layer(cfg, get(i), i, rank, tp_degree)) for i in range(cfg.num_hidden_layers)]
+            self._alloc_activations()
+        self._graph = None
+        self._graph_key = None
+
+    # ------------------------------------------------------------------ setup
+    def _prepare(self, i: int, w: dict) -> _Layer:
+        cfg, dev, p = self.cfg, self.device, f"layers.{i}"
+        t = lambda name: w[f"{p}.{name}"].to(dev, BF16).contiguous()  # noqa: E731
+        lin = lambda *names: ops.DeviceLinear(W.FP8Weight.cat_rows([w[f"{p}.{n}"] for n in names]), dev)  # noqa: E731
+        rows = self.batch * (2 if self.saved else 1)
+        if cfg.layer_types[i] == LINEAR:
+            hv = cfg.linear_num_value_heads // self.tp
+            conv_dim = cfg.linear_conv_dim // self.tp
+            mixer = _GDN(
+                qkvz=lin("linear_attn.in_proj_qkv", "linear_attn.in_proj_z"),
+                ab=torch.cat((t("linear_attn.in_proj_b"), t("linear_attn.in_proj_a"))).contiguous(),
+                conv_w=t("linear_attn.conv_weight"),
+                a_log=t("linear_attn.A_log"),
+                dt_bias=t("linear_attn.dt_bias"),
+                norm_w=t("linear_attn.norm_weight"),
+                out=lin("linear_attn.out_proj"),
+                conv_state=torch.zeros(rows, conv_dim, cfg.linear_conv_kernel_dim - 1, dtype=BF16, device=dev),
+                state=torch.zeros(rows, hv, cfg.linear_key_head_dim, cfg.linear_value_head_dim, dtype=BF16, device=dev),
+            )
+        elif cfg.layer_types[i] == FULL:
+            kvh = cfg.kv_heads_per_rank(self.tp)
+            mixer = _Attn(
+                qkv=lin("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"),
+                q_norm=t("self_attn.q_norm_weight"),
+                k_norm=t("self_attn.k_norm_weight"),
+                o=lin("self_attn.o_proj"),
+                k_cache=torch.zeros(self.batch, kvh, self.max_seq, cfg.head_dim, dtype=BF16, device=dev),
+                v_cache=torch.zeros(self.batch, kvh, self.max_seq, cfg.head_dim, dtype=BF16, device=dev),
+            )
+        else:
+            raise ValueError(cfg.layer_types[i])
+        return _Layer(cfg.layer_types[i], t("input_layernorm_weight"), t("post_attention_layernorm_weight"), mixer,
+                      lin("mlp.gate_proj", "mlp.up_proj"), lin("mlp.down_proj"))
+
+    def _alloc_activations(self):
+        cfg, dev, B, tp = self.cfg, self.device, self.batch, self.tp
+        H = cfg.hidden_size
+        hv = cfg.linear_num_value_heads // tp
+        vd = cfg.linear_value_dim // tp
+        heads = cfg.num_attention_heads // tp
+        inter = cfg.intermediate_size // tp
+        z = lambda *s, dt=BF16: torch.zeros(*s, dtype=dt, device=dev)  # noqa: E731
+        self.x = z(B, H)
+        self.x_in = z(B, H)
+        self.hb = z(B, H)
+        self.hq = z(B, H, dt=torch.uint8)
+        widths = [l.mixer.qkvz.out_features for l in self.layers if l.kind == LINEAR]
+        widths += [l.mixer.qkv.out_features for l in self.layers if l.kind == FULL]
+        self.proj = z(B, max(widths))
+        self.ab = z(B, 2 * hv)
+        self.mix_gdn = z(B, vd, dt=torch.uint8)
+        self.mix_attn = z(B, heads * cfg.head_dim, dt=torch.uint8)
+        self.gu = z(B, 2 * inter)
+        self.mlp_q = z(B, inter, dt=torch.uint8)
+        self.partial = z(B, H) if tp > 1 else None
+        self.cos = z(B, cfg.rotary_dim)
+        self.sin = z(B, cfg.rotary_dim)
+        self.position = z(B, dt=torch.int32)
+        self.active = z(B, dt=torch.float32)
+        # Split-K plans and one shared workspace for every row-parallel GEMM.
+        self.splits = {}
+        need = 0
+        for l in self.layers:
+            for lin in (l.mixer.out if l.kind == LINEAR else l.mixer.o, l.down, l.gate_up,
+                        l.mixer.qkvz if l.kind == LINEAR else l.mixer.qkv):
+                s = ops.choose_splits(B, lin.out_features, lin.in_features)
+                self.splits[id(lin)] = s
+                need = max(need, ops.gemm_workspace_bytes(B, lin.out_features, s))
+        self.workspace = z(max(need, 256), dt=torch.uint8)
+
+    # ------------------------------------------------------------------ kernels of one decode step
+    def _gemm(self, x_q, lin: ops.DeviceLinear, y, residual=None):
+        ops.fp8_gemm(x_q, lin, y, residual=residual, splits=self.splits.get(id(lin), 1), workspace=self.workspace)
+
+    def _row_parallel(self, x_q, lin: ops.DeviceLinear):
+        """x += all_reduce(bf16(x_q @ W^T)) (the reference's `x + all_reduce(proj(...))`)."""
+        if self.tp == 1:
+            self._gemm(x_q, lin, self.x, residual=self.x)
+            return
+        self._gemm(x_q, lin, self.partial)
+        torch.distributed.all_reduce(self.partial, group=self.group)
+        self.x.add_(self.partial)
+
+    def _decode_layers(self):
+        cfg, B, eps = self.cfg, self.batch, self.cfg.rms_norm_eps
+        tp = self.tp
+        self.x.copy_(self.x_in)
+        for l in self.layers:
+            m = l.mixer
+            if l.kind == LINEAR:
+                ops.rmsnorm_quant(self.x, l.ln_in, eps, y_bf16=self.hb, y_e5m2=self.hq)
+                self._gemm(self.hq, m.qkvz, self.proj)
+                ops.bf16_linear_small(self.hb, m.ab, self.ab)
+                vd = cfg.linear_value_dim // tp
+                ops.gdn_decode(self.proj, self.ab, m.conv_state, m.conv_w, m.a_log, m.dt_bias, m.norm_w, m.state,
+                               self.position, self.active, self.mix_gdn, batch=B,
+                               num_k_heads=cfg.linear_num_key_heads // tp, num_v_heads=cfg.linear_num_value_heads // tp,
+                               head_k=cfg.linear_key_head_dim, head_v=cfg.linear_value_head_dim, eps=eps)
+                self._row_parallel(self.mix_gdn, m.out)
+            else:
+                ops.rmsnorm_quant(self.x, l.ln_in, eps, y_e5m2=self.hq)
+                self._gemm(self.hq, m.qkv, self.proj)
+                heads = cfg.num_attention_heads // tp
+                ops.attn_decode(self.proj, m.q_norm, m.k_norm, self.cos, self.sin, m.k_cache, m.v_cache, self.position,
+                                self.active, self.mix_attn, batch=B, num_q_heads=heads,
+                                num_kv_heads=cfg.kv_heads_per_rank(tp), head_dim=cfg.head_dim,
+                                rot_dim=cfg.rotary_dim, eps=eps)
+                self._row_parallel(self.mix_attn, m.o)
+            ops.rmsnorm_quant(self.x, l.ln_post, eps, y_e5m2=self.hq)
+            self._gemm(self.hq, l.gate_up, self.gu)
+            inter = cfg.intermediate_size // tp
+            ops.silu_mul_quant(self.gu, inter, self.mlp_q)
+            self._row_parallel(self.mlp_q, l.down)
+
+    def kernels_per_decode_step(self) -> int:
+        """Launches of this library's kernels in one decode step (for the bench's gpu_launches)."""
+        n = 0
+        for l in self.layers:
+            n += (5 if l.kind == LINEAR else 4) + 4
+        return n
+
+    def decode_device(self):
+        """One decode step over the inputs already in the device buffers (x_in, cos, sin, position, active)."""
+        if self.use_graph and self.tp == 1:
+            if self._graph is None:
+                self._capture()
+            self._graph.replay()
+        else:
+            self._decode_layers()
+        return self.x
+
+    def _capture(self):
+        # One warm-up pass outside capture (per-device kernel attributes, module loading) with every
+        # row inactive: inactive rows keep their recurrent and conv states bit for bit and write their
+        # key/value only at the cache's last position, which no sequence reads (model.py:621).
+        active = self.active.clone()
+        self.active.zero_()
+        side = torch.cuda.Stream(device=self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self._decode_layers()
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        self.active.copy_(active)
+        self._graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self._graph):
+            self._decode_layers()
+
+    # ------------------------------------------------------------------ the reference's call
+    def __call__(self, inputs_embeds: torch.Tensor, **inputs: torch.Tensor) -> torch.Tensor:
+        if "save_slot" in inputs or "restore_slot" in inputs:
+            self.copy_states(inputs)
+            return inputs_embeds
+        if "accepted" in inputs:
+            raise NotImplementedError("verify steps are not built yet")
+        if "slot" in inputs:
+            raise NotImplementedError("prefill chunks are not built yet")
+        rows = inputs_embeds.shape[0]
+        if rows != self.batch or inputs_embeds.shape[1] != 1:
+            raise ValueError(f"decode takes [{self.batch}, 1, hidden], got {tuple(inputs_embeds.shape)}")
+        self.load_decode_inputs(inputs_embeds, inputs["cos"], inputs["sin"], inputs["position"], inputs["active"])
+        out = self.decode_device()
+        return out.to("cpu", non_blocking=False).reshape(rows, 1, -1)
+
+    def load_decode_inputs(self, embeds, cos, sin, position, active):
+        self.x_in.copy_(embeds.reshape(self.batch, -1), non_blocking=True)
+        self.cos.copy_(cos.reshape(self.batch, -1), non_blocking=True)
+        self.sin.copy_(sin.reshape(self.batch, -1), non_blocking=True)
+        self.position.copy_(position.reshape(-1).to(torch.int32), non_blocking=True)
+        self.active.copy_(active.reshape(-1).to(torch.float32), non_blocking=True)
+
+    def copy_states(self, inputs):
+        """Save one row's recurrent and conv states to its spare row or restore them (model.py:456-464)."""
+        if not self.saved:
+            raise ValueError("this step keeps no saved states")
+        to_saved = "save_slot" in inputs
+        slot = int((inputs["save_slot"] if to_saved else inputs["restore_slot"]).reshape(-1)[0])
+        src, dst = (slot, slot + self.batch) if to_saved else (slot + self.batch, slot)
+        for l in self.layers:
+            if l.kind == LINEAR:
+                l.mixer.state[dst].copy_(l.mixer.state[src])
+                l.mixer.conv_state[dst].copy_(l.mixer.conv_state[src])
+
+
+class B200Head:
+    """Final norm and the lm_head group maxima of one rank's vocab slice (HeadStep, model.py:863-900)."""
+
+    def __init__(self, cfg: TextConfig, head_weights: dict, batch_size: int, tp_degree: int = 1, rank: int = 0,
+                 device=None, group_rows: int = 32, process_group=None):
+        if group_rows != 32:
+            raise ValueError("the lm_head kernel takes groups of 32")
+        self.cfg, self.batch, self.tp, self.rank = cfg, batch_size, tp_degree, rank
+        self.group = process_group
+        self.device = torch.device(device or f"cuda:{torch.cuda.current_device()}")
+        shard = W.shard_head(cfg, head_weights, rank, tp_degree)
+        self.norm_w = shard["norm_weight"].to(self.device, BF16).contiguous()
+        # The kernel multiplies BF16 by BF16: the e4m3 * 2^s weights are exact in BF16.
+        self.lm_head = shard["lm_head"].to(self.device).dequant().to(BF16).contiguous()
+        self.vocab_local = self.lm_head.shape[0]
+        self.hidden = torch.zeros(batch_size, cfg.hidden_size, dtype=BF16, device=self.device)
+        self.xb = torch.zeros_like(self.hidden)
+        self.maxima = torch.zeros(batch_size, self.vocab_local // 32, dtype=torch.float32, device=self.device)
+        self.gathered = (torch.zeros(tp_degree, batch_size, self.vocab_local // 32, dtype=torch.float32, device=self.device)
+                         if tp_degree > 1 else None)
+
+    def maxima_device(self) -> torch.Tensor:
+        ops.rmsnorm_quant(self.hidden, self.norm_w, self.cfg.rms_norm_eps, y_bf16=self.xb)
+        ops.lm_head_groupmax(self.xb, self.lm_head, self.maxima)
+        if self.tp == 1:
+            return self.maxima
+        torch.distributed.all_gather_into_tensor(self.gathered, self.maxima, group=self.group)
+        return self.gathered.permute(1, 0, 2).reshape(self.batch, -1)
+
+    def run_graph(self, hidden: torch.Tensor) -> torch.Tensor:
+        rows = hidden.shape[0]
+        if rows != self.batch:
+            raise ValueError(f"the head graph takes {self.batch} rows, got {rows}")
+        self.hidden.copy_(hidden.reshape(rows, -1), non_blocking=True)
+        return self.maxima_device().to("cpu")

@@ -1,0 +1,207 @@
+"""Synthetic model weights and their tensor-parallel cut.
+
+Names follow the reference model's parameters (qwen38_inf2/model.py, as loaded by
+checkpoint.layer_weights, qwen38_inf2/checkpoint.py:185-224), with each FP8 linear held as an
+`FP8Weight` ([out, in] e4m3 bytes plus per-32 power-of-two scales) instead of the reference's
+[in, out] e5m2 `weight_fp8`. The cutting rules are the reference's: column-parallel matrices by
+output rows, row-parallel ones (down_proj, out_proj, o_proj) by input columns, in_proj_qkv and the
+conv weight block by block over [q | k | v] (checkpoint.py:150-174), plus KV-head replication when
+there are more ranks than KV heads.
+
+Values are seeded N(0, 0.02) for every matrix and vector (BASELINE configs 0 and 3), drawn per
+tensor from its own generator so any one layer can be regenerated alone, on CPU or on the GPU.
+"""
+
+from __future__ import annotations
+
+import hashlib
+from dataclasses import dataclass
+
+import torch
+
+from . import codec
+from .config import FULL, LINEAR, TextConfig
+
+STD = 0.02
+
+
+@dataclass
+class FP8Weight:
+    q: torch.Tensor  # uint8 [out, in], e4m3 bytes
+    scale: torch.Tensor  # float32 [out, in / 32], powers of two
+
+    @property
+    def shape(self) -> tuple[int, int]:
+        return tuple(self.q.shape)
+
+    def dequant(self) -> torch.Tensor:
+        return codec.dequantize_mx_e4m3(self.q, self.scale)
+
+    def rows(self, start: int, end: int) -> "FP8Weight":
+        return FP8Weight(self.q[start:end], self.scale[start:end])
+
+    def cols(self, start: int, end: int) -> "FP8Weight":
+        if start % codec.GROUP or end % codec.GROUP:
+            raise ValueError("a column cut must land on a 32-column scale group")
+        return FP8Weight(self.q[:, start:end], self.scale[:, start // codec.GROUP : end // codec.GROUP])
+
+    def to(self, device) -> "FP8Weight":
+        return FP8Weight(self.q.to(device), self.scale.to(device))
+
+    @staticmethod
+    def cat_rows(parts: list["FP8Weight"]) -> "FP8Weight":
+        return FP8Weight(torch.cat([p.q for p in parts]).contiguous(), torch.cat([p.scale for p in parts]).contiguous())
+
+    @staticmethod
+    def from_float(w: torch.Tensor) -> "FP8Weight":
+        q, s = codec.quantize_mx_e4m3(w)
+        return FP8Weight(q, s)
+
+
+def _seed(seed: int, name: str) -> int:
+    return int.from_bytes(hashlib.sha256(f"{seed}:{name}".encode()).digest()[:8], "little") & ((1 << 63) - 1)
+
+
+def _normal(shape, seed: int, name: str, device, std: float = STD) -> torch.Tensor:
+    gen = torch.Generator(device=device)
+    gen.manual_seed(_seed(seed, name))
+    return torch.randn(*shape, generator=gen, device=device, dtype=torch.float32) * std
+
+
+def _fp8(shape, seed, name, device, std=STD) -> FP8Weight:
+    # Drawn in row pieces so a 17408 x 5120 matrix never needs a second full fp32 copy.
+    rows, cols = shape
+    piece = max(1, (1 << 26) // cols)
+    qs, ss = [], []
+    gen = torch.Generator(device=device)
+    gen.manual_seed(_seed(seed, name))
+    for first in range(0, rows, piece):
+        n = min(piece, rows - first)
+        w = torch.randn(n, cols, generator=gen, device=device, dtype=torch.float32) * std
+        q, s = codec.quantize_mx_e4m3(w)
+        qs.append(q)
+        ss.append(s)
+    return FP8Weight(torch.cat(qs), torch.cat(ss))
+
+
+def _bf16(shape, seed, name, device, std=STD) -> torch.Tensor:
+    return _normal(shape, seed, name, device, std).to(torch.bfloat16)
+
+
+def synthetic_layer(cfg: TextConfig, index: int, seed: int = 0, device="cpu", std: float = STD) -> dict:
+    """All of one decoder layer's weights, unsharded, named as the reference's parameters."""
+    h, inter = cfg.hidden_size, cfg.intermediate_size
+    p = f"layers.{index}"
+    out = {
+        f"{p}.input_layernorm_weight": _bf16((h,), seed, f"{p}.input_layernorm", device, std),
+        f"{p}.post_attention_layernorm_weight": _bf16((h,), seed, f"{p}.post_attention_layernorm", device, std),
+        f"{p}.mlp.gate_proj": _fp8((inter, h), seed, f"{p}.mlp.gate_proj", device, std),
+        f"{p}.mlp.up_proj": _fp8((inter, h), seed, f"{p}.mlp.up_proj", device, std),
+        f"{p}.mlp.down_proj": _fp8((h, inter), seed, f"{p}.mlp.down_proj", device, std),
+    }
+    if cfg.layer_types[index] == LINEAR:
+        la = f"{p}.linear_attn"
+        hv = cfg.linear_num_value_heads
+        out |= {
+            f"{la}.in_proj_qkv": _fp8((cfg.linear_conv_dim, h), seed, f"{la}.in_proj_qkv", device, std),
+            f"{la}.in_proj_z": _fp8((cfg.linear_value_dim, h), seed, f"{la}.in_proj_z", device, std),
+            f"{la}.out_proj": _fp8((h, cfg.linear_value_dim), seed, f"{la}.out_proj", device, std),
+            f"{la}.in_proj_b": _bf16((hv, h), seed, f"{la}.in_proj_b", device, std),
+            f"{la}.in_proj_a": _bf16((hv, h), seed, f"{la}.in_proj_a", device, std),
+            f"{la}.conv_weight": _bf16((cfg.linear_conv_dim, cfg.linear_conv_kernel_dim), seed, f"{la}.conv1d", device, std),
+            f"{la}.A_log": _bf16((hv,), seed, f"{la}.A_log", device, std),
+            f"{la}.dt_bias": _bf16((hv,), seed, f"{la}.dt_bias", device, std),
+            f"{la}.norm_weight": _bf16((cfg.linear_value_head_dim,), seed, f"{la}.norm", device, std),
+        }
+    elif cfg.layer_types[index] == FULL:
+        sa = f"{p}.self_attn"
+        hd = cfg.head_dim
+        out |= {
+            f"{sa}.q_proj": _fp8((cfg.num_attention_heads * hd * 2, h), seed, f"{sa}.q_proj", device, std),
+            f"{sa}.k_proj": _fp8((cfg.num_key_value_heads * hd, h), seed, f"{sa}.k_proj", device, std),
+            f"{sa}.v_proj": _fp8((cfg.num_key_value_heads * hd, h), seed, f"{sa}.v_proj", device, std),
+            f"{sa}.o_proj": _fp8((h, cfg.num_attention_heads * hd), seed, f"{sa}.o_proj", device, std),
+            f"{sa}.q_norm_weight": _bf16((hd,), seed, f"{sa}.q_norm", device, std),
+            f"{sa}.k_norm_weight": _bf16((hd,), seed, f"{sa}.k_norm", device, std),
+        }
+    else:
+        raise ValueError(f"unknown layer type {cfg.layer_types[index]}")
+    return out
+
+
+def synthetic_head(cfg: TextConfig, seed: int = 0, device="cpu", std: float = STD) -> dict:
+    """Final norm and lm_head ``[vocab, hidden]``."""
+    return {
+        "norm_weight": _bf16((cfg.hidden_size,), seed, "model.norm", device, std),
+        "lm_head": _fp8((cfg.vocab_size, cfg.hidden_size), seed, "lm_head", device, std),
+    }
+
+
+def embedding_rows(cfg: TextConfig, token_ids, seed: int = 0, std: float = STD) -> torch.Tensor:
+    """Rows of a seeded N(0, std) embedding table ``[vocab, hidden]``, generated per token, bf16 on CPU."""
+    rows = [_normal((cfg.hidden_size,), seed, f"embed.{int(t)}", "cpu", std) for t in token_ids]
+    return torch.stack(rows).to(torch.bfloat16)
+
+
+# ----------------------------------------------------------------------------------------------
+# Tensor-parallel cut (qwen38_inf2/checkpoint.py:150-224)
+# ----------------------------------------------------------------------------------------------
+def _span(total: int, rank: int, tp: int) -> tuple[int, int]:
+    size = total // tp
+    return rank * size, (rank + 1) * size
+
+
+def _rows(t, rank, tp):
+    a, b = _span(t.shape[0], rank, tp)
+    return t.rows(a, b) if isinstance(t, FP8Weight) else t[a:b]
+
+
+def _cols(t: FP8Weight, rank, tp):
+    a, b = _span(t.shape[1], rank, tp)
+    return t.cols(a, b)
+
+
+def _qkv_rows(t, cfg: TextConfig, rank: int, tp: int):
+    kd, vd = cfg.linear_key_dim, cfg.linear_value_dim
+    blocks = [(0, kd), (kd, 2 * kd), (2 * kd, 2 * kd + vd)]
+    parts = []
+    for first, last in blocks:
+        a, b = _span(last - first, rank, tp)
+        parts.append(t.rows(first + a, first + b) if isinstance(t, FP8Weight) else t[first + a : first + b])
+    return FP8Weight.cat_rows(parts) if isinstance(t, FP8Weight) else torch.cat(parts)
+
+
+def _kv_rows(t, cfg: TextConfig, rank: int, tp: int):
+    hd = cfg.head_dim
+    first = cfg.kv_head_of_rank(rank, tp)
+    n = cfg.kv_heads_per_rank(tp)
+    return t.rows(first * hd, (first + n) * hd)
+
+
+def shard_layer(cfg: TextConfig, weights: dict, index: int, rank: int, tp: int) -> dict:
+    """One rank's share of layer `index`'s weights (all names kept)."""
+    p = f"layers.{index}"
+    out = {}
+    for name, t in weights.items():
+        if not name.startswith(p + "."):
+            continue
+        leaf = name[len(p) + 1 :]
+        if tp == 1 or leaf.endswith("norm_weight"):
+            out[name] = t
+        elif leaf in ("mlp.gate_proj", "mlp.up_proj", "linear_attn.in_proj_z", "linear_attn.in_proj_b",
+                      "linear_attn.in_proj_a", "linear_attn.A_log", "linear_attn.dt_bias", "self_attn.q_proj"):
+            out[name] = _rows(t, rank, tp)
+        elif leaf in ("mlp.down_proj", "linear_attn.out_proj", "self_attn.o_proj"):
+            out[name] = _cols(t, rank, tp)
+        elif leaf in ("linear_attn.in_proj_qkv", "linear_attn.conv_weight"):
+            out[name] = _qkv_rows(t, cfg, rank, tp)
+        elif leaf in ("self_attn.k_proj", "self_attn.v_proj"):
+            out[name] = _kv_rows(t, cfg, rank, tp)
+        else:
+            raise KeyError(f"no TP rule for {name}")
+    return out
+
+
+def shard_head(cfg: TextConfig, head: dict, rank: int, tp: int) -> dict:
+    a, b = _span(cfg.vocab_size, rank, tp)
+    return {"norm_weight": head["norm_weight"], "lm_head": head["lm_head"].rows(a, b)}

@@ -1,0 +1,39 @@
+"""The C-ABI library loads without a GPU and exports every function include/q38.h declares."""
+
+import re
+from pathlib import Path
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "q38.h"
+
+
+def declared_functions() -> set[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"^\s*(?:int|size_t)\s+(q38_\w+)\s*\(", text, flags=re.M))
+
+
+def test_header_declares_the_hot_path():
+    names = declared_functions()
+    for required in ("q38_fp8_gemm", "q38_gdn_decode", "q38_attn_decode", "q38_lm_head_groupmax", "q38_rmsnorm_quant"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib_mod = __import__(pkg.__name__ + "._lib", fromlist=["_lib"])
+    lib = lib_mod.load()
+    names = declared_functions()
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+    assert set(names) <= set(lib_mod.SIGNATURES), set(names) - set(lib_mod.SIGNATURES)
+    assert lib.q38_abi_version() >= 1
+
+
+def test_host_side_argument_checks_need_no_gpu(pkg):
+    """Bad arguments are refused on the host, before any CUDA call."""
+    lib_mod = __import__(pkg.__name__ + "._lib", fromlist=["_lib"])
+    lib = lib_mod.load()
+    assert lib.q38_fp8_gemm(None, 1, 128, None, None, 128, 0, None, 128, None, 0, 1, None, 0, None) == -1
+    assert "null pointer" in lib_mod.last_error()
+    assert lib.q38_sf_tile_bytes(5120, 17408) == 40 * 136 * 512
+    assert lib.q38_fp8_gemm_workspace_bytes(256, 5120, 1) == 0
+    assert lib.q38_fp8_gemm_workspace_bytes(256, 5120, 3) == 256 + 3 * 40 * 128 * 256 * 4

@@ -1,0 +1,113 @@
+"""The CPU oracle against golden vectors made by the reference itself (tests/golden/make_golden.py).
+
+These pin the oracle: every later GPU parity test compares the CUDA path with this oracle, so the
+oracle must first reproduce the reference's own outputs on the same inputs.
+"""
+
+import hashlib
+from pathlib import Path
+
+import pytest
+import torch
+from safetensors import safe_open
+
+from oracle import cpu_model as om
+
+GOLDEN = Path(__file__).resolve().parent / "golden" / "tiny_block.safetensors"
+
+
+def _digest(pkg, weights):
+    h = hashlib.sha256()
+    for name in sorted(weights):
+        t = weights[name]
+        parts = (t.q, t.scale) if isinstance(t, pkg.weights.FP8Weight) else (t,)
+        for p in parts:
+            h.update(name.encode())
+            h.update(p.contiguous().view(torch.uint8).numpy().tobytes())
+    return h.hexdigest()
+
+
+@pytest.fixture(scope="module")
+def golden():
+    with safe_open(str(GOLDEN), "pt") as f:
+        return {k: f.get_tensor(k) for k in f.keys()}, f.metadata()
+
+
+@pytest.fixture(scope="module")
+def tiny(pkg, golden):
+    tensors, meta = golden
+    cfg = pkg.config.tiny_config(num_blocks=1)
+    seed, std = int(meta["seed"]), float(meta["std"])
+    weights = {}
+    for i in range(cfg.num_hidden_layers):
+        weights |= pkg.weights.synthetic_layer(cfg, i, seed, "cpu", std)
+    head = pkg.weights.synthetic_head(cfg, seed, "cpu", std)
+    assert _digest(pkg, weights) == meta["weights_sha256"], "synthetic weights drifted from the fixture"
+    assert _digest(pkg, head) == meta["head_sha256"]
+    return cfg, weights, head, meta
+
+
+def _inputs(tensors, prefix):
+    keys = ("cos", "sin", "position", "active", "slot", "start", "n_valid")
+    return {k: tensors[f"{prefix}.{k}"] for k in keys if f"{prefix}.{k}" in tensors}
+
+
+def test_oracle_reproduces_reference_decode_prefill_and_states(golden, tiny):
+    tensors, _ = golden
+    cfg, weights, _, meta = tiny
+    step = om.OracleStep(cfg, weights, int(meta["max_seq"]), int(meta["batch"]))
+    worst = 0.0
+    for s in range(int(meta["decode_steps"])):
+        y = step(inputs_embeds=tensors[f"decode{s}.x"], **_inputs(tensors, f"decode{s}"))
+        want = tensors[f"decode{s}.y"]
+        active = tensors[f"decode{s}.active"] > 0.5
+        worst = max(worst, (y[active].float() - want[active].float()).abs().max().item())
+    for c in range(2):
+        y = step(inputs_embeds=tensors[f"prefill{c}.x"], **_inputs(tensors, f"prefill{c}"))
+        n = int(tensors[f"prefill{c}.n_valid"])
+        worst = max(worst, (y[:, :n].float() - tensors[f"prefill{c}.y"][:, :n].float()).abs().max().item())
+    y = step(inputs_embeds=tensors["after.x"], **_inputs(tensors, "after"))
+    worst = max(worst, (y.float() - tensors["after.y"].float()).abs().max().item())
+    assert worst == 0.0, f"oracle differs from the reference by {worst}"
+
+    # Final recurrent, conv and KV states, except the KV cache's junk tail (written by inactive rows).
+    for i, (kind, mixer, *_rest) in enumerate(step.layers):
+        if kind == om.LINEAR:
+            assert torch.equal(mixer.recurrent_state, tensors[f"state.layers.{i}.linear_attn.recurrent_state"])
+            assert torch.equal(mixer.conv_state, tensors[f"state.layers.{i}.linear_attn.conv_state"])
+        else:
+            tail = int(meta["chunk"])
+            assert torch.equal(mixer.k_cache[:, :, :-tail], tensors[f"state.layers.{i}.self_attn.k_cache"][:, :, :-tail])
+            assert torch.equal(mixer.v_cache[:, :, :-tail], tensors[f"state.layers.{i}.self_attn.v_cache"][:, :, :-tail])
+
+
+def test_oracle_head_maxima_match_reference(golden, tiny):
+    tensors, _ = golden
+    cfg, _, head, _ = tiny
+    got = om.head_maxima(cfg, tensors["head.hidden"], head["norm_weight"], head["lm_head"].q, head["lm_head"].scale)
+    assert torch.equal(got, tensors["head.maxima"])
+
+
+def test_oracle_kernels_match_reference(golden):
+    tensors, _ = golden
+    d = {k.split(".", 1)[1]: v for k, v in tensors.items() if k.startswith("delta.")}
+    out, s1 = om.chunked_gated_delta(d["q"], d["k"], d["v"], d["g"], d["b"], d["s0"], chunk=32)
+    assert torch.equal(out, d["out"]) and torch.equal(s1, d["s1"])
+    assert torch.equal(om.unit_lower_inverse(tensors["inverse.lower"]), tensors["inverse.out"])
+    got = om.blocked_attention(tensors["attn.q"], tensors["attn.k"], tensors["attn.v"], tensors["attn.visible"], 16)
+    assert torch.equal(got, tensors["attn.out"])
+
+
+def test_chunked_rule_matches_recurrent_rule():
+    """The property the reference tests (tests/test_prefill.py:29-49), here on the oracle."""
+    torch.manual_seed(0)
+    heads, tokens, dim = 3, 128, 32
+    q = torch.nn.functional.normalize(torch.randn(heads, tokens, dim), dim=-1) / dim**0.5
+    k = torch.nn.functional.normalize(torch.randn(heads, tokens, dim), dim=-1)
+    v = torch.randn(heads, tokens, dim)
+    g = -torch.rand(heads, tokens) * 0.5
+    b = torch.rand(heads, tokens)
+    s = torch.randn(heads, dim, dim)
+    want_o, want_s = om.recurrent_gated_delta(q, k, v, g, b, s)
+    got_o, got_s = om.chunked_gated_delta(q, k, v, g, b, s, chunk=64)
+    assert (got_o - want_o).abs().max() < 1e-3 and (got_s - want_s).abs().max() < 1e-3

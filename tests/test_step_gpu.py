@@ -1,0 +1,154 @@
+"""B200Step / B200Head through the reference's call, against the reference's golden vectors and the oracle.
+
+Tolerances: hidden states within 2e-2 relative (per row, of the row's largest
+value, and 1e-2 in relative L2), gated-delta state within 1e-2, greedy token ids identical.
+"""
+
+from pathlib import Path
+
+import pytest
+import torch
+from safetensors import safe_open
+
+from oracle import cpu_model as om
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden" / "tiny_block.safetensors"
+
+
+def assert_hidden_close(got, want, what=""):
+    got, want = got.float().reshape(want.shape[0], -1), want.float().reshape(want.shape[0], -1)
+    assert torch.isfinite(got).all(), f"{what}: non-finite"
+    peak = want.abs().amax(-1, keepdim=True).clamp_min(1e-6)
+    worst = ((got - want).abs() / peak).max().item()
+    rel_l2 = ((got - want).norm(dim=-1) / want.norm(dim=-1).clamp_min(1e-12)).max().item()
+    assert worst <= 2e-2 and rel_l2 <= 1e-2, f"{what}: max {worst:.3g} of the row peak, relative L2 {rel_l2:.3g}"
+
+
+@pytest.fixture(scope="module")
+def golden():
+    with safe_open(str(GOLDEN), "pt") as f:
+        return {k: f.get_tensor(k) for k in f.keys()}, f.metadata()
+
+
+@pytest.fixture(scope="module")
+def step_mod(pkg):
+    return __import__(pkg.__name__ + ".step", fromlist=["step"])
+
+
+def tiny_weights(pkg, meta):
+    cfg = pkg.config.tiny_config(num_blocks=1)
+    w = {}
+    for i in range(cfg.num_hidden_layers):
+        w |= pkg.weights.synthetic_layer(cfg, i, int(meta["seed"]), "cpu", float(meta["std"]))
+    return cfg, w
+
+
+def _decode_inputs(tensors, s):
+    return {k: tensors[f"decode{s}.{k}"] for k in ("cos", "sin", "position", "active")}
+
+
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_tiny_decode_matches_reference_golden(pkg, step_mod, golden, use_graph):
+    tensors, meta = golden
+    cfg, w = tiny_weights(pkg, meta)
+    step = step_mod.B200Step(cfg, w, int(meta["max_seq"]), int(meta["batch"]), use_graph=use_graph)
+    oracle = om.OracleStep(cfg, w, int(meta["max_seq"]), int(meta["batch"]))
+    for s in range(int(meta["decode_steps"])):
+        inputs = _decode_inputs(tensors, s)
+        y = step(inputs_embeds=tensors[f"decode{s}.x"], **inputs)
+        want = tensors[f"decode{s}.y"]
+        oracle(inputs_embeds=tensors[f"decode{s}.x"], **inputs)
+        on = inputs["active"] > 0.5
+        assert_hidden_close(y[on], want[on], what=f"decode step {s}")
+    for l, (kind, mixer, *_r) in zip(step.layers, oracle.layers):
+        if kind == om.LINEAR:
+            d = (l.mixer.state.cpu().float() - mixer.recurrent_state.float()).abs().max().item()
+            assert d < 1e-2, f"gated-delta state differs by {d}"
+        else:
+            keep = slice(0, int(meta["max_seq"]) - 1)  # the last position is the inactive rows' junk slot
+            d = (l.mixer.k_cache.cpu()[:, :, keep].float() - mixer.k_cache[:, :, keep].float()).abs().max().item()
+            assert d <= 2e-2 * mixer.k_cache.float().abs().max().item()
+
+
+def test_tiny_graph_replay_equals_eager(pkg, step_mod, golden):
+    tensors, meta = golden
+    cfg, w = tiny_weights(pkg, meta)
+    outs = {}
+    for use_graph in (False, True):
+        step = step_mod.B200Step(cfg, w, int(meta["max_seq"]), int(meta["batch"]), use_graph=use_graph)
+        outs[use_graph] = [step(inputs_embeds=tensors[f"decode{s}.x"], **_decode_inputs(tensors, s)) for s in range(4)]
+    for a, b in zip(outs[False], outs[True]):
+        assert torch.equal(a, b)
+
+
+def test_tiny_greedy_tokens_match_oracle(pkg, step_mod, golden):
+    """A greedy loop through B200Step + B200Head + the host recheck gives the oracle's tokens."""
+    tensors, meta = golden
+    cfg, w = tiny_weights(pkg, meta)
+    seed, std, batch, max_seq = int(meta["seed"]), float(meta["std"]), 3, int(meta["max_seq"])
+    head_w = pkg.weights.synthetic_head(cfg, seed, "cpu", std)
+    lm_rows = head_w["lm_head"].dequant()
+    step = step_mod.B200Step(cfg, w, max_seq, batch)
+    head = step_mod.B200Head(cfg, head_w, batch)
+    oracle = om.OracleStep(cfg, w, max_seq, batch)
+    prompts = [[3, 17, 42, 99, 5], [9, 9, 4], [77, 78, 79, 80, 1, 2]]
+    got, want = {r: list(p) for r, p in enumerate(prompts)}, {r: list(p) for r, p in enumerate(prompts)}
+    for pos in range(14):
+        for run, seqs in (("gpu", got), ("oracle", want)):
+            ids = [seqs[r][pos] for r in range(batch)]
+            emb = pkg.weights.embedding_rows(cfg, ids, seed, std).reshape(batch, 1, -1)
+            cos, sin = om.rotary(cfg, torch.full((batch,), pos), torch.bfloat16)
+            inputs = dict(cos=cos.unsqueeze(1), sin=sin.unsqueeze(1), position=torch.full((batch,), pos, dtype=torch.int32),
+                          active=torch.ones(batch))
+            if run == "gpu":
+                hidden = step(inputs_embeds=emb, **inputs)
+                maxima = head.run_graph(hidden)
+            else:
+                hidden = oracle(inputs_embeds=emb, **inputs)
+                maxima = om.head_maxima(cfg, hidden, head_w["norm_weight"], head_w["lm_head"].q, head_w["lm_head"].scale)
+            tokens = om.recheck_tokens(cfg, hidden, head_w["norm_weight"], lm_rows, maxima)
+            for r in range(batch):
+                if pos + 1 >= len(seqs[r]):
+                    seqs[r].append(tokens[r])
+    assert got == want
+
+
+def test_config0_full_width_block_decode_matches_oracle(pkg, step_mod):
+    """one full-width 4-layer block (3 gated-delta + 1 attention), batch 8 decode rows at
+    positions uniform in [0, 512) over seeded cache and state contents, two steps."""
+    cfg = pkg.config.full_config(num_blocks=1)
+    batch, max_seq = 8, 512
+    w = {}
+    for i in range(cfg.num_hidden_layers):
+        w |= pkg.weights.synthetic_layer(cfg, i, seed=0, device="cuda")
+    step = step_mod.B200Step(cfg, w, max_seq, batch)
+    wc = {k: (v.to("cpu") if hasattr(v, "to") else v) for k, v in w.items()}
+    oracle = om.OracleStep(cfg, wc, max_seq, batch)
+    gen = torch.Generator().manual_seed(0)
+    for l, (kind, mixer, *_r) in zip(step.layers, oracle.layers):
+        if kind == om.LINEAR:
+            mixer.recurrent_state.copy_((torch.randn(mixer.recurrent_state.shape, generator=gen) * 0.1).to(torch.bfloat16))
+            mixer.conv_state.copy_(torch.randn(mixer.conv_state.shape, generator=gen).to(torch.bfloat16))
+            l.mixer.state.copy_(mixer.recurrent_state)
+            l.mixer.conv_state.copy_(mixer.conv_state)
+        else:
+            mixer.k_cache.copy_(torch.randn(mixer.k_cache.shape, generator=gen).to(torch.bfloat16))
+            mixer.v_cache.copy_(torch.randn(mixer.v_cache.shape, generator=gen).to(torch.bfloat16))
+            l.mixer.k_cache.copy_(mixer.k_cache)
+            l.mixer.v_cache.copy_(mixer.v_cache)
+    position = torch.randint(0, max_seq - 2, (batch,), generator=gen, dtype=torch.int32)
+    tokens = torch.randint(0, cfg.vocab_size, (batch,), generator=gen)
+    for s in range(2):
+        emb = pkg.weights.embedding_rows(cfg, tokens.tolist()).reshape(batch, 1, -1)
+        cos, sin = om.rotary(cfg, position, torch.bfloat16)
+        inputs = dict(cos=cos.unsqueeze(1), sin=sin.unsqueeze(1), position=position, active=torch.ones(batch))
+        y = step(inputs_embeds=emb, **inputs)
+        want = oracle(inputs_embeds=emb, **inputs)
+        assert_hidden_close(y, want, what=f"config 0 step {s}")
+        position = position + 1
+        tokens = (tokens * 31 + 7) % cfg.vocab_size
+    for l, (kind, mixer, *_r) in zip(step.layers, oracle.layers):
+        if kind == om.LINEAR:
+            d = (l.mixer.state.cpu().float() - mixer.recurrent_state.float()).abs().max().item()
+            assert d < 1e-2, f"gated-delta state differs by {d}"
