@@ -92,6 +92,9 @@ class Linear:
     q: torch.Tensor
     scale: torch.Tensor
     _w: dict = field(default_factory=dict)
+    # Accumulate as an fp32 matmul instead of the BF16 one (same values, another summation order):
+    # used only to measure how much the model's output moves under a legitimate reordering.
+    fp32: bool = False
 
     def weight(self, dtype) -> torch.Tensor:
         if dtype not in self._w:
@@ -100,6 +103,8 @@ class Linear:
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         x = fp8_round(x)
+        if self.fp32:
+            return F.linear(x.float(), self.weight(torch.float32)).to(x.dtype)
         return F.linear(x, self.weight(x.dtype))
 
 
@@ -426,7 +431,7 @@ class OracleStep:
     """
 
     def __init__(self, cfg, weights: dict, max_seq_len: int, batch_size: int = 1, tp_degree: int = 1, rank: int = 0,
-                 all_reduce=None, dtype=torch.bfloat16, saved_states: bool = False):
+                 all_reduce=None, dtype=torch.bfloat16, saved_states: bool = False, linear_fp32: bool = False):
         self.cfg, self.dtype = cfg, dtype
         self.all_reduce = all_reduce or (lambda t: t)
         self.layers = []
@@ -436,6 +441,12 @@ class OracleStep:
                      else AttentionLayer(cfg, weights, p, tp_degree, rank, batch_size, max_seq_len, dtype))
             self.layers.append((kind, mixer, MLPLayer(weights, p), weights[f"{p}.input_layernorm_weight"].cpu().to(dtype),
                                 weights[f"{p}.post_attention_layernorm_weight"].cpu().to(dtype)))
+        if linear_fp32:
+            for _, mixer, mlp, *_r in self.layers:
+                for obj in (mixer, mlp):
+                    for v in vars(obj).values():
+                        if isinstance(v, Linear):
+                            v.fp32 = True
 
     def __call__(self, inputs_embeds, cos=None, sin=None, position=None, active=None, slot=None, start=None,
                  n_valid=None, save_slot=None, restore_slot=None, accepted=None):
@@ -447,17 +458,22 @@ class OracleStep:
                 if kind == LINEAR:
                     mixer.copy_states(int(which.reshape(-1)[0]), save_slot is not None)
             return inputs_embeds
-        eps = self.cfg.rms_norm_eps
         x = inputs_embeds.to(self.dtype)
-        for kind, mixer, mlp, w_in, w_post in self.layers:
-            h = rms_norm(x, w_in, eps)
-            if slot is not None:
-                m = mixer.prefill(h, slot, start, n_valid) if kind == LINEAR else mixer.prefill(h, cos, sin, slot, start, n_valid)
-            else:
-                m = mixer.decode(h, position, active) if kind == LINEAR else mixer.decode(h, cos, sin, position, active)
-            x = x + self.all_reduce(m)
-            x = x + self.all_reduce(mlp(rms_norm(x, w_post, eps)))
+        for i in range(len(self.layers)):
+            x = self.layer(i, x, cos, sin, position, active, slot, start, n_valid)
         return x
+
+    def layer(self, i, x, cos=None, sin=None, position=None, active=None, slot=None, start=None, n_valid=None):
+        """DecoderLayer.forward (model.py:918-930) for layer i alone."""
+        eps = self.cfg.rms_norm_eps
+        kind, mixer, mlp, w_in, w_post = self.layers[i]
+        h = rms_norm(x, w_in, eps)
+        if slot is not None:
+            m = mixer.prefill(h, slot, start, n_valid) if kind == LINEAR else mixer.prefill(h, cos, sin, slot, start, n_valid)
+        else:
+            m = mixer.decode(h, position, active) if kind == LINEAR else mixer.decode(h, cos, sin, position, active)
+        x = x + self.all_reduce(m)
+        return x + self.all_reduce(mlp(rms_norm(x, w_post, eps)))
 
 
 # ---------------------------------------------------------------------------------------------

@@ -173,10 +173,18 @@ class B200Step:
         self.x.add_(self.partial)
 
     def _decode_layers(self):
-        cfg, B, eps = self.cfg, self.batch, self.cfg.rms_norm_eps
-        tp = self.tp
         self.x.copy_(self.x_in)
         for l in self.layers:
+            self._decode_layer(l)
+
+    def run_layer(self, i: int) -> None:
+        """Layer i alone, eagerly, on self.x and the loaded decode inputs (for layer-by-layer checks)."""
+        self._decode_layer(self.layers[i])
+
+    def _decode_layer(self, l: _Layer):
+        cfg, B, eps = self.cfg, self.batch, self.cfg.rms_norm_eps
+        tp = self.tp
+        if True:
             m = l.mixer
             if l.kind == LINEAR:
                 ops.rmsnorm_quant(self.x, l.ln_in, eps, y_bf16=self.hb, y_e5m2=self.hq)
