@@ -354,8 +354,71 @@ def run_reference(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+def run_micro(args):
+    """One kernel alone, for profiling and per-kernel rooflines: `gdn` (BASELINE config 2 decode shape,
+    48 value heads, dk = dv = 128) or `gemm` (config 1, the down_proj shape 17408 -> 5120)."""
+    pkg = importlib.import_module(PACKAGE)
+    ops = importlib.import_module(f"{PACKAGE}.ops")
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    cfg = pkg.config.full_config(1)
+    B = args.batch
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(3)
+    bf = lambda *s: (torch.randn(*s, device=dev, generator=gen)).to(torch.bfloat16)  # noqa: E731
+    peak, peak_kind = peaks()
+    if args.micro == "gdn":
+        hv, dk, dv = cfg.linear_num_value_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim
+        conv_dim = cfg.linear_conv_dim
+        states = [(bf(B, hv, dk, dv) * 0.1, bf(B, conv_dim, 3)) for _ in range(args.copies)]
+        qkvz, ab = bf(B, conv_dim + cfg.linear_value_dim), bf(B, 2 * hv)
+        conv_w, a_log, dt, nw = bf(conv_dim, 4) * 0.1, bf(hv) * 0.1, bf(hv) * 0.1, bf(dv) * 0.1
+        pos = torch.randint(1, 500, (B,), device=dev, dtype=torch.int32)
+        act = torch.ones(B, device=dev)
+        out = torch.empty(B, cfg.linear_value_dim, dtype=torch.uint8, device=dev)
+
+        def launch(i):
+            st, cs = states[i % len(states)]
+            ops.gdn_decode(qkvz, ab, cs, conv_w, a_log, dt, nw, st, pos, act, out, batch=B, num_k_heads=cfg.linear_num_key_heads,
+                           num_v_heads=hv, head_k=dk, head_v=dv, eps=1e-6)
+        per = B * hv * dk * dv * 2 * 2 + B * conv_dim * 3 * 2 * 2 + B * (conv_dim + cfg.linear_value_dim + 2 * hv) * 2 + B * cfg.linear_value_dim
+        unit, bound = "GB/s", "hbm"
+    else:
+        k, n = cfg.intermediate_size // args.tp, cfg.hidden_size
+        lins = [ops.DeviceLinear(pkg.weights.FP8Weight.from_float(torch.randn(n, k, device=dev, generator=gen) * 0.02), dev)
+                for _ in range(args.copies)]
+        x = pkg.codec.to_e5m2_bytes(bf(B, k))
+        y = torch.empty(B, n, dtype=torch.bfloat16, device=dev)
+        splits = ops.choose_splits(B, n, k)
+        ws = torch.zeros(max(256, ops.gemm_workspace_bytes(B, n, splits)), dtype=torch.uint8, device=dev)
+
+        def launch(i):
+            ops.fp8_gemm(x, lins[i % len(lins)], y, splits=splits, workspace=ws)
+        per = n * k + n * (k // 32) + B * k + B * n * 2
+        unit, bound = "GB/s", "hbm"
+    for i in range(args.warmup):
+        launch(i)
+    torch.cuda.synchronize()
+    events = []
+    for i in range(args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        launch(i)
+        b.record()
+        events.append((a, b))
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in events) / len(events)
+    achieved = per / (ms * 1e-3) / 1e9
+    print(json.dumps({"micro": args.micro, "batch": B, "launch_ms": ms, "bytes_per_launch": per,
+                      "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": unit,
+                                   "frac": achieved / peak}}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--micro", choices=["gdn", "gemm"], help="time one kernel alone (profiling) instead of the step")
+    ap.add_argument("--copies", type=int, default=4, help="--micro: distinct weight/state copies cycled (defeat L2)")
+    ap.add_argument("--tp", type=int, default=1, help="--micro gemm: K = 17408 / tp")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
@@ -366,6 +429,9 @@ def main():
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     world, rank, local = dist_env()
+    if args.micro:
+        run_micro(args)
+        return
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}; launch N>1 with torch.distributed.run")
     if args.impl == "reference":
