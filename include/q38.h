@@ -74,6 +74,22 @@ int q38_fp8_gemm(const void* x, int64_t tokens, int64_t k, const void* w, const 
                  int epilogue, void* y, int64_t ldy, const void* residual, int64_t ldr, int splits, void* workspace,
                  size_t workspace_bytes, q38_stream_t stream);
 
+/*
+ * q38_fp8_gemm without a caller workspace, for callers that cannot allocate device memory: hosts whose
+ * memory is owned by a framework pool, plugins that must not synchronise the device, and FFI bindings
+ * that carry only input and output pointers. This entry point has no counterpart in the reference.
+ * The split-K partial sums go to a fixed array inside the library, Q38_STATIC_SCRATCH_BYTES on every
+ * GPU that loads it (kept until exit); a shape whose q38_fp8_gemm_workspace_bytes exceeds that is
+ * refused with Q38_ERR_ARG. The first call on a device looks the array's address up once
+ * (cudaGetSymbolAddress), so make that first call before any stream capture. All calls share the
+ * one array: calls that overlap on the GPU (other streams, other host threads) race on it.
+ * Arguments are those of q38_fp8_gemm without workspace and workspace_bytes.
+ */
+#define Q38_STATIC_SCRATCH_BYTES (16 * 1024 * 1024)
+int q38_fp8_gemm_static_scratch(const void* x, int64_t tokens, int64_t k, const void* w, const void* w_sf,
+                                int64_t features, int epilogue, void* y, int64_t ldy, const void* residual,
+                                int64_t ldr, int splits, q38_stream_t stream);
+
 /* Bytes of the pre-tiled scale array of a [features, k] weight. */
 size_t q38_sf_tile_bytes(int64_t features, int64_t k);
 

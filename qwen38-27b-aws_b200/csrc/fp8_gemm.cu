@@ -395,3 +395,68 @@ extern "C" int q38_lm_head_groupmax(const void* x, int64_t rows, int64_t k, cons
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return ntok == 256 ? launch_gemm<256, false>(tw, tx, a, grid, s) : launch_gemm<128, false>(tw, tx, a, grid, s);
 }
+
+// ------------------------------------------------------------------------------------------------
+// q38_fp8_gemm_static_scratch: the same GEMM for callers that cannot allocate device memory.
+//
+// Some callers cannot hand this library a workspace: a host whose device memory belongs to a
+// framework pool that allows no allocations of its own, a plugin that must not synchronise the
+// device (cudaMalloc and cudaFree do), or a thin binding (ctypes, cgo, JNI) that carries device
+// pointers for inputs and outputs but has no allocator. For them the split-K partial sums live in a
+// fixed array compiled into the library, Q38_STATIC_SCRATCH_BYTES per GPU, which every GPU that
+// loads the library keeps until the process exits.
+// ------------------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+
+static __device__ __align__(256) uint8_t g_static_scratch[Q38_STATIC_SCRATCH_BYTES];
+
+std::mutex g_static_scratch_mutex;
+void* g_static_scratch_ptr[64] = {nullptr};
+
+// The array's device address on the current device, looked up once per device. In host code the
+// array's name is only a host-side stand-in, so the address must come from cudaGetSymbolAddress.
+int static_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return q38host::cuda_status(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return q38host::set_error("device %d out of range", dev), Q38_ERR_ARG;
+  std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+  if (!g_static_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess) return q38host::cuda_status(e, "cudaGetSymbolAddress(static scratch)");
+    g_static_scratch_ptr[dev] = p;
+  }
+  *out = g_static_scratch_ptr[dev];
+  return Q38_OK;
+}
+
+}  // namespace
+
+extern "C" int q38_fp8_gemm_static_scratch(const void* x, int64_t tokens, int64_t k, const void* w, const void* w_sf,
+                                           int64_t features, int epilogue, void* y, int64_t ldy, const void* residual,
+                                           int64_t ldr, int splits, q38_stream_t stream) {
+  using namespace q38host;
+  if (splits < 1) return set_error("q38_fp8_gemm_static_scratch: splits must be >= 1"), Q38_ERR_ARG;
+  if (splits == 1)
+    return q38_fp8_gemm(x, tokens, k, w, w_sf, features, epilogue, y, ldy, residual, ldr, 1, nullptr, 0, stream);
+  const size_t need = q38_fp8_gemm_workspace_bytes(tokens, features, splits);
+  if (need > static_cast<size_t>(Q38_STATIC_SCRATCH_BYTES))
+    return set_error("q38_fp8_gemm_static_scratch: %lld tokens x %lld features with %d splits need %zu bytes of "
+                     "scratch, more than the library's fixed %d; use fewer splits or q38_fp8_gemm with a workspace",
+                     (long long)tokens, (long long)features, splits, need, Q38_STATIC_SCRATCH_BYTES),
+           Q38_ERR_ARG;
+  void* scratch = nullptr;
+  int st = static_scratch_address(&scratch);
+  if (st != Q38_OK) return st;
+  // The split counters must start at zero. A completed call leaves them at zero, but a call that
+  // gave up part-way would not, so clear them (a memset node, no allocation) before every call.
+  const int64_t ntok = tokens > 128 ? 256 : 128;
+  const size_t counters = static_cast<size_t>(((cdiv(features, BM) * cdiv(tokens, ntok)) * 4 + 255) / 256 * 256);
+  cudaError_t e = cudaMemsetAsync(scratch, 0, counters, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_status(e, "clear static scratch counters");
+  return q38_fp8_gemm(x, tokens, k, w, w_sf, features, epilogue, y, ldy, residual, ldr, splits, scratch,
+                      static_cast<size_t>(Q38_STATIC_SCRATCH_BYTES), stream);
+}
