@@ -12,9 +12,11 @@
  *            (qwen38_inf2/model.py:85-87, :224).
  *   e4m3   : FP8 E4M3 (OCP e4m3fn) byte, the weight format.
  *   ue8m0  : one byte per 32 weights along K, value 2^(byte-127) (power-of-two group scale).
- *   Weights are row-major [out_features, in_features] (K contiguous). Their scales are pre-tiled by
- *   q38_sf_tile_bytes/host code into 512-byte blocks, one per (128 output rows, 128 K): byte
- *   (r % 32) * 16 + (r / 32) * 4 + (g % 4) holds row r's scale for K group g.
+ *   Weights [out_features, in_features] are pre-tiled: 16 KB tiles of 128 rows x 128 bytes of K,
+ *   ordered [row tile][K tile], each tile 128-byte swizzled (16-byte chunk c of tile row r stored at
+ *   chunk c ^ (r % 8)), zero padded; q38_weight_tile_bytes gives the size. Their scales are pre-tiled
+ *   into 512-byte blocks, one per (128 output rows, 128 K): byte (r % 32) * 16 + (r / 32) * 4 + (g % 4)
+ *   holds row r's scale for K group g (q38_sf_tile_bytes).
  *
  * The reference's device path is NKI kernels called from PyTorch (qwen38_inf2/kernels.py); its
  * CPU branches (qwen38_inf2/model.py) define the arithmetic these kernels reproduce. Each function
@@ -61,7 +63,7 @@ int q38_device_status(int reset);
  * (norm, gated norm, attention, SiLU product) rounds it.
  *
  *   x        e5m2 [tokens, k]            (16-byte aligned, k % 16 == 0)
- *   w        e4m3 [features, k]
+ *   w        e4m3 [features, k], pre-tiled (see above)
  *   w_sf     pre-tiled ue8m0 scales, ceil(features/128) * ceil(k/128) blocks of 512 bytes
  *   y        bf16 [tokens, ldy]
  *   residual bf16 [tokens, ldr] for Q38_EPI_RESIDUAL, else NULL
@@ -93,6 +95,9 @@ int q38_fp8_gemm_static_scratch(const void* x, int64_t tokens, int64_t k, const 
 /* Bytes of the pre-tiled scale array of a [features, k] weight. */
 size_t q38_sf_tile_bytes(int64_t features, int64_t k);
 
+/* Bytes of a pre-tiled weight with `features` rows of `row_bytes` bytes (k for FP8, 2k for BF16). */
+size_t q38_weight_tile_bytes(int64_t features, int64_t row_bytes);
+
 /*
  * Decoder-layer input norms: h = bf16(rms_norm(x) * (1 + w)), written as bf16 (y_bf16, optional)
  * and as e5m2 (y_e5m2, optional). Replaces rms_norm (qwen38_inf2/model.py:54-57) as used by
@@ -111,11 +116,13 @@ int q38_silu_mul_quant(const void* gu, int64_t ld, int64_t rows, int64_t n, void
                        q38_stream_t stream);
 
 /*
- * y[r, o] = bf16(sum_k x[r, k] * w[o, k]) for small bf16 weights [n_out, k] (the gated delta
- * rule's in_proj_b / in_proj_a, which stay BF16: qwen38_inf2/model.py:294-296, :333-337).
+ * y[r, o] = bf16(sum_k x[r, k] * w[o, k]) with BF16 x [rows, k] (contiguous) and a pre-tiled BF16
+ * weight [n_out, k], fp32 accumulate on tcgen05 (kind::f16), split K as q38_fp8_gemm (same
+ * workspace rules). Used for the gated delta rule's in_proj_b / in_proj_a, which stay BF16 and take
+ * the unrounded normed input (qwen38_inf2/model.py:294-296, :333-337).
  */
-int q38_bf16_linear_small(const void* x, int64_t ldx, int64_t rows, int64_t k, const void* w, int64_t n_out,
-                          void* y, int64_t ldy, q38_stream_t stream);
+int q38_bf16_linear(const void* x, int64_t ldx, int64_t rows, int64_t k, const void* w, int64_t n_out, void* y,
+                    int64_t ldy, int splits, void* workspace, size_t workspace_bytes, q38_stream_t stream);
 
 /*
  * One decode token per row of the gated delta rule, everything between the input projections and
@@ -162,7 +169,7 @@ int q38_attn_decode(const void* qkv, int64_t ld_qkv, const void* q_norm_w, const
 
 /*
  * lm_head candidates: maxima[r, j] = max over the `group` vocab rows v in group j of
- * sum_k x[r, k] * w[v, k], fp32 (x bf16 [rows, k], w bf16 [vocab, k]). Replaces HeadStep.forward's
+ * sum_k x[r, k] * w[v, k], fp32 (x bf16 [rows, k], w bf16 [vocab, k] pre-tiled). Replaces HeadStep.forward's
  * logits and group maxima (qwen38_inf2/model.py:890-900) and the NKI lm_head_group_maxima
  * (kernels.py:126-172). group must be 32.
  */

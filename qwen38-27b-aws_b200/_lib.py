@@ -36,8 +36,10 @@ SIGNATURES = {
         c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_int64, c_void_p]
     ),
     "q38_silu_mul_quant": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p]),
-    "q38_bf16_linear_small": (
-        c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p]
+    "q38_weight_tile_bytes": (c_size_t, [c_int64, c_int64]),
+    "q38_bf16_linear": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_size_t, c_void_p],
     ),
     "q38_gdn_decode": (
         c_int,

@@ -82,6 +82,46 @@ def tile_scales(ue8m0: torch.Tensor) -> torch.Tensor:
     return t.permute(0, 3, 2, 1, 4).contiguous().reshape(-1)
 
 
+W_TILE_ROWS = 128
+W_TILE_BYTES = 128  # bytes of K per tile row: one 128-byte swizzle row
+W_TILE_SIZE = W_TILE_ROWS * W_TILE_BYTES
+
+
+def tile_weight(w: torch.Tensor) -> torch.Tensor:
+    """A weight [out, in] (any element size) to the GEMM kernel's tiled layout (flat uint8).
+
+    Tiles of 128 rows x 128 bytes of K, ordered [row tile][K tile], each 16 KB tile contiguous and
+    already 128-byte swizzled (16-byte chunk c of row r stored at chunk c ^ (r % 8)), which is the
+    layout a TMA load with 128-byte swizzle would leave in shared memory. A pipeline stage then moves
+    one contiguous 16 KB block with a single bulk copy, so HBM sees long sequential streams instead of
+    128-byte pieces of thousands of rows. Padding rows and K bytes are zero.
+    """
+    b = w.contiguous().view(torch.uint8)
+    rows, kb = b.shape
+    rp = -(-rows // W_TILE_ROWS) * W_TILE_ROWS
+    kp = -(-kb // W_TILE_BYTES) * W_TILE_BYTES
+    padded = torch.zeros((rp, kp), dtype=torch.uint8, device=b.device)
+    padded[:rows, :kb] = b
+    t = padded.reshape(rp // W_TILE_ROWS, W_TILE_ROWS, kp // W_TILE_BYTES, 8, 16)  # [rt, r, kt, chunk, byte]
+    r = torch.arange(W_TILE_ROWS, device=b.device)
+    chunk = torch.arange(8, device=b.device)
+    src = chunk.unsqueeze(0) ^ (r % 8).unsqueeze(1)  # stored chunk c holds logical chunk c ^ (r % 8)
+    t = t.gather(3, src.reshape(1, W_TILE_ROWS, 1, 8, 1).expand(t.shape[0], -1, t.shape[2], -1, 16))
+    return t.permute(0, 2, 1, 3, 4).contiguous().reshape(-1)
+
+
+def untile_weight(tiles: torch.Tensor, rows: int, row_bytes: int) -> torch.Tensor:
+    """Inverse of `tile_weight` on bytes (for tests)."""
+    rp = -(-rows // W_TILE_ROWS) * W_TILE_ROWS
+    kp = -(-row_bytes // W_TILE_BYTES) * W_TILE_BYTES
+    t = tiles.reshape(rp // W_TILE_ROWS, kp // W_TILE_BYTES, W_TILE_ROWS, 8, 16)
+    r = torch.arange(W_TILE_ROWS, device=tiles.device)
+    chunk = torch.arange(8, device=tiles.device)
+    src = chunk.unsqueeze(0) ^ (r % 8).unsqueeze(1)  # logical chunk c sits at stored chunk c ^ (r % 8)
+    t = t.gather(3, src.reshape(1, 1, W_TILE_ROWS, 8, 1).expand(t.shape[0], t.shape[1], -1, -1, 16))
+    return t.permute(0, 2, 1, 3, 4).reshape(rp, kp)[:rows, :row_bytes].contiguous()
+
+
 def untile_scales(tiles: torch.Tensor, rows: int, groups: int) -> torch.Tensor:
     """Inverse of `tile_scales` (for tests)."""
     rp = -(-rows // SF_TILE_ROWS) * SF_TILE_ROWS

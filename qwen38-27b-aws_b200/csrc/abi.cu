@@ -45,18 +45,20 @@ int cuda_status(cudaError_t e, const char* what) {
 }
 
 int encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t elem_bytes,
-                   uint32_t box_rows, uint32_t box_cols) {
+                   uint32_t box_rows, uint32_t box_cols, bool swizzle128, uint64_t ld) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error("cuTensorMapEncodeTiled is not available from the driver"), Q38_ERR_CUDA;
-  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (cols * elem_bytes) % 16 != 0)
-    return set_error("tensor map: base must be 16-byte aligned and rows a multiple of 16 bytes"), Q38_ERR_ARG;
+  if (ld == 0) ld = cols;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld * elem_bytes) % 16 != 0)
+    return set_error("tensor map: base must be 16-byte aligned and rows a multiple of 16 bytes apart"), Q38_ERR_ARG;
   const CUtensorMapDataType dt = elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols * elem_bytes};
+  cuuint64_t strides[1] = {ld * elem_bytes};
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error("cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu box=%ux%u", static_cast<int>(r),
                      static_cast<unsigned long long>(rows), static_cast<unsigned long long>(cols), box_rows, box_cols),

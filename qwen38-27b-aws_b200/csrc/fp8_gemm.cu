@@ -5,9 +5,13 @@
 // so a decode batch of 8..256 rows fills the MMA's N side and every weight byte is read once per
 // token tile. D[feature, token] accumulates in TMEM (lane = feature, column = token).
 //
+// Weights arrive pre-tiled (codec.tile_weight): 128 rows x 128 bytes of K per 16 KB tile, tiles of
+// one row block consecutive along K, each already 128-byte swizzled. A stage's W tile is therefore
+// one contiguous bulk copy, and a CTA streams one long contiguous run of HBM.
+//
 // Roles in one CTA of 192 threads:
-//   warp 0      TMA producer: W tile [128 x 128 B], X tile [NTOK x 128 B] (both 128-byte swizzled)
-//               and, for FP8, the 512-byte scale block of the W tile, into a STAGES-deep ring.
+//   warp 0      producer: W tile (bulk copy of 16 KB), X tile [NTOK x 128 B] (TMA, 128-byte
+//               swizzle) and, for FP8, the 512-byte scale block of the W tile, into a STAGES-deep ring.
 //   warp 1      MMA issuer: one thread copies the W scales to TMEM (tcgen05.cp) and issues the
 //               4 MMAs of each stage (K = 32 bytes each), then commits the stage back to warp 0.
 //   warps 2..5  epilogue: tcgen05.ld of their 32-lane quarter, then the epilogue below.
@@ -44,10 +48,13 @@ struct Cfg {
   static constexpr int TMEM_COLS = NTOK == 256 ? 512 : 256;
   static constexpr int SFA_COL = NTOK;       // 4 columns per stage
   static constexpr int SFB_COL = NTOK + 32;  // 8 columns of 1.0 scales for the activations
-  static constexpr size_t SMEM = 1024 + STAGES * (A_BYTES + B_BYTES + SF_BYTES) + 256;
+  static constexpr size_t PIPE = STAGES * (A_BYTES + B_BYTES + SF_BYTES);
+  static constexpr size_t SMEM = 1024 + PIPE + 256;
+  static_assert(NTOK * BM * 4 + NTOK * BM * 2 <= PIPE, "epilogue staging must fit in the pipeline buffers");
 };
 
 struct GemmArgs {
+  const uint8_t* w;   // pre-tiled W (16 KB tiles, [row tile][K tile])
   const uint8_t* sf;  // pre-tiled W scales (FP8 path)
   int T, F, nkc;      // tokens, features, K stages
   int splits, kc_per_split;
@@ -58,9 +65,16 @@ struct GemmArgs {
   int64_t ldr;
   float* maxima;  // group maxima [T, ldm] (EPI_GROUPMAX)
   int64_t ldm;
-  float* ws;              // split partials
-  unsigned int* counters; // one per output tile
+  float* ws;              // split partials (workspace mode)
+  unsigned int* counters; // one per output tile (workspace mode)
+  int cluster;            // > 0: epilogue through shared memory, the `cluster` K splits of a tile
+                          // forming one thread-block cluster; 0: workspace mode
 };
+
+// Epilogue staging (cluster mode), reusing the pipeline buffers once the accumulator is final:
+// fp32 partial [NTOK tokens][128 rows] at 0, then bf16 [NTOK][128] for the residual in and the
+// output out (the same bytes: each element is read before it is overwritten by its own thread).
+constexpr int TOK_BLOCK = 32;  // tokens per TMA box of the residual / output
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
@@ -93,7 +107,8 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, int row, int t0, c
 
 template <int NTOK, bool MX>
 __global__ void __launch_bounds__(192, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, GemmArgs a) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y,
+                const __grid_constant__ CUtensorMap tmap_r, GemmArgs a) {
   using C = Cfg<NTOK, MX>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -103,7 +118,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(sSF + C::STAGES * C::SF_BYTES);
   uint64_t* empty = full + C::STAGES;
   uint64_t* accf = empty + C::STAGES;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(accf + 1);
+  uint64_t* resbar = accf + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(resbar + 1);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_holder + 1);  // [0] abort, [1] last CTA
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -119,6 +135,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&empty[s], 1);
     }
     mbar_init(accf, 1);
+    mbar_init(resbar, 1);
     flags[0] = 0;
     flags[1] = 0;
     fence_mbar_init();
@@ -142,7 +159,6 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      prefetch_tmap(&tmap_w);
       prefetch_tmap(&tmap_x);
       int issued = 0;
       for (int i = 0; i < nk; ++i) {
@@ -154,7 +170,7 @@ __global__ void __launch_bounds__(192, 1)
         }
         mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES + C::SF_BYTES);
         const int kx = (kc0 + i) * (MX ? BK_BYTES : BK_BYTES / 2);  // element coordinate along K
-        tma_load_2d(sA + s * C::A_BYTES, &tmap_w, &full[s], kx, m0);
+        bulk_load(sA + s * C::A_BYTES, a.w + (static_cast<size_t>(mt) * a.nkc + kc0 + i) * C::A_BYTES, C::A_BYTES, &full[s]);
         tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0);
         if (MX) bulk_load(sSF + s * SF_BLOCK, a.sf + (static_cast<size_t>(mt) * a.nkc + kc0 + i) * SF_BLOCK, SF_BLOCK, &full[s]);
         issued = i + 1;
@@ -206,6 +222,38 @@ __global__ void __launch_bounds__(192, 1)
       tc_commit(accf);
     }
     __syncwarp();
+  } else if (a.cluster > 0) {
+    // Epilogue part 1: the accumulator into shared memory as fp32 [token][row]; the residual tile of
+    // this CTA's token slice starts loading by TMA meanwhile.
+    const int q = warp & 3;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    const bool ok = mbar_wait(accf, 0);
+    tc_fence_after();
+    if (!ok || flags[0]) {
+      flags[0] = 1;
+    } else {
+      fence_proxy_async_shared();
+      if (a.epilogue == EPI_RESIDUAL && warp == 2 && lane == 0) {
+        const int rank = static_cast<int>(cluster_rank());
+        const int nb = NTOK / TOK_BLOCK;
+        const int b0 = rank * nb / a.cluster, b1 = (rank + 1) * nb / a.cluster;
+        uint8_t* stage = smem + NTOK * BM * 4;
+        int issued = 0;
+        for (int b = b0; b < b1; ++b) issued += n0 + b * TOK_BLOCK < a.T;
+        mbar_arrive_expect_tx(resbar, issued * TOK_BLOCK * BM * 2);
+        for (int b = b0; b < b1; ++b)
+          if (n0 + b * TOK_BLOCK < a.T) tma_load_2d(stage + b * TOK_BLOCK * BM * 2, &tmap_r, resbar, m0, n0 + b * TOK_BLOCK);
+      }
+      float* part = reinterpret_cast<float*>(smem);
+      const int r = q * 32 + lane;
+      for (int c = 0; c < NTOK; c += 16) {
+        if (n0 + c >= a.T) break;
+        float v[16];
+        tmem_ld16(taddr + c, v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) part[(c + j) * BM + r] = v[j];
+      }
+    }
   } else {
     // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its hardware lane quarter).
     const int q = warp & 3;
@@ -225,13 +273,16 @@ __global__ void __launch_bounds__(192, 1)
     } else {
       const int tiles = gridDim.x * gridDim.y;
       const int tile = nt * gridDim.x + mt;
-      float* part = a.ws + (static_cast<size_t>(split) * tiles + tile) * BM * NTOK + static_cast<size_t>(q * 32 + lane) * NTOK;
+      // Partial tile layout [16-token chunk][128 rows][16 tokens]: a warp's 32 rows of one chunk are
+      // 2 KB contiguous.
+      float* part = a.ws + (static_cast<size_t>(split) * tiles + tile) * BM * NTOK + static_cast<size_t>(q * 32 + lane) * 16;
       for (int c = 0; c < NTOK; c += 16) {
         if (n0 + c >= a.T) break;
         float v[16];
         tmem_ld16(taddr + c, v);
+        float* dst = part + static_cast<size_t>(c / 16) * BM * 16;
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) __stcg(reinterpret_cast<float4*>(part + c + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+        for (int j = 0; j < 16; j += 4) __stcg(reinterpret_cast<float4*>(dst + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
       }
       __threadfence();
       epi_bar();
@@ -242,7 +293,7 @@ __global__ void __launch_bounds__(192, 1)
       epi_bar();
       if (flags[1]) {
         __threadfence();
-        const float* base = a.ws + static_cast<size_t>(tile) * BM * NTOK + static_cast<size_t>(q * 32 + lane) * NTOK;
+        const float* base = a.ws + static_cast<size_t>(tile) * BM * NTOK + static_cast<size_t>(q * 32 + lane) * 16;
         const size_t split_stride = static_cast<size_t>(tiles) * BM * NTOK;
         for (int c = 0; c < NTOK; c += 16) {
           if (n0 + c >= a.T) break;
@@ -250,7 +301,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = 0.f;
           for (int s = 0; s < a.splits; ++s) {
-            const float* p = base + s * split_stride + c;
+            const float* p = base + s * split_stride + static_cast<size_t>(c / 16) * BM * 16;
 #pragma unroll
             for (int j = 0; j < 16; j += 4) {
               const float4 f = __ldcg(reinterpret_cast<const float4*>(p + j));
@@ -267,6 +318,66 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
 
+  __syncwarp();  // the producer and MMA warps reconverge before any aligned barrier
+  if (a.cluster > 0) {
+    // Every CTA of the cluster has its partial tile in shared memory.
+    if (a.cluster > 1) cluster_sync();
+    else __syncthreads();
+    // Epilogue part 2: this CTA's slice of 32-token blocks, summed over the cluster's partials in rank
+    // order (deterministic), then the epilogue; lane l handles rows 4l .. 4l+3 of a token.
+    if (warp >= 2 && !flags[0]) {
+      const int rank = static_cast<int>(cluster_rank());
+      const int nb = NTOK / TOK_BLOCK;
+      const int b0 = rank * nb / a.cluster, b1 = (rank + 1) * nb / a.cluster;
+      const int t0 = n0 + b0 * TOK_BLOCK;
+      const int t1 = min(a.T, n0 + b1 * TOK_BLOCK);
+      uint8_t* stage = smem + NTOK * BM * 4;
+      const bool ok = a.epilogue != EPI_RESIDUAL || t0 >= t1 || mbar_wait(resbar, 0);
+      if (!ok) flags[0] = 1;
+      const uint32_t part0 = smem_u32(smem);
+      for (int t = t0 + (warp - 2); ok && t < t1; t += 4) {
+        const int tl = t - n0;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int src = 0; src < a.cluster; ++src) {
+          const float4 p = ld_cluster_f4(cluster_map(part0 + static_cast<uint32_t>((tl * BM + 4 * lane) * 4), src));
+          v[0] += p.x;
+          v[1] += p.y;
+          v[2] += p.z;
+          v[3] += p.w;
+        }
+        if (a.epilogue == EPI_GROUPMAX) {
+          // 8 lanes hold one group of 32 vocab rows; groups past the vocabulary are skipped.
+          float m = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+          const int f = m0 + 4 * lane;
+          if ((lane & 7) == 0 && f < a.F) a.maxima[static_cast<int64_t>(t) * a.ldm + (f >> 5)] = m;
+          continue;
+        }
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(stage) + tl * BM + 4 * lane;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float out = bf16r(v[j]);
+          if (a.epilogue == EPI_RESIDUAL) out = __bfloat162float(o[j]) + out;
+          o[j] = __float2bfloat16_rn(out);
+        }
+      }
+      if (a.epilogue != EPI_GROUPMAX) {
+        fence_proxy_async_shared();
+        epi_bar();
+        if (warp == 2 && lane == 0 && ok) {
+          for (int b = b0; b < b1; ++b)
+            if (n0 + b * TOK_BLOCK < a.T) tma_store_2d(&tmap_y, stage + b * TOK_BLOCK * BM * 2, m0, n0 + b * TOK_BLOCK);
+          bulk_commit();
+          bulk_wait_read0();
+        }
+      }
+    }
+    // No CTA leaves while a peer may still read its shared memory.
+    if (a.cluster > 1) cluster_sync();
+  }
+
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -276,7 +387,8 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 template <int NTOK, bool MX>
-int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, dim3 grid, cudaStream_t stream) {
+int launch_gemm(const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap& tr, const GemmArgs& a, dim3 grid,
+                cudaStream_t stream) {
   using C = Cfg<NTOK, MX>;
   // The shared-memory opt-in is per device; remember which devices have it.
   static unsigned long long done_mask = 0;
@@ -288,8 +400,20 @@ int launch_gemm(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a,
     if (e != cudaSuccess) return q38host::cuda_status(e, "cudaFuncSetAttribute(gemm)");
     done_mask |= 1ull << dev;
   }
-  gemm_kernel<NTOK, MX><<<grid, 192, C::SMEM, stream>>>(tw, tx, a);
-  return q38host::cuda_status(cudaGetLastError(), "gemm launch");
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = a.cluster > 1 ? static_cast<unsigned>(a.cluster) : 1u;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, gemm_kernel<NTOK, MX>, tx, ty, tr, a);
+  return q38host::cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "gemm launch");
 }
 
 int token_tile(int64_t tokens) { return tokens > 128 ? 256 : 128; }
@@ -298,11 +422,52 @@ int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+constexpr int kMaxClusterSplits = 8;  // portable cluster size
+
+// Picks the epilogue: through shared memory and a cluster of the K splits (no workspace) when the
+// splits fit a portable cluster and y / residual can be tensor-mapped; else the workspace path.
+// Fills the output and residual tensor maps for the cluster path.
+int setup_epilogue(GemmArgs& a, int splits, int64_t tokens, int64_t features, void* y, int64_t ldy,
+                   const void* residual, int64_t ldr, void* workspace, size_t workspace_bytes, CUtensorMap* ty,
+                   CUtensorMap* tr, const char* who) {
+  using namespace q38host;
+  const bool mappable = aligned16(y) && ldy % 8 == 0 && (!residual || (aligned16(residual) && ldr % 8 == 0));
+  if (splits <= kMaxClusterSplits && mappable) {
+    a.cluster = splits;
+    int st = encode_tmap_2d(ty, y, tokens, features, 2, TOK_BLOCK, BM, false, ldy);
+    if (st != Q38_OK) return st;
+    if (residual) {
+      st = encode_tmap_2d(tr, residual, tokens, features, 2, TOK_BLOCK, BM, false, ldr);
+      if (st != Q38_OK) return st;
+    } else {
+      *tr = *ty;
+    }
+    return Q38_OK;
+  }
+  a.cluster = 0;
+  if (splits > 1) {
+    const int ntok = token_tile(tokens);
+    const int64_t tiles = cdiv(features, BM) * cdiv(tokens, ntok);
+    const size_t need = q38_fp8_gemm_workspace_bytes(tokens, features, splits);
+    if (!workspace || workspace_bytes < need || !aligned16(workspace))
+      return set_error("%s: %d K splits need a 16-byte aligned workspace of %zu bytes", who, splits, need), Q38_ERR_ARG;
+    const size_t counters = static_cast<size_t>((tiles * 4 + 255) / 256 * 256);
+    a.counters = static_cast<unsigned int*>(workspace);
+    a.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
+  }
+  return Q38_OK;
+}
+
 }  // namespace
 
 extern "C" size_t q38_sf_tile_bytes(int64_t features, int64_t k) {
   if (features <= 0 || k <= 0) return 0;
   return static_cast<size_t>(cdiv(features, BM) * cdiv(k, BK_BYTES)) * SF_BLOCK;
+}
+
+extern "C" size_t q38_weight_tile_bytes(int64_t features, int64_t row_bytes) {
+  if (features <= 0 || row_bytes <= 0) return 0;
+  return static_cast<size_t>(cdiv(features, BM) * cdiv(row_bytes, BK_BYTES)) * BM * BK_BYTES;
 }
 
 extern "C" size_t q38_fp8_gemm_workspace_bytes(int64_t tokens, int64_t features, int splits) {
@@ -335,6 +500,7 @@ extern "C" int q38_fp8_gemm(const void* x, int64_t tokens, int64_t k, const void
   int kc_per = static_cast<int>(cdiv(nkc, std::min(splits, nkc)));
   splits = static_cast<int>(cdiv(nkc, kc_per));
   GemmArgs a{};
+  a.w = static_cast<const uint8_t*>(w);
   a.sf = static_cast<const uint8_t*>(w_sf);
   a.T = static_cast<int>(tokens);
   a.F = static_cast<int>(features);
@@ -346,23 +512,16 @@ extern "C" int q38_fp8_gemm(const void* x, int64_t tokens, int64_t k, const void
   a.ldy = ldy;
   a.res = static_cast<const __nv_bfloat16*>(residual);
   a.ldr = ldr;
-  const int64_t tiles = cdiv(features, BM) * cdiv(tokens, ntok);
-  if (splits > 1) {
-    const size_t need = q38_fp8_gemm_workspace_bytes(tokens, features, splits);
-    if (!workspace || workspace_bytes < need || !aligned16(workspace))
-      return set_error("q38_fp8_gemm: split-K needs a 16-byte aligned workspace of %zu bytes", need), Q38_ERR_ARG;
-    const size_t counters = static_cast<size_t>((tiles * 4 + 255) / 256 * 256);
-    a.counters = static_cast<unsigned int*>(workspace);
-    a.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
-  }
-  CUtensorMap tw, tx;
-  int st = encode_tmap_2d(&tw, w, features, k, 1, BM, BK_BYTES);
+  CUtensorMap tx, ty, tr;
+  int st = setup_epilogue(a, splits, tokens, features, y, ldy, epilogue == Q38_EPI_RESIDUAL ? residual : nullptr, ldr,
+                          workspace, workspace_bytes, &ty, &tr, "q38_fp8_gemm");
   if (st != Q38_OK) return st;
   st = encode_tmap_2d(&tx, x, tokens, k, 1, ntok, BK_BYTES);
   if (st != Q38_OK) return st;
+  if (a.cluster == 0) ty = tr = tx;
   dim3 grid(static_cast<unsigned>(cdiv(features, BM)), static_cast<unsigned>(cdiv(tokens, ntok)), static_cast<unsigned>(splits));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return ntok == 256 ? launch_gemm<256, true>(tw, tx, a, grid, s) : launch_gemm<128, true>(tw, tx, a, grid, s);
+  return ntok == 256 ? launch_gemm<256, true>(tx, ty, tr, a, grid, s) : launch_gemm<128, true>(tx, ty, tr, a, grid, s);
 }
 
 extern "C" int q38_lm_head_groupmax(const void* x, int64_t rows, int64_t k, const void* w, int64_t vocab, int group,
@@ -378,6 +537,7 @@ extern "C" int q38_lm_head_groupmax(const void* x, int64_t rows, int64_t k, cons
   if (ld_max < vocab / 32) return set_error("q38_lm_head_groupmax: ld_max too small"), Q38_ERR_ARG;
   const int ntok = token_tile(rows);
   GemmArgs a{};
+  a.w = static_cast<const uint8_t*>(w);
   a.T = static_cast<int>(rows);
   a.F = static_cast<int>(vocab);
   a.nkc = static_cast<int>(cdiv(k, BK_BYTES / 2));
@@ -386,14 +546,48 @@ extern "C" int q38_lm_head_groupmax(const void* x, int64_t rows, int64_t k, cons
   a.epilogue = EPI_GROUPMAX;
   a.maxima = maxima;
   a.ldm = ld_max;
-  CUtensorMap tw, tx;
-  int st = encode_tmap_2d(&tw, w, vocab, k, 2, BM, BK_BYTES / 2);
-  if (st != Q38_OK) return st;
-  st = encode_tmap_2d(&tx, x, rows, k, 2, ntok, BK_BYTES / 2);
+  a.cluster = 1;
+  CUtensorMap tx;
+  int st = encode_tmap_2d(&tx, x, rows, k, 2, ntok, BK_BYTES / 2);
   if (st != Q38_OK) return st;
   dim3 grid(static_cast<unsigned>(cdiv(vocab, BM)), static_cast<unsigned>(cdiv(rows, ntok)), 1);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return ntok == 256 ? launch_gemm<256, false>(tw, tx, a, grid, s) : launch_gemm<128, false>(tw, tx, a, grid, s);
+  return ntok == 256 ? launch_gemm<256, false>(tx, tx, tx, a, grid, s) : launch_gemm<128, false>(tx, tx, tx, a, grid, s);
+}
+
+extern "C" int q38_bf16_linear(const void* x, int64_t ldx, int64_t rows, int64_t k, const void* w, int64_t n_out,
+                               void* y, int64_t ldy, int splits, void* workspace, size_t workspace_bytes,
+                               q38_stream_t stream) {
+  using namespace q38host;
+  if (!x || !w || !y) return set_error("q38_bf16_linear: null pointer"), Q38_ERR_ARG;
+  if (rows <= 0 || k <= 0 || n_out <= 0 || k % 8 || ldx != k || ldy < n_out || rows > (1 << 24) || n_out > (1 << 30))
+    return set_error("q38_bf16_linear: bad sizes (x must be contiguous [rows, k], k %% 8 == 0)"), Q38_ERR_ARG;
+  if (!aligned16(x) || !aligned16(w) || splits < 1)
+    return set_error("q38_bf16_linear: x and w must be 16-byte aligned, splits >= 1"), Q38_ERR_ARG;
+  const int ntok = token_tile(rows);
+  const int nkc = static_cast<int>(cdiv(k, BK_BYTES / 2));
+  const int kc_per = static_cast<int>(cdiv(nkc, std::min(splits, nkc)));
+  splits = static_cast<int>(cdiv(nkc, kc_per));
+  GemmArgs a{};
+  a.w = static_cast<const uint8_t*>(w);
+  a.T = static_cast<int>(rows);
+  a.F = static_cast<int>(n_out);
+  a.nkc = nkc;
+  a.splits = splits;
+  a.kc_per_split = kc_per;
+  a.epilogue = EPI_BF16;
+  a.y = static_cast<__nv_bfloat16*>(y);
+  a.ldy = ldy;
+  CUtensorMap tx, ty, tr;
+  int st = setup_epilogue(a, splits, rows, n_out, y, ldy, nullptr, 0, workspace, workspace_bytes, &ty, &tr,
+                          "q38_bf16_linear");
+  if (st != Q38_OK) return st;
+  st = encode_tmap_2d(&tx, x, rows, k, 2, ntok, BK_BYTES / 2);
+  if (st != Q38_OK) return st;
+  if (a.cluster == 0) ty = tr = tx;
+  dim3 grid(static_cast<unsigned>(cdiv(n_out, BM)), static_cast<unsigned>(cdiv(rows, ntok)), static_cast<unsigned>(splits));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return ntok == 256 ? launch_gemm<256, false>(tx, ty, tr, a, grid, s) : launch_gemm<128, false>(tx, ty, tr, a, grid, s);
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -1,7 +1,6 @@
 // Element-wise and row kernels around the FP8 GEMMs, each rounding where the reference rounds:
 //   q38_rmsnorm_quant      rms_norm (model.py:54-57) -> bf16, and e5m2 for the next FP8 linear
 //   q38_silu_mul_quant     silu(gate) * up in bf16 steps (model.py:48-51, :259) -> e5m2
-//   q38_bf16_linear_small  x @ W^T for the BF16 in_proj_b / in_proj_a (model.py:333-337)
 // All are HBM-bound; rows are read with 16-byte vector loads.
 #include "q38_common.cuh"
 
@@ -92,46 +91,6 @@ __global__ void silu_mul_quant_kernel(const __nv_bfloat16* __restrict__ gu, int6
   }
 }
 
-// CTA = 4 rows of x staged in shared memory; warps take output columns round-robin and stream
-// their weight rows with 16-byte loads.
-constexpr int kLinRows = 4;
-__global__ void __launch_bounds__(256) bf16_linear_small_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
-                                                                 int rows, int k, const __nv_bfloat16* __restrict__ w,
-                                                                 int n_out, __nv_bfloat16* __restrict__ y, int64_t ldy) {
-  extern __shared__ uint4 xs_raw[];
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(xs_raw);
-  const int r0 = blockIdx.x * kLinRows;
-  const int nr = min(kLinRows, rows - r0);
-  const int chunks = k / 8;
-  for (int i = threadIdx.x; i < kLinRows * chunks; i += blockDim.x) {
-    const int r = i / chunks, c = i % chunks;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < nr) v = *reinterpret_cast<const uint4*>(x + (r0 + r) * ldx + c * 8);
-    reinterpret_cast<uint4*>(xs)[i] = v;
-  }
-  __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int o = warp; o < n_out; o += blockDim.x / 32) {
-    float acc[kLinRows] = {0.f, 0.f, 0.f, 0.f};
-    for (int c = lane; c < chunks; c += 32) {
-      Pack8 pw;
-      pw.u = *reinterpret_cast<const uint4*>(w + static_cast<int64_t>(o) * k + c * 8);
-#pragma unroll
-      for (int r = 0; r < kLinRows; ++r) {
-        Pack8 px;
-        px.u = reinterpret_cast<const uint4*>(xs)[r * chunks + c];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[r] += __bfloat162float(px.h[e]) * __bfloat162float(pw.h[e]);
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < kLinRows; ++r) {
-      const float s = warp_sum(acc[r]);
-      if (lane == 0 && r < nr) y[(r0 + r) * ldy + o] = __float2bfloat16_rn(s);
-    }
-  }
-}
-
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -164,24 +123,4 @@ extern "C" int q38_silu_mul_quant(const void* gu, int64_t ld, int64_t rows, int6
       static_cast<const __nv_bfloat16*>(gu), ld, static_cast<int>(rows), static_cast<int>(n),
       static_cast<uint8_t*>(y_e5m2), ldy);
   return cuda_status(cudaGetLastError(), "silu_mul_quant launch");
-}
-
-extern "C" int q38_bf16_linear_small(const void* x, int64_t ldx, int64_t rows, int64_t k, const void* w,
-                                     int64_t n_out, void* y, int64_t ldy, q38_stream_t stream) {
-  using namespace q38host;
-  if (!x || !w || !y) return set_error("q38_bf16_linear_small: null pointer"), Q38_ERR_ARG;
-  if (rows <= 0 || k <= 0 || n_out <= 0 || k % 8 || ldx % 8 || ldx < k || ldy < n_out || !al16(x) || !al16(w))
-    return set_error("q38_bf16_linear_small: bad sizes or alignment"), Q38_ERR_ARG;
-  const size_t smem = static_cast<size_t>(kLinRows) * k * sizeof(__nv_bfloat16);
-  if (smem > 200 * 1024) return set_error("q38_bf16_linear_small: k=%lld too large", (long long)k), Q38_ERR_ARG;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(bf16_linear_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return cuda_status(e, "cudaFuncSetAttribute(bf16_linear_small)");
-  }
-  const unsigned blocks = static_cast<unsigned>((rows + kLinRows - 1) / kLinRows);
-  bf16_linear_small_kernel<<<blocks, 256, smem, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), ldx, static_cast<int>(rows), static_cast<int>(k),
-      static_cast<const __nv_bfloat16*>(w), static_cast<int>(n_out), static_cast<__nv_bfloat16*>(y), ldy);
-  return cuda_status(cudaGetLastError(), "bf16_linear_small launch");
 }

@@ -93,6 +93,39 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
 }
+// Shared memory -> global through a tensor map (bulk group; wait with bulk_wait_read0 before reuse).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
+// Thread-block clusters: rank, barrier over every thread of every CTA, and loads from a peer CTA's
+// shared memory (distributed shared memory).
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_map(uint32_t local_smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
@@ -225,8 +258,9 @@ __device__ __forceinline__ float warp_max(float v) {
 namespace q38host {
 void set_error(const char* fmt, ...);
 int cuda_status(cudaError_t e, const char* what);
-// Encodes a 2D tensor map over a row-major [rows, cols] byte matrix (`elem_bytes` per element),
-// box [box_rows, box_cols], 128-byte swizzle. Returns Q38_OK or an error code.
+// Encodes a 2D tensor map over a row-major [rows, cols] matrix (`elem_bytes` per element, rows
+// `ld` elements apart; ld 0 means cols), box [box_rows, box_cols], 128-byte swizzle or none.
+// Returns Q38_OK or an error code.
 int encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t elem_bytes,
-                   uint32_t box_rows, uint32_t box_cols);
+                   uint32_t box_rows, uint32_t box_cols, bool swizzle128 = true, uint64_t ld = 0);
 }  // namespace q38host

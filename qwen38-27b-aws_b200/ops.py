@@ -30,17 +30,30 @@ def _cuda(*ts) -> None:
 
 
 class DeviceLinear:
-    """An FP8 linear prepared for the GEMM kernel: e4m3 bytes [out, in] and tiled UE8M0 scales."""
+    """An FP8 linear prepared for the GEMM kernel: e4m3 bytes [out, in] in 16 KB swizzled tiles and
+    tiled UE8M0 scales."""
 
     def __init__(self, w, device):
-        self.q = w.q.to(device=device, dtype=U8).contiguous()
+        self.out_features, self.in_features = w.q.shape
+        self.q = codec.tile_weight(w.q.to(device=device, dtype=U8))
         self.sf = codec.tile_scales(codec.scale_to_ue8m0(w.scale.to(device))).contiguous()
-        self.out_features, self.in_features = self.q.shape
-        _need(self.sf.numel() == _lib.load().q38_sf_tile_bytes(self.out_features, self.in_features), "scale tiling mismatch")
+        lib = _lib.load()
+        _need(self.sf.numel() == lib.q38_sf_tile_bytes(self.out_features, self.in_features), "scale tiling mismatch")
+        _need(self.q.numel() == lib.q38_weight_tile_bytes(self.out_features, self.in_features), "weight tiling mismatch")
 
     @property
     def nbytes(self) -> int:
         return self.q.numel() + self.sf.numel()
+
+
+class DeviceBF16Linear:
+    """A BF16 weight [out, in] in the GEMM kernel's swizzled 16 KB tiles (64 values of K per tile row)."""
+
+    def __init__(self, w: torch.Tensor, device):
+        self.out_features, self.in_features = w.shape
+        self.w = codec.tile_weight(w.to(device=device, dtype=BF16))
+        _need(self.w.numel() == _lib.load().q38_weight_tile_bytes(self.out_features, 2 * self.in_features),
+              "weight tiling mismatch")
 
 
 def token_tile(tokens: int) -> int:
@@ -101,12 +114,26 @@ def silu_mul_quant(gu: torch.Tensor, n: int, y_e5m2: torch.Tensor) -> None:
     _lib.call("q38_silu_mul_quant", gu.data_ptr(), gu.stride(0), rows, n, y_e5m2.data_ptr(), y_e5m2.stride(0), _stream())
 
 
-def bf16_linear_small(x: torch.Tensor, w: torch.Tensor, y: torch.Tensor) -> None:
-    _cuda(x, w, y)
+def bf16_linear(x: torch.Tensor, lin: DeviceBF16Linear, y: torch.Tensor, splits: int = 1,
+                workspace: torch.Tensor | None = None) -> None:
+    """y = bf16(x @ W^T), BF16 in, fp32 accumulate (tcgen05 kind::f16), split K through `workspace`."""
+    _cuda(x, y, workspace)
     rows, k = x.shape
-    _need(w.dtype == BF16 and w.shape[1] == k and w.is_contiguous(), "w must be contiguous bf16 [n_out, k]")
-    _lib.call("q38_bf16_linear_small", x.data_ptr(), x.stride(0), rows, k, w.data_ptr(), w.shape[0], y.data_ptr(),
-              y.stride(0), _stream())
+    _need(x.dtype == BF16 and x.is_contiguous() and k == lin.in_features, "x must be contiguous bf16 [rows, in]")
+    ws_ptr, ws_bytes = None, 0
+    if splits > 1:
+        _need(workspace is not None, "split K needs a workspace")
+        ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
+    _lib.call("q38_bf16_linear", x.data_ptr(), x.stride(0), rows, k, lin.w.data_ptr(), lin.out_features, y.data_ptr(),
+              y.stride(0), splits, ws_ptr, ws_bytes, _stream())
+
+
+def bf16_linear_splits(rows: int, n_out: int, k: int) -> int:
+    """K splits for a thin BF16 linear (96 outputs). The tile's last CTA sums every split's partial
+    tile, so more splits buy streaming parallelism at the price of that serial reduction: 8 balances
+    the two at 5120 x 96."""
+    kc = -(-k // 64)
+    return max(1, min(kc // 4, 8))
 
 
 def gdn_decode(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, state, position, active, out, *,
@@ -131,13 +158,13 @@ def attn_decode(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, position, a
               _stream())
 
 
-def lm_head_groupmax(x: torch.Tensor, w: torch.Tensor, maxima: torch.Tensor, group: int = 32) -> None:
-    _cuda(x, w, maxima)
+def lm_head_groupmax(x: torch.Tensor, lin: DeviceBF16Linear, maxima: torch.Tensor, group: int = 32) -> None:
+    _cuda(x, maxima)
     rows, k = x.shape
-    _need(x.is_contiguous() and w.is_contiguous() and w.dtype == BF16 and x.dtype == BF16, "bf16 contiguous x, w")
+    _need(x.is_contiguous() and x.dtype == BF16 and k == lin.in_features, "bf16 contiguous x [rows, hidden]")
     _need(maxima.dtype == torch.float32 and maxima.stride(1) == 1, "maxima fp32")
-    _lib.call("q38_lm_head_groupmax", x.data_ptr(), rows, k, w.data_ptr(), w.shape[0], group, maxima.data_ptr(),
-              maxima.stride(0), _stream())
+    _lib.call("q38_lm_head_groupmax", x.data_ptr(), rows, k, lin.w.data_ptr(), lin.out_features, group,
+              maxima.data_ptr(), maxima.stride(0), _stream())
 
 
 def device_status(reset: bool = True) -> int:

@@ -36,7 +36,7 @@ BF16 = torch.bfloat16
 @dataclass
 class _GDN:
     qkvz: ops.DeviceLinear
-    ab: torch.Tensor
+    ab: ops.DeviceBF16Linear
     conv_w: torch.Tensor
     a_log: torch.Tensor
     dt_bias: torch.Tensor
@@ -99,7 +99,7 @@ class B200Step:
             conv_dim = cfg.linear_conv_dim // self.tp
             mixer = _GDN(
                 qkvz=lin("linear_attn.in_proj_qkv", "linear_attn.in_proj_z"),
-                ab=torch.cat((t("linear_attn.in_proj_b"), t("linear_attn.in_proj_a"))).contiguous(),
+                ab=ops.DeviceBF16Linear(torch.cat((t("linear_attn.in_proj_b"), t("linear_attn.in_proj_a"))), dev),
                 conv_w=t("linear_attn.conv_weight"),
                 a_log=t("linear_attn.A_log"),
                 dt_bias=t("linear_attn.dt_bias"),
@@ -157,6 +157,9 @@ class B200Step:
                 s = ops.choose_splits(B, lin.out_features, lin.in_features)
                 self.splits[id(lin)] = s
                 need = max(need, ops.gemm_workspace_bytes(B, lin.out_features, s))
+        hv2 = 2 * cfg.linear_num_value_heads // tp
+        self.ab_splits = ops.bf16_linear_splits(B, hv2, H)
+        need = max(need, ops.gemm_workspace_bytes(B, hv2, self.ab_splits))
         self.workspace = z(max(need, 256), dt=torch.uint8)
 
     # ------------------------------------------------------------------ kernels of one decode step
@@ -189,7 +192,7 @@ class B200Step:
             if l.kind == LINEAR:
                 ops.rmsnorm_quant(self.x, l.ln_in, eps, y_bf16=self.hb, y_e5m2=self.hq)
                 self._gemm(self.hq, m.qkvz, self.proj)
-                ops.bf16_linear_small(self.hb, m.ab, self.ab)
+                ops.bf16_linear(self.hb, m.ab, self.ab, splits=self.ab_splits, workspace=self.workspace)
                 vd = cfg.linear_value_dim // tp
                 ops.gdn_decode(self.proj, self.ab, m.conv_state, m.conv_w, m.a_log, m.dt_bias, m.norm_w, m.state,
                                self.position, self.active, self.mix_gdn, batch=B,
@@ -293,8 +296,8 @@ class B200Head:
         shard = W.shard_head(cfg, head_weights, rank, tp_degree)
         self.norm_w = shard["norm_weight"].to(self.device, BF16).contiguous()
         # The kernel multiplies BF16 by BF16: the e4m3 * 2^s weights are exact in BF16.
-        self.lm_head = shard["lm_head"].to(self.device).dequant().to(BF16).contiguous()
-        self.vocab_local = self.lm_head.shape[0]
+        self.lm_head = ops.DeviceBF16Linear(shard["lm_head"].to(self.device).dequant().to(BF16), self.device)
+        self.vocab_local = self.lm_head.out_features
         self.hidden = torch.zeros(batch_size, cfg.hidden_size, dtype=BF16, device=self.device)
         self.xb = torch.zeros_like(self.hidden)
         self.maxima = torch.zeros(batch_size, self.vocab_local // 32, dtype=torch.float32, device=self.device)

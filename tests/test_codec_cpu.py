@@ -52,3 +52,20 @@ def test_e5m2_round_matches_reference_codec(pkg):
     """round_e5m2 is the reference's fp8_round (model.py:85-87): torch's e5m2 cast."""
     x = torch.linspace(-300, 300, 10001).to(torch.bfloat16)
     assert torch.equal(pkg.codec.round_e5m2(x), x.to(torch.float8_e5m2).to(torch.bfloat16))
+
+
+def test_weight_tiles_are_swizzled_16kb_blocks(pkg):
+    """tile_weight: [row tile][K tile] blocks of 128 rows x 128 bytes, chunk c of row r stored at c ^ (r % 8)."""
+    gen = torch.Generator().manual_seed(2)
+    w = torch.randint(0, 256, (300, 400), generator=gen, dtype=torch.int32).to(torch.uint8)
+    t = pkg.codec.tile_weight(w)
+    assert t.numel() == 3 * 4 * 16384
+    assert torch.equal(pkg.codec.untile_weight(t, 300, 400), w)
+    rt, kt, r, c = 1, 2, 13, 5  # row 128 + 13, bytes 256 + 16*5 ...
+    block = t[(rt * 4 + kt) * 16384 : (rt * 4 + kt + 1) * 16384].reshape(128, 128)
+    stored = c ^ (r % 8)
+    assert torch.equal(block[r, stored * 16 : stored * 16 + 16], w[rt * 128 + r, kt * 128 + c * 16 : kt * 128 + c * 16 + 16])
+    # Padding is zero; BF16 weights tile on their bytes.
+    assert int(t.reshape(3, 4, 128, 128)[2, :, 300 - 256 :].count_nonzero()) == 0
+    wb = torch.randn(130, 96, generator=gen).to(torch.bfloat16)
+    assert torch.equal(pkg.codec.untile_weight(pkg.codec.tile_weight(wb), 130, 192).view(torch.bfloat16), wb)

@@ -35,13 +35,14 @@ def assert_bf16_close(got, want, frac=0.02, what=""):
 def assert_gemm_close(got, exact, magnitude, what=""):
     """A GEMM with fp32 accumulation: within 1 bf16 ulp of the float64 result plus 2^-19 of
     sum_k |x_k w_k| (fp32 rounding of the running sum, visible only where the result cancels), and
-    beyond 1 ulp for at most 0.1% of elements."""
+    beyond 1 ulp for at most 0.5% of elements (and at most 8 of them in small outputs)."""
     got, exact, magnitude = got.double().cpu(), exact.cpu(), magnitude.cpu()
     assert torch.isfinite(got).all(), f"{what}: non-finite output"
     err = (got - exact).abs()
     ulp = bf16_ulp(exact).double()
     assert (err <= ulp * 1.01 + magnitude * 2.0**-19).all(), f"{what}: error {((err - ulp) / magnitude).max().item():.3g} of sum|xw|"
-    assert (err > ulp * 1.01).double().mean().item() <= 1e-3, f"{what}: too many elements beyond 1 ulp"
+    beyond = int((err > ulp * 1.01).sum())
+    assert beyond <= max(8, 5e-3 * err.numel()), f"{what}: {beyond} of {err.numel()} elements beyond 1 ulp"
 
 
 def e5m2_code(b: torch.Tensor) -> torch.Tensor:
@@ -84,6 +85,8 @@ GEMM_CASES = [
     (256, 17408, 5120, 3),
     (300, 640, 520, 2),
     (512, 17408, 5120, 1),
+    (256, 17408, 1024, 12),  # more splits than a portable cluster: the workspace path
+    (40, 2048, 640, 8),
 ]
 
 
@@ -167,15 +170,18 @@ def test_silu_mul_quant_matches_oracle(pkg, ops):
     assert_e5m2_close(y, om.silu(g) * u, frac=0.002, what="silu*up")
 
 
-def test_bf16_linear_small_matches_torch(pkg, ops):
-    gen = torch.Generator().manual_seed(8)
-    rows, k, n = 13, 5120, 96
+@pytest.mark.parametrize("rows,k,n,splits", [(13, 5120, 96, 1), (256, 5120, 96, 40), (8, 128, 12, 2), (200, 640, 130, 3)])
+def test_bf16_linear_matches_float64(pkg, ops, rows, k, n, splits):
+    gen = torch.Generator().manual_seed(8 + rows)
     x = torch.randn(rows, k, generator=gen).to(torch.bfloat16)
     w = (torch.randn(n, k, generator=gen) * 0.02).to(torch.bfloat16)
     y = torch.empty(rows, n, dtype=torch.bfloat16, device=DEV)
-    ops.bf16_linear_small(x.to(DEV), w.to(DEV), y)
+    lin = ops.DeviceBF16Linear(w, DEV)
+    ws = torch.zeros(max(256, ops.gemm_workspace_bytes(rows, n, splits)), dtype=torch.uint8, device=DEV)
+    ops.bf16_linear(x.to(DEV), lin, y, splits=splits, workspace=ws)
     torch.cuda.synchronize()
-    assert_bf16_close(y, torch.nn.functional.linear(x, w), what="bf16 linear")
+    exact = x.double() @ w.double().T
+    assert_gemm_close(y, exact, x.double().abs() @ w.double().abs().T, what=f"bf16 linear {rows}x{k}x{n}/{splits}")
 
 
 def _gdn_setup(pkg, cfg, batch, gen):
@@ -261,7 +267,7 @@ def test_lm_head_groupmax_matches_oracle(pkg, ops):
     w = pkg.weights.FP8Weight.from_float(torch.randn(vocab, h, generator=gen) * 0.02)
     x = torch.randn(rows, h, generator=gen).to(torch.bfloat16)
     maxima = torch.empty(rows, vocab // 32, device=DEV)
-    ops.lm_head_groupmax(x.to(DEV), w.dequant().to(torch.bfloat16).to(DEV), maxima)
+    ops.lm_head_groupmax(x.to(DEV), ops.DeviceBF16Linear(w.dequant().to(torch.bfloat16), DEV), maxima)
     torch.cuda.synchronize()
     logits = x.double() @ w.dequant().double().T
     want = logits.reshape(rows, -1, 32).amax(-1).float()

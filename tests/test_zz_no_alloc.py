@@ -25,7 +25,8 @@ def mods(pkg):
     return lib_mod, ops
 
 
-@pytest.mark.parametrize("tokens,k,features,splits", [(256, 17408, 5120, 3), (8, 6144, 5120, 3), (37, 512, 384, 2)])
+@pytest.mark.parametrize("tokens,k,features,splits",
+                         [(256, 17408, 5120, 3), (8, 6144, 5120, 3), (37, 512, 384, 2), (256, 17408, 1024, 12)])
 def test_static_scratch_gemm_matches_workspace_gemm_twice(pkg, mods, tokens, k, features, splits):
     lib_mod, ops = mods
     lib = lib_mod.load()
