@@ -135,25 +135,36 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(AttnArgs a) {
     for (int h = 0; h < kMaxGroups; ++h)
 #pragma unroll
       for (int e = 0; e < S::DPL; ++e) qreg[h][e] = h < G ? qf[h * HD + lane * S::DPL + e] : 0.f;
-    for (int p = warp; p < n_read; p += kThreads / 32) {
-      float kv[S::DPL];
-      if constexpr (S::DPL == 8) {
-        Pack8 pk;
-        pk.u = *reinterpret_cast<const uint4*>(kc + static_cast<int64_t>(p) * HD + lane * 8);
+    // Each warp takes 4 consecutive positions per step and loads their K rows before using them, so
+    // each warp keeps 4 rows (2 KB at head_dim 256) in flight.
+    constexpr int PW = 4;
+    for (int p0 = warp * PW; p0 < n_read; p0 += (kThreads / 32) * PW) {
+      float kv[PW][S::DPL];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) kv[e] = __bfloat162float(pk.h[e]);
-      } else {
+      for (int u = 0; u < PW; ++u) {
+        const int p = min(p0 + u, n_read - 1);
+        if constexpr (S::DPL == 8) {
+          Pack8 pk;
+          pk.u = __ldg(reinterpret_cast<const uint4*>(kc + static_cast<int64_t>(p) * HD + lane * 8));
 #pragma unroll
-        for (int e = 0; e < S::DPL; ++e) kv[e] = __bfloat162float(kc[static_cast<int64_t>(p) * HD + lane * S::DPL + e]);
+          for (int e = 0; e < 8; ++e) kv[u][e] = __bfloat162float(pk.h[e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < S::DPL; ++e) kv[u][e] = __bfloat162float(kc[static_cast<int64_t>(p) * HD + lane * S::DPL + e]);
+        }
       }
 #pragma unroll
-      for (int h = 0; h < kMaxGroups; ++h) {
-        if (h >= G) break;
-        float d = 0.f;
+      for (int u = 0; u < PW; ++u) {
+        const int p = p0 + u;
 #pragma unroll
-        for (int e = 0; e < S::DPL; ++e) d += qreg[h][e] * kv[e];
-        d = warp_sum(d);
-        if (lane == 0) sc[h * a.max_seq + p] = bf16r(d);
+        for (int h = 0; h < kMaxGroups; ++h) {
+          if (h >= G) break;
+          float d = 0.f;
+#pragma unroll
+          for (int e = 0; e < S::DPL; ++e) d += qreg[h][e] * kv[u][e];
+          d = warp_sum(d);
+          if (lane == 0 && p < n_read) sc[h * a.max_seq + p] = bf16r(d);
+        }
       }
     }
     // Own scores.
@@ -194,15 +205,26 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(AttnArgs a) {
     for (int h = 0; h < kMaxGroups; ++h)
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[h][e] = 0.f;
-    for (int p = pg; p < n_read; p += S::PGROUPS) {
-      Pack8 pv;
-      pv.u = *reinterpret_cast<const uint4*>(vc + static_cast<int64_t>(p) * HD + chunk * 8);
+    // 8 positions per step per thread, loaded before use (128 B in flight per thread).
+    constexpr int PV = 8;
+    for (int p0 = pg; p0 < n_read; p0 += S::PGROUPS * PV) {
+      Pack8 pv[PV];
 #pragma unroll
-      for (int h = 0; h < kMaxGroups; ++h) {
-        if (h >= G) break;
-        const float w = sc[h * a.max_seq + p];
+      for (int u = 0; u < PV; ++u) {
+        const int p = min(p0 + u * S::PGROUPS, n_read - 1);
+        pv[u].u = __ldg(reinterpret_cast<const uint4*>(vc + static_cast<int64_t>(p) * HD + chunk * 8));
+      }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[h][e] += w * __bfloat162float(pv.h[e]);
+      for (int u = 0; u < PV; ++u) {
+        const int p = p0 + u * S::PGROUPS;
+        if (p >= n_read) break;
+#pragma unroll
+        for (int h = 0; h < kMaxGroups; ++h) {
+          if (h >= G) break;
+          const float w = sc[h * a.max_seq + p];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[h][e] += w * __bfloat162float(pv[u].h[e]);
+        }
       }
     }
 #pragma unroll

@@ -46,6 +46,38 @@ __device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_
 }
 __device__ __forceinline__ void group_bar(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
 
+// CPL consecutive bf16 of a state row, as one vector access when CPL == 4 (8 bytes, conflict-free
+// across a warp's 32 lanes), element by element otherwise.
+template <int CPL>
+__device__ __forceinline__ void load_row(const __nv_bfloat16* p, float (&v)[CPL]) {
+  if constexpr (CPL == 4) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
+    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
+    v[0] = __low2float(a);
+    v[1] = __high2float(a);
+    v[2] = __low2float(b);
+    v[3] = __high2float(b);
+  } else {
+#pragma unroll
+    for (int t = 0; t < CPL; ++t) v[t] = __bfloat162float(p[t]);
+  }
+}
+template <int CPL>
+__device__ __forceinline__ void store_row(__nv_bfloat16* p, const float (&v)[CPL]) {
+  if constexpr (CPL == 4) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
+    __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&a);
+    u.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = u;
+  } else {
+#pragma unroll
+    for (int t = 0; t < CPL; ++t) p[t] = __float2bfloat16_rn(v[t]);
+  }
+}
+
 template <int DK, int DV, int R>
 struct GdnSmem {
   static constexpr int KCONV = 4;
@@ -167,12 +199,15 @@ __global__ void __launch_bounds__(R * 128) gdn_decode_kernel(GdnArgs a) {
   float kv[CPL];
 #pragma unroll
   for (int t = 0; t < CPL; ++t) kv[t] = 0.f;
+#pragma unroll 4
   for (int r = 0; r < ROWS_W; ++r) {
     const int i = gw * ROWS_W + r;
     const float ki = kn[i];
+    float sv[CPL];
+    load_row<CPL>(tile + i * DV + c0, sv);
 #pragma unroll
     for (int t = 0; t < CPL; ++t) {
-      const float s = keep != 0.0f ? __fmul_rn(__bfloat162float(tile[i * DV + c0 + t]), decay) : 0.0f;
+      const float s = keep != 0.0f ? __fmul_rn(sv[t], decay) : 0.0f;
       kv[t] = __fadd_rn(kv[t], __fmul_rn(s, ki));
     }
   }
@@ -191,16 +226,19 @@ __global__ void __launch_bounds__(R * 128) gdn_decode_kernel(GdnArgs a) {
   float o[CPL];
 #pragma unroll
   for (int t = 0; t < CPL; ++t) o[t] = 0.f;
+#pragma unroll 4
   for (int r = 0; r < ROWS_W; ++r) {
     const int i = gw * ROWS_W + r;
     const float ki = kn[i], qi = qn[i];
+    float sv[CPL];
+    load_row<CPL>(tile + i * DV + c0, sv);
 #pragma unroll
     for (int t = 0; t < CPL; ++t) {
-      const float s = keep != 0.0f ? __fmul_rn(__bfloat162float(tile[i * DV + c0 + t]), decay) : 0.0f;
-      const float s2 = __fadd_rn(s, __fmul_rn(ki, delta[t]));
-      tile[i * DV + c0 + t] = __float2bfloat16_rn(s2);
-      o[t] = __fadd_rn(o[t], __fmul_rn(s2, qi));
+      const float s = keep != 0.0f ? __fmul_rn(sv[t], decay) : 0.0f;
+      sv[t] = __fadd_rn(s, __fmul_rn(ki, delta[t]));
+      o[t] = __fadd_rn(o[t], __fmul_rn(sv[t], qi));
     }
+    store_row<CPL>(tile + i * DV + c0, sv);
   }
 #pragma unroll
   for (int t = 0; t < CPL; ++t) red2[(j * 4 + gw) * DV + c0 + t] = o[t];
