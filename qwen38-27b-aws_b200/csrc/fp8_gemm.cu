@@ -39,12 +39,16 @@ constexpr int SF_BLOCK = 512;    // scale bytes per (128 rows, 128 K) block
 
 enum : int { EPI_BF16 = 0, EPI_RESIDUAL = 1, EPI_GROUPMAX = 2 };
 
-template <int NTOK, bool MX>
+// PAIR: the 2-SM form. A cluster pair of CTAs computes 256 weight rows x NTOK tokens with
+// tcgen05.mma.cta_group::2 issued by the even CTA; each CTA loads its own 128 weight rows and half of
+// the tokens, so per SM a stage moves 16 KB of activations instead of 32 KB and six stages fit.
+template <int NTOK, bool MX, bool PAIR = false>
 struct Cfg {
   static constexpr int A_BYTES = BM * BK_BYTES;
-  static constexpr int B_BYTES = NTOK * BK_BYTES;
+  static constexpr int B_ROWS = PAIR ? NTOK / 2 : NTOK;
+  static constexpr int B_BYTES = B_ROWS * BK_BYTES;
   static constexpr int SF_BYTES = MX ? SF_BLOCK : 0;
-  static constexpr int STAGES = NTOK == 256 ? 4 : 6;
+  static constexpr int STAGES = (PAIR || NTOK != 256) ? 6 : 4;
   static constexpr int TMEM_COLS = NTOK == 256 ? 512 : 256;
   static constexpr int SFA_COL = NTOK;       // 4 columns per stage
   static constexpr int SFB_COL = NTOK + 32;  // 8 columns of 1.0 scales for the activations
@@ -105,11 +109,12 @@ __device__ __forceinline__ void epilogue16(const GemmArgs& a, int row, int t0, c
   }
 }
 
-template <int NTOK, bool MX>
+template <int NTOK, bool MX, bool PAIR>
 __global__ void __launch_bounds__(192, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y,
-                const __grid_constant__ CUtensorMap tmap_r, GemmArgs a) {
-  using C = Cfg<NTOK, MX>;
+                const __grid_constant__ CUtensorMap tmap_r, const __grid_constant__ CUtensorMap tmap_w,
+                const __grid_constant__ CUtensorMap tmap_sf, GemmArgs a) {
+  using C = Cfg<NTOK, MX, PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -124,6 +129,10 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int mt = blockIdx.x, nt = blockIdx.y, split = blockIdx.z;
+  const uint32_t crank = (a.cluster > 1 || PAIR) ? cluster_rank() : 0u;
+  const int prank = PAIR ? static_cast<int>(crank & 1u) : 0;           // 0: the pair's MMA leader
+  const int srank = PAIR ? static_cast<int>(crank >> 1) : static_cast<int>(crank);  // K split within the cluster
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << (crank & ~1u));
   const int m0 = mt * BM, n0 = nt * NTOK;
   const int kc0 = split * a.kc_per_split;
   const int kc1 = min(a.nkc, kc0 + a.kc_per_split);
@@ -141,11 +150,17 @@ __global__ void __launch_bounds__(192, 1)
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, C::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_holder, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, C::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's copies signal the leader's barriers: all initialised
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
   if (MX && warp >= 2) {
@@ -168,25 +183,36 @@ __global__ void __launch_bounds__(192, 1)
           flags[0] = 1;
           break;
         }
-        mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES + C::SF_BYTES);
         const int kx = (kc0 + i) * (MX ? BK_BYTES : BK_BYTES / 2);  // element coordinate along K
-        bulk_load(sA + s * C::A_BYTES, a.w + (static_cast<size_t>(mt) * a.nkc + kc0 + i) * C::A_BYTES, C::A_BYTES, &full[s]);
-        tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0);
-        if (MX) bulk_load(sSF + s * SF_BLOCK, a.sf + (static_cast<size_t>(mt) * a.nkc + kc0 + i) * SF_BLOCK, SF_BLOCK, &full[s]);
+        const int tile_id = mt * a.nkc + kc0 + i;
+        if constexpr (PAIR) {
+          // Both CTAs' bytes land on the leader's barrier; only the leader expects them.
+          if (prank == 0) mbar_arrive_expect_tx(&full[s], 2 * (C::A_BYTES + C::B_BYTES + C::SF_BYTES));
+          tma_load_2d_pair(sA + s * C::A_BYTES, &tmap_w, &full[s], 0, tile_id * BM);
+          tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0 + prank * C::B_ROWS);
+          tma_load_2d_pair(sSF + s * SF_BLOCK, &tmap_sf, &full[s], 0, tile_id * 32);
+        } else {
+          mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES + C::SF_BYTES);
+          bulk_load(sA + s * C::A_BYTES, a.w + static_cast<size_t>(tile_id) * C::A_BYTES, C::A_BYTES, &full[s]);
+          tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0);
+          if (MX) bulk_load(sSF + s * SF_BLOCK, a.sf + static_cast<size_t>(tile_id) * SF_BLOCK, SF_BLOCK, &full[s]);
+        }
         issued = i + 1;
       }
-      // Never leave with copies in flight: wait (bounded) for the last load of every stage.
-      for (int i = max(0, issued - C::STAGES); i < issued; ++i) mbar_wait(&full[i % C::STAGES], (i / C::STAGES) & 1);
+      // Never leave with copies in flight: wait (bounded) for the last load of every stage. (A pair's
+      // loads are counted on the leader's barriers, which the leader's MMA waits on before it ends.)
+      if (!PAIR || prank == 0)
+        for (int i = max(0, issued - C::STAGES); i < issued; ++i) mbar_wait(&full[i % C::STAGES], (i / C::STAGES) & 1);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && (!PAIR || prank == 0)) {
       uint32_t idesc;
       if (MX) {
         idesc = (0u << 7)                                  // A: E4M3
                 | (1u << 10)                               // B: E5M2
                 | (static_cast<uint32_t>(NTOK >> 3) << 17)  // N
                 | (1u << 23)                               // scales UE8M0
-                | (static_cast<uint32_t>(BM >> 4) << 24);   // M
+                | (static_cast<uint32_t>((PAIR ? 2 * BM : BM) >> 4) << 24);  // M
       } else {
         idesc = (1u << 4)                                  // D: F32
                 | (1u << 7) | (1u << 10)                   // A, B: BF16
@@ -202,7 +228,17 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
         const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES);
         const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
-        if (MX) {
+        if constexpr (PAIR) {
+          const uint32_t sfa = tmem + C::SFA_COL + 4 * s;
+          tmem_cp_32x128b_x4_pair(sfa, sdesc_rows16(smem_u32(sSF + s * SF_BLOCK)));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t id = idesc | (static_cast<uint32_t>(kk) << 29) | (static_cast<uint32_t>(kk) << 4);
+            mma_mxf8_pair(tmem, sdesc_sw128(a_addr + kk * 32), sdesc_sw128(b_addr + kk * 32), id,
+                          sfa | (static_cast<uint32_t>(kk) << 30), (tmem + C::SFB_COL) | (static_cast<uint32_t>(kk) << 30),
+                          (i | kk) != 0);
+          }
+        } else if (MX) {
           const uint32_t sfa = tmem + C::SFA_COL + 4 * s;
           tmem_cp_32x128b_x4(sfa, sdesc_rows16(smem_u32(sSF + s * SF_BLOCK)));
 #pragma unroll
@@ -217,9 +253,11 @@ __global__ void __launch_bounds__(192, 1)
           for (int kk = 0; kk < 4; ++kk)
             mma_f16(tmem, sdesc_sw128(a_addr + kk * 32), sdesc_sw128(b_addr + kk * 32), idesc, (i | kk) != 0);
         }
-        tc_commit(&empty[s]);
+        if constexpr (PAIR) tc_commit_pair(&empty[s], pair_mask);
+        else tc_commit(&empty[s]);
       }
-      tc_commit(accf);
+      if constexpr (PAIR) tc_commit_pair(accf, pair_mask);
+      else tc_commit(accf);
     }
     __syncwarp();
   } else if (a.cluster > 0) {
@@ -233,8 +271,8 @@ __global__ void __launch_bounds__(192, 1)
       flags[0] = 1;
     } else {
       fence_proxy_async_shared();
-      if (a.epilogue == EPI_RESIDUAL && warp == 2 && lane == 0) {
-        const int rank = static_cast<int>(cluster_rank());
+      if (a.epilogue == EPI_RESIDUAL && warp == 2 && lane == 0 && m0 < a.F) {
+        const int rank = srank;
         const int nb = NTOK / TOK_BLOCK;
         const int b0 = rank * nb / a.cluster, b1 = (rank + 1) * nb / a.cluster;
         uint8_t* stage = smem + NTOK * BM * 4;
@@ -321,25 +359,27 @@ __global__ void __launch_bounds__(192, 1)
   __syncwarp();  // the producer and MMA warps reconverge before any aligned barrier
   if (a.cluster > 0) {
     // Every CTA of the cluster has its partial tile in shared memory.
-    if (a.cluster > 1) cluster_sync();
+    if (a.cluster > 1 || PAIR) cluster_sync();
     else __syncthreads();
     // Epilogue part 2: this CTA's slice of 32-token blocks, summed over the cluster's partials in rank
     // order (deterministic), then the epilogue; lane l handles rows 4l .. 4l+3 of a token.
     if (warp >= 2 && !flags[0]) {
-      const int rank = static_cast<int>(cluster_rank());
+      const int rank = srank;
       const int nb = NTOK / TOK_BLOCK;
       const int b0 = rank * nb / a.cluster, b1 = (rank + 1) * nb / a.cluster;
       const int t0 = n0 + b0 * TOK_BLOCK;
       const int t1 = min(a.T, n0 + b1 * TOK_BLOCK);
       uint8_t* stage = smem + NTOK * BM * 4;
-      const bool ok = a.epilogue != EPI_RESIDUAL || t0 >= t1 || mbar_wait(resbar, 0);
+      const bool live = m0 < a.F;  // the odd CTA of the last pair may lie past the last row
+      const bool ok = a.epilogue != EPI_RESIDUAL || t0 >= t1 || !live || mbar_wait(resbar, 0);
       if (!ok) flags[0] = 1;
       const uint32_t part0 = smem_u32(smem);
-      for (int t = t0 + (warp - 2); ok && t < t1; t += 4) {
+      for (int t = t0 + (warp - 2); ok && live && t < t1; t += 4) {
         const int tl = t - n0;
         float v[4] = {0.f, 0.f, 0.f, 0.f};
         for (int src = 0; src < a.cluster; ++src) {
-          const float4 p = ld_cluster_f4(cluster_map(part0 + static_cast<uint32_t>((tl * BM + 4 * lane) * 4), src));
+          const uint32_t peer = PAIR ? static_cast<uint32_t>(prank + 2 * src) : static_cast<uint32_t>(src);
+          const float4 p = ld_cluster_f4(cluster_map(part0 + static_cast<uint32_t>((tl * BM + 4 * lane) * 4), peer));
           v[0] += p.x;
           v[1] += p.y;
           v[2] += p.z;
@@ -366,7 +406,7 @@ __global__ void __launch_bounds__(192, 1)
       if (a.epilogue != EPI_GROUPMAX) {
         fence_proxy_async_shared();
         epi_bar();
-        if (warp == 2 && lane == 0 && ok) {
+        if (warp == 2 && lane == 0 && ok && live) {
           for (int b = b0; b < b1; ++b)
             if (n0 + b * TOK_BLOCK < a.T) tma_store_2d(&tmap_y, stage + b * TOK_BLOCK * BM * 2, m0, n0 + b * TOK_BLOCK);
           bulk_commit();
@@ -374,29 +414,31 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
-    // No CTA leaves while a peer may still read its shared memory.
-    if (a.cluster > 1) cluster_sync();
+    // No CTA leaves while a peer may still read its shared memory (and a pair frees its tensor memory
+    // together).
+    if (a.cluster > 1 || PAIR) cluster_sync();
   }
 
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, C::TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem, C::TMEM_COLS);
+    else tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
 
-template <int NTOK, bool MX>
+template <int NTOK, bool MX, bool PAIR = false>
 int launch_gemm(const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap& tr, const GemmArgs& a, dim3 grid,
-                cudaStream_t stream) {
-  using C = Cfg<NTOK, MX>;
+                cudaStream_t stream, const CUtensorMap* tw = nullptr, const CUtensorMap* tsf = nullptr) {
+  using C = Cfg<NTOK, MX, PAIR>;
   // The shared-memory opt-in is per device; remember which devices have it.
   static unsigned long long done_mask = 0;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return q38host::cuda_status(e, "cudaGetDevice");
   if (dev < 64 && !(done_mask & (1ull << dev))) {
-    e = cudaFuncSetAttribute(gemm_kernel<NTOK, MX>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM));
+    e = cudaFuncSetAttribute(gemm_kernel<NTOK, MX, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::SMEM));
     if (e != cudaSuccess) return q38host::cuda_status(e, "cudaFuncSetAttribute(gemm)");
     done_mask |= 1ull << dev;
   }
@@ -407,12 +449,12 @@ int launch_gemm(const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap&
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.x = PAIR ? 2u : 1u;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = a.cluster > 1 ? static_cast<unsigned>(a.cluster) : 1u;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, gemm_kernel<NTOK, MX>, tx, ty, tr, a);
+  e = cudaLaunchKernelEx(&cfg, gemm_kernel<NTOK, MX, PAIR>, tx, ty, tr, tw ? *tw : tx, tsf ? *tsf : tx, a);
   return q38host::cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "gemm launch");
 }
 
@@ -519,8 +561,23 @@ extern "C" int q38_fp8_gemm(const void* x, int64_t tokens, int64_t k, const void
   st = encode_tmap_2d(&tx, x, tokens, k, 1, ntok, BK_BYTES);
   if (st != Q38_OK) return st;
   if (a.cluster == 0) ty = tr = tx;
-  dim3 grid(static_cast<unsigned>(cdiv(features, BM)), static_cast<unsigned>(cdiv(tokens, ntok)), static_cast<unsigned>(splits));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The 2-SM form for full 256-token tiles whose cluster (2 x splits) stays portable.
+  if (ntok == 256 && a.cluster > 0 && 2 * a.cluster <= kMaxClusterSplits && features > BM) {
+    // Each CTA of a pair loads half of the 256-token tile: the activation box is 128 rows.
+    st = encode_tmap_2d(&tx, x, tokens, k, 1, Cfg<256, true, true>::B_ROWS, BK_BYTES);
+    if (st != Q38_OK) return st;
+    CUtensorMap tw, tsf;
+    const int64_t tiles = cdiv(features, BM) * nkc;
+    st = encode_tmap_2d(&tw, w, tiles * BM, BK_BYTES, 1, BM, BK_BYTES, false);
+    if (st != Q38_OK) return st;
+    st = encode_tmap_2d(&tsf, w_sf, tiles * 32, 16, 1, 32, 16, false);
+    if (st != Q38_OK) return st;
+    dim3 grid(static_cast<unsigned>(2 * cdiv(features, 2 * BM)), static_cast<unsigned>(cdiv(tokens, ntok)),
+              static_cast<unsigned>(splits));
+    return launch_gemm<256, true, true>(tx, ty, tr, a, grid, s, &tw, &tsf);
+  }
+  dim3 grid(static_cast<unsigned>(cdiv(features, BM)), static_cast<unsigned>(cdiv(tokens, ntok)), static_cast<unsigned>(splits));
   return ntok == 256 ? launch_gemm<256, true>(tx, ty, tr, a, grid, s) : launch_gemm<128, true>(tx, ty, tr, a, grid, s);
 }
 
