@@ -385,6 +385,8 @@ def run_micro(args):
         unit, bound = "GB/s", "hbm"
     else:
         k, n = cfg.intermediate_size // args.tp, cfg.hidden_size
+        if args.shape:
+            n, k = (int(v) for v in args.shape.split(","))
         lins = [ops.DeviceLinear(pkg.weights.FP8Weight.from_float(torch.randn(n, k, device=dev, generator=gen) * 0.02), dev)
                 for _ in range(args.copies)]
         x = pkg.codec.to_e5m2_bytes(bf(B, k))
@@ -399,17 +401,22 @@ def run_micro(args):
     for i in range(args.warmup):
         launch(i)
     torch.cuda.synchronize()
-    events = []
-    for i in range(args.steps):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        launch(i)
-        b.record()
-        events.append((a, b))
+    # The K launches are captured in one CUDA graph and timed as one replay, so the host's launch
+    # cost never shows between kernels; consecutive launches cycle through `copies` buffers.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for i in range(args.steps):
+            launch(i)
+    graph.replay()
     torch.cuda.synchronize()
-    ms = sum(a.elapsed_time(b) for a, b in events) / len(events)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    graph.replay()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
     achieved = per / (ms * 1e-3) / 1e9
-    print(json.dumps({"micro": args.micro, "batch": B, "launch_ms": ms, "bytes_per_launch": per,
+    print(json.dumps({"micro": args.micro, "batch": B, "shape": args.shape, "launch_ms": ms, "bytes_per_launch": per,
                       "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": unit,
                                    "frac": achieved / peak}}), flush=True)
 
@@ -419,6 +426,7 @@ def main():
     ap.add_argument("--micro", choices=["gdn", "gemm"], help="time one kernel alone (profiling) instead of the step")
     ap.add_argument("--copies", type=int, default=4, help="--micro: distinct weight/state copies cycled (defeat L2)")
     ap.add_argument("--tp", type=int, default=1, help="--micro gemm: K = 17408 / tp")
+    ap.add_argument("--shape", help="--micro gemm: 'features,k' instead of the down_proj shape")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)

@@ -261,8 +261,9 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else if (a.cluster > 0) {
-    // Epilogue part 1: the accumulator into shared memory as fp32 [token][row]; the residual tile of
-    // this CTA's token slice starts loading by TMA meanwhile.
+    // Epilogue part 1. With one split the accumulator goes straight to its bf16 staging (or to the
+    // group maxima); with a cluster of splits it goes to shared memory as fp32 [token][row] for part
+    // 2. The residual tile of this CTA's token slice starts loading by TMA meanwhile.
     const int q = warp & 3;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const bool ok = mbar_wait(accf, 0);
@@ -271,25 +272,50 @@ __global__ void __launch_bounds__(192, 1)
       flags[0] = 1;
     } else {
       fence_proxy_async_shared();
+      uint8_t* stage = smem + NTOK * BM * 4;
       if (a.epilogue == EPI_RESIDUAL && warp == 2 && lane == 0 && m0 < a.F) {
         const int rank = srank;
         const int nb = NTOK / TOK_BLOCK;
         const int b0 = rank * nb / a.cluster, b1 = (rank + 1) * nb / a.cluster;
-        uint8_t* stage = smem + NTOK * BM * 4;
         int issued = 0;
         for (int b = b0; b < b1; ++b) issued += n0 + b * TOK_BLOCK < a.T;
         mbar_arrive_expect_tx(resbar, issued * TOK_BLOCK * BM * 2);
         for (int b = b0; b < b1; ++b)
           if (n0 + b * TOK_BLOCK < a.T) tma_load_2d(stage + b * TOK_BLOCK * BM * 2, &tmap_r, resbar, m0, n0 + b * TOK_BLOCK);
       }
-      float* part = reinterpret_cast<float*>(smem);
       const int r = q * 32 + lane;
-      for (int c = 0; c < NTOK; c += 16) {
-        if (n0 + c >= a.T) break;
-        float v[16];
-        tmem_ld16(taddr + c, v);
+      if (a.cluster > 1) {
+        float* part = reinterpret_cast<float*>(smem);
+        for (int c = 0; c < NTOK; c += 16) {
+          if (n0 + c >= a.T) break;
+          float v[16];
+          tmem_ld16(taddr + c, v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) part[(c + j) * BM + r] = v[j];
+          for (int j = 0; j < 16; ++j) part[(c + j) * BM + r] = v[j];
+        }
+      } else if (a.epilogue == EPI_GROUPMAX) {
+        for (int c = 0; c < NTOK; c += 16) {
+          if (n0 + c >= a.T) break;
+          float v[16];
+          tmem_ld16(taddr + c, v);
+          epilogue16(a, m0 + r, n0 + c, v, lane);
+        }
+      } else if (m0 < a.F) {
+        // Lanes are consecutive rows: a warp's stores of one token fill 64 contiguous bytes.
+        if (a.epilogue == EPI_RESIDUAL && !mbar_wait(resbar, 0)) flags[0] = 1;
+        __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stage);
+        for (int c = 0; c < NTOK; c += 16) {
+          if (n0 + c >= a.T) break;
+          float v[16];
+          tmem_ld16(taddr + c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int idx = (c + j) * BM + r;
+            float out = bf16r(v[j]);
+            if (a.epilogue == EPI_RESIDUAL) out = __bfloat162float(st[idx]) + out;
+            st[idx] = __float2bfloat16_rn(out);
+          }
+        }
       }
     }
   } else {
@@ -358,60 +384,79 @@ __global__ void __launch_bounds__(192, 1)
 
   __syncwarp();  // the producer and MMA warps reconverge before any aligned barrier
   if (a.cluster > 0) {
-    // Every CTA of the cluster has its partial tile in shared memory.
-    if (a.cluster > 1 || PAIR) cluster_sync();
-    else __syncthreads();
-    // Epilogue part 2: this CTA's slice of 32-token blocks, summed over the cluster's partials in rank
-    // order (deterministic), then the epilogue; lane l handles rows 4l .. 4l+3 of a token.
-    if (warp >= 2 && !flags[0]) {
-      const int rank = srank;
-      const int nb = NTOK / TOK_BLOCK;
-      const int b0 = rank * nb / a.cluster, b1 = (rank + 1) * nb / a.cluster;
-      const int t0 = n0 + b0 * TOK_BLOCK;
-      const int t1 = min(a.T, n0 + b1 * TOK_BLOCK);
-      uint8_t* stage = smem + NTOK * BM * 4;
-      const bool live = m0 < a.F;  // the odd CTA of the last pair may lie past the last row
-      const bool ok = a.epilogue != EPI_RESIDUAL || t0 >= t1 || !live || mbar_wait(resbar, 0);
-      if (!ok) flags[0] = 1;
-      const uint32_t part0 = smem_u32(smem);
-      for (int t = t0 + (warp - 2); ok && live && t < t1; t += 4) {
-        const int tl = t - n0;
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int src = 0; src < a.cluster; ++src) {
-          const uint32_t peer = PAIR ? static_cast<uint32_t>(prank + 2 * src) : static_cast<uint32_t>(src);
-          const float4 p = ld_cluster_f4(cluster_map(part0 + static_cast<uint32_t>((tl * BM + 4 * lane) * 4), peer));
-          v[0] += p.x;
-          v[1] += p.y;
-          v[2] += p.z;
-          v[3] += p.w;
-        }
-        if (a.epilogue == EPI_GROUPMAX) {
-          // 8 lanes hold one group of 32 vocab rows; groups past the vocabulary are skipped.
-          float m = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
-          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-          m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-          const int f = m0 + 4 * lane;
-          if ((lane & 7) == 0 && f < a.F) a.maxima[static_cast<int64_t>(t) * a.ldm + (f >> 5)] = m;
-          continue;
-        }
-        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(stage) + tl * BM + 4 * lane;
+    const int nb = NTOK / TOK_BLOCK;
+    const int b0 = srank * nb / a.cluster, b1 = (srank + 1) * nb / a.cluster;
+    const bool live = m0 < a.F;  // the odd CTA of the last pair may lie past the last row
+    uint8_t* stage = smem + NTOK * BM * 4;
+    if (a.cluster > 1) {
+      // Every CTA of the cluster has its partial tile in shared memory.
+      cluster_sync();
+      // Epilogue part 2: this CTA's slice of 32-token blocks, summed over the cluster's partials in
+      // rank order (deterministic), then the epilogue; lane l handles rows 4l .. 4l+3 of a token. A
+      // warp keeps U tokens' loads in flight per source so the reduction is not load-latency bound.
+      if (warp >= 2 && !flags[0]) {
+        constexpr int U = 8, NW = 4;
+        const int t0 = n0 + b0 * TOK_BLOCK;
+        const int t1 = min(a.T, n0 + b1 * TOK_BLOCK);
+        const bool ok = a.epilogue != EPI_RESIDUAL || t0 >= t1 || !live || mbar_wait(resbar, 0);
+        if (!ok) flags[0] = 1;
+        const uint32_t part0 = smem_u32(smem) + static_cast<uint32_t>(4 * lane * 4);
+        for (int tb = t0 + (warp - 2); ok && live && tb < t1; tb += NW * U) {
+          float4 acc[U];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          float out = bf16r(v[j]);
-          if (a.epilogue == EPI_RESIDUAL) out = __bfloat162float(o[j]) + out;
-          o[j] = __float2bfloat16_rn(out);
+          for (int u = 0; u < U; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          for (int src = 0; src < a.cluster; ++src) {
+            const uint32_t peer = PAIR ? static_cast<uint32_t>(prank + 2 * src) : static_cast<uint32_t>(src);
+            float4 p[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              const int t = tb + NW * u;
+              p[u] = t < t1 ? ld_cluster_f4(cluster_map(part0 + static_cast<uint32_t>((t - n0) * BM * 4), peer))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              acc[u].x += p[u].x;
+              acc[u].y += p[u].y;
+              acc[u].z += p[u].z;
+              acc[u].w += p[u].w;
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < U; ++u) {
+            const int t = tb + NW * u;
+            if (t >= t1) break;
+            const float v[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
+            if (a.epilogue == EPI_GROUPMAX) {
+              // 8 lanes hold one group of 32 vocab rows; groups past the vocabulary are skipped.
+              float m = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+              m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+              m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+              m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+              const int f = m0 + 4 * lane;
+              if ((lane & 7) == 0 && f < a.F) a.maxima[static_cast<int64_t>(t) * a.ldm + (f >> 5)] = m;
+              continue;
+            }
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(stage) + (t - n0) * BM + 4 * lane;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float out = bf16r(v[j]);
+              if (a.epilogue == EPI_RESIDUAL) out = __bfloat162float(o[j]) + out;
+              o[j] = __float2bfloat16_rn(out);
+            }
+          }
         }
       }
-      if (a.epilogue != EPI_GROUPMAX) {
-        fence_proxy_async_shared();
-        epi_bar();
-        if (warp == 2 && lane == 0 && ok && live) {
-          for (int b = b0; b < b1; ++b)
-            if (n0 + b * TOK_BLOCK < a.T) tma_store_2d(&tmap_y, stage + b * TOK_BLOCK * BM * 2, m0, n0 + b * TOK_BLOCK);
-          bulk_commit();
-          bulk_wait_read0();
-        }
+    }
+    // The staged bf16 slice goes out by TMA (boxes past the last token or feature are clipped).
+    if (warp >= 2 && a.epilogue != EPI_GROUPMAX) {
+      fence_proxy_async_shared();
+      epi_bar();
+      if (warp == 2 && lane == 0 && !flags[0] && live) {
+        for (int b = b0; b < b1; ++b)
+          if (n0 + b * TOK_BLOCK < a.T) tma_store_2d(&tmap_y, stage + b * TOK_BLOCK * BM * 2, m0, n0 + b * TOK_BLOCK);
+        bulk_commit();
+        bulk_wait_read0();
       }
     }
     // No CTA leaves while a peer may still read its shared memory (and a pair frees its tensor memory
