@@ -149,6 +149,50 @@ int q38_gdn_decode(const void* qkvz, int64_t ld_qkvz, const void* ab, int64_t ld
                    float eps, q38_stream_t stream);
 
 /*
+ * A prefill chunk of one row (slot) through the gated delta rule: the causal conv over
+ * [history * (start > 0), chunk] (bf16 products summed left to right in bf16), SiLU, L2 norms, the
+ * gates masked to the first n_valid tokens, the chunked rule from the row's state * (start > 0), the
+ * gated RMS norm times SiLU(z) rounded to e5m2 for out_proj; the row's state and conv state are
+ * replaced by their values after the chunk (the conv state keeps inputs n_valid - 3 .. n_valid - 1 of
+ * the window). Replaces GatedDeltaNetStep.prefill (qwen38_inf2/model.py:476-521, CPU branch; NKI
+ * delta_prefill kernels.py:843-904) between its input and output projections.
+ *
+ *   qkvz, ab     as q38_gdn_decode, [tokens, ld] for the chunk's tokens
+ *   conv_state   bf16 [state_rows, conv_dim, conv_kernel - 1]; state bf16 [state_rows, num_v_heads,
+ *                head_k, head_v]: the slot's rows are read and replaced
+ *   out          e5m2 [tokens, ld_out]
+ *   workspace    q38_gdn_prefill_workspace_bytes(tokens, ...) bytes, 256-byte aligned
+ */
+size_t q38_gdn_prefill_workspace_bytes(int64_t tokens, int num_k_heads, int num_v_heads, int head_k, int head_v);
+int q38_gdn_prefill_chunk(const void* qkvz, int64_t ld_qkvz, const void* ab, int64_t ld_ab, void* conv_state,
+                          const void* conv_weight, const void* a_log, const void* dt_bias, const void* norm_weight,
+                          void* state, int64_t slot, int64_t state_rows, int64_t tokens, int64_t start,
+                          int64_t n_valid, void* out, int64_t ld_out, int num_k_heads, int num_v_heads, int head_k,
+                          int head_v, int conv_kernel, float eps, void* workspace, size_t workspace_bytes,
+                          q38_stream_t stream);
+
+/*
+ * Keys-first gated attention of a prefill chunk of one row: q/k RMS norms (1 + w), partial rotary,
+ * queries scaled by head_dim^-0.5 in bf16; token t attends to cache positions < start and to chunk
+ * tokens <= t; output times sigmoid(gate), e5m2 for o_proj. The chunk's keys and values are written to
+ * the row's cache at start .. start + tokens - 1. Replaces FullAttentionStep.prefill
+ * (qwen38_inf2/model.py:732-786 with blocked_attention :170-191; NKI prefill_attention
+ * kernels.py:294-423) between its projections.
+ *
+ *   qkv      bf16 [tokens, ld_qkv], laid out as for q38_attn_decode
+ *   cos, sin bf16 [tokens, rot_dim] for positions start .. start + tokens - 1
+ *   k_cache, v_cache bf16 [cache_rows, num_kv_heads, max_seq, head_dim]
+ *   out      e5m2 [tokens, ld_out]
+ *   workspace q38_attn_prefill_workspace_bytes(tokens, num_q_heads, head_dim) bytes
+ */
+size_t q38_attn_prefill_workspace_bytes(int64_t tokens, int num_q_heads, int head_dim);
+int q38_attn_prefill(const void* qkv, int64_t ld_qkv, const void* q_norm_weight, const void* k_norm_weight,
+                     const void* cos, const void* sin, void* k_cache, void* v_cache, int64_t slot, int64_t cache_rows,
+                     int64_t max_seq, int64_t tokens, int64_t start, void* out, int64_t ld_out, int num_q_heads,
+                     int num_kv_heads, int head_dim, int rot_dim, float eps, void* workspace, size_t workspace_bytes,
+                     q38_stream_t stream);
+
+/*
  * One decode token per row of gated full attention with a BF16 KV cache: q/k RMS norms (1 + w),
  * partial rotary on the first rot_dim dims, softmax attention over cache positions < position plus
  * the token's own key/value, times sigmoid(gate), rounded to e5m2 for o_proj; the token's key and

@@ -295,17 +295,25 @@ class GDNLayer:
 
     def prefill(self, x, slot, start, n_valid):
         """A chunk of one row (model.py:476-521, CPU branch). x [1, T, H]."""
-        dt, T = x.dtype, x.shape[1]
+        T = x.shape[1]
+        h = self.prefill_core(self.qkv(x)[0], self.z(x)[0], F.linear(x[0], self.b), F.linear(x[0], self.a), slot, start,
+                              n_valid)
+        return self.out(h.reshape(T, 1, self.vd)).reshape(1, T, -1)
+
+    def prefill_core(self, qkv, z, b_raw, a_raw, slot, start, n_valid):
+        """Between the projections of `prefill`: qkv [T, conv_dim], z [T, value_dim], b_raw/a_raw [T, v_heads]
+        (the in_proj_b / in_proj_a outputs). Returns out_proj's input [T, value_dim] and replaces the
+        slot's states (model.py:481-521)."""
+        dt, T = qkv.dtype, qkv.shape[0]
         kern = self.cfg.linear_conv_kernel_dim
         s_idx, keep = int(slot.reshape(-1)[0]), (start > 0).to(dt)
         valid = (torch.arange(T) < n_valid).float()
-        qkv = self.qkv(x)[0]
         history = self.conv_state[s_idx] * keep
         window = torch.cat((history.transpose(0, 1), qkv))
         carried = window.index_select(0, n_valid.long().reshape(-1) + torch.arange(kern - 1)).transpose(0, 1)
         self.conv_state[s_idx] = carried
-        z = self.z(x)[0]
-        beta, log_decay = self.gates(x[0])
+        beta = b_raw.sigmoid().float()
+        log_decay = -self.A_log.float().exp() * F.softplus(a_raw.float() + self.dt_bias.float())
         beta, log_decay = beta * valid.unsqueeze(-1), log_decay * valid.unsqueeze(-1)
         state = self.recurrent_state[s_idx].float() * keep.float()
         conv = sum(window.transpose(0, 1)[:, j : j + T] * self.conv_w[:, j : j + 1] for j in range(kern))
@@ -314,7 +322,7 @@ class GDNLayer:
                                          beta.transpose(0, 1), state, min(DELTA_CHUNK, T))
         self.recurrent_state[s_idx] = state.to(self.state_dtype)
         z = z.reshape(T, self.hv, -1)
-        return self.finish(out.transpose(0, 1).to(dt), z).reshape(1, T, -1)
+        return self.gated_norm(out.transpose(0, 1).to(dt), z).reshape(T, self.vd)
 
     def copy_states(self, slot: int, to_saved: bool):
         """model.py:456-464."""
@@ -394,10 +402,15 @@ class AttentionLayer:
 
     def prefill(self, x, cos, sin, slot, start, n_valid):
         """model.py:732-786 (CPU branch, BF16 cache)."""
-        hd, T = self.cfg.head_dim, x.shape[1]
+        return self.o(self.prefill_core(self.q(x), self.k(x), self.v(x), cos, sin, slot, start))
+
+    def prefill_core(self, qg, k, v, cos, sin, slot, start):
+        """Between the projections of `prefill`: raw q_proj/k_proj/v_proj outputs [1, T, ...] to o_proj's input
+        [1, T, heads * hd], writing the chunk's keys and values to the slot's cache (model.py:735-786)."""
+        hd, T = self.cfg.head_dim, qg.shape[1]
         G = self.groups
         s_idx, st = int(slot.reshape(-1)[0]), int(start.reshape(-1)[0])
-        query, key, value, gate = self.project(x, cos, sin)
+        query, key, value, gate = self.norm_rope(qg, k, v, cos, sin)
         grouped = (query[0] * hd**-0.5).reshape(self.kv_heads, G * T, hd)
         own_k, own_v = key[0], value[0]
         index = torch.arange(G * T) % T
@@ -405,10 +418,10 @@ class AttentionLayer:
         keys = torch.cat((self.k_cache[s_idx], own_k), dim=1)
         values = torch.cat((self.v_cache[s_idx], own_v), dim=1)
         out = blocked_attention(grouped, keys, values, visible, ATTENTION_BLOCK)
-        out = out.to(x.dtype).reshape(self.heads, T, hd).transpose(0, 1).reshape(1, T, self.heads * hd)
+        out = out.to(qg.dtype).reshape(self.heads, T, hd).transpose(0, 1).reshape(1, T, self.heads * hd)
         self.k_cache[s_idx, :, st : st + T] = own_k
         self.v_cache[s_idx, :, st : st + T] = own_v
-        return self.o(out * torch.sigmoid(gate))
+        return out * torch.sigmoid(gate)
 
 
 class MLPLayer:

@@ -158,6 +158,42 @@ def attn_decode(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, position, a
               _stream())
 
 
+def gdn_prefill_workspace_bytes(tokens: int, num_k_heads: int, num_v_heads: int, head_k: int, head_v: int) -> int:
+    return _lib.load().q38_gdn_prefill_workspace_bytes(tokens, num_k_heads, num_v_heads, head_k, head_v)
+
+
+def gdn_prefill(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, state, out, workspace, *, slot: int,
+                start: int, n_valid: int, num_k_heads: int, num_v_heads: int, head_k: int, head_v: int,
+                eps: float) -> None:
+    """One row's prefill chunk through the gated delta rule (qkvz/ab rows are the chunk's tokens)."""
+    _cuda(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, state, out, workspace)
+    _need(state.is_contiguous() and conv_state.is_contiguous(), "state buffers must be contiguous")
+    tokens = qkvz.shape[0]
+    _need(ab.shape[0] >= tokens and out.shape[0] >= tokens, "ab and out need a row per token")
+    _lib.call("q38_gdn_prefill_chunk", qkvz.data_ptr(), qkvz.stride(0), ab.data_ptr(), ab.stride(0),
+              conv_state.data_ptr(), conv_weight.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(),
+              norm_weight.data_ptr(), state.data_ptr(), slot, state.shape[0], tokens, start, n_valid, out.data_ptr(),
+              out.stride(0), num_k_heads, num_v_heads, head_k, head_v, conv_weight.shape[1], eps, workspace.data_ptr(),
+              workspace.numel() * workspace.element_size(), _stream())
+
+
+def attn_prefill_workspace_bytes(tokens: int, num_q_heads: int, head_dim: int) -> int:
+    return _lib.load().q38_attn_prefill_workspace_bytes(tokens, num_q_heads, head_dim)
+
+
+def attn_prefill(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, out, workspace, *, slot: int, start: int,
+                 num_q_heads: int, num_kv_heads: int, head_dim: int, rot_dim: int, eps: float) -> None:
+    """One row's prefill chunk through keys-first gated attention; writes the chunk's K/V to the cache."""
+    _cuda(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, out, workspace)
+    _need(cos.is_contiguous() and sin.is_contiguous() and cos.shape[-1] == rot_dim, "cos/sin [tokens, rot] contiguous")
+    _need(k_cache.is_contiguous() and v_cache.is_contiguous(), "caches must be contiguous")
+    tokens = qkv.shape[0]
+    _lib.call("q38_attn_prefill", qkv.data_ptr(), qkv.stride(0), q_norm_w.data_ptr(), k_norm_w.data_ptr(),
+              cos.data_ptr(), sin.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), slot, k_cache.shape[0],
+              k_cache.shape[2], tokens, start, out.data_ptr(), out.stride(0), num_q_heads, num_kv_heads, head_dim,
+              rot_dim, eps, workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream())
+
+
 def lm_head_groupmax(x: torch.Tensor, lin: DeviceBF16Linear, maxima: torch.Tensor, group: int = 32) -> None:
     _cuda(x, maxima)
     rows, k = x.shape

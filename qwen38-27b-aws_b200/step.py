@@ -6,7 +6,8 @@ in, the hidden state ``[rows, tokens, hidden]`` back on the host, routed by whic
 exactly as `Qwen38Step.forward` routes them (model.py:983-995):
 
 * decode: inputs_embeds [B, 1, H], cos/sin [B, 1, rot], position int32 [B], active float32 [B];
-* prefill: inputs_embeds [1, C, H], cos/sin [1, C, rot], slot/start/n_valid int32 [1] (not built yet);
+* prefill: inputs_embeds [1, C, H], cos/sin [1, C, rot], slot/start/n_valid int32 [1]: one row's chunk
+  of C tokens, eagerly (the chunk length varies), with buffers sized on first use per C;
 * save_slot / restore_slot int32 [1]: copy one row's recurrent states, return inputs_embeds.
 
 `B200Head.run_graph(hidden=...)` is the reference's lm_head graph call (generate.py:194):
@@ -64,6 +65,10 @@ class _Layer:
     mixer: object
     gate_up: ops.DeviceLinear
     down: ops.DeviceLinear
+
+
+class _Acts:
+    """Activation buffers of one prefill chunk length (attributes set by B200Step._fill_acts)."""
 
 
 class B200Step:
@@ -124,95 +129,154 @@ class B200Step:
                       lin("mlp.gate_proj", "mlp.up_proj"), lin("mlp.down_proj"))
 
     def _alloc_activations(self):
-        cfg, dev, B, tp = self.cfg, self.device, self.batch, self.tp
+        self._fill_acts(self, self.batch)
+        self.position = torch.zeros(self.batch, dtype=torch.int32, device=self.device)
+        self.active = torch.zeros(self.batch, dtype=torch.float32, device=self.device)
+        self._prefill_acts = {}
+
+    def _fill_acts(self, a, rows: int) -> None:
+        """Activation buffers for `rows` token rows on `a` (the step itself for decode, a _Acts for a
+        prefill chunk), with the split-K plan of every GEMM at that row count and one shared workspace."""
+        cfg, dev, tp = self.cfg, self.device, self.tp
         H = cfg.hidden_size
         hv = cfg.linear_num_value_heads // tp
         vd = cfg.linear_value_dim // tp
         heads = cfg.num_attention_heads // tp
         inter = cfg.intermediate_size // tp
         z = lambda *s, dt=BF16: torch.zeros(*s, dtype=dt, device=dev)  # noqa: E731
-        self.x = z(B, H)
-        self.x_in = z(B, H)
-        self.hb = z(B, H)
-        self.hq = z(B, H, dt=torch.uint8)
+        a.x = z(rows, H)
+        a.x_in = z(rows, H)
+        a.hb = z(rows, H)
+        a.hq = z(rows, H, dt=torch.uint8)
         widths = [l.mixer.qkvz.out_features for l in self.layers if l.kind == LINEAR]
         widths += [l.mixer.qkv.out_features for l in self.layers if l.kind == FULL]
-        self.proj = z(B, max(widths))
-        self.ab = z(B, 2 * hv)
-        self.mix_gdn = z(B, vd, dt=torch.uint8)
-        self.mix_attn = z(B, heads * cfg.head_dim, dt=torch.uint8)
-        self.gu = z(B, 2 * inter)
-        self.mlp_q = z(B, inter, dt=torch.uint8)
-        self.partial = z(B, H) if tp > 1 else None
-        self.cos = z(B, cfg.rotary_dim)
-        self.sin = z(B, cfg.rotary_dim)
-        self.position = z(B, dt=torch.int32)
-        self.active = z(B, dt=torch.float32)
-        # Split-K plans and one shared workspace for every row-parallel GEMM.
-        self.splits = {}
+        a.proj = z(rows, max(widths))
+        a.ab = z(rows, 2 * hv)
+        a.mix_gdn = z(rows, vd, dt=torch.uint8)
+        a.mix_attn = z(rows, heads * cfg.head_dim, dt=torch.uint8)
+        a.gu = z(rows, 2 * inter)
+        a.mlp_q = z(rows, inter, dt=torch.uint8)
+        a.partial = z(rows, H) if tp > 1 else None
+        a.cos = z(rows, cfg.rotary_dim)
+        a.sin = z(rows, cfg.rotary_dim)
+        a.splits = {}
         need = 0
         for l in self.layers:
             for lin in (l.mixer.out if l.kind == LINEAR else l.mixer.o, l.down, l.gate_up,
                         l.mixer.qkvz if l.kind == LINEAR else l.mixer.qkv):
-                s = ops.choose_splits(B, lin.out_features, lin.in_features)
-                self.splits[id(lin)] = s
-                need = max(need, ops.gemm_workspace_bytes(B, lin.out_features, s))
+                sp = ops.choose_splits(rows, lin.out_features, lin.in_features)
+                a.splits[id(lin)] = sp
+                need = max(need, ops.gemm_workspace_bytes(rows, lin.out_features, sp))
         hv2 = 2 * cfg.linear_num_value_heads // tp
-        self.ab_splits = ops.bf16_linear_splits(B, hv2, H)
-        need = max(need, ops.gemm_workspace_bytes(B, hv2, self.ab_splits))
-        self.workspace = z(max(need, 256), dt=torch.uint8)
+        a.ab_splits = ops.bf16_linear_splits(rows, hv2, H)
+        need = max(need, ops.gemm_workspace_bytes(rows, hv2, a.ab_splits))
+        a.workspace = z(max(need, 256), dt=torch.uint8)
 
     # ------------------------------------------------------------------ kernels of one decode step
-    def _gemm(self, x_q, lin: ops.DeviceLinear, y, residual=None):
-        ops.fp8_gemm(x_q, lin, y, residual=residual, splits=self.splits.get(id(lin), 1), workspace=self.workspace)
+    def _gemm(self, a, x_q, lin: ops.DeviceLinear, y, residual=None):
+        ops.fp8_gemm(x_q, lin, y, residual=residual, splits=a.splits.get(id(lin), 1), workspace=a.workspace)
 
-    def _row_parallel(self, x_q, lin: ops.DeviceLinear):
+    def _row_parallel(self, a, x_q, lin: ops.DeviceLinear):
         """x += all_reduce(bf16(x_q @ W^T)) (the reference's `x + all_reduce(proj(...))`)."""
         if self.tp == 1:
-            self._gemm(x_q, lin, self.x, residual=self.x)
+            self._gemm(a, x_q, lin, a.x, residual=a.x)
             return
-        self._gemm(x_q, lin, self.partial)
-        torch.distributed.all_reduce(self.partial, group=self.group)
-        self.x.add_(self.partial)
+        self._gemm(a, x_q, lin, a.partial)
+        torch.distributed.all_reduce(a.partial, group=self.group)
+        a.x.add_(a.partial)
 
     def _decode_layers(self):
         self.x.copy_(self.x_in)
         for l in self.layers:
-            self._decode_layer(l)
+            self._layer(l, self)
 
     def run_layer(self, i: int) -> None:
         """Layer i alone, eagerly, on self.x and the loaded decode inputs (for layer-by-layer checks)."""
-        self._decode_layer(self.layers[i])
+        self._layer(self.layers[i], self)
 
-    def _decode_layer(self, l: _Layer):
-        cfg, B, eps = self.cfg, self.batch, self.cfg.rms_norm_eps
-        tp = self.tp
-        if True:
-            m = l.mixer
-            if l.kind == LINEAR:
-                ops.rmsnorm_quant(self.x, l.ln_in, eps, y_bf16=self.hb, y_e5m2=self.hq)
-                self._gemm(self.hq, m.qkvz, self.proj)
-                ops.bf16_linear(self.hb, m.ab, self.ab, splits=self.ab_splits, workspace=self.workspace)
-                vd = cfg.linear_value_dim // tp
-                ops.gdn_decode(self.proj, self.ab, m.conv_state, m.conv_w, m.a_log, m.dt_bias, m.norm_w, m.state,
-                               self.position, self.active, self.mix_gdn, batch=B,
-                               num_k_heads=cfg.linear_num_key_heads // tp, num_v_heads=cfg.linear_num_value_heads // tp,
-                               head_k=cfg.linear_key_head_dim, head_v=cfg.linear_value_head_dim, eps=eps)
-                self._row_parallel(self.mix_gdn, m.out)
+    def _layer(self, l: _Layer, a, chunk=None):
+        """DecoderLayer.forward (model.py:918-930) on the activation set `a`: a decode step over all
+        rows, or with `chunk` = (slot, start, n_valid) one row's prefill chunk of a.x's rows."""
+        cfg, eps, tp = self.cfg, self.cfg.rms_norm_eps, self.tp
+        m = l.mixer
+        if l.kind == LINEAR:
+            ops.rmsnorm_quant(a.x, l.ln_in, eps, y_bf16=a.hb, y_e5m2=a.hq)
+            self._gemm(a, a.hq, m.qkvz, a.proj)
+            ops.bf16_linear(a.hb, m.ab, a.ab, splits=a.ab_splits, workspace=a.workspace)
+            heads = dict(num_k_heads=cfg.linear_num_key_heads // tp, num_v_heads=cfg.linear_num_value_heads // tp,
+                         head_k=cfg.linear_key_head_dim, head_v=cfg.linear_value_head_dim, eps=eps)
+            if chunk is None:
+                ops.gdn_decode(a.proj, a.ab, m.conv_state, m.conv_w, m.a_log, m.dt_bias, m.norm_w, m.state,
+                               a.position, a.active, a.mix_gdn, batch=self.batch, **heads)
             else:
-                ops.rmsnorm_quant(self.x, l.ln_in, eps, y_e5m2=self.hq)
-                self._gemm(self.hq, m.qkv, self.proj)
-                heads = cfg.num_attention_heads // tp
-                ops.attn_decode(self.proj, m.q_norm, m.k_norm, self.cos, self.sin, m.k_cache, m.v_cache, self.position,
-                                self.active, self.mix_attn, batch=B, num_q_heads=heads,
-                                num_kv_heads=cfg.kv_heads_per_rank(tp), head_dim=cfg.head_dim,
-                                rot_dim=cfg.rotary_dim, eps=eps)
-                self._row_parallel(self.mix_attn, m.o)
-            ops.rmsnorm_quant(self.x, l.ln_post, eps, y_e5m2=self.hq)
-            self._gemm(self.hq, l.gate_up, self.gu)
-            inter = cfg.intermediate_size // tp
-            ops.silu_mul_quant(self.gu, inter, self.mlp_q)
-            self._row_parallel(self.mlp_q, l.down)
+                slot, start, n_valid = chunk
+                ops.gdn_prefill(a.proj, a.ab, m.conv_state, m.conv_w, m.a_log, m.dt_bias, m.norm_w, m.state, a.mix_gdn,
+                                a.gdn_ws, slot=slot, start=start, n_valid=n_valid, **heads)
+            self._row_parallel(a, a.mix_gdn, m.out)
+        else:
+            ops.rmsnorm_quant(a.x, l.ln_in, eps, y_e5m2=a.hq)
+            self._gemm(a, a.hq, m.qkv, a.proj)
+            heads = dict(num_q_heads=cfg.num_attention_heads // tp, num_kv_heads=cfg.kv_heads_per_rank(tp),
+                         head_dim=cfg.head_dim, rot_dim=cfg.rotary_dim, eps=eps)
+            if chunk is None:
+                ops.attn_decode(a.proj, m.q_norm, m.k_norm, a.cos, a.sin, m.k_cache, m.v_cache, a.position, a.active,
+                                a.mix_attn, batch=self.batch, **heads)
+            else:
+                slot, start, _ = chunk
+                ops.attn_prefill(a.proj, m.q_norm, m.k_norm, a.cos, a.sin, m.k_cache, m.v_cache, a.mix_attn, a.attn_ws,
+                                 slot=slot, start=start, **heads)
+            self._row_parallel(a, a.mix_attn, m.o)
+        ops.rmsnorm_quant(a.x, l.ln_post, eps, y_e5m2=a.hq)
+        self._gemm(a, a.hq, l.gate_up, a.gu)
+        ops.silu_mul_quant(a.gu, cfg.intermediate_size // tp, a.mlp_q)
+        self._row_parallel(a, a.mlp_q, l.down)
+
+    # ------------------------------------------------------------------ prefill
+    def _chunk_acts(self, tokens: int):
+        a = self._prefill_acts.get(tokens)
+        if a is None:
+            cfg, tp = self.cfg, self.tp
+            a = _Acts()
+            with torch.cuda.device(self.device):
+                self._fill_acts(a, tokens)
+                gdn = ops.gdn_prefill_workspace_bytes(tokens, cfg.linear_num_key_heads // tp,
+                                                      cfg.linear_num_value_heads // tp, cfg.linear_key_head_dim,
+                                                      cfg.linear_value_head_dim)
+                attn = ops.attn_prefill_workspace_bytes(tokens, cfg.num_attention_heads // tp, cfg.head_dim)
+                a.gdn_ws = torch.zeros(gdn, dtype=torch.uint8, device=self.device)
+                a.attn_ws = torch.zeros(max(attn, 256), dtype=torch.uint8, device=self.device)
+            self._prefill_acts[tokens] = a
+        return a
+
+    def prefill(self, embeds: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, slot: int, start: int,
+                n_valid: int) -> torch.Tensor:
+        """One row's chunk (model.py:983-995 with `slot`): embeds [1, C, H] -> hidden [C, H] on the device.
+        Tokens from n_valid on are padding: they run through the layers but leave the states alone."""
+        tokens = embeds.shape[1]
+        if embeds.shape[0] != 1:
+            raise ValueError(f"prefill takes [1, chunk, hidden], got {tuple(embeds.shape)}")
+        if not 0 <= slot < self.batch:
+            raise ValueError(f"slot {slot} outside the {self.batch} rows")
+        if not 0 <= n_valid <= tokens or start < 0 or start + tokens > self.max_seq:
+            raise ValueError(f"chunk at {start} of {tokens} tokens ({n_valid} valid) does not fit {self.max_seq} positions")
+        a = self._load_chunk(embeds, cos, sin)
+        for l in self.layers:
+            self._layer(l, a, (slot, start, n_valid))
+        return a.x
+
+    def _load_chunk(self, embeds, cos, sin):
+        tokens = embeds.shape[1]
+        a = self._chunk_acts(tokens)
+        a.x.copy_(embeds.reshape(tokens, -1), non_blocking=True)
+        a.cos.copy_(cos.reshape(tokens, -1), non_blocking=True)
+        a.sin.copy_(sin.reshape(tokens, -1), non_blocking=True)
+        return a
+
+    def run_prefill_layer(self, i: int, embeds, cos, sin, slot: int, start: int, n_valid: int) -> torch.Tensor:
+        """Layer i alone on a prefill chunk whose input is `embeds` [1, C, H] (for layer-by-layer checks)."""
+        a = self._load_chunk(embeds, cos, sin)
+        self._layer(self.layers[i], a, (slot, start, n_valid))
+        return a.x
 
     def kernels_per_decode_step(self) -> int:
         """Launches of this library's kernels in one decode step (for the bench's gpu_launches)."""
@@ -255,7 +319,10 @@ class B200Step:
         if "accepted" in inputs:
             raise NotImplementedError("verify steps are not built yet")
         if "slot" in inputs:
-            raise NotImplementedError("prefill chunks are not built yet")
+            scalar = lambda name: int(inputs[name].reshape(-1)[0])  # noqa: E731
+            out = self.prefill(inputs_embeds, inputs["cos"], inputs["sin"], scalar("slot"), scalar("start"),
+                               scalar("n_valid"))
+            return out.to("cpu").reshape(1, inputs_embeds.shape[1], -1)
         rows = inputs_embeds.shape[0]
         if rows != self.batch or inputs_embeds.shape[1] != 1:
             raise ValueError(f"decode takes [{self.batch}, 1, hidden], got {tuple(inputs_embeds.shape)}")
