@@ -324,6 +324,77 @@ class GDNLayer:
         z = z.reshape(T, self.hv, -1)
         return self.gated_norm(out.transpose(0, 1).to(dt), z).reshape(T, self.vd)
 
+    def verify(self, x, position, active, accepted):
+        """K tokens per row (model.py:376-454). x [B, K, H]."""
+        B, K = x.shape[:2]
+        xf = x.reshape(B * K, -1)
+        h = self.verify_core(self.qkv(x), self.z(x), F.linear(xf, self.b).reshape(B, K, -1),
+                             F.linear(xf, self.a).reshape(B, K, -1), position, active, accepted)
+        return self.out(h.reshape(B * K, 1, self.vd)).reshape(B, K, -1)
+
+    def verify_core(self, qkv, z, b_raw, a_raw, position, active, accepted):
+        """Between the projections of `verify`: qkv [B, K, conv_dim], z [B, K, value_dim], b_raw/a_raw
+        [B, K, v_heads]. Commits the last verify step's first `accepted` tokens (from the pending buffers),
+        runs the K tokens from the committed state as one small chunk, keeps their updates pending, and
+        returns out_proj's input [B, K, value_dim] (model.py:383-453, _commit_and_read :262-271)."""
+        dt = qkv.dtype
+        B, K = qkv.shape[:2]
+        kern = self.cfg.linear_conv_kernel_dim
+        dk, dv = self.cfg.linear_key_head_dim, self.cfg.linear_value_head_dim
+        on = (active > 0.5).reshape(B, 1)
+        keep = torch.where((position.reshape(B, 1) == 0) & on, 0.0, 1.0)
+        # Commit: decay by the accepted tokens' log decays, plus each one's key x delta decayed by those after it.
+        taken = [(accepted.reshape(B, 1) > j).float() for j in range(K)]
+        decays = [self.pending_decay[:, j] * taken[j] for j in range(K)]
+        remaining = sum(decays)
+        scale = torch.where(on, remaining.exp() * keep, 1.0)
+        weighted = []
+        for j in range(K):
+            remaining = remaining - decays[j]
+            weighted.append(self.pending_key[:, j] * (remaining.exp() * taken[j] * keep * on).unsqueeze(-1))
+        # The conv history: the kern - 1 inputs before the first uncommitted token.
+        cs = self.live(self.conv_state)
+        window = torch.cat((cs, self.pending_input.transpose(1, 2)), dim=-1)
+        at = (accepted.long().reshape(B, 1, 1) + torch.arange(kern - 1)).expand(-1, window.shape[1], -1)
+        history = torch.where(on.reshape(B, 1, 1), window.gather(2, at) * keep.reshape(B, 1, 1).to(dt), cs)
+        self.conv_state[:B] = history
+        window = torch.cat((history, qkv.transpose(1, 2)), dim=-1)
+        mixed = torch.stack([(window[:, :, t : t + kern] * self.conv_w).sum(dim=-1) for t in range(K)], dim=1)
+        q, k, v = (part.reshape(B, K, *part.shape[1:]) for part in self.split(silu(mixed).reshape(B * K, -1)))
+        beta = b_raw.sigmoid().float() * active.reshape(B, 1, 1)
+        log_decay = (-self.A_log.float().exp() * F.softplus(a_raw.float() + self.dt_bias.float())) * active.reshape(B, 1, 1)
+        # The committed state (rounded to the state's dtype) and the new tokens' keys and queries against it.
+        heads = self.hv
+        pairs = B * heads
+        state = self.live(self.recurrent_state).reshape(pairs, dk, dv)
+        w_k = torch.stack(weighted, dim=2).reshape(pairs, -1, dk)
+        deltas = self.pending_delta.transpose(1, 2).reshape(pairs, -1, dv)
+        committed = (state.float() * scale.reshape(pairs, 1, 1).expand(-1, dk, -1) + w_k.transpose(1, 2) @ deltas).to(state.dtype)
+        self.recurrent_state[:B] = committed.reshape(B, heads, dk, dv)
+        reads = torch.cat((k, q), dim=1).permute(0, 2, 3, 1).reshape(pairs, dk, 2 * K)
+        products = (reads.transpose(1, 2) @ committed.float()).reshape(B, heads, 2 * K, dv).transpose(1, 2)
+        k_state, q_state = products[:, :K], products[:, K:]
+        # The K tokens as one chunk: a K x K triangular solve for the deltas, then the outputs.
+        cum = [log_decay[:, 0]]
+        for t in range(1, K):
+            cum.append(cum[-1] + log_decay[:, t])
+        deltas, outs = [], []
+        for t in range(K):
+            d = v[:, t] - cum[t].exp().unsqueeze(-1) * k_state[:, t]
+            for j in range(t):
+                d = d - ((cum[t] - cum[j]).exp() * (k[:, t] * k[:, j]).sum(dim=-1)).unsqueeze(-1) * deltas[j]
+            deltas.append(d * beta[:, t].unsqueeze(-1))
+            o = cum[t].exp().unsqueeze(-1) * q_state[:, t]
+            for j in range(t + 1):
+                o = o + ((cum[t] - cum[j]).exp() * (q[:, t] * k[:, j]).sum(dim=-1)).unsqueeze(-1) * deltas[j]
+            outs.append(o)
+        self.pending_key = k.float().clone()
+        self.pending_delta = torch.stack(deltas, dim=1)
+        self.pending_decay = log_decay.float().clone()
+        self.pending_input = qkv.clone()
+        out = torch.stack(outs, dim=1).reshape(B * K, heads, -1).to(dt)
+        return self.gated_norm(out, z.reshape(B * K, heads, -1)).reshape(B, K, self.vd)
+
     def copy_states(self, slot: int, to_saved: bool):
         """model.py:456-464."""
         if self.recurrent_state.shape[0] == self.batch:
@@ -400,6 +471,31 @@ class AttentionLayer:
         self.write(key, value, where)
         return out * torch.sigmoid(gate)
 
+    def verify(self, x, cos, sin, position, active):
+        """K tokens per row (model.py:641-675, BF16 cache)."""
+        return self.o(self.verify_core(self.q(x), self.k(x), self.v(x), cos, sin, position, active))
+
+    def verify_core(self, qg, k, v, cos, sin, position, active):
+        """From the raw projections [B, K, ...] to o_proj's input [B, K, heads * hd]: each token against the
+        cache before `position` and the step's own tokens up to itself; the tokens' keys and values are
+        written from `position` on (inactive rows at the last K positions) (model.py:648-675)."""
+        hd = self.cfg.head_dim
+        B, K = qg.shape[:2]
+        query, key, value, gate = self.norm_rope(qg, k, v, cos, sin)
+        steps = torch.arange(K)
+        where = torch.where(active.unsqueeze(-1) > 0.5, position.long().unsqueeze(-1) + steps, self.max_seq - K + steps)
+        grouped = query.reshape(B, self.kv_heads, self.groups, K, hd)
+        earlier = torch.arange(self.max_seq) < position.unsqueeze(-1)
+        cached = torch.matmul(grouped, self.k_cache.unsqueeze(2).transpose(-1, -2)).float()
+        cached = cached + torch.where(earlier, 0.0, MASKED_SCORE).reshape(B, 1, 1, 1, -1)
+        causal = steps.unsqueeze(0) <= steps.unsqueeze(-1)
+        own = torch.matmul(grouped, key.unsqueeze(2).transpose(-1, -2)).float() + torch.where(causal, 0.0, MASKED_SCORE)
+        wts = torch.softmax(torch.cat((cached, own), dim=-1) * hd**-0.5, dim=-1).to(qg.dtype)
+        out = torch.matmul(wts[..., : self.max_seq], self.v_cache.unsqueeze(2)) + torch.matmul(wts[..., self.max_seq :], value.unsqueeze(2))
+        out = out.permute(0, 3, 1, 2, 4).reshape(B, K, self.heads * hd)
+        self.write(key, value, where)
+        return out * torch.sigmoid(gate)
+
     def prefill(self, x, cos, sin, slot, start, n_valid):
         """model.py:732-786 (CPU branch, BF16 cache)."""
         return self.o(self.prefill_core(self.q(x), self.k(x), self.v(x), cos, sin, slot, start))
@@ -444,13 +540,14 @@ class OracleStep:
     """
 
     def __init__(self, cfg, weights: dict, max_seq_len: int, batch_size: int = 1, tp_degree: int = 1, rank: int = 0,
-                 all_reduce=None, dtype=torch.bfloat16, saved_states: bool = False, linear_fp32: bool = False):
+                 all_reduce=None, dtype=torch.bfloat16, saved_states: bool = False, linear_fp32: bool = False,
+                 verify_tokens: int = 0):
         self.cfg, self.dtype = cfg, dtype
         self.all_reduce = all_reduce or (lambda t: t)
         self.layers = []
         for i, kind in enumerate(cfg.layer_types):
             p = f"layers.{i}"
-            mixer = (GDNLayer(cfg, weights, p, tp_degree, batch_size, dtype, saved_states=saved_states) if kind == LINEAR
+            mixer = (GDNLayer(cfg, weights, p, tp_degree, batch_size, dtype, verify_tokens, saved_states) if kind == LINEAR
                      else AttentionLayer(cfg, weights, p, tp_degree, rank, batch_size, max_seq_len, dtype))
             self.layers.append((kind, mixer, MLPLayer(weights, p), weights[f"{p}.input_layernorm_weight"].cpu().to(dtype),
                                 weights[f"{p}.post_attention_layernorm_weight"].cpu().to(dtype)))
@@ -463,8 +560,6 @@ class OracleStep:
 
     def __call__(self, inputs_embeds, cos=None, sin=None, position=None, active=None, slot=None, start=None,
                  n_valid=None, save_slot=None, restore_slot=None, accepted=None):
-        if accepted is not None:
-            raise NotImplementedError("verify steps are not restated yet")
         if save_slot is not None or restore_slot is not None:
             which = save_slot if save_slot is not None else restore_slot
             for kind, mixer, *_ in self.layers:
@@ -473,15 +568,18 @@ class OracleStep:
             return inputs_embeds
         x = inputs_embeds.to(self.dtype)
         for i in range(len(self.layers)):
-            x = self.layer(i, x, cos, sin, position, active, slot, start, n_valid)
+            x = self.layer(i, x, cos, sin, position, active, slot, start, n_valid, accepted)
         return x
 
-    def layer(self, i, x, cos=None, sin=None, position=None, active=None, slot=None, start=None, n_valid=None):
+    def layer(self, i, x, cos=None, sin=None, position=None, active=None, slot=None, start=None, n_valid=None,
+              accepted=None):
         """DecoderLayer.forward (model.py:918-930) for layer i alone."""
         eps = self.cfg.rms_norm_eps
         kind, mixer, mlp, w_in, w_post = self.layers[i]
         h = rms_norm(x, w_in, eps)
-        if slot is not None:
+        if accepted is not None:
+            m = mixer.verify(h, position, active, accepted) if kind == LINEAR else mixer.verify(h, cos, sin, position, active)
+        elif slot is not None:
             m = mixer.prefill(h, slot, start, n_valid) if kind == LINEAR else mixer.prefill(h, cos, sin, slot, start, n_valid)
         else:
             m = mixer.decode(h, position, active) if kind == LINEAR else mixer.decode(h, cos, sin, position, active)

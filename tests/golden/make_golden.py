@@ -36,6 +36,7 @@ STD = 0.1  # larger than the model's 0.02 so a 4-layer tiny block is far from li
 BATCH = 3
 MAX_SEQ = 64
 CHUNK = 16
+VERIFY = 4  # tokens per verify step
 
 
 def weights_digest(weights: dict) -> str:
@@ -68,6 +69,64 @@ def decode_schedule():
     ]
 
 
+def verify_schedule():
+    """(positions, active, accepted) per verify step: the first after decode commits nothing; then rows
+    accept different counts, a row idles, and a row starts a new sequence (its states must clear)."""
+    return [
+        ([2, 2, 2], [1, 1, 1], [0, 0, 0]),
+        ([4, 6, 3], [1, 1, 1], [2, 4, 1]),
+        ([7, 7, 3], [1, 1, 0], [3, 1, 0]),
+        ([0, 9, 3], [1, 1, 1], [0, 2, 0]),
+        ([1, 12, 5], [1, 1, 1], [1, 3, 2]),
+    ]
+
+
+def build_model(rmodel, ref_cfg, weights, verify_tokens=0):
+    """The reference's Qwen38Step on CPU with the synthetic weights loaded (FP8 linears through the
+    swapped codec of `fp8_forward` in main)."""
+    model = rmodel.Qwen38Step(ref_cfg, MAX_SEQ, tp_degree=1, dtype=torch.bfloat16, batch_size=BATCH,
+                              verify_tokens=verify_tokens).eval()
+    plain = {}
+    for name, t in weights.items():
+        if isinstance(t, pkg.weights.FP8Weight):
+            model.get_submodule(name)._b200_weight = t.dequant()
+        else:
+            plain[name] = t
+    missing, unexpected = model.load_state_dict(plain, strict=False)
+    assert not unexpected, unexpected
+    assert all(n.endswith(("weight_fp8", "_cache", "_state")) for n in missing), missing
+    return model
+
+
+def verify_goldens(rgen, ref_cfg, model, ours):
+    """Two decode steps, then the verify schedule, then a decode step; every output and the final buffers
+    (recurrent, conv and pending states, KV caches) into tiny_verify.safetensors."""
+    tensors: dict[str, torch.Tensor] = {}
+    gen = torch.Generator().manual_seed(SEED + 1)
+    with torch.no_grad():
+        for step in range(2):
+            x = torch.randn(BATCH, 1, ours.hidden_size, generator=gen).to(torch.bfloat16)
+            inputs = rgen.batch_step_inputs(ref_cfg, [step] * BATCH, MAX_SEQ, torch.bfloat16, [True] * BATCH)
+            tensors[f"decode{step}.x"] = x
+            tensors.update({f"decode{step}.{k}": v for k, v in inputs.items()})
+            tensors[f"decode{step}.y"] = model(inputs_embeds=x, **inputs)
+        for step, (positions, active, accepted) in enumerate(verify_schedule()):
+            x = torch.randn(BATCH, VERIFY, ours.hidden_size, generator=gen).to(torch.bfloat16)
+            inputs = rgen.verify_inputs(ref_cfg, positions, VERIFY, MAX_SEQ, torch.bfloat16, [bool(a) for a in active],
+                                        accepted)
+            tensors[f"verify{step}.x"] = x
+            tensors.update({f"verify{step}.{k}": v for k, v in inputs.items()})
+            tensors[f"verify{step}.y"] = model(inputs_embeds=x, **inputs)
+        x = torch.randn(BATCH, 1, ours.hidden_size, generator=gen).to(torch.bfloat16)
+        inputs = rgen.batch_step_inputs(ref_cfg, [2, 15, 7], MAX_SEQ, torch.bfloat16, [True] * BATCH)
+        tensors["after.x"] = x
+        tensors.update({f"after.{k}": v for k, v in inputs.items()})
+        tensors["after.y"] = model(inputs_embeds=x, **inputs)
+        for name, buf in model.named_buffers():
+            tensors[f"state.{name}"] = buf.clone()
+    return tensors
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="checkout of the reference (contains qwen38_inf2/)")
@@ -88,16 +147,7 @@ def main():
         return F.linear(x, self._b200_weight.to(x.dtype))
 
     rmodel.FP8Linear.forward = fp8_forward
-    model = rmodel.Qwen38Step(ref_cfg, MAX_SEQ, tp_degree=1, dtype=torch.bfloat16, batch_size=BATCH).eval()
-    plain = {}
-    for name, t in weights.items():
-        if isinstance(t, pkg.weights.FP8Weight):
-            model.get_submodule(name)._b200_weight = t.dequant()
-        else:
-            plain[name] = t
-    missing, unexpected = model.load_state_dict(plain, strict=False)
-    assert not unexpected, unexpected
-    assert all(n.endswith(("weight_fp8", "_cache", "_state")) for n in missing), missing
+    model = build_model(rmodel, ref_cfg, weights)
 
     tensors: dict[str, torch.Tensor] = {}
     gen = torch.Generator().manual_seed(SEED)
@@ -166,6 +216,12 @@ def main():
     save_file({k: v.contiguous() for k, v in tensors.items()}, str(HERE / "tiny_block.safetensors"), metadata=meta)
     print(json.dumps(meta, indent=1))
     print(f"{len(tensors)} tensors, {(HERE / 'tiny_block.safetensors').stat().st_size} bytes")
+
+    vtensors = verify_goldens(rgen, ref_cfg, build_model(rmodel, ref_cfg, weights, VERIFY), ours)
+    vmeta = dict(meta, verify_tokens=str(VERIFY), verify_steps=str(len(verify_schedule())))
+    del vmeta["decode_steps"], vmeta["chunk"]
+    save_file({k: v.contiguous() for k, v in vtensors.items()}, str(HERE / "tiny_verify.safetensors"), metadata=vmeta)
+    print(f"{len(vtensors)} tensors, {(HERE / 'tiny_verify.safetensors').stat().st_size} bytes")
 
 
 if __name__ == "__main__":

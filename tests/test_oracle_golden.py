@@ -111,3 +111,38 @@ def test_chunked_rule_matches_recurrent_rule():
     want_o, want_s = om.recurrent_gated_delta(q, k, v, g, b, s)
     got_o, got_s = om.chunked_gated_delta(q, k, v, g, b, s, chunk=64)
     assert (got_o - want_o).abs().max() < 1e-3 and (got_s - want_s).abs().max() < 1e-3
+
+
+VERIFY_GOLDEN = Path(__file__).resolve().parent / "golden" / "tiny_verify.safetensors"
+
+
+def test_oracle_reproduces_reference_verify_steps(pkg):
+    """Decode, five verify steps (commit-on-accept with different accepted counts, an idle row, a row
+    starting over), then decode: every output and the final recurrent, conv, pending and KV buffers."""
+    with safe_open(str(VERIFY_GOLDEN), "pt") as f:
+        tensors, meta = {k: f.get_tensor(k) for k in f.keys()}, f.metadata()
+    cfg = pkg.config.tiny_config(num_blocks=1)
+    weights = {}
+    for i in range(cfg.num_hidden_layers):
+        weights |= pkg.weights.synthetic_layer(cfg, i, int(meta["seed"]), "cpu", float(meta["std"]))
+    assert _digest(pkg, weights) == meta["weights_sha256"]
+    K = int(meta["verify_tokens"])
+    step = om.OracleStep(cfg, weights, int(meta["max_seq"]), int(meta["batch"]), verify_tokens=K)
+    calls = [f"decode{s}" for s in range(2)] + [f"verify{s}" for s in range(int(meta["verify_steps"]))] + ["after"]
+    for c in calls:
+        y = step(inputs_embeds=tensors[f"{c}.x"], **_inputs(tensors, c) | ({"accepted": tensors[f"{c}.accepted"]} if f"{c}.accepted" in tensors else {}))
+        active = tensors[f"{c}.active"] > 0.5
+        assert torch.equal(y[active], tensors[f"{c}.y"][active]), f"{c}: oracle differs from the reference"
+    for i, (kind, mixer, *_rest) in enumerate(step.layers):
+        if kind == om.LINEAR:
+            p = f"state.layers.{i}.linear_attn."
+            assert torch.equal(mixer.recurrent_state, tensors[p + "recurrent_state"])
+            assert torch.equal(mixer.conv_state, tensors[p + "conv_state"])
+            assert torch.equal(mixer.pending_key, tensors[p + "pending_key_state"])
+            assert torch.equal(mixer.pending_delta, tensors[p + "pending_delta_state"])
+            assert torch.equal(mixer.pending_decay, tensors[p + "pending_decay_state"])
+            assert torch.equal(mixer.pending_input, tensors[p + "pending_input_state"])
+        else:
+            tail = K  # the junk positions written by idle rows
+            assert torch.equal(mixer.k_cache[:, :, :-tail], tensors[f"state.layers.{i}.self_attn.k_cache"][:, :, :-tail])
+            assert torch.equal(mixer.v_cache[:, :, :-tail], tensors[f"state.layers.{i}.self_attn.v_cache"][:, :, :-tail])
