@@ -193,6 +193,45 @@ int q38_attn_prefill(const void* qkv, int64_t ld_qkv, const void* q_norm_weight,
                      q38_stream_t stream);
 
 /*
+ * K verify tokens per row through the gated delta rule with commit-on-accept: first the last verify
+ * step's first accepted[b] tokens are committed to the row's state and conv state from the pending
+ * buffers, then the K new tokens run from the committed state as one small chunk without changing it,
+ * their updates (key, delta, log decay, conv input) replacing the pending buffers; out gets the gated
+ * RMS norm times SiLU(z), e5m2, per token. Rows with active 0 keep their states exactly. Replaces
+ * GatedDeltaNetStep.verify (qwen38_inf2/model.py:376-454) with _commit_and_read (:262-271; NKI
+ * delta_verify_state kernels.py:936-968) between its projections.
+ *
+ *   qkvz, ab      as q38_gdn_decode with rows b * tokens + t
+ *   pending_key   f32 [batch, tokens, num_v_heads, head_k]; pending_delta f32 [batch, tokens, num_v_heads,
+ *                 head_v]; pending_decay f32 [batch, tokens, num_v_heads]; pending_input bf16 [batch, tokens,
+ *                 conv_dim]: read (the commit), then replaced
+ *   accepted      int32 [batch], 0 .. tokens; 0 after a decode or prefill step
+ *   out           e5m2 [batch * tokens, ld_out]
+ */
+int q38_gdn_verify_commit(const void* qkvz, int64_t ld_qkvz, const void* ab, int64_t ld_ab, void* conv_state,
+                          const void* conv_weight, const void* a_log, const void* dt_bias, const void* norm_weight,
+                          void* state, void* pending_key, void* pending_delta, void* pending_decay,
+                          void* pending_input, const int32_t* position, const float* active, const int32_t* accepted,
+                          void* out, int64_t ld_out, int64_t batch, int tokens, int num_k_heads, int num_v_heads,
+                          int head_k, int head_v, int conv_kernel, float eps, q38_stream_t stream);
+
+/*
+ * K verify tokens per row of gated full attention with a BF16 KV cache: token t attends to cache
+ * positions < position and to the step's own keys 0 .. t; the tokens' keys and values are written at
+ * position .. position + tokens - 1 (rows with active 0 at the cache's last `tokens` positions).
+ * Replaces FullAttentionStep.verify (qwen38_inf2/model.py:641-675; NKI verify_attention
+ * kernels.py:468-488) between its projections.
+ *
+ *   qkv      bf16 [batch * tokens, ld_qkv], rows b * tokens + t, laid out as for q38_attn_decode
+ *   cos, sin bf16 [batch * tokens, rot_dim]
+ *   out      e5m2 [batch * tokens, ld_out]
+ */
+int q38_attn_verify(const void* qkv, int64_t ld_qkv, const void* q_norm_w, const void* k_norm_w, const void* cos,
+                    const void* sin, void* k_cache, void* v_cache, int64_t max_seq, const int32_t* position,
+                    const float* active, void* out, int64_t ld_out, int64_t batch, int tokens, int num_q_heads,
+                    int num_kv_heads, int head_dim, int rot_dim, float eps, q38_stream_t stream);
+
+/*
  * One decode token per row of gated full attention with a BF16 KV cache: q/k RMS norms (1 + w),
  * partial rotary on the first rot_dim dims, softmax attention over cache positions < position plus
  * the token's own key/value, times sigmoid(gate), rounded to e5m2 for o_proj; the token's key and

@@ -14,7 +14,7 @@
 // gates and recurrence (products and sums unfused, as PyTorch evaluates them); the output o rounded
 // to bf16 before the gated RMS norm; bf16 after the norm, after the norm weight, and after the SiLU(z)
 // gate; finally e5m2 for out_proj.
-#include "q38_common.cuh"
+#include "gdn_common.cuh"
 
 namespace {
 
@@ -38,45 +38,6 @@ struct GdnArgs {
   int num_k_heads, num_v_heads;
   float eps;
 };
-
-__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
-               "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void group_bar(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
-
-// CPL consecutive bf16 of a state row, as one vector access when CPL == 4 (8 bytes, conflict-free
-// across a warp's 32 lanes), element by element otherwise.
-template <int CPL>
-__device__ __forceinline__ void load_row(const __nv_bfloat16* p, float (&v)[CPL]) {
-  if constexpr (CPL == 4) {
-    const uint2 u = *reinterpret_cast<const uint2*>(p);
-    const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&u.x);
-    const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&u.y);
-    v[0] = __low2float(a);
-    v[1] = __high2float(a);
-    v[2] = __low2float(b);
-    v[3] = __high2float(b);
-  } else {
-#pragma unroll
-    for (int t = 0; t < CPL; ++t) v[t] = __bfloat162float(p[t]);
-  }
-}
-template <int CPL>
-__device__ __forceinline__ void store_row(__nv_bfloat16* p, const float (&v)[CPL]) {
-  if constexpr (CPL == 4) {
-    __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]);
-    __nv_bfloat162 b = __floats2bfloat162_rn(v[2], v[3]);
-    uint2 u;
-    u.x = *reinterpret_cast<uint32_t*>(&a);
-    u.y = *reinterpret_cast<uint32_t*>(&b);
-    *reinterpret_cast<uint2*>(p) = u;
-  } else {
-#pragma unroll
-    for (int t = 0; t < CPL; ++t) p[t] = __float2bfloat16_rn(v[t]);
-  }
-}
 
 template <int DK, int DV, int R>
 struct GdnSmem {

@@ -194,6 +194,39 @@ def attn_prefill(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, out, works
               rot_dim, eps, workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream())
 
 
+def gdn_verify(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, state, pending_key, pending_delta,
+               pending_decay, pending_input, position, active, accepted, out, *, batch: int, tokens: int,
+               num_k_heads: int, num_v_heads: int, head_k: int, head_v: int, eps: float) -> None:
+    """K verify tokens per row with commit-on-accept (rows b * tokens + t of qkvz/ab/out)."""
+    _cuda(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, state, pending_key, pending_delta,
+          pending_decay, pending_input, position, active, accepted, out)
+    _need(position.dtype == torch.int32 and accepted.dtype == torch.int32 and active.dtype == torch.float32,
+          "position/accepted int32, active float32")
+    _need(pending_key.dtype == torch.float32 and pending_delta.dtype == torch.float32 and
+          pending_decay.dtype == torch.float32 and pending_input.dtype == BF16, "pending buffers f32 (input bf16)")
+    for t in (state, conv_state, pending_key, pending_delta, pending_decay, pending_input):
+        _need(t.is_contiguous(), "state and pending buffers must be contiguous")
+    _need(pending_key.shape[:2] == (batch, tokens), "pending buffers [batch, tokens, ...]")
+    _lib.call("q38_gdn_verify_commit", qkvz.data_ptr(), qkvz.stride(0), ab.data_ptr(), ab.stride(0),
+              conv_state.data_ptr(), conv_weight.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(),
+              norm_weight.data_ptr(), state.data_ptr(), pending_key.data_ptr(), pending_delta.data_ptr(),
+              pending_decay.data_ptr(), pending_input.data_ptr(), position.data_ptr(), active.data_ptr(),
+              accepted.data_ptr(), out.data_ptr(), out.stride(0), batch, tokens, num_k_heads, num_v_heads, head_k,
+              head_v, conv_weight.shape[1], eps, _stream())
+
+
+def attn_verify(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, position, active, out, *, batch: int, tokens: int,
+                num_q_heads: int, num_kv_heads: int, head_dim: int, rot_dim: int, eps: float) -> None:
+    """K verify tokens per row of gated attention (rows b * tokens + t); writes the tokens' K/V."""
+    _cuda(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, position, active, out)
+    _need(cos.is_contiguous() and sin.is_contiguous() and cos.shape[-1] == rot_dim, "cos/sin [rows, rot] contiguous")
+    _need(k_cache.is_contiguous() and v_cache.is_contiguous(), "caches must be contiguous")
+    _lib.call("q38_attn_verify", qkv.data_ptr(), qkv.stride(0), q_norm_w.data_ptr(), k_norm_w.data_ptr(),
+              cos.data_ptr(), sin.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2],
+              position.data_ptr(), active.data_ptr(), out.data_ptr(), out.stride(0), batch, tokens, num_q_heads,
+              num_kv_heads, head_dim, rot_dim, eps, _stream())
+
+
 def lm_head_groupmax(x: torch.Tensor, lin: DeviceBF16Linear, maxima: torch.Tensor, group: int = 32) -> None:
     _cuda(x, maxima)
     rows, k = x.shape

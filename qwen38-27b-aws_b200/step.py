@@ -8,6 +8,9 @@ exactly as `Qwen38Step.forward` routes them (model.py:983-995):
 * decode: inputs_embeds [B, 1, H], cos/sin [B, 1, rot], position int32 [B], active float32 [B];
 * prefill: inputs_embeds [1, C, H], cos/sin [1, C, rot], slot/start/n_valid int32 [1]: one row's chunk
   of C tokens, eagerly (the chunk length varies), with buffers sized on first use per C;
+* verify: inputs_embeds [B, K, H], cos/sin [B, K, rot], position/active as decode, accepted int32 [B]:
+  commit each row's accepted tokens of the last verify step, then run K tokens without changing the
+  states (their updates kept pending), eagerly (needs verify_tokens=K at construction);
 * save_slot / restore_slot int32 [1]: copy one row's recurrent states, return inputs_embeds.
 
 `B200Head.run_graph(hidden=...)` is the reference's lm_head graph call (generate.py:194):
@@ -45,6 +48,7 @@ class _GDN:
     out: ops.DeviceLinear
     conv_state: torch.Tensor
     state: torch.Tensor
+    pending: tuple | None = None  # verify: (key f32, delta f32, log decay f32, conv input bf16) [B, K, ...]
 
 
 @dataclass
@@ -76,7 +80,7 @@ class B200Step:
 
     def __init__(self, cfg: TextConfig, layer_weights, max_seq_len: int, batch_size: int, tp_degree: int = 1,
                  rank: int = 0, device: torch.device | str | None = None, saved_states: bool = False,
-                 use_graph: bool = True, process_group=None):
+                 use_graph: bool = True, process_group=None, verify_tokens: int = 0):
         """`layer_weights(i)` returns layer i's unsharded weights (weights.synthetic_layer names), or
         `layer_weights` is a dict holding them all."""
         cfg.validate_tp(tp_degree)
@@ -86,6 +90,7 @@ class B200Step:
         self.group = process_group
         self.use_graph = use_graph
         self.saved = saved_states
+        self.verify_tokens = verify_tokens
         get = layer_weights if callable(layer_weights) else (lambda i: layer_weights)
         with torch.cuda.device(self.device):
             self.layers = [self._prepare(i, W.shard_layer(cfg, get(i), i, rank, tp_degree)) for i in range(cfg.num_hidden_layers)]
@@ -113,6 +118,13 @@ class B200Step:
                 conv_state=torch.zeros(rows, conv_dim, cfg.linear_conv_kernel_dim - 1, dtype=BF16, device=dev),
                 state=torch.zeros(rows, hv, cfg.linear_key_head_dim, cfg.linear_value_head_dim, dtype=BF16, device=dev),
             )
+            K = self.verify_tokens
+            if K:
+                f32 = dict(dtype=torch.float32, device=dev)
+                mixer.pending = (torch.zeros(self.batch, K, hv, cfg.linear_key_head_dim, **f32),
+                                 torch.zeros(self.batch, K, hv, cfg.linear_value_head_dim, **f32),
+                                 torch.zeros(self.batch, K, hv, **f32),
+                                 torch.zeros(self.batch, K, conv_dim, dtype=BF16, device=dev))
         elif cfg.layer_types[i] == FULL:
             kvh = cfg.kv_heads_per_rank(self.tp)
             mixer = _Attn(
@@ -133,6 +145,7 @@ class B200Step:
         self.position = torch.zeros(self.batch, dtype=torch.int32, device=self.device)
         self.active = torch.zeros(self.batch, dtype=torch.float32, device=self.device)
         self._prefill_acts = {}
+        self._verify_acts = None
 
     def _fill_acts(self, a, rows: int) -> None:
         """Activation buffers for `rows` token rows on `a` (the step itself for decode, a _Acts for a
@@ -194,9 +207,10 @@ class B200Step:
         """Layer i alone, eagerly, on self.x and the loaded decode inputs (for layer-by-layer checks)."""
         self._layer(self.layers[i], self)
 
-    def _layer(self, l: _Layer, a, chunk=None):
+    def _layer(self, l: _Layer, a, chunk=None, verify: int = 0):
         """DecoderLayer.forward (model.py:918-930) on the activation set `a`: a decode step over all
-        rows, or with `chunk` = (slot, start, n_valid) one row's prefill chunk of a.x's rows."""
+        rows, with `chunk` = (slot, start, n_valid) one row's prefill chunk of a.x's rows, or with
+        `verify` = K the K tokens of every row (a.x row b * K + t)."""
         cfg, eps, tp = self.cfg, self.cfg.rms_norm_eps, self.tp
         m = l.mixer
         if l.kind == LINEAR:
@@ -205,7 +219,10 @@ class B200Step:
             ops.bf16_linear(a.hb, m.ab, a.ab, splits=a.ab_splits, workspace=a.workspace)
             heads = dict(num_k_heads=cfg.linear_num_key_heads // tp, num_v_heads=cfg.linear_num_value_heads // tp,
                          head_k=cfg.linear_key_head_dim, head_v=cfg.linear_value_head_dim, eps=eps)
-            if chunk is None:
+            if verify:
+                ops.gdn_verify(a.proj, a.ab, m.conv_state, m.conv_w, m.a_log, m.dt_bias, m.norm_w, m.state, *m.pending,
+                               a.position, a.active, a.accepted, a.mix_gdn, batch=self.batch, tokens=verify, **heads)
+            elif chunk is None:
                 ops.gdn_decode(a.proj, a.ab, m.conv_state, m.conv_w, m.a_log, m.dt_bias, m.norm_w, m.state,
                                a.position, a.active, a.mix_gdn, batch=self.batch, **heads)
             else:
@@ -218,7 +235,10 @@ class B200Step:
             self._gemm(a, a.hq, m.qkv, a.proj)
             heads = dict(num_q_heads=cfg.num_attention_heads // tp, num_kv_heads=cfg.kv_heads_per_rank(tp),
                          head_dim=cfg.head_dim, rot_dim=cfg.rotary_dim, eps=eps)
-            if chunk is None:
+            if verify:
+                ops.attn_verify(a.proj, m.q_norm, m.k_norm, a.cos, a.sin, m.k_cache, m.v_cache, a.position, a.active,
+                                a.mix_attn, batch=self.batch, tokens=verify, **heads)
+            elif chunk is None:
                 ops.attn_decode(a.proj, m.q_norm, m.k_norm, a.cos, a.sin, m.k_cache, m.v_cache, a.position, a.active,
                                 a.mix_attn, batch=self.batch, **heads)
             else:
@@ -278,6 +298,38 @@ class B200Step:
         self._layer(self.layers[i], a, (slot, start, n_valid))
         return a.x
 
+    # ------------------------------------------------------------------ verify
+    def verify(self, embeds, cos, sin, position, active, accepted) -> torch.Tensor:
+        """K tokens per row for speculative decoding (model.py:983-995 with `accepted`): embeds [B, K, H]
+        -> hidden [B * K, H] on the device."""
+        K = self.verify_tokens
+        B = self.batch
+        if not K:
+            raise ValueError("this step was built without verify_tokens")
+        if tuple(embeds.shape[:2]) != (B, K):
+            raise ValueError(f"verify takes [{B}, {K}, hidden], got {tuple(embeds.shape)}")
+        acc = accepted.reshape(-1)
+        if acc.numel() != B or int(acc.min()) < 0 or int(acc.max()) > K:
+            raise ValueError(f"accepted must hold {B} counts in 0..{K}")
+        a = self._verify_acts
+        if a is None:
+            a = _Acts()
+            with torch.cuda.device(self.device):
+                self._fill_acts(a, B * K)
+                a.position = torch.zeros(B, dtype=torch.int32, device=self.device)
+                a.active = torch.zeros(B, dtype=torch.float32, device=self.device)
+                a.accepted = torch.zeros(B, dtype=torch.int32, device=self.device)
+            self._verify_acts = a
+        a.x.copy_(embeds.reshape(B * K, -1), non_blocking=True)
+        a.cos.copy_(cos.reshape(B * K, -1), non_blocking=True)
+        a.sin.copy_(sin.reshape(B * K, -1), non_blocking=True)
+        a.position.copy_(position.reshape(-1).to(torch.int32), non_blocking=True)
+        a.active.copy_(active.reshape(-1).to(torch.float32), non_blocking=True)
+        a.accepted.copy_(acc.to(torch.int32), non_blocking=True)
+        for l in self.layers:
+            self._layer(l, a, verify=K)
+        return a.x
+
     def kernels_per_decode_step(self) -> int:
         """Launches of this library's kernels in one decode step (for the bench's gpu_launches)."""
         n = 0
@@ -317,7 +369,9 @@ class B200Step:
             self.copy_states(inputs)
             return inputs_embeds
         if "accepted" in inputs:
-            raise NotImplementedError("verify steps are not built yet")
+            out = self.verify(inputs_embeds, inputs["cos"], inputs["sin"], inputs["position"], inputs["active"],
+                              inputs["accepted"])
+            return out.to("cpu").reshape(self.batch, self.verify_tokens, -1)
         if "slot" in inputs:
             scalar = lambda name: int(inputs[name].reshape(-1)[0])  # noqa: E731
             out = self.prefill(inputs_embeds, inputs["cos"], inputs["sin"], scalar("slot"), scalar("start"),
