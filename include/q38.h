@@ -251,6 +251,36 @@ int q38_attn_decode(const void* qkv, int64_t ld_qkv, const void* q_norm_w, const
                     int num_kv_heads, int head_dim, int rot_dim, float eps, q38_stream_t stream);
 
 /*
+ * Tensor-parallel communicator for the fused GEMM + all-reduce. Each rank creates one exchange region
+ * (cudaMalloc) holding the residual stream x bf16 [max_tokens, hidden], the receive slots and the
+ * arrival flags; q38_comm_ipc_handle exports it, the host passes every rank's handle to every rank
+ * (the handles of ranks 0 .. world - 1, back to back), and q38_comm_connect maps the peers' regions
+ * over NVLink (CUDA IPC with peer access). No reference counterpart: it stands in for the NxD
+ * collective plumbing behind the reference's all_reduce (qwen38_inf2/neuron.py:9, model.py:44-45).
+ */
+typedef void* q38_comm_t;
+int q38_comm_init(int rank, int world, int64_t max_tokens, int64_t hidden, q38_comm_t* comm);
+size_t q38_comm_ipc_handle_bytes(void);
+int q38_comm_ipc_handle(q38_comm_t comm, void* handle, size_t handle_bytes);
+int q38_comm_connect(q38_comm_t comm, const void* handles);
+void* q38_comm_residual(q38_comm_t comm);  /* this rank's x, bf16 [max_tokens, hidden] */
+int q38_comm_destroy(q38_comm_t comm);
+
+/*
+ * x += all_reduce(bf16(e5m2(x_q) @ W^T)) over the communicator's ranks, in one kernel per rank: each
+ * 32-token x 128-feature output block has an owner rank; the other ranks store their bf16 partial
+ * into the owner's receive slot over NVLink, the owner sums the partials in rank order (fp32, one
+ * bf16 rounding), adds the residual (bf16) and stores the result into every rank's x. Every rank makes
+ * the same sequence of calls. x is the communicator's residual stream (rows 0 .. tokens - 1), so
+ * features == hidden. Replaces the row-parallel projection plus all-reduce of o_proj / out_proj /
+ * down_proj (qwen38_inf2/model.py:259, :374, :639 with the NxD reduce, neuron.py:9). Needs the whole
+ * grid resident (returns Q38_ERR_UNSUPPORTED otherwise) and at most 8 K splits; a wait on a peer that
+ * runs out (2 s) records Q38_ERR_TIMEOUT in the device error word.
+ */
+int q38_fp8_gemm_allreduce(const void* x_q, int64_t tokens, int64_t k, const void* w, const void* w_sf,
+                           int64_t features, int splits, q38_comm_t comm, q38_stream_t stream);
+
+/*
  * lm_head candidates: maxima[r, j] = max over the `group` vocab rows v in group j of
  * sum_k x[r, k] * w[v, k], fp32 (x bf16 [rows, k], w bf16 [vocab, k] pre-tiled). Replaces HeadStep.forward's
  * logits and group maxima (qwen38_inf2/model.py:890-900) and the NKI lm_head_group_maxima

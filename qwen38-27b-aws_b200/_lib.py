@@ -75,6 +75,13 @@ SIGNATURES = {
         [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
          c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p],
     ),
+    "q38_comm_init": (c_int, [c_int, c_int, c_int64, c_int64, ctypes.POINTER(c_void_p)]),
+    "q38_comm_ipc_handle_bytes": (c_size_t, []),
+    "q38_comm_ipc_handle": (c_int, [c_void_p, c_void_p, c_size_t]),
+    "q38_comm_connect": (c_int, [c_void_p, c_void_p]),
+    "q38_comm_residual": (c_void_p, [c_void_p]),
+    "q38_comm_destroy": (c_int, [c_void_p]),
+    "q38_fp8_gemm_allreduce": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
     "q38_lm_head_groupmax": (
         c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int, c_void_p, c_int64, c_void_p]
     ),

@@ -27,6 +27,7 @@
 #include <cmath>
 #include <cstdio>
 
+#include "comm_internal.cuh"
 #include "q38_common.cuh"
 
 namespace {
@@ -37,7 +38,7 @@ constexpr int BM = 128;          // features per tile (MMA M)
 constexpr int BK_BYTES = 128;    // K bytes per pipeline stage (one 128-byte swizzle row)
 constexpr int SF_BLOCK = 512;    // scale bytes per (128 rows, 128 K) block
 
-enum : int { EPI_BF16 = 0, EPI_RESIDUAL = 1, EPI_GROUPMAX = 2 };
+enum : int { EPI_BF16 = 0, EPI_RESIDUAL = 1, EPI_GROUPMAX = 2, EPI_ALLREDUCE = 3 };
 
 // PAIR: the 2-SM form. A cluster pair of CTAs computes 256 weight rows x NTOK tokens with
 // tcgen05.mma.cta_group::2 issued by the even CTA; each CTA loads its own 128 weight rows and half of
@@ -73,6 +74,7 @@ struct GemmArgs {
   unsigned int* counters; // one per output tile (workspace mode)
   int cluster;            // > 0: epilogue through shared memory, the `cluster` K splits of a tile
                           // forming one thread-block cluster; 0: workspace mode
+  ArArgs ar;              // EPI_ALLREDUCE: the ranks' exchange regions
 };
 
 // Epilogue staging (cluster mode), reusing the pipeline buffers once the accumulator is final:
@@ -81,6 +83,41 @@ struct GemmArgs {
 constexpr int TOK_BLOCK = 32;  // tokens per TMA box of the residual / output
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// The epilogue warps' barrier that also returns, to every one of them, whether any passed `pred`.
+__device__ __forceinline__ bool epi_bar_or(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred))
+      : "memory");
+  return r != 0;
+}
+
+// Peer-memory exchange of the fused all-reduce. Flags carry the call's epoch; a store's data is made
+// visible system-wide (fence.sc.sys by every storing thread, then the CTA barrier) before one thread
+// releases the flag, and every reader acquires the flag itself before it reads.
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Waits (bounded) until *flag >= epoch; false on timeout (recorded in the device error word).
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch) {
+  if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+  const unsigned long long t0 = global_ns();
+  while (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) < 0) {
+    if (global_ns() - t0 > kWaitLimitNs) {
+      record_error(Q38_ERR_TIMEOUT);
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
+}
 
 // Applies the epilogue to 16 consecutive tokens of one feature row.
 __device__ __forceinline__ void epilogue16(const GemmArgs& a, int row, int t0, const float (&v)[16], int lane) {
@@ -449,7 +486,7 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     // The staged bf16 slice goes out by TMA (boxes past the last token or feature are clipped).
-    if (warp >= 2 && a.epilogue != EPI_GROUPMAX) {
+    if (warp >= 2 && a.epilogue != EPI_GROUPMAX && a.epilogue != EPI_ALLREDUCE) {
       fence_proxy_async_shared();
       epi_bar();
       if (warp == 2 && lane == 0 && !flags[0] && live) {
@@ -458,6 +495,81 @@ __global__ void __launch_bounds__(192, 1)
         bulk_commit();
         bulk_wait_read0();
       }
+    }
+    // Fused all-reduce of the staged bf16 partial: the tile's owner rank sums every rank's partial in
+    // rank order (fp32, one bf16 rounding), adds the residual and writes the result into every rank's
+    // residual stream; the other ranks push their partial to the owner and wait for the result.
+    if (warp >= 2 && a.epilogue == EPI_ALLREDUCE) {
+      // Every branch below is uniform across the 128 epilogue threads: `failed` only changes through
+      // epi_bar_or, which hands all of them the same value.
+      bool failed = epi_bar_or(flags[0] != 0);  // also: the staged partial is complete
+      const ArArgs& r = a.ar;
+      const int te = threadIdx.x - 64;
+      const uint32_t ep = *reinterpret_cast<volatile uint32_t*>(r.epoch);
+      const int par = static_cast<int>(ep & 1u);
+      const int owner = static_cast<int>(static_cast<int64_t>(mt) * r.world / r.ftiles);
+      const __nv_bfloat16* sbase = reinterpret_cast<const __nv_bfloat16*>(stage);
+      for (int b = b0; b < b1 && live && !failed; ++b) {
+        const int t0 = n0 + b * TOK_BLOCK;
+        if (t0 >= a.T) break;
+        const int slot = (t0 / TOK_BLOCK) * r.ftiles + mt;
+        const __nv_bfloat16* sblk = sbase + b * TOK_BLOCK * BM;
+        if (owner != r.rank) {
+          __nv_bfloat16* dst = r.recv[owner] + (static_cast<int64_t>(par) * r.world + r.rank) * r.tmax * r.hidden;
+          for (int c = te; c < TOK_BLOCK * (BM / 8); c += 128) {
+            const int row = c / (BM / 8), cc = c % (BM / 8);
+            const int t = t0 + row, f = m0 + cc * 8;
+            if (t < a.T && f < a.F)
+              *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(t) * r.hidden + f) =
+                  *reinterpret_cast<const uint4*>(sblk + row * BM + cc * 8);
+          }
+          __threadfence_system();
+          epi_bar();
+          if (te == 0) st_release_sys(r.flags[owner] + (par * r.world + r.rank) * r.slots + slot, ep);
+        } else {
+          bool bad = false;
+          for (int c = te; c < TOK_BLOCK * (BM / 8) && !bad; c += 128) {
+            const int row = c / (BM / 8), cc = c % (BM / 8);
+            const int t = t0 + row, f = m0 + cc * 8;
+            if (t >= a.T || f >= a.F) continue;
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int src = 0; src < r.world && !bad; ++src) {
+              uint4 u;
+              if (src == r.rank) {
+                u = *reinterpret_cast<const uint4*>(sblk + row * BM + cc * 8);
+              } else {
+                bad = !wait_flag(r.flags[r.rank] + (par * r.world + src) * r.slots + slot, ep);
+                u = *reinterpret_cast<const uint4*>(r.recv[r.rank] +
+                                                    ((static_cast<int64_t>(par) * r.world + src) * r.tmax + t) * r.hidden + f);
+              }
+              const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], __bfloat162float(h[j]));
+            }
+            if (bad) break;
+            const int64_t at = static_cast<int64_t>(t) * r.hidden + f;
+            const uint4 xu = *reinterpret_cast<const uint4*>(r.x[r.rank] + at);
+            const __nv_bfloat16* xh = reinterpret_cast<const __nv_bfloat16*>(&xu);
+            uint4 ou;
+            __nv_bfloat16* oh = reinterpret_cast<__nv_bfloat16*>(&ou);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) oh[j] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(xh[j]), bf16r(acc[j])));
+            for (int q = 0; q < r.world; ++q) *reinterpret_cast<uint4*>(r.x[q] + at) = ou;
+          }
+          __threadfence_system();
+          failed = epi_bar_or(bad);
+          if (te == 0 && !failed)
+            for (int q = 0; q < r.world; ++q)
+              if (q != r.rank) st_release_sys(r.gflags[q] + par * r.slots + slot, ep);
+        }
+      }
+      // A rank that does not own the tile waits until the owner's result is in its residual stream.
+      if (owner != r.rank && live && !failed && te == 0)
+        for (int b = b0; b < b1; ++b) {
+          const int t0 = n0 + b * TOK_BLOCK;
+          if (t0 >= a.T) break;
+          if (!wait_flag(r.gflags[r.rank] + par * r.slots + (t0 / TOK_BLOCK) * r.ftiles + mt, ep)) break;
+        }
     }
     // No CTA leaves while a peer may still read its shared memory (and a pair frees its tensor memory
     // together).
@@ -471,11 +583,21 @@ __global__ void __launch_bounds__(192, 1)
     if constexpr (PAIR) tmem_dealloc_pair(tmem, C::TMEM_COLS);
     else tmem_dealloc(tmem, C::TMEM_COLS);
   }
+  // The last CTA of a fused all-reduce call advances the epoch for the next call (every CTA has read it).
+  if (a.epilogue == EPI_ALLREDUCE && threadIdx.x == 0) {
+    __threadfence();
+    const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+    if (atomicAdd(a.ar.done, 1u) == total - 1) {
+      *a.ar.done = 0u;
+      atomicAdd(a.ar.epoch, 1u);
+    }
+  }
 }
 
 template <int NTOK, bool MX, bool PAIR = false>
 int launch_gemm(const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap& tr, const GemmArgs& a, dim3 grid,
-                cudaStream_t stream, const CUtensorMap* tw = nullptr, const CUtensorMap* tsf = nullptr) {
+                cudaStream_t stream, const CUtensorMap* tw = nullptr, const CUtensorMap* tsf = nullptr,
+                bool resident = false) {
   using C = Cfg<NTOK, MX, PAIR>;
   // The shared-memory opt-in is per device; remember which devices have it.
   static unsigned long long done_mask = 0;
@@ -499,6 +621,18 @@ int launch_gemm(const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap&
   attr[0].val.clusterDim.z = a.cluster > 1 ? static_cast<unsigned>(a.cluster) : 1u;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (resident) {
+    // CTAs that wait on other GPUs must all be running at once: the whole grid has to fit.
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, gemm_kernel<NTOK, MX, PAIR>, &cfg);
+    if (e != cudaSuccess) return q38host::cuda_status(e, "cudaOccupancyMaxActiveClusters");
+    const unsigned csize = attr[0].val.clusterDim.x * attr[0].val.clusterDim.z;
+    const unsigned need = grid.x * grid.y * grid.z / csize;
+    if (static_cast<unsigned>(clusters) < need)
+      return q38host::set_error("fused all-reduce: %u clusters of %u CTAs must be resident, the device holds %d", need,
+                                csize, clusters),
+             Q38_ERR_UNSUPPORTED;
+  }
   e = cudaLaunchKernelEx(&cfg, gemm_kernel<NTOK, MX, PAIR>, tx, ty, tr, tw ? *tw : tx, tsf ? *tsf : tx, a);
   return q38host::cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "gemm launch");
 }
@@ -565,23 +699,13 @@ extern "C" size_t q38_fp8_gemm_workspace_bytes(int64_t tokens, int64_t features,
   return counters + static_cast<size_t>(splits) * tiles * BM * ntok * sizeof(float);
 }
 
-extern "C" int q38_fp8_gemm(const void* x, int64_t tokens, int64_t k, const void* w, const void* w_sf,
-                            int64_t features, int epilogue, void* y, int64_t ldy, const void* residual, int64_t ldr,
-                            int splits, void* workspace, size_t workspace_bytes, q38_stream_t stream) {
-  using namespace q38host;
-  if (!x || !w || !w_sf || !y) return set_error("q38_fp8_gemm: null pointer"), Q38_ERR_ARG;
-  if (tokens <= 0 || k <= 0 || features <= 0 || tokens > (1 << 24) || features > (1 << 30) || k > (1 << 30))
-    return set_error("q38_fp8_gemm: bad sizes tokens=%lld k=%lld features=%lld", (long long)tokens, (long long)k,
-                     (long long)features),
-           Q38_ERR_ARG;
-  if (k % 16 != 0 || !aligned16(x) || !aligned16(w) || !aligned16(w_sf))
-    return set_error("q38_fp8_gemm: k must be a multiple of 16 and x, w, w_sf 16-byte aligned"), Q38_ERR_ARG;
-  if (epilogue != Q38_EPI_BF16 && epilogue != Q38_EPI_RESIDUAL)
-    return set_error("q38_fp8_gemm: unknown epilogue %d", epilogue), Q38_ERR_ARG;
-  if (epilogue == Q38_EPI_RESIDUAL && !residual) return set_error("q38_fp8_gemm: residual epilogue needs residual"), Q38_ERR_ARG;
-  if (ldy < features || (residual && ldr < features)) return set_error("q38_fp8_gemm: leading dimension too small"), Q38_ERR_ARG;
-  if (splits < 1) return set_error("q38_fp8_gemm: splits must be >= 1"), Q38_ERR_ARG;
+namespace {
 
+// The FP8 GEMM for every epilogue; `ar` (EPI_ALLREDUCE) carries the communicator's device view.
+int gemm_fp8(const void* x, int64_t tokens, int64_t k, const void* w, const void* w_sf, int64_t features, int epilogue,
+             void* y, int64_t ldy, const void* residual, int64_t ldr, int splits, void* workspace,
+             size_t workspace_bytes, const ArArgs* ar, cudaStream_t s, const char* who) {
+  using namespace q38host;
   const int ntok = token_tile(tokens);
   const int nkc = static_cast<int>(cdiv(k, BK_BYTES));
   int kc_per = static_cast<int>(cdiv(nkc, std::min(splits, nkc)));
@@ -599,14 +723,17 @@ extern "C" int q38_fp8_gemm(const void* x, int64_t tokens, int64_t k, const void
   a.ldy = ldy;
   a.res = static_cast<const __nv_bfloat16*>(residual);
   a.ldr = ldr;
+  if (ar) a.ar = *ar;
   CUtensorMap tx, ty, tr;
   int st = setup_epilogue(a, splits, tokens, features, y, ldy, epilogue == Q38_EPI_RESIDUAL ? residual : nullptr, ldr,
-                          workspace, workspace_bytes, &ty, &tr, "q38_fp8_gemm");
+                          workspace, workspace_bytes, &ty, &tr, who);
   if (st != Q38_OK) return st;
+  if (ar && a.cluster == 0)
+    return set_error("%s: the fused all-reduce takes at most %d K splits", who, kMaxClusterSplits), Q38_ERR_UNSUPPORTED;
   st = encode_tmap_2d(&tx, x, tokens, k, 1, ntok, BK_BYTES);
   if (st != Q38_OK) return st;
   if (a.cluster == 0) ty = tr = tx;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool resident = ar != nullptr;
   // The 2-SM form for full 256-token tiles whose cluster (2 x splits) stays portable.
   if (ntok == 256 && a.cluster > 0 && 2 * a.cluster <= kMaxClusterSplits && features > BM) {
     // Each CTA of a pair loads half of the 256-token tile: the activation box is 128 rows.
@@ -620,10 +747,59 @@ extern "C" int q38_fp8_gemm(const void* x, int64_t tokens, int64_t k, const void
     if (st != Q38_OK) return st;
     dim3 grid(static_cast<unsigned>(2 * cdiv(features, 2 * BM)), static_cast<unsigned>(cdiv(tokens, ntok)),
               static_cast<unsigned>(splits));
-    return launch_gemm<256, true, true>(tx, ty, tr, a, grid, s, &tw, &tsf);
+    return launch_gemm<256, true, true>(tx, ty, tr, a, grid, s, &tw, &tsf, resident);
   }
   dim3 grid(static_cast<unsigned>(cdiv(features, BM)), static_cast<unsigned>(cdiv(tokens, ntok)), static_cast<unsigned>(splits));
-  return ntok == 256 ? launch_gemm<256, true>(tx, ty, tr, a, grid, s) : launch_gemm<128, true>(tx, ty, tr, a, grid, s);
+  return ntok == 256 ? launch_gemm<256, true>(tx, ty, tr, a, grid, s, nullptr, nullptr, resident)
+                     : launch_gemm<128, true>(tx, ty, tr, a, grid, s, nullptr, nullptr, resident);
+}
+
+int check_gemm_args(const void* x, int64_t tokens, int64_t k, const void* w, const void* w_sf, int64_t features,
+                    int splits, const char* who) {
+  using namespace q38host;
+  if (!x || !w || !w_sf) return set_error("%s: null pointer", who), Q38_ERR_ARG;
+  if (tokens <= 0 || k <= 0 || features <= 0 || tokens > (1 << 24) || features > (1 << 30) || k > (1 << 30))
+    return set_error("%s: bad sizes tokens=%lld k=%lld features=%lld", who, (long long)tokens, (long long)k,
+                     (long long)features),
+           Q38_ERR_ARG;
+  if (k % 16 != 0 || !aligned16(x) || !aligned16(w) || !aligned16(w_sf))
+    return set_error("%s: k must be a multiple of 16 and x, w, w_sf 16-byte aligned", who), Q38_ERR_ARG;
+  if (splits < 1) return set_error("%s: splits must be >= 1", who), Q38_ERR_ARG;
+  return Q38_OK;
+}
+
+}  // namespace
+
+extern "C" int q38_fp8_gemm(const void* x, int64_t tokens, int64_t k, const void* w, const void* w_sf,
+                            int64_t features, int epilogue, void* y, int64_t ldy, const void* residual, int64_t ldr,
+                            int splits, void* workspace, size_t workspace_bytes, q38_stream_t stream) {
+  using namespace q38host;
+  int st = check_gemm_args(x, tokens, k, w, w_sf, features, splits, "q38_fp8_gemm");
+  if (st != Q38_OK) return st;
+  if (!y) return set_error("q38_fp8_gemm: null pointer"), Q38_ERR_ARG;
+  if (epilogue != Q38_EPI_BF16 && epilogue != Q38_EPI_RESIDUAL)
+    return set_error("q38_fp8_gemm: unknown epilogue %d", epilogue), Q38_ERR_ARG;
+  if (epilogue == Q38_EPI_RESIDUAL && !residual) return set_error("q38_fp8_gemm: residual epilogue needs residual"), Q38_ERR_ARG;
+  if (ldy < features || (residual && ldr < features)) return set_error("q38_fp8_gemm: leading dimension too small"), Q38_ERR_ARG;
+  return gemm_fp8(x, tokens, k, w, w_sf, features, epilogue, y, ldy, residual, ldr, splits, workspace, workspace_bytes,
+                  nullptr, static_cast<cudaStream_t>(stream), "q38_fp8_gemm");
+}
+
+extern "C" int q38_fp8_gemm_allreduce(const void* x, int64_t tokens, int64_t k, const void* w, const void* w_sf,
+                                      int64_t features, int splits, void* comm, q38_stream_t stream) {
+  using namespace q38host;
+  int st = check_gemm_args(x, tokens, k, w, w_sf, features, splits, "q38_fp8_gemm_allreduce");
+  if (st != Q38_OK) return st;
+  const Comm* c = static_cast<const Comm*>(comm);
+  if (!c || !c->connected) return set_error("q38_fp8_gemm_allreduce: communicator not connected"), Q38_ERR_ARG;
+  if (features != c->hidden || tokens > c->tmax)
+    return set_error("q38_fp8_gemm_allreduce: output [%lld, %lld] does not fit the communicator's [%lld, %lld]",
+                     (long long)tokens, (long long)features, (long long)c->tmax, (long long)c->hidden),
+           Q38_ERR_ARG;
+  const ArArgs ar = ar_args(*c);
+  void* y = c->base + c->off_x;
+  return gemm_fp8(x, tokens, k, w, w_sf, features, EPI_ALLREDUCE, y, c->hidden, nullptr, 0, splits, nullptr, 0, &ar,
+                  static_cast<cudaStream_t>(stream), "q38_fp8_gemm_allreduce");
 }
 
 extern "C" int q38_lm_head_groupmax(const void* x, int64_t rows, int64_t k, const void* w, int64_t vocab, int group,

@@ -78,7 +78,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // ----------------------------------------------------------------------------------------------
-// TMA and bulk copies (never with cluster multicast)
+// TMA and bulk copies (each to the issuing CTA only)
 // ----------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
@@ -95,7 +95,7 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
 }
 // TMA load issued by either CTA of an MMA pair (cta_group::2): the data lands in the issuing CTA's
 // shared memory and its bytes are counted on the even (leader) CTA's mbarrier at the same offset
-// (the peer bit of the barrier address is cleared). No multicast.
+// (the peer bit of the barrier address is cleared). Each copy lands in its issuing CTA alone.
 __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(

@@ -6,6 +6,8 @@ dtypes are checked here so a wrong call fails on the host with a message, not on
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib, codec
@@ -95,6 +97,55 @@ def fp8_gemm(x_e5m2: torch.Tensor, lin: DeviceLinear, y: torch.Tensor, residual:
               y.data_ptr(), y.stride(0), residual.data_ptr() if residual is not None else None, ldr, splits, ws_ptr,
               ws_bytes, _stream())
     return y
+
+
+class _DeviceArray:
+    """A raw device allocation seen by torch through __cuda_array_interface__ (no copy)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class Communicator:
+    """One rank's side of the fused all-reduce: its exchange region, mapped into every peer over NVLink.
+
+    Every rank of `group` constructs it collectively (the IPC handles travel by an all-gather of the
+    group). `x` is this rank's residual stream, bf16 [max_tokens, hidden], living in the region: the
+    fused projections write their result into every rank's `x`."""
+
+    def __init__(self, rank: int, world: int, max_tokens: int, hidden: int, device, group=None):
+        lib = _lib.load()
+        handle = ctypes.c_void_p()
+        _lib.call("q38_comm_init", rank, world, max_tokens, hidden, ctypes.byref(handle))
+        self.handle = handle
+        self.rank, self.world, self.max_tokens, self.hidden = rank, world, max_tokens, hidden
+        nb = lib.q38_comm_ipc_handle_bytes()
+        buf = (ctypes.c_uint8 * nb)()
+        _lib.call("q38_comm_ipc_handle", handle, buf, nb)
+        mine = torch.tensor(bytearray(buf), dtype=torch.uint8, device=device)
+        every = torch.empty(world * nb, dtype=torch.uint8, device=device)
+        torch.distributed.all_gather_into_tensor(every, mine, group=group)
+        every = every.cpu().contiguous()
+        _lib.call("q38_comm_connect", handle, every.data_ptr())
+        ptr = lib.q38_comm_residual(handle)
+        self.x = torch.as_tensor(_DeviceArray(ptr, (max_tokens, hidden), "<i2"), device=device).view(BF16)
+
+    def close(self) -> None:
+        if self.handle is not None:
+            self.x = None
+            _lib.call("q38_comm_destroy", self.handle)
+            self.handle = None
+
+
+def fp8_gemm_allreduce(x_e5m2: torch.Tensor, lin: DeviceLinear, comm: Communicator, splits: int = 1) -> None:
+    """comm.x[:tokens] += all_reduce(bf16(e5m2(x) @ W^T)) across the communicator's ranks, fused."""
+    _cuda(x_e5m2)
+    _need(x_e5m2.dtype == U8 and x_e5m2.dim() == 2 and x_e5m2.is_contiguous(), "x must be contiguous uint8 e5m2")
+    tokens, k = x_e5m2.shape
+    _need(k == lin.in_features and lin.out_features == comm.hidden, "shape mismatch")
+    _lib.call("q38_fp8_gemm_allreduce", x_e5m2.data_ptr(), tokens, k, lin.q.data_ptr(), lin.sf.data_ptr(),
+              lin.out_features, splits, comm.handle, _stream())
 
 
 def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, y_bf16: torch.Tensor | None = None,

@@ -17,8 +17,11 @@ exactly as `Qwen38Step.forward` routes them (model.py:983-995):
 hidden [B, 1, H] -> group-of-32 maxima [B, V / 32] float32 on the host.
 
 One process drives one GPU. With tp_degree > 1 every rank makes the same calls with the same inputs
-(torch.distributed, NCCL), holds its slice of heads, and the row-parallel outputs are summed across
-ranks after o_proj / out_proj / down_proj (model.py:259, :374, :639).
+(torch.distributed), holds its slice of heads, and the row-parallel outputs are summed across ranks
+after o_proj / out_proj / down_proj (model.py:259, :374, :639): by default inside those projections'
+GEMM kernels over NVLink peer memory (ops.Communicator, q38_fp8_gemm_allreduce), the residual stream
+living in the communicator's shared region; with fused_allreduce=False by a GEMM then an NCCL
+all-reduce (the baseline).
 
 The decode step is captured once into a CUDA graph and replayed: ~9 kernels per layer, all on one
 stream, with every buffer allocated up front. Nothing here falls back to PyTorch math: the layer
@@ -80,7 +83,8 @@ class B200Step:
 
     def __init__(self, cfg: TextConfig, layer_weights, max_seq_len: int, batch_size: int, tp_degree: int = 1,
                  rank: int = 0, device: torch.device | str | None = None, saved_states: bool = False,
-                 use_graph: bool = True, process_group=None, verify_tokens: int = 0):
+                 use_graph: bool = True, process_group=None, verify_tokens: int = 0, fused_allreduce: bool = True,
+                 max_chunk: int = 512):
         """`layer_weights(i)` returns layer i's unsharded weights (weights.synthetic_layer names), or
         `layer_weights` is a dict holding them all."""
         cfg.validate_tp(tp_degree)
@@ -92,8 +96,12 @@ class B200Step:
         self.saved = saved_states
         self.verify_tokens = verify_tokens
         get = layer_weights if callable(layer_weights) else (lambda i: layer_weights)
+        self.comm = None
         with torch.cuda.device(self.device):
             self.layers = [self._prepare(i, W.shard_layer(cfg, get(i), i, rank, tp_degree)) for i in range(cfg.num_hidden_layers)]
+            if tp_degree > 1 and fused_allreduce:
+                rows = max(batch_size, batch_size * max(verify_tokens, 1), max_chunk)
+                self.comm = ops.Communicator(rank, tp_degree, rows, cfg.hidden_size, self.device, process_group)
             self._alloc_activations()
         self._graph = None
         self._graph_key = None
@@ -157,7 +165,8 @@ class B200Step:
         heads = cfg.num_attention_heads // tp
         inter = cfg.intermediate_size // tp
         z = lambda *s, dt=BF16: torch.zeros(*s, dtype=dt, device=dev)  # noqa: E731
-        a.x = z(rows, H)
+        # With the fused all-reduce the residual stream is the communicator's (peers write into it).
+        a.x = self.comm.x[:rows] if self.comm is not None else z(rows, H)
         a.x_in = z(rows, H)
         a.hb = z(rows, H)
         a.hq = z(rows, H, dt=torch.uint8)
@@ -169,7 +178,7 @@ class B200Step:
         a.mix_attn = z(rows, heads * cfg.head_dim, dt=torch.uint8)
         a.gu = z(rows, 2 * inter)
         a.mlp_q = z(rows, inter, dt=torch.uint8)
-        a.partial = z(rows, H) if tp > 1 else None
+        a.partial = z(rows, H) if tp > 1 and self.comm is None else None
         a.cos = z(rows, cfg.rotary_dim)
         a.sin = z(rows, cfg.rotary_dim)
         a.splits = {}
@@ -178,6 +187,8 @@ class B200Step:
             for lin in (l.mixer.out if l.kind == LINEAR else l.mixer.o, l.down, l.gate_up,
                         l.mixer.qkvz if l.kind == LINEAR else l.mixer.qkv):
                 sp = ops.choose_splits(rows, lin.out_features, lin.in_features)
+                if self.comm is not None and lin is not l.gate_up and lin is not (l.mixer.qkvz if l.kind == LINEAR else l.mixer.qkv):
+                    sp = min(sp, 8)  # the fused all-reduce reduces K splits within one portable cluster
                 a.splits[id(lin)] = sp
                 need = max(need, ops.gemm_workspace_bytes(rows, lin.out_features, sp))
         hv2 = 2 * cfg.linear_num_value_heads // tp
@@ -193,6 +204,9 @@ class B200Step:
         """x += all_reduce(bf16(x_q @ W^T)) (the reference's `x + all_reduce(proj(...))`)."""
         if self.tp == 1:
             self._gemm(a, x_q, lin, a.x, residual=a.x)
+            return
+        if self.comm is not None:
+            ops.fp8_gemm_allreduce(x_q, lin, self.comm, splits=a.splits.get(id(lin), 1))
             return
         self._gemm(a, x_q, lin, a.partial)
         torch.distributed.all_reduce(a.partial, group=self.group)
@@ -339,7 +353,7 @@ class B200Step:
 
     def decode_device(self):
         """One decode step over the inputs already in the device buffers (x_in, cos, sin, position, active)."""
-        if self.use_graph and self.tp == 1:
+        if self.use_graph and (self.tp == 1 or self.comm is not None):
             if self._graph is None:
                 self._capture()
             self._graph.replay()
@@ -362,6 +376,14 @@ class B200Step:
         self._graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self._graph):
             self._decode_layers()
+
+    def close(self) -> None:
+        """Releases the CUDA graph and the communicator's peer mappings (call before the process group goes)."""
+        self._graph = None
+        if self.comm is not None:
+            torch.cuda.synchronize(self.device)
+            self.comm.close()
+            self.comm = None
 
     # ------------------------------------------------------------------ the reference's call
     def __call__(self, inputs_embeds: torch.Tensor, **inputs: torch.Tensor) -> torch.Tensor:
