@@ -244,6 +244,7 @@ def run_ours(args, world, rank, local):
         line["cpu_baseline"] = cpu_baseline(cfg, pkg, B, samples=1)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    step.close()  # the decode graph and the communicator's peer mappings go before the process group
     del step, head
     if world > 1:
         torch.distributed.barrier()
@@ -421,9 +422,63 @@ def run_micro(args):
                                    "frac": achieved / peak}}), flush=True)
 
 
+def run_micro_allreduce(args, world, rank, local):
+    """The row-parallel projection at TP = world, alone: the plain GEMM, the fused GEMM + all-reduce, and the
+    GEMM followed by an NCCL all-reduce (the baseline), each timed as a CUDA graph of --steps launches,
+    max over ranks. Shapes: down_proj (17408 / world -> 5120) and o_proj (6144 / world -> 5120)."""
+    pkg = importlib.import_module(PACKAGE)
+    ops = importlib.import_module(f"{PACKAGE}.ops")
+    device = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(device)
+    torch.distributed.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=120))
+    B, H = args.batch, 5120
+    comm = ops.Communicator(rank, world, max(B, 512), H, device)
+    out = {}
+    for name, k in (("down_proj", 17408 // world), ("o_proj", 6144 // world)):
+        g = torch.Generator().manual_seed(rank)
+        lin = ops.DeviceLinear(pkg.weights.FP8Weight.from_float(torch.randn(H, k, generator=g) * 0.02), device)
+        xq = pkg.codec.to_e5m2_bytes(torch.randn(B, k, generator=g).to(torch.bfloat16)).to(device)
+        splits = min(ops.choose_splits(B, H, k), 8)
+        ws = torch.zeros(max(256, ops.gemm_workspace_bytes(B, H, splits)), dtype=torch.uint8, device=device)
+        part = torch.zeros(B, H, dtype=torch.bfloat16, device=device)
+        variants = {
+            "gemm": lambda: ops.fp8_gemm(xq, lin, part, splits=splits, workspace=ws),
+            "fused": lambda: ops.fp8_gemm_allreduce(xq, lin, comm, splits=splits),
+            "gemm+nccl": lambda: (ops.fp8_gemm(xq, lin, part, splits=splits, workspace=ws),
+                                  torch.distributed.all_reduce(part)),
+        }
+        for vname, fn in variants.items():
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            torch.distributed.barrier()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(args.steps):
+                    fn()
+            graph.replay()
+            torch.cuda.synchronize()
+            torch.distributed.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            graph.replay()
+            b.record()
+            torch.cuda.synchronize()
+            out[f"{name}.{vname}_us"] = round(max_over_ranks(a.elapsed_time(b), world, device) * 1e3 / args.steps, 2)
+            del graph
+            torch.distributed.barrier()
+        out[f"{name}.splits"] = splits
+    out["device_status"] = ops.device_status()
+    if rank == 0:
+        print(json.dumps({"micro": "gemm_allreduce", "tp": world, "batch": B, **out}), flush=True)
+    comm.close()
+    torch.distributed.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--micro", choices=["gdn", "gemm"], help="time one kernel alone (profiling) instead of the step")
+    ap.add_argument("--micro", choices=["gdn", "gemm", "gemm_ar"],
+                    help="time one kernel alone (profiling) instead of the step; gemm_ar: the fused all-reduce under torchrun")
     ap.add_argument("--copies", type=int, default=4, help="--micro: distinct weight/state copies cycled (defeat L2)")
     ap.add_argument("--tp", type=int, default=1, help="--micro gemm: K = 17408 / tp")
     ap.add_argument("--shape", help="--micro gemm: 'features,k' instead of the down_proj shape")
@@ -437,6 +492,9 @@ def main():
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     world, rank, local = dist_env()
+    if args.micro == "gemm_ar":
+        run_micro_allreduce(args, world, rank, local)
+        return
     if args.micro:
         run_micro(args)
         return

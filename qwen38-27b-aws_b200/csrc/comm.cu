@@ -29,21 +29,19 @@ extern "C" int q38_comm_init(int rank, int world, int64_t max_tokens, int64_t hi
   c->world = world;
   c->tmax = max_tokens;
   c->hidden = hidden;
-  c->slots = static_cast<int>(((max_tokens + 31) / 32) * (hidden / 128));
   cudaError_t e = cudaGetDevice(&c->device);
   if (e != cudaSuccess) {
     delete c;
     return cuda_status(e, "cudaGetDevice");
   }
+  const size_t words = static_cast<size_t>(max_tokens) * (hidden / 2);  // u64 words of one [tokens][hidden] bf16 slab
   size_t off = 0;
   c->off_x = off;
   off = align256(off + 2 * static_cast<size_t>(max_tokens) * hidden);
-  c->off_recv = off;
-  off = align256(off + 2 * 2 * static_cast<size_t>(world) * max_tokens * hidden);
-  c->off_flags = off;
-  off = align256(off + sizeof(uint32_t) * 2 * world * c->slots);
-  c->off_gflags = off;
-  off = align256(off + sizeof(uint32_t) * 2 * c->slots);
+  c->off_part = off;
+  off = align256(off + 8 * 2 * static_cast<size_t>(world) * words);
+  c->off_result = off;
+  off = align256(off + 8 * 2 * words);
   c->off_epoch = off;
   c->off_done = off + sizeof(uint32_t);
   c->bytes = align256(off + 2 * sizeof(uint32_t));
@@ -53,7 +51,7 @@ extern "C" int q38_comm_init(int rank, int world, int64_t max_tokens, int64_t hi
     return cuda_status(e, "cudaMalloc(comm region)");
   }
   e = cudaMemset(c->base, 0, c->bytes);
-  const uint32_t one = 1;  // epochs start at 1, flags at 0
+  const uint32_t one = 1;  // epochs start at 1: the zeroed words carry epoch 0
   if (e == cudaSuccess) e = cudaMemcpy(c->base + c->off_epoch, &one, sizeof(one), cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     cudaFree(c->base);

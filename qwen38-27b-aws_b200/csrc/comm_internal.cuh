@@ -2,15 +2,17 @@
 // communicator's C ABI (comm.cu).
 //
 // Each rank allocates one region with cudaMalloc and maps every peer's region through CUDA IPC (over
-// NVLink peer access), so a kernel can store straight into a peer's HBM. Layout (same offsets on every
-// rank):
-//   x       bf16 [max_tokens][hidden]      the residual stream, replicated on every rank
-//   recv    bf16 [2][world][max_tokens][hidden]   partial tiles pushed by each source rank, by epoch parity
-//   flags   u32  [2][world][slots]          "source's partial of this slot has arrived" (= epoch)
-//   gflags  u32  [2][slots]                 "the owner's reduced tile of this slot has arrived" (= epoch)
-//   epoch   u32                             the call counter, advanced by the last CTA of each call
-//   done    u32                             CTAs finished in the current call
-// A slot is one 32-token x 128-feature block of the output: slot = (token / 32) * feature_tiles + tile.
+// NVLink peer access), so a kernel can store straight into a peer's HBM. Everything that crosses
+// NVLink travels as 64-bit words {two bf16 values, the call's epoch}: an aligned 64-bit store arrives
+// whole, so a receiver polling its own memory sees data and "ready" together, with no fence and no
+// separate flag (a system-scope fence costs ~10 us on B200; this is the low-latency form of NCCL's LL
+// protocol). Layout (same offsets on every rank), by epoch parity so a rank one call ahead never
+// overwrites words still being read:
+//   x       bf16 [max_tokens][hidden]                 the residual stream, replicated on every rank
+//   part    u64  [2][world][max_tokens][hidden / 2]   partials pushed to this rank (the owner) by each source
+//   result  u64  [2][max_tokens][hidden / 2]          reduced rows pushed to this rank by their owners
+//   epoch   u32                                       the call counter, advanced by the last CTA of a call
+//   done    u32                                       CTAs finished in the current call
 #pragma once
 
 #include <stdint.h>
@@ -24,12 +26,10 @@ constexpr int kMaxRanks = 8;
 struct ArArgs {
   int rank, world;
   int ftiles;  // 128-feature tiles of hidden
-  int slots;   // per parity and source
   int64_t tmax, hidden;
   __nv_bfloat16* x[kMaxRanks];
-  __nv_bfloat16* recv[kMaxRanks];
-  uint32_t* flags[kMaxRanks];
-  uint32_t* gflags[kMaxRanks];
+  unsigned long long* part[kMaxRanks];
+  unsigned long long* result[kMaxRanks];
   uint32_t* epoch;  // this rank's
   uint32_t* done;   // this rank's
 };
@@ -41,8 +41,7 @@ namespace q38host {
 struct Comm {
   int rank = 0, world = 0, device = 0;
   int64_t tmax = 0, hidden = 0;
-  int slots = 0;
-  size_t off_x = 0, off_recv = 0, off_flags = 0, off_gflags = 0, off_epoch = 0, off_done = 0, bytes = 0;
+  size_t off_x = 0, off_part = 0, off_result = 0, off_epoch = 0, off_done = 0, bytes = 0;
   uint8_t* base = nullptr;                     // this rank's region
   uint8_t* peer[q38::kMaxRanks] = {nullptr};  // every rank's region as mapped here (peer[rank] == base)
   bool connected = false;
@@ -54,14 +53,12 @@ inline q38::ArArgs ar_args(const Comm& c) {
   a.rank = c.rank;
   a.world = c.world;
   a.ftiles = static_cast<int>((c.hidden + 127) / 128);
-  a.slots = c.slots;
   a.tmax = c.tmax;
   a.hidden = c.hidden;
   for (int r = 0; r < c.world; ++r) {
     a.x[r] = reinterpret_cast<__nv_bfloat16*>(c.peer[r] + c.off_x);
-    a.recv[r] = reinterpret_cast<__nv_bfloat16*>(c.peer[r] + c.off_recv);
-    a.flags[r] = reinterpret_cast<uint32_t*>(c.peer[r] + c.off_flags);
-    a.gflags[r] = reinterpret_cast<uint32_t*>(c.peer[r] + c.off_gflags);
+    a.part[r] = reinterpret_cast<unsigned long long*>(c.peer[r] + c.off_part);
+    a.result[r] = reinterpret_cast<unsigned long long*>(c.peer[r] + c.off_result);
   }
   a.epoch = reinterpret_cast<uint32_t*>(c.base + c.off_epoch);
   a.done = reinterpret_cast<uint32_t*>(c.base + c.off_done);

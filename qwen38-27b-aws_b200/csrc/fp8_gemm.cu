@@ -94,28 +94,37 @@ __device__ __forceinline__ bool epi_bar_or(bool pred) {
   return r != 0;
 }
 
-// Peer-memory exchange of the fused all-reduce. Flags carry the call's epoch; a store's data is made
-// visible system-wide (fence.sc.sys by every storing thread, then the CTA barrier) before one thread
-// releases the flag, and every reader acquires the flag itself before it reads.
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// Peer-memory exchange of the fused all-reduce: 64-bit words {two bf16, epoch}, stored whole over
+// NVLink and polled by the receiver in its own memory (an aligned 64-bit access is single-copy
+// atomic), so nothing needs a fence or a separate flag.
+__device__ __forceinline__ unsigned long long word(uint32_t bits, uint32_t epoch) {
+  return (static_cast<unsigned long long>(epoch) << 32) | bits;
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+// Two words (four bf16) in one 16-byte store; each 8-byte element is a single-copy atomic access.
+__device__ __forceinline__ void st_words2(unsigned long long* p, uint2 bits, uint32_t epoch) {
+  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(word(bits.x, epoch)), "l"(word(bits.y, epoch))
+               : "memory");
 }
-// Waits (bounded) until *flag >= epoch; false on timeout (recorded in the device error word).
-__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch) {
-  if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
-  const unsigned long long t0 = global_ns();
-  while (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) < 0) {
-    if (global_ns() - t0 > kWaitLimitNs) {
-      record_error(Q38_ERR_TIMEOUT);
-      return false;
-    }
-    __nanosleep(64);
+__device__ __forceinline__ void ld_words2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
+  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+// The two words (four bf16) at p once both carry `epoch`; false if that takes longer than the wait limit
+// (recorded in the device error word).
+__device__ __forceinline__ bool poll_words2(const unsigned long long* p, uint32_t epoch, uint2& out) {
+  unsigned long long a, b;
+  ld_words2(p, a, b);
+  if (static_cast<uint32_t>(a >> 32) != epoch || static_cast<uint32_t>(b >> 32) != epoch) {
+    const unsigned long long t0 = global_ns();
+    do {
+      if (global_ns() - t0 > kWaitLimitNs) {
+        record_error(Q38_ERR_TIMEOUT);
+        return false;
+      }
+      __nanosleep(32);
+      ld_words2(p, a, b);
+    } while (static_cast<uint32_t>(a >> 32) != epoch || static_cast<uint32_t>(b >> 32) != epoch);
   }
+  out = make_uint2(static_cast<uint32_t>(a), static_cast<uint32_t>(b));
   return true;
 }
 
@@ -500,76 +509,73 @@ __global__ void __launch_bounds__(192, 1)
     // rank order (fp32, one bf16 rounding), adds the residual and writes the result into every rank's
     // residual stream; the other ranks push their partial to the owner and wait for the result.
     if (warp >= 2 && a.epilogue == EPI_ALLREDUCE) {
-      // Every branch below is uniform across the 128 epilogue threads: `failed` only changes through
-      // epi_bar_or, which hands all of them the same value.
-      bool failed = epi_bar_or(flags[0] != 0);  // also: the staged partial is complete
+      // Each 8-byte piece (four bf16) of this CTA's token slice is handled by one thread end to end, with
+      // consecutive lanes on consecutive pieces so a warp's 16-byte word stores cover 512 contiguous
+      // bytes: a rank that does not own the tile pushes its partial to the owner as words, then waits for
+      // the owner's result words and writes them into its residual stream; the owner waits for every
+      // rank's words, sums the partials in rank order (fp32, one bf16 rounding), adds the residual and
+      // pushes the result to every other rank.
+      const bool failed = epi_bar_or(flags[0] != 0);  // also: the staged partial is complete
       const ArArgs& r = a.ar;
       const int te = threadIdx.x - 64;
       const uint32_t ep = *reinterpret_cast<volatile uint32_t*>(r.epoch);
       const int par = static_cast<int>(ep & 1u);
       const int owner = static_cast<int>(static_cast<int64_t>(mt) * r.world / r.ftiles);
       const __nv_bfloat16* sbase = reinterpret_cast<const __nv_bfloat16*>(stage);
-      for (int b = b0; b < b1 && live && !failed; ++b) {
-        const int t0 = n0 + b * TOK_BLOCK;
-        if (t0 >= a.T) break;
-        const int slot = (t0 / TOK_BLOCK) * r.ftiles + mt;
-        const __nv_bfloat16* sblk = sbase + b * TOK_BLOCK * BM;
+      const int tb0 = n0 + b0 * TOK_BLOCK;            // first token of the slice
+      const int tb1 = min(a.T, n0 + b1 * TOK_BLOCK);  // one past the last
+      constexpr int PPR = BM / 4;                     // 4-value pieces per row of the tile
+      const int pieces = tb1 > tb0 ? (tb1 - tb0) * PPR : 0;
+      const int64_t hw = r.hidden / 2;                // words per row
+      bool bad = false;
+      if (live && !failed) {
         if (owner != r.rank) {
-          __nv_bfloat16* dst = r.recv[owner] + (static_cast<int64_t>(par) * r.world + r.rank) * r.tmax * r.hidden;
-          for (int c = te; c < TOK_BLOCK * (BM / 8); c += 128) {
-            const int row = c / (BM / 8), cc = c % (BM / 8);
-            const int t = t0 + row, f = m0 + cc * 8;
-            if (t < a.T && f < a.F)
-              *reinterpret_cast<uint4*>(dst + static_cast<int64_t>(t) * r.hidden + f) =
-                  *reinterpret_cast<const uint4*>(sblk + row * BM + cc * 8);
+          unsigned long long* dst = r.part[owner] + (static_cast<int64_t>(par) * r.world + r.rank) * r.tmax * hw;
+          for (int q = te; q < pieces; q += 128) {
+            const int t = tb0 + q / PPR, f = m0 + (q % PPR) * 4;
+            if (f < a.F)
+              st_words2(dst + static_cast<int64_t>(t) * hw + f / 2,
+                        *reinterpret_cast<const uint2*>(sbase + (t - n0) * BM + (f - m0)), ep);
           }
-          __threadfence_system();
-          epi_bar();
-          if (te == 0) st_release_sys(r.flags[owner] + (par * r.world + r.rank) * r.slots + slot, ep);
+          const unsigned long long* res = r.result[r.rank] + static_cast<int64_t>(par) * r.tmax * hw;
+          for (int q = te; q < pieces && !bad; q += 128) {
+            const int t = tb0 + q / PPR, f = m0 + (q % PPR) * 4;
+            if (f >= a.F) continue;
+            uint2 u;
+            bad = !poll_words2(res + static_cast<int64_t>(t) * hw + f / 2, ep, u);
+            if (!bad) *reinterpret_cast<uint2*>(r.x[r.rank] + static_cast<int64_t>(t) * r.hidden + f) = u;
+          }
         } else {
-          bool bad = false;
-          for (int c = te; c < TOK_BLOCK * (BM / 8) && !bad; c += 128) {
-            const int row = c / (BM / 8), cc = c % (BM / 8);
-            const int t = t0 + row, f = m0 + cc * 8;
-            if (t >= a.T || f >= a.F) continue;
-            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          for (int q = te; q < pieces && !bad; q += 128) {
+            const int t = tb0 + q / PPR, f = m0 + (q % PPR) * 4;
+            if (f >= a.F) continue;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
             for (int src = 0; src < r.world && !bad; ++src) {
-              uint4 u;
-              if (src == r.rank) {
-                u = *reinterpret_cast<const uint4*>(sblk + row * BM + cc * 8);
-              } else {
-                bad = !wait_flag(r.flags[r.rank] + (par * r.world + src) * r.slots + slot, ep);
-                u = *reinterpret_cast<const uint4*>(r.recv[r.rank] +
-                                                    ((static_cast<int64_t>(par) * r.world + src) * r.tmax + t) * r.hidden + f);
-              }
+              uint2 u;
+              if (src == r.rank)
+                u = *reinterpret_cast<const uint2*>(sbase + (t - n0) * BM + (f - m0));
+              else
+                bad = !poll_words2(r.part[r.rank] + ((static_cast<int64_t>(par) * r.world + src) * r.tmax + t) * hw + f / 2,
+                                   ep, u);
               const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
-              for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], __bfloat162float(h[j]));
+              for (int j = 0; j < 4; ++j) acc[j] = __fadd_rn(acc[j], __bfloat162float(h[j]));
             }
             if (bad) break;
             const int64_t at = static_cast<int64_t>(t) * r.hidden + f;
-            const uint4 xu = *reinterpret_cast<const uint4*>(r.x[r.rank] + at);
+            const uint2 xu = *reinterpret_cast<const uint2*>(r.x[r.rank] + at);
             const __nv_bfloat16* xh = reinterpret_cast<const __nv_bfloat16*>(&xu);
-            uint4 ou;
+            uint2 ou;
             __nv_bfloat16* oh = reinterpret_cast<__nv_bfloat16*>(&ou);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) oh[j] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(xh[j]), bf16r(acc[j])));
-            for (int q = 0; q < r.world; ++q) *reinterpret_cast<uint4*>(r.x[q] + at) = ou;
+            for (int j = 0; j < 4; ++j) oh[j] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(xh[j]), bf16r(acc[j])));
+            *reinterpret_cast<uint2*>(r.x[r.rank] + at) = ou;
+            for (int dq = 0; dq < r.world; ++dq)
+              if (dq != r.rank) st_words2(r.result[dq] + (static_cast<int64_t>(par) * r.tmax + t) * hw + f / 2, ou, ep);
           }
-          __threadfence_system();
-          failed = epi_bar_or(bad);
-          if (te == 0 && !failed)
-            for (int q = 0; q < r.world; ++q)
-              if (q != r.rank) st_release_sys(r.gflags[q] + par * r.slots + slot, ep);
         }
       }
-      // A rank that does not own the tile waits until the owner's result is in its residual stream.
-      if (owner != r.rank && live && !failed && te == 0)
-        for (int b = b0; b < b1; ++b) {
-          const int t0 = n0 + b * TOK_BLOCK;
-          if (t0 >= a.T) break;
-          if (!wait_flag(r.gflags[r.rank] + par * r.slots + (t0 / TOK_BLOCK) * r.ftiles + mt, ep)) break;
-        }
+      epi_bar_or(bad);
     }
     // No CTA leaves while a peer may still read its shared memory (and a pair frees its tensor memory
     // together).

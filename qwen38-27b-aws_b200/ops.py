@@ -119,6 +119,7 @@ class Communicator:
         handle = ctypes.c_void_p()
         _lib.call("q38_comm_init", rank, world, max_tokens, hidden, ctypes.byref(handle))
         self.handle = handle
+        self.group = group
         self.rank, self.world, self.max_tokens, self.hidden = rank, world, max_tokens, hidden
         nb = lib.q38_comm_ipc_handle_bytes()
         buf = (ctypes.c_uint8 * nb)()
@@ -132,8 +133,11 @@ class Communicator:
         self.x = torch.as_tensor(_DeviceArray(ptr, (max_tokens, hidden), "<i2"), device=device).view(BF16)
 
     def close(self) -> None:
+        """Collective: every rank finishes its kernels, then unmaps its peers and frees its region."""
         if self.handle is not None:
             self.x = None
+            torch.cuda.synchronize()
+            torch.distributed.barrier(group=self.group)
             _lib.call("q38_comm_destroy", self.handle)
             self.handle = None
 
