@@ -384,6 +384,23 @@ def run_micro(args):
                            num_v_heads=hv, head_k=dk, head_v=dv, eps=1e-6)
         per = B * hv * dk * dv * 2 * 2 + B * conv_dim * 3 * 2 * 2 + B * (conv_dim + cfg.linear_value_dim + 2 * hv) * 2 + B * cfg.linear_value_dim
         unit, bound = "GB/s", "hbm"
+    elif args.micro == "attn":
+        # One attention layer's decode at BASELINE config 3: positions U[0, 512), BF16 cache of 512.
+        heads, kvh, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        caches = [(bf(B, kvh, MAX_SEQ, hd), bf(B, kvh, MAX_SEQ, hd)) for _ in range(args.copies)]
+        qkv = bf(B, heads * 2 * hd + 2 * kvh * hd)
+        qn, kn = bf(hd) * 0.1, bf(hd) * 0.1
+        pos = torch.randint(0, MAX_SEQ - 1, (B,), device=dev, dtype=torch.int32, generator=gen)
+        cs, sn = bf(B, cfg.rotary_dim), bf(B, cfg.rotary_dim)
+        act = torch.ones(B, device=dev)
+        out = torch.empty(B, heads * hd, dtype=torch.uint8, device=dev)
+
+        def launch(i):
+            kc, vc = caches[i % len(caches)]
+            ops.attn_decode(qkv, qn, kn, cs, sn, kc, vc, pos, act, out, batch=B, num_q_heads=heads, num_kv_heads=kvh,
+                            head_dim=hd, rot_dim=cfg.rotary_dim, eps=1e-6)
+        per = int(pos.sum().item()) * kvh * hd * 2 * 2 + B * qkv.shape[1] * 2 + B * heads * hd + B * kvh * hd * 2 * 2
+        unit, bound = "GB/s", "hbm"
     else:
         k, n = cfg.intermediate_size // args.tp, cfg.hidden_size
         if args.shape:
@@ -477,7 +494,7 @@ def run_micro_allreduce(args, world, rank, local):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--micro", choices=["gdn", "gemm", "gemm_ar"],
+    ap.add_argument("--micro", choices=["gdn", "gemm", "attn", "gemm_ar"],
                     help="time one kernel alone (profiling) instead of the step; gemm_ar: the fused all-reduce under torchrun")
     ap.add_argument("--copies", type=int, default=4, help="--micro: distinct weight/state copies cycled (defeat L2)")
     ap.add_argument("--tp", type=int, default=1, help="--micro gemm: K = 17408 / tp")
