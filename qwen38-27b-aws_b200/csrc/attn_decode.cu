@@ -13,7 +13,6 @@ namespace {
 
 using namespace q38;
 
-constexpr int kThreads = 256;
 constexpr int kMaxGroups = 8;
 
 struct AttnArgs {
@@ -34,37 +33,41 @@ struct AttnArgs {
   float eps;
 };
 
+constexpr int kWarps = 4;
+constexpr int KT = 32;     // cache positions per tile
+constexpr int MROWS = 16;  // the MMA's M: query heads, padded
+
 template <int HD>
 struct AttnSmem {
-  static constexpr int DPL = HD / 32;               // dims per lane in pass 1
-  static constexpr int CHUNKS = HD / 8;             // 8-dim chunks of a row
-  static constexpr int PGROUPS = kThreads / CHUNKS; // position groups in pass 2
+  static constexpr int ROWP = HD + 8;  // padded row (bf16): ldmatrix rows land in distinct banks
+  static constexpr int NPAD = 8;       // extra weight columns past max_seq
   static size_t bytes(int groups, int64_t max_seq) {
-    return sizeof(float) * (static_cast<size_t>(groups) * HD * 2 + 2 * HD + static_cast<size_t>(groups) * max_seq +
-                            static_cast<size_t>(PGROUPS) * groups * HD + 4 * kMaxGroups);
+    const size_t wcols = static_cast<size_t>((max_seq + KT - 1) / KT * KT + NPAD);
+    return 2 * (static_cast<size_t>(MROWS) * ROWP   // q (bf16)
+                + 2 * static_cast<size_t>(KT) * ROWP  // K / V tile ring
+                + MROWS * wcols)                      // scores, then weights (bf16)
+           + sizeof(float) * (static_cast<size_t>(groups) * HD + 2 * HD + 2 * kMaxGroups);
   }
 };
 
-union Pack8 {
-  uint4 u;
-  __nv_bfloat16 h[8];
-};
-
 template <int HD>
-__global__ void __launch_bounds__(kThreads) attn_decode_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kWarps * 32) attn_decode_kernel(AttnArgs a) {
   using S = AttnSmem<HD>;
-  extern __shared__ __align__(16) float sm[];
+  constexpr int ROWP = S::ROWP;
+  constexpr int KSTEPS = HD / 16;          // MMA k-steps over head_dim
+  constexpr int NT2 = HD / 8 / kWarps;     // pass-2 n-tiles (8 dims) per warp
+  extern __shared__ __align__(16) uint8_t smem_raw[];
   const int G = a.groups;
-  float* qf = sm;                              // [G][HD] normed, roped queries
-  float* gate = qf + G * HD;                   // [G][HD] gate values
-  float* kown = gate + G * HD;                 // [HD]
-  float* vown = kown + HD;                     // [HD]
-  float* sc = vown + HD;                       // [G][max_seq] scores, then weights
-  float* part = sc + G * a.max_seq;            // [PGROUPS][G][HD]
-  float* hs = part + S::PGROUPS * G * HD;      // [kMaxGroups] own weights; [kMaxGroups..] spare
+  const int wcols = static_cast<int>((a.max_seq + KT - 1) / KT * KT) + S::NPAD;
+  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem_raw);       // [16][ROWP]
+  __nv_bfloat16* ring = qs + MROWS * ROWP;                               // [2][KT][ROWP]
+  __nv_bfloat16* wb = ring + 2 * KT * ROWP;                              // [16][wcols]
+  float* qf = reinterpret_cast<float*>(wb + MROWS * wcols);             // [G][HD]
+  float* kown = qf + G * HD;                                             // [HD]
+  float* vown = kown + HD;                                               // [HD]
+  float* hs = vown + HD;                                                 // [2][kMaxGroups]
 
-  const int g = blockIdx.x;
-  const int b = blockIdx.y;
+  const int g = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool on = a.active[b] > 0.5f;
   const int pos = a.position[b];
@@ -73,153 +76,170 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(AttnArgs a) {
   const int64_t where = on ? (pos64 < a.max_seq - 1 ? pos64 : a.max_seq - 1) : a.max_seq - 1;
   const __nv_bfloat16* row = a.qkv + b * a.ld_qkv;
   const int qh0 = g * G;
+  const __nv_bfloat16* kc = a.k_cache + (static_cast<int64_t>(b) * a.num_kv_heads + g) * a.max_seq * HD;
+  const __nv_bfloat16* vc = a.v_cache + (static_cast<int64_t>(b) * a.num_kv_heads + g) * a.max_seq * HD;
+  const int ntiles = (n_read + KT - 1) / KT;
 
-  // Stage the raw query heads, gates, own key and value.
-  for (int i = tid; i < G * HD; i += kThreads) {
+  // Tile i of the stream: K tiles 0 .. ntiles-1, then V tiles. Rows past n_read are zero-filled.
+  auto load_tile = [&](int i) {
+    const bool is_v = i >= ntiles;
+    const int p0 = (is_v ? i - ntiles : i) * KT;
+    const __nv_bfloat16* src = is_v ? vc : kc;
+    __nv_bfloat16* dst = ring + (i & 1) * KT * ROWP;
+    for (int c = tid; c < KT * (HD / 8); c += kWarps * 32) {
+      const int r = c / (HD / 8), cc = c % (HD / 8);
+      const int p = p0 + r;
+      const bool ok = p < n_read;
+      cp_async16(smem_u32(dst + r * ROWP + cc * 8), src + static_cast<int64_t>(ok ? p : 0) * HD + cc * 8, ok ? 16u : 0u);
+    }
+    cp_async_commit();
+  };
+  if (ntiles > 0) load_tile(0);
+
+  // Stage the raw query heads, own key and value; norm + rotary; queries to bf16 MMA rows.
+  for (int i = tid; i < G * HD; i += kWarps * 32) {
     const int h = i / HD, d = i % HD;
-    const __nv_bfloat16* base = row + static_cast<int64_t>(qh0 + h) * 2 * HD;
-    qf[i] = __bfloat162float(base[d]);
-    gate[i] = __bfloat162float(base[HD + d]);
+    qf[i] = __bfloat162float(row[static_cast<int64_t>(qh0 + h) * 2 * HD + d]);
   }
   const __nv_bfloat16* kraw = row + static_cast<int64_t>(a.num_q_heads) * 2 * HD + static_cast<int64_t>(g) * HD;
   const __nv_bfloat16* vraw = kraw + static_cast<int64_t>(a.num_kv_heads) * HD;
-  for (int d = tid; d < HD; d += kThreads) {
+  for (int d = tid; d < HD; d += kWarps * 32) {
     kown[d] = __bfloat162float(kraw[d]);
     vown[d] = __bfloat162float(vraw[d]);
   }
   __syncthreads();
   const __nv_bfloat16* cs = a.cos + b * a.rot;
   const __nv_bfloat16* sn = a.sin + b * a.rot;
-  for (int h = warp; h <= G; h += kThreads / 32) {
+  for (int h = warp; h <= G; h += kWarps) {
     if (h < G) norm_rope_head<HD>(qf + h * HD, a.q_norm_w, cs, sn, a.rot, a.eps, lane);
     else norm_rope_head<HD>(kown, a.k_norm_w, cs, sn, a.rot, a.eps, lane);
   }
   __syncthreads();
-
-  // Pass 1: bf16-rounded scores of every visible cached position, one position per warp step.
-  const __nv_bfloat16* kc = a.k_cache + (static_cast<int64_t>(b) * a.num_kv_heads + g) * a.max_seq * HD;
-  const __nv_bfloat16* vc = a.v_cache + (static_cast<int64_t>(b) * a.num_kv_heads + g) * a.max_seq * HD;
-  {
-    float qreg[kMaxGroups][S::DPL];
-#pragma unroll
-    for (int h = 0; h < kMaxGroups; ++h)
-#pragma unroll
-      for (int e = 0; e < S::DPL; ++e) qreg[h][e] = h < G ? qf[h * HD + lane * S::DPL + e] : 0.f;
-    // Each warp takes 4 consecutive positions per step and loads their K rows before using them, so
-    // each warp keeps 4 rows (2 KB at head_dim 256) in flight.
-    constexpr int PW = 4;
-    for (int p0 = warp * PW; p0 < n_read; p0 += (kThreads / 32) * PW) {
-      float kv[PW][S::DPL];
-#pragma unroll
-      for (int u = 0; u < PW; ++u) {
-        const int p = min(p0 + u, n_read - 1);
-        if constexpr (S::DPL == 8) {
-          Pack8 pk;
-          pk.u = __ldg(reinterpret_cast<const uint4*>(kc + static_cast<int64_t>(p) * HD + lane * 8));
-#pragma unroll
-          for (int e = 0; e < 8; ++e) kv[u][e] = __bfloat162float(pk.h[e]);
-        } else {
-#pragma unroll
-          for (int e = 0; e < S::DPL; ++e) kv[u][e] = __bfloat162float(kc[static_cast<int64_t>(p) * HD + lane * S::DPL + e]);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < PW; ++u) {
-        const int p = p0 + u;
-#pragma unroll
-        for (int h = 0; h < kMaxGroups; ++h) {
-          if (h >= G) break;
-          float d = 0.f;
-#pragma unroll
-          for (int e = 0; e < S::DPL; ++e) d += qreg[h][e] * kv[u][e];
-          d = warp_sum(d);
-          if (lane == 0 && p < n_read) sc[h * a.max_seq + p] = bf16r(d);
-        }
-      }
-    }
-    // Own scores.
-    if (warp < G) {
-      float d = 0.f;
-      for (int e = lane; e < HD; e += 32) d += qf[warp * HD + e] * kown[e];
-      d = warp_sum(d);
-      if (lane == 0) hs[warp] = bf16r(d);
-    }
-  }
-  __syncthreads();
-
-  // Softmax of (scores / sqrt(head_dim)) per head; weights rounded to bf16.
-  const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(HD)));  // head**-0.5 as fp32
-  if (warp < G) {
-    float* s = sc + warp * a.max_seq;
-    const float own = __fmul_rn(hs[warp], scale);
-    float m = own;
-    for (int p = lane; p < n_read; p += 32) m = fmaxf(m, __fmul_rn(s[p], scale));
-    m = warp_max(m);
-    float sum = 0.f;
-    for (int p = lane; p < n_read; p += 32) sum += expf(__fsub_rn(__fmul_rn(s[p], scale), m));
-    sum = warp_sum(sum);
-    const float eown = expf(__fsub_rn(own, m));
-    sum = __fadd_rn(sum, eown);
-    for (int p = lane; p < n_read; p += 32) s[p] = bf16r(__fdiv_rn(expf(__fsub_rn(__fmul_rn(s[p], scale), m)), sum));
-    __syncwarp();
-    if (lane == 0) hs[kMaxGroups + warp] = bf16r(__fdiv_rn(eown, sum));
-  }
-  __syncthreads();
-
-  // Pass 2: sum_p w[h][p] * V[p], thread = (8-dim chunk, position group).
-  {
-    const int chunk = tid % S::CHUNKS;
-    const int pg = tid / S::CHUNKS;
-    float acc[kMaxGroups][8];
-#pragma unroll
-    for (int h = 0; h < kMaxGroups; ++h)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) acc[h][e] = 0.f;
-    // 8 positions per step per thread, loaded before use (128 B in flight per thread).
-    constexpr int PV = 8;
-    for (int p0 = pg; p0 < n_read; p0 += S::PGROUPS * PV) {
-      Pack8 pv[PV];
-#pragma unroll
-      for (int u = 0; u < PV; ++u) {
-        const int p = min(p0 + u * S::PGROUPS, n_read - 1);
-        pv[u].u = __ldg(reinterpret_cast<const uint4*>(vc + static_cast<int64_t>(p) * HD + chunk * 8));
-      }
-#pragma unroll
-      for (int u = 0; u < PV; ++u) {
-        const int p = p0 + u * S::PGROUPS;
-        if (p >= n_read) break;
-#pragma unroll
-        for (int h = 0; h < kMaxGroups; ++h) {
-          if (h >= G) break;
-          const float w = sc[h * a.max_seq + p];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[h][e] += w * __bfloat162float(pv[u].h[e]);
-        }
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < kMaxGroups; ++h) {
-      if (h >= G) break;
-#pragma unroll
-      for (int e = 0; e < 8; ++e) part[(pg * G + h) * HD + chunk * 8 + e] = acc[h][e];
-    }
-  }
-  __syncthreads();
-
-  // Final: bf16(bf16(sum) + bf16(w_own * v_own)), times bf16(sigmoid(gate)), to e5m2.
-  uint8_t* orow = a.out + b * a.ld_out;
-  for (int i = tid; i < G * HD; i += kThreads) {
+  for (int i = tid; i < MROWS * HD; i += kWarps * 32) {
     const int h = i / HD, d = i % HD;
-    float s = 0.f;
-    for (int pg = 0; pg < S::PGROUPS; ++pg) s += part[(pg * G + h) * HD + d];
-    const float o = bf16r(__fadd_rn(bf16r(s), bf16r(__fmul_rn(hs[kMaxGroups + h], vown[d]))));
-    const float gt = bf16r(sigmoidf_(gate[i]));
-    orow[static_cast<int64_t>(qh0 + h) * HD + d] = f32_to_e5m2(bf16r(__fmul_rn(o, gt)));
+    qs[h * ROWP + d] = __float2bfloat16_rn(h < G ? qf[i] : 0.f);
+  }
+  for (int i = tid; i < MROWS * wcols; i += kWarps * 32) wb[i] = __float2bfloat16_rn(0.f);
+  // Own scores (fp32 dot, bf16-rounded like the reference's matmul output).
+  for (int h = warp; h < G; h += kWarps) {
+    float d = 0.f;
+    for (int e = lane; e < HD; e += 32) d += qf[h * HD + e] * kown[e];
+    d = warp_sum(d);
+    if (lane == 0) hs[h] = bf16r(d);
+  }
+  __syncthreads();
+
+  // Query fragments for every k-step, kept in registers for pass 1.
+  uint32_t qa[KSTEPS][4];
+  {
+    const int r = lane & 15, co = (lane >> 4) * 8;
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ++ks)
+      ldsm_x4(smem_u32(qs + r * ROWP + ks * 16 + co), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+  }
+
+  float acc2[NT2][4];
+#pragma unroll
+  for (int n = 0; n < NT2; ++n) acc2[n][0] = acc2[n][1] = acc2[n][2] = acc2[n][3] = 0.f;
+  const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(HD)));  // head**-0.5 as fp32
+
+  for (int i = 0; i < 2 * ntiles; ++i) {
+    if (i + 1 < 2 * ntiles) {
+      load_tile(i + 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // tile i is in shared memory for every thread
+    const __nv_bfloat16* tile = ring + (i & 1) * KT * ROWP;
+    if (i < ntiles) {
+      // Pass 1: S[16 x 8] for this warp's 8 positions of the tile.
+      float s[4] = {0.f, 0.f, 0.f, 0.f};
+      const int n0 = warp * 8;
+      const int r = n0 + (lane & 7), co = (lane >> 3) * 8;  // x4: four k-chunks of 8
+#pragma unroll
+      for (int ks = 0; ks < KSTEPS; ks += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(smem_u32(tile + r * ROWP + ks * 16 + co), b0, b1, b2, b3);
+        mma_bf16_16816(s, qa[ks], b0, b1);
+        mma_bf16_16816(s, qa[ks + 1], b2, b3);
+      }
+      // C fragment: rows lane/4 (+8) = heads, columns 2*(lane%4) + {0,1} = positions.
+      const int h = lane >> 2, p = i * KT + n0 + 2 * (lane & 3);
+      if (h < G) {
+        if (p < n_read) wb[h * wcols + p] = __float2bfloat16_rn(s[0]);
+        if (p + 1 < n_read) wb[h * wcols + p + 1] = __float2bfloat16_rn(s[1]);
+      }
+    } else {
+      if (i == ntiles) {
+        // All scores are in: softmax of (score * head_dim^-0.5) per head over [cache, own];
+        // weights rounded to bf16 in place. (The barrier above ordered the last score writes.)
+        for (int h = warp; h < G; h += kWarps) {
+          __nv_bfloat16* w = wb + h * wcols;
+          const float own = __fmul_rn(hs[h], scale);
+          float m = own;
+          for (int p = lane; p < n_read; p += 32) m = fmaxf(m, __fmul_rn(__bfloat162float(w[p]), scale));
+          m = warp_max(m);
+          float sum = 0.f;
+          for (int p = lane; p < n_read; p += 32) sum += expf(__fsub_rn(__fmul_rn(__bfloat162float(w[p]), scale), m));
+          sum = warp_sum(sum);
+          const float eown = expf(__fsub_rn(own, m));
+          sum = __fadd_rn(sum, eown);
+          for (int p = lane; p < n_read; p += 32)
+            w[p] = __float2bfloat16_rn(__fdiv_rn(expf(__fsub_rn(__fmul_rn(__bfloat162float(w[p]), scale), m)), sum));
+          if (lane == 0) hs[kMaxGroups + h] = bf16r(__fdiv_rn(eown, sum));
+        }
+        __syncthreads();
+      }
+      // Pass 2: O[16 x this warp's dims] += W[16 x 32 positions] * V[32 x dims].
+      const int t = i - ntiles;
+#pragma unroll
+      for (int ks = 0; ks < KT / 16; ++ks) {
+        uint32_t wa[4];
+        ldsm_x4(smem_u32(wb + (lane & 15) * wcols + t * KT + ks * 16 + (lane >> 4) * 8), wa[0], wa[1], wa[2], wa[3]);
+        const int vr = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;  // x4.trans: (k 0-7 | 8-15) x (n 0-7 | 8-15)
+#pragma unroll
+        for (int n = 0; n < NT2; n += 2) {
+          const int d0 = (warp * NT2 + n) * 8 + (lane >> 4) * 8;
+          uint32_t b0, b1, b2, b3;
+          if constexpr (NT2 >= 2) {
+            ldsm_x4_t(smem_u32(tile + vr * ROWP + d0), b0, b1, b2, b3);
+            mma_bf16_16816(acc2[n], wa, b0, b1);
+            mma_bf16_16816(acc2[n + 1], wa, b2, b3);
+          } else {
+            ldsm_x2_t(smem_u32(tile + vr * ROWP + (warp * NT2 + n) * 8), b0, b1);
+            mma_bf16_16816(acc2[n], wa, b0, b1);
+          }
+        }
+      }
+    }
+    __syncthreads();  // every warp is done with tile i before its buffer is refilled
+  }
+  if (ntiles == 0) {
+    // No cached positions: only the own key; its weight is exp(0) / exp(0) = 1.
+    if (tid < G) hs[kMaxGroups + tid] = 1.0f;
+    __syncthreads();
+  }
+
+  // Final: bf16(bf16(W V) + bf16(w_own * v_own)) * bf16(sigmoid(gate)), to e5m2.
+  uint8_t* orow = a.out + b * a.ld_out;
+  const int h = lane >> 2;
+  if (h < G) {
+#pragma unroll
+    for (int n = 0; n < NT2; ++n) {
+      const int d = (warp * NT2 + n) * 8 + 2 * (lane & 3);
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float o = bf16r(__fadd_rn(bf16r(acc2[n][e]), bf16r(__fmul_rn(hs[kMaxGroups + h], vown[d + e]))));
+        const float gv = __bfloat162float(row[static_cast<int64_t>(qh0 + h) * 2 * HD + HD + d + e]);
+        orow[static_cast<int64_t>(qh0 + h) * HD + d + e] = f32_to_e5m2(bf16r(__fmul_rn(o, bf16r(sigmoidf_(gv)))));
+      }
+    }
   }
   // The token's key and value go to the cache at `where` (nothing above read that position).
   __nv_bfloat16* kw = a.k_cache + ((static_cast<int64_t>(b) * a.num_kv_heads + g) * a.max_seq + where) * HD;
   __nv_bfloat16* vw = a.v_cache + ((static_cast<int64_t>(b) * a.num_kv_heads + g) * a.max_seq + where) * HD;
-  for (int d = tid; d < HD; d += kThreads) {
+  for (int d = tid; d < HD; d += kWarps * 32) {
     kw[d] = __float2bfloat16_rn(kown[d]);
     vw[d] = __float2bfloat16_rn(vown[d]);
   }
@@ -237,7 +257,7 @@ int launch_attn(const AttnArgs& a, int64_t batch, cudaStream_t stream) {
     if (e != cudaSuccess) return q38host::cuda_status(e, "cudaFuncSetAttribute(attn_decode)");
   }
   dim3 grid(static_cast<unsigned>(a.num_kv_heads), static_cast<unsigned>(batch));
-  attn_decode_kernel<HD><<<grid, kThreads, smem, stream>>>(a);
+  attn_decode_kernel<HD><<<grid, kWarps * 32, smem, stream>>>(a);
   return q38host::cuda_status(cudaGetLastError(), "attn_decode launch");
 }
 
