@@ -35,6 +35,7 @@ struct AttnArgs {
 
 constexpr int kWarps = 4;
 constexpr int KT = 32;     // cache positions per tile
+constexpr int STAGES = 4;  // tiles in flight
 constexpr int MROWS = 16;  // the MMA's M: query heads, padded
 
 template <int HD>
@@ -44,7 +45,7 @@ struct AttnSmem {
   static size_t bytes(int groups, int64_t max_seq) {
     const size_t wcols = static_cast<size_t>((max_seq + KT - 1) / KT * KT + NPAD);
     return 2 * (static_cast<size_t>(MROWS) * ROWP   // q (bf16)
-                + 2 * static_cast<size_t>(KT) * ROWP  // K / V tile ring
+                + STAGES * static_cast<size_t>(KT) * ROWP  // K / V tile ring
                 + MROWS * wcols)                      // scores, then weights (bf16)
            + sizeof(float) * (static_cast<size_t>(groups) * HD + 2 * HD + 2 * kMaxGroups);
   }
@@ -60,8 +61,8 @@ __global__ void __launch_bounds__(kWarps * 32) attn_decode_kernel(AttnArgs a) {
   const int G = a.groups;
   const int wcols = static_cast<int>((a.max_seq + KT - 1) / KT * KT) + S::NPAD;
   __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem_raw);       // [16][ROWP]
-  __nv_bfloat16* ring = qs + MROWS * ROWP;                               // [2][KT][ROWP]
-  __nv_bfloat16* wb = ring + 2 * KT * ROWP;                              // [16][wcols]
+  __nv_bfloat16* ring = qs + MROWS * ROWP;                               // [STAGES][KT][ROWP]
+  __nv_bfloat16* wb = ring + STAGES * KT * ROWP;                         // [16][wcols]
   float* qf = reinterpret_cast<float*>(wb + MROWS * wcols);             // [G][HD]
   float* kown = qf + G * HD;                                             // [HD]
   float* vown = kown + HD;                                               // [HD]
@@ -85,7 +86,7 @@ __global__ void __launch_bounds__(kWarps * 32) attn_decode_kernel(AttnArgs a) {
     const bool is_v = i >= ntiles;
     const int p0 = (is_v ? i - ntiles : i) * KT;
     const __nv_bfloat16* src = is_v ? vc : kc;
-    __nv_bfloat16* dst = ring + (i & 1) * KT * ROWP;
+    __nv_bfloat16* dst = ring + (i % STAGES) * KT * ROWP;
     for (int c = tid; c < KT * (HD / 8); c += kWarps * 32) {
       const int r = c / (HD / 8), cc = c % (HD / 8);
       const int p = p0 + r;
@@ -94,7 +95,10 @@ __global__ void __launch_bounds__(kWarps * 32) attn_decode_kernel(AttnArgs a) {
     }
     cp_async_commit();
   };
-  if (ntiles > 0) load_tile(0);
+  for (int i = 0; i < STAGES - 1; ++i) {
+    if (i < 2 * ntiles) load_tile(i);
+    else cp_async_commit();  // empty groups keep the wait counts uniform
+  }
 
   // Stage the raw query heads, own key and value; norm + rotary; queries to bf16 MMA rows.
   for (int i = tid; i < G * HD; i += kWarps * 32) {
@@ -144,14 +148,11 @@ __global__ void __launch_bounds__(kWarps * 32) attn_decode_kernel(AttnArgs a) {
   const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(HD)));  // head**-0.5 as fp32
 
   for (int i = 0; i < 2 * ntiles; ++i) {
-    if (i + 1 < 2 * ntiles) {
-      load_tile(i + 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+    if (i + STAGES - 1 < 2 * ntiles) load_tile(i + STAGES - 1);
+    else cp_async_commit();
+    cp_async_wait<STAGES - 1>();
     __syncthreads();  // tile i is in shared memory for every thread
-    const __nv_bfloat16* tile = ring + (i & 1) * KT * ROWP;
+    const __nv_bfloat16* tile = ring + (i % STAGES) * KT * ROWP;
     if (i < ntiles) {
       // Pass 1: S[16 x 8] for this warp's 8 positions of the tile.
       float s[4] = {0.f, 0.f, 0.f, 0.f};
