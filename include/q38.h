@@ -141,12 +141,15 @@ int q38_bf16_linear(const void* x, int64_t ldx, int64_t rows, int64_t k, const v
  *               keep theirs bit for bit)
  *   position    int32 [batch]; active float32 [batch]
  *   out         e5m2 [batch, ld_out], num_v_heads * head_v columns
+ *   workspace   q38_gdn_decode_workspace_bytes(batch, num_k_heads, head_k) bytes, 16-byte aligned
+ *               (the normalised q and k of each row's key heads between the two launches)
  */
+size_t q38_gdn_decode_workspace_bytes(int64_t batch, int num_k_heads, int head_k);
 int q38_gdn_decode(const void* qkvz, int64_t ld_qkvz, const void* ab, int64_t ld_ab, void* conv_state,
                    const void* conv_weight, const void* a_log, const void* dt_bias, const void* norm_weight,
                    void* state, const int32_t* position, const float* active, void* out, int64_t ld_out,
                    int64_t batch, int num_k_heads, int num_v_heads, int head_k, int head_v, int conv_kernel,
-                   float eps, q38_stream_t stream);
+                   float eps, void* workspace, size_t workspace_bytes, q38_stream_t stream);
 
 /*
  * A prefill chunk of one row (slot) through the gated delta rule: the causal conv over

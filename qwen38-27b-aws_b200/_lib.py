@@ -41,10 +41,12 @@ SIGNATURES = {
         c_int,
         [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_size_t, c_void_p],
     ),
+    "q38_gdn_decode_workspace_bytes": (c_size_t, [c_int64, c_int, c_int]),
     "q38_gdn_decode": (
         c_int,
         [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-         c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p],
+         c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p, c_size_t,
+         c_void_p],
     ),
     "q38_attn_decode": (
         c_int,

@@ -191,15 +191,39 @@ def bf16_linear_splits(rows: int, n_out: int, k: int) -> int:
     return max(1, min(kc // 4, 8))
 
 
+def gdn_decode_workspace_bytes(batch: int, num_k_heads: int, head_k: int) -> int:
+    return _lib.load().q38_gdn_decode_workspace_bytes(batch, num_k_heads, head_k)
+
+
+_workspaces: dict = {}
+_retired: list = []
+
+
+def _workspace(device, nbytes: int) -> torch.Tensor:
+    """A per-device scratch buffer for callers that pass none. It only grows, and a replaced buffer is
+    kept alive, so a CUDA graph that captured an older one stays valid."""
+    key = torch.device(device).index
+    buf = _workspaces.get(key)
+    if buf is None or buf.numel() < nbytes:
+        if buf is not None:
+            _retired.append(buf)
+        buf = torch.zeros(max(nbytes, 256), dtype=U8, device=device)
+        _workspaces[key] = buf
+    return buf
+
+
 def gdn_decode(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, state, position, active, out, *,
-               batch: int, num_k_heads: int, num_v_heads: int, head_k: int, head_v: int, eps: float) -> None:
-    _cuda(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, state, position, active, out)
+               batch: int, num_k_heads: int, num_v_heads: int, head_k: int, head_v: int, eps: float,
+               workspace: torch.Tensor | None = None) -> None:
+    _cuda(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, state, position, active, out, workspace)
     _need(position.dtype == torch.int32 and active.dtype == torch.float32, "position int32, active float32")
     _need(state.is_contiguous() and conv_state.is_contiguous(), "state buffers must be contiguous")
+    need = _lib.load().q38_gdn_decode_workspace_bytes(batch, num_k_heads, head_k)
+    ws = workspace if workspace is not None else _workspace(qkvz.device, need)
     _lib.call("q38_gdn_decode", qkvz.data_ptr(), qkvz.stride(0), ab.data_ptr(), ab.stride(0), conv_state.data_ptr(),
               conv_weight.data_ptr(), a_log.data_ptr(), dt_bias.data_ptr(), norm_weight.data_ptr(), state.data_ptr(),
               position.data_ptr(), active.data_ptr(), out.data_ptr(), out.stride(0), batch, num_k_heads, num_v_heads,
-              head_k, head_v, conv_weight.shape[1], eps, _stream())
+              head_k, head_v, conv_weight.shape[1], eps, ws.data_ptr(), ws.numel() * ws.element_size(), _stream())
 
 
 def attn_decode(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, position, active, out, *, batch: int,

@@ -154,6 +154,9 @@ class B200Step:
         self.active = torch.zeros(self.batch, dtype=torch.float32, device=self.device)
         self._prefill_acts = {}
         self._verify_acts = None
+        cfg = self.cfg
+        need = ops.gdn_decode_workspace_bytes(self.batch, cfg.linear_num_key_heads // self.tp, cfg.linear_key_head_dim)
+        self.gdn_workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
 
     def _fill_acts(self, a, rows: int) -> None:
         """Activation buffers for `rows` token rows on `a` (the step itself for decode, a _Acts for a
@@ -238,7 +241,7 @@ class B200Step:
                                a.position, a.active, a.accepted, a.mix_gdn, batch=self.batch, tokens=verify, **heads)
             elif chunk is None:
                 ops.gdn_decode(a.proj, a.ab, m.conv_state, m.conv_w, m.a_log, m.dt_bias, m.norm_w, m.state,
-                               a.position, a.active, a.mix_gdn, batch=self.batch, **heads)
+                               a.position, a.active, a.mix_gdn, batch=self.batch, workspace=self.gdn_workspace, **heads)
             else:
                 slot, start, n_valid = chunk
                 ops.gdn_prefill(a.proj, a.ab, m.conv_state, m.conv_w, m.a_log, m.dt_bias, m.norm_w, m.state, a.mix_gdn,
@@ -348,7 +351,7 @@ class B200Step:
         """Launches of this library's kernels in one decode step (for the bench's gpu_launches)."""
         n = 0
         for l in self.layers:
-            n += (5 if l.kind == LINEAR else 4) + 4
+            n += (6 if l.kind == LINEAR else 4) + 4  # GDN: rmsnorm, qkvz, ab, q/k prep, decode, out_proj
         return n
 
     def decode_device(self):
