@@ -401,7 +401,7 @@ def run_micro(args):
                             head_dim=hd, rot_dim=cfg.rotary_dim, eps=1e-6)
         per = int(pos.sum().item()) * kvh * hd * 2 * 2 + B * qkv.shape[1] * 2 + B * heads * hd + B * kvh * hd * 2 * 2
         unit, bound = "GB/s", "hbm"
-    else:
+    elif args.micro == "gemm":
         k, n = cfg.intermediate_size // args.tp, cfg.hidden_size
         if args.shape:
             n, k = (int(v) for v in args.shape.split(","))
@@ -409,12 +409,26 @@ def run_micro(args):
                 for _ in range(args.copies)]
         x = pkg.codec.to_e5m2_bytes(bf(B, k))
         y = torch.empty(B, n, dtype=torch.bfloat16, device=dev)
-        splits = ops.choose_splits(B, n, k)
+        splits = args.splits or ops.choose_splits(B, n, k)
         ws = torch.zeros(max(256, ops.gemm_workspace_bytes(B, n, splits)), dtype=torch.uint8, device=dev)
 
         def launch(i):
             ops.fp8_gemm(x, lins[i % len(lins)], y, splits=splits, workspace=ws)
         per = n * k + n * (k // 32) + B * k + B * n * 2
+        unit, bound = "GB/s", "hbm"
+    if args.micro == "ab":
+        # in_proj_b/a of one GDN layer: BF16 [B, 5120] x [96, 5120]^T.
+        k, n = cfg.hidden_size, 2 * cfg.linear_num_value_heads
+        lins = [ops.DeviceBF16Linear((torch.randn(n, k, device=dev, generator=gen) * 0.02).to(torch.bfloat16), dev)
+                for _ in range(args.copies)]
+        x = bf(B, k)
+        y = torch.empty(B, n, dtype=torch.bfloat16, device=dev)
+        splits = args.splits or ops.bf16_linear_splits(B, n, k)
+        ws = torch.zeros(max(256, ops.gemm_workspace_bytes(B, n, splits)), dtype=torch.uint8, device=dev)
+
+        def launch(i):
+            ops.bf16_linear(x, lins[i % len(lins)], y, splits=splits, workspace=ws)
+        per = n * k * 2 + B * k * 2 + B * n * 2
         unit, bound = "GB/s", "hbm"
     for i in range(args.warmup):
         launch(i)
@@ -494,11 +508,12 @@ def run_micro_allreduce(args, world, rank, local):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--micro", choices=["gdn", "gemm", "attn", "gemm_ar"],
+    ap.add_argument("--micro", choices=["gdn", "gemm", "attn", "ab", "gemm_ar"],
                     help="time one kernel alone (profiling) instead of the step; gemm_ar: the fused all-reduce under torchrun")
     ap.add_argument("--copies", type=int, default=4, help="--micro: distinct weight/state copies cycled (defeat L2)")
     ap.add_argument("--tp", type=int, default=1, help="--micro gemm: K = 17408 / tp")
     ap.add_argument("--shape", help="--micro gemm: 'features,k' instead of the down_proj shape")
+    ap.add_argument("--splits", type=int, default=0, help="--micro gemm/ab: K splits instead of the default choice")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)

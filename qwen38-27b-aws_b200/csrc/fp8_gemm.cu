@@ -848,7 +848,9 @@ extern "C" int q38_bf16_linear(const void* x, int64_t ldx, int64_t rows, int64_t
     return set_error("q38_bf16_linear: bad sizes (x must be contiguous [rows, k], k %% 8 == 0)"), Q38_ERR_ARG;
   if (!aligned16(x) || !aligned16(w) || splits < 1)
     return set_error("q38_bf16_linear: x and w must be 16-byte aligned, splits >= 1"), Q38_ERR_ARG;
-  const int ntok = token_tile(rows);
+  // A thin output (one 128-row tile, e.g. in_proj_b/a's 96) gets 128-token tiles: twice the CTAs,
+  // each streaming half the activations.
+  const int ntok = n_out <= BM ? 128 : token_tile(rows);
   const int nkc = static_cast<int>(cdiv(k, BK_BYTES / 2));
   const int kc_per = static_cast<int>(cdiv(nkc, std::min(splits, nkc)));
   splits = static_cast<int>(cdiv(nkc, kc_per));
