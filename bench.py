@@ -36,6 +36,7 @@ sys.path.insert(0, str(ROOT))
 PACKAGE = "qwen38-27b-aws_b200"
 METRIC = "total tokens/s (64-layer decode step incl. lm_head maxima)"
 MAX_SEQ = 512
+GDN_TRAFFIC_B256 = 777.4e6  # dram__bytes per gdn_decode_kernel launch, batch 256, one GPU (ncu)
 LAYERS = 64
 
 
@@ -225,14 +226,16 @@ def run_ours(args, world, rank, local):
         },
         "e2e": {"value": tokens / (e2e_ms / 1e3), "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {
-            "kernel": "gdn_decode",
+            "kernel": "gdn_decode (q/k prep + per-value-head kernel, timed together)",
             "bound": "hbm",
             "achieved": achieved,
             "peak": peak,
             "peak_kind": peak_kind,
             "unit": "GB/s",
             "frac": achieved / peak,
-            "traffic": None,
+            # DRAM bytes of one gdn_decode_kernel launch at this shape from an ncu capture
+            # (profiles/gdn_decode_b256.md); not captured for other batch sizes or TP degrees.
+            "traffic": GDN_TRAFFIC_B256 if (B == 256 and world == 1) else None,
             "bytes_per_launch": per_launch,
             "launch_ms": gdn_ms,
         },
@@ -416,6 +419,70 @@ def run_micro(args):
             ops.fp8_gemm(x, lins[i % len(lins)], y, splits=splits, workspace=ws)
         per = n * k + n * (k // 32) + B * k + B * n * 2
         unit, bound = "GB/s", "hbm"
+    if args.micro == "gdn_prefill":
+        # one 512-token prefill chunk through the gated delta rule (48 value heads,
+        # dk = dv = 128), continuing a row (start > 0). Work: the chunked rule's fp32 products.
+        T = 512
+        hk, hv, dk, dv = cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim
+        conv_dim = cfg.linear_conv_dim
+        states = [(bf(1, hv, dk, dv) * 0.1, bf(1, conv_dim, 3)) for _ in range(args.copies)]
+        qkvz, ab = bf(T, conv_dim + cfg.linear_value_dim), bf(T, 2 * hv)
+        conv_w, a_log, dt, nw = bf(conv_dim, 4) * 0.1, bf(hv) * 0.1, bf(hv) * 0.1, bf(dv) * 0.1
+        out = torch.empty(T, cfg.linear_value_dim, dtype=torch.uint8, device=dev)
+        ws = torch.empty(ops.gdn_prefill_workspace_bytes(T, hk, hv, dk, dv), dtype=torch.uint8, device=dev)
+
+        def launch(i):
+            st, cs = states[i % len(states)]
+            ops.gdn_prefill(qkvz, ab, cs, conv_w, a_log, dt, nw, st, out, ws, slot=0, start=512, n_valid=T,
+                            num_k_heads=hk, num_v_heads=hv, head_k=dk, head_v=dv, eps=1e-6)
+        per = hv * dk * dv * 2 * 2 + T * (conv_dim + cfg.linear_value_dim + 2 * hv) * 2 + T * cfg.linear_value_dim
+        # fp32 FLOPs per chunk (64-token sub-chunks): K K^T, Q K^T (2 C^2 dk) per 32-column slice, the
+        # state products (3 C dk DVS), the solve and the attention-to-delta product, per head and slice.
+        C, slices = 64, dv // 32
+        flops = 2 * hv * slices * (T // C) * (2 * C * C * dk + 3 * C * dk * 32 + C * C * 32)
+        unit, bound = "GB/s", "fp32 FMA (SIMT)"
+    if args.micro == "attn_prefill":
+        # BASELINE config 0's prefill attention: a 512-token chunk of a row continuing 512 positions
+        # (cache of 1024), 24 query / 4 KV heads of 256.
+        T, start, mseq = 512, 512, 1024
+        heads, kvh, hd = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        caches = [(bf(1, kvh, mseq, hd), bf(1, kvh, mseq, hd)) for _ in range(args.copies)]
+        qkv = bf(T, heads * 2 * hd + 2 * kvh * hd)
+        qn, kn = bf(hd) * 0.1, bf(hd) * 0.1
+        cs, sn = bf(T, cfg.rotary_dim), bf(T, cfg.rotary_dim)
+        out = torch.empty(T, heads * hd, dtype=torch.uint8, device=dev)
+        ws = torch.empty(ops.attn_prefill_workspace_bytes(T, heads, hd), dtype=torch.uint8, device=dev)
+
+        def launch(i):
+            kc, vc = caches[i % len(caches)]
+            ops.attn_prefill(qkv, qn, kn, cs, sn, kc, vc, out, ws, slot=0, start=start, num_q_heads=heads,
+                             num_kv_heads=kvh, head_dim=hd, rot_dim=cfg.rotary_dim, eps=1e-6)
+        per = (start + T) * kvh * hd * 2 * 2 + T * qkv.shape[1] * 2 + T * heads * hd
+        keys = sum(start + t + 1 for t in range(T))  # visible keys summed over the chunk's tokens
+        flops = 2 * heads * keys * hd * 3  # scores twice (two passes per block) and the weighted values
+        unit, bound = "GB/s", "fp32 FMA (SIMT)"
+    if args.micro == "verify":
+        # One gated-delta layer's verify (K = 4 tokens per row, commit-on-accept) at batch B.
+        K = 4
+        hk, hv, dk, dv = cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim
+        conv_dim = cfg.linear_conv_dim
+        f32 = lambda *s: torch.randn(*s, device=dev, generator=gen) * 0.1  # noqa: E731
+        sets = [(bf(B, hv, dk, dv) * 0.1, bf(B, conv_dim, 3), f32(B, K, hv, dk), f32(B, K, hv, dv), -f32(B, K, hv).abs(),
+                 bf(B, K, conv_dim)) for _ in range(args.copies)]
+        qkvz, ab = bf(B * K, conv_dim + cfg.linear_value_dim), bf(B * K, 2 * hv)
+        conv_w, a_log, dt, nw = bf(conv_dim, 4) * 0.1, bf(hv) * 0.1, bf(hv) * 0.1, bf(dv) * 0.1
+        pos = torch.randint(1, 500, (B,), device=dev, dtype=torch.int32, generator=gen)
+        act = torch.ones(B, device=dev)
+        acc = torch.randint(0, K + 1, (B,), device=dev, dtype=torch.int32, generator=gen)
+        out = torch.empty(B * K, cfg.linear_value_dim, dtype=torch.uint8, device=dev)
+
+        def launch(i):
+            st, cs, pk, pd, pg, pi = sets[i % len(sets)]
+            ops.gdn_verify(qkvz, ab, cs, conv_w, a_log, dt, nw, st, pk, pd, pg, pi, pos, act, acc, out, batch=B,
+                           tokens=K, num_k_heads=hk, num_v_heads=hv, head_k=dk, head_v=dv, eps=1e-6)
+        per = (B * hv * dk * dv * 2 * 2 + B * conv_dim * 3 * 2 * 2 + B * K * hv * (dk + dv + 1) * 4 * 2
+               + B * K * conv_dim * 2 * 2 + B * K * (conv_dim + cfg.linear_value_dim + 2 * hv) * 2)
+        unit, bound = "GB/s", "hbm"
     if args.micro == "ab":
         # in_proj_b/a of one GDN layer: BF16 [B, 5120] x [96, 5120]^T.
         k, n = cfg.hidden_size, 2 * cfg.linear_num_value_heads
@@ -434,21 +501,31 @@ def run_micro(args):
         launch(i)
     torch.cuda.synchronize()
     # The K launches are captured in one CUDA graph and timed as one replay, so the host's launch
-    # cost never shows between kernels; consecutive launches cycle through `copies` buffers.
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
+    # cost never shows between kernels; consecutive launches cycle through `copies` buffers. --eager
+    # launches them one by one instead (for profilers, which then see plain kernel launches).
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.eager:
+        a.record()
         for i in range(args.steps):
             launch(i)
-    graph.replay()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    graph.replay()
-    b.record()
+        b.record()
+    else:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(args.steps):
+                launch(i)
+        graph.replay()
+        torch.cuda.synchronize()
+        a.record()
+        graph.replay()
+        b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / args.steps
     achieved = per / (ms * 1e-3) / 1e9
-    print(json.dumps({"micro": args.micro, "batch": B, "shape": args.shape, "launch_ms": ms, "bytes_per_launch": per,
+    extra = {}
+    if "flops" in locals():
+        extra = {"gflop_per_launch": flops / 1e9, "achieved_tflops": flops / (ms * 1e-3) / 1e12}
+    print(json.dumps({"micro": args.micro, "batch": B, "shape": args.shape, "launch_ms": ms, "bytes_per_launch": per, **extra,
                       "roofline": {"bound": bound, "achieved": achieved, "peak": peak, "peak_kind": peak_kind, "unit": unit,
                                    "frac": achieved / peak}}), flush=True)
 
@@ -508,12 +585,13 @@ def run_micro_allreduce(args, world, rank, local):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--micro", choices=["gdn", "gemm", "attn", "ab", "gemm_ar"],
+    ap.add_argument("--micro", choices=["gdn", "gemm", "attn", "ab", "gdn_prefill", "attn_prefill", "verify", "gemm_ar"],
                     help="time one kernel alone (profiling) instead of the step; gemm_ar: the fused all-reduce under torchrun")
     ap.add_argument("--copies", type=int, default=4, help="--micro: distinct weight/state copies cycled (defeat L2)")
     ap.add_argument("--tp", type=int, default=1, help="--micro gemm: K = 17408 / tp")
     ap.add_argument("--shape", help="--micro gemm: 'features,k' instead of the down_proj shape")
     ap.add_argument("--splits", type=int, default=0, help="--micro gemm/ab: K splits instead of the default choice")
+    ap.add_argument("--eager", action="store_true", help="--micro: launch one by one instead of one CUDA graph")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
