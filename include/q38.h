@@ -210,13 +210,16 @@ int q38_attn_prefill(const void* qkv, int64_t ld_qkv, const void* q_norm_weight,
  *                 conv_dim]: read (the commit), then replaced
  *   accepted      int32 [batch], 0 .. tokens; 0 after a decode or prefill step
  *   out           e5m2 [batch * tokens, ld_out]
+ *   workspace     q38_gdn_verify_workspace_bytes(batch, tokens, num_k_heads, head_k) bytes, 16-byte aligned
  */
+size_t q38_gdn_verify_workspace_bytes(int64_t batch, int tokens, int num_k_heads, int head_k);
 int q38_gdn_verify_commit(const void* qkvz, int64_t ld_qkvz, const void* ab, int64_t ld_ab, void* conv_state,
                           const void* conv_weight, const void* a_log, const void* dt_bias, const void* norm_weight,
                           void* state, void* pending_key, void* pending_delta, void* pending_decay,
                           void* pending_input, const int32_t* position, const float* active, const int32_t* accepted,
                           void* out, int64_t ld_out, int64_t batch, int tokens, int num_k_heads, int num_v_heads,
-                          int head_k, int head_v, int conv_kernel, float eps, q38_stream_t stream);
+                          int head_k, int head_v, int conv_kernel, float eps, void* workspace, size_t workspace_bytes,
+                          q38_stream_t stream);
 
 /*
  * K verify tokens per row of gated full attention with a BF16 KV cache: token t attends to cache

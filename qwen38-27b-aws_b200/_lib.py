@@ -66,11 +66,12 @@ SIGNATURES = {
         [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
          c_int64, c_int64, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_float, c_void_p, c_size_t, c_void_p],
     ),
+    "q38_gdn_verify_workspace_bytes": (c_size_t, [c_int64, c_int, c_int, c_int]),
     "q38_gdn_verify_commit": (
         c_int,
         [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int,
-         c_int, c_int, c_int, c_float, c_void_p],
+         c_int, c_int, c_int, c_float, c_void_p, c_size_t, c_void_p],
     ),
     "q38_attn_verify": (
         c_int,

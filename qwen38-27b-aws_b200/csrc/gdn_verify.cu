@@ -1,8 +1,10 @@
 // Gated delta rule, K verify tokens per row with commit-on-accept: GatedDeltaNetStep.verify
 // (qwen38_inf2/model.py:376-454) and the CPU form of _commit_and_read (model.py:262-271).
 //
-// One CTA per (row, key head), owning its R value heads' state tiles, conv channels and pending
-// slices outright (the decode kernel's partition), R * 128 threads. In one pass:
+// Two launches, the decode kernel's partition: one small CTA per (row, key head) convolves the K
+// tokens' q and k channels (past the accepted tokens' inputs) and L2-normalises them into a workspace;
+// then one CTA of 128 threads per (row, value head) owns that head's state tile, v channels and pending
+// slices outright. Together:
 //   1. commit: S' = bf16(S * e^{sum of the accepted tokens' log decays} * keep
 //                         + sum_s (k_s e^{decays after s}) delta_s^T)   from the pending buffers the
 //      last verify step kept (the closed form of applying those tokens one by one); the conv history
@@ -44,52 +46,145 @@ struct VerifyArgs {
   const int32_t* accepted;
   uint8_t* out;  // [batch * K, ld_out]
   int64_t ld_out;
-  int num_k_heads, num_v_heads, K;
+  int num_k_heads, num_v_heads, head_v, K;
   float eps;
 };
 
-template <int DK, int DV, int R>
+// One channel's conv for a verify step: the history is the KCONV - 1 inputs before the first uncommitted
+// token (window [conv state, pending inputs] from `acc`, times keep; a row with active 0 keeps its conv
+// state), then the K new inputs. Writes SiLU(conv) of each token to xs[t * stride], the new inputs to the
+// pending buffer and, for an active row, the history to the conv state.
+__device__ __forceinline__ void verify_conv_channel(const VerifyArgs& a, int b, int c, int conv_dim, int K, int acc,
+                                                    bool on, float keep, float* xs, int stride) {
+  constexpr int W = KCONV - 1 + KMAX;
+  __nv_bfloat16* cs = a.conv_state + (static_cast<int64_t>(b) * conv_dim + c) * (KCONV - 1);
+  float win[W];
+#pragma unroll
+  for (int j = 0; j < KCONV - 1; ++j) win[j] = __bfloat162float(cs[j]);
+#pragma unroll
+  for (int s = 0; s < KMAX; ++s)
+    win[KCONV - 1 + s] = s < K ? __bfloat162float(a.pending_input[(static_cast<int64_t>(b) * K + s) * conv_dim + c]) : 0.f;
+  float w2[W];
+#pragma unroll
+  for (int j = 0; j < KCONV - 1; ++j) {
+    float h = win[j];
+    if (on) {
+      // win[acc + j] without a dynamic register index
+#pragma unroll
+      for (int s = 1; s <= KMAX; ++s)
+        if (acc == s) h = win[s + j];
+      h = __fmul_rn(h, keep);
+    }
+    w2[j] = h;
+  }
+  float cw[KCONV];
+#pragma unroll
+  for (int j = 0; j < KCONV; ++j) cw[j] = __bfloat162float(a.conv_w[static_cast<int64_t>(c) * KCONV + j]);
+#pragma unroll
+  for (int t = 0; t < KMAX; ++t) {
+    w2[KCONV - 1 + t] = 0.f;
+    if (t < K) {
+      const __nv_bfloat16 xin = a.qkvz[(static_cast<int64_t>(b) * K + t) * a.ld_qkvz + c];
+      w2[KCONV - 1 + t] = __bfloat162float(xin);
+      a.pending_input[(static_cast<int64_t>(b) * K + t) * conv_dim + c] = xin;
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < KMAX; ++t) {
+    if (t >= K) break;
+    float sacc = 0.f;
+#pragma unroll
+    for (int j = 0; j < KCONV; ++j) sacc = __fadd_rn(sacc, bf16r(__fmul_rn(w2[t + j], cw[j])));
+    const float conv = bf16r(sacc);
+    xs[t * stride] = bf16r(__fmul_rn(conv, bf16r(sigmoidf_(conv))));
+  }
+  if (on) {
+#pragma unroll
+    for (int j = 0; j < KCONV - 1; ++j) cs[j] = __float2bfloat16_rn(w2[j]);
+  }
+}
+
+// Kernel 1, one CTA of DK threads per (row, key head): the q and k channels' conv for the K tokens,
+// their L2 norms (q / sqrt(dk)), into the workspace [row][key head][token][q | k][DK] (fp32).
+template <int DK>
+__global__ void __launch_bounds__(DK) gdn_verify_qk_kernel(VerifyArgs a, float* qk) {
+  constexpr int NW = DK / 32;
+  __shared__ float vals[2][KMAX][DK];
+  __shared__ float part[2][KMAX][NW];
+  const int kh = blockIdx.x, b = blockIdx.y, i = threadIdx.x, warp = i >> 5, lane = i & 31;
+  const int K = a.K;
+  const int pos = a.position[b];
+  const bool on = a.active[b] > 0.5f;
+  const float keep = (pos == 0 && on) ? 0.0f : 1.0f;
+  int acc = a.accepted[b];
+  acc = acc < 0 ? 0 : (acc > K ? K : acc);
+  const int key_dim = a.num_k_heads * DK;
+  const int conv_dim = 2 * key_dim + a.num_v_heads * a.head_v;
+  verify_conv_channel(a, b, kh * DK + i, conv_dim, K, acc, on, keep, &vals[0][0][i], DK);
+  verify_conv_channel(a, b, key_dim + kh * DK + i, conv_dim, K, acc, on, keep, &vals[1][0][i], DK);
+  for (int t = 0; t < K; ++t) {
+    const float sq = warp_sum(__fmul_rn(vals[0][t][i], vals[0][t][i]));
+    const float sk = warp_sum(__fmul_rn(vals[1][t][i], vals[1][t][i]));
+    if (lane == 0) {
+      part[0][t][warp] = sq;
+      part[1][t][warp] = sk;
+    }
+  }
+  __syncthreads();
+  const float inv_scale = static_cast<float>(sqrt(static_cast<double>(DK)));  // math.sqrt(k_head) as fp32
+  float* dst = qk + (static_cast<int64_t>(b) * a.num_k_heads + kh) * K * 2 * DK;
+  for (int t = 0; t < K; ++t) {
+    float sq = 0.f, sk = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) {
+      sq = __fadd_rn(sq, part[0][t][w]);
+      sk = __fadd_rn(sk, part[1][t][w]);
+    }
+    dst[(t * 2 + 0) * DK + i] = __fdiv_rn(__fmul_rn(vals[0][t][i], 1.0f / sqrtf(sq + 1e-6f)), inv_scale);
+    dst[(t * 2 + 1) * DK + i] = __fmul_rn(vals[1][t][i], 1.0f / sqrtf(sk + 1e-6f));
+  }
+}
+
+template <int DK, int DV>
 struct VerifySmem {
-  static constexpr int CH = 2 * DK + R * DV;
-  static constexpr size_t STATE = static_cast<size_t>(R) * DK * DV * 2;
-  static constexpr size_t XS = STATE;                                          // [KMAX][CH] conv + SiLU
-  static constexpr size_t QN = XS + sizeof(float) * KMAX * CH;                 // [KMAX][DK]
-  static constexpr size_t KN = QN + sizeof(float) * KMAX * DK;                 // [KMAX][DK]
-  static constexpr size_t WK = KN + sizeof(float) * KMAX * DK;                 // [R][KMAX][DK] weighted pending keys
-  static constexpr size_t DL = WK + sizeof(float) * R * KMAX * DK;             // [R][KMAX][DV] pending deltas
-  static constexpr size_t RED = DL + sizeof(float) * R * KMAX * DV;            // [R][4][2 KMAX][DV]
-  static constexpr size_t OB = RED + sizeof(float) * R * 4 * 2 * KMAX * DV;    // [R][KMAX][DV] outputs
-  static constexpr size_t DOT = OB + sizeof(float) * R * KMAX * DV;            // [2][KMAX][KMAX] k.k, q.k
-  static constexpr size_t GT = DOT + sizeof(float) * 2 * KMAX * KMAX;          // [R][KMAX][2] beta, log decay
-  static constexpr size_t SC = GT + sizeof(float) * R * KMAX * 2;              // [R] commit scale
-  static constexpr size_t BAR = (SC + sizeof(float) * R + 7) & ~size_t(7);     // [R] mbarriers, then [R] flags
-  static constexpr size_t TOTAL = BAR + 8 * R + 4 * R + 16;
+  static constexpr size_t TILE = static_cast<size_t>(DK) * DV * 2;
+  static constexpr size_t FLOATS = static_cast<size_t>(KMAX) * DV        // xv: the K tokens' v (conv + SiLU)
+                                   + 2 * KMAX * DK                       // qn, kn
+                                   + KMAX * DK + KMAX * DV               // weighted pending keys, pending deltas
+                                   + 4 * 2 * KMAX * DV                   // the 4 warps' [k; q]^T S' partials
+                                   + KMAX * DV                           // outputs before the norm
+                                   + 2 * KMAX * KMAX + 2 * KMAX + KMAX + 4;  // dots, gates, commit weights, scale
+  static constexpr size_t TOTAL = TILE + sizeof(float) * FLOATS + 16;
 };
 
-template <int DK, int DV, int R>
-__global__ void __launch_bounds__(R * 128) gdn_verify_kernel(VerifyArgs a) {
-  using S = VerifySmem<DK, DV, R>;
-  constexpr int ROWS_W = DK / 4;  // state rows per warp of a value-head group
+// Kernel 2, one CTA of 128 threads per (row, value head): the commit into its state tile, the head's v
+// channels, the K x K chunk, the pending buffers and the gated norm.
+template <int DK, int DV>
+__global__ void __launch_bounds__(128) gdn_verify_kernel(VerifyArgs a, const float* qk) {
+  using S = VerifySmem<DK, DV>;
+  constexpr int ROWS_W = DK / 4;  // state rows per warp
   constexpr int CPL = DV / 32;    // state columns per lane
   constexpr uint32_t TILE_BYTES = DK * DV * 2;
   extern __shared__ __align__(128) uint8_t smem[];
-  __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(smem);
-  float* xs = reinterpret_cast<float*>(smem + S::XS);
-  float* qn = reinterpret_cast<float*>(smem + S::QN);
-  float* kn = reinterpret_cast<float*>(smem + S::KN);
-  float* wk = reinterpret_cast<float*>(smem + S::WK);
-  float* dl = reinterpret_cast<float*>(smem + S::DL);
-  float* red = reinterpret_cast<float*>(smem + S::RED);
-  float* ob = reinterpret_cast<float*>(smem + S::OB);
-  float* dots = reinterpret_cast<float*>(smem + S::DOT);
-  float* gt = reinterpret_cast<float*>(smem + S::GT);
-  float* scl = reinterpret_cast<float*>(smem + S::SC);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR);
-  volatile int* failed = reinterpret_cast<volatile int*>(bars + R);
+  __nv_bfloat16* tile = reinterpret_cast<__nv_bfloat16*>(smem);
+  float* xv = reinterpret_cast<float*>(smem + S::TILE);  // [KMAX][DV]
+  float* qn = xv + KMAX * DV;                            // [KMAX][DK]
+  float* kn = qn + KMAX * DK;                            // [KMAX][DK]
+  float* wk = kn + KMAX * DK;                            // [KMAX][DK]
+  float* dl = wk + KMAX * DK;                            // [KMAX][DV]
+  float* red = dl + KMAX * DV;                           // [4][2 KMAX][DV]
+  float* ob = red + 4 * 2 * KMAX * DV;                   // [KMAX][DV]
+  float* dots = ob + KMAX * DV;                          // [2][KMAX][KMAX]
+  float* gt = dots + 2 * KMAX * KMAX;                    // [KMAX][2] beta, log decay
+  float* fw = gt + 2 * KMAX;                             // [KMAX] commit weights
+  float* scl = fw + KMAX;                                // commit scale
+  uint64_t* bar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(scl + 4) + 7) & ~uintptr_t(7));
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int kh = blockIdx.x, b = blockIdx.y;
+  const int h = blockIdx.x, b = blockIdx.y;
   const int K = a.K;
+  const int R = a.num_v_heads / a.num_k_heads;
+  const int kh = h / R;
   const int pos = a.position[b];
   const bool on = a.active[b] > 0.5f;
   const float act = a.active[b];
@@ -98,24 +193,13 @@ __global__ void __launch_bounds__(R * 128) gdn_verify_kernel(VerifyArgs a) {
   acc = acc < 0 ? 0 : (acc > K ? K : acc);
   const int key_dim = a.num_k_heads * DK;
   const int conv_dim = 2 * key_dim + a.num_v_heads * DV;
-  const int h0 = kh * R;
 
   if (tid == 0) {
-    for (int j = 0; j < R; ++j) mbar_init(&bars[j], 1);
+    mbar_init(bar, 1);
     fence_mbar_init();
-  }
-  __syncthreads();
-  if (tid == 0) {
-    for (int j = 0; j < R; ++j) {
-      mbar_arrive_expect_tx(&bars[j], TILE_BYTES);
-      bulk_load(st + static_cast<size_t>(j) * DK * DV,
-                a.state + (static_cast<int64_t>(b) * a.num_v_heads + h0 + j) * DK * DV, TILE_BYTES, &bars[j]);
-    }
-  }
-
-  // Commit factors and the pending slices of this CTA's heads (read before this step overwrites them).
-  if (tid < R) {
-    const int h = h0 + tid;
+    mbar_arrive_expect_tx(bar, TILE_BYTES);
+    bulk_load(tile, a.state + (static_cast<int64_t>(b) * a.num_v_heads + h) * DK * DV, TILE_BYTES, bar);
+    // Commit factors: the accepted tokens' log decays, summed in order, and what is left after each.
     float d[KMAX];
     float total = 0.f;
 #pragma unroll
@@ -124,127 +208,72 @@ __global__ void __launch_bounds__(R * 128) gdn_verify_kernel(VerifyArgs a) {
                    : 0.f;
       if (s < K) total = __fadd_rn(total, d[s]);
     }
-    scl[tid] = on ? __fmul_rn(expf(total), keep) : 1.0f;
+    scl[0] = on ? __fmul_rn(expf(total), keep) : 1.0f;
     float rem = total;
 #pragma unroll
     for (int s = 0; s < KMAX; ++s) {
       if (s >= K) break;
       rem = __fsub_rn(rem, d[s]);
-      const float f = __fmul_rn(__fmul_rn(__fmul_rn(expf(rem), s < acc ? 1.f : 0.f), keep), on ? 1.f : 0.f);
-      gt[(tid * KMAX + s) * 2] = f;  // weight of pending token s (reuses the gate slot until the gates below)
+      fw[s] = __fmul_rn(__fmul_rn(__fmul_rn(expf(rem), s < acc ? 1.f : 0.f), keep), on ? 1.f : 0.f);
     }
   }
-  __syncthreads();
-  for (int i = tid; i < R * K * (DK + DV); i += blockDim.x) {
-    const int j = i / (K * (DK + DV)), rest = i % (K * (DK + DV));
-    const int s = rest / (DK + DV), e = rest % (DK + DV);
-    const int64_t base = (static_cast<int64_t>(b) * K + s) * a.num_v_heads + h0 + j;
-    if (e < DK) wk[(j * KMAX + s) * DK + e] = __fmul_rn(a.pending_key[base * DK + e], gt[(j * KMAX + s) * 2]);
-    else dl[(j * KMAX + s) * DV + (e - DK)] = a.pending_delta[base * DV + (e - DK)];
+  // The head's v channels: history, the K tokens' conv and SiLU, conv state and pending inputs.
+  for (int i = tid; i < DV; i += 128)
+    verify_conv_channel(a, b, 2 * key_dim + h * DV + i, conv_dim, K, acc, on, keep, xv + i, DV);
+  // This key head's normalised q and k of the K tokens.
+  const float* src = qk + (static_cast<int64_t>(b) * a.num_k_heads + kh) * K * 2 * DK;
+  for (int i = tid; i < K * 2 * DK; i += 128) {
+    const int t = i / (2 * DK), which = (i / DK) & 1, e = i % DK;
+    (which ? kn : qn)[t * DK + e] = src[i];
   }
-
-  // Conv: history = the KCONV - 1 inputs before the first uncommitted token (times keep), then the K tokens.
-  for (int i = tid; i < S::CH; i += blockDim.x) {
-    int c;
-    if (i < DK) c = kh * DK + i;
-    else if (i < 2 * DK) c = key_dim + kh * DK + (i - DK);
-    else c = 2 * key_dim + h0 * DV + (i - 2 * DK);
-    __nv_bfloat16* cs = a.conv_state + (static_cast<int64_t>(b) * conv_dim + c) * (KCONV - 1);
-    float win[KCONV - 1 + KMAX];
-#pragma unroll
-    for (int j = 0; j < KCONV - 1; ++j) win[j] = __bfloat162float(cs[j]);
-    for (int s = 0; s < K; ++s) win[KCONV - 1 + s] = __bfloat162float(a.pending_input[(static_cast<int64_t>(b) * K + s) * conv_dim + c]);
-    float hist[KCONV - 1];
-#pragma unroll
-    for (int j = 0; j < KCONV - 1; ++j) hist[j] = on ? __fmul_rn(win[acc + j], keep) : win[j];
-    float cw[KCONV];
-#pragma unroll
-    for (int j = 0; j < KCONV; ++j) cw[j] = __bfloat162float(a.conv_w[static_cast<int64_t>(c) * KCONV + j]);
-    float w2[KCONV - 1 + KMAX];
-#pragma unroll
-    for (int j = 0; j < KCONV - 1; ++j) w2[j] = hist[j];
-    for (int t = 0; t < K; ++t) {
-      const __nv_bfloat16 xin = a.qkvz[(static_cast<int64_t>(b) * K + t) * a.ld_qkvz + c];
-      w2[KCONV - 1 + t] = __bfloat162float(xin);
-      a.pending_input[(static_cast<int64_t>(b) * K + t) * conv_dim + c] = xin;
-    }
-    for (int t = 0; t < K; ++t) {
-      float sacc = 0.f;
-#pragma unroll
-      for (int j = 0; j < KCONV; ++j) sacc = __fadd_rn(sacc, bf16r(__fmul_rn(w2[t + j], cw[j])));
-      const float conv = bf16r(sacc);
-      xs[t * S::CH + i] = bf16r(__fmul_rn(conv, bf16r(sigmoidf_(conv))));
-    }
-    if (on) {
-#pragma unroll
-      for (int j = 0; j < KCONV - 1; ++j) cs[j] = __float2bfloat16_rn(hist[j]);
-    }
-  }
-  __syncthreads();
-  // Gates per (value head, token).
-  if (tid < R * K) {
-    const int j = tid / K, t = tid % K, h = h0 + j;
-    const int64_t r = static_cast<int64_t>(b) * K + t;
+  // Gates per token: beta = bf16(sigmoid(b)) * active, g = -exp(A_log) * softplus(a + dt_bias) * active.
+  if (tid < K) {
+    const int64_t r = static_cast<int64_t>(b) * K + tid;
     const float braw = __bfloat162float(a.ab[r * a.ld_ab + h]);
     const float araw = __bfloat162float(a.ab[r * a.ld_ab + a.num_v_heads + h]);
-    gt[(j * KMAX + t) * 2 + 0] = __fmul_rn(bf16r(sigmoidf_(braw)), act);
-    gt[(j * KMAX + t) * 2 + 1] = __fmul_rn(
+    gt[tid * 2 + 0] = __fmul_rn(bf16r(sigmoidf_(braw)), act);
+    gt[tid * 2 + 1] = __fmul_rn(
         __fmul_rn(-expf(__bfloat162float(a.a_log[h])), softplusf_(__fadd_rn(araw, __bfloat162float(a.dt_bias[h])))), act);
   }
-  // L2 norms of q (then / sqrt(dk)) and k per token.
-  const float inv_scale = static_cast<float>(sqrt(static_cast<double>(DK)));
-  for (int p = warp; p < 2 * K; p += blockDim.x / 32) {
-    const int t = p >> 1, which = p & 1;
-    const float* src = xs + t * S::CH + which * DK;
-    float* dst = (which ? kn : qn) + t * DK;
-    float ss = 0.f;
-    for (int i = lane; i < DK; i += 32) ss = __fadd_rn(ss, __fmul_rn(src[i], src[i]));
-    ss = warp_sum(ss);
-    const float r = 1.0f / sqrtf(ss + 1e-6f);
-    for (int i = lane; i < DK; i += 32) {
-      const float v = __fmul_rn(src[i], r);
-      dst[i] = which == 0 ? __fdiv_rn(v, inv_scale) : v;
-    }
+  __syncthreads();  // commit factors, v, q, k, gates
+  // The pending slices of this head (read before this step replaces them), weighted for the commit.
+  for (int i = tid; i < K * (DK + DV); i += 128) {
+    const int s = i / (DK + DV), e = i % (DK + DV);
+    const int64_t base = (static_cast<int64_t>(b) * K + s) * a.num_v_heads + h;
+    if (e < DK) wk[s * DK + e] = __fmul_rn(a.pending_key[base * DK + e], fw[s]);
+    else dl[s * DV + (e - DK)] = a.pending_delta[base * DV + (e - DK)];
   }
-  __syncthreads();
-  // k_t . k_s (s < t) and q_t . k_s (s <= t).
-  for (int p = warp; p < 2 * K * K; p += blockDim.x / 32) {
+  // k_t . k_s (s < t) and q_t . k_s (s <= t), one warp per dot.
+  for (int p = warp; p < 2 * K * K; p += 4) {
     const int which = p / (K * K), t = (p / K) % K, s = p % K;
     const float* x = (which ? qn : kn) + t * DK;
     const float* y = kn + s * DK;
-    float d = 0.f;
-    for (int i = lane; i < DK; i += 32) d = fmaf(x[i], y[i], d);
-    d = warp_sum(d);
-    if (lane == 0) dots[(which * KMAX + t) * KMAX + s] = d;
+    float dsum = 0.f;
+    for (int i = lane; i < DK; i += 32) dsum = fmaf(x[i], y[i], dsum);
+    dsum = warp_sum(dsum);
+    if (lane == 0) dots[(which * KMAX + t) * KMAX + s] = dsum;
   }
+  const bool ok = mbar_wait(bar, 0);
+  if (__syncthreads_or(!ok)) return;  // the copy timed out (recorded): nothing written
 
-  // Per value head group: commit, products, the chunk, pending, output.
-  const int j = tid >> 7;
-  const int gl = tid & 127;
-  const int gw = gl >> 5;
+  // Commit S' = bf16(S * scale + sum_s w_s k_s delta_s^T) in place, and [k_t; q_t]^T S'.
   const int c0 = lane * CPL;
-  const int h = h0 + j;
-  __syncthreads();  // the dots and norms above are complete
-  if (gl == 0) failed[j] = 0;
-  group_bar(1 + j);
-  if (!mbar_wait(&bars[j], 0)) failed[j] = 1;
-  group_bar(1 + j);
-  if (failed[j]) return;  // no block-wide barrier follows: each group leaves on its own
-  __nv_bfloat16* tile = st + static_cast<size_t>(j) * DK * DV;
-  const float scale = scl[j];
+  const float scale = scl[0];
   float prod[2 * KMAX][CPL];
 #pragma unroll
   for (int t = 0; t < 2 * KMAX; ++t)
 #pragma unroll
     for (int e = 0; e < CPL; ++e) prod[t][e] = 0.f;
   for (int r = 0; r < ROWS_W; ++r) {
-    const int i = gw * ROWS_W + r;
+    const int i = warp * ROWS_W + r;
     float sv[CPL];
     load_row<CPL>(tile + i * DV + c0, sv);
 #pragma unroll
     for (int e = 0; e < CPL; ++e) {
       float w = 0.f;
-      for (int s = 0; s < K; ++s) w = fmaf(wk[(j * KMAX + s) * DK + i], dl[(j * KMAX + s) * DV + c0 + e], w);
+#pragma unroll
+      for (int s = 0; s < KMAX; ++s)
+        if (s < K) w = fmaf(wk[s * DK + i], dl[s * DV + c0 + e], w);
       sv[e] = bf16r(__fadd_rn(__fmul_rn(sv[e], scale), w));
     }
     if (on) store_row<CPL>(tile + i * DV + c0, sv);
@@ -264,60 +293,59 @@ __global__ void __launch_bounds__(R * 128) gdn_verify_kernel(VerifyArgs a) {
     if (t >= K) break;
 #pragma unroll
     for (int e = 0; e < CPL; ++e) {
-      red[((j * 4 + gw) * 2 * KMAX + t) * DV + c0 + e] = prod[t][e];
-      red[((j * 4 + gw) * 2 * KMAX + KMAX + t) * DV + c0 + e] = prod[KMAX + t][e];
+      red[(warp * 2 * KMAX + t) * DV + c0 + e] = prod[t][e];
+      red[(warp * 2 * KMAX + KMAX + t) * DV + c0 + e] = prod[KMAX + t][e];
     }
   }
   fence_proxy_async_shared();  // the committed tile is visible to the bulk copy engine
-  group_bar(1 + j);
-  if (gl == 0 && on) {
+  __syncthreads();
+  if (tid == 0 && on) {
     bulk_store(a.state + (static_cast<int64_t>(b) * a.num_v_heads + h) * DK * DV, tile, TILE_BYTES);
     bulk_commit();
   }
   // The K x K chunk, one state column per thread.
-  if (gl < DV) {
-    const int c = gl;
+  for (int c = tid; c < DV; c += 128) {
     float cum[KMAX], dlt[KMAX];
 #pragma unroll
     for (int t = 0; t < KMAX; ++t) {
-      cum[t] = t == 0 ? gt[(j * KMAX) * 2 + 1] : __fadd_rn(cum[t - 1], gt[(j * KMAX + t) * 2 + 1]);
+      cum[t] = t == 0 ? gt[1] : __fadd_rn(cum[t - 1], gt[t * 2 + 1]);
       dlt[t] = 0.f;
     }
 #pragma unroll
     for (int t = 0; t < KMAX; ++t) {
       if (t >= K) break;
       float ks = 0.f, qs = 0.f;
+#pragma unroll
       for (int w = 0; w < 4; ++w) {
-        ks = __fadd_rn(ks, red[((j * 4 + w) * 2 * KMAX + t) * DV + c]);
-        qs = __fadd_rn(qs, red[((j * 4 + w) * 2 * KMAX + KMAX + t) * DV + c]);
+        ks = __fadd_rn(ks, red[(w * 2 * KMAX + t) * DV + c]);
+        qs = __fadd_rn(qs, red[(w * 2 * KMAX + KMAX + t) * DV + c]);
       }
-      const float v = xs[t * S::CH + 2 * DK + j * DV + c];
-      float d = __fsub_rn(v, __fmul_rn(expf(cum[t]), ks));
+      float dd = __fsub_rn(xv[t * DV + c], __fmul_rn(expf(cum[t]), ks));
 #pragma unroll
       for (int s = 0; s < t; ++s)
-        d = __fsub_rn(d, __fmul_rn(__fmul_rn(expf(__fsub_rn(cum[t], cum[s])), dots[(0 * KMAX + t) * KMAX + s]), dlt[s]));
-      dlt[t] = __fmul_rn(d, gt[(j * KMAX + t) * 2 + 0]);
+        dd = __fsub_rn(dd, __fmul_rn(__fmul_rn(expf(__fsub_rn(cum[t], cum[s])), dots[(0 * KMAX + t) * KMAX + s]), dlt[s]));
+      dlt[t] = __fmul_rn(dd, gt[t * 2 + 0]);
       float o = __fmul_rn(expf(cum[t]), qs);
 #pragma unroll
       for (int s = 0; s <= t; ++s)
         o = __fadd_rn(o, __fmul_rn(__fmul_rn(expf(__fsub_rn(cum[t], cum[s])), dots[(1 * KMAX + t) * KMAX + s]), dlt[s]));
-      ob[(j * KMAX + t) * DV + c] = bf16r(o);
+      ob[t * DV + c] = bf16r(o);
       a.pending_delta[((static_cast<int64_t>(b) * K + t) * a.num_v_heads + h) * DV + c] = dlt[t];
     }
   }
-  for (int i = gl; i < K * DK; i += 128) {
+  for (int i = tid; i < K * DK; i += 128) {
     const int t = i / DK, e = i % DK;
     a.pending_key[((static_cast<int64_t>(b) * K + t) * a.num_v_heads + h) * DK + e] = kn[t * DK + e];
   }
-  if (gl < K) a.pending_decay[(static_cast<int64_t>(b) * K + gl) * a.num_v_heads + h] = gt[(j * KMAX + gl) * 2 + 1];
-  group_bar(1 + j);
-  // Gated RMS norm of each token's output for this head, times SiLU(z); e5m2 out.
-  for (int t = gw; t < K; t += 4) {
+  if (tid < K) a.pending_decay[(static_cast<int64_t>(b) * K + tid) * a.num_v_heads + h] = gt[tid * 2 + 1];
+  __syncthreads();
+  // Gated RMS norm of each token's output for this head, times SiLU(z); e5m2 out. Warp w: tokens w, w+4, ...
+  for (int t = warp; t < K; t += 4) {
     float o[CPL];
     float ss = 0.f;
 #pragma unroll
     for (int e = 0; e < CPL; ++e) {
-      o[e] = ob[(j * KMAX + t) * DV + c0 + e];
+      o[e] = ob[t * DV + c0 + e];
       ss = __fadd_rn(ss, __fmul_rn(o[e], o[e]));
     }
     ss = warp_sum(ss);
@@ -334,28 +362,35 @@ __global__ void __launch_bounds__(R * 128) gdn_verify_kernel(VerifyArgs a) {
       orow[c] = f32_to_e5m2(bf16r(__fmul_rn(n2, __fmul_rn(z, sigmoidf_(z)))));
     }
   }
-  if (gl == 0 && on) bulk_wait_read0();  // the tile must stay until the copy engine has read it
+  if (tid == 0 && on) bulk_wait_read0();  // the tile must stay until the copy engine has read it
 }
 
-template <int DK, int DV, int R>
-int launch_verify(const VerifyArgs& a, int64_t batch, cudaStream_t stream) {
-  using S = VerifySmem<DK, DV, R>;
+template <int DK, int DV>
+int launch_verify(const VerifyArgs& a, int64_t batch, float* qk, cudaStream_t stream) {
+  using S = VerifySmem<DK, DV>;
   static unsigned long long done_mask = 0;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return q38host::cuda_status(e, "cudaGetDevice");
   if (dev < 64 && !(done_mask & (1ull << dev))) {
-    e = cudaFuncSetAttribute(gdn_verify_kernel<DK, DV, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(gdn_verify_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(S::TOTAL));
     if (e != cudaSuccess) return q38host::cuda_status(e, "cudaFuncSetAttribute(gdn_verify)");
     done_mask |= 1ull << dev;
   }
-  dim3 grid(static_cast<unsigned>(a.num_k_heads), static_cast<unsigned>(batch));
-  gdn_verify_kernel<DK, DV, R><<<grid, R * 128, S::TOTAL, stream>>>(a);
+  gdn_verify_qk_kernel<DK><<<dim3(a.num_k_heads, static_cast<unsigned>(batch)), DK, 0, stream>>>(a, qk);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return q38host::cuda_status(e, "gdn_verify_qk launch");
+  gdn_verify_kernel<DK, DV><<<dim3(a.num_v_heads, static_cast<unsigned>(batch)), 128, S::TOTAL, stream>>>(a, qk);
   return q38host::cuda_status(cudaGetLastError(), "gdn_verify launch");
 }
 
 }  // namespace
+
+extern "C" size_t q38_gdn_verify_workspace_bytes(int64_t batch, int tokens, int num_k_heads, int head_k) {
+  if (batch <= 0 || tokens <= 0 || num_k_heads <= 0 || head_k <= 0) return 0;
+  return sizeof(float) * static_cast<size_t>(batch) * num_k_heads * tokens * 2 * head_k;
+}
 
 extern "C" int q38_gdn_verify_commit(const void* qkvz, int64_t ld_qkvz, const void* ab, int64_t ld_ab, void* conv_state,
                                      const void* conv_weight, const void* a_log, const void* dt_bias,
@@ -363,10 +398,11 @@ extern "C" int q38_gdn_verify_commit(const void* qkvz, int64_t ld_qkvz, const vo
                                      void* pending_decay, void* pending_input, const int32_t* position,
                                      const float* active, const int32_t* accepted, void* out, int64_t ld_out,
                                      int64_t batch, int tokens, int num_k_heads, int num_v_heads, int head_k,
-                                     int head_v, int conv_kernel, float eps, q38_stream_t stream) {
+                                     int head_v, int conv_kernel, float eps, void* workspace, size_t workspace_bytes,
+                                     q38_stream_t stream) {
   using namespace q38host;
   if (!qkvz || !ab || !conv_state || !conv_weight || !a_log || !dt_bias || !norm_weight || !state || !pending_key ||
-      !pending_delta || !pending_decay || !pending_input || !position || !active || !accepted || !out)
+      !pending_delta || !pending_decay || !pending_input || !position || !active || !accepted || !out || !workspace)
     return set_error("q38_gdn_verify_commit: null pointer"), Q38_ERR_ARG;
   if (batch <= 0 || batch > 65535 || tokens < 1 || tokens > KMAX)
     return set_error("q38_gdn_verify_commit: batch %lld / %d tokens per row (1..%d built)", static_cast<long long>(batch),
@@ -381,6 +417,11 @@ extern "C" int q38_gdn_verify_commit(const void* qkvz, int64_t ld_qkvz, const vo
   if (ld_qkvz < conv_dim + static_cast<int64_t>(num_v_heads) * head_v || ld_ab < 2 * num_v_heads ||
       ld_out < static_cast<int64_t>(num_v_heads) * head_v)
     return set_error("q38_gdn_verify_commit: leading dimension too small"), Q38_ERR_ARG;
+  if (workspace_bytes < q38_gdn_verify_workspace_bytes(batch, tokens, num_k_heads, head_k) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 15u) != 0)
+    return set_error("q38_gdn_verify_commit: workspace needs %zu bytes, 16-byte aligned",
+                     q38_gdn_verify_workspace_bytes(batch, tokens, num_k_heads, head_k)),
+           Q38_ERR_ARG;
   VerifyArgs a{};
   a.qkvz = static_cast<const __nv_bfloat16*>(qkvz);
   a.ld_qkvz = ld_qkvz;
@@ -403,12 +444,14 @@ extern "C" int q38_gdn_verify_commit(const void* qkvz, int64_t ld_qkvz, const vo
   a.ld_out = ld_out;
   a.num_k_heads = num_k_heads;
   a.num_v_heads = num_v_heads;
+  a.head_v = head_v;
   a.K = tokens;
   a.eps = eps;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int rep = num_v_heads / num_k_heads;
-  if (head_k == 128 && head_v == 128 && rep == 3) return launch_verify<128, 128, 3>(a, batch, s);
-  if (head_k == 32 && head_v == 32 && rep == 3) return launch_verify<32, 32, 3>(a, batch, s);
+  float* qk = static_cast<float*>(workspace);
+  if (head_k == 128 && head_v == 128 && rep == 3) return launch_verify<128, 128>(a, batch, qk, s);
+  if (head_k == 32 && head_v == 32 && rep == 3) return launch_verify<32, 32>(a, batch, qk, s);
   return set_error("q38_gdn_verify_commit: head dims %d/%d with %d value heads per key head not built", head_k, head_v,
                    rep),
          Q38_ERR_UNSUPPORTED;

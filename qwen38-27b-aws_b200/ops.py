@@ -195,6 +195,10 @@ def gdn_decode_workspace_bytes(batch: int, num_k_heads: int, head_k: int) -> int
     return _lib.load().q38_gdn_decode_workspace_bytes(batch, num_k_heads, head_k)
 
 
+def gdn_verify_workspace_bytes(batch: int, tokens: int, num_k_heads: int, head_k: int) -> int:
+    return _lib.load().q38_gdn_verify_workspace_bytes(batch, tokens, num_k_heads, head_k)
+
+
 _workspaces: dict = {}
 _retired: list = []
 
@@ -275,10 +279,13 @@ def attn_prefill(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, out, works
 
 def gdn_verify(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, state, pending_key, pending_delta,
                pending_decay, pending_input, position, active, accepted, out, *, batch: int, tokens: int,
-               num_k_heads: int, num_v_heads: int, head_k: int, head_v: int, eps: float) -> None:
+               num_k_heads: int, num_v_heads: int, head_k: int, head_v: int, eps: float,
+               workspace: torch.Tensor | None = None) -> None:
     """K verify tokens per row with commit-on-accept (rows b * tokens + t of qkvz/ab/out)."""
     _cuda(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, state, pending_key, pending_delta,
-          pending_decay, pending_input, position, active, accepted, out)
+          pending_decay, pending_input, position, active, accepted, out, workspace)
+    need = _lib.load().q38_gdn_verify_workspace_bytes(batch, tokens, num_k_heads, head_k)
+    ws = workspace if workspace is not None else _workspace(qkvz.device, need)
     _need(position.dtype == torch.int32 and accepted.dtype == torch.int32 and active.dtype == torch.float32,
           "position/accepted int32, active float32")
     _need(pending_key.dtype == torch.float32 and pending_delta.dtype == torch.float32 and
@@ -291,7 +298,7 @@ def gdn_verify(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, s
               norm_weight.data_ptr(), state.data_ptr(), pending_key.data_ptr(), pending_delta.data_ptr(),
               pending_decay.data_ptr(), pending_input.data_ptr(), position.data_ptr(), active.data_ptr(),
               accepted.data_ptr(), out.data_ptr(), out.stride(0), batch, tokens, num_k_heads, num_v_heads, head_k,
-              head_v, conv_weight.shape[1], eps, _stream())
+              head_v, conv_weight.shape[1], eps, ws.data_ptr(), ws.numel() * ws.element_size(), _stream())
 
 
 def attn_verify(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, position, active, out, *, batch: int, tokens: int,

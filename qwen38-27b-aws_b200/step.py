@@ -238,7 +238,8 @@ class B200Step:
                          head_k=cfg.linear_key_head_dim, head_v=cfg.linear_value_head_dim, eps=eps)
             if verify:
                 ops.gdn_verify(a.proj, a.ab, m.conv_state, m.conv_w, m.a_log, m.dt_bias, m.norm_w, m.state, *m.pending,
-                               a.position, a.active, a.accepted, a.mix_gdn, batch=self.batch, tokens=verify, **heads)
+                               a.position, a.active, a.accepted, a.mix_gdn, batch=self.batch, tokens=verify,
+                               workspace=a.gdn_verify_ws, **heads)
             elif chunk is None:
                 ops.gdn_decode(a.proj, a.ab, m.conv_state, m.conv_w, m.a_log, m.dt_bias, m.norm_w, m.state,
                                a.position, a.active, a.mix_gdn, batch=self.batch, workspace=self.gdn_workspace, **heads)
@@ -336,6 +337,9 @@ class B200Step:
                 a.position = torch.zeros(B, dtype=torch.int32, device=self.device)
                 a.active = torch.zeros(B, dtype=torch.float32, device=self.device)
                 a.accepted = torch.zeros(B, dtype=torch.int32, device=self.device)
+                cfg = self.cfg
+                need = ops.gdn_verify_workspace_bytes(B, K, cfg.linear_num_key_heads // self.tp, cfg.linear_key_head_dim)
+                a.gdn_verify_ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
             self._verify_acts = a
         a.x.copy_(embeds.reshape(B * K, -1), non_blocking=True)
         a.cos.copy_(cos.reshape(B * K, -1), non_blocking=True)
