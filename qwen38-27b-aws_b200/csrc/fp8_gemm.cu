@@ -600,6 +600,285 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// ---------------------------------------------------------------------------------------------
+// Persistent form for unsplit GEMMs (EPI_BF16, EPI_GROUPMAX): each CTA (or 2-SM pair) walks output
+// tiles. The producer's stage ring runs on across tiles; the MMA warp waits for "TMEM empty" before a
+// tile's first MMA; the epilogue warps drain the accumulator into their own staging buffer, release
+// TMEM at once, and store while the next tile's mainloop runs. Per-CTA setup and the pipeline fill
+// are paid once per CTA instead of once per tile, and a grid that would take 1.8 waves becomes one
+// pass over the tiles.
+// ---------------------------------------------------------------------------------------------
+template <int NTOK, bool MX, bool PAIR>
+struct PCfg {
+  static constexpr int A_BYTES = BM * BK_BYTES;
+  static constexpr int B_ROWS = PAIR ? NTOK / 2 : NTOK;
+  static constexpr int B_BYTES = B_ROWS * BK_BYTES;
+  static constexpr int SF_BYTES = MX ? SF_BLOCK : 0;
+  static constexpr int STAGES = PAIR ? 4 : 3;  // leaves room for the output staging tile
+  static constexpr int TMEM_COLS = NTOK == 256 ? 512 : 256;
+  static constexpr int SFA_COL = NTOK;
+  static constexpr int SFB_COL = NTOK + 32;
+  static constexpr size_t PIPE = STAGES * (A_BYTES + B_BYTES + SF_BYTES);
+  static constexpr size_t OUT = static_cast<size_t>(NTOK) * BM * 2;  // bf16 [NTOK tokens][128 rows]
+  static constexpr size_t SMEM = 1024 + PIPE + OUT + 256;
+  static_assert(SFA_COL + 4 * STAGES <= SFB_COL && SFB_COL + 8 <= TMEM_COLS, "TMEM columns");
+};
+
+template <int NTOK, bool MX, bool PAIR>
+__global__ void __launch_bounds__(192, 1)
+    gemm_persistent_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_y,
+                           const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_sf,
+                           GemmArgs a) {
+  using C = PCfg<NTOK, MX, PAIR>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + C::STAGES * C::A_BYTES;
+  uint8_t* sSF = sB + C::STAGES * C::B_BYTES;
+  uint8_t* sOut = smem + C::PIPE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sOut + C::OUT);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* accf = empty + C::STAGES;
+  uint64_t* tmem_empty = accf + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_empty + 1);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_holder + 1);  // [0] abort
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t crank = PAIR ? cluster_rank() : 0u;
+  const int prank = PAIR ? static_cast<int>(crank & 1u) : 0;
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << (crank & ~1u));
+  const int group = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int ngroups = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int rows_per_unit = PAIR ? 2 * BM : BM;
+  const int m_units = (a.F + rows_per_unit - 1) / rows_per_unit;
+  const int n_tiles = (a.T + NTOK - 1) / NTOK;
+  const int units = m_units * n_tiles;
+  const int nk = a.nkc;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accf, 1);
+    mbar_init(tmem_empty, PAIR ? 2 : 1);
+    flags[0] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_holder, C::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_holder, C::TMEM_COLS);
+      tmem_relinquish();
+    }
+  }
+  tc_fence_before();
+  if constexpr (PAIR) cluster_sync();
+  else __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_holder;
+  if (MX && warp >= 2) tmem_st8_fill(tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16) + C::SFB_COL, 0x7f7f7f7fu);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmap_x);
+      int it = 0;
+      for (int u = group; u < units && !flags[0]; u += ngroups) {
+        const int mp = u % m_units, nt = u / m_units;
+        const int mt = PAIR ? 2 * mp + prank : mp;
+        const int n0 = nt * NTOK;
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (flags[0] || !mbar_wait(&empty[s], ph ^ 1)) {
+            flags[0] = 1;
+            break;
+          }
+          const int kx = i * (MX ? BK_BYTES : BK_BYTES / 2);
+          const int tile_id = mt * a.nkc + i;
+          if constexpr (PAIR) {
+            if (prank == 0) mbar_arrive_expect_tx(&full[s], 2 * (C::A_BYTES + C::B_BYTES + C::SF_BYTES));
+            tma_load_2d_pair(sA + s * C::A_BYTES, &tmap_w, &full[s], 0, tile_id * BM);
+            tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0 + prank * C::B_ROWS);
+            tma_load_2d_pair(sSF + s * SF_BLOCK, &tmap_sf, &full[s], 0, tile_id * 32);
+          } else {
+            mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES + C::SF_BYTES);
+            bulk_load(sA + s * C::A_BYTES, a.w + static_cast<size_t>(tile_id) * C::A_BYTES, C::A_BYTES, &full[s]);
+            tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0);
+            if (MX) bulk_load(sSF + s * SF_BLOCK, a.sf + static_cast<size_t>(tile_id) * SF_BLOCK, SF_BLOCK, &full[s]);
+          }
+        }
+      }
+      // Never leave with copies in flight: wait (bounded) for the last load of every stage.
+      if (!PAIR || prank == 0)
+        for (int j = max(0, it - C::STAGES); j < it; ++j) mbar_wait(&full[j % C::STAGES], (j / C::STAGES) & 1);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && (!PAIR || prank == 0)) {
+      uint32_t idesc;
+      if (MX) {
+        idesc = (0u << 7) | (1u << 10) | (static_cast<uint32_t>(NTOK >> 3) << 17) | (1u << 23) |
+                (static_cast<uint32_t>((PAIR ? 2 * BM : BM) >> 4) << 24);
+      } else {
+        idesc = (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(NTOK >> 3) << 17) |
+                (static_cast<uint32_t>(BM >> 4) << 24);
+      }
+      int it = 0, tc = 0;
+      for (int u = group; u < units && !flags[0]; u += ngroups, ++tc) {
+        // The epilogue has drained the previous tile's accumulator.
+        if (!mbar_wait(tmem_empty, (tc & 1) ^ 1)) {
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        for (int i = 0; i < nk; ++i, ++it) {
+          const int s = it % C::STAGES;
+          const uint32_t ph = (it / C::STAGES) & 1;
+          if (flags[0] || !mbar_wait(&full[s], ph)) {
+            flags[0] = 1;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + s * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + s * C::B_BYTES);
+          if constexpr (PAIR) {
+            const uint32_t sfa = tmem + C::SFA_COL + 4 * s;
+            tmem_cp_32x128b_x4_pair(sfa, sdesc_rows16(smem_u32(sSF + s * SF_BLOCK)));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t id = idesc | (static_cast<uint32_t>(kk) << 29) | (static_cast<uint32_t>(kk) << 4);
+              mma_mxf8_pair(tmem, sdesc_sw128(a_addr + kk * 32), sdesc_sw128(b_addr + kk * 32), id,
+                            sfa | (static_cast<uint32_t>(kk) << 30), (tmem + C::SFB_COL) | (static_cast<uint32_t>(kk) << 30),
+                            (i | kk) != 0);
+            }
+            tc_commit_pair(&empty[s], pair_mask);
+          } else if (MX) {
+            const uint32_t sfa = tmem + C::SFA_COL + 4 * s;
+            tmem_cp_32x128b_x4(sfa, sdesc_rows16(smem_u32(sSF + s * SF_BLOCK)));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t id = idesc | (static_cast<uint32_t>(kk) << 29) | (static_cast<uint32_t>(kk) << 4);
+              mma_mxf8(tmem, sdesc_sw128(a_addr + kk * 32), sdesc_sw128(b_addr + kk * 32), id,
+                       sfa | (static_cast<uint32_t>(kk) << 30), (tmem + C::SFB_COL) | (static_cast<uint32_t>(kk) << 30),
+                       (i | kk) != 0);
+            }
+            tc_commit(&empty[s]);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_f16(tmem, sdesc_sw128(a_addr + kk * 32), sdesc_sw128(b_addr + kk * 32), idesc, (i | kk) != 0);
+            tc_commit(&empty[s]);
+          }
+        }
+        if (flags[0]) break;
+        if constexpr (PAIR) tc_commit_pair(accf, pair_mask);
+        else tc_commit(accf);
+      }
+    }
+    __syncwarp();
+  } else {
+    // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31; lane = output row.
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(sOut);
+    int tc = 0;
+    for (int u = group; u < units; u += ngroups, ++tc) {
+      const int mp = u % m_units, nt = u / m_units;
+      const int mt = PAIR ? 2 * mp + prank : mp;
+      const int m0 = mt * BM, n0 = nt * NTOK;
+      const bool ok = !epi_bar_or(!mbar_wait(accf, tc & 1));
+      if (!ok) {
+        if (threadIdx.x == 64) flags[0] = 1;
+        break;
+      }
+      tc_fence_after();
+      // The previous tile's store has finished reading the staging buffer.
+      if (a.epilogue != EPI_GROUPMAX && threadIdx.x == 64) bulk_wait_read0();
+      epi_bar();
+      for (int c = 0; c < NTOK; c += 16) {
+        if (n0 + c >= a.T) break;
+        float v[16];
+        tmem_ld16(taddr + c, v);
+        if (a.epilogue == EPI_GROUPMAX) {
+          epilogue16(a, m0 + r, n0 + c, v, lane);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) st[(c + j) * BM + r] = __float2bfloat16_rn(v[j]);
+        }
+      }
+      // Every TMEM read of this tile is complete: hand the accumulator back to the MMA warp.
+      tc_fence_before();
+      epi_bar();
+      if (threadIdx.x == 64) {
+        if constexpr (PAIR) mbar_arrive_cluster(tmem_empty, crank & ~1u);
+        else mbar_arrive(tmem_empty);
+      }
+      if (a.epilogue != EPI_GROUPMAX) {
+        fence_proxy_async_shared();
+        epi_bar();
+        if (threadIdx.x == 64 && m0 < a.F) {
+          for (int b = 0; b < NTOK / TOK_BLOCK; ++b)
+            if (n0 + b * TOK_BLOCK < a.T) tma_store_2d(&tmap_y, sOut + b * TOK_BLOCK * BM * 2, m0, n0 + b * TOK_BLOCK);
+          bulk_commit();
+        }
+      }
+    }
+    if (threadIdx.x == 64) bulk_wait_read0();
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  if constexpr (PAIR) cluster_sync();  // the pair frees its tensor memory together
+  else __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    if constexpr (PAIR) tmem_dealloc_pair(tmem, C::TMEM_COLS);
+    else tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int NTOK, bool MX, bool PAIR>
+int launch_persistent(const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap& tw, const CUtensorMap& tsf,
+                      const GemmArgs& a, cudaStream_t stream) {
+  using C = PCfg<NTOK, MX, PAIR>;
+  static unsigned long long done_mask = 0;
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return q38host::cuda_status(e, "cudaGetDevice");
+  if (dev >= 64) return q38host::set_error("device ordinal %d too large", dev), Q38_ERR_UNSUPPORTED;
+  if (!(done_mask & (1ull << dev))) {
+    e = cudaFuncSetAttribute(gemm_persistent_kernel<NTOK, MX, PAIR>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(C::SMEM));
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return q38host::cuda_status(e, "persistent gemm setup");
+    done_mask |= 1ull << dev;
+  }
+  const int rows_per_unit = PAIR ? 2 * BM : BM;
+  const int units = static_cast<int>(((a.F + rows_per_unit - 1) / rows_per_unit) * ((a.T + NTOK - 1) / NTOK));
+  const int groups = std::min(units, PAIR ? sms[dev] / 2 : sms[dev]);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(PAIR ? 2 * groups : groups), 1, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = PAIR ? 2u : 1u;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, gemm_persistent_kernel<NTOK, MX, PAIR>, tx, ty, tw, tsf, a);
+  return q38host::cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "persistent gemm launch");
+}
+
 template <int NTOK, bool MX, bool PAIR = false>
 int launch_gemm(const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap& tr, const GemmArgs& a, dim3 grid,
                 cudaStream_t stream, const CUtensorMap* tw = nullptr, const CUtensorMap* tsf = nullptr,
@@ -740,6 +1019,8 @@ int gemm_fp8(const void* x, int64_t tokens, int64_t k, const void* w, const void
   if (st != Q38_OK) return st;
   if (a.cluster == 0) ty = tr = tx;
   const bool resident = ar != nullptr;
+  // Unsplit bf16 outputs take the persistent tile loop.
+  const bool persistent = ar == nullptr && epilogue == Q38_EPI_BF16 && a.cluster == 1;
   // The 2-SM form for full 256-token tiles whose cluster (2 x splits) stays portable.
   if (ntok == 256 && a.cluster > 0 && 2 * a.cluster <= kMaxClusterSplits && features > BM) {
     // Each CTA of a pair loads half of the 256-token tile: the activation box is 128 rows.
@@ -751,10 +1032,14 @@ int gemm_fp8(const void* x, int64_t tokens, int64_t k, const void* w, const void
     if (st != Q38_OK) return st;
     st = encode_tmap_2d(&tsf, w_sf, tiles * 32, 16, 1, 32, 16, false);
     if (st != Q38_OK) return st;
+    if (persistent) return launch_persistent<256, true, true>(tx, ty, tw, tsf, a, s);
     dim3 grid(static_cast<unsigned>(2 * cdiv(features, 2 * BM)), static_cast<unsigned>(cdiv(tokens, ntok)),
               static_cast<unsigned>(splits));
     return launch_gemm<256, true, true>(tx, ty, tr, a, grid, s, &tw, &tsf, resident);
   }
+  if (persistent)
+    return ntok == 256 ? launch_persistent<256, true, false>(tx, ty, tx, tx, a, s)
+                       : launch_persistent<128, true, false>(tx, ty, tx, tx, a, s);
   dim3 grid(static_cast<unsigned>(cdiv(features, BM)), static_cast<unsigned>(cdiv(tokens, ntok)), static_cast<unsigned>(splits));
   return ntok == 256 ? launch_gemm<256, true>(tx, ty, tr, a, grid, s, nullptr, nullptr, resident)
                      : launch_gemm<128, true>(tx, ty, tr, a, grid, s, nullptr, nullptr, resident);
@@ -834,9 +1119,9 @@ extern "C" int q38_lm_head_groupmax(const void* x, int64_t rows, int64_t k, cons
   CUtensorMap tx;
   int st = encode_tmap_2d(&tx, x, rows, k, 2, ntok, BK_BYTES / 2);
   if (st != Q38_OK) return st;
-  dim3 grid(static_cast<unsigned>(cdiv(vocab, BM)), static_cast<unsigned>(cdiv(rows, ntok)), 1);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return ntok == 256 ? launch_gemm<256, false>(tx, tx, tx, a, grid, s) : launch_gemm<128, false>(tx, tx, tx, a, grid, s);
+  return ntok == 256 ? launch_persistent<256, false, false>(tx, tx, tx, tx, a, s)
+                     : launch_persistent<128, false, false>(tx, tx, tx, tx, a, s);
 }
 
 extern "C" int q38_bf16_linear(const void* x, int64_t ldx, int64_t rows, int64_t k, const void* w, int64_t n_out,
