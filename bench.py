@@ -419,6 +419,18 @@ def run_micro(args):
             ops.fp8_gemm(x, lins[i % len(lins)], y, splits=splits, workspace=ws)
         per = n * k + n * (k // 32) + B * k + B * n * 2
         unit, bound = "GB/s", "hbm"
+    elif args.micro == "gemm_silu":
+        # The MLP's gate/up GEMM with SiLU(gate) * up in the epilogue (hidden -> 2 x intermediate).
+        k, inter = cfg.hidden_size, cfg.intermediate_size // args.tp
+        rnd = lambda: pkg.weights.FP8Weight.from_float(torch.randn(inter, k, device=dev, generator=gen) * 0.02)  # noqa: E731
+        lins = [ops.DeviceLinear(pkg.weights.FP8Weight.interleave_rows(rnd(), rnd()), dev) for _ in range(args.copies)]
+        x = pkg.codec.to_e5m2_bytes(bf(B, k))
+        y = torch.empty(B, inter, dtype=torch.uint8, device=dev)
+
+        def launch(i):
+            ops.fp8_gemm_silu(x, lins[i % len(lins)], y)
+        per = 2 * inter * k + 2 * inter * (k // 32) + B * k + B * inter
+        unit, bound = "GB/s", "hbm"
     if args.micro == "gdn_prefill":
         # one 512-token prefill chunk through the gated delta rule (48 value heads,
         # dk = dv = 128), continuing a row (start > 0). Work: the chunked rule's fp32 products.
@@ -585,7 +597,7 @@ def run_micro_allreduce(args, world, rank, local):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--micro", choices=["gdn", "gemm", "attn", "ab", "gdn_prefill", "attn_prefill", "verify", "gemm_ar"],
+    ap.add_argument("--micro", choices=["gdn", "gemm", "gemm_silu", "attn", "ab", "gdn_prefill", "attn_prefill", "verify", "gemm_ar"],
                     help="time one kernel alone (profiling) instead of the step; gemm_ar: the fused all-reduce under torchrun")
     ap.add_argument("--copies", type=int, default=4, help="--micro: distinct weight/state copies cycled (defeat L2)")
     ap.add_argument("--tp", type=int, default=1, help="--micro gemm: K = 17408 / tp")

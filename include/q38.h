@@ -287,6 +287,17 @@ int q38_fp8_gemm_allreduce(const void* x_q, int64_t tokens, int64_t k, const voi
                            int64_t features, int splits, q38_comm_t comm, q38_stream_t stream);
 
 /*
+ * The MLP's gate and up projections with SiLU(gate) * up fused into the epilogue: x_q e5m2 [tokens, k]
+ * times the FP8 weight whose 128-row tiles hold 64 gate rows then the 64 matching up rows
+ * (FP8Weight.interleave_rows), y e5m2 [tokens, ldy] with features / 2 columns:
+ * y = e5m2(bf16(bf16(g * bf16(sigmoid(g))) * u)), g and u the bf16 projections. Replaces
+ * `silu(gate_proj(x)) * up_proj(x)` and down_proj's input rounding (qwen38_inf2/model.py:259, :85-87;
+ * NKI mlp_up kernels.py:74-118).
+ */
+int q38_fp8_gemm_silu(const void* x_q, int64_t tokens, int64_t k, const void* w, const void* w_sf, int64_t features,
+                      void* y, int64_t ldy, q38_stream_t stream);
+
+/*
  * lm_head candidates: maxima[r, j] = max over the `group` vocab rows v in group j of
  * sum_k x[r, k] * w[v, k], fp32 (x bf16 [rows, k], w bf16 [vocab, k] pre-tiled). Replaces HeadStep.forward's
  * logits and group maxima (qwen38_inf2/model.py:890-900) and the NKI lm_head_group_maxima

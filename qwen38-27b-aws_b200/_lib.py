@@ -85,6 +85,7 @@ SIGNATURES = {
     "q38_comm_residual": (c_void_p, [c_void_p]),
     "q38_comm_destroy": (c_int, [c_void_p]),
     "q38_fp8_gemm_allreduce": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_void_p]),
+    "q38_fp8_gemm_silu": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p]),
     "q38_lm_head_groupmax": (
         c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int, c_void_p, c_int64, c_void_p]
     ),

@@ -38,7 +38,7 @@ constexpr int BM = 128;          // features per tile (MMA M)
 constexpr int BK_BYTES = 128;    // K bytes per pipeline stage (one 128-byte swizzle row)
 constexpr int SF_BLOCK = 512;    // scale bytes per (128 rows, 128 K) block
 
-enum : int { EPI_BF16 = 0, EPI_RESIDUAL = 1, EPI_GROUPMAX = 2, EPI_ALLREDUCE = 3 };
+enum : int { EPI_BF16 = 0, EPI_RESIDUAL = 1, EPI_GROUPMAX = 2, EPI_ALLREDUCE = 3, EPI_SILU = 4 };
 
 // PAIR: the 2-SM form. A cluster pair of CTAs computes 256 weight rows x NTOK tokens with
 // tcgen05.mma.cta_group::2 issued by the even CTA; each CTA loads its own 128 weight rows and half of
@@ -75,6 +75,8 @@ struct GemmArgs {
   int cluster;            // > 0: epilogue through shared memory, the `cluster` K splits of a tile
                           // forming one thread-block cluster; 0: workspace mode
   ArArgs ar;              // EPI_ALLREDUCE: the ranks' exchange regions
+  uint8_t* yq;            // EPI_SILU: e5m2 [T, ldq] of SiLU(gate) * up
+  int64_t ldq;
 };
 
 // Epilogue staging (cluster mode), reusing the pipeline buffers once the accumulator is final:
@@ -801,6 +803,47 @@ __global__ void __launch_bounds__(192, 1)
       // The previous tile's store has finished reading the staging buffer.
       if (a.epilogue != EPI_GROUPMAX && threadIdx.x == 64) bulk_wait_read0();
       epi_bar();
+      if (a.epilogue == EPI_SILU) {
+        // Rows 0..63 of the tile are gate rows, 64..127 the matching up rows (features mt*64 ..): both go
+        // to shared memory as bf16 (the reference's gate_proj / up_proj outputs), TMEM is handed back,
+        // then h = bf16(bf16(g * bf16(sigmoid(g))) * u) goes out as e5m2 (down_proj's input rounding).
+        __nv_bfloat16* sg = st;                 // [NTOK][64]
+        __nv_bfloat16* su = st + NTOK * 64;     // [NTOK][64]
+        __nv_bfloat16* dst = r < 64 ? sg : su;
+        for (int c = 0; c < NTOK; c += 16) {
+          if (n0 + c >= a.T) break;
+          float v[16];
+          tmem_ld16(taddr + c, v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) dst[(c + j) * 64 + (r & 63)] = __float2bfloat16_rn(v[j]);
+        }
+        tc_fence_before();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          if constexpr (PAIR) mbar_arrive_cluster(tmem_empty, crank & ~1u);
+          else mbar_arrive(tmem_empty);
+        }
+        const int ntv = min(NTOK, a.T - n0);
+        const int f0 = mt * 64;
+        if (m0 < a.F) {
+          // 8 features per thread and step: independent chains that pipeline through the SFU.
+          for (int idx = threadIdx.x - 64; idx < ntv * 8; idx += 128) {
+            const int t = idx >> 3, qd = (idx & 7) * 8;
+            const uint4 gw = *reinterpret_cast<const uint4*>(sg + t * 64 + qd);
+            const uint4 uw = *reinterpret_cast<const uint4*>(su + t * 64 + qd);
+            const __nv_bfloat16* gh = reinterpret_cast<const __nv_bfloat16*>(&gw);
+            const __nv_bfloat16* uh = reinterpret_cast<const __nv_bfloat16*>(&uw);
+            float h[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) h[e] = silu_mul_bf16(__bfloat162float(gh[e]), __bfloat162float(uh[e]));
+            uint2 o;
+            o.x = pack4_e5m2(h[0], h[1], h[2], h[3]);
+            o.y = pack4_e5m2(h[4], h[5], h[6], h[7]);
+            *reinterpret_cast<uint2*>(a.yq + static_cast<int64_t>(n0 + t) * a.ldq + f0 + qd) = o;
+          }
+        }
+        continue;
+      }
       for (int c = 0; c < NTOK; c += 16) {
         if (n0 + c >= a.T) break;
         float v[16];
@@ -1091,6 +1134,48 @@ extern "C" int q38_fp8_gemm_allreduce(const void* x, int64_t tokens, int64_t k, 
   void* y = c->base + c->off_x;
   return gemm_fp8(x, tokens, k, w, w_sf, features, EPI_ALLREDUCE, y, c->hidden, nullptr, 0, splits, nullptr, 0, &ar,
                   static_cast<cudaStream_t>(stream), "q38_fp8_gemm_allreduce");
+}
+
+extern "C" int q38_fp8_gemm_silu(const void* x, int64_t tokens, int64_t k, const void* w, const void* w_sf,
+                                 int64_t features, void* y, int64_t ldy, q38_stream_t stream) {
+  using namespace q38host;
+  int st = check_gemm_args(x, tokens, k, w, w_sf, features, 1, "q38_fp8_gemm_silu");
+  if (st != Q38_OK) return st;
+  if (!y) return set_error("q38_fp8_gemm_silu: null output"), Q38_ERR_ARG;
+  if (features % BM != 0 || ldy < features / 2 || ldy % 8 != 0 || (reinterpret_cast<uintptr_t>(y) & 7u) != 0)
+    return set_error("q38_fp8_gemm_silu: rows must be a multiple of 128 (64 gate + 64 up per tile), ldy >= rows / 2 "
+                     "and a multiple of 8, y 8-byte aligned"),
+           Q38_ERR_ARG;
+  const int ntok = token_tile(tokens);
+  GemmArgs a{};
+  a.w = static_cast<const uint8_t*>(w);
+  a.sf = static_cast<const uint8_t*>(w_sf);
+  a.T = static_cast<int>(tokens);
+  a.F = static_cast<int>(features);
+  a.nkc = static_cast<int>(cdiv(k, BK_BYTES));
+  a.splits = 1;
+  a.kc_per_split = a.nkc;
+  a.epilogue = EPI_SILU;
+  a.cluster = 1;
+  a.yq = static_cast<uint8_t*>(y);
+  a.ldq = ldy;
+  CUtensorMap tx;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (ntok == 256 && features > BM) {
+    st = encode_tmap_2d(&tx, x, tokens, k, 1, Cfg<256, true, true>::B_ROWS, BK_BYTES);
+    if (st != Q38_OK) return st;
+    CUtensorMap tw, tsf;
+    const int64_t tiles = cdiv(features, BM) * a.nkc;
+    st = encode_tmap_2d(&tw, w, tiles * BM, BK_BYTES, 1, BM, BK_BYTES, false);
+    if (st != Q38_OK) return st;
+    st = encode_tmap_2d(&tsf, w_sf, tiles * 32, 16, 1, 32, 16, false);
+    if (st != Q38_OK) return st;
+    return launch_persistent<256, true, true>(tx, tx, tw, tsf, a, s);
+  }
+  st = encode_tmap_2d(&tx, x, tokens, k, 1, ntok, BK_BYTES);
+  if (st != Q38_OK) return st;
+  return ntok == 256 ? launch_persistent<256, true, false>(tx, tx, tx, tx, a, s)
+                     : launch_persistent<128, true, false>(tx, tx, tx, tx, a, s);
 }
 
 extern "C" int q38_lm_head_groupmax(const void* x, int64_t rows, int64_t k, const void* w, int64_t vocab, int group,

@@ -78,12 +78,7 @@ __global__ void silu_mul_quant_kernel(const __nv_bfloat16* __restrict__ gu, int6
     u.u = *reinterpret_cast<const uint4*>(gu + row * ld + n + c * 8);
     float h[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float gf = __bfloat162float(g.h[k]);
-      const float s = bf16r(sigmoidf_(gf));
-      const float t = bf16r(__fmul_rn(gf, s));
-      h[k] = bf16r(__fmul_rn(t, __bfloat162float(u.h[k])));
-    }
+    for (int k = 0; k < 8; ++k) h[k] = silu_mul_bf16(__bfloat162float(g.h[k]), __bfloat162float(u.h[k]));
     uint2 o;
     o.x = pack4_e5m2(h[0], h[1], h[2], h[3]);
     o.y = pack4_e5m2(h[4], h[5], h[6], h[7]);

@@ -277,15 +277,26 @@ __device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__floa
 __device__ __forceinline__ uint8_t f32_to_e5m2(float x) {
   return static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E5M2));
 }
-// Pack four e5m2 bytes of four floats.
+// Pack four e5m2 bytes of four floats (a in the low byte), two conversions of a pair each.
 __device__ __forceinline__ uint32_t pack4_e5m2(float a, float b, float c, float d) {
-  return static_cast<uint32_t>(f32_to_e5m2(a)) | (static_cast<uint32_t>(f32_to_e5m2(b)) << 8) |
-         (static_cast<uint32_t>(f32_to_e5m2(c)) << 16) | (static_cast<uint32_t>(f32_to_e5m2(d)) << 24);
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E5M2);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E5M2);
+  return lo | (hi << 16);
 }
 
 // The logistic function in fp32. expf is CUDA's own; the result is rounded by the caller where the
 // reference rounds.
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+// The logistic function for the MLP's SiLU, branch-free so many elements pipeline: exp through
+// __expf (ex2.approx) and the reciprocal through __fdividef (rcp.approx). Its relative error is a few
+// fp32 ulps (2^-20 at |x| = 10), far below the bf16 rounding every caller applies next (2^-9), so it
+// changes bf16(sigmoid(x)) only for x within that error of a rounding boundary.
+__device__ __forceinline__ float sigmoid_mlp(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+// h = bf16(bf16(g * bf16(sigmoid(g))) * u): silu(gate) * up in the reference's bf16 steps.
+__device__ __forceinline__ float silu_mul_bf16(float g, float u) {
+  const float s = bf16r(sigmoid_mlp(g));
+  return bf16r(__fmul_rn(bf16r(__fmul_rn(g, s)), u));
+}
 // softplus with the threshold torch uses (beta 1, threshold 20).
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 

@@ -152,6 +152,18 @@ def fp8_gemm_allreduce(x_e5m2: torch.Tensor, lin: DeviceLinear, comm: Communicat
               lin.out_features, splits, comm.handle, _stream())
 
 
+def fp8_gemm_silu(x_e5m2: torch.Tensor, lin: DeviceLinear, y_e5m2: torch.Tensor) -> torch.Tensor:
+    """y = e5m2(SiLU(gate) * up) with `lin` the gate/up weight interleaved in 64-row blocks."""
+    _cuda(x_e5m2, y_e5m2)
+    _need(x_e5m2.dtype == U8 and x_e5m2.is_contiguous(), "x must be contiguous uint8 e5m2 [tokens, k]")
+    tokens, k = x_e5m2.shape
+    _need(k == lin.in_features, f"x has {k} columns, the weight {lin.in_features}")
+    _need(y_e5m2.dtype == U8 and y_e5m2.stride(1) == 1 and y_e5m2.shape[0] >= tokens, "y must be uint8 [tokens, >= out / 2]")
+    _lib.call("q38_fp8_gemm_silu", x_e5m2.data_ptr(), tokens, k, lin.q.data_ptr(), lin.sf.data_ptr(), lin.out_features,
+              y_e5m2.data_ptr(), y_e5m2.stride(0), _stream())
+    return y_e5m2
+
+
 def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, y_bf16: torch.Tensor | None = None,
                   y_e5m2: torch.Tensor | None = None) -> None:
     _cuda(x, w, y_bf16, y_e5m2)

@@ -145,8 +145,11 @@ class B200Step:
             )
         else:
             raise ValueError(cfg.layer_types[i])
+        # gate_proj and up_proj interleaved in 64-row blocks: the fused GEMM's epilogue finds each gate row's
+        # up row in the same 128-row tile and writes SiLU(gate) * up as down_proj's e5m2 input.
+        gate_up = ops.DeviceLinear(W.FP8Weight.interleave_rows(w[f"{p}.mlp.gate_proj"], w[f"{p}.mlp.up_proj"]), dev)
         return _Layer(cfg.layer_types[i], t("input_layernorm_weight"), t("post_attention_layernorm_weight"), mixer,
-                      lin("mlp.gate_proj", "mlp.up_proj"), lin("mlp.down_proj"))
+                      gate_up, lin("mlp.down_proj"))
 
     def _alloc_activations(self):
         self._fill_acts(self, self.batch)
@@ -179,7 +182,6 @@ class B200Step:
         a.ab = z(rows, 2 * hv)
         a.mix_gdn = z(rows, vd, dt=torch.uint8)
         a.mix_attn = z(rows, heads * cfg.head_dim, dt=torch.uint8)
-        a.gu = z(rows, 2 * inter)
         a.mlp_q = z(rows, inter, dt=torch.uint8)
         a.partial = z(rows, H) if tp > 1 and self.comm is None else None
         a.cos = z(rows, cfg.rotary_dim)
@@ -187,10 +189,10 @@ class B200Step:
         a.splits = {}
         need = 0
         for l in self.layers:
-            for lin in (l.mixer.out if l.kind == LINEAR else l.mixer.o, l.down, l.gate_up,
+            for lin in (l.mixer.out if l.kind == LINEAR else l.mixer.o, l.down,
                         l.mixer.qkvz if l.kind == LINEAR else l.mixer.qkv):
                 sp = ops.choose_splits(rows, lin.out_features, lin.in_features)
-                if self.comm is not None and lin is not l.gate_up and lin is not (l.mixer.qkvz if l.kind == LINEAR else l.mixer.qkv):
+                if self.comm is not None and lin is not (l.mixer.qkvz if l.kind == LINEAR else l.mixer.qkv):
                     sp = min(sp, 8)  # the fused all-reduce reduces K splits within one portable cluster
                 a.splits[id(lin)] = sp
                 need = max(need, ops.gemm_workspace_bytes(rows, lin.out_features, sp))
@@ -265,8 +267,7 @@ class B200Step:
                                  slot=slot, start=start, **heads)
             self._row_parallel(a, a.mix_attn, m.o)
         ops.rmsnorm_quant(a.x, l.ln_post, eps, y_e5m2=a.hq)
-        self._gemm(a, a.hq, l.gate_up, a.gu)
-        ops.silu_mul_quant(a.gu, cfg.intermediate_size // tp, a.mlp_q)
+        ops.fp8_gemm_silu(a.hq, l.gate_up, a.mlp_q)
         self._row_parallel(a, a.mlp_q, l.down)
 
     # ------------------------------------------------------------------ prefill
@@ -355,7 +356,7 @@ class B200Step:
         """Launches of this library's kernels in one decode step (for the bench's gpu_launches)."""
         n = 0
         for l in self.layers:
-            n += (6 if l.kind == LINEAR else 4) + 4  # GDN: rmsnorm, qkvz, ab, q/k prep, decode, out_proj
+            n += (6 if l.kind == LINEAR else 4) + 3  # GDN: rmsnorm, qkvz, ab, q/k prep, decode, out_proj; MLP: 3
         return n
 
     def decode_device(self):

@@ -53,6 +53,17 @@ class FP8Weight:
         return FP8Weight(torch.cat([p.q for p in parts]).contiguous(), torch.cat([p.scale for p in parts]).contiguous())
 
     @staticmethod
+    def interleave_rows(a: "FP8Weight", b: "FP8Weight", block: int = 64) -> "FP8Weight":
+        """Rows a[0:block], b[0:block], a[block:2 block], b[block:2 block], ...: the gate/up layout of the
+        fused MLP GEMM, whose 128-row tiles each hold matching gate and up rows."""
+        if a.shape != b.shape or a.shape[0] % block:
+            raise ValueError(f"interleave needs equal shapes with rows a multiple of {block}: {a.shape}, {b.shape}")
+        n = a.shape[0] // block
+        q = torch.stack((a.q.reshape(n, block, -1), b.q.reshape(n, block, -1)), 1).reshape(2 * a.shape[0], -1)
+        sc = torch.stack((a.scale.reshape(n, block, -1), b.scale.reshape(n, block, -1)), 1).reshape(2 * a.shape[0], -1)
+        return FP8Weight(q.contiguous(), sc.contiguous())
+
+    @staticmethod
     def from_float(w: torch.Tensor) -> "FP8Weight":
         q, s = codec.quantize_mx_e4m3(w)
         return FP8Weight(q, s)

@@ -170,6 +170,34 @@ def test_silu_mul_quant_matches_oracle(pkg, ops):
     assert_e5m2_close(y, om.silu(g) * u, frac=0.002, what="silu*up")
 
 
+@pytest.mark.parametrize("tokens,k,inter", [(8, 5120, 17408), (256, 5120, 17408), (37, 512, 256), (300, 1024, 640),
+                                             (512, 5120, 8704)])
+def test_fp8_gemm_silu_matches_oracle(pkg, ops, tokens, k, inter):
+    """The gate/up GEMM with SiLU(gate) * up fused into its epilogue (weights interleaved in 64-row
+    blocks) against (1) the unfused kernels on the same inputs, bit for bit, and (2) the oracle's
+    BF16 gate_proj / up_proj then silu(gate) * up, in e5m2 codes."""
+    gen = torch.Generator().manual_seed(tokens + inter)
+    gate = pkg.weights.FP8Weight.from_float(torch.randn(inter, k, generator=gen) * 0.03)
+    up = pkg.weights.FP8Weight.from_float(torch.randn(inter, k, generator=gen) * 0.03)
+    x = torch.randn(tokens, k, generator=gen).to(torch.bfloat16)
+    xq = pkg.codec.to_e5m2_bytes(x).to(DEV)
+    fused = ops.DeviceLinear(pkg.weights.FP8Weight.interleave_rows(gate, up), DEV)
+    y = torch.full((tokens, inter), 0x7F, dtype=torch.uint8, device=DEV)
+    ops.fp8_gemm_silu(xq, fused, y)
+    # Unfused: one GEMM over [gate; up] (single K split, the fused kernel's summation order), then silu*up.
+    plain = ops.DeviceLinear(pkg.weights.FP8Weight.cat_rows([gate, up]), DEV)
+    gu = torch.empty(tokens, 2 * inter, dtype=torch.bfloat16, device=DEV)
+    ops.fp8_gemm(xq, plain, gu, splits=1)
+    want = torch.empty_like(y)
+    ops.silu_mul_quant(gu, inter, want)
+    torch.cuda.synchronize()
+    assert torch.equal(y, want), f"fused vs unfused: {(y != want).sum().item()} of {y.numel()} bytes differ"
+    if tokens * k * inter <= 2e9:  # the oracle's CPU matmuls stay within seconds
+        xd = pkg.codec.e5m2_bytes_to_float(xq.cpu()).to(torch.bfloat16)
+        ref = om.silu(om.linear_of(gate)(xd)) * om.linear_of(up)(xd)
+        assert_e5m2_close(y, ref, frac=0.01, what=f"fused silu {tokens}x{k}x{inter}")
+
+
 @pytest.mark.parametrize("rows,k,n,splits", [(13, 5120, 96, 1), (256, 5120, 96, 40), (8, 128, 12, 2), (200, 640, 130, 3)])
 def test_bf16_linear_matches_float64(pkg, ops, rows, k, n, splits):
     gen = torch.Generator().manual_seed(8 + rows)
