@@ -509,6 +509,19 @@ def run_micro(args):
             ops.bf16_linear(x, lins[i % len(lins)], y, splits=splits, workspace=ws)
         per = n * k * 2 + B * k * 2 + B * n * 2
         unit, bound = "GB/s", "hbm"
+    if args.micro == "head":
+        # The lm_head group-of-32 maxima over the whole vocabulary (BF16 [vocab, 5120], one rank).
+        k, n = cfg.hidden_size, cfg.vocab_size // args.tp
+        lins = [ops.DeviceBF16Linear((torch.randn(n, k, device=dev, generator=gen) * 0.02).to(torch.bfloat16), dev)
+                for _ in range(min(args.copies, 2))]
+        x = bf(B, k)
+        maxima = torch.empty(B, n // 32, dtype=torch.float32, device=dev)
+
+        def launch(i):
+            ops.lm_head_groupmax(x, lins[i % len(lins)], maxima)
+        per = n * k * 2 + B * k * 2 + B * (n // 32) * 4
+        flops = 2 * B * n * k
+        unit, bound = "GB/s", "hbm"
     for i in range(args.warmup):
         launch(i)
     torch.cuda.synchronize()
@@ -597,7 +610,7 @@ def run_micro_allreduce(args, world, rank, local):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--micro", choices=["gdn", "gemm", "gemm_silu", "attn", "ab", "gdn_prefill", "attn_prefill", "verify", "gemm_ar"],
+    ap.add_argument("--micro", choices=["gdn", "gemm", "gemm_silu", "head", "attn", "ab", "gdn_prefill", "attn_prefill", "verify", "gemm_ar"],
                     help="time one kernel alone (profiling) instead of the step; gemm_ar: the fused all-reduce under torchrun")
     ap.add_argument("--copies", type=int, default=4, help="--micro: distinct weight/state copies cycled (defeat L2)")
     ap.add_argument("--tp", type=int, default=1, help="--micro gemm: K = 17408 / tp")

@@ -1178,37 +1178,6 @@ extern "C" int q38_fp8_gemm_silu(const void* x, int64_t tokens, int64_t k, const
                      : launch_persistent<128, true, false>(tx, tx, tx, tx, a, s);
 }
 
-extern "C" int q38_lm_head_groupmax(const void* x, int64_t rows, int64_t k, const void* w, int64_t vocab, int group,
-                                    float* maxima, int64_t ld_max, q38_stream_t stream) {
-  using namespace q38host;
-  if (!x || !w || !maxima) return set_error("q38_lm_head_groupmax: null pointer"), Q38_ERR_ARG;
-  if (group != 32) return set_error("q38_lm_head_groupmax: group must be 32, got %d", group), Q38_ERR_ARG;
-  if (rows <= 0 || k <= 0 || vocab <= 0 || vocab % 32 != 0 || k % 8 != 0 || rows > (1 << 24) || vocab > (1 << 30))
-    return set_error("q38_lm_head_groupmax: bad sizes rows=%lld k=%lld vocab=%lld", (long long)rows, (long long)k,
-                     (long long)vocab),
-           Q38_ERR_ARG;
-  if (!aligned16(x) || !aligned16(w)) return set_error("q38_lm_head_groupmax: x and w must be 16-byte aligned"), Q38_ERR_ARG;
-  if (ld_max < vocab / 32) return set_error("q38_lm_head_groupmax: ld_max too small"), Q38_ERR_ARG;
-  const int ntok = token_tile(rows);
-  GemmArgs a{};
-  a.w = static_cast<const uint8_t*>(w);
-  a.T = static_cast<int>(rows);
-  a.F = static_cast<int>(vocab);
-  a.nkc = static_cast<int>(cdiv(k, BK_BYTES / 2));
-  a.splits = 1;
-  a.kc_per_split = a.nkc;
-  a.epilogue = EPI_GROUPMAX;
-  a.maxima = maxima;
-  a.ldm = ld_max;
-  a.cluster = 1;
-  CUtensorMap tx;
-  int st = encode_tmap_2d(&tx, x, rows, k, 2, ntok, BK_BYTES / 2);
-  if (st != Q38_OK) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return ntok == 256 ? launch_persistent<256, false, false>(tx, tx, tx, tx, a, s)
-                     : launch_persistent<128, false, false>(tx, tx, tx, tx, a, s);
-}
-
 extern "C" int q38_bf16_linear(const void* x, int64_t ldx, int64_t rows, int64_t k, const void* w, int64_t n_out,
                                void* y, int64_t ldy, int splits, void* workspace, size_t workspace_bytes,
                                q38_stream_t stream) {

@@ -288,13 +288,16 @@ def test_attn_decode_matches_oracle(pkg, ops, shape, batch, max_seq):
     assert torch.equal(d_v.cpu(), layer.v_cache)
 
 
-def test_lm_head_groupmax_matches_oracle(pkg, ops):
+@pytest.mark.parametrize("rows,vocab", [(11, 4096), (64, 4224), (100, 3104), (256, 4096), (300, 4224), (256, 8192 + 96)])
+def test_lm_head_groupmax_matches_oracle(pkg, ops, rows, vocab):
+    """Group-of-32 maxima of the logits against float64: batch tiles of 64/128/256 and several of
+    them (300 rows), an odd count of 128-row weight tiles (4224) and a partial last tile (3104)."""
     cfg = pkg.config.full_config(1)
-    gen = torch.Generator().manual_seed(14)
-    vocab, h, rows = 4096, cfg.hidden_size, 11
+    gen = torch.Generator().manual_seed(14 + rows + vocab)
+    h = cfg.hidden_size
     w = pkg.weights.FP8Weight.from_float(torch.randn(vocab, h, generator=gen) * 0.02)
     x = torch.randn(rows, h, generator=gen).to(torch.bfloat16)
-    maxima = torch.empty(rows, vocab // 32, device=DEV)
+    maxima = torch.full((rows, vocab // 32), float("nan"), device=DEV)  # every entry must be written
     ops.lm_head_groupmax(x.to(DEV), ops.DeviceBF16Linear(w.dequant().to(torch.bfloat16), DEV), maxima)
     torch.cuda.synchronize()
     logits = x.double() @ w.dequant().double().T
