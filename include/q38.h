@@ -274,10 +274,13 @@ int q38_comm_destroy(q38_comm_t comm);
 
 /*
  * x += all_reduce(bf16(e5m2(x_q) @ W^T)) over the communicator's ranks, in one kernel per rank: each
- * 32-token x 128-feature output block has an owner rank; the other ranks store their bf16 partial
- * into the owner's receive slot over NVLink, the owner sums the partials in rank order (fp32, one
- * bf16 rounding), adds the residual (bf16) and stores the result into every rank's x. Every rank makes
- * the same sequence of calls. x is the communicator's residual stream (rows 0 .. tokens - 1), so
+ * output tile has an owner rank; every rank pushes its bf16 partial of the tile into the owner's
+ * `part` slot over NVLink as 64-bit words {two bf16, the call's epoch}, so a word's arrival is its own
+ * ready flag (no fences, no separate flags). The owner polls its slots, sums the partials in rank
+ * order (fp32, one bf16 rounding), adds the residual (bf16) and pushes the new rows the same way into
+ * every rank's `result` slot, from which each rank writes its own x. The epoch advances on the device
+ * (last CTA of the call), and slots alternate by epoch parity, so calls replay inside CUDA graphs.
+ * Every rank makes the same sequence of calls. x is the communicator's residual stream (rows 0 .. tokens - 1), so
  * features == hidden. Replaces the row-parallel projection plus all-reduce of o_proj / out_proj /
  * down_proj (qwen38_inf2/model.py:259, :374, :639 with the NxD reduce, neuron.py:9). Needs the whole
  * grid resident (returns Q38_ERR_UNSUPPORTED otherwise) and at most 8 K splits; a wait on a peer that

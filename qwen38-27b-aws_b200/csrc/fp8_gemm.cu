@@ -1,4 +1,4 @@
-// Tensor-core GEMMs for sm_100a: the FP8 linear layers and the lm_head group-of-32 maxima.
+// Tensor-core GEMMs for sm_100a: the FP8 linear layers (and their fused epilogues) and the BF16 linear.
 //
 // Layout ("swap AB"): the weight matrix W [features, K] is the MMA's A operand (M = 128 features
 // per tile) and the activations X [tokens, K] are its B operand (N = 128 or 256 tokens per tile),
@@ -18,7 +18,7 @@
 //
 // FP8 path: tcgen05.mma kind::mxf8f6f4.block_scale, A = e4m3 weights with UE8M0 scales per 32 K
 // (exact dequantisation: the reference's weights are e4m3 * 2^s), B = e5m2 activations with scale
-// 1.0. BF16 path (lm_head): kind::f16 with BF16 A and B.
+// 1.0. BF16 path (in_proj_b/a): kind::f16 with BF16 A and B. The lm_head has its own kernel (lm_head.cu).
 //
 // Split K: with splits > 1 each CTA stores its fp32 partial tile in the workspace; the last CTA of
 // a tile (by an atomic counter) sums the partials in split order 0..S-1, so results do not depend
@@ -38,7 +38,7 @@ constexpr int BM = 128;          // features per tile (MMA M)
 constexpr int BK_BYTES = 128;    // K bytes per pipeline stage (one 128-byte swizzle row)
 constexpr int SF_BLOCK = 512;    // scale bytes per (128 rows, 128 K) block
 
-enum : int { EPI_BF16 = 0, EPI_RESIDUAL = 1, EPI_GROUPMAX = 2, EPI_ALLREDUCE = 3, EPI_SILU = 4 };
+enum : int { EPI_BF16 = 0, EPI_RESIDUAL = 1, EPI_ALLREDUCE = 3, EPI_SILU = 4 };
 
 // PAIR: the 2-SM form. A cluster pair of CTAs computes 256 weight rows x NTOK tokens with
 // tcgen05.mma.cta_group::2 issued by the even CTA; each CTA loads its own 128 weight rows and half of
@@ -68,8 +68,6 @@ struct GemmArgs {
   int64_t ldy;
   const __nv_bfloat16* res;
   int64_t ldr;
-  float* maxima;  // group maxima [T, ldm] (EPI_GROUPMAX)
-  int64_t ldm;
   float* ws;              // split partials (workspace mode)
   unsigned int* counters; // one per output tile (workspace mode)
   int cluster;            // > 0: epilogue through shared memory, the `cluster` K splits of a tile
@@ -130,21 +128,8 @@ __device__ __forceinline__ bool poll_words2(const unsigned long long* p, uint32_
   return true;
 }
 
-// Applies the epilogue to 16 consecutive tokens of one feature row.
+// Applies the bf16 (or bf16 + residual) epilogue to 16 consecutive tokens of one feature row.
 __device__ __forceinline__ void epilogue16(const GemmArgs& a, int row, int t0, const float (&v)[16], int lane) {
-  if (a.epilogue == EPI_GROUPMAX) {
-    // The warp's 32 lanes are 32 consecutive vocab rows: one group (F is a multiple of 32, so a
-    // group is either wholly inside or wholly past the vocabulary).
-    if ((row & ~31) >= a.F) return;
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      float m = row < a.F ? v[j] : -INFINITY;
-      m = warp_max(m);
-      const int t = t0 + j;
-      if (lane == 0 && t < a.T) a.maxima[static_cast<int64_t>(t) * a.ldm + (row >> 5)] = m;
-    }
-    return;
-  }
   if (row >= a.F) return;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
@@ -309,8 +294,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else if (a.cluster > 0) {
-    // Epilogue part 1. With one split the accumulator goes straight to its bf16 staging (or to the
-    // group maxima); with a cluster of splits it goes to shared memory as fp32 [token][row] for part
+    // Epilogue part 1. With one split the accumulator goes straight to its bf16 staging; with a cluster of splits it goes to shared memory as fp32 [token][row] for part
     // 2. The residual tile of this CTA's token slice starts loading by TMA meanwhile.
     const int q = warp & 3;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
@@ -340,13 +324,6 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld16(taddr + c, v);
 #pragma unroll
           for (int j = 0; j < 16; ++j) part[(c + j) * BM + r] = v[j];
-        }
-      } else if (a.epilogue == EPI_GROUPMAX) {
-        for (int c = 0; c < NTOK; c += 16) {
-          if (n0 + c >= a.T) break;
-          float v[16];
-          tmem_ld16(taddr + c, v);
-          epilogue16(a, m0 + r, n0 + c, v, lane);
         }
       } else if (m0 < a.F) {
         // Lanes are consecutive rows: a warp's stores of one token fill 64 contiguous bytes.
@@ -475,16 +452,6 @@ __global__ void __launch_bounds__(192, 1)
             const int t = tb + NW * u;
             if (t >= t1) break;
             const float v[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
-            if (a.epilogue == EPI_GROUPMAX) {
-              // 8 lanes hold one group of 32 vocab rows; groups past the vocabulary are skipped.
-              float m = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
-              m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-              m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-              m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
-              const int f = m0 + 4 * lane;
-              if ((lane & 7) == 0 && f < a.F) a.maxima[static_cast<int64_t>(t) * a.ldm + (f >> 5)] = m;
-              continue;
-            }
             __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(stage) + (t - n0) * BM + 4 * lane;
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
@@ -497,7 +464,7 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     // The staged bf16 slice goes out by TMA (boxes past the last token or feature are clipped).
-    if (warp >= 2 && a.epilogue != EPI_GROUPMAX && a.epilogue != EPI_ALLREDUCE) {
+    if (warp >= 2 && a.epilogue != EPI_ALLREDUCE) {
       fence_proxy_async_shared();
       epi_bar();
       if (warp == 2 && lane == 0 && !flags[0] && live) {
@@ -603,7 +570,7 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------------------------
-// Persistent form for unsplit GEMMs (EPI_BF16, EPI_GROUPMAX): each CTA (or 2-SM pair) walks output
+// Persistent form for unsplit GEMMs (EPI_BF16, EPI_SILU): each CTA (or 2-SM pair) walks output
 // tiles. The producer's stage ring runs on across tiles; the MMA warp waits for "TMEM empty" before a
 // tile's first MMA; the epilogue warps drain the accumulator into their own staging buffer, release
 // TMEM at once, and store while the next tile's mainloop runs. Per-CTA setup and the pipeline fill
@@ -801,7 +768,7 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_after();
       // The previous tile's store has finished reading the staging buffer.
-      if (a.epilogue != EPI_GROUPMAX && threadIdx.x == 64) bulk_wait_read0();
+      if (threadIdx.x == 64) bulk_wait_read0();
       epi_bar();
       if (a.epilogue == EPI_SILU) {
         // Rows 0..63 of the tile are gate rows, 64..127 the matching up rows (features mt*64 ..): both go
@@ -848,12 +815,8 @@ __global__ void __launch_bounds__(192, 1)
         if (n0 + c >= a.T) break;
         float v[16];
         tmem_ld16(taddr + c, v);
-        if (a.epilogue == EPI_GROUPMAX) {
-          epilogue16(a, m0 + r, n0 + c, v, lane);
-        } else {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) st[(c + j) * BM + r] = __float2bfloat16_rn(v[j]);
-        }
+        for (int j = 0; j < 16; ++j) st[(c + j) * BM + r] = __float2bfloat16_rn(v[j]);
       }
       // Every TMEM read of this tile is complete: hand the accumulator back to the MMA warp.
       tc_fence_before();
@@ -862,14 +825,12 @@ __global__ void __launch_bounds__(192, 1)
         if constexpr (PAIR) mbar_arrive_cluster(tmem_empty, crank & ~1u);
         else mbar_arrive(tmem_empty);
       }
-      if (a.epilogue != EPI_GROUPMAX) {
-        fence_proxy_async_shared();
-        epi_bar();
-        if (threadIdx.x == 64 && m0 < a.F) {
-          for (int b = 0; b < NTOK / TOK_BLOCK; ++b)
-            if (n0 + b * TOK_BLOCK < a.T) tma_store_2d(&tmap_y, sOut + b * TOK_BLOCK * BM * 2, m0, n0 + b * TOK_BLOCK);
-          bulk_commit();
-        }
+      fence_proxy_async_shared();
+      epi_bar();
+      if (threadIdx.x == 64 && m0 < a.F) {
+        for (int b = 0; b < NTOK / TOK_BLOCK; ++b)
+          if (n0 + b * TOK_BLOCK < a.T) tma_store_2d(&tmap_y, sOut + b * TOK_BLOCK * BM * 2, m0, n0 + b * TOK_BLOCK);
+        bulk_commit();
       }
     }
     if (threadIdx.x == 64) bulk_wait_read0();

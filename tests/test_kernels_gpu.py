@@ -45,6 +45,19 @@ def assert_gemm_close(got, exact, magnitude, what=""):
     assert beyond <= max(8, 5e-3 * err.numel()), f"{what}: {beyond} of {err.numel()} elements beyond 1 ulp"
 
 
+def assert_attention_e5m2_close(got_bytes, want_bf16, what=""):
+    """Attention outputs in e5m2: at most 2% of codes differ, 0.1% by more than one code, and every
+    row within 2e-2 relative L2 of the oracle."""
+    want_codes = want_bf16.float().to(torch.float8_e5m2).view(torch.uint8)
+    d = (e5m2_code(got_bytes) - e5m2_code(want_codes)).abs()
+    differ, far = (d > 0).float().mean().item(), (d > 1).float().mean().item()
+    got = got_bytes.view(torch.float8_e5m2).float()
+    want = want_codes.view(torch.float8_e5m2).float()
+    rel = ((got - want).norm(dim=-1) / want.norm(dim=-1).clamp_min(1e-12)).max().item()
+    msg = f"{what}: {differ:.4f} of codes differ, {far:.5f} by more than one, worst row relative L2 {rel:.3g}"
+    assert differ <= 0.02 and far <= 1e-3 and rel <= 2e-2, msg
+
+
 def e5m2_code(b: torch.Tensor) -> torch.Tensor:
     b = b.to(torch.int32)
     mag = b & 0x7F
@@ -257,8 +270,11 @@ def test_gdn_decode_matches_oracle(pkg, ops, shape, batch):
     assert torch.equal(d_conv.cpu(), layer.conv_state)
 
 
-@pytest.mark.parametrize("shape,batch,max_seq", [("tiny", 4, 64), ("full", 9, 512)])
+@pytest.mark.parametrize("shape,batch,max_seq", [("tiny", 4, 64), ("full", 9, 512), ("full", 40, 512), ("tiny", 12, 200)])
 def test_attn_decode_matches_oracle(pkg, ops, shape, batch, max_seq):
+    """Against the oracle's decode, rows at positions on and around the 64- and 128-position chunk
+    edges, the last position and inactive rows; a second call gives the same bytes (the kernels'
+    chunk counters are back at zero)."""
     cfg = pkg.config.tiny_config(1) if shape == "tiny" else pkg.config.full_config(1)
     gen = torch.Generator().manual_seed(13)
     w = pkg.weights.synthetic_layer(cfg, 3, seed=11, device="cpu", std=0.1)
@@ -270,7 +286,9 @@ def test_attn_decode_matches_oracle(pkg, ops, shape, batch, max_seq):
     k = torch.randn(batch, 1, kvh * hd, generator=gen).to(torch.bfloat16)
     v = torch.randn(batch, 1, kvh * hd, generator=gen).to(torch.bfloat16)
     position = torch.randint(1, max_seq - 1, (batch,), generator=gen, dtype=torch.int32)
-    position[0] = 0
+    edges = torch.tensor([0, 63, 64, 65, 127, 128, 129, 255, 256, max_seq - 2, max_seq - 1], dtype=torch.int32)
+    edges = edges[edges < max_seq][: batch - 1]
+    position[: edges.numel()] = edges
     active = torch.ones(batch)
     active[-1] = 0.0
     cos, sin = om.rotary(cfg, position, torch.bfloat16)
@@ -281,9 +299,17 @@ def test_attn_decode_matches_oracle(pkg, ops, shape, batch, max_seq):
                     cos.to(DEV), sin.to(DEV), d_k, d_v, position.to(DEV), active.to(DEV), out, batch=batch,
                     num_q_heads=heads, num_kv_heads=kvh, head_dim=hd, rot_dim=cfg.rotary_dim, eps=cfg.rms_norm_eps)
     torch.cuda.synchronize()
+    out2 = torch.empty_like(out)
+    ops.attn_decode(torch.cat((qg, k, v), -1).reshape(batch, -1).to(DEV), layer.q_norm.to(DEV), layer.k_norm.to(DEV),
+                    cos.to(DEV), sin.to(DEV), d_k, d_v, position.to(DEV), active.to(DEV), out2, batch=batch,
+                    num_q_heads=heads, num_kv_heads=kvh, head_dim=hd, rot_dim=cfg.rotary_dim, eps=cfg.rms_norm_eps)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2), "a repeated call must give the same bytes"
     want = layer.decode_core(qg, k, v, cos.unsqueeze(1), sin.unsqueeze(1), position, active).reshape(batch, -1)
     on = active > 0.5
-    assert_e5m2_close(out.cpu()[on], want[on], what="attention out")
+    # fp32 summation order differs from the oracle's matmul: where W V nearly cancels the own value's
+    # term the small result can move by more than one e5m2 code (rare, bounded in L2).
+    assert_attention_e5m2_close(out.cpu()[on], want[on], what="attention out")
     assert_bf16_close(d_k.cpu(), layer.k_cache, frac=0.001, what="k cache")
     assert torch.equal(d_v.cpu(), layer.v_cache)
 

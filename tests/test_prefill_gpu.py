@@ -22,7 +22,7 @@ import torch
 from safetensors import safe_open
 
 from oracle import cpu_model as om
-from tests.test_kernels_gpu import assert_bf16_close, assert_e5m2_close, e5m2_code
+from tests.test_kernels_gpu import assert_attention_e5m2_close, assert_bf16_close, assert_e5m2_close, e5m2_code
 from tests.test_step_gpu import assert_hidden_close
 
 pytestmark = pytest.mark.gpu
@@ -38,17 +38,6 @@ def ops(pkg):
 @pytest.fixture(scope="module")
 def step_mod(pkg):
     return __import__(pkg.__name__ + ".step", fromlist=["step"])
-
-
-def assert_attention_e5m2_close(got_bytes, want_bf16, what=""):
-    want_codes = want_bf16.float().to(torch.float8_e5m2).view(torch.uint8)
-    d = (e5m2_code(got_bytes) - e5m2_code(want_codes)).abs()
-    differ, far = (d > 0).float().mean().item(), (d > 1).float().mean().item()
-    got = got_bytes.view(torch.float8_e5m2).float()
-    want = want_codes.view(torch.float8_e5m2).float()
-    rel = ((got - want).norm(dim=-1) / want.norm(dim=-1).clamp_min(1e-12)).max().item()
-    msg = f"{what}: {differ:.4f} of codes differ, {far:.5f} by more than one, worst token relative L2 {rel:.3g}"
-    assert differ <= 0.02 and far <= 1e-3 and rel <= 2e-2, msg
 
 
 def _scalar(v):
