@@ -3,10 +3,17 @@
 //
 // One CTA per (row, KV head) with its G query heads. The reference computes the scores as a BF16
 // matmul (fp32 sums rounded to bf16), a fp32 softmax over cache positions < position plus the
-// token's own key, weights rounded to bf16, and the output as a BF16 matmul plus the own value's
-// bf16 term. This kernel keeps those rounding points, so it takes two passes: scores for every
-// visible position into shared memory (K streamed once), then the normalised weights against V
-// (V streamed once). It is HBM-bound on the cache: position * head_dim * 4 bytes per (row, KV head).
+// token's own key, weights rounded to bf16 after normalisation, and the output as a BF16 matmul plus
+// the own value's bf16 term. This kernel keeps those rounding points, so it takes two passes: scores
+// for every visible position into shared memory (K streamed once), then the normalised weights
+// against V (V streamed once).
+//
+// It is HBM-bound on the cache (position * head_dim * 4 bytes per (row, KV head)), so the CTA is
+// built around the copy stream: a copy warp keeps a ring of 5 tiles of 32 positions in flight (one
+// bulk copy per 512-byte row, into rows padded for conflict-free ldmatrix), K tiles then V tiles,
+// handed over through full / empty mbarriers, so it runs ahead into V while the four compute warps
+// finish the softmax; the compute warps multiply on mma.sync (BF16, fp32 accumulate) and never wait
+// on a CTA-wide barrier per tile. Two CTAs per SM.
 #include "attn_common.cuh"
 
 namespace {
@@ -33,40 +40,81 @@ struct AttnArgs {
   float eps;
 };
 
-constexpr int kWarps = 4;
-constexpr int KT = 32;     // cache positions per tile
-constexpr int STAGES = 4;  // tiles in flight
-constexpr int MROWS = 16;  // the MMA's M: query heads, padded
+constexpr int kComputeWarps = 4;
+constexpr int kThreads = (kComputeWarps + 1) * 32;  // compute warps + one copy warp
+constexpr int KT = 32;                               // cache positions per tile
+constexpr int STAGES = 5;                            // tiles in flight per CTA
+constexpr int MROWS = 16;                            // the MMA's M: query heads, padded by a zero row
 
-template <int HD>
-struct AttnSmem {
-  static constexpr int ROWP = HD + 8;  // padded row (bf16): ldmatrix rows land in distinct banks
-  static constexpr int NPAD = 8;       // extra weight columns past max_seq
-  static size_t bytes(int groups, int64_t max_seq) {
-    const size_t wcols = static_cast<size_t>((max_seq + KT - 1) / KT * KT + NPAD);
-    return 2 * (static_cast<size_t>(MROWS) * ROWP   // q (bf16)
-                + STAGES * static_cast<size_t>(KT) * ROWP  // K / V tile ring
-                + MROWS * wcols)                      // scores, then weights (bf16)
-           + sizeof(float) * (static_cast<size_t>(groups) * HD + 2 * HD + 2 * kMaxGroups);
+__host__ __device__ constexpr size_t al16(size_t x) { return (x + 15) & ~size_t(15); }
+
+// Shared memory of one CTA (byte offsets; the same arithmetic on host and device).
+struct DecLayout {
+  int rowp;      // padded K / V / q row (bf16): ldmatrix rows land in distinct banks
+  int wcols;     // score / weight row length (bf16)
+  size_t ring;   // [STAGES][KT][rowp] bf16   K tiles, then V tiles
+  size_t q;      // [groups][rowp] bf16      queries after norm + rotary
+  size_t sc;     // [groups][wcols] bf16     scores, then weights in place
+  size_t qf;     // [groups][hd] fp32        query staging
+  size_t kown;   // [hd] fp32                own key staging
+  size_t prm;    // [4][hd] bf16             q / k norm weights, cos, sin
+  size_t zero;   // 16 zero bytes: the MMA rows past the group
+  size_t bars;   // full[STAGES], empty[STAGES]
+  size_t stats;  // [kMaxGroups] fp32 own scores, then own weights
+  size_t total;
+  __host__ __device__ DecLayout(int hd, int groups, int64_t max_seq) {
+    rowp = hd + 8;
+    wcols = static_cast<int>((max_seq + KT - 1) / KT * KT) + 8;
+    size_t off = 0;
+    ring = off;
+    off = al16(off + static_cast<size_t>(STAGES) * KT * rowp * 2);
+    q = off;
+    off = al16(off + static_cast<size_t>(groups) * rowp * 2);
+    sc = off;
+    off = al16(off + static_cast<size_t>(groups) * wcols * 2);
+    qf = off;
+    off = al16(off + static_cast<size_t>(groups) * hd * 4);
+    kown = off;
+    off = al16(off + static_cast<size_t>(hd) * 4);
+    prm = off;
+    off = al16(off + static_cast<size_t>(4) * hd * 2);
+    zero = off;
+    off += 16;
+    bars = off;
+    off += 2 * STAGES * 8;
+    stats = off;
+    off = al16(off + kMaxGroups * 4);
+    total = off;
   }
 };
 
+// Barrier among the compute warps only (the copy warp runs on its own).
+__device__ __forceinline__ void compute_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32) : "memory");
+}
+
 template <int HD>
-__global__ void __launch_bounds__(kWarps * 32) attn_decode_kernel(AttnArgs a) {
-  using S = AttnSmem<HD>;
-  constexpr int ROWP = S::ROWP;
-  constexpr int KSTEPS = HD / 16;          // MMA k-steps over head_dim
-  constexpr int NT2 = HD / 8 / kWarps;     // pass-2 n-tiles (8 dims) per warp
+__global__ void __launch_bounds__(kThreads) attn_decode_kernel(AttnArgs a) {
+  constexpr int KSTEPS = HD / 16;                  // MMA k-steps over head_dim
+  constexpr int NT2 = HD / 8 / kComputeWarps;      // pass-2 n-tiles (8 dims) per warp
+  static_assert(KT == 8 * kComputeWarps, "one 8-position n-tile per compute warp in pass 1");
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const int G = a.groups;
-  const int wcols = static_cast<int>((a.max_seq + KT - 1) / KT * KT) + S::NPAD;
-  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem_raw);       // [16][ROWP]
-  __nv_bfloat16* ring = qs + MROWS * ROWP;                               // [STAGES][KT][ROWP]
-  __nv_bfloat16* wb = ring + STAGES * KT * ROWP;                         // [16][wcols]
-  float* qf = reinterpret_cast<float*>(wb + MROWS * wcols);             // [G][HD]
-  float* kown = qf + G * HD;                                             // [HD]
-  float* vown = kown + HD;                                               // [HD]
-  float* hs = vown + HD;                                                 // [2][kMaxGroups]
+  const DecLayout L(HD, G, a.max_seq);
+  const int ROWP = L.rowp, wcols = L.wcols;
+  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.ring);
+  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.q);
+  __nv_bfloat16* sc = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.sc);
+  float* qf = reinterpret_cast<float*>(smem_raw + L.qf);
+  float* kown = reinterpret_cast<float*>(smem_raw + L.kown);
+  __nv_bfloat16* wq = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.prm);
+  __nv_bfloat16* wk = wq + HD;
+  __nv_bfloat16* cs = wk + HD;
+  __nv_bfloat16* sn = cs + HD;
+  uint32_t* zero = reinterpret_cast<uint32_t*>(smem_raw + L.zero);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + L.bars);
+  uint64_t* empty = full + STAGES;
+  float* stats = reinterpret_cast<float*>(smem_raw + L.stats);
 
   const int g = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -75,151 +123,168 @@ __global__ void __launch_bounds__(kWarps * 32) attn_decode_kernel(AttnArgs a) {
   const int64_t pos64 = pos < 0 ? 0 : pos;
   const int n_read = on ? static_cast<int>(pos64 < a.max_seq ? pos64 : a.max_seq) : 0;
   const int64_t where = on ? (pos64 < a.max_seq - 1 ? pos64 : a.max_seq - 1) : a.max_seq - 1;
-  const __nv_bfloat16* row = a.qkv + b * a.ld_qkv;
-  const int qh0 = g * G;
-  const __nv_bfloat16* kc = a.k_cache + (static_cast<int64_t>(b) * a.num_kv_heads + g) * a.max_seq * HD;
-  const __nv_bfloat16* vc = a.v_cache + (static_cast<int64_t>(b) * a.num_kv_heads + g) * a.max_seq * HD;
   const int ntiles = (n_read + KT - 1) / KT;
+  const int64_t head_row = static_cast<int64_t>(b) * a.num_kv_heads + g;
+  const __nv_bfloat16* kc = a.k_cache + head_row * a.max_seq * HD;
+  const __nv_bfloat16* vc = a.v_cache + head_row * a.max_seq * HD;
 
-  // Tile i of the stream: K tiles 0 .. ntiles-1, then V tiles. Rows past n_read are zero-filled.
-  auto load_tile = [&](int i) {
-    const bool is_v = i >= ntiles;
-    const int p0 = (is_v ? i - ntiles : i) * KT;
-    const __nv_bfloat16* src = is_v ? vc : kc;
-    __nv_bfloat16* dst = ring + (i % STAGES) * KT * ROWP;
-    for (int c = tid; c < KT * (HD / 8); c += kWarps * 32) {
-      const int r = c / (HD / 8), cc = c % (HD / 8);
-      const int p = p0 + r;
-      const bool ok = p < n_read;
-      cp_async16(smem_u32(dst + r * ROWP + cc * 8), src + static_cast<int64_t>(ok ? p : 0) * HD + cc * 8, ok ? 16u : 0u);
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kComputeWarps);
     }
-    cp_async_commit();
-  };
-  for (int i = 0; i < STAGES - 1; ++i) {
-    if (i < 2 * ntiles) load_tile(i);
-    else cp_async_commit();  // empty groups keep the wait counts uniform
+    fence_mbar_init();
+  }
+  if (tid < 4) zero[tid] = 0u;
+  __syncthreads();
+
+  if (warp == kComputeWarps) {
+    // Copy warp: K tiles 0 .. ntiles-1, then V tiles, one bulk copy per 512-byte row into the padded
+    // ring. A V tile's rows past n_read are zeroed (their weights are zero; 0 x stale data could be NaN).
+    for (int i = 0; i < 2 * ntiles; ++i) {
+      const int s = i % STAGES;
+      if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) break;
+      const bool is_v = i >= ntiles;
+      const int p0 = (is_v ? i - ntiles : i) * KT;
+      const int rows = min(KT, n_read - p0);
+      __nv_bfloat16* dst = ring + s * KT * ROWP;
+      if (is_v)
+        for (int c = lane; c < (KT - rows) * (HD / 8); c += 32)
+          *reinterpret_cast<uint4*>(dst + (rows + c / (HD / 8)) * ROWP + (c % (HD / 8)) * 8) = make_uint4(0u, 0u, 0u, 0u);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rows * HD * 2));
+      __syncwarp();
+      const __nv_bfloat16* src = (is_v ? vc : kc) + static_cast<int64_t>(p0) * HD;
+      for (int r = lane; r < rows; r += 32) bulk_load(dst + r * ROWP, src + static_cast<int64_t>(r) * HD, HD * 2, &full[s]);
+    }
+    return;
   }
 
-  // Stage the raw query heads, own key and value; norm + rotary; queries to bf16 MMA rows.
-  for (int i = tid; i < G * HD; i += kWarps * 32) {
+  // ---- compute warps: the queries and the own key (norm + rotary), staged in one round trip.
+  const __nv_bfloat16* row = a.qkv + b * a.ld_qkv;
+  const int qh0 = g * G;
+  for (int i = tid; i < G * HD; i += kComputeWarps * 32) {
     const int h = i / HD, d = i % HD;
     qf[i] = __bfloat162float(row[static_cast<int64_t>(qh0 + h) * 2 * HD + d]);
   }
   const __nv_bfloat16* kraw = row + static_cast<int64_t>(a.num_q_heads) * 2 * HD + static_cast<int64_t>(g) * HD;
   const __nv_bfloat16* vraw = kraw + static_cast<int64_t>(a.num_kv_heads) * HD;
-  for (int d = tid; d < HD; d += kWarps * 32) {
+  for (int d = tid; d < HD; d += kComputeWarps * 32) {
     kown[d] = __bfloat162float(kraw[d]);
-    vown[d] = __bfloat162float(vraw[d]);
+    wq[d] = a.q_norm_w[d];
+    wk[d] = a.k_norm_w[d];
+    if (d < a.rot) {
+      cs[d] = a.cos[b * a.rot + d];
+      sn[d] = a.sin[b * a.rot + d];
+    }
   }
-  __syncthreads();
-  const __nv_bfloat16* cs = a.cos + b * a.rot;
-  const __nv_bfloat16* sn = a.sin + b * a.rot;
-  for (int h = warp; h <= G; h += kWarps) {
-    if (h < G) norm_rope_head<HD>(qf + h * HD, a.q_norm_w, cs, sn, a.rot, a.eps, lane);
-    else norm_rope_head<HD>(kown, a.k_norm_w, cs, sn, a.rot, a.eps, lane);
+  // Weights past n_read in the last tile are zero.
+  for (int i = tid; i < G * KT; i += kComputeWarps * 32) {
+    const int h = i / KT, p = n_read + i % KT;
+    if (p < ntiles * KT) sc[h * wcols + p] = __float2bfloat16_rn(0.f);
   }
-  __syncthreads();
-  for (int i = tid; i < MROWS * HD; i += kWarps * 32) {
-    const int h = i / HD, d = i % HD;
-    qs[h * ROWP + d] = __float2bfloat16_rn(h < G ? qf[i] : 0.f);
+  compute_bar();
+  for (int h = warp; h <= G; h += kComputeWarps) {
+    if (h < G) norm_rope_head<HD>(qf + h * HD, wq, cs, sn, a.rot, a.eps, lane);
+    else norm_rope_head<HD>(kown, wk, cs, sn, a.rot, a.eps, lane);
   }
-  for (int i = tid; i < MROWS * wcols; i += kWarps * 32) wb[i] = __float2bfloat16_rn(0.f);
+  compute_bar();
+  for (int i = tid; i < G * HD; i += kComputeWarps * 32) qs[(i / HD) * ROWP + i % HD] = __float2bfloat16_rn(qf[i]);
   // Own scores (fp32 dot, bf16-rounded like the reference's matmul output).
-  for (int h = warp; h < G; h += kWarps) {
+  for (int h = warp; h < G; h += kComputeWarps) {
     float d = 0.f;
     for (int e = lane; e < HD; e += 32) d += qf[h * HD + e] * kown[e];
     d = warp_sum(d);
-    if (lane == 0) hs[h] = bf16r(d);
+    if (lane == 0) stats[h] = bf16r(d);
   }
-  __syncthreads();
+  compute_bar();
 
-  // Query fragments for every k-step, kept in registers for pass 1.
+  // Query fragments for every k-step (A rows past the group read the zero chunk).
   uint32_t qa[KSTEPS][4];
   {
-    const int r = lane & 15, co = (lane >> 4) * 8;
+    const int qr = lane & 15;
+    const uint32_t base = qr < G ? smem_u32(qs + qr * ROWP + (lane >> 4) * 8) : smem_u32(zero);
+    const uint32_t step = qr < G ? 32u : 0u;
 #pragma unroll
-    for (int ks = 0; ks < KSTEPS; ++ks)
-      ldsm_x4(smem_u32(qs + r * ROWP + ks * 16 + co), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+    for (int ks = 0; ks < KSTEPS; ++ks) ldsm_x4(base + ks * step, qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
   }
 
+  // ---- pass 1: S[16 x 8] per warp and K tile (this warp's 8 positions), bf16 into the score rows.
+  for (int t = 0; t < ntiles; ++t) {
+    const int s = t % STAGES;
+    mbar_wait(&full[s], (t / STAGES) & 1);
+    const __nv_bfloat16* tile = ring + s * KT * ROWP;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const int n0 = warp * 8;
+#pragma unroll
+    for (int ks = 0; ks < KSTEPS; ks += 2) {
+      uint32_t b0, b1, b2, b3;  // x4: k 0-7, 8-15 of k-step ks, then of ks + 1
+      ldsm_x4(smem_u32(tile + (n0 + (lane & 7)) * ROWP + ks * 16 + (lane >> 3) * 8), b0, b1, b2, b3);
+      mma_bf16_16816(acc, qa[ks], b0, b1);
+      mma_bf16_16816(acc, qa[ks + 1], b2, b3);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    // C fragment: rows lane/4 (+8) = heads, columns 2*(lane%4) + {0,1} = positions.
+    const int h = lane >> 2, p = t * KT + n0 + 2 * (lane & 3);
+    if (h < G) {
+      if (p < n_read) sc[h * wcols + p] = __float2bfloat16_rn(acc[0]);
+      if (p + 1 < n_read) sc[h * wcols + p + 1] = __float2bfloat16_rn(acc[1]);
+    }
+  }
+  compute_bar();
+
+  // ---- softmax of (score * head_dim^-0.5) per head over [cache, own]; weights bf16 in place.
+  const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(HD)));  // head**-0.5 as fp32
+  for (int h = warp; h < G; h += kComputeWarps) {
+    __nv_bfloat16* w = sc + h * wcols;
+    const float own = __fmul_rn(stats[h], scale);
+    float m = own;
+    for (int p = lane; p < n_read; p += 32) m = fmaxf(m, __fmul_rn(__bfloat162float(w[p]), scale));
+    m = warp_max(m);
+    float sum = 0.f;
+    for (int p = lane; p < n_read; p += 32) sum += expf(__fsub_rn(__fmul_rn(__bfloat162float(w[p]), scale), m));
+    sum = warp_sum(sum);
+    const float eown = expf(__fsub_rn(own, m));
+    sum = __fadd_rn(sum, eown);
+    for (int p = lane; p < n_read; p += 32)
+      w[p] = __float2bfloat16_rn(__fdiv_rn(expf(__fsub_rn(__fmul_rn(__bfloat162float(w[p]), scale), m)), sum));
+    __syncwarp();
+    if (lane == 0) stats[h] = bf16r(__fdiv_rn(eown, sum));  // now the own key's weight
+  }
+  compute_bar();
+
+  // ---- pass 2: O[16 x this warp's dims] += W[16 x 32 positions] * V[32 x dims] per V tile.
   float acc2[NT2][4];
 #pragma unroll
   for (int n = 0; n < NT2; ++n) acc2[n][0] = acc2[n][1] = acc2[n][2] = acc2[n][3] = 0.f;
-  const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(HD)));  // head**-0.5 as fp32
-
-  for (int i = 0; i < 2 * ntiles; ++i) {
-    if (i + STAGES - 1 < 2 * ntiles) load_tile(i + STAGES - 1);
-    else cp_async_commit();
-    cp_async_wait<STAGES - 1>();
-    __syncthreads();  // tile i is in shared memory for every thread
-    const __nv_bfloat16* tile = ring + (i % STAGES) * KT * ROWP;
-    if (i < ntiles) {
-      // Pass 1: S[16 x 8] for this warp's 8 positions of the tile.
-      float s[4] = {0.f, 0.f, 0.f, 0.f};
-      const int n0 = warp * 8;
-      const int r = n0 + (lane & 7), co = (lane >> 3) * 8;  // x4: four k-chunks of 8
+  const int wr = lane & 15;
+  const uint32_t wbase = wr < G ? smem_u32(sc + wr * wcols + (lane >> 4) * 8) : smem_u32(zero);
+  const uint32_t wstep = wr < G ? 32u : 0u;  // bytes per 16 positions
+  for (int t = 0; t < ntiles; ++t) {
+    const int i = ntiles + t, s = i % STAGES;
+    mbar_wait(&full[s], (i / STAGES) & 1);
+    const __nv_bfloat16* tile = ring + s * KT * ROWP;
 #pragma unroll
-      for (int ks = 0; ks < KSTEPS; ks += 2) {
+    for (int ks = 0; ks < KT / 16; ++ks) {
+      uint32_t wa[4];
+      ldsm_x4(wbase + (t * (KT / 16) + ks) * wstep, wa[0], wa[1], wa[2], wa[3]);
+      const int vr = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;  // x4.trans: (k 0-7 | 8-15) x (n 0-7 | 8-15)
+#pragma unroll
+      for (int n = 0; n < NT2; n += 2) {
         uint32_t b0, b1, b2, b3;
-        ldsm_x4(smem_u32(tile + r * ROWP + ks * 16 + co), b0, b1, b2, b3);
-        mma_bf16_16816(s, qa[ks], b0, b1);
-        mma_bf16_16816(s, qa[ks + 1], b2, b3);
-      }
-      // C fragment: rows lane/4 (+8) = heads, columns 2*(lane%4) + {0,1} = positions.
-      const int h = lane >> 2, p = i * KT + n0 + 2 * (lane & 3);
-      if (h < G) {
-        if (p < n_read) wb[h * wcols + p] = __float2bfloat16_rn(s[0]);
-        if (p + 1 < n_read) wb[h * wcols + p + 1] = __float2bfloat16_rn(s[1]);
-      }
-    } else {
-      if (i == ntiles) {
-        // All scores are in: softmax of (score * head_dim^-0.5) per head over [cache, own];
-        // weights rounded to bf16 in place. (The barrier above ordered the last score writes.)
-        for (int h = warp; h < G; h += kWarps) {
-          __nv_bfloat16* w = wb + h * wcols;
-          const float own = __fmul_rn(hs[h], scale);
-          float m = own;
-          for (int p = lane; p < n_read; p += 32) m = fmaxf(m, __fmul_rn(__bfloat162float(w[p]), scale));
-          m = warp_max(m);
-          float sum = 0.f;
-          for (int p = lane; p < n_read; p += 32) sum += expf(__fsub_rn(__fmul_rn(__bfloat162float(w[p]), scale), m));
-          sum = warp_sum(sum);
-          const float eown = expf(__fsub_rn(own, m));
-          sum = __fadd_rn(sum, eown);
-          for (int p = lane; p < n_read; p += 32)
-            w[p] = __float2bfloat16_rn(__fdiv_rn(expf(__fsub_rn(__fmul_rn(__bfloat162float(w[p]), scale), m)), sum));
-          if (lane == 0) hs[kMaxGroups + h] = bf16r(__fdiv_rn(eown, sum));
-        }
-        __syncthreads();
-      }
-      // Pass 2: O[16 x this warp's dims] += W[16 x 32 positions] * V[32 x dims].
-      const int t = i - ntiles;
-#pragma unroll
-      for (int ks = 0; ks < KT / 16; ++ks) {
-        uint32_t wa[4];
-        ldsm_x4(smem_u32(wb + (lane & 15) * wcols + t * KT + ks * 16 + (lane >> 4) * 8), wa[0], wa[1], wa[2], wa[3]);
-        const int vr = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;  // x4.trans: (k 0-7 | 8-15) x (n 0-7 | 8-15)
-#pragma unroll
-        for (int n = 0; n < NT2; n += 2) {
-          const int d0 = (warp * NT2 + n) * 8 + (lane >> 4) * 8;
-          uint32_t b0, b1, b2, b3;
-          if constexpr (NT2 >= 2) {
-            ldsm_x4_t(smem_u32(tile + vr * ROWP + d0), b0, b1, b2, b3);
-            mma_bf16_16816(acc2[n], wa, b0, b1);
-            mma_bf16_16816(acc2[n + 1], wa, b2, b3);
-          } else {
-            ldsm_x2_t(smem_u32(tile + vr * ROWP + (warp * NT2 + n) * 8), b0, b1);
-            mma_bf16_16816(acc2[n], wa, b0, b1);
-          }
+        if constexpr (NT2 >= 2) {
+          ldsm_x4_t(smem_u32(tile + vr * ROWP + (warp * NT2 + n) * 8 + (lane >> 4) * 8), b0, b1, b2, b3);
+          mma_bf16_16816(acc2[n], wa, b0, b1);
+          mma_bf16_16816(acc2[n + 1], wa, b2, b3);
+        } else {
+          ldsm_x2_t(smem_u32(tile + vr * ROWP + (warp * NT2 + n) * 8), b0, b1);
+          mma_bf16_16816(acc2[n], wa, b0, b1);
         }
       }
     }
-    __syncthreads();  // every warp is done with tile i before its buffer is refilled
-  }
-  if (ntiles == 0) {
-    // No cached positions: only the own key; its weight is exp(0) / exp(0) = 1.
-    if (tid < G) hs[kMaxGroups + tid] = 1.0f;
-    __syncthreads();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
   }
 
   // Final: bf16(bf16(W V) + bf16(w_own * v_own)) * bf16(sigmoid(gate)), to e5m2.
@@ -231,34 +296,33 @@ __global__ void __launch_bounds__(kWarps * 32) attn_decode_kernel(AttnArgs a) {
       const int d = (warp * NT2 + n) * 8 + 2 * (lane & 3);
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const float o = bf16r(__fadd_rn(bf16r(acc2[n][e]), bf16r(__fmul_rn(hs[kMaxGroups + h], vown[d + e]))));
+        const float o = bf16r(__fadd_rn(bf16r(acc2[n][e]), bf16r(__fmul_rn(stats[h], __bfloat162float(vraw[d + e])))));
         const float gv = __bfloat162float(row[static_cast<int64_t>(qh0 + h) * 2 * HD + HD + d + e]);
         orow[static_cast<int64_t>(qh0 + h) * HD + d + e] = f32_to_e5m2(bf16r(__fmul_rn(o, bf16r(sigmoidf_(gv)))));
       }
     }
   }
-  // The token's key and value go to the cache at `where` (nothing above read that position).
-  __nv_bfloat16* kw = a.k_cache + ((static_cast<int64_t>(b) * a.num_kv_heads + g) * a.max_seq + where) * HD;
-  __nv_bfloat16* vw = a.v_cache + ((static_cast<int64_t>(b) * a.num_kv_heads + g) * a.max_seq + where) * HD;
-  for (int d = tid; d < HD; d += kWarps * 32) {
+  // The token's key and value go to the cache at `where`: every read of this (row, KV head)'s cache
+  // this step has completed above.
+  __nv_bfloat16* kw = a.k_cache + (head_row * a.max_seq + where) * HD;
+  __nv_bfloat16* vw = a.v_cache + (head_row * a.max_seq + where) * HD;
+  for (int d = tid; d < HD; d += kComputeWarps * 32) {
     kw[d] = __float2bfloat16_rn(kown[d]);
-    vw[d] = __float2bfloat16_rn(vown[d]);
+    vw[d] = vraw[d];
   }
 }
 
 template <int HD>
 int launch_attn(const AttnArgs& a, int64_t batch, cudaStream_t stream) {
-  const size_t smem = AttnSmem<HD>::bytes(a.groups, a.max_seq);
+  const size_t smem = DecLayout(HD, a.groups, a.max_seq).total;
   if (smem > 220 * 1024)
     return q38host::set_error("q38_attn_decode: max_seq %lld needs %zu bytes of shared memory", (long long)a.max_seq, smem),
            Q38_ERR_UNSUPPORTED;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem));
-    if (e != cudaSuccess) return q38host::cuda_status(e, "cudaFuncSetAttribute(attn_decode)");
-  }
+  cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return q38host::cuda_status(e, "cudaFuncSetAttribute(attn_decode)");
   dim3 grid(static_cast<unsigned>(a.num_kv_heads), static_cast<unsigned>(batch));
-  attn_decode_kernel<HD><<<grid, kWarps * 32, smem, stream>>>(a);
+  attn_decode_kernel<HD><<<grid, kThreads, smem, stream>>>(a);
   return q38host::cuda_status(cudaGetLastError(), "attn_decode launch");
 }
 
