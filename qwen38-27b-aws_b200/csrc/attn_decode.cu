@@ -9,11 +9,12 @@
 // against V (V streamed once).
 //
 // It is HBM-bound on the cache (position * head_dim * 4 bytes per (row, KV head)), so the CTA is
-// built around the copy stream: a copy warp keeps a ring of 5 tiles of 32 positions in flight (one
-// bulk copy per 512-byte row, into rows padded for conflict-free ldmatrix), K tiles then V tiles,
-// handed over through full / empty mbarriers, so it runs ahead into V while the four compute warps
-// finish the softmax; the compute warps multiply on mma.sync (BF16, fp32 accumulate) and never wait
-// on a CTA-wide barrier per tile. Two CTAs per SM.
+// built around the copy stream: a copy warp keeps a ring of tiles of 32 positions in flight (tensor
+// copies of 64-dim boxes with 128-byte swizzle), K tiles then V tiles, handed over through full /
+// empty mbarriers, so it runs ahead into V while the four compute warps finish the softmax; the
+// compute warps multiply on mma.sync (BF16, fp32 accumulate) and never wait on a CTA-wide barrier per
+// tile. Every other input of the row (queries, own key / value, gates, norm weights, cos / sin) is
+// fetched in one round trip at the start. Three CTAs per SM.
 #include "attn_common.cuh"
 
 namespace {
@@ -43,48 +44,71 @@ struct AttnArgs {
 constexpr int kComputeWarps = 4;
 constexpr int kThreads = (kComputeWarps + 1) * 32;  // compute warps + one copy warp
 constexpr int KT = 32;                               // cache positions per tile
-constexpr int STAGES = 5;                            // tiles in flight per CTA
+constexpr int kStages = 3;                           // tiles in flight per CTA (three CTAs per SM)
 constexpr int MROWS = 16;                            // the MMA's M: query heads, padded by a zero row
 
 __host__ __device__ constexpr size_t al16(size_t x) { return (x + 15) & ~size_t(15); }
 
-// Shared memory of one CTA (byte offsets; the same arithmetic on host and device).
+// K / V tile geometry: [KT positions][HD] bf16 as boxes of up to 64 dims (128-byte rows), written by
+// the tensor copy with 128-byte swizzle (16-byte chunk c of row r stored at chunk c ^ (r % 8)), so
+// ldmatrix reads of 8 rows at one chunk hit 8 distinct bank groups. Heads narrower than 64 dims
+// (the test config) use one unswizzled box.
+template <int HD>
+struct TileGeom {
+  static constexpr bool kSwizzle = HD >= 64;
+  static constexpr int kBoxCols = kSwizzle ? 64 : HD;
+  static constexpr int kBoxes = HD / kBoxCols;
+  static constexpr int kBoxBytes = KT * kBoxCols * 2;
+  static constexpr int kTileBytes = KT * HD * 2;
+  // Byte offset of 16-byte chunk `c` (8 dims) of position row `r` within a tile.
+  __device__ static __forceinline__ uint32_t at(int r, int c) {
+    if constexpr (kSwizzle) {
+      return static_cast<uint32_t>((c >> 3) * kBoxBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+    } else {
+      return static_cast<uint32_t>(r * HD * 2 + c * 16);
+    }
+  }
+};
+
+// Shared memory of one CTA (byte offsets from a 1024-byte aligned base; the same arithmetic on host
+// and device).
+template <int HD, int STAGES>
 struct DecLayout {
-  int rowp;      // padded K / V / q row (bf16): ldmatrix rows land in distinct banks
+  int rowp;      // padded q row (bf16): ldmatrix rows land in distinct banks
   int wcols;     // score / weight row length (bf16)
-  size_t ring;   // [STAGES][KT][rowp] bf16   K tiles, then V tiles
-  size_t q;      // [groups][rowp] bf16      queries after norm + rotary
-  size_t sc;     // [groups][wcols] bf16     scores, then weights in place
-  size_t qf;     // [groups][hd] fp32        query staging
-  size_t kown;   // [hd] fp32                own key staging
-  size_t prm;    // [4][hd] bf16             q / k norm weights, cos, sin
+  size_t ring;   // [STAGES] tiles        K tiles, then V tiles
+  size_t q;      // [groups][rowp] bf16   queries after norm + rotary
+  size_t sc;     // [groups][wcols] bf16  scores, then weights in place
+  size_t qf;     // [groups][hd] fp32     query staging
+  size_t kown;   // [hd] fp32             own key staging
+  size_t prm;    // [4][hd] bf16          q / k norm weights, cos, sin
+  size_t gate;   // [groups][hd] bf16     output gates
+  size_t vown;   // [hd] bf16             own value
   size_t zero;   // 16 zero bytes: the MMA rows past the group
   size_t bars;   // full[STAGES], empty[STAGES]
   size_t stats;  // [kMaxGroups] fp32 own scores, then own weights
-  size_t total;
-  __host__ __device__ DecLayout(int hd, int groups, int64_t max_seq) {
-    rowp = hd + 8;
+  size_t total;  // including the alignment slack of the base
+  __host__ __device__ DecLayout(int groups, int64_t max_seq) {
+    rowp = HD + 8;
     wcols = static_cast<int>((max_seq + KT - 1) / KT * KT) + 8;
     size_t off = 0;
-    ring = off;
-    off = al16(off + static_cast<size_t>(STAGES) * KT * rowp * 2);
-    q = off;
-    off = al16(off + static_cast<size_t>(groups) * rowp * 2);
-    sc = off;
-    off = al16(off + static_cast<size_t>(groups) * wcols * 2);
-    qf = off;
-    off = al16(off + static_cast<size_t>(groups) * hd * 4);
-    kown = off;
-    off = al16(off + static_cast<size_t>(hd) * 4);
-    prm = off;
-    off = al16(off + static_cast<size_t>(4) * hd * 2);
-    zero = off;
-    off += 16;
-    bars = off;
-    off += 2 * STAGES * 8;
-    stats = off;
-    off = al16(off + kMaxGroups * 4);
-    total = off;
+    auto take = [&](size_t bytes) {
+      const size_t at = off;
+      off = al16(off + bytes);
+      return at;
+    };
+    ring = take(static_cast<size_t>(STAGES) * TileGeom<HD>::kTileBytes);
+    q = take(static_cast<size_t>(groups) * rowp * 2);
+    sc = take(static_cast<size_t>(groups) * wcols * 2);
+    qf = take(static_cast<size_t>(groups) * HD * 4);
+    kown = take(static_cast<size_t>(HD) * 4);
+    prm = take(static_cast<size_t>(4) * HD * 2);
+    gate = take(static_cast<size_t>(groups) * HD * 2);
+    vown = take(static_cast<size_t>(HD) * 2);
+    zero = take(16);
+    bars = take(2 * STAGES * 8);
+    stats = take(kMaxGroups * 4);
+    total = off + 1024;
   }
 };
 
@@ -93,40 +117,38 @@ __device__ __forceinline__ void compute_bar() {
   asm volatile("bar.sync 1, %0;" ::"n"(kComputeWarps * 32) : "memory");
 }
 
-template <int HD>
-__global__ void __launch_bounds__(kThreads) attn_decode_kernel(AttnArgs a) {
+template <int HD, int STAGES>
+__global__ void __launch_bounds__(kThreads, 3) attn_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
+                                                               const __grid_constant__ CUtensorMap tmap_v, AttnArgs a) {
+  using T = TileGeom<HD>;
   constexpr int KSTEPS = HD / 16;                  // MMA k-steps over head_dim
   constexpr int NT2 = HD / 8 / kComputeWarps;      // pass-2 n-tiles (8 dims) per warp
   static_assert(KT == 8 * kComputeWarps, "one 8-position n-tile per compute warp in pass 1");
-  extern __shared__ __align__(16) uint8_t smem_raw[];
+  static_assert(KSTEPS % 2 == 0 && NT2 >= 1, "head_dim");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int G = a.groups;
-  const DecLayout L(HD, G, a.max_seq);
+  const DecLayout<HD, STAGES> L(G, a.max_seq);
   const int ROWP = L.rowp, wcols = L.wcols;
-  __nv_bfloat16* ring = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.ring);
-  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.q);
-  __nv_bfloat16* sc = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.sc);
-  float* qf = reinterpret_cast<float*>(smem_raw + L.qf);
-  float* kown = reinterpret_cast<float*>(smem_raw + L.kown);
-  __nv_bfloat16* wq = reinterpret_cast<__nv_bfloat16*>(smem_raw + L.prm);
+  uint8_t* ring = smem + L.ring;
+  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem + L.q);
+  __nv_bfloat16* sc = reinterpret_cast<__nv_bfloat16*>(smem + L.sc);
+  float* qf = reinterpret_cast<float*>(smem + L.qf);
+  float* kown = reinterpret_cast<float*>(smem + L.kown);
+  __nv_bfloat16* wq = reinterpret_cast<__nv_bfloat16*>(smem + L.prm);
   __nv_bfloat16* wk = wq + HD;
   __nv_bfloat16* cs = wk + HD;
   __nv_bfloat16* sn = cs + HD;
-  uint32_t* zero = reinterpret_cast<uint32_t*>(smem_raw + L.zero);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw + L.bars);
+  __nv_bfloat16* gates = reinterpret_cast<__nv_bfloat16*>(smem + L.gate);
+  __nv_bfloat16* vown = reinterpret_cast<__nv_bfloat16*>(smem + L.vown);
+  uint32_t* zero = reinterpret_cast<uint32_t*>(smem + L.zero);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
   uint64_t* empty = full + STAGES;
-  float* stats = reinterpret_cast<float*>(smem_raw + L.stats);
+  float* stats = reinterpret_cast<float*>(smem + L.stats);
 
   const int g = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const bool on = a.active[b] > 0.5f;
-  const int pos = a.position[b];
-  const int64_t pos64 = pos < 0 ? 0 : pos;
-  const int n_read = on ? static_cast<int>(pos64 < a.max_seq ? pos64 : a.max_seq) : 0;
-  const int64_t where = on ? (pos64 < a.max_seq - 1 ? pos64 : a.max_seq - 1) : a.max_seq - 1;
-  const int ntiles = (n_read + KT - 1) / KT;
   const int64_t head_row = static_cast<int64_t>(b) * a.num_kv_heads + g;
-  const __nv_bfloat16* kc = a.k_cache + head_row * a.max_seq * HD;
-  const __nv_bfloat16* vc = a.v_cache + head_row * a.max_seq * HD;
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -136,46 +158,92 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(AttnArgs a) {
     fence_mbar_init();
   }
   if (tid < 4) zero[tid] = 0u;
+  const bool on = a.active[b] > 0.5f;
+  const int pos = a.position[b];
+  const int64_t pos64 = pos < 0 ? 0 : pos;
+  const int n_read = on ? static_cast<int>(pos64 < a.max_seq ? pos64 : a.max_seq) : 0;
+  const int64_t where = on ? (pos64 < a.max_seq - 1 ? pos64 : a.max_seq - 1) : a.max_seq - 1;
+  const int ntiles = (n_read + KT - 1) / KT;
   __syncthreads();
 
   if (warp == kComputeWarps) {
-    // Copy warp: K tiles 0 .. ntiles-1, then V tiles, one bulk copy per 512-byte row into the padded
-    // ring. A V tile's rows past n_read are zeroed (their weights are zero; 0 x stale data could be NaN).
-    for (int i = 0; i < 2 * ntiles; ++i) {
-      const int s = i % STAGES;
-      if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) break;
-      const bool is_v = i >= ntiles;
-      const int p0 = (is_v ? i - ntiles : i) * KT;
-      const int rows = min(KT, n_read - p0);
-      __nv_bfloat16* dst = ring + s * KT * ROWP;
-      if (is_v)
-        for (int c = lane; c < (KT - rows) * (HD / 8); c += 32)
-          *reinterpret_cast<uint4*>(dst + (rows + c / (HD / 8)) * ROWP + (c % (HD / 8)) * 8) = make_uint4(0u, 0u, 0u, 0u);
-      __syncwarp();
-      if (lane == 0) mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rows * HD * 2));
-      __syncwarp();
-      const __nv_bfloat16* src = (is_v ? vc : kc) + static_cast<int64_t>(p0) * HD;
-      for (int r = lane; r < rows; r += 32) bulk_load(dst + r * ROWP, src + static_cast<int64_t>(r) * HD, HD * 2, &full[s]);
+    // Copy warp: K tiles 0 .. ntiles-1, then V tiles, each as T::kBoxes tensor copies of [KT rows x
+    // box] at row head_row * max_seq + p0. Rows past n_read bring other positions' (finite) data or
+    // zeros past the cache's end; the compute warps ignore or clear them.
+    if (lane == 0) {
+      prefetch_tmap(&tmap_k);
+      prefetch_tmap(&tmap_v);
+      const int y0 = static_cast<int>(head_row * a.max_seq);
+      for (int i = 0; i < 2 * ntiles; ++i) {
+        const int s = i % STAGES;
+        if (i >= STAGES && !mbar_wait(&empty[s], ((i / STAGES) - 1) & 1)) break;
+        const bool is_v = i >= ntiles;
+        const int p0 = (is_v ? i - ntiles : i) * KT;
+        uint8_t* dst = ring + s * T::kTileBytes;
+        mbar_arrive_expect_tx(&full[s], T::kTileBytes);
+#pragma unroll
+        for (int bx = 0; bx < T::kBoxes; ++bx)
+          tma_load_2d(dst + bx * T::kBoxBytes, is_v ? &tmap_v : &tmap_k, &full[s], bx * T::kBoxCols, y0 + p0);
+      }
     }
     return;
   }
 
-  // ---- compute warps: the queries and the own key (norm + rotary), staged in one round trip.
+  // ---- compute warps: every input of the row in one round trip (queries, own key and value, norm
+  // weights, cos / sin, gates), then norm + rotary.
+  // All loads are issued before any store (16-byte vectors into registers), so the staging costs one
+  // round trip instead of one per loop iteration.
+  constexpr int CT = kComputeWarps * 32;
+  constexpr int HV = HD / 8;  // 16-byte vectors per head row
+  static_assert(kMaxGroups * HV <= 2 * CT && 4 * HV <= CT, "staging covers a group in two vectors per thread");
   const __nv_bfloat16* row = a.qkv + b * a.ld_qkv;
   const int qh0 = g * G;
-  for (int i = tid; i < G * HD; i += kComputeWarps * 32) {
-    const int h = i / HD, d = i % HD;
-    qf[i] = __bfloat162float(row[static_cast<int64_t>(qh0 + h) * 2 * HD + d]);
-  }
   const __nv_bfloat16* kraw = row + static_cast<int64_t>(a.num_q_heads) * 2 * HD + static_cast<int64_t>(g) * HD;
   const __nv_bfloat16* vraw = kraw + static_cast<int64_t>(a.num_kv_heads) * HD;
-  for (int d = tid; d < HD; d += kComputeWarps * 32) {
-    kown[d] = __bfloat162float(kraw[d]);
-    wq[d] = a.q_norm_w[d];
-    wk[d] = a.k_norm_w[d];
-    if (d < a.rot) {
-      cs[d] = a.cos[b * a.rot + d];
-      sn[d] = a.sin[b * a.rot + d];
+  {
+    uint4 rq[2], rg[2], rp;
+    __nv_bfloat16 rc[2], rs[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = tid + k * CT;
+      if (i < G * HV) {
+        const uint4* src = reinterpret_cast<const uint4*>(row + static_cast<int64_t>(qh0 + i / HV) * 2 * HD);
+        rq[k] = src[i % HV];
+        rg[k] = src[HV + i % HV];
+      }
+      const int d = tid + k * CT;
+      if (d < a.rot) {
+        rc[k] = a.cos[b * a.rot + d];
+        rs[k] = a.sin[b * a.rot + d];
+      }
+    }
+    // Threads 0..4*HV-1: the own key, own value, q and k norm weights (one vector each).
+    const int which = tid / HV, c = tid % HV;
+    if (which < 4) {
+      const __nv_bfloat16* src = which == 0 ? kraw : which == 1 ? vraw : which == 2 ? a.q_norm_w : a.k_norm_w;
+      rp = reinterpret_cast<const uint4*>(src)[c];
+    }
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = tid + k * CT;
+      if (i < G * HV) {
+        const __nv_bfloat16* qv = reinterpret_cast<const __nv_bfloat16*>(&rq[k]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) qf[i * 8 + e] = __bfloat162float(qv[e]);
+        reinterpret_cast<uint4*>(gates)[i] = rg[k];
+      }
+      const int d = tid + k * CT;
+      if (d < a.rot) {
+        cs[d] = rc[k];
+        sn[d] = rs[k];
+      }
+    }
+    if (which == 0) {
+      const __nv_bfloat16* kv = reinterpret_cast<const __nv_bfloat16*>(&rp);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) kown[c * 8 + e] = __bfloat162float(kv[e]);
+    } else if (which < 4) {
+      reinterpret_cast<uint4*>(which == 1 ? vown : which == 2 ? wq : wk)[c] = rp;
     }
   }
   // Weights past n_read in the last tile are zero.
@@ -210,26 +278,28 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(AttnArgs a) {
   }
 
   // ---- pass 1: S[16 x 8] per warp and K tile (this warp's 8 positions), bf16 into the score rows.
+  // Two accumulators (even / odd k-step pairs) halve the dependent MMA chain.
+  const int n0 = warp * 8;
   for (int t = 0; t < ntiles; ++t) {
     const int s = t % STAGES;
     mbar_wait(&full[s], (t / STAGES) & 1);
-    const __nv_bfloat16* tile = ring + s * KT * ROWP;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    const int n0 = warp * 8;
+    const uint32_t tile = smem_u32(ring + s * T::kTileBytes);
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    const int r = n0 + (lane & 7);
 #pragma unroll
     for (int ks = 0; ks < KSTEPS; ks += 2) {
       uint32_t b0, b1, b2, b3;  // x4: k 0-7, 8-15 of k-step ks, then of ks + 1
-      ldsm_x4(smem_u32(tile + (n0 + (lane & 7)) * ROWP + ks * 16 + (lane >> 3) * 8), b0, b1, b2, b3);
-      mma_bf16_16816(acc, qa[ks], b0, b1);
-      mma_bf16_16816(acc, qa[ks + 1], b2, b3);
+      ldsm_x4(tile + T::at(r, 2 * ks + (lane >> 3)), b0, b1, b2, b3);
+      mma_bf16_16816(acc[(ks >> 1) & 1], qa[ks], b0, b1);
+      mma_bf16_16816(acc[(ks >> 1) & 1], qa[ks + 1], b2, b3);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
     // C fragment: rows lane/4 (+8) = heads, columns 2*(lane%4) + {0,1} = positions.
     const int h = lane >> 2, p = t * KT + n0 + 2 * (lane & 3);
     if (h < G) {
-      if (p < n_read) sc[h * wcols + p] = __float2bfloat16_rn(acc[0]);
-      if (p + 1 < n_read) sc[h * wcols + p + 1] = __float2bfloat16_rn(acc[1]);
+      if (p < n_read) sc[h * wcols + p] = __float2bfloat16_rn(__fadd_rn(acc[0][0], acc[1][0]));
+      if (p + 1 < n_read) sc[h * wcols + p + 1] = __float2bfloat16_rn(__fadd_rn(acc[0][1], acc[1][1]));
     }
   }
   compute_bar();
@@ -261,10 +331,20 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(AttnArgs a) {
   const int wr = lane & 15;
   const uint32_t wbase = wr < G ? smem_u32(sc + wr * wcols + (lane >> 4) * 8) : smem_u32(zero);
   const uint32_t wstep = wr < G ? 32u : 0u;  // bytes per 16 positions
+  const int c0 = warp * NT2;                 // this warp's first 8-dim chunk
   for (int t = 0; t < ntiles; ++t) {
     const int i = ntiles + t, s = i % STAGES;
     mbar_wait(&full[s], (i / STAGES) & 1);
-    const __nv_bfloat16* tile = ring + s * KT * ROWP;
+    uint8_t* tp = ring + s * T::kTileBytes;
+    const uint32_t tile = smem_u32(tp);
+    const int rows = min(KT, n_read - t * KT);
+    if (rows < KT) {
+      // Positions past n_read (zero weight) must not bring stale non-finite values into 0 x V.
+      for (int e = lane; e < (KT - rows) * NT2; e += 32)
+        *reinterpret_cast<uint4*>(tp + T::at(rows + e / NT2, c0 + e % NT2)) = make_uint4(0u, 0u, 0u, 0u);
+      fence_proxy_async_shared();  // ordered before the slot's next tensor copy
+      __syncwarp();
+    }
 #pragma unroll
     for (int ks = 0; ks < KT / 16; ++ks) {
       uint32_t wa[4];
@@ -274,11 +354,11 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(AttnArgs a) {
       for (int n = 0; n < NT2; n += 2) {
         uint32_t b0, b1, b2, b3;
         if constexpr (NT2 >= 2) {
-          ldsm_x4_t(smem_u32(tile + vr * ROWP + (warp * NT2 + n) * 8 + (lane >> 4) * 8), b0, b1, b2, b3);
+          ldsm_x4_t(tile + T::at(vr, c0 + n + (lane >> 4)), b0, b1, b2, b3);
           mma_bf16_16816(acc2[n], wa, b0, b1);
           mma_bf16_16816(acc2[n + 1], wa, b2, b3);
         } else {
-          ldsm_x2_t(smem_u32(tile + vr * ROWP + (warp * NT2 + n) * 8), b0, b1);
+          ldsm_x2_t(tile + T::at(vr, c0 + n), b0, b1);
           mma_bf16_16816(acc2[n], wa, b0, b1);
         }
       }
@@ -293,11 +373,11 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(AttnArgs a) {
   if (h < G) {
 #pragma unroll
     for (int n = 0; n < NT2; ++n) {
-      const int d = (warp * NT2 + n) * 8 + 2 * (lane & 3);
+      const int d = (c0 + n) * 8 + 2 * (lane & 3);
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const float o = bf16r(__fadd_rn(bf16r(acc2[n][e]), bf16r(__fmul_rn(stats[h], __bfloat162float(vraw[d + e])))));
-        const float gv = __bfloat162float(row[static_cast<int64_t>(qh0 + h) * 2 * HD + HD + d + e]);
+        const float o = bf16r(__fadd_rn(bf16r(acc2[n][e]), bf16r(__fmul_rn(stats[h], __bfloat162float(vown[d + e])))));
+        const float gv = __bfloat162float(gates[h * HD + d + e]);
         orow[static_cast<int64_t>(qh0 + h) * HD + d + e] = f32_to_e5m2(bf16r(__fmul_rn(o, bf16r(sigmoidf_(gv)))));
       }
     }
@@ -308,21 +388,29 @@ __global__ void __launch_bounds__(kThreads) attn_decode_kernel(AttnArgs a) {
   __nv_bfloat16* vw = a.v_cache + (head_row * a.max_seq + where) * HD;
   for (int d = tid; d < HD; d += kComputeWarps * 32) {
     kw[d] = __float2bfloat16_rn(kown[d]);
-    vw[d] = vraw[d];
+    vw[d] = vown[d];
   }
 }
 
 template <int HD>
 int launch_attn(const AttnArgs& a, int64_t batch, cudaStream_t stream) {
-  const size_t smem = DecLayout(HD, a.groups, a.max_seq).total;
+  using T = TileGeom<HD>;
+  const size_t smem = DecLayout<HD, kStages>(a.groups, a.max_seq).total;
   if (smem > 220 * 1024)
     return q38host::set_error("q38_attn_decode: max_seq %lld needs %zu bytes of shared memory", (long long)a.max_seq, smem),
            Q38_ERR_UNSUPPORTED;
-  cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  const uint64_t rows = static_cast<uint64_t>(batch) * a.num_kv_heads * a.max_seq;
+  if (rows + KT > (1ull << 31))
+    return q38host::set_error("q38_attn_decode: cache of %llu rows too large", (unsigned long long)rows), Q38_ERR_UNSUPPORTED;
+  CUtensorMap tk, tv;
+  int st = q38host::encode_tmap_2d(&tk, a.k_cache, rows, HD, 2, KT, T::kBoxCols, T::kSwizzle);
+  if (st == Q38_OK) st = q38host::encode_tmap_2d(&tv, a.v_cache, rows, HD, 2, KT, T::kBoxCols, T::kSwizzle);
+  if (st != Q38_OK) return st;
+  cudaError_t e = cudaFuncSetAttribute(attn_decode_kernel<HD, kStages>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return q38host::cuda_status(e, "cudaFuncSetAttribute(attn_decode)");
   dim3 grid(static_cast<unsigned>(a.num_kv_heads), static_cast<unsigned>(batch));
-  attn_decode_kernel<HD><<<grid, kThreads, smem, stream>>>(a);
+  attn_decode_kernel<HD, kStages><<<grid, kThreads, smem, stream>>>(tk, tv, a);
   return q38host::cuda_status(cudaGetLastError(), "attn_decode launch");
 }
 
@@ -342,8 +430,9 @@ extern "C" int q38_attn_decode(const void* qkv, int64_t ld_qkv, const void* q_no
   if (ld_qkv < static_cast<int64_t>(2 * num_q_heads + 2 * num_kv_heads) * head_dim ||
       ld_out < static_cast<int64_t>(num_q_heads) * head_dim || ld_qkv % 8)
     return set_error("q38_attn_decode: leading dimension too small"), Q38_ERR_ARG;
-  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) | reinterpret_cast<uintptr_t>(qkv)) & 15u)
-    return set_error("q38_attn_decode: qkv and caches must be 16-byte aligned"), Q38_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) | reinterpret_cast<uintptr_t>(qkv) |
+       reinterpret_cast<uintptr_t>(q_norm_w) | reinterpret_cast<uintptr_t>(k_norm_w)) & 15u)
+    return set_error("q38_attn_decode: qkv, caches and norm weights must be 16-byte aligned"), Q38_ERR_ARG;
   AttnArgs a{};
   a.qkv = static_cast<const __nv_bfloat16*>(qkv);
   a.ld_qkv = ld_qkv;
