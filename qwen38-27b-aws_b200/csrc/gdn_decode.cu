@@ -54,24 +54,31 @@ __global__ void __launch_bounds__(DK) gdn_qk_kernel(GdnArgs a, float* qk) {
   const int key_dim = a.num_k_heads * DK;
   const int conv_dim = 2 * key_dim + a.num_v_heads * a.head_v;
   const __nv_bfloat16* xrow = a.qkvz + b * a.ld_qkvz;
-  float val[2];
+  // Both channels' loads before any store: one round trip.
+  float win[2][KCONV], cwv[2][KCONV];
+  __nv_bfloat16* cs[2];
 #pragma unroll
   for (int which = 0; which < 2; ++which) {
     const int c = which * key_dim + kh * DK + i;
-    __nv_bfloat16* cs = a.conv_state + (static_cast<int64_t>(b) * conv_dim + c) * (KCONV - 1);
+    cs[which] = a.conv_state + (static_cast<int64_t>(b) * conv_dim + c) * (KCONV - 1);
     const __nv_bfloat16* cw = a.conv_w + static_cast<int64_t>(c) * KCONV;
-    float win[KCONV];
 #pragma unroll
-    for (int j = 0; j < KCONV - 1; ++j) win[j] = __bfloat162float(cs[j]) * keep;
-    win[KCONV - 1] = __bfloat162float(xrow[c]);
+    for (int j = 0; j < KCONV - 1; ++j) win[which][j] = __bfloat162float(cs[which][j]) * keep;
+    win[which][KCONV - 1] = __bfloat162float(xrow[c]);
+#pragma unroll
+    for (int j = 0; j < KCONV; ++j) cwv[which][j] = __bfloat162float(cw[j]);
+  }
+  float val[2];
+#pragma unroll
+  for (int which = 0; which < 2; ++which) {
     float acc = 0.f;
 #pragma unroll
-    for (int j = 0; j < KCONV; ++j) acc = __fadd_rn(acc, bf16r(__fmul_rn(win[j], __bfloat162float(cw[j]))));
+    for (int j = 0; j < KCONV; ++j) acc = __fadd_rn(acc, bf16r(__fmul_rn(win[which][j], cwv[which][j])));
     const float conv = bf16r(acc);
     val[which] = bf16r(__fmul_rn(conv, bf16r(sigmoidf_(conv))));
     if (on) {
 #pragma unroll
-      for (int j = 0; j < KCONV - 1; ++j) cs[j] = __float2bfloat16_rn(win[j + 1]);
+      for (int j = 0; j < KCONV - 1; ++j) cs[which][j] = __float2bfloat16_rn(win[which][j + 1]);
     }
   }
   float sq = warp_sum(__fmul_rn(val[0], val[0])), sk = warp_sum(__fmul_rn(val[1], val[1]));
@@ -96,7 +103,7 @@ __global__ void __launch_bounds__(DK) gdn_qk_kernel(GdnArgs a, float* qk) {
 template <int DK, int DV>
 struct GdnSmem {
   static constexpr size_t TILE = static_cast<size_t>(DK) * DV * 2;
-  static constexpr size_t TOTAL = TILE + sizeof(float) * (DV + 2 * DK + 4 * DV + 4) + 16;
+  static constexpr size_t TOTAL = TILE + sizeof(float) * (DV + 2 * DK + 4 * DV + 4) + 2 * 2 * DV + 16;
 };
 
 // Kernel 2, one CTA of 128 threads per (row, value head): the head's v conv, gates, the recurrence on
@@ -116,7 +123,9 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(GdnArgs a, const float*
   float* kn = qn + DK;                                   // [DK]
   float* red = kn + DK;                                  // [4][DV], both reductions in turn
   float* gates = red + 4 * DV;                           // beta, decay
-  uint64_t* bar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(gates + 4) + 7) & ~uintptr_t(7));
+  __nv_bfloat16* nws = reinterpret_cast<__nv_bfloat16*>(gates + 4);  // [DV] norm weight
+  __nv_bfloat16* zs = nws + DV;                                      // [DV] z
+  uint64_t* bar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(zs + DV) + 7) & ~uintptr_t(7));
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.x, b = blockIdx.y;
@@ -137,36 +146,67 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(GdnArgs a, const float*
       bulk_load(tile, a.state + (static_cast<int64_t>(b) * a.num_v_heads + h) * DK * DV, TILE_BYTES, bar);
     }
   }
-  // v conv + SiLU for this head's DV channels.
+  // Every input of the head, loaded into registers before any store so the whole prologue is one
+  // round trip: the v channels' conv window and weights, the normalised q / k, the norm weight, z and
+  // the gate inputs.
+  constexpr int VN = (DV + 127) / 128;      // v channels per thread
+  constexpr int QN = (2 * DK + 127) / 128;  // q / k values per thread
   const __nv_bfloat16* xrow = a.qkvz + b * a.ld_qkvz;
-  for (int i = tid; i < DV; i += 128) {
-    const int c = 2 * key_dim + h * DV + i;
-    __nv_bfloat16* cs = a.conv_state + (static_cast<int64_t>(b) * conv_dim + c) * (KCONV - 1);
-    const __nv_bfloat16* cw = a.conv_w + static_cast<int64_t>(c) * KCONV;
-    float win[KCONV];
+  const __nv_bfloat16* zrow = xrow + conv_dim + h * DV;
+  const float* qkrow = qk + (static_cast<int64_t>(b) * a.num_k_heads + kh) * 2 * DK;
+  float win[VN][KCONV], cwv[VN][KCONV], qkr[QN], graw[4];
+  __nv_bfloat16 nwr[VN], zr[VN];
+  __nv_bfloat16* csp[VN];
 #pragma unroll
-    for (int j = 0; j < KCONV - 1; ++j) win[j] = __bfloat162float(cs[j]) * keep;
-    win[KCONV - 1] = __bfloat162float(xrow[c]);
-    float acc = 0.f;
+  for (int v = 0; v < VN; ++v) {
+    const int i = tid + 128 * v;
+    if (i < DV) {
+      const int c = 2 * key_dim + h * DV + i;
+      csp[v] = a.conv_state + (static_cast<int64_t>(b) * conv_dim + c) * (KCONV - 1);
+      const __nv_bfloat16* cw = a.conv_w + static_cast<int64_t>(c) * KCONV;
 #pragma unroll
-    for (int j = 0; j < KCONV; ++j) acc = __fadd_rn(acc, bf16r(__fmul_rn(win[j], __bfloat162float(cw[j]))));
-    const float conv = bf16r(acc);
-    xv[i] = bf16r(__fmul_rn(conv, bf16r(sigmoidf_(conv))));
-    if (on) {
+      for (int j = 0; j < KCONV - 1; ++j) win[v][j] = __bfloat162float(csp[v][j]) * keep;
+      win[v][KCONV - 1] = __bfloat162float(xrow[c]);
 #pragma unroll
-      for (int j = 0; j < KCONV - 1; ++j) cs[j] = __float2bfloat16_rn(win[j + 1]);
+      for (int j = 0; j < KCONV; ++j) cwv[v][j] = __bfloat162float(cw[j]);
+      nwr[v] = a.norm_w[i];
+      zr[v] = zrow[i];
     }
   }
-  const float* qkrow = qk + (static_cast<int64_t>(b) * a.num_k_heads + kh) * 2 * DK;
-  for (int i = tid; i < 2 * DK; i += 128) qn[i] = qkrow[i];  // qn then kn, adjacent
+#pragma unroll
+  for (int k = 0; k < QN; ++k)
+    if (tid + 128 * k < 2 * DK) qkr[k] = qkrow[tid + 128 * k];
+  if (tid == 0) {
+    graw[0] = __bfloat162float(a.ab[b * a.ld_ab + h]);
+    graw[1] = __bfloat162float(a.ab[b * a.ld_ab + a.num_v_heads + h]);
+    graw[2] = __bfloat162float(a.a_log[h]);
+    graw[3] = __bfloat162float(a.dt_bias[h]);
+  }
+  // v conv + SiLU for this head's DV channels; the conv state moves on.
+#pragma unroll
+  for (int v = 0; v < VN; ++v) {
+    const int i = tid + 128 * v;
+    if (i < DV) {
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < KCONV; ++j) acc = __fadd_rn(acc, bf16r(__fmul_rn(win[v][j], cwv[v][j])));
+      const float conv = bf16r(acc);
+      xv[i] = bf16r(__fmul_rn(conv, bf16r(sigmoidf_(conv))));
+      nws[i] = nwr[v];
+      zs[i] = zr[v];
+      if (on) {
+#pragma unroll
+        for (int j = 0; j < KCONV - 1; ++j) csp[v][j] = __float2bfloat16_rn(win[v][j + 1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < QN; ++k)
+    if (tid + 128 * k < 2 * DK) qn[tid + 128 * k] = qkr[k];  // qn then kn, adjacent
   // Gates: beta = bf16(sigmoid(b)) * active, g = -exp(A_log) * softplus(a + dt_bias) * active.
   if (tid == 0) {
-    const float braw = __bfloat162float(a.ab[b * a.ld_ab + h]);
-    const float araw = __bfloat162float(a.ab[b * a.ld_ab + a.num_v_heads + h]);
-    const float beta = __fmul_rn(bf16r(sigmoidf_(braw)), act);
-    const float g = __fmul_rn(__fmul_rn(-expf(__bfloat162float(a.a_log[h])),
-                                        softplusf_(__fadd_rn(araw, __bfloat162float(a.dt_bias[h])))),
-                              act);
+    const float beta = __fmul_rn(bf16r(sigmoidf_(graw[0])), act);
+    const float g = __fmul_rn(__fmul_rn(-expf(graw[2]), softplusf_(__fadd_rn(graw[1], graw[3]))), act);
     gates[0] = beta;
     gates[1] = expf(g);
   }
@@ -240,14 +280,13 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(GdnArgs a, const float*
     }
     ss = warp_sum(ss);
     const float r = 1.0f / sqrtf(__fadd_rn(__fdiv_rn(ss, static_cast<float>(DV)), a.eps));
-    const __nv_bfloat16* zrow = xrow + conv_dim + h * DV;
     uint8_t* orow = a.out + b * a.ld_out + h * DV;
 #pragma unroll
     for (int t = 0; t < CPL; ++t) {
       const int c = c0 + t;
       const float n1 = bf16r(__fmul_rn(ob[t], r));
-      const float n2 = bf16r(__fmul_rn(__bfloat162float(a.norm_w[c]), n1));
-      const float z = __bfloat162float(zrow[c]);
+      const float n2 = bf16r(__fmul_rn(__bfloat162float(nws[c]), n1));
+      const float z = __bfloat162float(zs[c]);
       const float sz = __fmul_rn(z, sigmoidf_(z));
       orow[c] = f32_to_e5m2(bf16r(__fmul_rn(n2, sz)));
     }
