@@ -48,6 +48,14 @@ typedef void* q38_stream_t; /* a cudaStream_t */
 /* ABI version, bumped on any signature change. */
 int q38_abi_version(void);
 
+/*
+ * Programmatic dependent launch for the decode path's kernels (GEMMs, lm_head, norms, gated delta and
+ * attention decode): each may start while the previous kernel in its stream drains, running its
+ * prologue and prefetching its weights, and waits on the device before touching activations. On by
+ * default (the environment variable Q38_PDL=0 turns it off); applies to launches after the call.
+ */
+int q38_set_pdl(int enable);
+
 /* Copies the last error message of this host thread into buf (NUL-terminated). Returns its length. */
 int q38_last_error(char* buf, size_t n);
 

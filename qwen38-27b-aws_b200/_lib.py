@@ -19,6 +19,7 @@ ERRORS = {-1: "bad argument", -2: "CUDA error", -3: "device wait timed out", -4:
 SIGNATURES = {
     "q38_abi_version": (c_int, []),
     "q38_last_error": (c_int, [ctypes.c_char_p, c_size_t]),
+    "q38_set_pdl": (c_int, [c_int]),
     "q38_device_status": (c_int, [c_int]),
     "q38_fp8_gemm_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int]),
     "q38_fp8_gemm": (

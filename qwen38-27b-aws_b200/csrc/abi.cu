@@ -1,5 +1,7 @@
 // Host-side plumbing of the C ABI: error messages, the device error word, tensor-map encoding.
+#include <atomic>
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 
@@ -30,6 +32,20 @@ EncodeTiledFn encode_fn() {
 }  // namespace
 
 namespace q38host {
+
+namespace {
+std::atomic<int> g_pdl{-1};  // -1: not decided yet (environment), 0 off, 1 on
+}
+
+bool pdl_enabled() {
+  int v = g_pdl.load(std::memory_order_relaxed);
+  if (v < 0) {
+    const char* env = std::getenv("Q38_PDL");
+    v = (env && env[0] == '0') ? 0 : 1;
+    g_pdl.store(v, std::memory_order_relaxed);
+  }
+  return v != 0;
+}
 
 void set_error(const char* fmt, ...) {
   va_list ap;
@@ -69,6 +85,11 @@ int encode_tmap_2d(CUtensorMap* map, const void* base, uint64_t rows, uint64_t c
 }  // namespace q38host
 
 extern "C" int q38_abi_version(void) { return 1; }
+
+extern "C" int q38_set_pdl(int enable) {
+  q38host::g_pdl.store(enable ? 1 : 0, std::memory_order_relaxed);
+  return Q38_OK;
+}
 
 extern "C" int q38_last_error(char* buf, size_t n) {
   const size_t len = strlen(g_last_error);

@@ -149,6 +149,8 @@ __global__ void __launch_bounds__(kThreads, 3) attn_decode_kernel(const __grid_c
   const int g = blockIdx.x, b = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t head_row = static_cast<int64_t>(b) * a.num_kv_heads + g;
+  pdl_wait();
+  pdl_trigger();
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -410,8 +412,8 @@ int launch_attn(const AttnArgs& a, int64_t batch, cudaStream_t stream) {
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return q38host::cuda_status(e, "cudaFuncSetAttribute(attn_decode)");
   dim3 grid(static_cast<unsigned>(a.num_kv_heads), static_cast<unsigned>(batch));
-  attn_decode_kernel<HD, kStages><<<grid, kThreads, smem, stream>>>(tk, tv, a);
-  return q38host::cuda_status(cudaGetLastError(), "attn_decode launch");
+  e = q38host::launch_pdl(attn_decode_kernel<HD, kStages>, grid, dim3(kThreads), smem, stream, tk, tv, a);
+  return q38host::cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "attn_decode launch");
 }
 
 }  // namespace

@@ -208,28 +208,42 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     if (lane == 0) {
       prefetch_tmap(&tmap_x);
-      int issued = 0;
-      for (int i = 0; i < nk; ++i) {
+      // Stage i's weight tile and scales (constant: they may load before the programmatic-launch
+      // wait) and its activation tile (after it). Both CTAs of a pair count on the leader's barrier.
+      auto load_w = [&](int i) {
+        const int s = i % C::STAGES;
+        const int tile_id = mt * a.nkc + kc0 + i;
+        if constexpr (PAIR) {
+          if (prank == 0) mbar_arrive_expect_tx(&full[s], 2 * (C::A_BYTES + C::B_BYTES + C::SF_BYTES));
+          tma_load_2d_pair(sA + s * C::A_BYTES, &tmap_w, &full[s], 0, tile_id * BM);
+          tma_load_2d_pair(sSF + s * SF_BLOCK, &tmap_sf, &full[s], 0, tile_id * 32);
+        } else {
+          mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES + C::SF_BYTES);
+          bulk_load(sA + s * C::A_BYTES, a.w + static_cast<size_t>(tile_id) * C::A_BYTES, C::A_BYTES, &full[s]);
+          if (MX) bulk_load(sSF + s * SF_BLOCK, a.sf + static_cast<size_t>(tile_id) * SF_BLOCK, SF_BLOCK, &full[s]);
+        }
+      };
+      auto load_x = [&](int i) {
+        const int s = i % C::STAGES;
+        const int kx = (kc0 + i) * (MX ? BK_BYTES : BK_BYTES / 2);  // element coordinate along K
+        if constexpr (PAIR) tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0 + prank * C::B_ROWS);
+        else tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0);
+      };
+      // The ring's first pass needs no slot to drain: its weights start before the wait.
+      const int pre = min(nk, C::STAGES);
+      for (int i = 0; i < pre; ++i) load_w(i);
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) load_x(i);
+      int issued = pre;
+      for (int i = pre; i < nk; ++i) {
         const int s = i % C::STAGES;
         const uint32_t ph = (i / C::STAGES) & 1;
         if (flags[0] || !mbar_wait(&empty[s], ph ^ 1)) {
           flags[0] = 1;
           break;
         }
-        const int kx = (kc0 + i) * (MX ? BK_BYTES : BK_BYTES / 2);  // element coordinate along K
-        const int tile_id = mt * a.nkc + kc0 + i;
-        if constexpr (PAIR) {
-          // Both CTAs' bytes land on the leader's barrier; only the leader expects them.
-          if (prank == 0) mbar_arrive_expect_tx(&full[s], 2 * (C::A_BYTES + C::B_BYTES + C::SF_BYTES));
-          tma_load_2d_pair(sA + s * C::A_BYTES, &tmap_w, &full[s], 0, tile_id * BM);
-          tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0 + prank * C::B_ROWS);
-          tma_load_2d_pair(sSF + s * SF_BLOCK, &tmap_sf, &full[s], 0, tile_id * 32);
-        } else {
-          mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES + C::SF_BYTES);
-          bulk_load(sA + s * C::A_BYTES, a.w + static_cast<size_t>(tile_id) * C::A_BYTES, C::A_BYTES, &full[s]);
-          tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0);
-          if (MX) bulk_load(sSF + s * SF_BLOCK, a.sf + static_cast<size_t>(tile_id) * SF_BLOCK, SF_BLOCK, &full[s]);
-        }
+        load_w(i);
+        load_x(i);
         issued = i + 1;
       }
       // Never leave with copies in flight: wait (bounded) for the last load of every stage. (A pair's
@@ -294,11 +308,16 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else if (a.cluster > 0) {
-    // Epilogue part 1. With one split the accumulator goes straight to its bf16 staging; with a cluster of splits it goes to shared memory as fp32 [token][row] for part
-    // 2. The residual tile of this CTA's token slice starts loading by TMA meanwhile.
+    // Epilogue part 1. With one split the accumulator goes straight to its bf16 staging; with a
+    // cluster of splits it goes to shared memory as fp32 [token][row] for part 2. The residual tile of
+    // this CTA's token slice starts loading by TMA meanwhile.
     const int q = warp & 3;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    pdl_wait();
     const bool ok = mbar_wait(accf, 0);
+    // The mainloop is done: the next kernel may launch its prologue. Never from the all-reduce, whose
+    // CTAs must all find room on the GPU while peers wait on them.
+    if (a.epilogue != EPI_ALLREDUCE) pdl_trigger();
     tc_fence_after();
     if (!ok || flags[0]) {
       flags[0] = 1;
@@ -345,10 +364,12 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31 (its hardware lane quarter).
+    pdl_wait();
     const int q = warp & 3;
     const int row = m0 + q * 32 + lane;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
     const bool ok = mbar_wait(accf, 0);
+    pdl_trigger();
     tc_fence_after();
     if (!ok || flags[0]) {
       flags[0] = 1;
@@ -656,31 +677,53 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     if (lane == 0) {
       prefetch_tmap(&tmap_x);
+      // Ring slot `it` for K step i of weight tile mt: the weight tile and scales (constant, so they
+      // may load before the programmatic-launch wait), then the activation tile.
+      auto load_w = [&](int it, int mt, int i) {
+        const int s = it % C::STAGES;
+        const int tile_id = mt * a.nkc + i;
+        if constexpr (PAIR) {
+          if (prank == 0) mbar_arrive_expect_tx(&full[s], 2 * (C::A_BYTES + C::B_BYTES + C::SF_BYTES));
+          tma_load_2d_pair(sA + s * C::A_BYTES, &tmap_w, &full[s], 0, tile_id * BM);
+          tma_load_2d_pair(sSF + s * SF_BLOCK, &tmap_sf, &full[s], 0, tile_id * 32);
+        } else {
+          mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES + C::SF_BYTES);
+          bulk_load(sA + s * C::A_BYTES, a.w + static_cast<size_t>(tile_id) * C::A_BYTES, C::A_BYTES, &full[s]);
+          if (MX) bulk_load(sSF + s * SF_BLOCK, a.sf + static_cast<size_t>(tile_id) * SF_BLOCK, SF_BLOCK, &full[s]);
+        }
+      };
+      auto load_x = [&](int it, int n0, int i) {
+        const int s = it % C::STAGES;
+        const int kx = i * (MX ? BK_BYTES : BK_BYTES / 2);
+        if constexpr (PAIR) tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0 + prank * C::B_ROWS);
+        else tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0);
+      };
+      // The first pass over the ring needs no slot to drain: the first tile's weights go first.
+      int pre = 0;
+      if (group < units) {
+        const int mt = PAIR ? 2 * (group % m_units) + prank : group % m_units;
+        pre = min(nk, C::STAGES);
+        for (int i = 0; i < pre; ++i) load_w(i, mt, i);
+      }
+      pdl_wait();
       int it = 0;
       for (int u = group; u < units && !flags[0]; u += ngroups) {
         const int mp = u % m_units, nt = u / m_units;
         const int mt = PAIR ? 2 * mp + prank : mp;
         const int n0 = nt * NTOK;
         for (int i = 0; i < nk; ++i, ++it) {
+          if (it < pre) {
+            load_x(it, n0, i);
+            continue;
+          }
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
           if (flags[0] || !mbar_wait(&empty[s], ph ^ 1)) {
             flags[0] = 1;
             break;
           }
-          const int kx = i * (MX ? BK_BYTES : BK_BYTES / 2);
-          const int tile_id = mt * a.nkc + i;
-          if constexpr (PAIR) {
-            if (prank == 0) mbar_arrive_expect_tx(&full[s], 2 * (C::A_BYTES + C::B_BYTES + C::SF_BYTES));
-            tma_load_2d_pair(sA + s * C::A_BYTES, &tmap_w, &full[s], 0, tile_id * BM);
-            tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0 + prank * C::B_ROWS);
-            tma_load_2d_pair(sSF + s * SF_BLOCK, &tmap_sf, &full[s], 0, tile_id * 32);
-          } else {
-            mbar_arrive_expect_tx(&full[s], C::A_BYTES + C::B_BYTES + C::SF_BYTES);
-            bulk_load(sA + s * C::A_BYTES, a.w + static_cast<size_t>(tile_id) * C::A_BYTES, C::A_BYTES, &full[s]);
-            tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0);
-            if (MX) bulk_load(sSF + s * SF_BLOCK, a.sf + static_cast<size_t>(tile_id) * SF_BLOCK, SF_BLOCK, &full[s]);
-          }
+          load_w(it, mt, i);
+          load_x(it, n0, i);
         }
       }
       // Never leave with copies in flight: wait (bounded) for the last load of every stage.
@@ -756,6 +799,7 @@ __global__ void __launch_bounds__(192, 1)
     const int r = q * 32 + lane;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
     __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(sOut);
+    pdl_wait();
     int tc = 0;
     for (int u = group; u < units; u += ngroups, ++tc) {
       const int mp = u % m_units, nt = u / m_units;
@@ -766,6 +810,7 @@ __global__ void __launch_bounds__(192, 1)
         if (threadIdx.x == 64) flags[0] = 1;
         break;
       }
+      if (u + ngroups >= units) pdl_trigger();  // this CTA's last mainloop is done
       tc_fence_after();
       // The previous tile's store has finished reading the staging buffer.
       if (threadIdx.x == 64) bulk_wait_read0();
@@ -872,13 +917,13 @@ int launch_persistent(const CUtensorMap& tx, const CUtensorMap& ty, const CUtens
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = PAIR ? 2u : 1u;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = q38host::add_pdl(attr, 1);
   e = cudaLaunchKernelEx(&cfg, gemm_persistent_kernel<NTOK, MX, PAIR>, tx, ty, tw, tsf, a);
   return q38host::cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "persistent gemm launch");
 }
@@ -903,7 +948,7 @@ int launch_gemm(const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap&
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = PAIR ? 2u : 1u;
   attr[0].val.clusterDim.y = 1;
@@ -922,6 +967,7 @@ int launch_gemm(const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap&
                                 csize, clusters),
              Q38_ERR_UNSUPPORTED;
   }
+  cfg.numAttrs = q38host::add_pdl(attr, 1);
   e = cudaLaunchKernelEx(&cfg, gemm_kernel<NTOK, MX, PAIR>, tx, ty, tr, tw ? *tw : tx, tsf ? *tsf : tx, a);
   return q38host::cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "gemm launch");
 }

@@ -47,6 +47,8 @@ __global__ void __launch_bounds__(DK) gdn_qk_kernel(GdnArgs a, float* qk) {
   constexpr int KCONV = 4;
   constexpr int NW = DK / 32;
   __shared__ float part[2][NW];
+  pdl_wait();
+  pdl_trigger();
   const int kh = blockIdx.x, b = blockIdx.y, i = threadIdx.x, warp = i >> 5, lane = i & 31;
   const int pos = a.position[b];
   const bool on = a.active[b] > 0.5f;
@@ -127,6 +129,8 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(GdnArgs a, const float*
   __nv_bfloat16* zs = nws + DV;                                      // [DV] z
   uint64_t* bar = reinterpret_cast<uint64_t*>((reinterpret_cast<uintptr_t>(zs + DV) + 7) & ~uintptr_t(7));
 
+  pdl_wait();
+  pdl_trigger();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int h = blockIdx.x, b = blockIdx.y;
   const int R = a.num_v_heads / a.num_k_heads;
@@ -182,6 +186,10 @@ __global__ void __launch_bounds__(128) gdn_decode_kernel(GdnArgs a, const float*
     graw[2] = __bfloat162float(a.a_log[h]);
     graw[3] = __bfloat162float(a.dt_bias[h]);
   }
+  // Thread 0's barrier initialisation is visible to every thread before any waits on it (an mbarrier
+  // must be initialised before any other operation on it; the shared memory may still hold a previous
+  // CTA's data).
+  __syncthreads();
   // v conv + SiLU for this head's DV channels; the conv state moves on.
 #pragma unroll
   for (int v = 0; v < VN; ++v) {
@@ -307,11 +315,12 @@ int launch_gdn(const GdnArgs& a, int64_t batch, float* qk, cudaStream_t stream) 
     if (e != cudaSuccess) return q38host::cuda_status(e, "cudaFuncSetAttribute(gdn_decode)");
     done_mask |= 1ull << dev;
   }
-  gdn_qk_kernel<DK><<<dim3(a.num_k_heads, static_cast<unsigned>(batch)), DK, 0, stream>>>(a, qk);
-  e = cudaGetLastError();
+  e = q38host::launch_pdl(gdn_qk_kernel<DK>, dim3(a.num_k_heads, static_cast<unsigned>(batch)), dim3(DK), 0, stream, a,
+                          qk);
   if (e != cudaSuccess) return q38host::cuda_status(e, "gdn_qk launch");
-  gdn_decode_kernel<DK, DV><<<dim3(a.num_v_heads, static_cast<unsigned>(batch)), 128, S::TOTAL, stream>>>(a, qk);
-  return q38host::cuda_status(cudaGetLastError(), "gdn_decode launch");
+  e = q38host::launch_pdl(gdn_decode_kernel<DK, DV>, dim3(a.num_v_heads, static_cast<unsigned>(batch)), dim3(128),
+                          S::TOTAL, stream, a, static_cast<const float*>(qk));
+  return q38host::cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "gdn_decode launch");
 }
 
 }  // namespace

@@ -146,22 +146,41 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       prefetch_tmap(&tmap_x);
       prefetch_tmap(&tmap_w);
+      // Both CTAs' bytes land on the leader's barrier. A weight tile past the vocabulary (odd tile
+      // count) reads as zeros and its groups are never stored. The first unit's first ring pass of
+      // weights (constant) starts before the programmatic-launch wait; activations follow it.
+      auto load_w = [&](int it, int mt, int i) {
+        const int s = it % C::STAGES;
+        if (prank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE_BYTES);
+        tma_load_2d_pair(sA + s * C::A_BYTES, &tmap_w, &full[s], 0, (mt * nk + i) * BM);
+      };
+      auto load_x = [&](int it, int n0, int i) {
+        const int s = it % C::STAGES;
+        tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_x, &full[s], i * KSTEP, n0 + prank * C::B_ROWS);
+      };
+      int pre = 0;
+      if (group < units) {
+        pre = min(nk, C::STAGES);
+        for (int i = 0; i < pre; ++i) load_w(i, 2 * (group / n_tiles) + prank, i);
+      }
+      pdl_wait();
       int it = 0;
       for (int u = group; u < units && !flags[0]; u += ngroups) {
         const int mt = 2 * (u / n_tiles) + prank;
         const int n0 = (u % n_tiles) * NTOK;
         for (int i = 0; i < nk; ++i, ++it) {
+          if (it < pre) {
+            load_x(it, n0, i);
+            continue;
+          }
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
           if (flags[0] || !mbar_wait(&empty[s], ph ^ 1)) {
             flags[0] = 1;
             break;
           }
-          // Both CTAs' bytes land on the leader's barrier. A weight tile past the vocabulary (odd tile
-          // count) reads as zeros and its groups are never stored.
-          if (prank == 0) mbar_arrive_expect_tx(&full[s], 2 * C::STAGE_BYTES);
-          tma_load_2d_pair(sA + s * C::A_BYTES, &tmap_w, &full[s], 0, (mt * nk + i) * BM);
-          tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_x, &full[s], i * KSTEP, n0 + prank * C::B_ROWS);
+          load_w(it, mt, i);
+          load_x(it, n0, i);
         }
       }
       // Never leave with copies in flight: wait (bounded) for the last load of every stage.
@@ -206,6 +225,7 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // Epilogue: warp w reads TMEM lanes 32*(w%4) .. +31, i.e. vocabulary group mt*4 + w%4.
     const int q = warp & 3;
+    pdl_wait();
     int tc = 0;
     for (int u = group; u < units; u += ngroups, ++tc) {
       const int b = tc & 1;
@@ -215,6 +235,7 @@ __global__ void __launch_bounds__(192, 1)
         flags[0] = 1;
         break;
       }
+      if (u + ngroups >= units) pdl_trigger();  // this CTA's last mainloop is done
       tc_fence_after();
       const int g = mt * 4 + q;
       if (g * 32 < a.F) {
@@ -266,13 +287,13 @@ int launch_head(const CUtensorMap& tx, const CUtensorMap& tw, const HeadArgs& a,
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = C::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = q38host::add_pdl(attr, 1);
   e = cudaLaunchKernelEx(&cfg, lm_head_kernel<NTOK>, tx, tw, a);
   return q38host::cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "lm_head launch");
 }

@@ -15,13 +15,15 @@ union Pack8 {
   __nv_bfloat16 h[8];
 };
 
-// One CTA per row. Two passes over the row: sum of squares, then scale. The second read of the
-// row hits L1/L2.
+// Rows too long for registers: one CTA per row, two passes over the row (sum of squares, then scale;
+// the second read hits L1/L2).
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                                                       const __nv_bfloat16* __restrict__ w, int n,
                                                                       float eps, __nv_bfloat16* __restrict__ y,
                                                                       int64_t ldy, uint8_t* __restrict__ q,
                                                                       int64_t ldq) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   const __nv_bfloat16* xr = x + row * ldx;
   const int chunks = n / 8;
@@ -52,6 +54,71 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_quant_kernel(const __nv_
     for (int i = 0; i < 8; ++i) {
       const float scaled = __fmul_rn(__bfloat162float(p.h[i]), r);
       h[i] = bf16r(__fmul_rn(scaled, __fadd_rn(1.0f, __bfloat162float(pw.h[i]))));
+      out.h[i] = __float2bfloat16_rn(h[i]);
+    }
+    if (y) *reinterpret_cast<uint4*>(y + row * ldy + c * 8) = out.u;
+    if (q) {
+      uint2 o;
+      o.x = pack4_e5m2(h[0], h[1], h[2], h[3]);
+      o.y = pack4_e5m2(h[4], h[5], h[6], h[7]);
+      *reinterpret_cast<uint2*>(q + row * ldq + c * 8) = o;
+    }
+  }
+}
+
+// One CTA of kRegThreads per row with the whole row in registers: each thread loads its PER 8-column
+// chunks of x and of the weight in one batch (a single round trip), then the sum of squares, one block
+// reduction, and the outputs from registers.
+constexpr int kRegThreads = 128;
+
+template <int PER>
+__global__ void __launch_bounds__(kRegThreads) rmsnorm_quant_reg_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                                       const __nv_bfloat16* __restrict__ w, int n,
+                                                                       float eps, __nv_bfloat16* __restrict__ y,
+                                                                       int64_t ldy, uint8_t* __restrict__ q, int64_t ldq) {
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * ldx;
+  const int chunks = n / 8;
+  Pack8 px[PER], pw[PER];
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int c = threadIdx.x + k * kRegThreads;
+    if (c < chunks) {
+      px[k].u = *reinterpret_cast<const uint4*>(xr + c * 8);
+      pw[k].u = *reinterpret_cast<const uint4*>(w + c * 8);
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    if (threadIdx.x + k * kRegThreads < chunks) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float f = __bfloat162float(px[k].h[i]);
+        ss += f * f;
+      }
+    }
+  }
+  __shared__ float red[kRegThreads / 32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRegThreads / 32; ++i) total += red[i];
+  const float r = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
+#pragma unroll
+  for (int k = 0; k < PER; ++k) {
+    const int c = threadIdx.x + k * kRegThreads;
+    if (c >= chunks) continue;
+    Pack8 out;
+    float h[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float scaled = __fmul_rn(__bfloat162float(px[k].h[i]), r);
+      h[i] = bf16r(__fmul_rn(scaled, __fadd_rn(1.0f, __bfloat162float(pw[k].h[i]))));
       out.h[i] = __float2bfloat16_rn(h[i]);
     }
     if (y) *reinterpret_cast<uint4*>(y + row * ldy + c * 8) = out.u;
@@ -99,10 +166,28 @@ extern "C" int q38_rmsnorm_quant(const void* x, int64_t ldx, const void* w, int6
   if (!al16(x) || !al16(w) || (y_bf16 && !al16(y_bf16)) || (y_e5m2 && reinterpret_cast<uintptr_t>(y_e5m2) % 8) ||
       ldx % 8 || (y_bf16 && ldy % 8) || (y_e5m2 && ldq % 8))
     return set_error("q38_rmsnorm_quant: misaligned pointer or leading dimension"), Q38_ERR_ARG;
-  rmsnorm_quant_kernel<<<static_cast<unsigned>(rows), kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w), static_cast<int>(n), eps,
-      static_cast<__nv_bfloat16*>(y_bf16), ldy, static_cast<uint8_t*>(y_e5m2), ldq);
-  return cuda_status(cudaGetLastError(), "rmsnorm_quant launch");
+  const auto* xb = static_cast<const __nv_bfloat16*>(x);
+  const auto* wb = static_cast<const __nv_bfloat16*>(w);
+  auto* yb = static_cast<__nv_bfloat16*>(y_bf16);
+  auto* qb = static_cast<uint8_t*>(y_e5m2);
+  const unsigned grid = static_cast<unsigned>(rows);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int per = static_cast<int>((n / 8 + kRegThreads - 1) / kRegThreads);
+  const int ni = static_cast<int>(n);
+  cudaError_t e = cudaSuccess;
+  switch (per) {  // rows up to 8 * 128 * 8 = 8192 columns live in registers
+    case 1: e = launch_pdl(rmsnorm_quant_reg_kernel<1>, dim3(grid), dim3(kRegThreads), 0, s, xb, ldx, wb, ni, eps, yb, ldy, qb, ldq); break;
+    case 2: e = launch_pdl(rmsnorm_quant_reg_kernel<2>, dim3(grid), dim3(kRegThreads), 0, s, xb, ldx, wb, ni, eps, yb, ldy, qb, ldq); break;
+    case 3: e = launch_pdl(rmsnorm_quant_reg_kernel<3>, dim3(grid), dim3(kRegThreads), 0, s, xb, ldx, wb, ni, eps, yb, ldy, qb, ldq); break;
+    case 4: e = launch_pdl(rmsnorm_quant_reg_kernel<4>, dim3(grid), dim3(kRegThreads), 0, s, xb, ldx, wb, ni, eps, yb, ldy, qb, ldq); break;
+    case 5: e = launch_pdl(rmsnorm_quant_reg_kernel<5>, dim3(grid), dim3(kRegThreads), 0, s, xb, ldx, wb, ni, eps, yb, ldy, qb, ldq); break;
+    case 6:
+    case 7:
+    case 8: e = launch_pdl(rmsnorm_quant_reg_kernel<8>, dim3(grid), dim3(kRegThreads), 0, s, xb, ldx, wb, ni, eps, yb, ldy, qb, ldq); break;
+    default:
+      e = launch_pdl(rmsnorm_quant_kernel, dim3(grid), dim3(kNormThreads), 0, s, xb, ldx, wb, ni, eps, yb, ldy, qb, ldq);
+  }
+  return cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "rmsnorm_quant launch");
 }
 
 extern "C" int q38_silu_mul_quant(const void* gu, int64_t ld, int64_t rows, int64_t n, void* y_e5m2, int64_t ldy,

@@ -300,6 +300,17 @@ __device__ __forceinline__ float silu_mul_bf16(float g, float u) {
 // softplus with the threshold torch uses (beta 1, threshold 20).
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
+// ----------------------------------------------------------------------------------------------
+// Programmatic dependent launch. A kernel launched with the programmatic-serialization attribute
+// (q38host::launch_attrs) may start while the previous kernel in the stream drains: it must call
+// pdl_wait() before it reads anything an earlier kernel wrote or writes anything an earlier kernel
+// reads (loads of constant weights may come first), and every CTA waits before it exits, so that
+// "this grid completed" still implies "every earlier grid completed". pdl_trigger() lets the next
+// kernel's CTAs launch and run their own prologue.
+// ----------------------------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -317,6 +328,32 @@ __device__ __forceinline__ float warp_max(float v) {
 namespace q38host {
 void set_error(const char* fmt, ...);
 int cuda_status(cudaError_t e, const char* what);
+// Programmatic dependent launch for the kernels that call pdl_wait (on unless q38_set_pdl(0) or the
+// environment variable Q38_PDL=0).
+bool pdl_enabled();
+// Appends the programmatic-serialization attribute when enabled; returns the new attribute count.
+inline unsigned add_pdl(cudaLaunchAttribute* attrs, unsigned n) {
+  if (pdl_enabled()) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  return n;
+}
+// Launches a kernel that calls pdl_wait (no cluster) with the programmatic-serialization attribute.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  cfg.numAttrs = add_pdl(attrs, 0);
+  cfg.attrs = attrs;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Args&&>(args)...);
+}
 // Encodes a 2D tensor map over a row-major [rows, cols] matrix (`elem_bytes` per element, rows
 // `ld` elements apart; ld 0 means cols), box [box_rows, box_cols], 128-byte swizzle or none.
 // Returns Q38_OK or an error code.
