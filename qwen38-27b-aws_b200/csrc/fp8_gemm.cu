@@ -337,23 +337,23 @@ __global__ void __launch_bounds__(192, 1)
       const int r = q * 32 + lane;
       if (a.cluster > 1) {
         float* part = reinterpret_cast<float*>(smem);
-        for (int c = 0; c < NTOK; c += 16) {
+        for (int c = 0; c < NTOK; c += 64) {
           if (n0 + c >= a.T) break;
-          float v[16];
-          tmem_ld16(taddr + c, v);
+          float v[64];
+          tmem_ld64(taddr + c, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) part[(c + j) * BM + r] = v[j];
+          for (int j = 0; j < 64; ++j) part[(c + j) * BM + r] = v[j];
         }
       } else if (m0 < a.F) {
         // Lanes are consecutive rows: a warp's stores of one token fill 64 contiguous bytes.
         if (a.epilogue == EPI_RESIDUAL && !mbar_wait(resbar, 0)) flags[0] = 1;
         __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stage);
-        for (int c = 0; c < NTOK; c += 16) {
+        for (int c = 0; c < NTOK; c += 64) {
           if (n0 + c >= a.T) break;
-          float v[16];
-          tmem_ld16(taddr + c, v);
+          float v[64];
+          tmem_ld64(taddr + c, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
+          for (int j = 0; j < 64; ++j) {
             const int idx = (c + j) * BM + r;
             float out = bf16r(v[j]);
             if (a.epilogue == EPI_RESIDUAL) out = __bfloat162float(st[idx]) + out;
@@ -374,11 +374,17 @@ __global__ void __launch_bounds__(192, 1)
     if (!ok || flags[0]) {
       flags[0] = 1;
     } else if (a.splits == 1) {
-      for (int c = 0; c < NTOK; c += 16) {
+      for (int c = 0; c < NTOK; c += 64) {
         if (n0 + c >= a.T) break;
-        float v[16];
-        tmem_ld16(taddr + c, v);
-        epilogue16(a, row, n0 + c, v, lane);
+        float v[64];
+        tmem_ld64(taddr + c, v);
+#pragma unroll
+        for (int k = 0; k < 64; k += 16) {
+          float w[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) w[j] = v[k + j];
+          epilogue16(a, row, n0 + c + k, w, lane);
+        }
       }
     } else {
       const int tiles = gridDim.x * gridDim.y;
@@ -386,13 +392,18 @@ __global__ void __launch_bounds__(192, 1)
       // Partial tile layout [16-token chunk][128 rows][16 tokens]: a warp's 32 rows of one chunk are
       // 2 KB contiguous.
       float* part = a.ws + (static_cast<size_t>(split) * tiles + tile) * BM * NTOK + static_cast<size_t>(q * 32 + lane) * 16;
-      for (int c = 0; c < NTOK; c += 16) {
+      for (int c = 0; c < NTOK; c += 64) {
         if (n0 + c >= a.T) break;
-        float v[16];
-        tmem_ld16(taddr + c, v);
-        float* dst = part + static_cast<size_t>(c / 16) * BM * 16;
+        float v[64];
+        tmem_ld64(taddr + c, v);
 #pragma unroll
-        for (int j = 0; j < 16; j += 4) __stcg(reinterpret_cast<float4*>(dst + j), make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]));
+        for (int k = 0; k < 64; k += 16) {
+          if (n0 + c + k >= a.T) break;
+          float* dst = part + static_cast<size_t>((c + k) / 16) * BM * 16;
+#pragma unroll
+          for (int j = 0; j < 16; j += 4)
+            __stcg(reinterpret_cast<float4*>(dst + j), make_float4(v[k + j], v[k + j + 1], v[k + j + 2], v[k + j + 3]));
+        }
       }
       __threadfence();
       epi_bar();
@@ -822,12 +833,12 @@ __global__ void __launch_bounds__(192, 1)
         __nv_bfloat16* sg = st;                 // [NTOK][64]
         __nv_bfloat16* su = st + NTOK * 64;     // [NTOK][64]
         __nv_bfloat16* dst = r < 64 ? sg : su;
-        for (int c = 0; c < NTOK; c += 16) {
+        for (int c = 0; c < NTOK; c += 64) {
           if (n0 + c >= a.T) break;
-          float v[16];
-          tmem_ld16(taddr + c, v);
+          float v[64];
+          tmem_ld64(taddr + c, v);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) dst[(c + j) * 64 + (r & 63)] = __float2bfloat16_rn(v[j]);
+          for (int j = 0; j < 64; ++j) dst[(c + j) * 64 + (r & 63)] = __float2bfloat16_rn(v[j]);
         }
         tc_fence_before();
         epi_bar();
@@ -856,12 +867,12 @@ __global__ void __launch_bounds__(192, 1)
         }
         continue;
       }
-      for (int c = 0; c < NTOK; c += 16) {
+      for (int c = 0; c < NTOK; c += 64) {
         if (n0 + c >= a.T) break;
-        float v[16];
-        tmem_ld16(taddr + c, v);
+        float v[64];
+        tmem_ld64(taddr + c, v);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) st[(c + j) * BM + r] = __float2bfloat16_rn(v[j]);
+        for (int j = 0; j < 64; ++j) st[(c + j) * BM + r] = __float2bfloat16_rn(v[j]);
       }
       // Every TMEM read of this tile is complete: hand the accumulator back to the MMA warp.
       tc_fence_before();

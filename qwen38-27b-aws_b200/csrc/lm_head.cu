@@ -61,22 +61,6 @@ __device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, ui
       : "memory");
 }
 
-// A warp reads 32 consecutive fp32 columns of its own 32 TMEM lanes.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
 // v[c] is lane i's value of column c (i = a vocabulary row of the group, c = a batch row). Returns,
 // in lane j, the maximum over all 32 lanes of column j: each halving step trades the half of the
 // columns this lane gives up for its partner's copy of the half it keeps (16 + 8 + 4 + 2 + 1 shuffles).
@@ -241,12 +225,18 @@ __global__ void __launch_bounds__(192, 1)
       if (g * 32 < a.F) {
         const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * NTOK);
 #pragma unroll 1
-        for (int c = 0; c < NTOK && n0 + c < a.T; c += 32) {
-          float v[32];
-          tmem_ld32(taddr + c, v);
-          const float m = transpose_max32(v, lane);
-          const int t = n0 + c + lane;
-          if (t < a.T) a.maxima[static_cast<int64_t>(t) * a.ldm + g] = m;
+        for (int c = 0; c < NTOK && n0 + c < a.T; c += 64) {
+          float v[64];
+          tmem_ld64(taddr + c, v);  // one TMEM round trip per 64 columns
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            float w[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = v[half * 32 + j];
+            const float m = transpose_max32(w, lane);
+            const int t = n0 + c + half * 32 + lane;
+            if (t < a.T) a.maxima[static_cast<int64_t>(t) * a.ldm + g] = m;
+          }
         }
       }
       // This warp's reads of the accumulator are complete: one arrival per warp on the leader's barrier.
