@@ -450,9 +450,10 @@ __global__ void __launch_bounds__(192, 1)
       cluster_sync();
       // Epilogue part 2: this CTA's slice of 32-token blocks, summed over the cluster's partials in
       // rank order (deterministic), then the epilogue; lane l handles rows 4l .. 4l+3 of a token. A
-      // warp keeps U tokens' loads in flight per source so the reduction is not load-latency bound.
+      // warp issues U tokens' loads from up to SB sources before it adds any of them, so one round
+      // trip of distributed shared memory covers SB x U loads (the reduction is latency-bound).
       if (warp >= 2 && !flags[0]) {
-        constexpr int U = 8, NW = 4;
+        constexpr int U = 8, NW = 4, SB = 4;
         const int t0 = n0 + b0 * TOK_BLOCK;
         const int t1 = min(a.T, n0 + b1 * TOK_BLOCK);
         const bool ok = a.epilogue != EPI_RESIDUAL || t0 >= t1 || !live || mbar_wait(resbar, 0);
@@ -462,7 +463,33 @@ __global__ void __launch_bounds__(192, 1)
           float4 acc[U];
 #pragma unroll
           for (int u = 0; u < U; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-          for (int src = 0; src < a.cluster; ++src) {
+          // Sources 0 .. SB-1: every load first, then the sums in rank order.
+          {
+            float4 p[SB][U];
+#pragma unroll
+            for (int src = 0; src < SB; ++src) {
+              const uint32_t peer = PAIR ? static_cast<uint32_t>(prank + 2 * src) : static_cast<uint32_t>(src);
+#pragma unroll
+              for (int u = 0; u < U; ++u) {
+                const int t = tb + NW * u;
+                p[src][u] = src < a.cluster && t < t1
+                                ? ld_cluster_f4(cluster_map(part0 + static_cast<uint32_t>((t - n0) * BM * 4), peer))
+                                : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+            }
+#pragma unroll
+            for (int src = 0; src < SB; ++src) {
+              if (src >= a.cluster) break;
+#pragma unroll
+              for (int u = 0; u < U; ++u) {
+                acc[u].x += p[src][u].x;
+                acc[u].y += p[src][u].y;
+                acc[u].z += p[src][u].z;
+                acc[u].w += p[src][u].w;
+              }
+            }
+          }
+          for (int src = SB; src < a.cluster; ++src) {
             const uint32_t peer = PAIR ? static_cast<uint32_t>(prank + 2 * src) : static_cast<uint32_t>(src);
             float4 p[U];
 #pragma unroll
