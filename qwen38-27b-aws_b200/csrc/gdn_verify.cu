@@ -80,13 +80,17 @@ __device__ __forceinline__ void verify_conv_channel(const VerifyArgs& a, int b, 
   float cw[KCONV];
 #pragma unroll
   for (int j = 0; j < KCONV; ++j) cw[j] = __bfloat162float(a.conv_w[static_cast<int64_t>(c) * KCONV + j]);
+  // Every token's input is loaded before the pending buffer is overwritten (one round trip, not K).
+  __nv_bfloat16 xin[KMAX];
+#pragma unroll
+  for (int t = 0; t < KMAX; ++t)
+    if (t < K) xin[t] = a.qkvz[(static_cast<int64_t>(b) * K + t) * a.ld_qkvz + c];
 #pragma unroll
   for (int t = 0; t < KMAX; ++t) {
     w2[KCONV - 1 + t] = 0.f;
     if (t < K) {
-      const __nv_bfloat16 xin = a.qkvz[(static_cast<int64_t>(b) * K + t) * a.ld_qkvz + c];
-      w2[KCONV - 1 + t] = __bfloat162float(xin);
-      a.pending_input[(static_cast<int64_t>(b) * K + t) * conv_dim + c] = xin;
+      w2[KCONV - 1 + t] = __bfloat162float(xin[t]);
+      a.pending_input[(static_cast<int64_t>(b) * K + t) * conv_dim + c] = xin[t];
     }
   }
 #pragma unroll
@@ -220,11 +224,34 @@ __global__ void __launch_bounds__(128) gdn_verify_kernel(VerifyArgs a, const flo
   // The head's v channels: history, the K tokens' conv and SiLU, conv state and pending inputs.
   for (int i = tid; i < DV; i += 128)
     verify_conv_channel(a, b, 2 * key_dim + h * DV + i, conv_dim, K, acc, on, keep, xv + i, DV);
-  // This key head's normalised q and k of the K tokens.
-  const float* src = qk + (static_cast<int64_t>(b) * a.num_k_heads + kh) * K * 2 * DK;
-  for (int i = tid; i < K * 2 * DK; i += 128) {
-    const int t = i / (2 * DK), which = (i / DK) & 1, e = i % DK;
-    (which ? kn : qn)[t * DK + e] = src[i];
+  // This key head's normalised q and k of the K tokens, and this head's pending slices (read before
+  // this step replaces them): 16-byte loads into registers first, stores after, one round trip.
+  constexpr int QKV4 = (KMAX * 2 * DK / 4 + 127) / 128;       // float4 of q / k per thread
+  constexpr int PV4 = (KMAX * (DK + DV) / 4 + 127) / 128;     // float4 of pending key / delta per thread
+  const float4* src4 = reinterpret_cast<const float4*>(qk + (static_cast<int64_t>(b) * a.num_k_heads + kh) * K * 2 * DK);
+  float4 rqk[QKV4], rpd[PV4];
+#pragma unroll
+  for (int j = 0; j < QKV4; ++j) {
+    const int i4 = tid + 128 * j;
+    if (i4 < K * 2 * DK / 4) rqk[j] = src4[i4];
+  }
+#pragma unroll
+  for (int j = 0; j < PV4; ++j) {
+    const int i4 = tid + 128 * j;
+    if (i4 < K * (DK + DV) / 4) {
+      const int s2 = i4 / ((DK + DV) / 4), e = (i4 % ((DK + DV) / 4)) * 4;
+      const int64_t base = (static_cast<int64_t>(b) * K + s2) * a.num_v_heads + h;
+      rpd[j] = e < DK ? *reinterpret_cast<const float4*>(a.pending_key + base * DK + e)
+                      : *reinterpret_cast<const float4*>(a.pending_delta + base * DV + (e - DK));
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < QKV4; ++j) {
+    const int i4 = tid + 128 * j;
+    if (i4 < K * 2 * DK / 4) {
+      const int i = i4 * 4, t = i / (2 * DK), which = (i / DK) & 1, e = i % DK;
+      *reinterpret_cast<float4*>((which ? kn : qn) + t * DK + e) = rqk[j];
+    }
   }
   // Gates per token: beta = bf16(sigmoid(b)) * active, g = -exp(A_log) * softplus(a + dt_bias) * active.
   if (tid < K) {
@@ -236,12 +263,20 @@ __global__ void __launch_bounds__(128) gdn_verify_kernel(VerifyArgs a, const flo
         __fmul_rn(-expf(__bfloat162float(a.a_log[h])), softplusf_(__fadd_rn(araw, __bfloat162float(a.dt_bias[h])))), act);
   }
   __syncthreads();  // commit factors, v, q, k, gates
-  // The pending slices of this head (read before this step replaces them), weighted for the commit.
-  for (int i = tid; i < K * (DK + DV); i += 128) {
-    const int s = i / (DK + DV), e = i % (DK + DV);
-    const int64_t base = (static_cast<int64_t>(b) * K + s) * a.num_v_heads + h;
-    if (e < DK) wk[s * DK + e] = __fmul_rn(a.pending_key[base * DK + e], fw[s]);
-    else dl[s * DV + (e - DK)] = a.pending_delta[base * DV + (e - DK)];
+  // The pending slices, weighted for the commit.
+#pragma unroll
+  for (int j = 0; j < PV4; ++j) {
+    const int i4 = tid + 128 * j;
+    if (i4 < K * (DK + DV) / 4) {
+      const int s2 = i4 / ((DK + DV) / 4), e = (i4 % ((DK + DV) / 4)) * 4;
+      if (e < DK) {
+        const float f = fw[s2];
+        *reinterpret_cast<float4*>(wk + s2 * DK + e) =
+            make_float4(__fmul_rn(rpd[j].x, f), __fmul_rn(rpd[j].y, f), __fmul_rn(rpd[j].z, f), __fmul_rn(rpd[j].w, f));
+      } else {
+        *reinterpret_cast<float4*>(dl + s2 * DV + (e - DK)) = rpd[j];
+      }
+    }
   }
   // k_t . k_s (s < t) and q_t . k_s (s <= t), one warp per dot.
   for (int p = warp; p < 2 * K * K; p += 4) {
