@@ -299,16 +299,26 @@ __global__ void __launch_bounds__(128) gdn_verify_kernel(VerifyArgs a, const flo
   for (int t = 0; t < 2 * KMAX; ++t)
 #pragma unroll
     for (int e = 0; e < CPL; ++e) prod[t][e] = 0.f;
+  // This thread's columns of the pending deltas are the same for every row: registers.
+  float dlr[KMAX][CPL];
+#pragma unroll
+  for (int s = 0; s < KMAX; ++s)
+#pragma unroll
+    for (int e = 0; e < CPL; ++e) dlr[s][e] = s < K ? dl[s * DV + c0 + e] : 0.f;
+#pragma unroll 4
   for (int r = 0; r < ROWS_W; ++r) {
     const int i = warp * ROWS_W + r;
     float sv[CPL];
     load_row<CPL>(tile + i * DV + c0, sv);
+    float wki[KMAX];
+#pragma unroll
+    for (int s = 0; s < KMAX; ++s) wki[s] = s < K ? wk[s * DK + i] : 0.f;
 #pragma unroll
     for (int e = 0; e < CPL; ++e) {
       float w = 0.f;
 #pragma unroll
       for (int s = 0; s < KMAX; ++s)
-        if (s < K) w = fmaf(wk[s * DK + i], dl[s * DV + c0 + e], w);
+        if (s < K) w = fmaf(wki[s], dlr[s][e], w);
       sv[e] = bf16r(__fadd_rn(__fmul_rn(sv[e], scale), w));
     }
     if (on) store_row<CPL>(tile + i * DV + c0, sv);
@@ -388,12 +398,18 @@ __global__ void __launch_bounds__(128) gdn_verify_kernel(VerifyArgs a, const flo
     const int64_t row = static_cast<int64_t>(b) * K + t;
     const __nv_bfloat16* zrow = a.qkvz + row * a.ld_qkvz + conv_dim + h * DV;
     uint8_t* orow = a.out + row * a.ld_out + h * DV;
+    float nwv[CPL], zv[CPL];  // loaded before any output store (one round trip)
+#pragma unroll
+    for (int e = 0; e < CPL; ++e) {
+      nwv[e] = __bfloat162float(a.norm_w[c0 + e]);
+      zv[e] = __bfloat162float(zrow[c0 + e]);
+    }
 #pragma unroll
     for (int e = 0; e < CPL; ++e) {
       const int c = c0 + e;
       const float n1 = bf16r(__fmul_rn(o[e], r));
-      const float n2 = bf16r(__fmul_rn(__bfloat162float(a.norm_w[c]), n1));
-      const float z = __bfloat162float(zrow[c]);
+      const float n2 = bf16r(__fmul_rn(nwv[e], n1));
+      const float z = zv[e];
       orow[c] = f32_to_e5m2(bf16r(__fmul_rn(n2, __fmul_rn(z, sigmoidf_(z)))));
     }
   }
