@@ -127,7 +127,10 @@ int q38_silu_mul_quant(const void* gu, int64_t ld, int64_t rows, int64_t n, void
  * y[r, o] = bf16(sum_k x[r, k] * w[o, k]) with BF16 x [rows, k] (contiguous) and a pre-tiled BF16
  * weight [n_out, k], fp32 accumulate on tcgen05 (kind::f16), split K as q38_fp8_gemm (same
  * workspace rules). Used for the gated delta rule's in_proj_b / in_proj_a, which stay BF16 and take
- * the unrounded normed input (qwen38_inf2/model.py:294-296, :333-337).
+ * the unrounded normed input (qwen38_inf2/model.py:294-296, :333-337). With splits > 1 and a
+ * workspace the split partials go through the workspace and the CTAs run in pairs on whichever SMs
+ * are free (for a launch beside another kernel); without one, the splits of a tile form a thread-block
+ * cluster. The result is the same bits either way.
  */
 int q38_bf16_linear(const void* x, int64_t ldx, int64_t rows, int64_t k, const void* w, int64_t n_out, void* y,
                     int64_t ldy, int splits, void* workspace, size_t workspace_bytes, q38_stream_t stream);

@@ -966,10 +966,12 @@ int launch_persistent(const CUtensorMap& tx, const CUtensorMap& ty, const CUtens
   return q38host::cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "persistent gemm launch");
 }
 
+// `pair_place` (workspace mode, grid.z even): the K splits launch as 2-CTA clusters, which only
+// places each pair on the two SMs of one TPC; the kernel uses no cluster feature then.
 template <int NTOK, bool MX, bool PAIR = false>
 int launch_gemm(const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap& tr, const GemmArgs& a, dim3 grid,
                 cudaStream_t stream, const CUtensorMap* tw = nullptr, const CUtensorMap* tsf = nullptr,
-                bool resident = false) {
+                bool resident = false, bool pair_place = false) {
   using C = Cfg<NTOK, MX, PAIR>;
   // The shared-memory opt-in is per device; remember which devices have it.
   static unsigned long long done_mask = 0;
@@ -990,7 +992,7 @@ int launch_gemm(const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap&
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = PAIR ? 2u : 1u;
   attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = a.cluster > 1 ? static_cast<unsigned>(a.cluster) : 1u;
+  attr[0].val.clusterDim.z = a.cluster > 1 ? static_cast<unsigned>(a.cluster) : (pair_place && grid.z % 2 == 0 ? 2u : 1u);
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (resident) {
@@ -1023,10 +1025,10 @@ constexpr int kMaxClusterSplits = 8;  // portable cluster size
 // Fills the output and residual tensor maps for the cluster path.
 int setup_epilogue(GemmArgs& a, int splits, int64_t tokens, int64_t features, void* y, int64_t ldy,
                    const void* residual, int64_t ldr, void* workspace, size_t workspace_bytes, CUtensorMap* ty,
-                   CUtensorMap* tr, const char* who) {
+                   CUtensorMap* tr, const char* who, bool allow_cluster = true) {
   using namespace q38host;
   const bool mappable = aligned16(y) && ldy % 8 == 0 && (!residual || (aligned16(residual) && ldr % 8 == 0));
-  if (splits <= kMaxClusterSplits && mappable) {
+  if (allow_cluster && splits <= kMaxClusterSplits && mappable) {
     a.cluster = splits;
     int st = encode_tmap_2d(ty, y, tokens, features, 2, TOK_BLOCK, BM, false, ldy);
     if (st != Q38_OK) return st;
@@ -1248,16 +1250,23 @@ extern "C" int q38_bf16_linear(const void* x, int64_t ldx, int64_t rows, int64_t
   a.epilogue = EPI_BF16;
   a.y = static_cast<__nv_bfloat16*>(y);
   a.ldy = ldy;
+  // Given a workspace, the split partials go through it: the CTAs need no K-split cluster and run on
+  // whichever SMs are free (beside another kernel on a second stream, say), launched in 2-CTA
+  // clusters so each pair takes a whole TPC and leaves whole TPCs to 2-SM kernels. Without one, the
+  // splits of a tile form a cluster and sum through shared memory. Both sum the fp32 partials in
+  // split order 0..S-1 from zero: the same bits either way.
+  const bool via_workspace = splits > 1 && workspace != nullptr;
   CUtensorMap tx, ty, tr;
   int st = setup_epilogue(a, splits, rows, n_out, y, ldy, nullptr, 0, workspace, workspace_bytes, &ty, &tr,
-                          "q38_bf16_linear");
+                          "q38_bf16_linear", !via_workspace);
   if (st != Q38_OK) return st;
   st = encode_tmap_2d(&tx, x, rows, k, 2, ntok, BK_BYTES / 2);
   if (st != Q38_OK) return st;
   if (a.cluster == 0) ty = tr = tx;
   dim3 grid(static_cast<unsigned>(cdiv(n_out, BM)), static_cast<unsigned>(cdiv(rows, ntok)), static_cast<unsigned>(splits));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  return ntok == 256 ? launch_gemm<256, false>(tx, ty, tr, a, grid, s) : launch_gemm<128, false>(tx, ty, tr, a, grid, s);
+  return ntok == 256 ? launch_gemm<256, false>(tx, ty, tr, a, grid, s, nullptr, nullptr, false, via_workspace)
+                     : launch_gemm<128, false>(tx, ty, tr, a, grid, s, nullptr, nullptr, false, via_workspace);
 }
 
 // ------------------------------------------------------------------------------------------------

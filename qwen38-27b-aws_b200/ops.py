@@ -183,22 +183,23 @@ def silu_mul_quant(gu: torch.Tensor, n: int, y_e5m2: torch.Tensor) -> None:
 
 def bf16_linear(x: torch.Tensor, lin: DeviceBF16Linear, y: torch.Tensor, splits: int = 1,
                 workspace: torch.Tensor | None = None) -> None:
-    """y = bf16(x @ W^T), BF16 in, fp32 accumulate (tcgen05 kind::f16), split K through `workspace`."""
+    """y = bf16(x @ W^T), BF16 in, fp32 accumulate (tcgen05 kind::f16). Split K sums the partials
+    through `workspace` when one is given (CTAs in pairs on any free SMs: the form to run beside
+    another kernel), else through the shared memory of a cluster of the splits; same bits either way."""
     _cuda(x, y, workspace)
     rows, k = x.shape
     _need(x.dtype == BF16 and x.is_contiguous() and k == lin.in_features, "x must be contiguous bf16 [rows, in]")
     ws_ptr, ws_bytes = None, 0
-    if splits > 1:
-        _need(workspace is not None, "split K needs a workspace")
+    if splits > 1 and workspace is not None:
         ws_ptr, ws_bytes = workspace.data_ptr(), workspace.numel() * workspace.element_size()
     _lib.call("q38_bf16_linear", x.data_ptr(), x.stride(0), rows, k, lin.w.data_ptr(), lin.out_features, y.data_ptr(),
               y.stride(0), splits, ws_ptr, ws_bytes, _stream())
 
 
 def bf16_linear_splits(rows: int, n_out: int, k: int) -> int:
-    """K splits for a thin BF16 linear (96 outputs). The tile's last CTA sums every split's partial
-    tile, so more splits buy streaming parallelism at the price of that serial reduction: 8 balances
-    the two at 5120 x 96."""
+    """K splits for a thin BF16 linear (96 outputs): 8 balance streaming parallelism against the
+    reduction of the split partials at 5120 x 96. The partials are summed in split order, so the
+    split count fixes the fp32 summation order and with it the last bit of every output."""
     kc = -(-k // 64)
     return max(1, min(kc // 4, 8))
 

@@ -103,6 +103,7 @@ class B200Step:
                 rows = max(batch_size, batch_size * max(verify_tokens, 1), max_chunk)
                 self.comm = ops.Communicator(rank, tp_degree, rows, cfg.hidden_size, self.device, process_group)
             self._alloc_activations()
+            self._side = torch.cuda.Stream(device=self.device)
         self._graph = None
         self._graph_key = None
 
@@ -198,7 +199,7 @@ class B200Step:
                 need = max(need, ops.gemm_workspace_bytes(rows, lin.out_features, sp))
         hv2 = 2 * cfg.linear_num_value_heads // tp
         a.ab_splits = ops.bf16_linear_splits(rows, hv2, H)
-        need = max(need, ops.gemm_workspace_bytes(rows, hv2, a.ab_splits))
+        a.ab_workspace = z(max(ops.gemm_workspace_bytes(rows, hv2, a.ab_splits), 256), dt=torch.uint8)
         a.workspace = z(max(need, 256), dt=torch.uint8)
 
     # ------------------------------------------------------------------ kernels of one decode step
@@ -234,8 +235,14 @@ class B200Step:
         m = l.mixer
         if l.kind == LINEAR:
             ops.rmsnorm_quant(a.x, l.ln_in, eps, y_bf16=a.hb, y_e5m2=a.hq)
+            # in_proj_b/a (a thin BF16 GEMM on a few SMs, with its own workspace) runs on a side stream
+            # beside in_proj_qkvz, whose 2-SM tiles leave SM pairs idle; both join before the mixer.
+            main = torch.cuda.current_stream(self.device)
+            self._side.wait_stream(main)
+            with torch.cuda.stream(self._side):
+                ops.bf16_linear(a.hb, m.ab, a.ab, splits=a.ab_splits, workspace=a.ab_workspace)
             self._gemm(a, a.hq, m.qkvz, a.proj)
-            ops.bf16_linear(a.hb, m.ab, a.ab, splits=a.ab_splits, workspace=a.workspace)
+            main.wait_stream(self._side)
             heads = dict(num_k_heads=cfg.linear_num_key_heads // tp, num_v_heads=cfg.linear_num_value_heads // tp,
                          head_k=cfg.linear_key_head_dim, head_v=cfg.linear_value_head_dim, eps=eps)
             if verify:

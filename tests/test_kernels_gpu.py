@@ -225,6 +225,24 @@ def test_bf16_linear_matches_float64(pkg, ops, rows, k, n, splits):
     assert_gemm_close(y, exact, x.double().abs() @ w.double().abs().T, what=f"bf16 linear {rows}x{k}x{n}/{splits}")
 
 
+@pytest.mark.parametrize("rows,splits", [(8, 8), (100, 4), (256, 8), (256, 2)])
+def test_bf16_linear_workspace_and_cluster_paths_agree_bitwise(pkg, ops, rows, splits):
+    """Split partials through the workspace (independent CTA pairs) and through a cluster's shared
+    memory are summed in the same split order: the outputs are the same bits. Run twice through the
+    workspace, which must have reset its counters."""
+    gen = torch.Generator().manual_seed(21 + rows)
+    x = torch.randn(rows, 5120, generator=gen).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(96, 5120, generator=gen) * 0.02).to(torch.bfloat16)
+    lin = ops.DeviceBF16Linear(w, DEV)
+    ws = torch.zeros(max(256, ops.gemm_workspace_bytes(rows, 96, splits)), dtype=torch.uint8, device=DEV)
+    y_ws, y_cl = (torch.empty(rows, 96, dtype=torch.bfloat16, device=DEV) for _ in range(2))
+    for _ in range(2):
+        ops.bf16_linear(x, lin, y_ws, splits=splits, workspace=ws)
+    ops.bf16_linear(x, lin, y_cl, splits=splits, workspace=None)
+    torch.cuda.synchronize()
+    assert torch.equal(y_ws.view(torch.int16), y_cl.view(torch.int16))
+
+
 def _gdn_setup(pkg, cfg, batch, gen):
     w = pkg.weights.synthetic_layer(cfg, 0, seed=11, device="cpu", std=0.1)
     layer = om.GDNLayer(cfg, w, "layers.0", 1, batch, torch.bfloat16)
