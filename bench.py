@@ -398,10 +398,12 @@ def run_micro(args):
         act = torch.ones(B, device=dev)
         out = torch.empty(B, heads * hd, dtype=torch.uint8, device=dev)
 
+        order = ops.attn_row_order(pos, act, MAX_SEQ, torch.empty(B, dtype=torch.int32, device=dev))
+
         def launch(i):
             kc, vc = caches[i % len(caches)]
             ops.attn_decode(qkv, qn, kn, cs, sn, kc, vc, pos, act, out, batch=B, num_q_heads=heads, num_kv_heads=kvh,
-                            head_dim=hd, rot_dim=cfg.rotary_dim, eps=1e-6)
+                            head_dim=hd, rot_dim=cfg.rotary_dim, eps=1e-6, row_order=order)
         per = int(pos.sum().item()) * kvh * hd * 2 * 2 + B * qkv.shape[1] * 2 + B * heads * hd + B * kvh * hd * 2 * 2
         unit, bound = "GB/s", "hbm"
     elif args.micro == "gemm":

@@ -261,11 +261,24 @@ int q38_attn_verify(const void* qkv, int64_t ld_qkv, const void* q_norm_w, const
  *   cos, sin bf16 [batch, rot_dim]
  *   k_cache, v_cache bf16 [batch, num_kv_heads, max_seq, head_dim]
  *   out      e5m2 [batch, ld_out], num_q_heads * head_dim columns
+ *   row_order int32 [batch], a permutation of the rows (q38_attn_row_order's), or NULL: the order in
+ *            which the rows are scheduled. It changes no result, only how the grid's tail is filled.
  */
 int q38_attn_decode(const void* qkv, int64_t ld_qkv, const void* q_norm_w, const void* k_norm_w, const void* cos,
                     const void* sin, void* k_cache, void* v_cache, int64_t max_seq, const int32_t* position,
                     const float* active, void* out, int64_t ld_out, int64_t batch, int num_q_heads,
-                    int num_kv_heads, int head_dim, int rot_dim, float eps, q38_stream_t stream);
+                    int num_kv_heads, int head_dim, int rot_dim, float eps, const int32_t* row_order,
+                    q38_stream_t stream);
+
+/*
+ * The longest-first schedule for q38_attn_decode: row_order int32 [batch] = the rows by decreasing
+ * count of visible cache positions (min(position, max_seq) for active rows, none for inactive ones),
+ * in tiles of 32, ties by row index. Positions and activity are the same for every attention layer
+ * of a decode step, so one call per step serves all of them. batch <= 4096. No reference counterpart
+ * (scheduling only).
+ */
+int q38_attn_row_order(const int32_t* position, const float* active, int64_t max_seq, int64_t batch,
+                       int32_t* row_order, q38_stream_t stream);
 
 /*
  * Tensor-parallel communicator for the fused GEMM + all-reduce. Each rank creates one exchange region

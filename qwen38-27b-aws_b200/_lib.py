@@ -52,8 +52,9 @@ SIGNATURES = {
     "q38_attn_decode": (
         c_int,
         [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
-         c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_float, c_void_p],
+         c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_float, c_void_p, c_void_p],
     ),
+    "q38_attn_row_order": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
     "q38_gdn_prefill_workspace_bytes": (c_size_t, [c_int64, c_int, c_int, c_int, c_int]),
     "q38_gdn_prefill_chunk": (
         c_int,

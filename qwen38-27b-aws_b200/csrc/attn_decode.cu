@@ -15,6 +15,11 @@
 // compute warps multiply on mma.sync (BF16, fp32 accumulate) and never wait on a CTA-wide barrier per
 // tile. Every other input of the row (queries, own key / value, gates, norm weights, cos / sin) is
 // fetched in one round trip at the start. Three CTAs per SM.
+//
+// Rows differ in length (each streams position * head_dim * 4 bytes per KV head), and a CTA streams
+// at a fraction of the SM's bandwidth, so a long row that starts in the grid's last wave sets the
+// kernel's end. With a row order (attn_row_order_kernel, once per step) the CTAs take the rows
+// longest first; any order gives the same bytes.
 #include "attn_common.cuh"
 
 namespace {
@@ -37,6 +42,7 @@ struct AttnArgs {
   const float* active;
   uint8_t* out;
   int64_t ld_out;
+  const int32_t* order;  // row for each blockIdx.y (a permutation), or null: blockIdx.y itself
   int num_q_heads, num_kv_heads, groups, rot;
   float eps;
 };
@@ -146,11 +152,11 @@ __global__ void __launch_bounds__(kThreads, 3) attn_decode_kernel(const __grid_c
   uint64_t* empty = full + STAGES;
   float* stats = reinterpret_cast<float*>(smem + L.stats);
 
-  const int g = blockIdx.x, b = blockIdx.y;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t head_row = static_cast<int64_t>(b) * a.num_kv_heads + g;
   pdl_wait();
   pdl_trigger();
+  const int g = blockIdx.x, b = a.order ? a.order[blockIdx.y] : static_cast<int>(blockIdx.y);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t head_row = static_cast<int64_t>(b) * a.num_kv_heads + g;
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -394,6 +400,32 @@ __global__ void __launch_bounds__(kThreads, 3) attn_decode_kernel(const __grid_c
   }
 }
 
+// The longest-first row order for attn_decode_kernel: rows by decreasing count of visible cache tiles
+// (KT positions; inactive rows see none), ties by row index. One CTA; each thread ranks its rows
+// against all others, O(batch^2) comparisons (a few microseconds at 4096 rows).
+constexpr int kOrderMaxRows = 4096;
+__global__ void __launch_bounds__(1024) attn_row_order_kernel(const int32_t* position, const float* active,
+                                                              int64_t max_seq, int batch, int32_t* order) {
+  __shared__ int tiles[kOrderMaxRows];
+  pdl_wait();
+  pdl_trigger();
+  for (int r = threadIdx.x; r < batch; r += blockDim.x) {
+    const int64_t p = position[r] < 0 ? 0 : position[r];
+    const int64_t n = active[r] > 0.5f ? (p < max_seq ? p : max_seq) : 0;
+    tiles[r] = static_cast<int>((n + KT - 1) / KT);
+  }
+  __syncthreads();
+  for (int r = threadIdx.x; r < batch; r += blockDim.x) {
+    const int tr = tiles[r];
+    int rank = 0;
+    for (int j = 0; j < batch; ++j) {
+      const int tj = tiles[j];
+      rank += (tj > tr) || (tj == tr && j < r);
+    }
+    order[rank] = r;
+  }
+}
+
 template <int HD>
 int launch_attn(const AttnArgs& a, int64_t batch, cudaStream_t stream) {
   using T = TileGeom<HD>;
@@ -422,7 +454,7 @@ extern "C" int q38_attn_decode(const void* qkv, int64_t ld_qkv, const void* q_no
                                const void* cos, const void* sin, void* k_cache, void* v_cache, int64_t max_seq,
                                const int32_t* position, const float* active, void* out, int64_t ld_out,
                                int64_t batch, int num_q_heads, int num_kv_heads, int head_dim, int rot_dim, float eps,
-                               q38_stream_t stream) {
+                               const int32_t* row_order, q38_stream_t stream) {
   using namespace q38host;
   if (!qkv || !q_norm_w || !k_norm_w || !cos || !sin || !k_cache || !v_cache || !position || !active || !out)
     return set_error("q38_attn_decode: null pointer"), Q38_ERR_ARG;
@@ -449,6 +481,7 @@ extern "C" int q38_attn_decode(const void* qkv, int64_t ld_qkv, const void* q_no
   a.active = active;
   a.out = static_cast<uint8_t*>(out);
   a.ld_out = ld_out;
+  a.order = row_order;
   a.num_q_heads = num_q_heads;
   a.num_kv_heads = num_kv_heads;
   a.groups = num_q_heads / num_kv_heads;
@@ -458,4 +491,16 @@ extern "C" int q38_attn_decode(const void* qkv, int64_t ld_qkv, const void* q_no
   if (head_dim == 256) return launch_attn<256>(a, batch, s);
   if (head_dim == 32) return launch_attn<32>(a, batch, s);
   return set_error("q38_attn_decode: head_dim %d not built (256, 32 are)", head_dim), Q38_ERR_UNSUPPORTED;
+}
+
+extern "C" int q38_attn_row_order(const int32_t* position, const float* active, int64_t max_seq, int64_t batch,
+                                  int32_t* row_order, q38_stream_t stream) {
+  using namespace q38host;
+  if (!position || !active || !row_order) return set_error("q38_attn_row_order: null pointer"), Q38_ERR_ARG;
+  if (batch <= 0 || batch > kOrderMaxRows || max_seq <= 0)
+    return set_error("q38_attn_row_order: batch must be 1..%d", kOrderMaxRows), Q38_ERR_ARG;
+  const unsigned threads = static_cast<unsigned>(batch >= 1024 ? 1024 : (batch + 31) / 32 * 32);
+  const cudaError_t e = launch_pdl(attn_row_order_kernel, dim3(1), dim3(threads), 0, static_cast<cudaStream_t>(stream),
+                                   position, active, max_seq, static_cast<int>(batch), row_order);
+  return cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "attn_row_order launch");
 }

@@ -244,14 +244,33 @@ def gdn_decode(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, s
 
 
 def attn_decode(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, position, active, out, *, batch: int,
-                num_q_heads: int, num_kv_heads: int, head_dim: int, rot_dim: int, eps: float) -> None:
-    _cuda(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, position, active, out)
+                num_q_heads: int, num_kv_heads: int, head_dim: int, rot_dim: int, eps: float,
+                row_order: torch.Tensor | None = None) -> None:
+    """`row_order` (int32 [batch], from attn_row_order) schedules the rows longest first; same bytes."""
+    _cuda(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, position, active, out, row_order)
     _need(cos.is_contiguous() and sin.is_contiguous() and cos.shape[-1] == rot_dim, "cos/sin [batch, rot] contiguous")
     _need(k_cache.is_contiguous() and v_cache.is_contiguous(), "caches must be contiguous")
+    _need(row_order is None or (row_order.dtype == torch.int32 and row_order.numel() == batch), "row_order int32 [batch]")
     _lib.call("q38_attn_decode", qkv.data_ptr(), qkv.stride(0), q_norm_w.data_ptr(), k_norm_w.data_ptr(), cos.data_ptr(),
               sin.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), k_cache.shape[2], position.data_ptr(),
               active.data_ptr(), out.data_ptr(), out.stride(0), batch, num_q_heads, num_kv_heads, head_dim, rot_dim, eps,
+              None if row_order is None else row_order.data_ptr(), _stream())
+
+
+ATTN_ORDER_MAX_ROWS = 4096  # q38_attn_row_order's batch limit
+
+
+def attn_row_order(position: torch.Tensor, active: torch.Tensor, max_seq: int, row_order: torch.Tensor) -> torch.Tensor:
+    """row_order = the rows by decreasing visible cache length (ties by index), for attn_decode."""
+    _cuda(position, active, row_order)
+    batch = position.numel()
+    _need(position.dtype == torch.int32 and active.dtype == torch.float32 and active.numel() == batch,
+          "position int32 [batch], active float32 [batch]")
+    _need(row_order.dtype == torch.int32 and row_order.numel() == batch and row_order.is_contiguous(),
+          "row_order int32 [batch] contiguous")
+    _lib.call("q38_attn_row_order", position.data_ptr(), active.data_ptr(), max_seq, batch, row_order.data_ptr(),
               _stream())
+    return row_order
 
 
 def gdn_prefill_workspace_bytes(tokens: int, num_k_heads: int, num_v_heads: int, head_k: int, head_v: int) -> int:

@@ -156,6 +156,9 @@ class B200Step:
         self._fill_acts(self, self.batch)
         self.position = torch.zeros(self.batch, dtype=torch.int32, device=self.device)
         self.active = torch.zeros(self.batch, dtype=torch.float32, device=self.device)
+        # Attention decode's schedule: rows longest first, recomputed at the start of every decode step
+        # (a permutation at all times, so a layer run on its own between steps is still correct).
+        self.attn_order = torch.arange(self.batch, dtype=torch.int32, device=self.device)
         self._prefill_acts = {}
         self._verify_acts = None
         cfg = self.cfg
@@ -220,8 +223,13 @@ class B200Step:
 
     def _decode_layers(self):
         self.x.copy_(self.x_in)
+        if self._orders_rows():
+            ops.attn_row_order(self.position, self.active, self.max_seq, self.attn_order)
         for l in self.layers:
             self._layer(l, self)
+
+    def _orders_rows(self) -> bool:
+        return any(l.kind == FULL for l in self.layers) and self.batch <= ops.ATTN_ORDER_MAX_ROWS
 
     def run_layer(self, i: int) -> None:
         """Layer i alone, eagerly, on self.x and the loaded decode inputs (for layer-by-layer checks)."""
@@ -267,7 +275,7 @@ class B200Step:
                                 a.mix_attn, batch=self.batch, tokens=verify, **heads)
             elif chunk is None:
                 ops.attn_decode(a.proj, m.q_norm, m.k_norm, a.cos, a.sin, m.k_cache, m.v_cache, a.position, a.active,
-                                a.mix_attn, batch=self.batch, **heads)
+                                a.mix_attn, batch=self.batch, row_order=self.attn_order, **heads)
             else:
                 slot, start, _ = chunk
                 ops.attn_prefill(a.proj, m.q_norm, m.k_norm, a.cos, a.sin, m.k_cache, m.v_cache, a.mix_attn, a.attn_ws,
@@ -361,7 +369,7 @@ class B200Step:
 
     def kernels_per_decode_step(self) -> int:
         """Launches of this library's kernels in one decode step (for the bench's gpu_launches)."""
-        n = 0
+        n = 1 if self._orders_rows() else 0  # the attention row order
         for l in self.layers:
             n += (6 if l.kind == LINEAR else 4) + 3  # GDN: rmsnorm, qkvz, ab, q/k prep, decode, out_proj; MLP: 3
         return n

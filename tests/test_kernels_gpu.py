@@ -243,6 +243,21 @@ def test_bf16_linear_workspace_and_cluster_paths_agree_bitwise(pkg, ops, rows, s
     assert torch.equal(y_ws.view(torch.int16), y_cl.view(torch.int16))
 
 
+@pytest.mark.parametrize("batch,max_seq", [(1, 64), (256, 512), (1000, 300), (4096, 2048)])
+def test_attn_row_order_is_longest_first(ops, batch, max_seq):
+    """The schedule is the permutation that sorts rows by decreasing visible 32-position tiles (inactive
+    rows see none), ties by row index, as a stable CPU sort gives it."""
+    gen = torch.Generator().manual_seed(batch)
+    position = torch.randint(-3, max_seq + 40, (batch,), generator=gen, dtype=torch.int32)
+    active = (torch.rand(batch, generator=gen) > 0.1).float()
+    order = ops.attn_row_order(position.to(DEV), active.to(DEV), max_seq, torch.full((batch,), -1, dtype=torch.int32, device=DEV))
+    torch.cuda.synchronize()
+    seen = torch.where(active > 0.5, position.clamp(0, max_seq), torch.zeros_like(position))
+    tiles = (seen.long() + 31) // 32
+    want = sorted(range(batch), key=lambda r: (-int(tiles[r]), r))
+    assert order.cpu().tolist() == want
+
+
 def _gdn_setup(pkg, cfg, batch, gen):
     w = pkg.weights.synthetic_layer(cfg, 0, seed=11, device="cpu", std=0.1)
     layer = om.GDNLayer(cfg, w, "layers.0", 1, batch, torch.bfloat16)
@@ -317,12 +332,16 @@ def test_attn_decode_matches_oracle(pkg, ops, shape, batch, max_seq):
                     cos.to(DEV), sin.to(DEV), d_k, d_v, position.to(DEV), active.to(DEV), out, batch=batch,
                     num_q_heads=heads, num_kv_heads=kvh, head_dim=hd, rot_dim=cfg.rotary_dim, eps=cfg.rms_norm_eps)
     torch.cuda.synchronize()
+    # Again, scheduled longest row first: the same bytes (the order only places the rows' CTAs).
     out2 = torch.empty_like(out)
+    order = ops.attn_row_order(position.to(DEV), active.to(DEV), max_seq, torch.empty(batch, dtype=torch.int32, device=DEV))
     ops.attn_decode(torch.cat((qg, k, v), -1).reshape(batch, -1).to(DEV), layer.q_norm.to(DEV), layer.k_norm.to(DEV),
                     cos.to(DEV), sin.to(DEV), d_k, d_v, position.to(DEV), active.to(DEV), out2, batch=batch,
-                    num_q_heads=heads, num_kv_heads=kvh, head_dim=hd, rot_dim=cfg.rotary_dim, eps=cfg.rms_norm_eps)
+                    num_q_heads=heads, num_kv_heads=kvh, head_dim=hd, rot_dim=cfg.rotary_dim, eps=cfg.rms_norm_eps,
+                    row_order=order)
     torch.cuda.synchronize()
-    assert torch.equal(out, out2), "a repeated call must give the same bytes"
+    assert sorted(order.cpu().tolist()) == list(range(batch))
+    assert torch.equal(out, out2), "a repeated, reordered call must give the same bytes"
     want = layer.decode_core(qg, k, v, cos.unsqueeze(1), sin.unsqueeze(1), position, active).reshape(batch, -1)
     on = active > 0.5
     # fp32 summation order differs from the oracle's matmul: where W V nearly cancels the own value's
