@@ -203,7 +203,25 @@ def run_ours(args, world, rank, local):
     peak, peak_kind = peaks()
     achieved = per_launch / (gdn_ms * 1e-3) / 1e9
 
+    # Prefill: one MAX_SEQ-token chunk of one row (slot 0, position 0) through all layers, inputs
+    # resident, timed on the device after one untimed chunk.
+    C, chunks = MAX_SEQ, 3
+    p_emb = (torch.randn(1, C, cfg.hidden_size, generator=g_cpu) * 0.02).to(torch.bfloat16).to(device)
+    p_cos, p_sin = (t.unsqueeze(0).to(device) for t in rotary(cfg, torch.arange(C)))
+    step.prefill(p_emb, p_cos, p_sin, slot=0, start=0, n_valid=C)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    p_start, p_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p_start.record()
+    for _ in range(chunks):
+        step.prefill(p_emb, p_cos, p_sin, slot=0, start=0, n_valid=C)
+    p_end.record()
+    torch.cuda.synchronize()
+    prefill_ms = max_over_ranks(p_start.elapsed_time(p_end), world, device) / chunks
+
     tokens = B * args.steps
+    step_bytes = decode_step_bytes(step, head, pkg.config.LINEAR, positions[args.warmup:])
     line = {
         "metric": METRIC,
         "value": tokens / (dev_ms / 1e3),
@@ -239,6 +257,21 @@ def run_ours(args, world, rank, local):
             "bytes_per_launch": per_launch,
             "launch_ms": gdn_ms,
         },
+        # The whole step against HBM: the algorithmic bytes of one decode step (FP8 weights and scales,
+        # the BF16 lm_head and in_proj_b/a, gated-delta and conv state in and out, the KV cache below
+        # each row's position) over the measured step time.
+        "step_roofline": {
+            "bytes_per_step": step_bytes,
+            "achieved": step_bytes / (dev_ms / args.steps * 1e-3) / 1e9,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": step_bytes / (dev_ms / args.steps * 1e-3) / 1e9 / peak,
+        },
+        "prefill": {
+            "workload": f"one {C}-token chunk of one row through all {LAYERS} layers (device-timed, {chunks} chunks)",
+            "ms_per_chunk": prefill_ms,
+            "tokens_per_s": C / (prefill_ms / 1e3),
+        },
         "clocks": clocks,
         "gpu_launches": (step.kernels_per_decode_step() + 2) * args.steps,
         "build_s": round(build_s, 1),
@@ -252,6 +285,24 @@ def run_ours(args, world, rank, local):
     if world > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+def decode_step_bytes(step, head, linear_kind: str, positions: torch.Tensor) -> int:
+    """HBM bytes one decode step must move on this rank, averaged over the timed steps' positions."""
+    fp8 = lambda lin: lin.out_features * lin.in_features * 33 // 32  # e4m3 bytes + UE8M0 per 32  # noqa: E731
+    total = head.lm_head.out_features * head.lm_head.in_features * 2
+    kv_positions = positions.clamp(max=MAX_SEQ).long().sum(dim=1).float().mean().item()
+    for l in step.layers:
+        total += fp8(l.gate_up) + fp8(l.down)
+        if l.kind == linear_kind:
+            m = l.mixer
+            total += fp8(m.qkvz) + fp8(m.out) + m.ab.out_features * m.ab.in_features * 2
+            total += m.state.numel() * 2 * 2 + m.conv_state.numel() * 2 * 2
+        else:
+            m = l.mixer
+            kvh, hd = m.k_cache.shape[1], m.k_cache.shape[3]
+            total += fp8(m.qkv) + fp8(m.o) + int(kv_positions * kvh * hd * 2 * 2)
+    return int(total)
 
 
 def time_gdn_launches(step, ops, pkg, repeats: int) -> float:

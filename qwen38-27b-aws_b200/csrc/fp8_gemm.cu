@@ -647,7 +647,11 @@ struct PCfg {
   static constexpr int SFA_COL = NTOK;
   static constexpr int SFB_COL = NTOK + 32;
   static constexpr size_t PIPE = STAGES * (A_BYTES + B_BYTES + SF_BYTES);
-  static constexpr size_t OUT = static_cast<size_t>(NTOK) * BM * 2;  // bf16 [NTOK tokens][128 rows]
+  // Output staging: bf16 [NTOK tokens][128 rows] (EPI_BF16, stored by TMA), or bf16 [128 rows][SROW
+  // tokens] (EPI_SILU: gate rows then up rows, each row padded by 16 bytes so that a warp's 16-byte
+  // accesses of 32 rows fall in distinct bank groups).
+  static constexpr int SROW = NTOK + 8;
+  static constexpr size_t OUT = static_cast<size_t>(BM) * SROW * 2;
   static constexpr size_t SMEM = 1024 + PIPE + OUT + 256;
   static_assert(SFA_COL + 4 * STAGES <= SFB_COL && SFB_COL + 8 <= TMEM_COLS, "TMEM columns");
 };
@@ -855,17 +859,20 @@ __global__ void __launch_bounds__(192, 1)
       epi_bar();
       if (a.epilogue == EPI_SILU) {
         // Rows 0..63 of the tile are gate rows, 64..127 the matching up rows (features mt*64 ..): both go
-        // to shared memory as bf16 (the reference's gate_proj / up_proj outputs), TMEM is handed back,
-        // then h = bf16(bf16(g * bf16(sigmoid(g))) * u) goes out as e5m2 (down_proj's input rounding).
-        __nv_bfloat16* sg = st;                 // [NTOK][64]
-        __nv_bfloat16* su = st + NTOK * 64;     // [NTOK][64]
-        __nv_bfloat16* dst = r < 64 ? sg : su;
+        // to shared memory as bf16 (the reference's gate_proj / up_proj outputs; row r of the tile is
+        // row r of the staging, 8 tokens per 16-byte store), TMEM is handed back, then
+        // h = bf16(bf16(g * bf16(sigmoid(g))) * u) goes out as e5m2 (down_proj's input rounding). The
+        // epilogue is bound by the conversion unit, so bf16 roundings go two per conversion.
+        constexpr int SROW = C::SROW;
+        uint4* srow = reinterpret_cast<uint4*>(st + r * SROW);
         for (int c = 0; c < NTOK; c += 64) {
           if (n0 + c >= a.T) break;
           float v[64];
           tmem_ld64(taddr + c, v);
 #pragma unroll
-          for (int j = 0; j < 64; ++j) dst[(c + j) * 64 + (r & 63)] = __float2bfloat16_rn(v[j]);
+          for (int j = 0; j < 64; j += 8)
+            srow[(c + j) / 8] = make_uint4(pack_bf16x2(v[j], v[j + 1]), pack_bf16x2(v[j + 2], v[j + 3]),
+                                           pack_bf16x2(v[j + 4], v[j + 5]), pack_bf16x2(v[j + 6], v[j + 7]));
         }
         tc_fence_before();
         epi_bar();
@@ -876,20 +883,22 @@ __global__ void __launch_bounds__(192, 1)
         const int ntv = min(NTOK, a.T - n0);
         const int f0 = mt * 64;
         if (m0 < a.F) {
-          // 8 features per thread and step: independent chains that pipeline through the SFU.
-          for (int idx = threadIdx.x - 64; idx < ntv * 8; idx += 128) {
-            const int t = idx >> 3, qd = (idx & 7) * 8;
-            const uint4 gw = *reinterpret_cast<const uint4*>(sg + t * 64 + qd);
-            const uint4 uw = *reinterpret_cast<const uint4*>(su + t * 64 + qd);
-            const __nv_bfloat16* gh = reinterpret_cast<const __nv_bfloat16*>(&gw);
-            const __nv_bfloat16* uh = reinterpret_cast<const __nv_bfloat16*>(&uw);
-            float h[8];
+          // One feature and 8 tokens per thread and step (consecutive lanes, consecutive features: their
+          // e5m2 bytes of one token are 32 contiguous bytes); 8 independent chains per thread.
+          const int items = (ntv + 7) / 8 * 64;
+          for (int idx = threadIdx.x - 64; idx < items; idx += 128) {
+            const int f = idx & 63, t0 = (idx >> 6) * 8;
+            const uint4 gw = *reinterpret_cast<const uint4*>(st + f * SROW + t0);
+            const uint4 uw = *reinterpret_cast<const uint4*>(st + (64 + f) * SROW + t0);
+            const uint32_t gp[4] = {gw.x, gw.y, gw.z, gw.w}, up[4] = {uw.x, uw.y, uw.z, uw.w};
+            uint8_t* dst = a.yq + static_cast<int64_t>(n0 + t0) * a.ldq + f0 + f;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) h[e] = silu_mul_bf16(__bfloat162float(gh[e]), __bfloat162float(uh[e]));
-            uint2 o;
-            o.x = pack4_e5m2(h[0], h[1], h[2], h[3]);
-            o.y = pack4_e5m2(h[4], h[5], h[6], h[7]);
-            *reinterpret_cast<uint2*>(a.yq + static_cast<int64_t>(n0 + t) * a.ldq + f0 + qd) = o;
+            for (int e = 0; e < 4; ++e) {
+              const float2 h = silu_mul_bf16x2(unpack_bf16x2(gp[e]), unpack_bf16x2(up[e]));
+              const uint32_t q = __nv_cvt_float2_to_fp8x2(h, __NV_SATFINITE, __NV_E5M2);
+              if (t0 + 2 * e < ntv) dst[static_cast<int64_t>(2 * e) * a.ldq] = static_cast<uint8_t>(q & 0xffu);
+              if (t0 + 2 * e + 1 < ntv) dst[static_cast<int64_t>(2 * e + 1) * a.ldq] = static_cast<uint8_t>(q >> 8);
+            }
           }
         }
         continue;

@@ -310,6 +310,22 @@ __device__ __forceinline__ float silu_mul_bf16(float g, float u) {
   const float s = bf16r(sigmoid_mlp(g));
   return bf16r(__fmul_rn(bf16r(__fmul_rn(g, s)), u));
 }
+// Two floats as a bf16 pair (round to nearest even, a in the low half) in one conversion.
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// The two bf16 of a pair, as floats (exact).
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+// silu_mul_bf16 of two elements, each bf16 rounding done for both in one conversion: the same
+// values, with half the conversions (the epilogue that runs it is bound by the conversion unit).
+__device__ __forceinline__ float2 silu_mul_bf16x2(float2 g, float2 u) {
+  const float2 s = unpack_bf16x2(pack_bf16x2(sigmoid_mlp(g.x), sigmoid_mlp(g.y)));
+  const float2 t = unpack_bf16x2(pack_bf16x2(__fmul_rn(g.x, s.x), __fmul_rn(g.y, s.y)));
+  return unpack_bf16x2(pack_bf16x2(__fmul_rn(t.x, u.x), __fmul_rn(t.y, u.y)));
+}
 // softplus with the threshold torch uses (beta 1, threshold 20).
 __device__ __forceinline__ float softplusf_(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
 
