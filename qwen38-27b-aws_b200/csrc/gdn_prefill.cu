@@ -1,22 +1,22 @@
 // Gated delta rule over a prefill chunk of one row: GatedDeltaNetStep.prefill
 // (qwen38_inf2/model.py:476-521) with the chunked rule of model.py:90-128.
 //
-// Three launches per call, all on the caller's stream:
+// Four launches per call, all on the caller's stream:
 //   prep   one CTA per (32-token tile, key head): the causal conv over [history * keep, chunk] with
 //          the CPU branch's rounding (bf16 products summed left to right in bf16, model.py:513),
 //          bf16 SiLU, fp32 L2 norms of q (then / sqrt(dk)) and k, and the gates beta, log decay
 //          (masked to the valid tokens). q and k are written transposed, [key head][dk][tokens], so
 //          the delta kernel's loads of a sub-chunk are contiguous runs of 256 bytes.
-//   delta  one CTA per (value head, 32-column slice of the state). The state's value columns evolve
-//          independently given k, beta and g, so the slices need no exchange; each CTA keeps its
-//          [dk x 32] fp32 slice in shared memory across the chunk and walks it in sub-chunks of 64
-//          tokens:   r  = beta * (v - e^g (k . S))            o_in = e^g (q . S)
-//                    (I + N) vn = r,  N = strictly_lower(beta (k k^T) * decay)   (blocked solve)
-//                    o  = o_in + ((q k^T) * decay) vn
-//                    S  = e^{g_last} S + (k e^{g_last - g})^T vn
-//          which is the reference's u - w S with u = A (v beta), w = A (k beta e^g), A = (I + N)^-1,
-//          regrouped as A (beta (v - e^g k S)) (same values, fp32 sums in another order). The sub-chunk
-//          length is 64 instead of the CPU branch's 128 (model.py:34): the rule is exact for any split.
+//   chunk  (delta, phase A) one CTA per (value head, sub-chunk of 64 tokens), all at once: the
+//          state-free matrices of each sub-chunk, Aqk = (q k^T) * decay (lower), and the reference's
+//          u = A (v beta), w = A (k beta e^g) with A = (I + N)^-1, N = strictly_lower(beta (k k^T) *
+//          decay) (blocked solve), plus q e^g and k e^{g_last - g}, into the workspace.
+//   state  (delta, phase B) one CTA per (value head, 32-column slice of the state). The state's value
+//          columns evolve independently given phase A's matrices, so the slices need no exchange; each
+//          CTA keeps its [dk x 32] fp32 slice in shared memory across the chunk and walks the
+//          sub-chunks:  v' = u - w S,  o = (q e^g) S + Aqk v',  S = e^{g_last} S + (k e^{g_last - g})^T v'
+//          (model.py:110-128). The sub-chunk length is 64 instead of the CPU branch's 128 (model.py:34):
+//          the rule is exact for any split.
 //   norm   one CTA per token: the gated RMS norm of each value head (model.py:339-344), times SiLU(z),
 //          e5m2 for out_proj; one more CTA carries the last conv_kernel-1 valid inputs into the conv
 //          state (model.py:490-492) after the prep CTAs have read the old history.
@@ -56,6 +56,7 @@ struct PrefillArgs {
   float* beta;  // [num_v_heads][tokens]
   float* g;     // [num_v_heads][tokens]
   __nv_bfloat16* o;  // [tokens][num_v_heads * dv]
+  float* chunks;     // [num_v_heads][sub-chunks] phase A's per-sub-chunk matrices (ChunkWs)
 };
 
 // ---------------------------------------------------------------------------------------------
@@ -153,41 +154,49 @@ __global__ void __launch_bounds__(256) gdn_prefill_prep_kernel(PrefillArgs a) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// delta
+// delta, phase A: everything of a sub-chunk that does not involve the state, for all (value head,
+// sub-chunk) pairs at once. With gc the running sum of the sub-chunk's log decays:
+//   Aqk[a][b] = (q_a . k_b) e^{gc_a - gc_b}            for a >= b, else 0
+//   N[a][b]   = beta_a (k_a . k_b) e^{gc_a - gc_b}     for a > b
+//   [u | w]   = (I + N)^-1 [beta v | beta e^{gc} k]    (the reference's u and w, model.py:110-116)
+//   qg = q e^{gc},  kd = k e^{gc_last - gc},  el = e^{gc_last}
+// go to the workspace, each matrix with padded rows so that phase B can bulk-copy it into shared
+// memory as is. (I + N)^-1 is applied by blocked forward substitution: the four 16 x 16 diagonal
+// blocks are inverted explicitly, one column of [u | w] per thread with the column in registers.
 // ---------------------------------------------------------------------------------------------
+template <int DK, int DV>
+struct ChunkWs {
+  static constexpr int RS = DK + 4;   // row stride of w, qg, kd (floats)
+  static constexpr int AS = SUB + 4;  // row stride of Aqk
+  static constexpr size_t AQK = 0;                               // [SUB][AS]
+  static constexpr size_t U = AQK + SUB * AS;                    // [SUB][DV]
+  static constexpr size_t W = U + SUB * DV;                      // [SUB][RS]
+  static constexpr size_t QG = W + SUB * RS;                     // [SUB][RS]
+  static constexpr size_t KD = QG + SUB * RS;                    // [SUB][RS]
+  static constexpr size_t EL = KD + SUB * RS;                    // e^{gc_last} (4 floats)
+  static constexpr size_t ITEM = EL + 4;                         // floats per (value head, sub-chunk)
+  static_assert(AQK % 4 == 0 && U % 4 == 0 && W % 4 == 0 && QG % 4 == 0 && KD % 4 == 0 && EL % 4 == 0,
+                "16-byte aligned pieces for the bulk copies");
+};
+
 template <int DK>
-struct DeltaSmem {
-  static constexpr int KDP = DK + 4;
-  static constexpr size_t QT = 0;                                  // [DK][SUBP]
-  static constexpr size_t KT = QT + sizeof(float) * DK * SUBP;     // [DK][SUBP]
-  static constexpr size_t KD = KT + sizeof(float) * DK * SUBP;     // [SUB][KDP] k_a[d] e^{g_last - g_a}
-  static constexpr size_t ST = KD + sizeof(float) * SUB * KDP;     // [DK][DVS]
-  static constexpr size_t VS = ST + sizeof(float) * DK * DVS;      // [SUB][DVS]
-  static constexpr size_t RR = VS + sizeof(float) * SUB * DVS;     // [SUB][DVS] r
-  static constexpr size_t OI = RR + sizeof(float) * SUB * DVS;     // [SUB][DVS] o_in
-  static constexpr size_t VN = OI + sizeof(float) * SUB * DVS;     // [SUB][DVS]
-  static constexpr size_t TB = VN + sizeof(float) * SUB * DVS;     // [16][DVS]
-  static constexpr size_t AT = TB + sizeof(float) * 16 * DVS;      // [SUB][SUBP] (q k^T * decay)^T
-  static constexpr size_t NT = AT + sizeof(float) * SUB * SUBP;    // [SUB][SUBP] N^T
-  static constexpr size_t INV = NT + sizeof(float) * SUB * SUBP;   // [4][16][16]
-  static constexpr size_t VEC = INV + sizeof(float) * 4 * 16 * 16; // gc, eg, beta, graw, wl [SUB] each
+struct ChunkSmem {
+  static constexpr size_t QT = 0;                                   // [DK][SUBP]
+  static constexpr size_t KT = QT + sizeof(float) * DK * SUBP;      // [DK][SUBP]
+  static constexpr size_t NT = KT + sizeof(float) * DK * SUBP;      // [SUB][SUBP] N^T
+  static constexpr size_t INV = NT + sizeof(float) * SUB * SUBP;    // [4][16][16]
+  static constexpr size_t VEC = INV + sizeof(float) * 4 * 16 * 16;  // gc, eg, beta, graw, wl [SUB] each
   static constexpr size_t TOTAL = VEC + sizeof(float) * 5 * SUB;
 };
 
 template <int DK, int DV>
-__global__ void __launch_bounds__(256, 1) gdn_prefill_delta_kernel(PrefillArgs a) {
-  using S = DeltaSmem<DK>;
+__global__ void __launch_bounds__(256, 2) gdn_prefill_chunk_kernel(PrefillArgs a) {
+  using S = ChunkSmem<DK>;
+  using W = ChunkWs<DK, DV>;
+  static_assert(DK + DV <= 256, "one [u | w] column per thread");
   extern __shared__ __align__(16) uint8_t smem[];
   float* qT = reinterpret_cast<float*>(smem + S::QT);
   float* kT = reinterpret_cast<float*>(smem + S::KT);
-  float* kd = reinterpret_cast<float*>(smem + S::KD);
-  float* st = reinterpret_cast<float*>(smem + S::ST);
-  float* vs = reinterpret_cast<float*>(smem + S::VS);
-  float* rr = reinterpret_cast<float*>(smem + S::RR);
-  float* oi = reinterpret_cast<float*>(smem + S::OI);
-  float* vn = reinterpret_cast<float*>(smem + S::VN);
-  float* tb = reinterpret_cast<float*>(smem + S::TB);
-  float* atT = reinterpret_cast<float*>(smem + S::AT);
   float* nT = reinterpret_cast<float*>(smem + S::NT);
   float* inv = reinterpret_cast<float*>(smem + S::INV);
   float* gc = reinterpret_cast<float*>(smem + S::VEC);
@@ -197,12 +206,186 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_delta_kernel(PrefillArgs a
   float* wl = graw + SUB;
 
   const int tid = threadIdx.x;
-  const int h = blockIdx.x;
-  const int c0 = blockIdx.y * DVS;  // first state column of this CTA
+  const int h = blockIdx.x, c = blockIdx.y;
   const int R = a.num_v_heads / a.num_k_heads;
   const int kh = h / R;
   const int T = a.tokens;
+  const int s0 = c * SUB, n = min(SUB, T - s0);
+  float* item = a.chunks + (static_cast<size_t>(h) * gridDim.y + c) * W::ITEM;
+
+  for (int i = tid; i < DK * SUB; i += 256) {
+    const int d = i / SUB, t = i % SUB;
+    const int64_t src = (static_cast<int64_t>(kh) * DK + d) * T + s0 + t;
+    qT[d * SUBP + t] = t < n ? a.qT[src] : 0.f;
+    kT[d * SUBP + t] = t < n ? a.kT[src] : 0.f;
+  }
+  if (tid < SUB) {
+    be[tid] = tid < n ? a.beta[static_cast<int64_t>(h) * T + s0 + tid] : 0.f;
+    graw[tid] = tid < n ? a.g[static_cast<int64_t>(h) * T + s0 + tid] : 0.f;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    // Inclusive cumulative sum of the log decays (accumulated in double, rounded per element).
+    double acc = 0.0;
+    for (int t = 0; t < SUB; ++t) {
+      acc += graw[t];
+      gc[t] = static_cast<float>(acc);
+    }
+  }
+  __syncthreads();
+  if (tid < SUB) {
+    eg[tid] = expf(gc[tid]);
+    wl[tid] = expf(__fsub_rn(gc[SUB - 1], gc[tid]));
+  }
+  // Aqk (to the workspace) and N^T (to shared memory): the 64 x 64 products, 4 x 4 per thread.
+  {
+    const int ai = tid >> 4, bi = tid & 15;
+    float accq[4][4], acck[4][4];
+#pragma unroll
+    for (int x = 0; x < 4; ++x)
+#pragma unroll
+      for (int y = 0; y < 4; ++y) accq[x][y] = acck[x][y] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < DK; ++d) {
+      const float4 qa = *reinterpret_cast<const float4*>(qT + d * SUBP + 4 * ai);
+      const float4 ka = *reinterpret_cast<const float4*>(kT + d * SUBP + 4 * ai);
+      const float4 kb = *reinterpret_cast<const float4*>(kT + d * SUBP + 4 * bi);
+      const float qv[4] = {qa.x, qa.y, qa.z, qa.w}, kv[4] = {ka.x, ka.y, ka.z, ka.w}, bv[4] = {kb.x, kb.y, kb.z, kb.w};
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) {
+          accq[x][y] = fmaf(qv[x], bv[y], accq[x][y]);
+          acck[x][y] = fmaf(kv[x], bv[y], acck[x][y]);
+        }
+    }
+    float aq[4][4];
+#pragma unroll
+    for (int y = 0; y < 4; ++y) {
+      const int b = 4 * bi + y;
+      float nn[4];
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const int a_ = 4 * ai + x;
+        const float dec = a_ >= b ? expf(__fsub_rn(gc[a_], gc[b])) : 0.f;
+        aq[x][y] = a_ >= b ? __fmul_rn(accq[x][y], dec) : 0.f;
+        nn[x] = a_ > b ? __fmul_rn(__fmul_rn(be[a_], acck[x][y]), dec) : 0.f;
+      }
+      *reinterpret_cast<float4*>(nT + b * SUBP + 4 * ai) = make_float4(nn[0], nn[1], nn[2], nn[3]);
+    }
+#pragma unroll
+    for (int x = 0; x < 4; ++x)
+      *reinterpret_cast<float4*>(item + W::AQK + (4 * ai + x) * W::AS + 4 * bi) = make_float4(aq[x][0], aq[x][1], aq[x][2], aq[x][3]);
+  }
+  __syncthreads();  // N^T, eg and wl complete
+  // Inverses of the four 16 x 16 unit lower diagonal blocks of I + N (a column per thread).
+  if (tid < 64) {
+    const int blk = tid >> 4, col_i = tid & 15, base = blk * 16;
+    float col[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float sacc = 0.f;
+#pragma unroll
+      for (int b = 0; b < r; ++b) sacc = fmaf(nT[(base + b) * SUBP + base + r], col[b], sacc);
+      col[r] = r < col_i ? 0.f : (r == col_i ? 1.f : -sacc);
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) inv[(blk * 16 + r) * 16 + col_i] = col[r];
+  }
+  // qg = q e^{gc}, kd = k e^{gc_last - gc}, token-major with padded rows.
+  for (int i = tid; i < SUB * DK; i += 256) {
+    const int t = i / DK, d = i % DK;
+    item[W::QG + t * W::RS + d] = __fmul_rn(qT[d * SUBP + t], eg[t]);
+    item[W::KD + t * W::RS + d] = __fmul_rn(kT[d * SUBP + t], wl[t]);
+  }
+  if (tid == 0) item[W::EL] = eg[SUB - 1];
+  __syncthreads();  // the inverses
+  // [u | w] = (I + N)^-1 [beta v | beta e^{gc} k]: column j of the right-hand side in registers.
+  if (tid < DV + DK) {
+    const int j = tid;
+    float x[SUB];
+    if (j < DV) {
+      const float* vsrc = a.v + (static_cast<int64_t>(h) * T + s0) * DV + j;
+#pragma unroll
+      for (int t = 0; t < SUB; ++t) x[t] = t < n ? __fmul_rn(be[t], vsrc[static_cast<int64_t>(t) * DV]) : 0.f;
+    } else {
+      const float* kcol = kT + (j - DV) * SUBP;
+#pragma unroll
+      for (int t = 0; t < SUB; ++t) x[t] = __fmul_rn(__fmul_rn(kcol[t], be[t]), eg[t]);
+    }
+#pragma unroll
+    for (int blk = 0; blk < SUB / 16; ++blk) {
+      float tv[16];
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        const int row = blk * 16 + r;
+        float sacc = x[row];
+#pragma unroll
+        for (int b = 0; b < blk * 16; ++b) sacc = fmaf(-nT[b * SUBP + row], x[b], sacc);
+        tv[r] = sacc;
+      }
+#pragma unroll
+      for (int r = 0; r < 16; ++r) {
+        float v = 0.f;
+#pragma unroll
+        for (int cc = 0; cc <= r; ++cc) v = fmaf(inv[(blk * 16 + r) * 16 + cc], tv[cc], v);
+        x[blk * 16 + r] = v;
+      }
+    }
+    if (j < DV) {
+#pragma unroll
+      for (int t = 0; t < SUB; ++t) item[W::U + t * DV + j] = x[t];
+    } else {
+#pragma unroll
+      for (int t = 0; t < SUB; ++t) item[W::W + t * W::RS + (j - DV)] = x[t];
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// delta, phase B: the state walk. One CTA per (value head, DVS state columns); the columns of S evolve
+// independently given phase A's matrices, so the slices need no exchange. The fp32 slice stays in
+// shared memory across the chunk; per sub-chunk
+//   v' = u - w S,   o = qg S + Aqk v' (bf16 out),   S = el S + kd^T v'
+// with w and qg bulk-copied in ahead of time (the next sub-chunk's while this one updates S) and
+// Aqk and kd while v' is computed.
+// ---------------------------------------------------------------------------------------------
+template <int DK, int DV>
+struct StateSmem {
+  using W = ChunkWs<DK, DV>;
+  static constexpr size_t ST = 0;                                         // [DK][DVS]
+  static constexpr size_t WS = ST + sizeof(float) * DK * DVS;             // [SUB][RS] w
+  static constexpr size_t QG = WS + sizeof(float) * SUB * W::RS;          // [SUB][RS] qg
+  static constexpr size_t KD = QG + sizeof(float) * SUB * W::RS;          // [SUB][RS] kd
+  static constexpr size_t AQ = KD + sizeof(float) * SUB * W::RS;          // [SUB][AS] Aqk
+  static constexpr size_t VP = AQ + sizeof(float) * SUB * W::AS;          // [SUB][DVS] v'
+  static constexpr size_t BAR = VP + sizeof(float) * SUB * DVS;           // two mbarriers
+  static constexpr size_t TOTAL = BAR + 16;
+};
+
+template <int DK, int DV>
+__global__ void __launch_bounds__(256, 1) gdn_prefill_state_kernel(PrefillArgs a) {
+  using S = StateSmem<DK, DV>;
+  using W = ChunkWs<DK, DV>;
+  constexpr uint32_t WQ_BYTES = 2u * sizeof(float) * SUB * W::RS;
+  constexpr uint32_t AK_BYTES = sizeof(float) * (SUB * W::RS + SUB * W::AS);
+  extern __shared__ __align__(16) uint8_t smem[];
+  float* st = reinterpret_cast<float*>(smem + S::ST);
+  float* ws = reinterpret_cast<float*>(smem + S::WS);
+  float* qg = reinterpret_cast<float*>(smem + S::QG);
+  float* kd = reinterpret_cast<float*>(smem + S::KD);
+  float* aq = reinterpret_cast<float*>(smem + S::AQ);
+  float* vp = reinterpret_cast<float*>(smem + S::VP);
+  uint64_t* bar_wq = reinterpret_cast<uint64_t*>(smem + S::BAR);
+  uint64_t* bar_ak = bar_wq + 1;
+
+  const int tid = threadIdx.x;
+  const int h = blockIdx.x;
+  const int c0 = blockIdx.y * DVS;  // first state column of this CTA
+  const int T = a.tokens;
+  const int nsub = (T + SUB - 1) / SUB;
   const int64_t vd_all = static_cast<int64_t>(a.num_v_heads) * DV;
+  const float* items = a.chunks + static_cast<size_t>(h) * nsub * W::ITEM;
 
   // The state slice, fp32, zero unless the row continues (start > 0).
   __nv_bfloat16* srow = a.state + static_cast<int64_t>(h) * DK * DV;
@@ -210,182 +393,89 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_delta_kernel(PrefillArgs a
     const int d = i / DVS, j = i % DVS;
     st[i] = __fmul_rn(__bfloat162float(srow[d * DV + c0 + j]), a.keep);
   }
+  if (tid == 0) {
+    mbar_init(bar_wq, 1);
+    mbar_init(bar_ak, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();  // the barriers are initialised before anyone waits on them
+  auto load_wq = [&](int c) {
+    const float* it = items + static_cast<size_t>(c) * W::ITEM;
+    mbar_arrive_expect_tx(bar_wq, WQ_BYTES);
+    bulk_load(ws, it + W::W, WQ_BYTES / 2, bar_wq);
+    bulk_load(qg, it + W::QG, WQ_BYTES / 2, bar_wq);
+  };
+  auto load_ak = [&](int c) {
+    const float* it = items + static_cast<size_t>(c) * W::ITEM;
+    mbar_arrive_expect_tx(bar_ak, AK_BYTES);
+    bulk_load(kd, it + W::KD, sizeof(float) * SUB * W::RS, bar_ak);
+    bulk_load(aq, it + W::AQK, sizeof(float) * SUB * W::AS, bar_ak);
+  };
+  if (tid == 0) {
+    load_wq(0);
+    load_ak(0);
+  }
 
-  // Thread tilings (256 threads):
-  //   C: the 64 x 64 products, 4 x 4 per thread.
-  const int ai = tid >> 4, bi = tid & 15;
-  //   D, F: [SUB][DVS], RPT rows x 4 columns per thread.
+  // Thread tilings (256 threads): [SUB][DVS] outputs as RPT rows x 4 columns, [DK][DVS] as DPT x 4.
   constexpr int CG = DVS / 4, RG = 256 / CG, RPT = SUB / RG;
-  const int ri = tid / CG, ci = tid % CG;
-  //   G: [DK][DVS], DPT rows x 4 columns per thread.
   constexpr int DG = 256 / CG, DPT = DK / DG;
-  static_assert(RPT >= 1 && DPT >= 1 && DK % DG == 0, "tiling");
+  static_assert(RPT >= 1 && DPT >= 1 && DK % DG == 0 && SUB % RG == 0, "tiling");
+  const int ri = tid / CG, ci = tid % CG;
+  const int a0 = ri * RPT, d0 = ri * DPT;
+  bool ok = true;
 
-  for (int s0 = 0; s0 < T; s0 += SUB) {
-    const int n = min(SUB, T - s0);
-    __syncthreads();  // the previous sub-chunk is done with every buffer
-    for (int i = tid; i < DK * SUB; i += 256) {
-      const int d = i / SUB, c = i % SUB;
-      const int64_t src = (static_cast<int64_t>(kh) * DK + d) * T + s0 + c;
-      qT[d * SUBP + c] = c < n ? a.qT[src] : 0.f;
-      kT[d * SUBP + c] = c < n ? a.kT[src] : 0.f;
-    }
-    for (int i = tid; i < SUB * DVS; i += 256) {
-      const int c = i / DVS, j = i % DVS;
-      vs[i] = c < n ? a.v[(static_cast<int64_t>(h) * T + s0 + c) * DV + c0 + j] : 0.f;
-    }
-    if (tid < SUB) {
-      be[tid] = tid < n ? a.beta[static_cast<int64_t>(h) * T + s0 + tid] : 0.f;
-      graw[tid] = tid < n ? a.g[static_cast<int64_t>(h) * T + s0 + tid] : 0.f;
-    }
-    __syncthreads();
-    if (tid == 0) {
-      // Inclusive cumulative sum of the log decays (accumulated in double, rounded per element).
-      double acc = 0.0;
-      for (int c = 0; c < SUB; ++c) {
-        acc += graw[c];
-        gc[c] = static_cast<float>(acc);
-      }
-    }
-    __syncthreads();
-    if (tid < SUB) {
-      eg[tid] = expf(gc[tid]);
-      wl[tid] = expf(__fsub_rn(gc[SUB - 1], gc[tid]));
-    }
-
-    // C: attT[b][a] = (q_a . k_b) e^{g_a - g_b} for a >= b; nT[b][a] = beta_a (k_a . k_b) e^{g_a - g_b} for a > b.
-    {
-      float accq[4][4], acck[4][4];
+  for (int c = 0; c < nsub; ++c) {
+    const float* it = items + static_cast<size_t>(c) * W::ITEM;
+    const int s0 = c * SUB, n = min(SUB, T - s0);
+    float4 u4[RPT];
 #pragma unroll
-      for (int x = 0; x < 4; ++x)
+    for (int x = 0; x < RPT; ++x) u4[x] = *reinterpret_cast<const float4*>(it + W::U + (a0 + x) * DV + c0 + 4 * ci);
+    const float el = it[W::EL];
+    ok = ok && mbar_wait(bar_wq, c & 1);
+    // v' = u - w S and qg S, both against the state before this sub-chunk.
+    float accv[RPT][4], accq[RPT][4];
 #pragma unroll
-        for (int y = 0; y < 4; ++y) accq[x][y] = acck[x][y] = 0.f;
+    for (int x = 0; x < RPT; ++x)
+#pragma unroll
+      for (int y = 0; y < 4; ++y) accv[x][y] = accq[x][y] = 0.f;
 #pragma unroll 4
-      for (int d = 0; d < DK; ++d) {
-        const float4 qa = *reinterpret_cast<const float4*>(qT + d * SUBP + 4 * ai);
-        const float4 ka = *reinterpret_cast<const float4*>(kT + d * SUBP + 4 * ai);
-        const float4 kb = *reinterpret_cast<const float4*>(kT + d * SUBP + 4 * bi);
-        const float qv[4] = {qa.x, qa.y, qa.z, qa.w}, kv[4] = {ka.x, ka.y, ka.z, ka.w}, bv[4] = {kb.x, kb.y, kb.z, kb.w};
-#pragma unroll
-        for (int x = 0; x < 4; ++x)
-#pragma unroll
-          for (int y = 0; y < 4; ++y) {
-            accq[x][y] = fmaf(qv[x], bv[y], accq[x][y]);
-            acck[x][y] = fmaf(kv[x], bv[y], acck[x][y]);
-          }
-      }
-#pragma unroll
-      for (int y = 0; y < 4; ++y) {
-        const int b = 4 * bi + y;
-        float at[4], nn[4];
-#pragma unroll
-        for (int x = 0; x < 4; ++x) {
-          const int a_ = 4 * ai + x;
-          const float dec = a_ >= b ? expf(__fsub_rn(gc[a_], gc[b])) : 0.f;
-          at[x] = a_ >= b ? __fmul_rn(accq[x][y], dec) : 0.f;
-          nn[x] = a_ > b ? __fmul_rn(__fmul_rn(be[a_], acck[x][y]), dec) : 0.f;
-        }
-        *reinterpret_cast<float4*>(atT + b * SUBP + 4 * ai) = make_float4(at[0], at[1], at[2], at[3]);
-        *reinterpret_cast<float4*>(nT + b * SUBP + 4 * ai) = make_float4(nn[0], nn[1], nn[2], nn[3]);
-      }
-    }
-    __syncthreads();  // eg, wl visible
-    // D: r = beta (v - e^g (k . S)), o_in = e^g (q . S); and kd = k e^{g_last - g}.
-    {
-      float accr[RPT][4], acco[RPT][4];
-#pragma unroll
-      for (int x = 0; x < RPT; ++x)
-#pragma unroll
-        for (int y = 0; y < 4; ++y) accr[x][y] = acco[x][y] = 0.f;
-      const int a0 = ri * RPT;
-#pragma unroll 4
-      for (int d = 0; d < DK; ++d) {
-        const float4 sv = *reinterpret_cast<const float4*>(st + d * DVS + 4 * ci);
-        const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
-#pragma unroll
-        for (int x = 0; x < RPT; ++x) {
-          const float kx = kT[d * SUBP + a0 + x], qx = qT[d * SUBP + a0 + x];
-#pragma unroll
-          for (int y = 0; y < 4; ++y) {
-            accr[x][y] = fmaf(kx, s4[y], accr[x][y]);
-            acco[x][y] = fmaf(qx, s4[y], acco[x][y]);
-          }
-        }
-      }
+    for (int d = 0; d < DK; ++d) {
+      const float4 sv = *reinterpret_cast<const float4*>(st + d * DVS + 4 * ci);
+      const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
       for (int x = 0; x < RPT; ++x) {
-        const int a_ = a0 + x;
+        const float wx = ws[(a0 + x) * W::RS + d], qx = qg[(a0 + x) * W::RS + d];
 #pragma unroll
         for (int y = 0; y < 4; ++y) {
-          const int j = 4 * ci + y;
-          rr[a_ * DVS + j] = __fmul_rn(be[a_], __fsub_rn(vs[a_ * DVS + j], __fmul_rn(eg[a_], accr[x][y])));
-          oi[a_ * DVS + j] = __fmul_rn(eg[a_], acco[x][y]);
+          accv[x][y] = fmaf(wx, s4[y], accv[x][y]);
+          accq[x][y] = fmaf(qx, s4[y], accq[x][y]);
         }
       }
-      for (int i = tid; i < SUB * DK; i += 256) {
-        const int a_ = i / DK, d = i % DK;
-        kd[a_ * S::KDP + d] = __fmul_rn(kT[d * SUBP + a_], wl[a_]);
-      }
     }
-    // E0: inverses of the four 16 x 16 unit lower diagonal blocks of I + N (two warps, a column per lane).
-    if (tid < 64) {
-      const int blk = tid >> 4, c = tid & 15, base = blk * 16;
-      float col[16];
 #pragma unroll
-      for (int r = 0; r < 16; ++r) {
-        float s = 0.f;
+    for (int x = 0; x < RPT; ++x) {
+      const float u[4] = {u4[x].x, u4[x].y, u4[x].z, u4[x].w};
+      float v[4];
 #pragma unroll
-        for (int b = 0; b < r; ++b) s = fmaf(nT[(base + b) * SUBP + base + r], col[b], s);
-        col[r] = r < c ? 0.f : (r == c ? 1.f : -s);
-      }
-#pragma unroll
-      for (int r = 0; r < 16; ++r) inv[(blk * 16 + r) * 16 + c] = col[r];
+      for (int y = 0; y < 4; ++y) v[y] = __fsub_rn(u[y], accv[x][y]);
+      *reinterpret_cast<float4*>(vp + (a0 + x) * DVS + 4 * ci) = make_float4(v[0], v[1], v[2], v[3]);
     }
-    __syncthreads();
-    // E: (I + N) vn = r, block by block.
+    __syncthreads();  // v' complete; w and qg are read
+    if (tid == 0 && ok && c + 1 < nsub) load_wq(c + 1);
+    ok = ok && mbar_wait(bar_ak, c & 1);
+    // o = qg S + Aqk v' (Aqk is zero above the diagonal), bf16 out.
     {
-      constexpr int JPT = DVS / 16;
-      const int ar = tid >> 4, j0 = (tid & 15) * JPT;
-      for (int blk = 0; blk < 4; ++blk) {
-        const int a_ = blk * 16 + ar;
-        float t[JPT];
-#pragma unroll
-        for (int y = 0; y < JPT; ++y) t[y] = rr[a_ * DVS + j0 + y];
-        for (int b = 0; b < blk * 16; ++b) {
-          const float nab = nT[b * SUBP + a_];
-#pragma unroll
-          for (int y = 0; y < JPT; ++y) t[y] = fmaf(-nab, vn[b * DVS + j0 + y], t[y]);
-        }
-#pragma unroll
-        for (int y = 0; y < JPT; ++y) tb[ar * DVS + j0 + y] = t[y];
-        __syncthreads();
-        float v[JPT];
-#pragma unroll
-        for (int y = 0; y < JPT; ++y) v[y] = 0.f;
-        for (int c = 0; c <= ar; ++c) {
-          const float m = inv[(blk * 16 + ar) * 16 + c];
-#pragma unroll
-          for (int y = 0; y < JPT; ++y) v[y] = fmaf(m, tb[c * DVS + j0 + y], v[y]);
-        }
-#pragma unroll
-        for (int y = 0; y < JPT; ++y) vn[a_ * DVS + j0 + y] = v[y];
-        __syncthreads();
-      }
-    }
-    // F: o = o_in + attn vn, bf16 out. G: S = e^{g_last} S + kd^T vn.
-    {
-      const int a0 = ri * RPT;
       float acc[RPT][4];
 #pragma unroll
       for (int x = 0; x < RPT; ++x)
 #pragma unroll
         for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
       for (int b = 0; b < a0 + RPT; ++b) {
-        const float4 vv = *reinterpret_cast<const float4*>(vn + b * DVS + 4 * ci);
+        const float4 vv = *reinterpret_cast<const float4*>(vp + b * DVS + 4 * ci);
         const float v4[4] = {vv.x, vv.y, vv.z, vv.w};
 #pragma unroll
         for (int x = 0; x < RPT; ++x) {
-          const float m = atT[b * SUBP + a0 + x];
+          const float m = aq[(a0 + x) * W::AS + b];
 #pragma unroll
           for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(m, v4[y], acc[x][y]);
         }
@@ -396,25 +486,24 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_delta_kernel(PrefillArgs a
         if (a_ < n) {
           __nv_bfloat16* orow = a.o + static_cast<int64_t>(s0 + a_) * vd_all + static_cast<int64_t>(h) * DV + c0 + 4 * ci;
 #pragma unroll
-          for (int y = 0; y < 4; ++y) orow[y] = __float2bfloat16_rn(__fadd_rn(oi[a_ * DVS + 4 * ci + y], acc[x][y]));
+          for (int y = 0; y < 4; ++y) orow[y] = __float2bfloat16_rn(__fadd_rn(accq[x][y], acc[x][y]));
         }
       }
     }
+    // S = el S + kd^T v'.
     {
-      const int di = tid / CG, d0 = di * DPT;
-      const float el = eg[SUB - 1];
       float acc[DPT][4];
 #pragma unroll
       for (int x = 0; x < DPT; ++x)
 #pragma unroll
         for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
 #pragma unroll 4
-      for (int a_ = 0; a_ < SUB; ++a_) {
-        const float4 vv = *reinterpret_cast<const float4*>(vn + a_ * DVS + 4 * ci);
+      for (int t = 0; t < SUB; ++t) {
+        const float4 vv = *reinterpret_cast<const float4*>(vp + t * DVS + 4 * ci);
         const float v4[4] = {vv.x, vv.y, vv.z, vv.w};
 #pragma unroll
         for (int x = 0; x < DPT; ++x) {
-          const float kx = kd[a_ * S::KDP + d0 + x];
+          const float kx = kd[t * W::RS + d0 + x];
 #pragma unroll
           for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(kx, v4[y], acc[x][y]);
         }
@@ -427,8 +516,11 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_delta_kernel(PrefillArgs a
           *p = __fadd_rn(__fmul_rn(*p, el), acc[x][y]);
         }
     }
+    __syncthreads();  // S updated; kd, Aqk and v' are read
+    if (tid == 0 && ok && c + 1 < nsub) load_ak(c + 1);
   }
-  __syncthreads();
+  // A copy that timed out (recorded in the device error word) leaves the state untouched.
+  if (__syncthreads_or(!ok)) return;
   for (int i = tid; i < DK * DVS; i += 256) {
     const int d = i / DVS, j = i % DVS;
     srow[d * DV + c0 + j] = __float2bfloat16_rn(st[i]);
@@ -487,8 +579,13 @@ __global__ void __launch_bounds__(256) gdn_prefill_norm_kernel(PrefillArgs a, in
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct WsLayout {
-  size_t qT, kT, v, beta, g, o, total;
+  size_t qT, kT, v, beta, g, o, chunks, total;
 };
+
+// Floats of phase A's output per (value head, sub-chunk): ChunkWs<dk, dv>::ITEM for the built shapes.
+size_t chunk_item_floats(int dk, int dv) {
+  return static_cast<size_t>(SUB) * (SUB + 4) + static_cast<size_t>(SUB) * dv + 3 * static_cast<size_t>(SUB) * (dk + 4) + 4;
+}
 
 WsLayout ws_layout(int64_t tokens, int hk, int hv, int dk, int dv) {
   WsLayout w{};
@@ -505,13 +602,17 @@ WsLayout ws_layout(int64_t tokens, int hk, int hv, int dk, int dv) {
   off = align256(off + sizeof(float) * hv * tokens);
   w.o = off;
   off = align256(off + 2 * static_cast<size_t>(tokens) * hv * dv);
+  w.chunks = off;
+  off = align256(off + sizeof(float) * hv * static_cast<size_t>((tokens + SUB - 1) / SUB) * chunk_item_floats(dk, dv));
   w.total = off;
   return w;
 }
 
 template <int DK, int DV, int R>
 int launch_prefill(PrefillArgs a, int conv_dim, cudaStream_t stream) {
-  using S = DeltaSmem<DK>;
+  using CS = ChunkSmem<DK>;
+  using SS = StateSmem<DK, DV>;
+  static_assert(ChunkWs<DK, DV>::ITEM == (SUB * (SUB + 4) + SUB * DV + 3 * SUB * (DK + 4) + 4), "workspace size");
   static unsigned long long done_mask = 0;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -521,8 +622,11 @@ int launch_prefill(PrefillArgs a, int conv_dim, cudaStream_t stream) {
     e = cudaFuncSetAttribute(gdn_prefill_prep_kernel<DK, DV, R>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(prep_smem));
     if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(gdn_prefill_delta_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(S::TOTAL));
+      e = cudaFuncSetAttribute(gdn_prefill_chunk_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(CS::TOTAL));
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gdn_prefill_state_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(SS::TOTAL));
     if (e != cudaSuccess) return q38host::cuda_status(e, "cudaFuncSetAttribute(gdn_prefill)");
     done_mask |= 1ull << dev;
   }
@@ -530,10 +634,14 @@ int launch_prefill(PrefillArgs a, int conv_dim, cudaStream_t stream) {
   gdn_prefill_prep_kernel<DK, DV, R><<<gp, 256, prep_smem, stream>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return q38host::cuda_status(e, "gdn_prefill_prep launch");
-  dim3 gd(a.num_v_heads, DV / DVS);
-  gdn_prefill_delta_kernel<DK, DV><<<gd, 256, S::TOTAL, stream>>>(a);
+  dim3 gc(a.num_v_heads, (a.tokens + SUB - 1) / SUB);
+  gdn_prefill_chunk_kernel<DK, DV><<<gc, 256, CS::TOTAL, stream>>>(a);
   e = cudaGetLastError();
-  if (e != cudaSuccess) return q38host::cuda_status(e, "gdn_prefill_delta launch");
+  if (e != cudaSuccess) return q38host::cuda_status(e, "gdn_prefill_chunk launch");
+  dim3 gd(a.num_v_heads, DV / DVS);
+  gdn_prefill_state_kernel<DK, DV><<<gd, 256, SS::TOTAL, stream>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return q38host::cuda_status(e, "gdn_prefill_state launch");
   gdn_prefill_norm_kernel<DV><<<a.tokens + 1, 256, 0, stream>>>(a, conv_dim);
   return q38host::cuda_status(cudaGetLastError(), "gdn_prefill_norm launch");
 }
@@ -596,6 +704,7 @@ extern "C" int q38_gdn_prefill_chunk(const void* qkvz, int64_t ld_qkvz, const vo
   a.beta = reinterpret_cast<float*>(ws + w.beta);
   a.g = reinterpret_cast<float*>(ws + w.g);
   a.o = reinterpret_cast<__nv_bfloat16*>(ws + w.o);
+  a.chunks = reinterpret_cast<float*>(ws + w.chunks);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int rep = num_v_heads / num_k_heads;
   if (head_k == 128 && head_v == 128 && rep == 3) return launch_prefill<128, 128, 3>(a, static_cast<int>(conv_dim), s);
