@@ -63,7 +63,7 @@ struct PrefillArgs {
 // prep
 // ---------------------------------------------------------------------------------------------
 template <int DK, int DV, int R>
-__global__ void __launch_bounds__(256) gdn_prefill_prep_kernel(PrefillArgs a) {
+__global__ void __launch_bounds__(256, 2) gdn_prefill_prep_kernel(PrefillArgs a) {
   constexpr int CH = 2 * DK + R * DV;
   extern __shared__ __align__(16) uint8_t smem[];
   float* xs = reinterpret_cast<float*>(smem);  // [CH][PREP_TOK + 1]
@@ -89,18 +89,21 @@ __global__ void __launch_bounds__(256) gdn_prefill_prep_kernel(PrefillArgs a) {
       win[j] = t >= 0 ? __bfloat162float(a.qkvz[static_cast<int64_t>(t) * a.ld_qkvz + c])
                       : __bfloat162float(a.conv_state[static_cast<int64_t>(c) * (KCONV - 1) + (t + KCONV - 1)]) * a.keep;
     }
+    // The tile's inputs of this channel, all loads in flight at once.
+    float xin[PREP_TOK];
+#pragma unroll
     for (int tt = 0; tt < PREP_TOK; ++tt) {
       const int t = t0 + tt;
-      if (t >= a.tokens) {
-        xs[i * (PREP_TOK + 1) + tt] = 0.f;
-        continue;
-      }
-      win[KCONV - 1] = __bfloat162float(a.qkvz[static_cast<int64_t>(t) * a.ld_qkvz + c]);
+      xin[tt] = t < a.tokens ? __bfloat162float(a.qkvz[static_cast<int64_t>(t) * a.ld_qkvz + c]) : 0.f;
+    }
+#pragma unroll
+    for (int tt = 0; tt < PREP_TOK; ++tt) {
+      win[KCONV - 1] = xin[tt];
       // Python's sum over the taps: each addition rounds to bf16.
       float s = bf16r(__fmul_rn(win[0], w[0]));
 #pragma unroll
       for (int j = 1; j < KCONV; ++j) s = bf16r(__fadd_rn(s, bf16r(__fmul_rn(win[j], w[j]))));
-      xs[i * (PREP_TOK + 1) + tt] = bf16r(__fmul_rn(s, bf16r(sigmoidf_(s))));
+      xs[i * (PREP_TOK + 1) + tt] = t0 + tt < a.tokens ? bf16r(__fmul_rn(s, bf16r(sigmoidf_(s)))) : 0.f;
 #pragma unroll
       for (int j = 0; j < KCONV - 1; ++j) win[j] = win[j + 1];
     }
@@ -347,37 +350,38 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_chunk_kernel(PrefillArgs a
 // independently given phase A's matrices, so the slices need no exchange. The fp32 slice stays in
 // shared memory across the chunk; per sub-chunk
 //   v' = u - w S,   o = qg S + Aqk v' (bf16 out),   S = el S + kd^T v'
-// with w and qg bulk-copied in ahead of time (the next sub-chunk's while this one updates S) and
-// Aqk and kd while v' is computed.
+// with the inputs bulk-copied in while the previous step computes: qg and Aqk of the next sub-chunk
+// during this one, kd (into w's buffer, once w is read) during o, and the next w during the next
+// step's wait. Two CTAs share an SM, so one's copies overlap the other's arithmetic.
 // ---------------------------------------------------------------------------------------------
 template <int DK, int DV>
 struct StateSmem {
   using W = ChunkWs<DK, DV>;
   static constexpr size_t ST = 0;                                         // [DK][DVS]
-  static constexpr size_t WS = ST + sizeof(float) * DK * DVS;             // [SUB][RS] w
-  static constexpr size_t QG = WS + sizeof(float) * SUB * W::RS;          // [SUB][RS] qg
-  static constexpr size_t KD = QG + sizeof(float) * SUB * W::RS;          // [SUB][RS] kd
-  static constexpr size_t AQ = KD + sizeof(float) * SUB * W::RS;          // [SUB][AS] Aqk
+  static constexpr size_t WK = ST + sizeof(float) * DK * DVS;             // [SUB][RS] w, then kd
+  static constexpr size_t QG = WK + sizeof(float) * SUB * W::RS;          // [SUB][RS] qg
+  static constexpr size_t AQ = QG + sizeof(float) * SUB * W::RS;          // [SUB][AS] Aqk
   static constexpr size_t VP = AQ + sizeof(float) * SUB * W::AS;          // [SUB][DVS] v'
-  static constexpr size_t BAR = VP + sizeof(float) * SUB * DVS;           // two mbarriers
-  static constexpr size_t TOTAL = BAR + 16;
+  static constexpr size_t BAR = VP + sizeof(float) * SUB * DVS;           // four mbarriers
+  static constexpr size_t TOTAL = BAR + 32;
 };
 
 template <int DK, int DV>
-__global__ void __launch_bounds__(256, 1) gdn_prefill_state_kernel(PrefillArgs a) {
+__global__ void __launch_bounds__(256, 2) gdn_prefill_state_kernel(PrefillArgs a) {
   using S = StateSmem<DK, DV>;
   using W = ChunkWs<DK, DV>;
-  constexpr uint32_t WQ_BYTES = 2u * sizeof(float) * SUB * W::RS;
-  constexpr uint32_t AK_BYTES = sizeof(float) * (SUB * W::RS + SUB * W::AS);
+  constexpr uint32_t RS_BYTES = sizeof(float) * SUB * W::RS;
+  constexpr uint32_t AS_BYTES = sizeof(float) * SUB * W::AS;
   extern __shared__ __align__(16) uint8_t smem[];
   float* st = reinterpret_cast<float*>(smem + S::ST);
-  float* ws = reinterpret_cast<float*>(smem + S::WS);
+  float* wk = reinterpret_cast<float*>(smem + S::WK);
   float* qg = reinterpret_cast<float*>(smem + S::QG);
-  float* kd = reinterpret_cast<float*>(smem + S::KD);
   float* aq = reinterpret_cast<float*>(smem + S::AQ);
   float* vp = reinterpret_cast<float*>(smem + S::VP);
-  uint64_t* bar_wq = reinterpret_cast<uint64_t*>(smem + S::BAR);
-  uint64_t* bar_ak = bar_wq + 1;
+  uint64_t* bar_w = reinterpret_cast<uint64_t*>(smem + S::BAR);
+  uint64_t* bar_q = bar_w + 1;
+  uint64_t* bar_k = bar_w + 2;
+  uint64_t* bar_a = bar_w + 3;
 
   const int tid = threadIdx.x;
   const int h = blockIdx.x;
@@ -394,26 +398,18 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_state_kernel(PrefillArgs a
     st[i] = __fmul_rn(__bfloat162float(srow[d * DV + c0 + j]), a.keep);
   }
   if (tid == 0) {
-    mbar_init(bar_wq, 1);
-    mbar_init(bar_ak, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(bar_w + i, 1);
     fence_mbar_init();
   }
   __syncthreads();  // the barriers are initialised before anyone waits on them
-  auto load_wq = [&](int c) {
-    const float* it = items + static_cast<size_t>(c) * W::ITEM;
-    mbar_arrive_expect_tx(bar_wq, WQ_BYTES);
-    bulk_load(ws, it + W::W, WQ_BYTES / 2, bar_wq);
-    bulk_load(qg, it + W::QG, WQ_BYTES / 2, bar_wq);
-  };
-  auto load_ak = [&](int c) {
-    const float* it = items + static_cast<size_t>(c) * W::ITEM;
-    mbar_arrive_expect_tx(bar_ak, AK_BYTES);
-    bulk_load(kd, it + W::KD, sizeof(float) * SUB * W::RS, bar_ak);
-    bulk_load(aq, it + W::AQK, sizeof(float) * SUB * W::AS, bar_ak);
+  auto load = [&](uint64_t* bar, float* dst, int c, size_t off, uint32_t bytes) {
+    mbar_arrive_expect_tx(bar, bytes);
+    bulk_load(dst, items + static_cast<size_t>(c) * W::ITEM + off, bytes, bar);
   };
   if (tid == 0) {
-    load_wq(0);
-    load_ak(0);
+    load(bar_w, wk, 0, W::W, RS_BYTES);
+    load(bar_q, qg, 0, W::QG, RS_BYTES);
+    load(bar_a, aq, 0, W::AQK, AS_BYTES);
   }
 
   // Thread tilings (256 threads): [SUB][DVS] outputs as RPT rows x 4 columns, [DK][DVS] as DPT x 4.
@@ -427,29 +423,41 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_state_kernel(PrefillArgs a
   for (int c = 0; c < nsub; ++c) {
     const float* it = items + static_cast<size_t>(c) * W::ITEM;
     const int s0 = c * SUB, n = min(SUB, T - s0);
+    const uint32_t ph = c & 1;
     float4 u4[RPT];
 #pragma unroll
     for (int x = 0; x < RPT; ++x) u4[x] = *reinterpret_cast<const float4*>(it + W::U + (a0 + x) * DV + c0 + 4 * ci);
     const float el = it[W::EL];
-    ok = ok && mbar_wait(bar_wq, c & 1);
-    // v' = u - w S and qg S, both against the state before this sub-chunk.
+    ok = ok && mbar_wait(bar_w, ph) && mbar_wait(bar_q, ph);
+    // v' = u - w S and qg S, both against the state before this sub-chunk; four d per step.
     float accv[RPT][4], accq[RPT][4];
 #pragma unroll
     for (int x = 0; x < RPT; ++x)
 #pragma unroll
       for (int y = 0; y < 4; ++y) accv[x][y] = accq[x][y] = 0.f;
-#pragma unroll 4
-    for (int d = 0; d < DK; ++d) {
-      const float4 sv = *reinterpret_cast<const float4*>(st + d * DVS + 4 * ci);
-      const float s4[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll 2
+    for (int d = 0; d < DK; d += 4) {
+      float s4[4][4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float4 sv = *reinterpret_cast<const float4*>(st + (d + k) * DVS + 4 * ci);
+        s4[k][0] = sv.x;
+        s4[k][1] = sv.y;
+        s4[k][2] = sv.z;
+        s4[k][3] = sv.w;
+      }
 #pragma unroll
       for (int x = 0; x < RPT; ++x) {
-        const float wx = ws[(a0 + x) * W::RS + d], qx = qg[(a0 + x) * W::RS + d];
+        const float4 w4 = *reinterpret_cast<const float4*>(wk + (a0 + x) * W::RS + d);
+        const float4 q4 = *reinterpret_cast<const float4*>(qg + (a0 + x) * W::RS + d);
+        const float wx[4] = {w4.x, w4.y, w4.z, w4.w}, qx[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
-        for (int y = 0; y < 4; ++y) {
-          accv[x][y] = fmaf(wx, s4[y], accv[x][y]);
-          accq[x][y] = fmaf(qx, s4[y], accq[x][y]);
-        }
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int y = 0; y < 4; ++y) {
+            accv[x][y] = fmaf(wx[k], s4[k][y], accv[x][y]);
+            accq[x][y] = fmaf(qx[k], s4[k][y], accq[x][y]);
+          }
       }
     }
 #pragma unroll
@@ -461,23 +469,37 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_state_kernel(PrefillArgs a
       *reinterpret_cast<float4*>(vp + (a0 + x) * DVS + 4 * ci) = make_float4(v[0], v[1], v[2], v[3]);
     }
     __syncthreads();  // v' complete; w and qg are read
-    if (tid == 0 && ok && c + 1 < nsub) load_wq(c + 1);
-    ok = ok && mbar_wait(bar_ak, c & 1);
-    // o = qg S + Aqk v' (Aqk is zero above the diagonal), bf16 out.
+    if (tid == 0 && ok) {
+      load(bar_k, wk, c, W::KD, RS_BYTES);
+      if (c + 1 < nsub) load(bar_q, qg, c + 1, W::QG, RS_BYTES);
+    }
+    ok = ok && mbar_wait(bar_a, ph);
+    // o = qg S + Aqk v' (Aqk is zero above the diagonal), bf16 out; four b per step, the step past
+    // a0 + RPT - 1 adding zeros.
     {
       float acc[RPT][4];
 #pragma unroll
       for (int x = 0; x < RPT; ++x)
 #pragma unroll
         for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
-      for (int b = 0; b < a0 + RPT; ++b) {
-        const float4 vv = *reinterpret_cast<const float4*>(vp + b * DVS + 4 * ci);
-        const float v4[4] = {vv.x, vv.y, vv.z, vv.w};
+      for (int b = 0; b < a0 + RPT; b += 4) {
+        float v4[4][4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float4 vv = *reinterpret_cast<const float4*>(vp + (b + k) * DVS + 4 * ci);
+          v4[k][0] = vv.x;
+          v4[k][1] = vv.y;
+          v4[k][2] = vv.z;
+          v4[k][3] = vv.w;
+        }
 #pragma unroll
         for (int x = 0; x < RPT; ++x) {
-          const float m = aq[(a0 + x) * W::AS + b];
+          const float4 m4 = *reinterpret_cast<const float4*>(aq + (a0 + x) * W::AS + b);
+          const float m[4] = {m4.x, m4.y, m4.z, m4.w};
 #pragma unroll
-          for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(m, v4[y], acc[x][y]);
+          for (int k = 0; k < 4; ++k)
+#pragma unroll
+            for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(m[k], v4[k][y], acc[x][y]);
         }
       }
 #pragma unroll
@@ -490,6 +512,7 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_state_kernel(PrefillArgs a
         }
       }
     }
+    ok = ok && mbar_wait(bar_k, ph);
     // S = el S + kd^T v'.
     {
       float acc[DPT][4];
@@ -501,12 +524,24 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_state_kernel(PrefillArgs a
       for (int t = 0; t < SUB; ++t) {
         const float4 vv = *reinterpret_cast<const float4*>(vp + t * DVS + 4 * ci);
         const float v4[4] = {vv.x, vv.y, vv.z, vv.w};
+        float kx[DPT];
+        if constexpr (DPT % 4 == 0) {
 #pragma unroll
-        for (int x = 0; x < DPT; ++x) {
-          const float kx = kd[t * W::RS + d0 + x];
+          for (int x = 0; x < DPT; x += 4) {
+            const float4 k4 = *reinterpret_cast<const float4*>(wk + t * W::RS + d0 + x);
+            kx[x] = k4.x;
+            kx[x + 1] = k4.y;
+            kx[x + 2] = k4.z;
+            kx[x + 3] = k4.w;
+          }
+        } else {
 #pragma unroll
-          for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(kx, v4[y], acc[x][y]);
+          for (int x = 0; x < DPT; ++x) kx[x] = wk[t * W::RS + d0 + x];
         }
+#pragma unroll
+        for (int x = 0; x < DPT; ++x)
+#pragma unroll
+          for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(kx[x], v4[y], acc[x][y]);
       }
 #pragma unroll
       for (int x = 0; x < DPT; ++x)
@@ -517,7 +552,10 @@ __global__ void __launch_bounds__(256, 1) gdn_prefill_state_kernel(PrefillArgs a
         }
     }
     __syncthreads();  // S updated; kd, Aqk and v' are read
-    if (tid == 0 && ok && c + 1 < nsub) load_ak(c + 1);
+    if (tid == 0 && ok && c + 1 < nsub) {
+      load(bar_w, wk, c + 1, W::W, RS_BYTES);
+      load(bar_a, aq, c + 1, W::AQK, AS_BYTES);
+    }
   }
   // A copy that timed out (recorded in the device error word) leaves the state untouched.
   if (__syncthreads_or(!ok)) return;
