@@ -9,21 +9,22 @@
 //              same bf16 numbers, so writing first lets the attention read one key range.
 //   attention  one CTA per (KV head, 48 / G-token tile) holding that KV head's G query heads for those
 //              tokens (48 query rows), so each key and value tile is read once for G heads. Token t sees
-//              cache positions 0 .. start + t. The arithmetic keeps the reference's rounding points:
-//              scores are bf16-rounded fp32 dot products (its BF16 matmul); the online softmax walks the
-//              reference's own blocks of 2048 keys of [cache, chunk], each in two passes (the block's
-//              maximum, then weights exp(s - max) summed in fp32 and, rounded to bf16, multiplied into
-//              the values); the block's weighted values are rounded to bf16 (its BF16 matmul output)
-//              before the fp32 rescale-and-add. Output: bf16(out / total) * bf16(sigmoid(gate)) in
-//              bf16, then e5m2 for o_proj.
+//              cache positions 0 .. start + t. Scores and weighted values are mma.sync tensor-core
+//              products (BF16 in, fp32 accumulate) over 64-key tiles double-buffered by cp.async. The
+//              arithmetic keeps the reference's rounding points: scores are bf16-rounded fp32 dot
+//              products (its BF16 matmul); the online softmax walks the reference's own blocks of 2048
+//              keys of [cache, chunk], each in two passes (the block's maximum, then weights
+//              exp(s - max) summed in fp32 and, rounded to bf16, multiplied into the values); the
+//              block's weighted values are rounded to bf16 (its BF16 matmul output) before the fp32
+//              rescale-and-add. Output: bf16(out / total) * bf16(sigmoid(gate)) in bf16, then e5m2 for
+//              o_proj.
 #include "attn_common.cuh"
 
 namespace {
 
 using namespace q38;
 
-constexpr int kThreads = 256;
-constexpr int KT = 32;  // keys per tile (one per lane)
+constexpr int kThreads = 256;  // prep
 
 struct AttnPrefillArgs {
   const __nv_bfloat16* qkv;  // [tokens, ld_qkv]: per q head [query | gate], then k, then v
@@ -82,17 +83,23 @@ __global__ void __launch_bounds__(kThreads) attn_prefill_prep_kernel(AttnPrefill
   }
 }
 
-constexpr int RPW = 6;                       // query rows per warp
-constexpr int ROWS = RPW * (kThreads / 32);  // query rows per CTA: G heads x (ROWS / G) tokens
-constexpr int REF_BLOCK = 2048;              // keys per block of the reference's online softmax
+constexpr int PF_WARPS = 6;                   // two per 16-row MMA tile of the CTA's 48 query rows
+constexpr int PF_THREADS = PF_WARPS * 32;
+constexpr int ROWS = 48;                      // query rows per CTA: G heads x (ROWS / G) tokens
+constexpr int KB = 64;                        // keys per tile
+constexpr int REF_BLOCK = 2048;               // keys per block of the reference's online softmax
 
 template <int HD>
 struct PrefillSmem {
-  static constexpr size_t QF = 0;                                  // [ROWS][HD] fp32 queries
-  static constexpr size_t KTR = QF + sizeof(float) * ROWS * HD;    // [HD][KT] keys, transposed
-  static constexpr size_t VT = KTR + sizeof(float) * HD * KT;      // [KT][HD] values
-  static constexpr size_t PW = VT + sizeof(float) * KT * HD;       // [ROWS][KT] bf16-rounded weights
-  static constexpr size_t TOTAL = PW + sizeof(float) * ROWS * KT;
+  static constexpr int QP = HD + 8;  // padded bf16 rows: the 8 rows of an ldmatrix land in distinct banks
+  static constexpr int PP = KB + 8;
+  static constexpr size_t QS = 0;                                      // [ROWS][QP] bf16 queries
+  static constexpr size_t KS = QS + 2 * ROWS * QP;                     // [2][KB][QP] bf16 key tiles
+  static constexpr size_t VS = KS + 2 * 2 * KB * QP;                   // [2][KB][QP] bf16 value tiles
+  static constexpr size_t PS = VS + 2 * 2 * KB * QP;                   // [ROWS][PP] bf16 weights
+  static constexpr size_t RED = PS + 2 * ROWS * PP;                    // [2][ROWS] fp32, per half-warp pair
+  static constexpr size_t TOTAL = RED + sizeof(float) * 2 * ROWS;
+  static_assert(KS % 16 == 0 && VS % 16 == 0 && PS % 16 == 0 && RED % 16 == 0, "16-byte aligned regions");
 };
 
 // The reference's softmax block of a key: it concatenates the row's cache (max_seq positions, those
@@ -103,95 +110,114 @@ __device__ __forceinline__ int64_t ref_block(int64_t key, int64_t start, int64_t
   return (key < start ? key : max_seq + key - start) / REF_BLOCK;
 }
 
-// Rows of the CTA: r = g * tq + tt (query head g of the KV head, token t0 + tt); warp w owns rows
-// w * RPW .. w * RPW + RPW - 1.
+// Rows of the CTA: r = g * tq + tt (query head g of the KV head, token t0 + tt), 3 MMA row tiles;
+// warp w holds row tile w / 2 and, of each 64-key tile, keys 32 (w % 2) .. + 31 for the scores and
+// head dims (w % 2) HD / 2 .. + HD / 2 - 1 for the weighted values. Scores and weighted values run on
+// mma.sync (BF16 in, fp32 accumulate): the reference's BF16 matmuls.
 template <int HD>
-__global__ void __launch_bounds__(kThreads, 1) attn_prefill_kernel(AttnPrefillArgs a) {
+__global__ void __launch_bounds__(PF_THREADS, 1) attn_prefill_kernel(AttnPrefillArgs a) {
   using S = PrefillSmem<HD>;
-  constexpr int DPL = HD / 32;  // output dims per lane
+  constexpr int QP = S::QP, PP = S::PP;
+  constexpr int KSTEPS = HD / 16;  // score k-steps over head_dim
+  constexpr int NTW = HD / 16;     // weighted-value n-tiles (8 dims) per warp: half the head
+  static_assert(NTW % 2 == 0, "n-tiles in pairs per ldmatrix");
   extern __shared__ __align__(16) uint8_t smem[];
-  float* qf = reinterpret_cast<float*>(smem + S::QF);
-  float* kT = reinterpret_cast<float*>(smem + S::KTR);
-  float* vt = reinterpret_cast<float*>(smem + S::VT);
-  float* pw = reinterpret_cast<float*>(smem + S::PW);
+  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem + S::QS);
+  __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(smem + S::KS);
+  __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(smem + S::VS);
+  __nv_bfloat16* ps = reinterpret_cast<__nv_bfloat16*>(smem + S::PS);
+  float* red = reinterpret_cast<float*>(smem + S::RED);
   const int G = a.groups;
   const int tq = ROWS / G;
   const int kvh = blockIdx.x;
   const int t0 = blockIdx.y * tq;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-
-  for (int i = tid; i < ROWS * HD; i += kThreads) {
-    const int r = i / HD, d = i % HD;
-    const int g = r / tq, t = t0 + r % tq;
-    qf[i] = t < a.tokens ? __bfloat162float(a.qs[((static_cast<int64_t>(kvh) * G + g) * a.tokens + t) * HD + d]) : 0.f;
-  }
+  const int wm = warp >> 1, wh = warp & 1;
   const int t_last = min(t0 + tq, a.tokens) - 1;
   const int n_keys = a.start + t_last + 1;
   const __nv_bfloat16* kc = a.k_cache + static_cast<int64_t>(kvh) * a.max_seq * HD;
   const __nv_bfloat16* vc = a.v_cache + static_cast<int64_t>(kvh) * a.max_seq * HD;
 
-  const int r0 = warp * RPW;
-  int tok[RPW];
-  float best[RPW], total[RPW], out[RPW][DPL];
-#pragma unroll
-  for (int x = 0; x < RPW; ++x) {
-    tok[x] = t0 + (r0 + x) % tq;
-    best[x] = -INFINITY;
-    total[x] = 0.f;
-#pragma unroll
-    for (int d = 0; d < DPL; ++d) out[x][d] = 0.f;
+  // Queries (rows past the chunk are zero).
+  for (int i = tid; i < ROWS * (HD / 8); i += PF_THREADS) {
+    const int r = i / (HD / 8), c = i % (HD / 8);
+    const int g = r / tq, t = t0 + r % tq;
+    const __nv_bfloat16* src = a.qs + ((static_cast<int64_t>(kvh) * G + g) * a.tokens + min(t, a.tokens - 1)) * HD + 8 * c;
+    cp_async16(smem_u32(qs + r * QP + 8 * c), src, t < a.tokens ? 16u : 0u);
   }
+  cp_async_commit();
 
-  // Stages keys [kb, kb + KT) (and values) of this KV head; zero past n_keys.
-  auto load_tile = [&](int kb, bool values) {
-    __syncthreads();  // the previous tile is consumed (and, the first time, the queries are staged)
-    for (int i = tid; i < KT * (HD / 8); i += kThreads) {
-      const int j = i / (HD / 8), c = (i % (HD / 8)) * 8;
-      uint4 ku = make_uint4(0, 0, 0, 0), vu = make_uint4(0, 0, 0, 0);
-      if (kb + j < n_keys) {
-        ku = __ldg(reinterpret_cast<const uint4*>(kc + static_cast<int64_t>(kb + j) * HD + c));
-        if (values) vu = __ldg(reinterpret_cast<const uint4*>(vc + static_cast<int64_t>(kb + j) * HD + c));
-      }
-      const __nv_bfloat16* kh = reinterpret_cast<const __nv_bfloat16*>(&ku);
-      const __nv_bfloat16* vh = reinterpret_cast<const __nv_bfloat16*>(&vu);
+  // This thread's two rows (MMA fragment rows lane / 4 and + 8 of its row tile): key bounds.
+  const int rlo = 16 * wm + (lane >> 2), rhi = rlo + 8;
+  const int tlo = t0 + rlo % tq, thi = t0 + rhi % tq;
+  const int lim_lo = tlo < a.tokens ? a.start + tlo + 1 : 0;  // keys < lim are visible to the row
+  const int lim_hi = thi < a.tokens ? a.start + thi + 1 : 0;
+
+  // Keys [kb, kb + KB) (and values) into buffer `buf`; zero past n_keys.
+  auto load_tile = [&](int kb, int buf, bool values) {
+    __nv_bfloat16* kd = ks + buf * KB * QP;
+    __nv_bfloat16* vd = vs + buf * KB * QP;
+    for (int i = tid; i < KB * (HD / 8); i += PF_THREADS) {
+      const int j = i / (HD / 8), c = i % (HD / 8);
+      const int key = kb + j;
+      const bool in = key < n_keys;
+      const int64_t off = static_cast<int64_t>(in ? key : 0) * HD + 8 * c;
+      cp_async16(smem_u32(kd + j * QP + 8 * c), kc + off, in ? 16u : 0u);
+      if (values) cp_async16(smem_u32(vd + j * QP + 8 * c), vc + off, in ? 16u : 0u);
+    }
+    cp_async_commit();
+  };
+  // This warp's scores: its 16 rows x 32 keys of the tile in buffer `buf`, bf16-rounded, -inf where
+  // the key is hidden from the row or outside [kb, kend).
+  auto scores = [&](int buf, int kb, int kend, float (&s)[4][4]) {
+    const __nv_bfloat16* kt = ks + buf * KB * QP;
+    float acc[4][4];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        kT[(c + e) * KT + j] = __bfloat162float(kh[e]);
-        if (values) vt[j * HD + c + e] = __bfloat162float(vh[e]);
+    for (int nt = 0; nt < 4; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    const uint32_t abase = smem_u32(qs + (16 * wm + (lane & 15)) * QP + 8 * (lane >> 4));
+    const int krow = 32 * wh + (lane & 7) + 8 * (lane >> 4);
+#pragma unroll
+    for (int k = 0; k < KSTEPS; ++k) {
+      uint32_t af[4];
+      ldsm_x4(abase + k * 32, af[0], af[1], af[2], af[3]);
+#pragma unroll
+      for (int np = 0; np < 2; ++np) {
+        uint32_t b0, b1, b2, b3;  // keys 16 np + 0..7 (b0, b1) and + 8..15 (b2, b3), dims 16 k .. + 15
+        ldsm_x4(smem_u32(kt + (krow + 16 * np) * QP + 16 * k + 8 * ((lane >> 3) & 1)), b0, b1, b2, b3);
+        mma_bf16_16816(acc[2 * np], af, b0, b1);
+        mma_bf16_16816(acc[2 * np + 1], af, b2, b3);
       }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) {
+      const int key = kb + 32 * wh + 8 * nt + 2 * (lane & 3);
+      s[nt][0] = key < kend && key < lim_lo ? bf16r(acc[nt][0]) : -INFINITY;
+      s[nt][1] = key + 1 < kend && key + 1 < lim_lo ? bf16r(acc[nt][1]) : -INFINITY;
+      s[nt][2] = key < kend && key < lim_hi ? bf16r(acc[nt][2]) : -INFINITY;
+      s[nt][3] = key + 1 < kend && key + 1 < lim_hi ? bf16r(acc[nt][3]) : -INFINITY;
+    }
+  };
+  // Per row across the two warps of a row tile: red[half][row], combined half 0 then half 1.
+  auto pair_combine = [&](float lo, float hi, bool is_max, float& out_lo, float& out_hi) {
+    if ((lane & 3) == 0) {
+      red[wh * ROWS + rlo] = lo;
+      red[wh * ROWS + rhi] = hi;
     }
     __syncthreads();
+    out_lo = is_max ? fmaxf(red[rlo], red[ROWS + rlo]) : __fadd_rn(red[rlo], red[ROWS + rlo]);
+    out_hi = is_max ? fmaxf(red[rhi], red[ROWS + rhi]) : __fadd_rn(red[rhi], red[ROWS + rhi]);
+    __syncthreads();  // red is read before it is written again
   };
-  // Scores of this warp's rows against the staged keys (lane = key), bf16-rounded, -inf where hidden.
-  auto scores = [&](int kb, float (&s)[RPW]) {
-    float acc[RPW];
+
+  float out[NTW][4];
 #pragma unroll
-    for (int x = 0; x < RPW; ++x) acc[x] = 0.f;
-#pragma unroll 2
-    for (int d = 0; d < HD; d += 4) {
-      const float k0 = kT[(d + 0) * KT + lane], k1 = kT[(d + 1) * KT + lane];
-      const float k2 = kT[(d + 2) * KT + lane], k3 = kT[(d + 3) * KT + lane];
-#pragma unroll
-      for (int x = 0; x < RPW; ++x) {
-        const float4 q = *reinterpret_cast<const float4*>(qf + (r0 + x) * HD + d);
-        acc[x] = fmaf(q.x, k0, acc[x]);
-        acc[x] = fmaf(q.y, k1, acc[x]);
-        acc[x] = fmaf(q.z, k2, acc[x]);
-        acc[x] = fmaf(q.w, k3, acc[x]);
-      }
-    }
-    const int key = kb + lane;
-#pragma unroll
-    for (int x = 0; x < RPW; ++x) {
-      const bool vis = tok[x] < a.tokens && key < n_keys && key <= a.start + tok[x];
-      s[x] = vis ? bf16r(acc[x]) : -INFINITY;
-    }
-  };
+  for (int n = 0; n < NTW; ++n) out[n][0] = out[n][1] = out[n][2] = out[n][3] = 0.f;
+  float best_lo = -INFINITY, best_hi = -INFINITY, tot_lo = 0.f, tot_hi = 0.f;
 
   for (int seg = 0; seg < n_keys;) {
     // The keys of one reference block: [seg, seg_end).
     const int64_t blk = ref_block(seg, a.start, a.max_seq);
-    int seg_end = seg + 1;
+    int seg_end;
     {
       // ref_block is nondecreasing in the key index: find where it moves past blk.
       int64_t lo = seg, hi = n_keys;  // blk(lo) == blk, answer in (lo, hi]
@@ -202,83 +228,127 @@ __global__ void __launch_bounds__(kThreads, 1) attn_prefill_kernel(AttnPrefillAr
       }
       seg_end = static_cast<int>(hi);
     }
-    // Pass 1: the block's maximum per row.
-    float bm[RPW];
-#pragma unroll
-    for (int x = 0; x < RPW; ++x) bm[x] = -INFINITY;
-    for (int kb = seg; kb < seg_end; kb += KT) {
-      load_tile(kb, false);
-      float s[RPW];
-      scores(kb, s);
-#pragma unroll
-      for (int x = 0; x < RPW; ++x) {
-        const bool in = kb + lane < seg_end;
-        bm[x] = fmaxf(bm[x], warp_max(in ? s[x] : -INFINITY));
+    // Pass 1: the block's maximum score per row.
+    float bm_lo = -INFINITY, bm_hi = -INFINITY;
+    load_tile(seg, 0, false);
+    for (int kb = seg, buf = 0; kb < seg_end; kb += KB, buf ^= 1) {
+      if (kb + KB < seg_end) {
+        load_tile(kb + KB, buf ^ 1, false);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
       }
+      __syncthreads();
+      float sc[4][4];
+      scores(buf, kb, seg_end, sc);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        bm_lo = fmaxf(bm_lo, fmaxf(sc[nt][0], sc[nt][1]));
+        bm_hi = fmaxf(bm_hi, fmaxf(sc[nt][2], sc[nt][3]));
+      }
+      __syncthreads();  // the tile is consumed before its buffer is refilled
     }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      bm_lo = fmaxf(bm_lo, __shfl_xor_sync(0xffffffffu, bm_lo, o));
+      bm_hi = fmaxf(bm_hi, __shfl_xor_sync(0xffffffffu, bm_hi, o));
+    }
+    pair_combine(bm_lo, bm_hi, true, bm_lo, bm_hi);
     // Pass 2: weights exp(s - nb), their fp32 sum, and the weighted values with bf16 weights.
-    float nb[RPW], bsum[RPW], acc[RPW][DPL];
+    const float nb_lo = fmaxf(best_lo, bm_lo), nb_hi = fmaxf(best_hi, bm_hi);
+    float acc[NTW][4];
 #pragma unroll
-    for (int x = 0; x < RPW; ++x) {
-      nb[x] = fmaxf(best[x], bm[x]);
-      bsum[x] = 0.f;
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) acc[x][d] = 0.f;
-    }
-    for (int kb = seg; kb < seg_end; kb += KT) {
-      load_tile(kb, true);
-      float s[RPW];
-      scores(kb, s);
-#pragma unroll
-      for (int x = 0; x < RPW; ++x) {
-        const bool in = kb + lane < seg_end && s[x] != -INFINITY;
-        const float p = in ? expf(__fsub_rn(s[x], nb[x])) : 0.f;
-        bsum[x] = __fadd_rn(bsum[x], warp_sum(p));
-        pw[(r0 + x) * KT + lane] = bf16r(p);
+    for (int n = 0; n < NTW; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+    float bs_lo = 0.f, bs_hi = 0.f;
+    load_tile(seg, 0, true);
+    for (int kb = seg, buf = 0; kb < seg_end; kb += KB, buf ^= 1) {
+      if (kb + KB < seg_end) {
+        load_tile(kb + KB, buf ^ 1, true);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
       }
-      __syncwarp();
-#pragma unroll 4
-      for (int j = 0; j < KT; ++j) {
-        float vv[DPL];
+      __syncthreads();
+      float sc[4][4];
+      scores(buf, kb, seg_end, sc);
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) vv[d] = vt[j * HD + lane * DPL + d];
+      for (int nt = 0; nt < 4; ++nt) {
+        const float p0 = sc[nt][0] == -INFINITY ? 0.f : expf(__fsub_rn(sc[nt][0], nb_lo));
+        const float p1 = sc[nt][1] == -INFINITY ? 0.f : expf(__fsub_rn(sc[nt][1], nb_lo));
+        const float p2 = sc[nt][2] == -INFINITY ? 0.f : expf(__fsub_rn(sc[nt][2], nb_hi));
+        const float p3 = sc[nt][3] == -INFINITY ? 0.f : expf(__fsub_rn(sc[nt][3], nb_hi));
+        bs_lo = __fadd_rn(__fadd_rn(bs_lo, p0), p1);
+        bs_hi = __fadd_rn(__fadd_rn(bs_hi, p2), p3);
+        const int col = 32 * wh + 8 * nt + 2 * (lane & 3);
+        *reinterpret_cast<uint32_t*>(ps + rlo * PP + col) = pack_bf16x2(p0, p1);
+        *reinterpret_cast<uint32_t*>(ps + rhi * PP + col) = pack_bf16x2(p2, p3);
+      }
+      // The two warps of this row tile have written its weights.
+      asm volatile("bar.sync %0, %1;" ::"r"(1 + wm), "r"(64) : "memory");
+      const uint32_t pbase = smem_u32(ps + (16 * wm + (lane & 15)) * PP + 8 * (lane >> 4));
+      const __nv_bfloat16* vt = vs + buf * KB * QP;
 #pragma unroll
-        for (int x = 0; x < RPW; ++x) {
-          const float p = pw[(r0 + x) * KT + j];
+      for (int k = 0; k < KB / 16; ++k) {
+        uint32_t pa[4];
+        ldsm_x4(pbase + k * 32, pa[0], pa[1], pa[2], pa[3]);
+        const int vr = 16 * k + (lane & 7) + 8 * ((lane >> 3) & 1);  // x4.trans: (keys 0-7 | 8-15) x (n | n + 1)
 #pragma unroll
-          for (int d = 0; d < DPL; ++d) acc[x][d] = fmaf(p, vv[d], acc[x][d]);
+        for (int n = 0; n < NTW; n += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(smem_u32(vt + vr * QP + wh * (HD / 2) + 8 * (n + (lane >> 4))), b0, b1, b2, b3);
+          mma_bf16_16816(acc[n], pa, b0, b1);
+          mma_bf16_16816(acc[n + 1], pa, b2, b3);
         }
       }
-      __syncwarp();
+      __syncthreads();  // keys, values and weights are consumed before the buffers are refilled
     }
+#pragma unroll
+    for (int o = 1; o <= 2; o <<= 1) {
+      bs_lo = __fadd_rn(bs_lo, __shfl_xor_sync(0xffffffffu, bs_lo, o));
+      bs_hi = __fadd_rn(bs_hi, __shfl_xor_sync(0xffffffffu, bs_hi, o));
+    }
+    pair_combine(bs_lo, bs_hi, false, bs_lo, bs_hi);
     // Merge the block (the reference's out * rescale + bf16(wts @ values)); rows that see nothing in
     // this block are unchanged (their weights there are exactly zero).
+    if (bm_lo != -INFINITY) {
+      const float rescale = best_lo == -INFINITY ? 0.f : expf(__fsub_rn(best_lo, nb_lo));
+      tot_lo = __fadd_rn(__fmul_rn(tot_lo, rescale), bs_lo);
 #pragma unroll
-    for (int x = 0; x < RPW; ++x) {
-      if (bm[x] == -INFINITY) continue;
-      const float rescale = best[x] == -INFINITY ? 0.f : expf(__fsub_rn(best[x], nb[x]));
-      total[x] = __fadd_rn(__fmul_rn(total[x], rescale), bsum[x]);
+      for (int n = 0; n < NTW; ++n)
 #pragma unroll
-      for (int d = 0; d < DPL; ++d) out[x][d] = __fadd_rn(__fmul_rn(out[x][d], rescale), bf16r(acc[x][d]));
-      best[x] = nb[x];
+        for (int e = 0; e < 2; ++e) out[n][e] = __fadd_rn(__fmul_rn(out[n][e], rescale), bf16r(acc[n][e]));
+      best_lo = nb_lo;
+    }
+    if (bm_hi != -INFINITY) {
+      const float rescale = best_hi == -INFINITY ? 0.f : expf(__fsub_rn(best_hi, nb_hi));
+      tot_hi = __fadd_rn(__fmul_rn(tot_hi, rescale), bs_hi);
+#pragma unroll
+      for (int n = 0; n < NTW; ++n)
+#pragma unroll
+        for (int e = 2; e < 4; ++e) out[n][e] = __fadd_rn(__fmul_rn(out[n][e], rescale), bf16r(acc[n][e]));
+      best_hi = nb_hi;
     }
     seg = seg_end;
   }
   // Epilogue: bf16(out / total) * bf16(sigmoid(gate)), e5m2.
 #pragma unroll
-  for (int x = 0; x < RPW; ++x) {
-    const int t = tok[x];
+  for (int half = 0; half < 2; ++half) {
+    const int r = half ? rhi : rlo;
+    const int t = half ? thi : tlo;
     if (t >= a.tokens) continue;
-    const int h = kvh * G + (r0 + x) / tq;
+    const float total = half ? tot_hi : tot_lo;
+    const int h = kvh * G + r / tq;
     const __nv_bfloat16* gate = a.qkv + static_cast<int64_t>(t) * a.ld_qkv + static_cast<int64_t>(h) * 2 * HD + HD;
     uint8_t* dst = a.out + static_cast<int64_t>(t) * a.ld_out + static_cast<int64_t>(h) * HD;
 #pragma unroll
-    for (int d = 0; d < DPL; ++d) {
-      const int dd = lane * DPL + d;
-      const float ob = bf16r(__fdiv_rn(out[x][d], total[x]));
-      const float gs = bf16r(sigmoidf_(__bfloat162float(gate[dd])));
-      dst[dd] = f32_to_e5m2(bf16r(__fmul_rn(ob, gs)));
-    }
+    for (int n = 0; n < NTW; ++n)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int dd = wh * (HD / 2) + 8 * n + 2 * (lane & 3) + e;
+        const float ob = bf16r(__fdiv_rn(out[n][2 * half + e], total));
+        const float gs = bf16r(sigmoidf_(__bfloat162float(gate[dd])));
+        dst[dd] = f32_to_e5m2(bf16r(__fmul_rn(ob, gs)));
+      }
   }
 }
 
@@ -301,7 +371,7 @@ int launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t stream) {
   if (e != cudaSuccess) return q38host::cuda_status(e, "attn_prefill_prep launch");
   const int tq = ROWS / a.groups;
   dim3 grid(a.num_kv_heads, (a.tokens + tq - 1) / tq);
-  attn_prefill_kernel<HD><<<grid, kThreads, S::TOTAL, stream>>>(a);
+  attn_prefill_kernel<HD><<<grid, PF_THREADS, S::TOTAL, stream>>>(a);
   return q38host::cuda_status(cudaGetLastError(), "attn_prefill launch");
 }
 
