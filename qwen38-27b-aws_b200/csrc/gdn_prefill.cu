@@ -295,9 +295,12 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_chunk_kernel(PrefillArgs a
 #pragma unroll
     for (int r = 0; r < 16; ++r) inv[(blk * 16 + r) * 16 + col_i] = col[r];
   }
-  // qg = q e^{gc}, kd = k e^{gc_last - gc}, token-major with padded rows.
+  // qg = q e^{gc}, kd = k e^{gc_last - gc}, token-major with padded rows. A warp covers 8 features x
+  // 4 tokens: its shared-memory reads of the [d][t] tiles hit 32 distinct banks, its global writes are
+  // four 32-byte runs.
   for (int i = tid; i < SUB * DK; i += 256) {
-    const int t = i / DK, d = i % DK;
+    const int l = i & 31, grp = i >> 5;
+    const int d = (grp % (DK / 8)) * 8 + (l & 7), t = (grp / (DK / 8)) * 4 + (l >> 3);
     item[W::QG + t * W::RS + d] = __fmul_rn(qT[d * SUBP + t], eg[t]);
     item[W::KD + t * W::RS + d] = __fmul_rn(kT[d * SUBP + t], wl[t]);
   }
@@ -312,9 +315,14 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_chunk_kernel(PrefillArgs a
 #pragma unroll
       for (int t = 0; t < SUB; ++t) x[t] = t < n ? __fmul_rn(be[t], vsrc[static_cast<int64_t>(t) * DV]) : 0.f;
     } else {
-      const float* kcol = kT + (j - DV) * SUBP;
+      const float* kcol = kT + (j - DV) * SUBP;  // 16-byte reads: a warp's 32 rows take the minimum 4 wavefronts
 #pragma unroll
-      for (int t = 0; t < SUB; ++t) x[t] = __fmul_rn(__fmul_rn(kcol[t], be[t]), eg[t]);
+      for (int t = 0; t < SUB; t += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(kcol + t);
+        const float kk[4] = {k4.x, k4.y, k4.z, k4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) x[t + e] = __fmul_rn(__fmul_rn(kk[e], be[t + e]), eg[t + e]);
+      }
     }
 #pragma unroll
     for (int blk = 0; blk < SUB / 16; ++blk) {
