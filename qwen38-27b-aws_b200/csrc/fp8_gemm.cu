@@ -630,7 +630,9 @@ __global__ void __launch_bounds__(192, 1)
 
 // ---------------------------------------------------------------------------------------------
 // Persistent form for unsplit GEMMs (EPI_BF16, EPI_SILU): each CTA (or 2-SM pair) walks output
-// tiles. The producer's stage ring runs on across tiles; the MMA warp waits for "TMEM empty" before a
+// tiles, unit u = (weight rows u / n_tiles, token tile u % n_tiles): the token tiles of one weight tile
+// go to neighbouring groups at the same time, so the weight tile comes from HBM once and from L2 for
+// the others. The producer's stage ring runs on across tiles; the MMA warp waits for "TMEM empty" before a
 // tile's first MMA; the epilogue warps drain the accumulator into their own staging buffer, release
 // TMEM at once, and store while the next tile's mainloop runs. Per-CTA setup and the pipeline fill
 // are paid once per CTA instead of once per tile, and a grid that would take 1.8 waves becomes one
@@ -743,14 +745,14 @@ __global__ void __launch_bounds__(192, 1)
       // The first pass over the ring needs no slot to drain: the first tile's weights go first.
       int pre = 0;
       if (group < units) {
-        const int mt = PAIR ? 2 * (group % m_units) + prank : group % m_units;
+        const int mt = PAIR ? 2 * (group / n_tiles) + prank : group / n_tiles;
         pre = min(nk, C::STAGES);
         for (int i = 0; i < pre; ++i) load_w(i, mt, i);
       }
       pdl_wait();
       int it = 0;
       for (int u = group; u < units && !flags[0]; u += ngroups) {
-        const int mp = u % m_units, nt = u / m_units;
+        const int mp = u / n_tiles, nt = u % n_tiles;
         const int mt = PAIR ? 2 * mp + prank : mp;
         const int n0 = nt * NTOK;
         for (int i = 0; i < nk; ++i, ++it) {
@@ -844,7 +846,7 @@ __global__ void __launch_bounds__(192, 1)
     pdl_wait();
     int tc = 0;
     for (int u = group; u < units; u += ngroups, ++tc) {
-      const int mp = u % m_units, nt = u / m_units;
+      const int mp = u / n_tiles, nt = u % n_tiles;
       const int mt = PAIR ? 2 * mp + prank : mp;
       const int m0 = mt * BM, n0 = nt * NTOK;
       const bool ok = !epi_bar_or(!mbar_wait(accf, tc & 1));
