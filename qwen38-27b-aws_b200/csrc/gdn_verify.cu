@@ -155,7 +155,7 @@ struct VerifySmem {
   static constexpr size_t FLOATS = static_cast<size_t>(KMAX) * DV        // xv: the K tokens' v (conv + SiLU)
                                    + 2 * KMAX * DK                       // qn, kn
                                    + KMAX * DK + KMAX * DV               // weighted pending keys, pending deltas
-                                   + 4 * 2 * KMAX * DV                   // the 4 warps' [k; q]^T S' partials
+                                   + 4 * KMAX * DV                       // the 4 warps' k^T S' partials, then q^T S'
                                    + KMAX * DV                           // outputs before the norm
                                    + 2 * KMAX * KMAX + 2 * KMAX + KMAX + 4;  // dots, gates, commit weights, scale
   static constexpr size_t TOTAL = TILE + sizeof(float) * FLOATS + 16;
@@ -176,8 +176,8 @@ __global__ void __launch_bounds__(128) gdn_verify_kernel(VerifyArgs a, const flo
   float* kn = qn + KMAX * DK;                            // [KMAX][DK]
   float* wk = kn + KMAX * DK;                            // [KMAX][DK]
   float* dl = wk + KMAX * DK;                            // [KMAX][DV]
-  float* red = dl + KMAX * DV;                           // [4][2 KMAX][DV]
-  float* ob = red + 4 * 2 * KMAX * DV;                   // [KMAX][DV]
+  float* red = dl + KMAX * DV;                           // [4][KMAX][DV], k^T S' partials, then q^T S'
+  float* ob = red + 4 * KMAX * DV;                       // [KMAX][DV]
   float* dots = ob + KMAX * DV;                          // [2][KMAX][KMAX]
   float* gt = dots + 2 * KMAX * KMAX;                    // [KMAX][2] beta, log decay
   float* fw = gt + 2 * KMAX;                             // [KMAX] commit weights
@@ -333,23 +333,38 @@ __global__ void __launch_bounds__(128) gdn_verify_kernel(VerifyArgs a, const flo
       }
     }
   }
+  // The 4 warps' partials summed per column in warp order, k^T S' first, then q^T S' through the same
+  // buffer (half the shared memory of both at once: 4 CTAs per SM instead of 3). One column per thread.
+  static_assert(DV <= 128, "one state column per thread");
+  const int c = tid;
+  float ksum[KMAX], qsum[KMAX];
 #pragma unroll
-  for (int t = 0; t < KMAX; ++t) {
-    if (t >= K) break;
+  for (int half = 0; half < 2; ++half) {
 #pragma unroll
-    for (int e = 0; e < CPL; ++e) {
-      red[(warp * 2 * KMAX + t) * DV + c0 + e] = prod[t][e];
-      red[(warp * 2 * KMAX + KMAX + t) * DV + c0 + e] = prod[KMAX + t][e];
+    for (int t = 0; t < KMAX; ++t) {
+      if (t >= K) break;
+#pragma unroll
+      for (int e = 0; e < CPL; ++e) red[(warp * KMAX + t) * DV + c0 + e] = prod[half * KMAX + t][e];
     }
-  }
-  fence_proxy_async_shared();  // the committed tile is visible to the bulk copy engine
-  __syncthreads();
-  if (tid == 0 && on) {
-    bulk_store(a.state + (static_cast<int64_t>(b) * a.num_v_heads + h) * DK * DV, tile, TILE_BYTES);
-    bulk_commit();
+    if (half == 0) fence_proxy_async_shared();  // the committed tile is visible to the bulk copy engine
+    __syncthreads();
+    if (half == 0 && tid == 0 && on) {
+      bulk_store(a.state + (static_cast<int64_t>(b) * a.num_v_heads + h) * DK * DV, tile, TILE_BYTES);
+      bulk_commit();
+    }
+#pragma unroll
+    for (int t = 0; t < KMAX; ++t) {
+      float sum = 0.f;
+      if (t < K && c < DV) {
+#pragma unroll
+        for (int w = 0; w < 4; ++w) sum = __fadd_rn(sum, red[(w * KMAX + t) * DV + c]);
+      }
+      (half == 0 ? ksum : qsum)[t] = sum;
+    }
+    __syncthreads();  // the partials are read before the buffer is reused
   }
   // The K x K chunk, one state column per thread.
-  for (int c = tid; c < DV; c += 128) {
+  if (c < DV) {
     float cum[KMAX], dlt[KMAX];
 #pragma unroll
     for (int t = 0; t < KMAX; ++t) {
@@ -359,12 +374,7 @@ __global__ void __launch_bounds__(128) gdn_verify_kernel(VerifyArgs a, const flo
 #pragma unroll
     for (int t = 0; t < KMAX; ++t) {
       if (t >= K) break;
-      float ks = 0.f, qs = 0.f;
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {
-        ks = __fadd_rn(ks, red[(w * 2 * KMAX + t) * DV + c]);
-        qs = __fadd_rn(qs, red[(w * 2 * KMAX + KMAX + t) * DV + c]);
-      }
+      const float ks = ksum[t], qs = qsum[t];
       float dd = __fsub_rn(xv[t * DV + c], __fmul_rn(expf(cum[t]), ks));
 #pragma unroll
       for (int s = 0; s < t; ++s)
