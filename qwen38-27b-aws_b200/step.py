@@ -416,18 +416,18 @@ class B200Step:
         if "accepted" in inputs:
             out = self.verify(inputs_embeds, inputs["cos"], inputs["sin"], inputs["position"], inputs["active"],
                               inputs["accepted"])
-            return out.to("cpu").reshape(self.batch, self.verify_tokens, -1)
+            return _to_host(out).reshape(self.batch, self.verify_tokens, -1)
         if "slot" in inputs:
             scalar = lambda name: int(inputs[name].reshape(-1)[0])  # noqa: E731
             out = self.prefill(inputs_embeds, inputs["cos"], inputs["sin"], scalar("slot"), scalar("start"),
                                scalar("n_valid"))
-            return out.to("cpu").reshape(1, inputs_embeds.shape[1], -1)
+            return _to_host(out).reshape(1, inputs_embeds.shape[1], -1)
         rows = inputs_embeds.shape[0]
         if rows != self.batch or inputs_embeds.shape[1] != 1:
             raise ValueError(f"decode takes [{self.batch}, 1, hidden], got {tuple(inputs_embeds.shape)}")
         self.load_decode_inputs(inputs_embeds, inputs["cos"], inputs["sin"], inputs["position"], inputs["active"])
         out = self.decode_device()
-        return out.to("cpu", non_blocking=False).reshape(rows, 1, -1)
+        return _to_host(out).reshape(rows, 1, -1)
 
     def load_decode_inputs(self, embeds, cos, sin, position, active):
         self.x_in.copy_(embeds.reshape(self.batch, -1), non_blocking=True)
@@ -447,6 +447,17 @@ class B200Step:
             if l.kind == LINEAR:
                 l.mixer.state[dst].copy_(l.mixer.state[src])
                 l.mixer.conv_state[dst].copy_(l.mixer.conv_state[src])
+
+
+def _to_host(t: torch.Tensor) -> torch.Tensor:
+    """A new host tensor holding t, in page-locked memory from torch's caching host allocator (a fresh
+    tensor per call costs no allocation once the cache holds a block of its size), copied at full PCIe
+    speed; returns once the copy is done. Page-locked outputs also make a caller's copy back to the
+    device (the head's input) a true asynchronous copy."""
+    out = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+    out.copy_(t, non_blocking=True)
+    torch.cuda.current_stream(t.device).synchronize()
+    return out
 
 
 class B200Head:
@@ -483,4 +494,4 @@ class B200Head:
         if rows != self.batch:
             raise ValueError(f"the head graph takes {self.batch} rows, got {rows}")
         self.hidden.copy_(hidden.reshape(rows, -1), non_blocking=True)
-        return self.maxima_device().to("cpu")
+        return _to_host(self.maxima_device())
