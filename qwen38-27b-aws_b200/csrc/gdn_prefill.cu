@@ -62,8 +62,15 @@ struct PrefillArgs {
 // ---------------------------------------------------------------------------------------------
 // prep
 // ---------------------------------------------------------------------------------------------
+// Threads of a prep CTA: two channels each (of 2 dk + R dv), so no thread waits on another's third.
 template <int DK, int DV, int R>
-__global__ void __launch_bounds__(256, 2) gdn_prefill_prep_kernel(PrefillArgs a) {
+constexpr int prep_threads() {
+  return ((2 * DK + R * DV + 1) / 2 + 31) / 32 * 32;
+}
+constexpr int PREP_MAX_THREADS = 320;
+
+template <int DK, int DV, int R>
+__global__ void __launch_bounds__(PREP_MAX_THREADS, 2) gdn_prefill_prep_kernel(PrefillArgs a) {
   constexpr int CH = 2 * DK + R * DV;
   extern __shared__ __align__(16) uint8_t smem[];
   float* xs = reinterpret_cast<float*>(smem);  // [CH][PREP_TOK + 1]
@@ -677,7 +684,8 @@ int launch_prefill(PrefillArgs a, int conv_dim, cudaStream_t stream) {
     done_mask |= 1ull << dev;
   }
   dim3 gp((a.tokens + PREP_TOK - 1) / PREP_TOK, a.num_k_heads);
-  gdn_prefill_prep_kernel<DK, DV, R><<<gp, 256, prep_smem, stream>>>(a);
+  static_assert(prep_threads<DK, DV, R>() <= PREP_MAX_THREADS, "prep CTA size");
+  gdn_prefill_prep_kernel<DK, DV, R><<<gp, prep_threads<DK, DV, R>(), prep_smem, stream>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return q38host::cuda_status(e, "gdn_prefill_prep launch");
   dim3 gc(a.num_v_heads, (a.tokens + SUB - 1) / SUB);
