@@ -30,7 +30,8 @@ constexpr int KCONV = 4;
 constexpr int PREP_TOK = 32;  // tokens per prep CTA
 constexpr int SUB = 64;       // tokens per sub-chunk of the delta rule
 constexpr int SUBP = SUB + 4; // padded row of the transposed [dk][SUB] tiles (keeps float4 alignment)
-constexpr int DVS = 32;       // state columns per delta CTA
+constexpr int SDV = 44;       // state columns per state-walk CTA at most (128 columns: slices of 44, 44, 40)
+constexpr int STH = SDV / 4 * 16;  // its threads: 11 column groups of 4 x 16 row groups
 
 struct PrefillArgs {
   const __nv_bfloat16* qkvz;  // [tokens, ld_qkvz]: q | k | v | z
@@ -361,28 +362,29 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_chunk_kernel(PrefillArgs a
 }
 
 // ---------------------------------------------------------------------------------------------
-// delta, phase B: the state walk. One CTA per (value head, DVS state columns); the columns of S evolve
-// independently given phase A's matrices, so the slices need no exchange. The fp32 slice stays in
+// delta, phase B: the state walk. One CTA per (value head, up to SDV state columns); the columns of S
+// evolve independently given phase A's matrices, so the slices need no exchange. Three slices per
+// head of 128 columns make 144 CTAs for 48 heads, one wave with one CTA per SM. The fp32 slice stays in
 // shared memory across the chunk; per sub-chunk
 //   v' = u - w S,   o = qg S + Aqk v' (bf16 out),   S = el S + kd^T v'
 // with the inputs bulk-copied in while the previous step computes: qg and Aqk of the next sub-chunk
 // during this one, kd (into w's buffer, once w is read) during o, and the next w during the next
-// step's wait. Two CTAs share an SM, so one's copies overlap the other's arithmetic.
+// step's wait.
 // ---------------------------------------------------------------------------------------------
 template <int DK, int DV>
 struct StateSmem {
   using W = ChunkWs<DK, DV>;
-  static constexpr size_t ST = 0;                                         // [DK][DVS]
-  static constexpr size_t WK = ST + sizeof(float) * DK * DVS;             // [SUB][RS] w, then kd
+  static constexpr size_t ST = 0;                                         // [DK][SDV]
+  static constexpr size_t WK = ST + sizeof(float) * DK * SDV;             // [SUB][RS] w, then kd
   static constexpr size_t QG = WK + sizeof(float) * SUB * W::RS;          // [SUB][RS] qg
   static constexpr size_t AQ = QG + sizeof(float) * SUB * W::RS;          // [SUB][AS] Aqk
-  static constexpr size_t VP = AQ + sizeof(float) * SUB * W::AS;          // [SUB][DVS] v'
-  static constexpr size_t BAR = VP + sizeof(float) * SUB * DVS;           // four mbarriers
+  static constexpr size_t VP = AQ + sizeof(float) * SUB * W::AS;          // [SUB][SDV] v'
+  static constexpr size_t BAR = VP + sizeof(float) * SUB * SDV;           // four mbarriers
   static constexpr size_t TOTAL = BAR + 32;
 };
 
 template <int DK, int DV>
-__global__ void __launch_bounds__(256, 2) gdn_prefill_state_kernel(PrefillArgs a) {
+__global__ void __launch_bounds__(STH, 1) gdn_prefill_state_kernel(PrefillArgs a) {
   using S = StateSmem<DK, DV>;
   using W = ChunkWs<DK, DV>;
   constexpr uint32_t RS_BYTES = sizeof(float) * SUB * W::RS;
@@ -400,7 +402,8 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_state_kernel(PrefillArgs a
 
   const int tid = threadIdx.x;
   const int h = blockIdx.x;
-  const int c0 = blockIdx.y * DVS;  // first state column of this CTA
+  const int c0 = blockIdx.y * SDV;  // first state column of this CTA
+  const int ncols = min(SDV, DV - c0);  // a multiple of 4
   const int T = a.tokens;
   const int nsub = (T + SUB - 1) / SUB;
   const int64_t vd_all = static_cast<int64_t>(a.num_v_heads) * DV;
@@ -408,9 +411,9 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_state_kernel(PrefillArgs a
 
   // The state slice, fp32, zero unless the row continues (start > 0).
   __nv_bfloat16* srow = a.state + static_cast<int64_t>(h) * DK * DV;
-  for (int i = tid; i < DK * DVS; i += 256) {
-    const int d = i / DVS, j = i % DVS;
-    st[i] = __fmul_rn(__bfloat162float(srow[d * DV + c0 + j]), a.keep);
+  for (int i = tid; i < DK * SDV; i += STH) {
+    const int d = i / SDV, j = i % SDV;
+    st[i] = j < ncols ? __fmul_rn(__bfloat162float(srow[d * DV + c0 + j]), a.keep) : 0.f;
   }
   if (tid == 0) {
     for (int i = 0; i < 4; ++i) mbar_init(bar_w + i, 1);
@@ -427,11 +430,13 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_state_kernel(PrefillArgs a
     load(bar_a, aq, 0, W::AQK, AS_BYTES);
   }
 
-  // Thread tilings (256 threads): [SUB][DVS] outputs as RPT rows x 4 columns, [DK][DVS] as DPT x 4.
-  constexpr int CG = DVS / 4, RG = 256 / CG, RPT = SUB / RG;
-  constexpr int DG = 256 / CG, DPT = DK / DG;
-  static_assert(RPT >= 1 && DPT >= 1 && DK % DG == 0 && SUB % RG == 0, "tiling");
+  // Thread tilings (STH threads): [SUB][SDV] outputs as RPT rows x 4 columns, [DK][SDV] as DPT x 4;
+  // column groups past this slice's ncols compute zeros and store nothing.
+  constexpr int CG = SDV / 4, RG = STH / CG, RPT = SUB / RG;
+  constexpr int DG = STH / CG, DPT = DK / DG;
+  static_assert(RPT >= 1 && DPT >= 1 && DK % DG == 0 && SUB % RG == 0 && RPT % 4 == 0, "tiling");
   const int ri = tid / CG, ci = tid % CG;
+  const bool col_ok = 4 * ci < ncols;
   const int a0 = ri * RPT, d0 = ri * DPT;
   bool ok = true;
 
@@ -441,7 +446,8 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_state_kernel(PrefillArgs a
     const uint32_t ph = c & 1;
     float4 u4[RPT];
 #pragma unroll
-    for (int x = 0; x < RPT; ++x) u4[x] = *reinterpret_cast<const float4*>(it + W::U + (a0 + x) * DV + c0 + 4 * ci);
+    for (int x = 0; x < RPT; ++x)
+      u4[x] = col_ok ? *reinterpret_cast<const float4*>(it + W::U + (a0 + x) * DV + c0 + 4 * ci) : make_float4(0.f, 0.f, 0.f, 0.f);
     const float el = it[W::EL];
     ok = ok && mbar_wait(bar_w, ph) && mbar_wait(bar_q, ph);
     // v' = u - w S and qg S, both against the state before this sub-chunk; four d per step.
@@ -455,7 +461,7 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_state_kernel(PrefillArgs a
       float s4[4][4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const float4 sv = *reinterpret_cast<const float4*>(st + (d + k) * DVS + 4 * ci);
+        const float4 sv = *reinterpret_cast<const float4*>(st + (d + k) * SDV + 4 * ci);
         s4[k][0] = sv.x;
         s4[k][1] = sv.y;
         s4[k][2] = sv.z;
@@ -481,7 +487,7 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_state_kernel(PrefillArgs a
       float v[4];
 #pragma unroll
       for (int y = 0; y < 4; ++y) v[y] = __fsub_rn(u[y], accv[x][y]);
-      *reinterpret_cast<float4*>(vp + (a0 + x) * DVS + 4 * ci) = make_float4(v[0], v[1], v[2], v[3]);
+      *reinterpret_cast<float4*>(vp + (a0 + x) * SDV + 4 * ci) = make_float4(v[0], v[1], v[2], v[3]);
     }
     __syncthreads();  // v' complete; w and qg are read
     if (tid == 0 && ok) {
@@ -501,7 +507,7 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_state_kernel(PrefillArgs a
         float v4[4][4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          const float4 vv = *reinterpret_cast<const float4*>(vp + (b + k) * DVS + 4 * ci);
+          const float4 vv = *reinterpret_cast<const float4*>(vp + (b + k) * SDV + 4 * ci);
           v4[k][0] = vv.x;
           v4[k][1] = vv.y;
           v4[k][2] = vv.z;
@@ -520,7 +526,7 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_state_kernel(PrefillArgs a
 #pragma unroll
       for (int x = 0; x < RPT; ++x) {
         const int a_ = a0 + x;
-        if (a_ < n) {
+        if (a_ < n && col_ok) {
           __nv_bfloat16* orow = a.o + static_cast<int64_t>(s0 + a_) * vd_all + static_cast<int64_t>(h) * DV + c0 + 4 * ci;
 #pragma unroll
           for (int y = 0; y < 4; ++y) orow[y] = __float2bfloat16_rn(__fadd_rn(accq[x][y], acc[x][y]));
@@ -537,7 +543,7 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_state_kernel(PrefillArgs a
         for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
 #pragma unroll 4
       for (int t = 0; t < SUB; ++t) {
-        const float4 vv = *reinterpret_cast<const float4*>(vp + t * DVS + 4 * ci);
+        const float4 vv = *reinterpret_cast<const float4*>(vp + t * SDV + 4 * ci);
         const float v4[4] = {vv.x, vv.y, vv.z, vv.w};
         float kx[DPT];
         if constexpr (DPT % 4 == 0) {
@@ -562,7 +568,7 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_state_kernel(PrefillArgs a
       for (int x = 0; x < DPT; ++x)
 #pragma unroll
         for (int y = 0; y < 4; ++y) {
-          float* p = st + (d0 + x) * DVS + 4 * ci + y;
+          float* p = st + (d0 + x) * SDV + 4 * ci + y;
           *p = __fadd_rn(__fmul_rn(*p, el), acc[x][y]);
         }
     }
@@ -574,9 +580,9 @@ __global__ void __launch_bounds__(256, 2) gdn_prefill_state_kernel(PrefillArgs a
   }
   // A copy that timed out (recorded in the device error word) leaves the state untouched.
   if (__syncthreads_or(!ok)) return;
-  for (int i = tid; i < DK * DVS; i += 256) {
-    const int d = i / DVS, j = i % DVS;
-    srow[d * DV + c0 + j] = __float2bfloat16_rn(st[i]);
+  for (int i = tid; i < DK * SDV; i += STH) {
+    const int d = i / SDV, j = i % SDV;
+    if (j < ncols) srow[d * DV + c0 + j] = __float2bfloat16_rn(st[i]);
   }
 }
 
@@ -692,8 +698,8 @@ int launch_prefill(PrefillArgs a, int conv_dim, cudaStream_t stream) {
   gdn_prefill_chunk_kernel<DK, DV><<<gc, 256, CS::TOTAL, stream>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return q38host::cuda_status(e, "gdn_prefill_chunk launch");
-  dim3 gd(a.num_v_heads, DV / DVS);
-  gdn_prefill_state_kernel<DK, DV><<<gd, 256, SS::TOTAL, stream>>>(a);
+  dim3 gd(a.num_v_heads, (DV + SDV - 1) / SDV);
+  gdn_prefill_state_kernel<DK, DV><<<gd, STH, SS::TOTAL, stream>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return q38host::cuda_status(e, "gdn_prefill_state launch");
   gdn_prefill_norm_kernel<DV><<<a.tokens + 1, 256, 0, stream>>>(a, conv_dim);
