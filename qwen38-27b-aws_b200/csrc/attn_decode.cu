@@ -14,7 +14,7 @@
 // empty mbarriers, so it runs ahead into V while the four compute warps finish the softmax; the
 // compute warps multiply on mma.sync (BF16, fp32 accumulate) and never wait on a CTA-wide barrier per
 // tile. Every other input of the row (queries, own key / value, gates, norm weights, cos / sin) is
-// fetched in one round trip at the start. Three CTAs per SM.
+// fetched in one round trip at the start. Four CTAs per SM (two tiles in flight each).
 //
 // Rows differ in length (each streams position * head_dim * 4 bytes per KV head), and a CTA streams
 // at a fraction of the SM's bandwidth, so a long row that starts in the grid's last wave sets the
@@ -50,7 +50,7 @@ struct AttnArgs {
 constexpr int kComputeWarps = 4;
 constexpr int kThreads = (kComputeWarps + 1) * 32;  // compute warps + one copy warp
 constexpr int KT = 32;                               // cache positions per tile
-constexpr int kStages = 3;                           // tiles in flight per CTA (three CTAs per SM)
+constexpr int kStages = 2;                           // tiles in flight per CTA (four CTAs per SM)
 constexpr int MROWS = 16;                            // the MMA's M: query heads, padded by a zero row
 
 __host__ __device__ constexpr size_t al16(size_t x) { return (x + 15) & ~size_t(15); }
@@ -124,7 +124,7 @@ __device__ __forceinline__ void compute_bar() {
 }
 
 template <int HD, int STAGES>
-__global__ void __launch_bounds__(kThreads, 3) attn_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
+__global__ void __launch_bounds__(kThreads, 4) attn_decode_kernel(const __grid_constant__ CUtensorMap tmap_k,
                                                                const __grid_constant__ CUtensorMap tmap_v, AttnArgs a) {
   using T = TileGeom<HD>;
   constexpr int KSTEPS = HD / 16;                  // MMA k-steps over head_dim
