@@ -12,7 +12,9 @@ are seeded random values (the bytes moved are the same as a real prompt's).
 
 The JSON line's `value` is tokens/s with the step inputs already on the device; `e2e` is the same
 through the reference-facing calls (B200Step(**host tensors) -> host hidden, B200Head.run_graph ->
-host maxima), host<->device copies included. `--impl reference` times the CPU oracle (the reference's
+host maxima), host<->device copies included. `step_roofline` sets the algorithmic HBM bytes of one
+whole decode step against the step time; `prefill` is one 512-token chunk of one row through all
+layers, device-timed (the prefill half of the tokens/s metric). `--impl reference` times the CPU oracle (the reference's
 CPU path restated) on this host's cores on a bounded sample: one 4-layer block per step at the same
 batch, scaled to 64 layers.
 """
