@@ -11,7 +11,7 @@
 //          state-free matrices of each sub-chunk, Aqk = (q k^T) * decay (lower), and the reference's
 //          u = A (v beta), w = A (k beta e^g) with A = (I + N)^-1, N = strictly_lower(beta (k k^T) *
 //          decay) (blocked solve), plus q e^g and k e^{g_last - g}, into the workspace.
-//   state  (delta, phase B) one CTA per (value head, 32-column slice of the state). The state's value
+//   state  (delta, phase B) one CTA per (value head, slice of up to 44 state columns). The state's value
 //          columns evolve independently given phase A's matrices, so the slices need no exchange; each
 //          CTA keeps its [dk x 32] fp32 slice in shared memory across the chunk and walks the
 //          sub-chunks:  v' = u - w S,  o = (q e^g) S + Aqk v',  S = e^{g_last} S + (k e^{g_last - g})^T v'
