@@ -13,7 +13,7 @@
 //          decay) (blocked solve), plus q e^g and k e^{g_last - g}, into the workspace.
 //   state  (delta, phase B) one CTA per (value head, slice of up to 44 state columns). The state's value
 //          columns evolve independently given phase A's matrices, so the slices need no exchange; each
-//          CTA keeps its [dk x 32] fp32 slice in shared memory across the chunk and walks the
+//          CTA keeps its fp32 slice in shared memory across the chunk and walks the
 //          sub-chunks:  v' = u - w S,  o = (q e^g) S + Aqk v',  S = e^{g_last} S + (k e^{g_last - g})^T v'
 //          (model.py:110-128). The sub-chunk length is 64 instead of the CPU branch's 128 (model.py:34):
 //          the rule is exact for any split.
