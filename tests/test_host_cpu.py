@@ -1,0 +1,53 @@
+"""Host-side planning without a GPU: the GEMMs' K-split choices and the bench's per-step byte count."""
+
+import importlib
+from types import SimpleNamespace
+
+import pytest
+
+
+@pytest.fixture(scope="module")
+def ops(pkg):
+    return importlib.import_module(pkg.__name__ + ".ops")
+
+
+def test_decode_split_choices_fill_one_wave(ops):
+    # 256 rows: 5120-output row-parallel projections get 3 K splits (40 tiles x 3 = 120 CTAs on 148 SMs);
+    # the wide column-parallel projections, whose grids already cover the SMs, run unsplit.
+    assert ops.choose_splits(256, 5120, 17408) == 3
+    assert ops.choose_splits(256, 5120, 6144) == 3
+    assert ops.choose_splits(256, 16384, 5120) == 1
+    assert ops.choose_splits(256, 14336, 5120) == 1
+    # Few rows: the same single wave, with at least 4 K stages per split.
+    assert ops.choose_splits(8, 5120, 6144) == 3
+    assert ops.choose_splits(8, 5120, 1024) == 2
+
+
+def test_token_tiles_and_bf16_splits(ops):
+    assert ops.token_tile(1) == 128 and ops.token_tile(128) == 128 and ops.token_tile(129) == 256
+    # in_proj_b / in_proj_a: 8 splits at 5120 (the split count fixes the fp32 summation order).
+    assert ops.bf16_linear_splits(256, 96, 5120) == 8
+    assert ops.bf16_linear_splits(256, 96, 128) == 1
+
+
+def test_decode_step_bytes_counts_weights_state_and_cache():
+    bench = importlib.import_module("bench")
+    torch = importlib.import_module("torch")
+    lin = lambda o, i: SimpleNamespace(out_features=o, in_features=i)  # noqa: E731
+    gdn = SimpleNamespace(kind="linear_attention", gate_up=lin(64, 32), down=lin(32, 32),
+                          mixer=SimpleNamespace(qkvz=lin(96, 32), out=lin(32, 64), ab=lin(4, 32),
+                                                state=torch.zeros(2, 4, 8, 8), conv_state=torch.zeros(2, 10, 3)))
+    attn = SimpleNamespace(kind="full_attention", gate_up=lin(64, 32), down=lin(32, 32),
+                           mixer=SimpleNamespace(qkv=lin(48, 32), o=lin(32, 32), k_cache=torch.zeros(2, 1, 16, 8)))
+    step = SimpleNamespace(layers=[gdn, attn])
+    head = SimpleNamespace(lm_head=lin(320, 32))
+    positions = torch.tensor([[3, 600], [4, 20]], dtype=torch.int32)  # two steps; 600 counts as MAX_SEQ (512)
+    fp8 = lambda o, i: o * i * 33 // 32  # noqa: E731
+    want = 320 * 32 * 2                                                    # BF16 lm_head
+    want += 2 * (fp8(64, 32) + fp8(32, 32))                                # MLPs
+    want += fp8(96, 32) + fp8(32, 64) + 4 * 32 * 2                         # GDN projections, BF16 in_proj_b/a
+    want += (2 * 4 * 8 * 8 + 2 * 10 * 3) * 2 * 2                           # state and conv state in and out
+    kv_positions = (3 + 512 + 4 + 20) / 2                                  # mean over the steps of the rows' sum
+    want += fp8(48, 32) + fp8(32, 32) + int(kv_positions * 1 * 8 * 2 * 2)  # attention projections, K and V
+    assert bench.MAX_SEQ == 512
+    assert bench.decode_step_bytes(step, head, "linear_attention", positions) == want
