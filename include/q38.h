@@ -89,8 +89,11 @@ int q38_fp8_gemm(const void* x, int64_t tokens, int64_t k, const void* w, const 
  * memory is owned by a framework pool, plugins that must not synchronise the device, and FFI bindings
  * that carry only input and output pointers. This entry point has no counterpart in the reference.
  * The split-K partial sums go to a fixed array inside the library, Q38_STATIC_SCRATCH_BYTES on every
- * GPU that loads it (kept until exit); a shape whose q38_fp8_gemm_workspace_bytes exceeds that is
- * refused with Q38_ERR_ARG. The first call on a device looks the array's address up once
+ * GPU that loads it (kept until exit). Only calls that need the workspace epilogue use the array:
+ * more than 8 K splits, or an output (or residual) that cannot be tensor-mapped (not 16-byte aligned,
+ * or a row stride that is not a multiple of 8 elements); other calls run as q38_fp8_gemm does without
+ * a workspace. Of the calls that use it, a shape whose q38_fp8_gemm_workspace_bytes exceeds the array
+ * is refused with Q38_ERR_ARG. Every argument is checked on the host before the array is touched. The first call on a device looks the array's address up once
  * (cudaGetSymbolAddress), so make that first call before any stream capture. All calls share the
  * one array: calls that overlap on the GPU (other streams, other host threads) race on it.
  * Arguments are those of q38_fp8_gemm without workspace and workspace_bytes.

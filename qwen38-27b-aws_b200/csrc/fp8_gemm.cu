@@ -1034,11 +1034,32 @@ constexpr int kMaxClusterSplits = 8;  // portable cluster size
 // Picks the epilogue: through shared memory and a cluster of the K splits (no workspace) when the
 // splits fit a portable cluster and y / residual can be tensor-mapped; else the workspace path.
 // Fills the output and residual tensor maps for the cluster path.
+// The split-K workspace starts with one counter per output tile, padded to 256 bytes; the fp32
+// partials follow.
+size_t split_counter_bytes(int64_t tokens, int64_t features) {
+  const int64_t tiles = cdiv(features, BM) * cdiv(tokens, token_tile(tokens));
+  return static_cast<size_t>((tiles * 4 + 255) / 256 * 256);
+}
+
+// The K splits a launch really runs: K stages are dealt out evenly, so asking for more splits than
+// ceil(stages / ceil(stages / splits)) gives that many.
+int effective_splits(int64_t k, int splits, int k_stage_bytes = BK_BYTES) {
+  const int nkc = static_cast<int>(cdiv(k, k_stage_bytes));
+  const int kc_per = static_cast<int>(cdiv(nkc, std::min(splits, nkc)));
+  return static_cast<int>(cdiv(nkc, kc_per));
+}
+
+// Whether y (and the residual, when the epilogue reads one) can be tensor-mapped for the cluster
+// epilogue.
+bool epilogue_mappable(const void* y, int64_t ldy, const void* residual, int64_t ldr) {
+  return aligned16(y) && ldy % 8 == 0 && (!residual || (aligned16(residual) && ldr % 8 == 0));
+}
+
 int setup_epilogue(GemmArgs& a, int splits, int64_t tokens, int64_t features, void* y, int64_t ldy,
                    const void* residual, int64_t ldr, void* workspace, size_t workspace_bytes, CUtensorMap* ty,
                    CUtensorMap* tr, const char* who, bool allow_cluster = true) {
   using namespace q38host;
-  const bool mappable = aligned16(y) && ldy % 8 == 0 && (!residual || (aligned16(residual) && ldr % 8 == 0));
+  const bool mappable = epilogue_mappable(y, ldy, residual, ldr);
   if (allow_cluster && splits <= kMaxClusterSplits && mappable) {
     a.cluster = splits;
     int st = encode_tmap_2d(ty, y, tokens, features, 2, TOK_BLOCK, BM, false, ldy);
@@ -1053,14 +1074,11 @@ int setup_epilogue(GemmArgs& a, int splits, int64_t tokens, int64_t features, vo
   }
   a.cluster = 0;
   if (splits > 1) {
-    const int ntok = token_tile(tokens);
-    const int64_t tiles = cdiv(features, BM) * cdiv(tokens, ntok);
     const size_t need = q38_fp8_gemm_workspace_bytes(tokens, features, splits);
     if (!workspace || workspace_bytes < need || !aligned16(workspace))
       return set_error("%s: %d K splits need a 16-byte aligned workspace of %zu bytes", who, splits, need), Q38_ERR_ARG;
-    const size_t counters = static_cast<size_t>((tiles * 4 + 255) / 256 * 256);
     a.counters = static_cast<unsigned int*>(workspace);
-    a.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
+    a.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + split_counter_bytes(tokens, features));
   }
   return Q38_OK;
 }
@@ -1081,8 +1099,7 @@ extern "C" size_t q38_fp8_gemm_workspace_bytes(int64_t tokens, int64_t features,
   if (tokens <= 0 || features <= 0 || splits <= 1) return 0;
   const int ntok = token_tile(tokens);
   const int64_t tiles = cdiv(features, BM) * cdiv(tokens, ntok);
-  const size_t counters = static_cast<size_t>((tiles * 4 + 255) / 256 * 256);
-  return counters + static_cast<size_t>(splits) * tiles * BM * ntok * sizeof(float);
+  return split_counter_bytes(tokens, features) + static_cast<size_t>(splits) * tiles * BM * ntok * sizeof(float);
 }
 
 namespace {
@@ -1094,8 +1111,7 @@ int gemm_fp8(const void* x, int64_t tokens, int64_t k, const void* w, const void
   using namespace q38host;
   const int ntok = token_tile(tokens);
   const int nkc = static_cast<int>(cdiv(k, BK_BYTES));
-  int kc_per = static_cast<int>(cdiv(nkc, std::min(splits, nkc)));
-  splits = static_cast<int>(cdiv(nkc, kc_per));
+  splits = effective_splits(k, splits);
   GemmArgs a{};
   a.w = static_cast<const uint8_t*>(w);
   a.sf = static_cast<const uint8_t*>(w_sf);
@@ -1103,7 +1119,7 @@ int gemm_fp8(const void* x, int64_t tokens, int64_t k, const void* w, const void
   a.F = static_cast<int>(features);
   a.nkc = nkc;
   a.splits = splits;
-  a.kc_per_split = kc_per;
+  a.kc_per_split = static_cast<int>(cdiv(nkc, splits));
   a.epilogue = epilogue;
   a.y = static_cast<__nv_bfloat16*>(y);
   a.ldy = ldy;
@@ -1160,19 +1176,30 @@ int check_gemm_args(const void* x, int64_t tokens, int64_t k, const void* w, con
   return Q38_OK;
 }
 
+// Every check of q38_fp8_gemm's arguments that needs no workspace.
+int check_fp8_gemm_call(const void* x, int64_t tokens, int64_t k, const void* w, const void* w_sf, int64_t features,
+                        int epilogue, const void* y, int64_t ldy, const void* residual, int64_t ldr, int splits,
+                        const char* who) {
+  using namespace q38host;
+  int st = check_gemm_args(x, tokens, k, w, w_sf, features, splits, who);
+  if (st != Q38_OK) return st;
+  if (!y) return set_error("%s: null pointer", who), Q38_ERR_ARG;
+  if (epilogue != Q38_EPI_BF16 && epilogue != Q38_EPI_RESIDUAL)
+    return set_error("%s: unknown epilogue %d", who, epilogue), Q38_ERR_ARG;
+  if (epilogue == Q38_EPI_RESIDUAL && !residual) return set_error("%s: residual epilogue needs residual", who), Q38_ERR_ARG;
+  if (ldy < features || (residual && ldr < features)) return set_error("%s: leading dimension too small", who), Q38_ERR_ARG;
+  return Q38_OK;
+}
+
 }  // namespace
 
 extern "C" int q38_fp8_gemm(const void* x, int64_t tokens, int64_t k, const void* w, const void* w_sf,
                             int64_t features, int epilogue, void* y, int64_t ldy, const void* residual, int64_t ldr,
                             int splits, void* workspace, size_t workspace_bytes, q38_stream_t stream) {
   using namespace q38host;
-  int st = check_gemm_args(x, tokens, k, w, w_sf, features, splits, "q38_fp8_gemm");
+  const int st = check_fp8_gemm_call(x, tokens, k, w, w_sf, features, epilogue, y, ldy, residual, ldr, splits,
+                                     "q38_fp8_gemm");
   if (st != Q38_OK) return st;
-  if (!y) return set_error("q38_fp8_gemm: null pointer"), Q38_ERR_ARG;
-  if (epilogue != Q38_EPI_BF16 && epilogue != Q38_EPI_RESIDUAL)
-    return set_error("q38_fp8_gemm: unknown epilogue %d", epilogue), Q38_ERR_ARG;
-  if (epilogue == Q38_EPI_RESIDUAL && !residual) return set_error("q38_fp8_gemm: residual epilogue needs residual"), Q38_ERR_ARG;
-  if (ldy < features || (residual && ldr < features)) return set_error("q38_fp8_gemm: leading dimension too small"), Q38_ERR_ARG;
   return gemm_fp8(x, tokens, k, w, w_sf, features, epilogue, y, ldy, residual, ldr, splits, workspace, workspace_bytes,
                   nullptr, static_cast<cudaStream_t>(stream), "q38_fp8_gemm");
 }
@@ -1323,24 +1350,29 @@ extern "C" int q38_fp8_gemm_static_scratch(const void* x, int64_t tokens, int64_
                                            int64_t features, int epilogue, void* y, int64_t ldy, const void* residual,
                                            int64_t ldr, int splits, q38_stream_t stream) {
   using namespace q38host;
-  if (splits < 1) return set_error("q38_fp8_gemm_static_scratch: splits must be >= 1"), Q38_ERR_ARG;
-  if (splits == 1)
-    return q38_fp8_gemm(x, tokens, k, w, w_sf, features, epilogue, y, ldy, residual, ldr, 1, nullptr, 0, stream);
-  const size_t need = q38_fp8_gemm_workspace_bytes(tokens, features, splits);
+  const char* who = "q38_fp8_gemm_static_scratch";
+  // Every argument is checked before the fixed array is touched.
+  int st = check_fp8_gemm_call(x, tokens, k, w, w_sf, features, epilogue, y, ldy, residual, ldr, splits, who);
+  if (st != Q38_OK) return st;
+  // Only the workspace epilogue (more than 8 K splits, or an output or residual that cannot be
+  // tensor-mapped) uses scratch; every other call runs exactly as q38_fp8_gemm without one.
+  const int runs = effective_splits(k, splits);
+  const void* res = epilogue == Q38_EPI_RESIDUAL ? residual : nullptr;
+  if (runs == 1 || (runs <= kMaxClusterSplits && epilogue_mappable(y, ldy, res, ldr)))
+    return q38_fp8_gemm(x, tokens, k, w, w_sf, features, epilogue, y, ldy, residual, ldr, splits, nullptr, 0, stream);
+  const size_t need = q38_fp8_gemm_workspace_bytes(tokens, features, runs);
   if (need > static_cast<size_t>(Q38_STATIC_SCRATCH_BYTES))
-    return set_error("q38_fp8_gemm_static_scratch: %lld tokens x %lld features with %d splits need %zu bytes of "
-                     "scratch, more than the library's fixed %d; use fewer splits or q38_fp8_gemm with a workspace",
-                     (long long)tokens, (long long)features, splits, need, Q38_STATIC_SCRATCH_BYTES),
+    return set_error("%s: %lld tokens x %lld features with %d splits need %zu bytes of scratch, more than the "
+                     "library's fixed %d; use fewer splits or q38_fp8_gemm with a workspace",
+                     who, (long long)tokens, (long long)features, runs, need, Q38_STATIC_SCRATCH_BYTES),
            Q38_ERR_ARG;
   void* scratch = nullptr;
-  int st = static_scratch_address(&scratch);
+  st = static_scratch_address(&scratch);
   if (st != Q38_OK) return st;
   // The split counters must start at zero. A completed call leaves them at zero, but a call that
   // gave up part-way would not, so clear them (a memset node, no allocation) before every call.
-  const int64_t ntok = tokens > 128 ? 256 : 128;
-  const size_t counters = static_cast<size_t>(((cdiv(features, BM) * cdiv(tokens, ntok)) * 4 + 255) / 256 * 256);
-  cudaError_t e = cudaMemsetAsync(scratch, 0, counters, static_cast<cudaStream_t>(stream));
+  cudaError_t e = cudaMemsetAsync(scratch, 0, split_counter_bytes(tokens, features), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_status(e, "clear static scratch counters");
-  return q38_fp8_gemm(x, tokens, k, w, w_sf, features, epilogue, y, ldy, residual, ldr, splits, scratch,
+  return q38_fp8_gemm(x, tokens, k, w, w_sf, features, epilogue, y, ldy, residual, ldr, runs, scratch,
                       static_cast<size_t>(Q38_STATIC_SCRATCH_BYTES), stream);
 }

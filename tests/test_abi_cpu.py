@@ -37,3 +37,23 @@ def test_host_side_argument_checks_need_no_gpu(pkg):
     assert lib.q38_sf_tile_bytes(5120, 17408) == 40 * 136 * 512
     assert lib.q38_fp8_gemm_workspace_bytes(256, 5120, 1) == 0
     assert lib.q38_fp8_gemm_workspace_bytes(256, 5120, 3) == 256 + 3 * 40 * 128 * 256 * 4
+
+
+def test_static_scratch_gemm_checks_arguments_before_any_device_call(pkg):
+    """q38_fp8_gemm_static_scratch refuses bad sizes, null pointers and oversized shapes on the host,
+    before it looks up or clears its fixed scratch array (no GPU here, so any CUDA call would fail)."""
+    import ctypes
+
+    lib_mod = __import__(pkg.__name__ + "._lib", fromlist=["_lib"])
+    lib = lib_mod.load()
+    dummy = ctypes.c_void_p(16)
+    for tokens, features in ((0, 1024), (-5, 1024), (64, 0), (64, -128)):
+        status = lib.q38_fp8_gemm_static_scratch(dummy, tokens, 4096, dummy, dummy, features, 0, dummy, 1024, None, 0,
+                                                 12, None)
+        assert status == -1 and "bad sizes" in lib_mod.last_error(), (tokens, features, lib_mod.last_error())
+    assert lib.q38_fp8_gemm_static_scratch(dummy, 64, 4096, dummy, dummy, 1024, 0, None, 1024, None, 0, 12, None) == -1
+    assert "null pointer" in lib_mod.last_error()
+    assert lib.q38_fp8_gemm_static_scratch(dummy, 64, 4096, dummy, dummy, 1024, 1, dummy, 1024, None, 0, 12, None) == -1
+    assert "residual" in lib_mod.last_error()
+    status = lib.q38_fp8_gemm_static_scratch(dummy, 4096, 4096, dummy, dummy, 32768, 0, dummy, 32768, None, 0, 12, None)
+    assert status == -1 and "scratch" in lib_mod.last_error()

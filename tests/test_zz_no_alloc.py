@@ -25,9 +25,16 @@ def mods(pkg):
     return lib_mod, ops
 
 
-@pytest.mark.parametrize("tokens,k,features,splits",
-                         [(256, 17408, 5120, 3), (8, 6144, 5120, 3), (37, 512, 384, 2), (256, 17408, 1024, 12)])
-def test_static_scratch_gemm_matches_workspace_gemm_twice(pkg, mods, tokens, k, features, splits):
+# (tokens, k, features, splits, row padding of the output). Padding of 4 bf16 makes the output's row
+# stride no multiple of 16 bytes, so it cannot be tensor-mapped and the partial sums go through the
+# scratch array even with few splits; more than 8 splits always use it. The other shapes take the
+# cluster epilogue, which needs no scratch: the entry point must give the same bits there too.
+CASES = [(256, 17408, 5120, 3, 0), (8, 6144, 5120, 3, 0), (37, 512, 384, 2, 0), (256, 17408, 1024, 12, 0),
+         (64, 4096, 1024, 4, 4), (200, 3072, 640, 2, 4)]
+
+
+@pytest.mark.parametrize("tokens,k,features,splits,pad", CASES)
+def test_static_scratch_gemm_matches_workspace_gemm_twice(pkg, mods, tokens, k, features, splits, pad):
     lib_mod, ops = mods
     lib = lib_mod.load()
     gen = torch.Generator().manual_seed(tokens + k)
@@ -35,9 +42,9 @@ def test_static_scratch_gemm_matches_workspace_gemm_twice(pkg, mods, tokens, k, 
     stream = torch.cuda.current_stream().cuda_stream
     for call in range(2):
         x = pkg.codec.to_e5m2_bytes(torch.randn(tokens, k, generator=gen).to(torch.bfloat16)).to(DEV)
-        res = torch.randn(tokens, features, generator=gen).to(torch.bfloat16).to(DEV)
+        res = torch.randn(tokens, features + pad, generator=gen).to(torch.bfloat16).to(DEV)
         want = res.clone()
-        ws = torch.zeros(ops.gemm_workspace_bytes(tokens, features, splits), dtype=torch.uint8, device=DEV)
+        ws = torch.zeros(max(256, ops.gemm_workspace_bytes(tokens, features, splits)), dtype=torch.uint8, device=DEV)
         ops.fp8_gemm(x, lin, want, residual=want, splits=splits, workspace=ws)
         got = res.clone()
         status = lib.q38_fp8_gemm_static_scratch(x.data_ptr(), tokens, k, lin.q.data_ptr(), lin.sf.data_ptr(), features,
@@ -51,7 +58,7 @@ def test_static_scratch_gemm_matches_workspace_gemm_twice(pkg, mods, tokens, k, 
 def test_static_scratch_refuses_shapes_beyond_its_size(pkg, mods):
     lib_mod, _ = mods
     lib = lib_mod.load()
-    tokens, features, splits = 4096, 32768, 8
+    tokens, features, splits = 4096, 32768, 12  # more than 8 splits: the scratch path
     assert lib.q38_fp8_gemm_workspace_bytes(tokens, features, splits) > 16 * 1024 * 1024
     dummy = ctypes.c_void_p(16)
     status = lib.q38_fp8_gemm_static_scratch(dummy, tokens, 4096, dummy, dummy, features, 0, dummy, features, None, 0,
