@@ -93,8 +93,9 @@ int q38_fp8_gemm(const void* x, int64_t tokens, int64_t k, const void* w, const 
  * more than 8 K splits, or an output (or residual) that cannot be tensor-mapped (not 16-byte aligned,
  * or a row stride that is not a multiple of 8 elements); other calls run as q38_fp8_gemm does without
  * a workspace. Of the calls that use it, a shape whose q38_fp8_gemm_workspace_bytes exceeds the array
- * is refused with Q38_ERR_ARG. Every argument is checked on the host before the array is touched. The first call on a device looks the array's address up once
- * (cudaGetSymbolAddress), so make that first call before any stream capture. All calls share the
+ * is refused with Q38_ERR_ARG. Every argument is checked on the host before the array is touched.
+ * The first call on a device looks the array's address up once (cudaGetSymbolAddress), so make that
+ * first call before any stream capture. All calls share the
  * one array: calls that overlap on the GPU (other streams, other host threads) race on it.
  * Arguments are those of q38_fp8_gemm without workspace and workspace_bytes.
  */
@@ -326,6 +327,17 @@ int q38_fp8_gemm_allreduce(const void* x_q, int64_t tokens, int64_t k, const voi
  */
 int q38_fp8_gemm_silu(const void* x_q, int64_t tokens, int64_t k, const void* w, const void* w_sf, int64_t features,
                       void* y, int64_t ldy, q38_stream_t stream);
+
+/*
+ * Save / restore of one slot's recurrent states for prefix reuse: row src_row of each of n_buffers
+ * device buffers copied to row dst_row, in one launch (more than 96 buffers take more launches).
+ * buffers[i] is a contiguous device array of rows[i] rows of row_bytes[i] bytes (a gated-delta layer's
+ * recurrent state [rows, heads, dk, dv] or conv state [rows, conv_dim, kernel - 1]); the three arrays
+ * are host memory. src_row == dst_row copies nothing. Replaces GatedDeltaNetStep.copy_states
+ * (qwen38_inf2/model.py:456-464) over every layer (Qwen38Step.forward, model.py:987-990).
+ */
+int q38_copy_state_rows(void* const* buffers, const int64_t* row_bytes, const int64_t* rows, int n_buffers,
+                        int64_t src_row, int64_t dst_row, q38_stream_t stream);
 
 /*
  * lm_head candidates: maxima[r, j] = max over the `group` vocab rows v in group j of

@@ -90,6 +90,9 @@ SIGNATURES = {
     "q38_fp8_gemm_silu": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p]),
     "q38_lm_head_groupmax": (
         c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int, c_void_p, c_int64, c_void_p]
+    ),    "q38_copy_state_rows": (
+        c_int, [ctypes.POINTER(c_void_p), ctypes.POINTER(c_int64), ctypes.POINTER(c_int64), c_int, c_int64, c_int64,
+                c_void_p]
     ),
 }
 

@@ -354,5 +354,24 @@ def lm_head_groupmax(x: torch.Tensor, lin: DeviceBF16Linear, maxima: torch.Tenso
               maxima.data_ptr(), maxima.stride(0), _stream())
 
 
+class StateRows:
+    """A fixed list of state buffers whose rows `copy` moves together (q38_copy_state_rows), e.g. every
+    gated-delta layer's recurrent and conv state: rows of the same index across all of them."""
+
+    def __init__(self, buffers: list[torch.Tensor]):
+        _cuda(*buffers)
+        for t in buffers:
+            _need(t.is_contiguous() and t.dim() >= 1, "state buffers must be contiguous with rows along dim 0")
+        self.buffers = list(buffers)  # keeps the storage alive
+        n = len(buffers)
+        self._ptrs = (ctypes.c_void_p * n)(*[t.data_ptr() for t in buffers])
+        self._row_bytes = (ctypes.c_int64 * n)(*[t[0].numel() * t.element_size() if t.shape[0] else 0 for t in buffers])
+        self._rows = (ctypes.c_int64 * n)(*[t.shape[0] for t in buffers])
+
+    def copy(self, src_row: int, dst_row: int) -> None:
+        _lib.call("q38_copy_state_rows", self._ptrs, self._row_bytes, self._rows, len(self.buffers), src_row, dst_row,
+                  _stream())
+
+
 def device_status(reset: bool = True) -> int:
     return _lib.load().q38_device_status(1 if reset else 0)

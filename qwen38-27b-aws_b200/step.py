@@ -106,6 +106,7 @@ class B200Step:
             self._side = torch.cuda.Stream(device=self.device)
         self._graph = None
         self._graph_key = None
+        self._state_rows = None  # every gated-delta layer's state buffers, for copy_states
 
     # ------------------------------------------------------------------ setup
     def _prepare(self, i: int, w: dict) -> _Layer:
@@ -442,11 +443,14 @@ class B200Step:
             raise ValueError("this step keeps no saved states")
         to_saved = "save_slot" in inputs
         slot = int((inputs["save_slot"] if to_saved else inputs["restore_slot"]).reshape(-1)[0])
+        if not 0 <= slot < self.batch:
+            raise ValueError(f"slot {slot} outside the {self.batch} rows")
         src, dst = (slot, slot + self.batch) if to_saved else (slot + self.batch, slot)
-        for l in self.layers:
-            if l.kind == LINEAR:
-                l.mixer.state[dst].copy_(l.mixer.state[src])
-                l.mixer.conv_state[dst].copy_(l.mixer.conv_state[src])
+        if self._state_rows is None:
+            bufs = [b for l in self.layers if l.kind == LINEAR for b in (l.mixer.state, l.mixer.conv_state)]
+            self._state_rows = ops.StateRows(bufs)
+        with torch.cuda.device(self.device):
+            self._state_rows.copy(src, dst)
 
 
 def _to_host(t: torch.Tensor) -> torch.Tensor:

@@ -57,3 +57,20 @@ def test_static_scratch_gemm_checks_arguments_before_any_device_call(pkg):
     assert "residual" in lib_mod.last_error()
     status = lib.q38_fp8_gemm_static_scratch(dummy, 4096, 4096, dummy, dummy, 32768, 0, dummy, 32768, None, 0, 12, None)
     assert status == -1 and "scratch" in lib_mod.last_error()
+
+
+def test_copy_state_rows_checks_rows_on_the_host(pkg):
+    """Rows outside a buffer, null buffers and empty rows are refused before any CUDA call."""
+    import ctypes
+
+    lib_mod = __import__(pkg.__name__ + "._lib", fromlist=["_lib"])
+    lib = lib_mod.load()
+    ptrs = (ctypes.c_void_p * 2)(16, 32)
+    row_bytes = (ctypes.c_int64 * 2)(64, 128)
+    rows = (ctypes.c_int64 * 2)(4, 2)
+    assert lib.q38_copy_state_rows(ptrs, row_bytes, rows, 2, 0, 3, None) == -1  # row 3 of a 2-row buffer
+    assert "outside" in lib_mod.last_error()
+    assert lib.q38_copy_state_rows(ptrs, row_bytes, rows, 2, -1, 0, None) == -1
+    assert lib.q38_copy_state_rows((ctypes.c_void_p * 2)(16, None), row_bytes, rows, 2, 0, 1, None) == -1
+    assert lib.q38_copy_state_rows(ptrs, row_bytes, rows, 2, 1, 1, None) == 0  # same row: nothing to do
+    assert lib.q38_copy_state_rows(None, None, None, 0, 0, 1, None) == 0
