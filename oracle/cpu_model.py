@@ -404,11 +404,17 @@ class GDNLayer:
         self.conv_state[dst] = self.conv_state[src]
 
 
-class AttentionLayer:
-    """FullAttentionStep's CPU branches (model.py:524-809) with a BF16 cache, for one rank's heads."""
+FP8_E4M3_MAX = 240.0  # model.py:37-41: the largest e4m3 value the cache's static scales assume
 
-    def __init__(self, cfg, w: dict, prefix: str, tp: int, rank: int, batch: int, max_seq: int, dtype):
+
+class AttentionLayer:
+    """FullAttentionStep's CPU branches (model.py:524-809) for one rank's heads, with a BF16 cache or,
+    with `kv_scales` = (k_scale, v_scale) (bf16 scalars), the FP8 e4m3 cache (uint8 bytes of
+    value / scale, clamped to +-240; model.py:579-608)."""
+
+    def __init__(self, cfg, w: dict, prefix: str, tp: int, rank: int, batch: int, max_seq: int, dtype, kv_scales=None):
         self.cfg, self.dtype, self.max_seq = cfg, dtype, max_seq
+        self.scales = None if kv_scales is None else tuple(torch.as_tensor(s, dtype=dtype).reshape(1) for s in kv_scales)
         sa = f"{prefix}.self_attn"
         self.q = linear_of(w[f"{sa}.q_proj"])
         self.k = linear_of(w[f"{sa}.k_proj"])
@@ -419,12 +425,30 @@ class AttentionLayer:
         self.heads = cfg.num_attention_heads // tp
         self.kv_heads = cfg.kv_heads_per_rank(tp)
         hd = cfg.head_dim
-        self.k_cache = torch.zeros(batch, self.kv_heads, max_seq, hd, dtype=dtype)
-        self.v_cache = torch.zeros(batch, self.kv_heads, max_seq, hd, dtype=dtype)
+        cache_dtype = dtype if self.scales is None else torch.uint8
+        self.k_cache = torch.zeros(batch, self.kv_heads, max_seq, hd, dtype=cache_dtype)
+        self.v_cache = torch.zeros(batch, self.kv_heads, max_seq, hd, dtype=cache_dtype)
 
     @property
     def groups(self):
         return self.heads // self.kv_heads
+
+    def store(self, t, which: int):
+        """What the cache holds for t: itself, or e4m3 bytes of t / scale clamped to +-240 (model.py:579-585)."""
+        if self.scales is None:
+            return t
+        scale = self.scales[which].float()
+        return (t.float() / scale).clamp(-FP8_E4M3_MAX, FP8_E4M3_MAX).to(torch.float8_e4m3fn).view(torch.uint8)
+
+    def load(self, t, which: int):
+        """Cached values back from `store` (model.py:587-589)."""
+        if self.scales is None:
+            return t
+        return (t.view(torch.float8_e4m3fn).to(self.dtype) * self.scales[which]).to(self.dtype)
+
+    def round_trip(self, t, which: int):
+        """A key or value as it reads back from the cache (model.py:591-593)."""
+        return self.load(self.store(t, which), which)
 
     def project(self, x, cos, sin):
         """model.py:565-577."""
@@ -463,12 +487,13 @@ class AttentionLayer:
         grouped = query.reshape(B, self.kv_heads, self.groups, hd)
         where = torch.where(active > 0.5, position.long(), self.max_seq - 1).unsqueeze(-1)
         earlier = torch.arange(self.max_seq) < position.unsqueeze(-1)
-        cached = torch.matmul(grouped, self.k_cache.transpose(2, 3)).float() + torch.where(earlier, 0.0, MASKED_SCORE).reshape(B, 1, 1, -1)
-        own = torch.matmul(grouped, key.transpose(2, 3)).float()
+        keys, values = self.load(self.k_cache, 0), self.load(self.v_cache, 1)
+        cached = torch.matmul(grouped, keys.transpose(2, 3)).float() + torch.where(earlier, 0.0, MASKED_SCORE).reshape(B, 1, 1, -1)
+        own = torch.matmul(grouped, self.round_trip(key, 0).transpose(2, 3)).float()
         wts = torch.softmax(torch.cat((cached, own), dim=-1) * hd**-0.5, dim=-1).to(qg.dtype)
-        out = torch.matmul(wts[..., :-1], self.v_cache) + wts[..., -1:] * value
+        out = torch.matmul(wts[..., :-1], values) + wts[..., -1:] * self.round_trip(value, 1)
         out = out.reshape(B, 1, self.heads * hd)
-        self.write(key, value, where)
+        self.write(self.store(key, 0), self.store(value, 1), where)
         return out * torch.sigmoid(gate)
 
     def verify(self, x, cos, sin, position, active):
@@ -486,14 +511,17 @@ class AttentionLayer:
         where = torch.where(active.unsqueeze(-1) > 0.5, position.long().unsqueeze(-1) + steps, self.max_seq - K + steps)
         grouped = query.reshape(B, self.kv_heads, self.groups, K, hd)
         earlier = torch.arange(self.max_seq) < position.unsqueeze(-1)
-        cached = torch.matmul(grouped, self.k_cache.unsqueeze(2).transpose(-1, -2)).float()
+        keys, values = self.load(self.k_cache, 0), self.load(self.v_cache, 1)
+        cached = torch.matmul(grouped, keys.unsqueeze(2).transpose(-1, -2)).float()
         cached = cached + torch.where(earlier, 0.0, MASKED_SCORE).reshape(B, 1, 1, 1, -1)
         causal = steps.unsqueeze(0) <= steps.unsqueeze(-1)
-        own = torch.matmul(grouped, key.unsqueeze(2).transpose(-1, -2)).float() + torch.where(causal, 0.0, MASKED_SCORE)
+        own_key = self.round_trip(key, 0).unsqueeze(2)
+        own = torch.matmul(grouped, own_key.transpose(-1, -2)).float() + torch.where(causal, 0.0, MASKED_SCORE)
         wts = torch.softmax(torch.cat((cached, own), dim=-1) * hd**-0.5, dim=-1).to(qg.dtype)
-        out = torch.matmul(wts[..., : self.max_seq], self.v_cache.unsqueeze(2)) + torch.matmul(wts[..., self.max_seq :], value.unsqueeze(2))
+        out = (torch.matmul(wts[..., : self.max_seq], values.unsqueeze(2))
+               + torch.matmul(wts[..., self.max_seq :], self.round_trip(value, 1).unsqueeze(2)))
         out = out.permute(0, 3, 1, 2, 4).reshape(B, K, self.heads * hd)
-        self.write(key, value, where)
+        self.write(self.store(key, 0), self.store(value, 1), where)
         return out * torch.sigmoid(gate)
 
     def prefill(self, x, cos, sin, slot, start, n_valid):
@@ -508,15 +536,15 @@ class AttentionLayer:
         s_idx, st = int(slot.reshape(-1)[0]), int(start.reshape(-1)[0])
         query, key, value, gate = self.norm_rope(qg, k, v, cos, sin)
         grouped = (query[0] * hd**-0.5).reshape(self.kv_heads, G * T, hd)
-        own_k, own_v = key[0], value[0]
+        own_k, own_v = self.round_trip(key[0], 0), self.round_trip(value[0], 1)
         index = torch.arange(G * T) % T
         visible = torch.cat(((torch.arange(self.max_seq) < st).expand(G * T, -1), torch.arange(T).unsqueeze(0) <= index.unsqueeze(-1)), dim=-1)
-        keys = torch.cat((self.k_cache[s_idx], own_k), dim=1)
-        values = torch.cat((self.v_cache[s_idx], own_v), dim=1)
+        keys = torch.cat((self.load(self.k_cache[s_idx], 0), own_k), dim=1)
+        values = torch.cat((self.load(self.v_cache[s_idx], 1), own_v), dim=1)
         out = blocked_attention(grouped, keys, values, visible, ATTENTION_BLOCK)
         out = out.to(qg.dtype).reshape(self.heads, T, hd).transpose(0, 1).reshape(1, T, self.heads * hd)
-        self.k_cache[s_idx, :, st : st + T] = own_k
-        self.v_cache[s_idx, :, st : st + T] = own_v
+        self.k_cache[s_idx, :, st : st + T] = self.store(key[0], 0)
+        self.v_cache[s_idx, :, st : st + T] = self.store(value[0], 1)
         return out * torch.sigmoid(gate)
 
 
@@ -541,14 +569,16 @@ class OracleStep:
 
     def __init__(self, cfg, weights: dict, max_seq_len: int, batch_size: int = 1, tp_degree: int = 1, rank: int = 0,
                  all_reduce=None, dtype=torch.bfloat16, saved_states: bool = False, linear_fp32: bool = False,
-                 verify_tokens: int = 0):
+                 verify_tokens: int = 0, kv_scales=None):
+        """`kv_scales` {layer index: (k_scale, v_scale)} gives those attention layers the FP8 e4m3 cache."""
         self.cfg, self.dtype = cfg, dtype
         self.all_reduce = all_reduce or (lambda t: t)
         self.layers = []
         for i, kind in enumerate(cfg.layer_types):
             p = f"layers.{i}"
             mixer = (GDNLayer(cfg, weights, p, tp_degree, batch_size, dtype, verify_tokens, saved_states) if kind == LINEAR
-                     else AttentionLayer(cfg, weights, p, tp_degree, rank, batch_size, max_seq_len, dtype))
+                     else AttentionLayer(cfg, weights, p, tp_degree, rank, batch_size, max_seq_len, dtype,
+                                         (kv_scales or {}).get(i)))
             self.layers.append((kind, mixer, MLPLayer(weights, p), weights[f"{p}.input_layernorm_weight"].cpu().to(dtype),
                                 weights[f"{p}.post_attention_layernorm_weight"].cpu().to(dtype)))
         if linear_fp32:

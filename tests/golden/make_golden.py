@@ -2,7 +2,12 @@
 
 Run in a checkout of the reference (read-only is fine), never on the GPU box:
 
-    python tests/golden/make_golden.py --reference /path/to/reference
+    python tests/golden/make_golden.py --reference /path/to/reference [--full-width]
+
+--full-width writes full_block.safetensors instead: BASELINE config 0 at full width (one 4-layer block,
+batch 8, rows at positions uniform in [0, 512) over seeded cache and state contents), two greedy
+decode steps through the reference's Qwen38Step, HeadStep maxima over the whole 248,320-token vocabulary
+and ChipHead.next_tokens (the exact top-4 recheck). It takes a few minutes and ~20 GB of host memory.
 
 The reference's `Qwen38Step` and `HeadStep` run their CPU branches on seeded synthetic weights
 (weights.synthetic_layer, tiny config). The one change is the weight codec, swapped the way the
@@ -94,7 +99,7 @@ def build_model(rmodel, ref_cfg, weights, verify_tokens=0):
             plain[name] = t
     missing, unexpected = model.load_state_dict(plain, strict=False)
     assert not unexpected, unexpected
-    assert all(n.endswith(("weight_fp8", "_cache", "_state")) for n in missing), missing
+    assert all(n.endswith(("weight_fp8", "_cache", "_state", "_scale")) for n in missing), missing
     return model
 
 
@@ -127,19 +132,154 @@ def verify_goldens(rgen, ref_cfg, model, ours):
     return tensors
 
 
+FP8_SCALES = (2.0 ** -5, 2.0 ** -6)  # k_scale, v_scale: the value scale clamps the largest values at 240
+
+
+def fp8_cache_goldens(rconfig, rmodel, rgen, ours, weights):
+    """The FP8 e4m3 KV cache (kv_cache_format "fp8", model.py:579-608): decode steps with fresh and idle
+    rows, a prefill chunk, a decode step, then a verify model's decode and verify steps, every output and
+    the final caches, into tiny_fp8.safetensors."""
+    tensors: dict[str, torch.Tensor] = {}
+    gen = torch.Generator().manual_seed(SEED + 2)
+    for verify in (0, VERIFY):
+        ref_cfg = replace(rconfig.tiny_config(num_blocks=1), weight_format="fp8", recurrent_state_format="bf16",
+                          kv_cache_format="fp8")
+        model = build_model(rmodel, ref_cfg, weights, verify)
+        for layer in model.layers:
+            if hasattr(layer, "self_attn"):
+                layer.self_attn.k_scale.data.fill_(FP8_SCALES[0])
+                layer.self_attn.v_scale.data.fill_(FP8_SCALES[1])
+        tag = "v" if verify else "d"
+        calls = []
+        if not verify:
+            for step, (positions, active) in enumerate(decode_schedule()[:4]):
+                calls.append((f"{tag}decode{step}", BATCH, rgen.batch_step_inputs(ref_cfg, positions, MAX_SEQ, torch.bfloat16,
+                                                                                   [bool(a) for a in active])))
+            calls.append((f"{tag}prefill", 1, rgen.prefill_inputs(ref_cfg, 2, 9, CHUNK, CHUNK, torch.bfloat16)))
+            calls.append((f"{tag}after", BATCH, rgen.batch_step_inputs(ref_cfg, [4, 3, CHUNK + 9], MAX_SEQ, torch.bfloat16,
+                                                                        [True] * BATCH)))
+        else:
+            for step in range(2):
+                calls.append((f"{tag}decode{step}", BATCH, rgen.batch_step_inputs(ref_cfg, [step] * BATCH, MAX_SEQ, torch.bfloat16,
+                                                                                   [True] * BATCH)))
+            for step, (positions, active, accepted) in enumerate(verify_schedule()):
+                calls.append((f"{tag}verify{step}", BATCH, rgen.verify_inputs(ref_cfg, positions, VERIFY, MAX_SEQ, torch.bfloat16,
+                                                                               [bool(a) for a in active], accepted)))
+        with torch.no_grad():
+            for name, rows, inputs in calls:
+                width = VERIFY if "verify" in name else (CHUNK if "prefill" in name else 1)
+                x = torch.randn(rows, width, ours.hidden_size, generator=gen).to(torch.bfloat16)
+                tensors[f"{name}.x"] = x
+                tensors.update({f"{name}.{k}": v for k, v in inputs.items()})
+                tensors[f"{name}.y"] = model(inputs_embeds=x, **inputs)
+            for bname, buf in model.named_buffers():
+                if "_cache" in bname:
+                    tensors[f"{tag}state.{bname}"] = buf.clone()
+        tensors[f"{tag}calls"] = torch.tensor([len(calls)])
+    return tensors
+
+
+FULL_BATCH = 8
+FULL_MAX_SEQ = 512
+FULL_STATE_SEED = 1
+FULL_STEPS = 2
+
+
+def full_width_states(cfg, batch: int = FULL_BATCH, max_seq: int = FULL_MAX_SEQ, seed: int = FULL_STATE_SEED):
+    """Seeded recurrent states and KV caches for a full-width block, in layer order: per gated-delta layer
+    (recurrent state N(0, 0.1) [batch, heads, dk, dv], conv state N(0, 1) [batch, conv_dim, kernel - 1]),
+    per attention layer (k_cache, v_cache N(0, 1) [batch, kv_heads, max_seq, head_dim]), all bf16."""
+    gen = torch.Generator().manual_seed(seed)
+    out = []
+    for kind in cfg.layer_types:
+        if kind == pkg.config.LINEAR:
+            st = torch.randn(batch, cfg.linear_num_value_heads, cfg.linear_key_head_dim, cfg.linear_value_head_dim,
+                             generator=gen) * 0.1
+            conv = torch.randn(batch, cfg.linear_conv_dim, cfg.linear_conv_kernel_dim - 1, generator=gen)
+            out.append((st.to(torch.bfloat16), conv.to(torch.bfloat16)))
+        else:
+            shape = (batch, cfg.num_key_value_heads, max_seq, cfg.head_dim)
+            out.append((torch.randn(shape, generator=gen).to(torch.bfloat16), torch.randn(shape, generator=gen).to(torch.bfloat16)))
+    return out
+
+
+def full_width_schedule(cfg):
+    """Step 0's token ids and positions (seed 0), as BASELINE config 0 draws them."""
+    gen = torch.Generator().manual_seed(0)
+    position = torch.randint(0, FULL_MAX_SEQ - FULL_STEPS, (FULL_BATCH,), generator=gen, dtype=torch.int32)
+    tokens = torch.randint(0, cfg.vocab_size, (FULL_BATCH,), generator=gen)
+    return tokens.tolist(), position
+
+
+def full_width_golden(rconfig, rmodel, rgen, rcheckpoint):
+    ours = pkg.config.full_config(num_blocks=1)
+    fields = ("vocab_size", "hidden_size", "intermediate_size", "layer_types", "num_attention_heads",
+              "num_key_value_heads", "head_dim", "linear_num_key_heads", "linear_num_value_heads", "linear_key_head_dim",
+              "linear_value_head_dim", "linear_conv_kernel_dim", "rms_norm_eps", "rope_theta", "partial_rotary_factor")
+    ref_cfg = rconfig.TextConfig(**{f: getattr(ours, f) for f in fields}, weight_format="fp8",
+                                 recurrent_state_format="bf16", kv_cache_format="bf16")
+    weights = {}
+    for i in range(ours.num_hidden_layers):
+        weights |= pkg.weights.synthetic_layer(ours, i, 0, "cpu")
+    model = rmodel.Qwen38Step(ref_cfg, FULL_MAX_SEQ, tp_degree=1, dtype=torch.bfloat16, batch_size=FULL_BATCH).eval()
+    plain = {}
+    for name, t in weights.items():
+        if isinstance(t, pkg.weights.FP8Weight):
+            model.get_submodule(name)._b200_weight = t.dequant()
+        else:
+            plain[name] = t
+    model.load_state_dict(plain, strict=False)
+    for layer, (a, b) in zip(model.layers, full_width_states(ours)):
+        if hasattr(layer, "linear_attn"):
+            layer.linear_attn.recurrent_state = a.clone()
+            layer.linear_attn.conv_state = b.clone()
+        else:
+            layer.self_attn.k_cache = a.clone()
+            layer.self_attn.v_cache = b.clone()
+    head = pkg.weights.synthetic_head(ours, 0, "cpu")
+    lm_rows = head["lm_head"].dequant().to(torch.bfloat16)  # e4m3 x 2^s: exact in bf16
+    hstep = rmodel.HeadStep(ref_cfg, 1, FULL_BATCH, group_rows=32, head_format="bf16").eval()
+    hstep.norm_weight.data = head["norm_weight"]
+    hstep.lm_head.data = lm_rows.transpose(0, 1).contiguous()
+    hstep.rank_gate.data = torch.ones(1)
+    source = rcheckpoint.DictSource({rcheckpoint.FINAL_NORM: head["norm_weight"], rcheckpoint.LM_HEAD: lm_rows})
+    chip = rgen.ChipHead(source, ours.rms_norm_eps, lambda hidden: hstep(hidden), FULL_BATCH)
+
+    tensors = {}
+    tokens, position = full_width_schedule(ours)
+    with torch.no_grad():
+        for step in range(FULL_STEPS):
+            x = pkg.weights.embedding_rows(ours, tokens).reshape(FULL_BATCH, 1, -1)
+            inputs = rgen.batch_step_inputs(ref_cfg, (position + step).tolist(), FULL_MAX_SEQ, torch.bfloat16,
+                                            [True] * FULL_BATCH)
+            y = model(inputs_embeds=x, **inputs)
+            maxima = hstep(y)
+            tensors[f"step{step}.tokens_in"] = torch.tensor(tokens, dtype=torch.int64)
+            tensors[f"step{step}.x"] = x
+            tensors.update({f"step{step}.{k}": v for k, v in inputs.items()})
+            tensors[f"step{step}.y"] = y
+            tensors[f"step{step}.maxima"] = maxima
+            tensors[f"step{step}.top4"] = maxima.float().topk(4, dim=-1).indices
+            tokens = chip.next_tokens(y)
+            tensors[f"step{step}.tokens_out"] = torch.tensor(tokens, dtype=torch.int64)
+    meta = {"seed": "0", "std": str(pkg.weights.STD), "batch": str(FULL_BATCH), "max_seq": str(FULL_MAX_SEQ),
+            "state_seed": str(FULL_STATE_SEED), "steps": str(FULL_STEPS), "weights_sha256": weights_digest(weights),
+            "head_sha256": weights_digest(head), "generator": "tests/golden/make_golden.py --full-width"}
+    path = HERE / "full_block.safetensors"
+    save_file({k: v.contiguous() for k, v in tensors.items()}, str(path), metadata=meta)
+    print(json.dumps(meta, indent=1))
+    print(f"{len(tensors)} tensors, {path.stat().st_size} bytes")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="checkout of the reference (contains qwen38_inf2/)")
+    ap.add_argument("--full-width", action="store_true", help="write full_block.safetensors (config 0 at full width)")
     args = ap.parse_args()
     sys.path.insert(0, str(Path(args.reference).resolve()))
     rconfig = importlib.import_module("qwen38_inf2.config")
     rmodel = importlib.import_module("qwen38_inf2.model")
     rgen = importlib.import_module("qwen38_inf2.generate")
-
-    ours = pkg.config.tiny_config(num_blocks=1)
-    ref_cfg = replace(rconfig.tiny_config(num_blocks=1), weight_format="fp8", recurrent_state_format="bf16", kv_cache_format="bf16")
-    assert ref_cfg.layer_types == ours.layer_types and ref_cfg.hidden_size == ours.hidden_size
-    weights = tiny_weights(ours)
 
     def fp8_forward(self, x):
         # The reference's CPU branch (model.py:222-225) with the weight decode swapped to e4m3 * 2^s.
@@ -147,6 +287,14 @@ def main():
         return F.linear(x, self._b200_weight.to(x.dtype))
 
     rmodel.FP8Linear.forward = fp8_forward
+    if args.full_width:
+        full_width_golden(rconfig, rmodel, rgen, importlib.import_module("qwen38_inf2.checkpoint"))
+        return
+
+    ours = pkg.config.tiny_config(num_blocks=1)
+    ref_cfg = replace(rconfig.tiny_config(num_blocks=1), weight_format="fp8", recurrent_state_format="bf16", kv_cache_format="bf16")
+    assert ref_cfg.layer_types == ours.layer_types and ref_cfg.hidden_size == ours.hidden_size
+    weights = tiny_weights(ours)
     model = build_model(rmodel, ref_cfg, weights)
 
     tensors: dict[str, torch.Tensor] = {}
@@ -216,6 +364,12 @@ def main():
     save_file({k: v.contiguous() for k, v in tensors.items()}, str(HERE / "tiny_block.safetensors"), metadata=meta)
     print(json.dumps(meta, indent=1))
     print(f"{len(tensors)} tensors, {(HERE / 'tiny_block.safetensors').stat().st_size} bytes")
+
+    ftensors = fp8_cache_goldens(rconfig, rmodel, rgen, ours, weights)
+    fmeta = dict(meta, k_scale=str(FP8_SCALES[0]), v_scale=str(FP8_SCALES[1]), verify_tokens=str(VERIFY))
+    del fmeta["decode_steps"]
+    save_file({k: v.contiguous() for k, v in ftensors.items()}, str(HERE / "tiny_fp8.safetensors"), metadata=fmeta)
+    print(f"{len(ftensors)} tensors, {(HERE / 'tiny_fp8.safetensors').stat().st_size} bytes")
 
     vtensors = verify_goldens(rgen, ref_cfg, build_model(rmodel, ref_cfg, weights, VERIFY), ours)
     vmeta = dict(meta, verify_tokens=str(VERIFY), verify_steps=str(len(verify_schedule())))

@@ -146,3 +146,54 @@ def test_oracle_reproduces_reference_verify_steps(pkg):
             tail = K  # the junk positions written by idle rows
             assert torch.equal(mixer.k_cache[:, :, :-tail], tensors[f"state.layers.{i}.self_attn.k_cache"][:, :, :-tail])
             assert torch.equal(mixer.v_cache[:, :, :-tail], tensors[f"state.layers.{i}.self_attn.v_cache"][:, :, :-tail])
+
+
+FP8_GOLDEN = Path(__file__).resolve().parent / "golden" / "tiny_fp8.safetensors"
+
+
+def test_oracle_reproduces_reference_fp8_kv_cache(pkg):
+    """The FP8 e4m3 KV cache with static scales (model.py:579-608), made by the reference with its
+    kv_cache_format "fp8": decode steps (fresh and idle rows), a prefill chunk, decode again, then a
+    verify model's decode and verify steps; every output and the final cache bytes. The value scale
+    is small enough that the largest values clamp at 240."""
+    with safe_open(str(FP8_GOLDEN), "pt") as f:
+        tensors, meta = {k: f.get_tensor(k) for k in f.keys()}, f.metadata()
+    cfg = pkg.config.tiny_config(num_blocks=1)
+    weights = {}
+    for i in range(cfg.num_hidden_layers):
+        weights |= pkg.weights.synthetic_layer(cfg, i, int(meta["seed"]), "cpu", float(meta["std"]))
+    assert _digest(pkg, weights) == meta["weights_sha256"]
+    scales = {i: (float(meta["k_scale"]), float(meta["v_scale"])) for i, kind in enumerate(cfg.layer_types) if kind == om.FULL}
+    # The calls in the order they were made: decode steps, then the prefill chunk and the decode after it,
+    # or the verify steps.
+    order = {"decode": 0, "prefill": 1, "verify": 1, "after": 2}
+
+    def rank(name):
+        kind = name[1:].rstrip("0123456789")
+        return order[kind], int(name[1 + len(kind):] or 0)
+
+    clamped = False
+    for tag, K in (("d", 0), ("v", int(meta["verify_tokens"]))):
+        step = om.OracleStep(cfg, weights, int(meta["max_seq"]), int(meta["batch"]), verify_tokens=K, kv_scales=scales)
+        names = sorted({k.rsplit(".", 1)[0] for k in tensors if k.startswith(tag) and k.endswith(".y")}, key=rank)
+        assert len(names) == int(tensors[f"{tag}calls"])
+        for name in names:
+            keys = ("cos", "sin", "position", "active", "slot", "start", "n_valid", "accepted")
+            inputs = {k: tensors[f"{name}.{k}"] for k in keys if f"{name}.{k}" in tensors}
+            y = step(inputs_embeds=tensors[f"{name}.x"], **inputs)
+            want = tensors[f"{name}.y"]
+            if "active" in inputs:
+                on = inputs["active"] > 0.5
+                y, want = y[on], want[on]
+            elif "n_valid" in inputs:
+                n = int(inputs["n_valid"])
+                y, want = y[:, :n], want[:, :n]
+            assert torch.equal(y, want), f"{name}: oracle differs from the reference"
+        for i, (kind, mixer, *_rest) in enumerate(step.layers):
+            if kind == om.FULL:
+                tail = max(K, 1) if tag == "v" else int(meta["chunk"])
+                for which, cache in (("k_cache", mixer.k_cache), ("v_cache", mixer.v_cache)):
+                    want = tensors[f"{tag}state.layers.{i}.self_attn.{which}"]
+                    assert want.dtype == torch.uint8 and torch.equal(cache[:, :, :-tail], want[:, :, :-tail])
+                    clamped |= bool((want.view(torch.float8_e4m3fn).float().abs() == 240).any())
+    assert clamped, "no cached value reached the 240 clamp"
