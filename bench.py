@@ -610,55 +610,84 @@ def run_micro(args):
                                    "frac": achieved / peak}}), flush=True)
 
 
+NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool (the profiling recipe's figure)
+
+
 def run_micro_allreduce(args, world, rank, local):
-    """The row-parallel projection at TP = world, alone: the plain GEMM, the fused GEMM + all-reduce, and the
-    GEMM followed by an NCCL all-reduce (the baseline), each timed as a CUDA graph of --steps launches,
-    max over ranks. Shapes: down_proj (17408 / world -> 5120) and o_proj (6144 / world -> 5120)."""
+    """the row-parallel projection at TP = world, alone, at M in {64, 256, 512} rows
+    (or --batch): the plain GEMM, the fused GEMM + all-reduce, and the GEMM followed by an NCCL all-reduce
+    (the baseline), each timed as a CUDA graph of --steps launches, max over ranks. Shapes: down_proj
+    (17408 / world -> 5120) and o_proj (6144 / world -> 5120). Per shape it reports
+    hidden = 1 - (fused - gemm) / (nccl - gemm), the share of the baseline's communication time the
+    fused kernel hides, and the roofline of the fused call: the slowest of its HBM bytes at the measured
+    HBM peak, its FLOPs at the FP8 tensor peak (twice the measured BF16 peak), and the all-reduce's
+    NVLink bytes (2 (t - 1) / t x M x 5120 x 2 per rank, the reduce-scatter + all-gather minimum) at the
+    measured 770 GB/s per direction."""
     pkg = importlib.import_module(PACKAGE)
     ops = importlib.import_module(f"{PACKAGE}.ops")
     device = torch.device(f"cuda:{local}")
     torch.cuda.set_device(device)
     torch.distributed.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=120))
-    B, H = args.batch, 5120
-    comm = ops.Communicator(rank, world, max(B, 512), H, device)
-    out = {}
-    for name, k in (("down_proj", 17408 // world), ("o_proj", 6144 // world)):
-        g = torch.Generator().manual_seed(rank)
-        lin = ops.DeviceLinear(pkg.weights.FP8Weight.from_float(torch.randn(H, k, generator=g) * 0.02), device)
-        xq = pkg.codec.to_e5m2_bytes(torch.randn(B, k, generator=g).to(torch.bfloat16)).to(device)
-        splits = min(ops.choose_splits(B, H, k), 8)
-        ws = torch.zeros(max(256, ops.gemm_workspace_bytes(B, H, splits)), dtype=torch.uint8, device=device)
-        part = torch.zeros(B, H, dtype=torch.bfloat16, device=device)
-        variants = {
-            "gemm": lambda: ops.fp8_gemm(xq, lin, part, splits=splits, workspace=ws),
-            "fused": lambda: ops.fp8_gemm_allreduce(xq, lin, comm, splits=splits),
-            "gemm+nccl": lambda: (ops.fp8_gemm(xq, lin, part, splits=splits, workspace=ws),
-                                  torch.distributed.all_reduce(part)),
-        }
-        for vname, fn in variants.items():
-            for _ in range(3):
-                fn()
-            torch.cuda.synchronize()
-            torch.distributed.barrier()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph):
-                for _ in range(args.steps):
+    H = 5120
+    batches = [args.batch] if args.batch_given else [64, 256, 512]
+    comm = ops.Communicator(rank, world, max(max(batches), 512), H, device)
+    hbm, _ = peaks()
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    bf16_tf = float(json.loads(peaks_path.read_text())["bf16_tflops"]) if peaks_path.exists() else 1590.0
+    rows = []
+    for B in batches:
+        for name, k in (("down_proj", 17408 // world), ("o_proj", 6144 // world)):
+            g = torch.Generator().manual_seed(rank)
+            lin = ops.DeviceLinear(pkg.weights.FP8Weight.from_float(torch.randn(H, k, generator=g) * 0.02), device)
+            xq = pkg.codec.to_e5m2_bytes(torch.randn(B, k, generator=g).to(torch.bfloat16)).to(device)
+            splits = min(ops.choose_splits(B, H, k), 8)
+            ws = torch.zeros(max(256, ops.gemm_workspace_bytes(B, H, splits)), dtype=torch.uint8, device=device)
+            part = torch.zeros(B, H, dtype=torch.bfloat16, device=device)
+            variants = {
+                "gemm": lambda: ops.fp8_gemm(xq, lin, part, splits=splits, workspace=ws),
+                "fused": lambda: ops.fp8_gemm_allreduce(xq, lin, comm, splits=splits),
+                "gemm+nccl": lambda: (ops.fp8_gemm(xq, lin, part, splits=splits, workspace=ws),
+                                      torch.distributed.all_reduce(part)),
+            }
+            t = {}
+            for vname, fn in variants.items():
+                for _ in range(3):
                     fn()
-            graph.replay()
-            torch.cuda.synchronize()
-            torch.distributed.barrier()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record()
-            graph.replay()
-            b.record()
-            torch.cuda.synchronize()
-            out[f"{name}.{vname}_us"] = round(max_over_ranks(a.elapsed_time(b), world, device) * 1e3 / args.steps, 2)
-            del graph
-            torch.distributed.barrier()
-        out[f"{name}.splits"] = splits
-    out["device_status"] = ops.device_status()
+                torch.cuda.synchronize()
+                torch.distributed.barrier()
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for _ in range(args.steps):
+                        fn()
+                graph.replay()
+                torch.cuda.synchronize()
+                torch.distributed.barrier()
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ev0.record()
+                graph.replay()
+                ev1.record()
+                torch.cuda.synchronize()
+                t[vname] = max_over_ranks(ev0.elapsed_time(ev1), world, device) * 1e3 / args.steps
+                del graph
+                torch.distributed.barrier()
+            hbm_bytes = H * k * 33 // 32 + B * k + 2 * B * H * 2  # weights + scales, x, residual in and out
+            flops = 2 * B * k * H
+            nvlink_bytes = 2 * (world - 1) / world * B * H * 2
+            bounds = {"hbm_us": hbm_bytes / (hbm * 1e3), "tensor_us": flops / (2 * bf16_tf * 1e6),
+                      "nvlink_us": nvlink_bytes / (NVLINK_GBS * 1e3)}
+            target = max(bounds.values())
+            comm_nccl = t["gemm+nccl"] - t["gemm"]
+            rows.append({"shape": name, "M": B, "k": k, "splits": splits, "gemm_us": round(t["gemm"], 2),
+                         "fused_us": round(t["fused"], 2), "nccl_us": round(t["gemm+nccl"], 2),
+                         "hidden": round(1 - (t["fused"] - t["gemm"]) / comm_nccl, 3) if comm_nccl > 0 else None,
+                         "roofline_us": round(target, 2), "roofline_bound": max(bounds, key=bounds.get)[:-3],
+                         "roofline_frac": round(target / t["fused"], 3),
+                         **{key: round(v, 2) for key, v in bounds.items()}})
+    status = ops.device_status()
     if rank == 0:
-        print(json.dumps({"micro": "gemm_allreduce", "tp": world, "batch": B, **out}), flush=True)
+        print(json.dumps({"micro": "gemm_allreduce", "tp": world, "steps": args.steps, "device_status": status,
+                          "peaks": {"hbm_gbs": hbm, "fp8_tflops": 2 * bf16_tf, "nvlink_gbs": NVLINK_GBS},
+                          "rows": rows}), flush=True)
     comm.close()
     torch.distributed.destroy_process_group()
 
@@ -676,9 +705,12 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    args.batch_given = args.batch is not None
+    if args.batch is None:
+        args.batch = 256
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     world, rank, local = dist_env()

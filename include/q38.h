@@ -301,13 +301,14 @@ void* q38_comm_residual(q38_comm_t comm);  /* this rank's x, bf16 [max_tokens, h
 int q38_comm_destroy(q38_comm_t comm);
 
 /*
- * x += all_reduce(bf16(e5m2(x_q) @ W^T)) over the communicator's ranks, in one kernel per rank: each
- * output tile has an owner rank; every rank pushes its bf16 partial of the tile into the owner's
- * `part` slot over NVLink as 64-bit words {two bf16, the call's epoch}, so a word's arrival is its own
- * ready flag (no fences, no separate flags). The owner polls its slots, sums the partials in rank
- * order (fp32, one bf16 rounding), adds the residual (bf16) and pushes the new rows the same way into
- * every rank's `result` slot, from which each rank writes its own x. The epoch advances on the device
- * (last CTA of the call), and slots alternate by epoch parity, so calls replay inside CUDA graphs.
+ * x += all_reduce(bf16(e5m2(x_q) @ W^T)) over the communicator's ranks, in one kernel per rank. Each
+ * token row of the output has an owner rank (row % world), so every CTA reduces 1/world of the rows of
+ * its own tile: the other ranks push their bf16 partial of the row into the owner's `part` slot over
+ * NVLink as 64-bit words {two bf16, the call's epoch}, so a word's arrival is its own ready flag (no
+ * fences, no separate flags). The owner polls its slots, sums the partials in rank order (fp32, one
+ * bf16 rounding), adds the residual (bf16) and pushes the new row the same way into every rank's
+ * `result` slot, from which each rank writes its own x. The epoch advances on the device (last CTA of
+ * the call), and slots alternate by epoch parity, so calls replay inside CUDA graphs.
  * Every rank makes the same sequence of calls. x is the communicator's residual stream (rows 0 .. tokens - 1), so
  * features == hidden. Replaces the row-parallel projection plus all-reduce of o_proj / out_proj /
  * down_proj (qwen38_inf2/model.py:259, :374, :639 with the NxD reduce, neuron.py:9). Needs the whole

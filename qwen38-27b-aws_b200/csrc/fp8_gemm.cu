@@ -533,61 +533,70 @@ __global__ void __launch_bounds__(192, 1)
         bulk_wait_read0();
       }
     }
-    // Fused all-reduce of the staged bf16 partial: the tile's owner rank sums every rank's partial in
-    // rank order (fp32, one bf16 rounding), adds the residual and writes the result into every rank's
-    // residual stream; the other ranks push their partial to the owner and wait for the result.
+    // Fused all-reduce of the staged bf16 partial. Every token row of the output has an owner rank,
+    // t % world, so every CTA owns 1/world of its own slice and the reduction is spread over all CTAs
+    // of every rank. Warp w of the epilogue takes the slice's rows w, w + 4, ...; lane l their features
+    // 4l .. 4l + 3. A row's owner sums every rank's partial in rank order (fp32, one bf16 rounding),
+    // adds the residual and pushes the new row to every other rank; the other ranks push their partial
+    // of the row to the owner and take the owner's result. Polls are batched: a lane issues the loads of
+    // several rows (and of every source) before it checks any of them, so one round trip covers many.
     if (warp >= 2 && a.epilogue == EPI_ALLREDUCE) {
-      // Each 8-byte piece (four bf16) of this CTA's token slice is handled by one thread end to end, with
-      // consecutive lanes on consecutive pieces so a warp's 16-byte word stores cover 512 contiguous
-      // bytes: a rank that does not own the tile pushes its partial to the owner as words, then waits for
-      // the owner's result words and writes them into its residual stream; the owner waits for every
-      // rank's words, sums the partials in rank order (fp32, one bf16 rounding), adds the residual and
-      // pushes the result to every other rank.
       const bool failed = epi_bar_or(flags[0] != 0);  // also: the staged partial is complete
       const ArArgs& r = a.ar;
-      const int te = threadIdx.x - 64;
       const uint32_t ep = *reinterpret_cast<volatile uint32_t*>(r.epoch);
-      const int par = static_cast<int>(ep & 1u);
-      const int owner = static_cast<int>(static_cast<int64_t>(mt) * r.world / r.ftiles);
+      const int64_t par = static_cast<int64_t>(ep & 1u);
       const __nv_bfloat16* sbase = reinterpret_cast<const __nv_bfloat16*>(stage);
       const int tb0 = n0 + b0 * TOK_BLOCK;            // first token of the slice
       const int tb1 = min(a.T, n0 + b1 * TOK_BLOCK);  // one past the last
-      constexpr int PPR = BM / 4;                     // 4-value pieces per row of the tile
-      const int pieces = tb1 > tb0 ? (tb1 - tb0) * PPR : 0;
       const int64_t hw = r.hidden / 2;                // words per row
+      const int f = m0 + lane * 4;                    // this lane's four features
+      const int first = tb0 + (warp - 2);             // this warp's rows: first, first + 4, ...
+      constexpr int RSTEP = 4;
       bool bad = false;
-      if (live && !failed) {
-        if (owner != r.rank) {
-          unsigned long long* dst = r.part[owner] + (static_cast<int64_t>(par) * r.world + r.rank) * r.tmax * hw;
-          for (int q = te; q < pieces; q += 128) {
-            const int t = tb0 + q / PPR, f = m0 + (q % PPR) * 4;
-            if (f < a.F)
-              st_words2(dst + static_cast<int64_t>(t) * hw + f / 2,
-                        *reinterpret_cast<const uint2*>(sbase + (t - n0) * BM + (f - m0)), ep);
-          }
-          const unsigned long long* res = r.result[r.rank] + static_cast<int64_t>(par) * r.tmax * hw;
-          for (int q = te; q < pieces && !bad; q += 128) {
-            const int t = tb0 + q / PPR, f = m0 + (q % PPR) * 4;
-            if (f >= a.F) continue;
-            uint2 u;
-            bad = !poll_words2(res + static_cast<int64_t>(t) * hw + f / 2, ep, u);
-            if (!bad) *reinterpret_cast<uint2*>(r.x[r.rank] + static_cast<int64_t>(t) * r.hidden + f) = u;
-          }
-        } else {
-          for (int q = te; q < pieces && !bad; q += 128) {
-            const int t = tb0 + q / PPR, f = m0 + (q % PPR) * 4;
-            if (f >= a.F) continue;
+      if (live && !failed && f < a.F) {
+        auto partial = [&](int t) { return *reinterpret_cast<const uint2*>(sbase + (t - n0) * BM + (f - m0)); };
+        auto part_word = [&](int owner, int src, int t) {
+          return r.part[owner] + ((par * r.world + src) * r.tmax + t) * hw + f / 2;
+        };
+        // 1. Rows owned elsewhere: this rank's partial to the owner.
+        for (int t = first; t < tb1; t += RSTEP) {
+          const int owner = t % r.world;
+          if (owner != r.rank) st_words2(part_word(owner, r.rank, t), partial(t), ep);
+        }
+        // 2. Owned rows, UB at a time: every source's words loaded before any is checked.
+        constexpr int UB = 2;
+        for (int t = first; t < tb1 && !bad;) {
+          int rows[UB];
+          int n = 0;
+          for (; t < tb1 && n < UB; t += RSTEP)
+            if (t % r.world == r.rank) rows[n++] = t;
+          if (n == 0) break;
+          unsigned long long lo[UB][kMaxRanks], hi[UB][kMaxRanks];
+#pragma unroll
+          for (int j = 0; j < UB; ++j)
+#pragma unroll
+            for (int src = 0; src < kMaxRanks; ++src)
+              if (j < n && src < r.world && src != r.rank) ld_words2(part_word(r.rank, src, rows[j]), lo[j][src], hi[j][src]);
+#pragma unroll
+          for (int j = 0; j < UB; ++j) {
+            if (j >= n || bad) break;
+            const int t = rows[j];
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int src = 0; src < r.world && !bad; ++src) {
+#pragma unroll
+            for (int src = 0; src < kMaxRanks; ++src) {
+              if (src >= r.world) break;
               uint2 u;
-              if (src == r.rank)
-                u = *reinterpret_cast<const uint2*>(sbase + (t - n0) * BM + (f - m0));
-              else
-                bad = !poll_words2(r.part[r.rank] + ((static_cast<int64_t>(par) * r.world + src) * r.tmax + t) * hw + f / 2,
-                                   ep, u);
+              if (src == r.rank) {
+                u = partial(t);
+              } else if (static_cast<uint32_t>(lo[j][src] >> 32) == ep && static_cast<uint32_t>(hi[j][src] >> 32) == ep) {
+                u = make_uint2(static_cast<uint32_t>(lo[j][src]), static_cast<uint32_t>(hi[j][src]));
+              } else if (!poll_words2(part_word(r.rank, src, t), ep, u)) {
+                bad = true;
+                break;
+              }
               const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
 #pragma unroll
-              for (int j = 0; j < 4; ++j) acc[j] = __fadd_rn(acc[j], __bfloat162float(h[j]));
+              for (int e = 0; e < 4; ++e) acc[e] = __fadd_rn(acc[e], __bfloat162float(h[e]));
             }
             if (bad) break;
             const int64_t at = static_cast<int64_t>(t) * r.hidden + f;
@@ -596,10 +605,36 @@ __global__ void __launch_bounds__(192, 1)
             uint2 ou;
             __nv_bfloat16* oh = reinterpret_cast<__nv_bfloat16*>(&ou);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) oh[j] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(xh[j]), bf16r(acc[j])));
+            for (int e = 0; e < 4; ++e) oh[e] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(xh[e]), bf16r(acc[e])));
             *reinterpret_cast<uint2*>(r.x[r.rank] + at) = ou;
             for (int dq = 0; dq < r.world; ++dq)
-              if (dq != r.rank) st_words2(r.result[dq] + (static_cast<int64_t>(par) * r.tmax + t) * hw + f / 2, ou, ep);
+              if (dq != r.rank) st_words2(r.result[dq] + (par * r.tmax + t) * hw + f / 2, ou, ep);
+          }
+        }
+        // 3. Rows owned elsewhere, UC at a time: the owners' results into this rank's residual stream.
+        constexpr int UC = 8;
+        const unsigned long long* res = r.result[r.rank] + par * r.tmax * hw + f / 2;
+        for (int t = first; t < tb1 && !bad;) {
+          int rows[UC];
+          int n = 0;
+          for (; t < tb1 && n < UC; t += RSTEP)
+            if (t % r.world != r.rank) rows[n++] = t;
+          if (n == 0) break;
+          unsigned long long lo[UC], hi[UC];
+#pragma unroll
+          for (int j = 0; j < UC; ++j)
+            if (j < n) ld_words2(res + static_cast<int64_t>(rows[j]) * hw, lo[j], hi[j]);
+#pragma unroll
+          for (int j = 0; j < UC; ++j) {
+            if (j >= n) break;
+            uint2 u;
+            if (static_cast<uint32_t>(lo[j] >> 32) == ep && static_cast<uint32_t>(hi[j] >> 32) == ep) {
+              u = make_uint2(static_cast<uint32_t>(lo[j]), static_cast<uint32_t>(hi[j]));
+            } else if (!poll_words2(res + static_cast<int64_t>(rows[j]) * hw, ep, u)) {
+              bad = true;
+              break;
+            }
+            *reinterpret_cast<uint2*>(r.x[r.rank] + static_cast<int64_t>(rows[j]) * r.hidden + f) = u;
           }
         }
       }
