@@ -1,19 +1,22 @@
-"""The fused GEMM + all-reduce over NVLink peer memory, on 2 GPUs (skipped with fewer).
+"""The fused GEMM + all-reduce over NVLink peer memory, and B200Step at TP = 2, 4 and 8 (each world
+skipped when the box has fewer GPUs).
 
-Two spawned processes, one per GPU, NCCL process group on 127.0.0.1 (used only to pass the IPC
-handles and for the baseline). Checks, per rank:
+One spawned process per GPU, NCCL process group on 127.0.0.1 (used only to pass the IPC handles, for
+the baseline and to compare ranks). Checks, per rank:
 * q38_fp8_gemm_allreduce equals, bit for bit, its stated arithmetic: every rank's bf16 partial (the
   plain GEMM with the same K splits), summed in fp32 in rank order, rounded to bf16 once, added to the
   residual in bf16; for decode, verify and prefill shapes, over consecutive calls (both epoch
   parities) and inside a replayed CUDA graph.
-* B200Step at TP=2 with the fused all-reduce, layer by layer (the same input on both sides), against
-  the oracle running the same TP=2 arithmetic (two oracle ranks in threads whose all-reduce sums the
-  bf16 partials in fp32 in rank order): within 2e-2 (BASELINE). TP=2 is not compared with TP=1 end
-  to end: rounding each rank's partial to bf16 moves later e5m2 roundings, as the reference's own
-  TP test avoids by running in float32 (tests/test_model_parity.py:141-170).
+* B200Step at TP = world with the fused all-reduce (one full-width 4-layer block; at TP = 8 two ranks
+  share each of the 4 KV heads), layer by layer (the same input on both sides), against the oracle
+  running the same TP arithmetic (world oracle ranks in threads whose all-reduce sums the bf16
+  partials in fp32 in rank order): within 2e-2 (BASELINE). The oracle runs once, in the test process,
+  before the GPU ranks start. Every rank's residual stream must equal rank 0's bit for bit. TP is not
+  compared with TP = 1 end to end: rounding each rank's partial to bf16 moves later e5m2 roundings, as
+  the reference's own TP test avoids by running in float32 (tests/test_model_parity.py:141-170).
 * the same step with the NCCL baseline instead of the fused all-reduce, end to end: within 2e-2.
 Each worker bounds its collectives (a short process-group timeout) and the parent kills workers that
-outlive their budget.
+outlive their budget. NVLS stays off (NCCL_NVLS_ENABLE=0) and the fused kernels use plain peer stores.
 """
 
 import importlib
@@ -37,7 +40,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, queue):
+def _worker(rank, world, port, queue, oracle_path):
     try:
         sys.path.insert(0, str(ROOT))
         os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -104,76 +107,31 @@ def _worker(rank, world, port, queue):
         torch.cuda.synchronize()
         comm.close()
 
-        # B200Step at TP=2: layer by layer against the TP=2 oracle, and fused against NCCL end to end.
-        import threading
-
+        # B200Step at TP = world: layer by layer against the oracle's layer outputs (computed by the parent).
         step_mod = importlib.import_module("qwen38-27b-aws_b200.step")
-        from oracle import cpu_model as om
-
+        ref = torch.load(oracle_path)
         cfg = pkg.config.full_config(num_blocks=1)
-        w = {}
-        for i in range(cfg.num_hidden_layers):
-            w |= pkg.weights.synthetic_layer(cfg, i, seed=0, device=dev)
-        wc = {k: v.to("cpu") for k, v in w.items()}
-        batch = 8
-        g = torch.Generator().manual_seed(0)
-        position = torch.randint(0, 510, (batch,), generator=g, dtype=torch.int32)
-        emb = pkg.weights.embedding_rows(cfg, torch.randint(0, cfg.vocab_size, (batch,), generator=g).tolist())
-        emb = emb.reshape(batch, 1, -1).to(torch.bfloat16)
-        cos, sin = om.rotary(cfg, position, torch.bfloat16)
-        inputs = dict(cos=cos.unsqueeze(1), sin=sin.unsqueeze(1), position=position, active=torch.ones(batch))
-
-        class RankSum:
-            """The TP all-reduce for oracle ranks in threads: fp32 sum in rank order, back to the dtype."""
-
-            def __init__(self, n):
-                self.vals, self.out = {}, None
-                self.bar = threading.Barrier(n, action=self._sum)
-
-            def _sum(self):
-                acc = None
-                for r in sorted(self.vals):
-                    acc = self.vals[r].float() if acc is None else acc + self.vals[r].float()
-                self.out, self.vals = acc, {}
-
-            def bind(self, r):
-                def reduce(t):
-                    self.vals[r] = t
-                    self.bar.wait()
-                    return self.out.to(t.dtype)
-                return reduce
-
-        reducer = RankSum(world)
-        oracles = []
-        for rr in range(world):
-            shard = {}
-            for i in range(cfg.num_hidden_layers):
-                shard |= pkg.weights.shard_layer(cfg, wc, i, rr, world)
-            oracles.append(om.OracleStep(cfg, shard, 512, batch, tp_degree=world, rank=rr, all_reduce=reducer.bind(rr)))
+        w = _block_weights(pkg, cfg)
+        emb, inputs, xs = ref["emb"], ref["inputs"], ref["layers"]
+        batch = emb.shape[0]
         step = step_mod.B200Step(cfg, w, 512, batch, tp_degree=world, rank=rank, device=dev, use_graph=False)
         step.load_decode_inputs(emb, inputs["cos"], inputs["sin"], inputs["position"], inputs["active"])
-        x = emb
         for i in range(cfg.num_hidden_layers):
-            step.x.copy_(x.reshape(batch, -1))
+            step.x.copy_(xs[i].reshape(batch, -1))
+            torch.distributed.barrier()
             step.run_layer(i)
+            torch.cuda.synchronize()
+            every = torch.empty(world * batch, cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+            torch.distributed.all_gather_into_tensor(every, step.x.contiguous())
+            same = all(torch.equal(every[r * batch:(r + 1) * batch], step.x) for r in range(world))
+            results.append((f"TP={world} layer {i}: every rank's residual stream equals rank 0's", same, ""))
             got = step.x.float().cpu()
-            outs = {}
-
-            def run(rr):
-                outs[rr] = oracles[rr].layer(i, x, **inputs)
-
-            threads = [threading.Thread(target=run, args=(rr,)) for rr in range(world)]
-            for t in threads:
-                t.start()
-            for t in threads:
-                t.join()
-            want = outs[0].float().reshape(batch, -1)
+            want = xs[i + 1].float().reshape(batch, -1)
             peak = want.abs().amax(-1, keepdim=True)
             worst = ((got - want).abs() / peak).max().item()
             rel = ((got - want).norm(dim=-1) / want.norm(dim=-1)).max().item()
-            results.append((f"TP=2 layer {i} vs TP=2 oracle", worst <= 2e-2 and rel <= 2e-2,
+            results.append((f"TP={world} layer {i} vs TP={world} oracle", worst <= 2e-2 and rel <= 2e-2,
                             f"max {worst:.3g} of the row peak, relative L2 {rel:.3g}"))
-            x = outs[0]
         step.close()
         torch.distributed.barrier()
         outs = {}
@@ -186,25 +144,97 @@ def _worker(rank, world, port, queue):
         for s in range(2):
             a, b = outs["fused"][s].reshape(batch, -1), outs["nccl"][s].reshape(batch, -1)
             rel = ((a - b).norm(dim=-1) / b.norm(dim=-1)).max().item()
-            results.append((f"step {s} fused vs nccl", rel <= 2e-2, f"relative L2 {rel:.3g}"))
+            results.append((f"TP={world} step {s} fused vs nccl", rel <= 2e-2, f"relative L2 {rel:.3g}"))
         torch.distributed.destroy_process_group()
         queue.put((rank, results, None))
     except Exception:  # noqa: BLE001
         queue.put((rank, [], traceback.format_exc()))
 
 
-def test_fused_gemm_allreduce_on_two_gpus():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def _block_weights(pkg, cfg) -> dict:
+    """One full-width 4-layer block's unsharded weights, drawn on the CPU (the same values in every process)."""
+    w = {}
+    for i in range(cfg.num_hidden_layers):
+        w |= pkg.weights.synthetic_layer(cfg, i, seed=0, device="cpu")
+    return w
+
+
+def _oracle_layers(world: int, path: Path) -> None:
+    """The TP = world oracle's output after each layer of the block, teacher-forced (layer i gets the
+    oracle's own output of layer i - 1), with the decode inputs, saved for the GPU ranks."""
+    import threading
+
+    from oracle import cpu_model as om
+
+    pkg = importlib.import_module("qwen38-27b-aws_b200")
+    cfg = pkg.config.full_config(num_blocks=1)
+    w = _block_weights(pkg, cfg)
+    batch = 8
+    g = torch.Generator().manual_seed(0)
+    position = torch.randint(0, 510, (batch,), generator=g, dtype=torch.int32)
+    emb = pkg.weights.embedding_rows(cfg, torch.randint(0, cfg.vocab_size, (batch,), generator=g).tolist())
+    emb = emb.reshape(batch, 1, -1).to(torch.bfloat16)
+    cos, sin = om.rotary(cfg, position, torch.bfloat16)
+    inputs = dict(cos=cos.unsqueeze(1), sin=sin.unsqueeze(1), position=position, active=torch.ones(batch))
+
+    class RankSum:
+        """The TP all-reduce for oracle ranks in threads: fp32 sum in rank order, back to the dtype."""
+
+        def __init__(self, n):
+            self.vals, self.out = {}, None
+            self.bar = threading.Barrier(n, action=self._sum)
+
+        def _sum(self):
+            acc = None
+            for r in sorted(self.vals):
+                acc = self.vals[r].float() if acc is None else acc + self.vals[r].float()
+            self.out, self.vals = acc, {}
+
+        def bind(self, r):
+            def reduce(t):
+                self.vals[r] = t
+                self.bar.wait()
+                return self.out.to(t.dtype)
+            return reduce
+
+    reducer = RankSum(world)
+    oracles = []
+    for rr in range(world):
+        shard = {}
+        for i in range(cfg.num_hidden_layers):
+            shard |= pkg.weights.shard_layer(cfg, w, i, rr, world)
+        oracles.append(om.OracleStep(cfg, shard, 512, batch, tp_degree=world, rank=rr, all_reduce=reducer.bind(rr)))
+    xs = [emb]
+    for i in range(cfg.num_hidden_layers):
+        outs = {}
+
+        def run(rr):
+            outs[rr] = oracles[rr].layer(i, xs[-1], **inputs)
+
+        threads = [threading.Thread(target=run, args=(rr,)) for rr in range(world)]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        xs.append(outs[0])
+    torch.save({"emb": emb, "inputs": inputs, "layers": xs}, path)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_gemm_allreduce_and_tp_step(world, tmp_path):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    oracle_path = tmp_path / f"oracle_tp{world}.pt"
+    _oracle_layers(world, oracle_path)
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, queue)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue, str(oracle_path))) for r in range(world)]
     for p in procs:
         p.start()
     got = {}
     try:
-        for _ in range(2):
+        for _ in range(world):
             rank, results, err = queue.get(timeout=900)
             got[rank] = (results, err)
     finally:
