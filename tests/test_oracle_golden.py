@@ -197,3 +197,30 @@ def test_oracle_reproduces_reference_fp8_kv_cache(pkg):
                     assert want.dtype == torch.uint8 and torch.equal(cache[:, :, :-tail], want[:, :, :-tail])
                     clamped |= bool((want.view(torch.float8_e4m3fn).float().abs() == 240).any())
     assert clamped, "no cached value reached the 240 clamp"
+
+
+def test_oracle_reproduces_full_width_reference_steps_and_head(pkg):
+    """BASELINE config 0 at full width, made by the reference (tests/golden/make_golden.py --full-width):
+    two greedy decode steps of one 4-layer block at batch 8 over seeded states, each output bit for bit,
+    then HeadStep's maxima over the whole 248,320-token vocabulary (fp32 logits in another summation
+    layout: within 1e-5 relative) and ChipHead's tokens and top-4 groups exactly."""
+    from tests import full_width as fw
+
+    tensors, meta = fw.load()
+    cfg, w, head = fw.model(pkg, meta)
+    batch = int(meta["batch"])
+    oracle = om.OracleStep(cfg, w, int(meta["max_seq"]), batch)
+    fw.seed_oracle(oracle, cfg, meta)
+    lm_rows = head["lm_head"].dequant()
+    for s in range(int(meta["steps"])):
+        y = oracle(inputs_embeds=tensors[f"step{s}.x"], **fw.inputs(tensors, s))
+        assert torch.equal(y, tensors[f"step{s}.y"]), f"step {s}: oracle differs from the reference"
+        maxima = om.head_maxima(cfg, y, head["norm_weight"], head["lm_head"].q, head["lm_head"].scale)
+        want = tensors[f"step{s}.maxima"]
+        rel = ((maxima - want).abs() / want.abs().amax(-1, keepdim=True)).max().item()
+        assert rel <= 1e-5, f"step {s}: maxima differ by {rel:.3g} of the row peak"
+        assert torch.equal(maxima.topk(4, dim=-1).indices, tensors[f"step{s}.top4"])
+        tokens = om.recheck_tokens(cfg, y, head["norm_weight"], lm_rows, maxima)
+        assert tokens == tensors[f"step{s}.tokens_out"].tolist()
+        if s + 1 < int(meta["steps"]):
+            assert tokens == tensors[f"step{s + 1}.tokens_in"].tolist()
