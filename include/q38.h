@@ -211,6 +211,18 @@ int q38_attn_prefill(const void* qkv, int64_t ld_qkv, const void* q_norm_weight,
                      q38_stream_t stream);
 
 /*
+ * q38_attn_prefill with the FP8 e4m3 cache (uint8 [cache_rows, num_kv_heads, max_seq, head_dim]): the
+ * chunk's keys and values are written as e4m3 bytes of value / scale clamped to +-240, and every cached
+ * key and value, the chunk's own included, is read back as bf16(e4m3 * scale) (FullAttentionStep.prefill
+ * with kv_cache_format "fp8", qwen38_inf2/model.py:732-786 with _store / _load / _round_trip :579-593).
+ */
+int q38_attn_prefill_e4m3(const void* qkv, int64_t ld_qkv, const void* q_norm_weight, const void* k_norm_weight,
+                          const void* cos, const void* sin, void* k_cache, void* v_cache, float k_scale, float v_scale,
+                          int64_t slot, int64_t cache_rows, int64_t max_seq, int64_t tokens, int64_t start, void* out,
+                          int64_t ld_out, int num_q_heads, int num_kv_heads, int head_dim, int rot_dim, float eps,
+                          void* workspace, size_t workspace_bytes, q38_stream_t stream);
+
+/*
  * K verify tokens per row through the gated delta rule with commit-on-accept: first the last verify
  * step's first accepted[b] tokens are committed to the row's state and conv state from the pending
  * buffers, then the K new tokens run from the committed state as one small chunk without changing it,
@@ -273,6 +285,34 @@ int q38_attn_decode(const void* qkv, int64_t ld_qkv, const void* q_norm_w, const
                     const float* active, void* out, int64_t ld_out, int64_t batch, int num_q_heads,
                     int num_kv_heads, int head_dim, int rot_dim, float eps, const int32_t* row_order,
                     q38_stream_t stream);
+
+/*
+ * Gated full attention against a cache of any length, split along the cache: decode (tokens = 1) or
+ * verify (tokens = K, each token attending to cache positions < position and to the step's own tokens
+ * up to itself), with a BF16 cache or an FP8 e4m3 cache with static scales (kv_format Q38_KV_E4M3:
+ * the cache holds e4m3 bytes of value / scale clamped to +-240 and reads back as bf16(e4m3 * scale),
+ * the step's own keys and values taking the same round trip). The output and the cache writes are
+ * those of q38_attn_decode / q38_attn_verify. Three launches: per (chunk of the cache, row, KV head) the
+ * bf16 scores and their softmax statistics, then the bf16 weights times the values, then per (row, KV
+ * head) the chunks' partials summed in chunk order, the own term and the gate. Replaces
+ * FullAttentionStep.forward / verify (qwen38_inf2/model.py:610-675) with _store / _load / _round_trip
+ * (:579-593) and the NKI decode / verify attention (kernels.py:437-488, :491-644) for long caches.
+ *
+ *   qkv, cos, sin, position, active, out   as q38_attn_verify (rows b * tokens + t)
+ *   k_cache, v_cache   [batch, num_kv_heads, max_seq, head_dim], bf16 or e4m3 bytes
+ *   k_scale, v_scale   the FP8 cache's scales (ignored for BF16)
+ *   workspace          q38_attn_split_workspace_bytes(...) bytes, 16-byte aligned
+ * groups x tokens <= 32, tokens <= 8.
+ */
+#define Q38_KV_BF16 0
+#define Q38_KV_E4M3 1
+size_t q38_attn_split_workspace_bytes(int64_t batch, int num_q_heads, int num_kv_heads, int tokens, int64_t max_seq,
+                                      int head_dim);
+int q38_attn_split(const void* qkv, int64_t ld_qkv, const void* q_norm_w, const void* k_norm_w, const void* cos,
+                   const void* sin, void* k_cache, void* v_cache, int kv_format, float k_scale, float v_scale,
+                   int64_t max_seq, const int32_t* position, const float* active, void* out, int64_t ld_out,
+                   int64_t batch, int tokens, int num_q_heads, int num_kv_heads, int head_dim, int rot_dim, float eps,
+                   void* workspace, size_t workspace_bytes, q38_stream_t stream);
 
 /*
  * The longest-first schedule for q38_attn_decode: row_order int32 [batch] = the rows by decreasing

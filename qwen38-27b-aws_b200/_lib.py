@@ -68,6 +68,12 @@ SIGNATURES = {
         [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
          c_int64, c_int64, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_float, c_void_p, c_size_t, c_void_p],
     ),
+    "q38_attn_prefill_e4m3": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_float, c_int64,
+         c_int64, c_int64, c_int64, c_int64, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_float, c_void_p, c_size_t,
+         c_void_p],
+    ),
     "q38_gdn_verify_workspace_bytes": (c_size_t, [c_int64, c_int, c_int, c_int]),
     "q38_gdn_verify_commit": (
         c_int,
@@ -90,7 +96,14 @@ SIGNATURES = {
     "q38_fp8_gemm_silu": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p]),
     "q38_lm_head_groupmax": (
         c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int, c_void_p, c_int64, c_void_p]
-    ),    "q38_copy_state_rows": (
+    ),    "q38_attn_split_workspace_bytes": (c_size_t, [c_int64, c_int, c_int, c_int, c_int64, c_int]),
+    "q38_attn_split": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float, c_float,
+         c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p,
+         c_size_t, c_void_p],
+    ),
+    "q38_copy_state_rows": (
         c_int, [ctypes.POINTER(c_void_p), ctypes.POINTER(c_int64), ctypes.POINTER(c_int64), c_int, c_int64, c_int64,
                 c_void_p]
     ),

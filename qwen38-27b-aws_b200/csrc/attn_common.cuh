@@ -1,9 +1,35 @@
 // Pieces shared by the decode and prefill attention kernels.
 #pragma once
 
+#include <cuda_fp8.h>
+
 #include "q38_common.cuh"
 
 namespace q38 {
+
+// The FP8 e4m3 KV cache with static scales (qwen38_inf2/model.py:579-593): the cache holds e4m3 bytes of
+// value / scale clamped to +-240 (the reference's FP8_E4M3_MAX, model.py:37-41), and reads back as
+// bf16(e4m3 * scale).
+constexpr float kKvFp8Max = 240.0f;
+__device__ __forceinline__ float fp8_load(uint8_t b, float scale) {
+  const __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b), __NV_E4M3);
+  return bf16r(__fmul_rn(__half2float(__half(h)), scale));
+}
+__device__ __forceinline__ uint8_t fp8_store(float x, float scale) {
+  const float v = fminf(fmaxf(__fdiv_rn(x, scale), -kKvFp8Max), kKvFp8Max);
+  return static_cast<uint8_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3));
+}
+// Sixteen e4m3 bytes decoded to sixteen bf16 values (two 16-byte pieces).
+__device__ __forceinline__ void fp8_load16(const uint4& v, float scale, uint4& lo, uint4& hi) {
+  const uint8_t* b = reinterpret_cast<const uint8_t*>(&v);
+  uint32_t* l = reinterpret_cast<uint32_t*>(&lo);
+  uint32_t* h = reinterpret_cast<uint32_t*>(&hi);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    l[e] = pack_bf16x2(fp8_load(b[2 * e], scale), fp8_load(b[2 * e + 1], scale));
+    h[e] = pack_bf16x2(fp8_load(b[8 + 2 * e], scale), fp8_load(b[8 + 2 * e + 1], scale));
+  }
+}
 
 // RMS norm (1 + w) of one head held by a warp (values in smem, in place), then partial rotary on
 // the first `rot` dims: bf16(bf16(x*cos) + bf16(rotate_half(x)*sin)) (model.py:54-57, :70-82).

@@ -18,6 +18,12 @@
 //              block's weighted values are rounded to bf16 (its BF16 matmul output) before the fp32
 //              rescale-and-add. Output: bf16(out / total) * bf16(sigmoid(gate)) in bf16, then e5m2 for
 //              o_proj.
+// With the FP8 e4m3 cache (q38_attn_prefill_e4m3) the prep kernel writes the chunk's keys and values as
+// cache bytes, and the attention decodes every 64-key tile to bf16(e4m3 * scale) on its way into shared
+// memory, so the chunk's own keys and values are read as the cache's round trip of them, as the
+// reference attends to them (model.py:748-752).
+#include <cmath>
+
 #include "attn_common.cuh"
 
 namespace {
@@ -33,8 +39,9 @@ struct AttnPrefillArgs {
   const __nv_bfloat16* k_norm_w;
   const __nv_bfloat16* cos;  // [tokens, rot]
   const __nv_bfloat16* sin;
-  __nv_bfloat16* k_cache;  // this row: [num_kv_heads][max_seq][HD]
-  __nv_bfloat16* v_cache;
+  uint8_t* k_cache;  // this row: [num_kv_heads][max_seq][HD], bf16 or e4m3 bytes
+  uint8_t* v_cache;
+  float k_scale, v_scale;  // e4m3 cache
   int64_t max_seq;
   int tokens, start;
   uint8_t* out;
@@ -44,7 +51,7 @@ struct AttnPrefillArgs {
   __nv_bfloat16* qs;  // workspace [num_kv_heads][groups][tokens][HD]
 };
 
-template <int HD>
+template <int HD, bool FP8>
 __global__ void __launch_bounds__(kThreads) attn_prefill_prep_kernel(AttnPrefillArgs a) {
   extern __shared__ __align__(16) float xs[];  // [heads + kv heads][HD]
   const int t = blockIdx.x;
@@ -71,13 +78,17 @@ __global__ void __launch_bounds__(kThreads) attn_prefill_prep_kernel(AttnPrefill
       for (int d = lane; d < HD; d += 32) dst[d] = __float2bfloat16_rn(__fmul_rn(x[d], a.scale));
     } else {
       const int kvh = h - a.num_q_heads;
-      __nv_bfloat16* kd = a.k_cache + (static_cast<int64_t>(kvh) * a.max_seq + pos) * HD;
-      __nv_bfloat16* vd = a.v_cache + (static_cast<int64_t>(kvh) * a.max_seq + pos) * HD;
+      const int64_t at = (static_cast<int64_t>(kvh) * a.max_seq + pos) * HD;
       const __nv_bfloat16* vraw = row + static_cast<int64_t>(a.num_q_heads) * 2 * HD +
                                   static_cast<int64_t>(a.num_kv_heads + kvh) * HD;
       for (int d = lane; d < HD; d += 32) {
-        kd[d] = __float2bfloat16_rn(x[d]);
-        vd[d] = vraw[d];
+        if constexpr (FP8) {
+          a.k_cache[at + d] = fp8_store(x[d], a.k_scale);
+          a.v_cache[at + d] = fp8_store(__bfloat162float(vraw[d]), a.v_scale);
+        } else {
+          reinterpret_cast<__nv_bfloat16*>(a.k_cache)[at + d] = __float2bfloat16_rn(x[d]);
+          reinterpret_cast<__nv_bfloat16*>(a.v_cache)[at + d] = vraw[d];
+        }
       }
     }
   }
@@ -114,7 +125,7 @@ __device__ __forceinline__ int64_t ref_block(int64_t key, int64_t start, int64_t
 // warp w holds row tile w / 2 and, of each 64-key tile, keys 32 (w % 2) .. + 31 for the scores and
 // head dims (w % 2) HD / 2 .. + HD / 2 - 1 for the weighted values. Scores and weighted values run on
 // mma.sync (BF16 in, fp32 accumulate): the reference's BF16 matmuls.
-template <int HD>
+template <int HD, bool FP8>
 __global__ void __launch_bounds__(PF_THREADS, 1) attn_prefill_kernel(AttnPrefillArgs a) {
   using S = PrefillSmem<HD>;
   constexpr int QP = S::QP, PP = S::PP;
@@ -135,8 +146,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1) attn_prefill_kernel(AttnPrefill
   const int wm = warp >> 1, wh = warp & 1;
   const int t_last = min(t0 + tq, a.tokens) - 1;
   const int n_keys = a.start + t_last + 1;
-  const __nv_bfloat16* kc = a.k_cache + static_cast<int64_t>(kvh) * a.max_seq * HD;
-  const __nv_bfloat16* vc = a.v_cache + static_cast<int64_t>(kvh) * a.max_seq * HD;
+  const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(a.k_cache) + static_cast<int64_t>(kvh) * a.max_seq * HD;
+  const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(a.v_cache) + static_cast<int64_t>(kvh) * a.max_seq * HD;
+  const uint8_t* kc8 = a.k_cache + static_cast<int64_t>(kvh) * a.max_seq * HD;  // e4m3 cache
+  const uint8_t* vc8 = a.v_cache + static_cast<int64_t>(kvh) * a.max_seq * HD;
 
   // Queries (rows past the chunk are zero).
   for (int i = tid; i < ROWS * (HD / 8); i += PF_THREADS) {
@@ -157,6 +170,34 @@ __global__ void __launch_bounds__(PF_THREADS, 1) attn_prefill_kernel(AttnPrefill
   auto load_tile = [&](int kb, int buf, bool values) {
     __nv_bfloat16* kd = ks + buf * KB * QP;
     __nv_bfloat16* vd = vs + buf * KB * QP;
+    if constexpr (FP8) {
+      // Decoded on the way in: every 16-byte piece loaded before any is stored.
+      constexpr int PIECES = KB * (HD / 16), PER = (PIECES + PF_THREADS - 1) / PF_THREADS;
+      uint4 rk[PER], rv[PER];
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int i = tid + u * PF_THREADS, j = i / (HD / 16), c = i % (HD / 16);
+        const bool in = i < PIECES && kb + j < n_keys;
+        const int64_t off = static_cast<int64_t>(kb + j) * HD + 16 * c;
+        rk[u] = in ? *reinterpret_cast<const uint4*>(kc8 + off) : make_uint4(0u, 0u, 0u, 0u);
+        rv[u] = in && values ? *reinterpret_cast<const uint4*>(vc8 + off) : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int i = tid + u * PF_THREADS, j = i / (HD / 16), c = i % (HD / 16);
+        if (i >= PIECES) break;
+        uint4 lo, hi;
+        fp8_load16(rk[u], a.k_scale, lo, hi);
+        *reinterpret_cast<uint4*>(kd + j * QP + 16 * c) = lo;
+        *reinterpret_cast<uint4*>(kd + j * QP + 16 * c + 8) = hi;
+        if (values) {
+          fp8_load16(rv[u], a.v_scale, lo, hi);
+          *reinterpret_cast<uint4*>(vd + j * QP + 16 * c) = lo;
+          *reinterpret_cast<uint4*>(vd + j * QP + 16 * c + 8) = hi;
+        }
+      }
+      return;
+    }
     for (int i = tid; i < KB * (HD / 8); i += PF_THREADS) {
       const int j = i / (HD / 8), c = i % (HD / 8);
       const int key = kb + j;
@@ -352,7 +393,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) attn_prefill_kernel(AttnPrefill
   }
 }
 
-template <int HD>
+template <int HD, bool FP8>
 int launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t stream) {
   using S = PrefillSmem<HD>;
   static unsigned long long done_mask = 0;
@@ -360,18 +401,18 @@ int launch_attn_prefill(const AttnPrefillArgs& a, cudaStream_t stream) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return q38host::cuda_status(e, "cudaGetDevice");
   if (dev < 64 && !(done_mask & (1ull << dev))) {
-    e = cudaFuncSetAttribute(attn_prefill_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    e = cudaFuncSetAttribute(attn_prefill_kernel<HD, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(S::TOTAL));
     if (e != cudaSuccess) return q38host::cuda_status(e, "cudaFuncSetAttribute(attn_prefill)");
     done_mask |= 1ull << dev;
   }
   const size_t prep_smem = sizeof(float) * (a.num_q_heads + a.num_kv_heads) * HD;
-  attn_prefill_prep_kernel<HD><<<a.tokens, kThreads, prep_smem, stream>>>(a);
+  attn_prefill_prep_kernel<HD, FP8><<<a.tokens, kThreads, prep_smem, stream>>>(a);
   e = cudaGetLastError();
   if (e != cudaSuccess) return q38host::cuda_status(e, "attn_prefill_prep launch");
   const int tq = ROWS / a.groups;
   dim3 grid(a.num_kv_heads, (a.tokens + tq - 1) / tq);
-  attn_prefill_kernel<HD><<<grid, PF_THREADS, S::TOTAL, stream>>>(a);
+  attn_prefill_kernel<HD, FP8><<<grid, PF_THREADS, S::TOTAL, stream>>>(a);
   return q38host::cuda_status(cudaGetLastError(), "attn_prefill launch");
 }
 
@@ -382,11 +423,13 @@ extern "C" size_t q38_attn_prefill_workspace_bytes(int64_t tokens, int num_q_hea
   return 2 * static_cast<size_t>(tokens) * num_q_heads * head_dim;
 }
 
-extern "C" int q38_attn_prefill(const void* qkv, int64_t ld_qkv, const void* q_norm_weight, const void* k_norm_weight,
-                                const void* cos, const void* sin, void* k_cache, void* v_cache, int64_t slot,
-                                int64_t cache_rows, int64_t max_seq, int64_t tokens, int64_t start, void* out,
-                                int64_t ld_out, int num_q_heads, int num_kv_heads, int head_dim, int rot_dim, float eps,
-                                void* workspace, size_t workspace_bytes, q38_stream_t stream) {
+namespace {
+
+int attn_prefill_any(const void* qkv, int64_t ld_qkv, const void* q_norm_weight, const void* k_norm_weight,
+                     const void* cos, const void* sin, void* k_cache, void* v_cache, bool fp8, float k_scale,
+                     float v_scale, int64_t slot, int64_t cache_rows, int64_t max_seq, int64_t tokens, int64_t start,
+                     void* out, int64_t ld_out, int num_q_heads, int num_kv_heads, int head_dim, int rot_dim, float eps,
+                     void* workspace, size_t workspace_bytes, q38_stream_t stream) {
   using namespace q38host;
   if (!qkv || !q_norm_weight || !k_norm_weight || !cos || !sin || !k_cache || !v_cache || !out || !workspace)
     return set_error("q38_attn_prefill: null pointer"), Q38_ERR_ARG;
@@ -406,16 +449,20 @@ extern "C" int q38_attn_prefill(const void* qkv, int64_t ld_qkv, const void* q_n
     return set_error("q38_attn_prefill: workspace too small"), Q38_ERR_ARG;
   if ((reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache)) & 15u)
     return set_error("q38_attn_prefill: caches must be 16-byte aligned"), Q38_ERR_ARG;
+  if (fp8 && !(k_scale > 0.f && v_scale > 0.f && std::isfinite(k_scale) && std::isfinite(v_scale)))
+    return set_error("q38_attn_prefill_e4m3: scales must be positive"), Q38_ERR_ARG;
   AttnPrefillArgs a{};
-  const int64_t row_elems = static_cast<int64_t>(num_kv_heads) * max_seq * head_dim;
+  const int64_t row_bytes = static_cast<int64_t>(num_kv_heads) * max_seq * head_dim * (fp8 ? 1 : 2);
   a.qkv = static_cast<const __nv_bfloat16*>(qkv);
   a.ld_qkv = ld_qkv;
   a.q_norm_w = static_cast<const __nv_bfloat16*>(q_norm_weight);
   a.k_norm_w = static_cast<const __nv_bfloat16*>(k_norm_weight);
   a.cos = static_cast<const __nv_bfloat16*>(cos);
   a.sin = static_cast<const __nv_bfloat16*>(sin);
-  a.k_cache = static_cast<__nv_bfloat16*>(k_cache) + slot * row_elems;
-  a.v_cache = static_cast<__nv_bfloat16*>(v_cache) + slot * row_elems;
+  a.k_cache = static_cast<uint8_t*>(k_cache) + slot * row_bytes;
+  a.v_cache = static_cast<uint8_t*>(v_cache) + slot * row_bytes;
+  a.k_scale = k_scale;
+  a.v_scale = v_scale;
   a.max_seq = max_seq;
   a.tokens = static_cast<int>(tokens);
   a.start = static_cast<int>(start);
@@ -431,7 +478,30 @@ extern "C" int q38_attn_prefill(const void* qkv, int64_t ld_qkv, const void* q_n
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (ROWS % a.groups != 0)
     return set_error("q38_attn_prefill: %d query heads per KV head do not divide %d rows", a.groups, ROWS), Q38_ERR_UNSUPPORTED;
-  if (head_dim == 256) return launch_attn_prefill<256>(a, s);
-  if (head_dim == 32) return launch_attn_prefill<32>(a, s);
+  if (head_dim == 256) return fp8 ? launch_attn_prefill<256, true>(a, s) : launch_attn_prefill<256, false>(a, s);
+  if (head_dim == 32) return fp8 ? launch_attn_prefill<32, true>(a, s) : launch_attn_prefill<32, false>(a, s);
   return set_error("q38_attn_prefill: head_dim %d not built (256, 32 are)", head_dim), Q38_ERR_UNSUPPORTED;
+}
+
+}  // namespace
+
+extern "C" int q38_attn_prefill(const void* qkv, int64_t ld_qkv, const void* q_norm_weight, const void* k_norm_weight,
+                                const void* cos, const void* sin, void* k_cache, void* v_cache, int64_t slot,
+                                int64_t cache_rows, int64_t max_seq, int64_t tokens, int64_t start, void* out,
+                                int64_t ld_out, int num_q_heads, int num_kv_heads, int head_dim, int rot_dim, float eps,
+                                void* workspace, size_t workspace_bytes, q38_stream_t stream) {
+  return attn_prefill_any(qkv, ld_qkv, q_norm_weight, k_norm_weight, cos, sin, k_cache, v_cache, false, 1.f, 1.f, slot,
+                          cache_rows, max_seq, tokens, start, out, ld_out, num_q_heads, num_kv_heads, head_dim, rot_dim,
+                          eps, workspace, workspace_bytes, stream);
+}
+
+extern "C" int q38_attn_prefill_e4m3(const void* qkv, int64_t ld_qkv, const void* q_norm_weight,
+                                     const void* k_norm_weight, const void* cos, const void* sin, void* k_cache,
+                                     void* v_cache, float k_scale, float v_scale, int64_t slot, int64_t cache_rows,
+                                     int64_t max_seq, int64_t tokens, int64_t start, void* out, int64_t ld_out,
+                                     int num_q_heads, int num_kv_heads, int head_dim, int rot_dim, float eps,
+                                     void* workspace, size_t workspace_bytes, q38_stream_t stream) {
+  return attn_prefill_any(qkv, ld_qkv, q_norm_weight, k_norm_weight, cos, sin, k_cache, v_cache, true, k_scale, v_scale,
+                          slot, cache_rows, max_seq, tokens, start, out, ld_out, num_q_heads, num_kv_heads, head_dim,
+                          rot_dim, eps, workspace, workspace_bytes, stream);
 }

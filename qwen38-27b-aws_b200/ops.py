@@ -297,16 +297,26 @@ def attn_prefill_workspace_bytes(tokens: int, num_q_heads: int, head_dim: int) -
 
 
 def attn_prefill(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, out, workspace, *, slot: int, start: int,
-                 num_q_heads: int, num_kv_heads: int, head_dim: int, rot_dim: int, eps: float) -> None:
-    """One row's prefill chunk through keys-first gated attention; writes the chunk's K/V to the cache."""
+                 num_q_heads: int, num_kv_heads: int, head_dim: int, rot_dim: int, eps: float,
+                 kv_scales: tuple[float, float] | None = None) -> None:
+    """One row's prefill chunk through keys-first gated attention; writes the chunk's K/V to the cache.
+    `kv_scales` = (k_scale, v_scale) selects the FP8 e4m3 cache (uint8 k_cache / v_cache)."""
     _cuda(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, out, workspace)
     _need(cos.is_contiguous() and sin.is_contiguous() and cos.shape[-1] == rot_dim, "cos/sin [tokens, rot] contiguous")
     _need(k_cache.is_contiguous() and v_cache.is_contiguous(), "caches must be contiguous")
+    fp8 = kv_scales is not None
+    _need(k_cache.dtype == (U8 if fp8 else BF16) and v_cache.dtype == k_cache.dtype,
+          "caches: uint8 e4m3 with kv_scales, else bf16")
     tokens = qkv.shape[0]
-    _lib.call("q38_attn_prefill", qkv.data_ptr(), qkv.stride(0), q_norm_w.data_ptr(), k_norm_w.data_ptr(),
-              cos.data_ptr(), sin.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), slot, k_cache.shape[0],
-              k_cache.shape[2], tokens, start, out.data_ptr(), out.stride(0), num_q_heads, num_kv_heads, head_dim,
-              rot_dim, eps, workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream())
+    head = (qkv.data_ptr(), qkv.stride(0), q_norm_w.data_ptr(), k_norm_w.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+            k_cache.data_ptr(), v_cache.data_ptr())
+    tail = (slot, k_cache.shape[0], k_cache.shape[2], tokens, start, out.data_ptr(), out.stride(0), num_q_heads,
+            num_kv_heads, head_dim, rot_dim, eps, workspace.data_ptr(), workspace.numel() * workspace.element_size(),
+            _stream())
+    if fp8:
+        _lib.call("q38_attn_prefill_e4m3", *head, float(kv_scales[0]), float(kv_scales[1]), *tail)
+    else:
+        _lib.call("q38_attn_prefill", *head, *tail)
 
 
 def gdn_verify(qkvz, ab, conv_state, conv_weight, a_log, dt_bias, norm_weight, state, pending_key, pending_delta,
@@ -352,6 +362,37 @@ def lm_head_groupmax(x: torch.Tensor, lin: DeviceBF16Linear, maxima: torch.Tenso
     _need(maxima.dtype == torch.float32 and maxima.stride(1) == 1, "maxima fp32")
     _lib.call("q38_lm_head_groupmax", x.data_ptr(), rows, k, lin.w.data_ptr(), lin.out_features, group,
               maxima.data_ptr(), maxima.stride(0), _stream())
+
+
+KV_BF16, KV_E4M3 = 0, 1  # cache formats of attn_split
+
+
+def attn_split_workspace_bytes(batch: int, num_q_heads: int, num_kv_heads: int, tokens: int, max_seq: int,
+                               head_dim: int) -> int:
+    return _lib.load().q38_attn_split_workspace_bytes(batch, num_q_heads, num_kv_heads, tokens, max_seq, head_dim)
+
+
+def attn_split(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, position, active, out, *, batch: int, tokens: int,
+               num_q_heads: int, num_kv_heads: int, head_dim: int, rot_dim: int, eps: float,
+               kv_scales: tuple[float, float] | None = None, workspace: torch.Tensor | None = None) -> None:
+    """Decode (tokens = 1) or verify (tokens = K) attention split along the cache, for caches of any
+    length; `kv_scales` = (k_scale, v_scale) selects the FP8 e4m3 cache (uint8 k_cache / v_cache)."""
+    _cuda(qkv, q_norm_w, k_norm_w, cos, sin, k_cache, v_cache, position, active, out, workspace)
+    fp8 = kv_scales is not None
+    _need(k_cache.dtype == (U8 if fp8 else BF16) and v_cache.dtype == k_cache.dtype,
+          "caches: uint8 e4m3 with kv_scales, else bf16")
+    _need(k_cache.is_contiguous() and v_cache.is_contiguous(), "caches must be contiguous")
+    _need(cos.is_contiguous() and sin.is_contiguous() and cos.shape[-1] == rot_dim, "cos/sin [rows, rot] contiguous")
+    _need(position.dtype == torch.int32 and active.dtype == torch.float32, "position int32, active float32")
+    max_seq = k_cache.shape[2]
+    need = attn_split_workspace_bytes(batch, num_q_heads, num_kv_heads, tokens, max_seq, head_dim)
+    ws = workspace if workspace is not None else _workspace(qkv.device, need)
+    ks, vs = kv_scales if fp8 else (1.0, 1.0)
+    _lib.call("q38_attn_split", qkv.data_ptr(), qkv.stride(0), q_norm_w.data_ptr(), k_norm_w.data_ptr(), cos.data_ptr(),
+              sin.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), KV_E4M3 if fp8 else KV_BF16, float(ks), float(vs),
+              max_seq, position.data_ptr(), active.data_ptr(), out.data_ptr(), out.stride(0), batch, tokens,
+              num_q_heads, num_kv_heads, head_dim, rot_dim, eps, ws.data_ptr(), ws.numel() * ws.element_size(),
+              _stream())
 
 
 class StateRows:
