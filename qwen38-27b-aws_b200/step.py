@@ -62,6 +62,7 @@ class _Attn:
     o: ops.DeviceLinear
     k_cache: torch.Tensor
     v_cache: torch.Tensor
+    kv_scales: tuple[float, float] | None = None  # the FP8 e4m3 cache's static scales (None: a BF16 cache)
 
 
 @dataclass
@@ -84,9 +85,15 @@ class B200Step:
     def __init__(self, cfg: TextConfig, layer_weights, max_seq_len: int, batch_size: int, tp_degree: int = 1,
                  rank: int = 0, device: torch.device | str | None = None, saved_states: bool = False,
                  use_graph: bool = True, process_group=None, verify_tokens: int = 0, fused_allreduce: bool = True,
-                 max_chunk: int = 512):
+                 max_chunk: int = 512, kv_cache_format: str = "bf16", kv_scales=None):
         """`layer_weights(i)` returns layer i's unsharded weights (weights.synthetic_layer names), or
-        `layer_weights` is a dict holding them all."""
+        `layer_weights` is a dict holding them all. `kv_cache_format` "fp8" keeps the KV cache as FP8 e4m3
+        bytes with static per-layer scales (the reference's kv_cache_format, model.py:556-563): `kv_scales`
+        {layer index: (k_scale, v_scale)}, by default weights.synthetic_kv_scales."""
+        if kv_cache_format not in ("bf16", "fp8"):
+            raise ValueError(f"kv_cache_format must be bf16 or fp8, not {kv_cache_format!r}")
+        self.kv_fp8 = kv_cache_format == "fp8"
+        self.kv_scales = kv_scales
         cfg.validate_tp(tp_degree)
         self.cfg, self.tp, self.rank = cfg, tp_degree, rank
         self.max_seq, self.batch = max_seq_len, batch_size
@@ -137,13 +144,19 @@ class B200Step:
                                  torch.zeros(self.batch, K, conv_dim, dtype=BF16, device=dev))
         elif cfg.layer_types[i] == FULL:
             kvh = cfg.kv_heads_per_rank(self.tp)
+            scales = None
+            if self.kv_fp8:
+                scales = (self.kv_scales or {}).get(i) or W.synthetic_kv_scales(cfg, i)
+                scales = tuple(float(torch.tensor(float(v), dtype=BF16)) for v in scales)  # the bf16 parameters
+            cache_dtype = torch.uint8 if self.kv_fp8 else BF16
             mixer = _Attn(
                 qkv=lin("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj"),
                 q_norm=t("self_attn.q_norm_weight"),
                 k_norm=t("self_attn.k_norm_weight"),
                 o=lin("self_attn.o_proj"),
-                k_cache=torch.zeros(self.batch, kvh, self.max_seq, cfg.head_dim, dtype=BF16, device=dev),
-                v_cache=torch.zeros(self.batch, kvh, self.max_seq, cfg.head_dim, dtype=BF16, device=dev),
+                k_cache=torch.zeros(self.batch, kvh, self.max_seq, cfg.head_dim, dtype=cache_dtype, device=dev),
+                v_cache=torch.zeros(self.batch, kvh, self.max_seq, cfg.head_dim, dtype=cache_dtype, device=dev),
+                kv_scales=scales,
             )
         else:
             raise ValueError(cfg.layer_types[i])
@@ -165,6 +178,11 @@ class B200Step:
         cfg = self.cfg
         need = ops.gdn_decode_workspace_bytes(self.batch, cfg.linear_num_key_heads // self.tp, cfg.linear_key_head_dim)
         self.gdn_workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
+        # Attention split along the cache (long caches, the FP8 cache): one workspace for decode and verify.
+        heads, kvh = cfg.num_attention_heads // self.tp, cfg.kv_heads_per_rank(self.tp)
+        need = max(ops.attn_split_workspace_bytes(self.batch, heads, kvh, k, self.max_seq, cfg.head_dim)
+                   for k in {1, max(self.verify_tokens, 1)})
+        self.attn_workspace = torch.zeros(max(need, 256), dtype=torch.uint8, device=self.device)
 
     def _fill_acts(self, a, rows: int) -> None:
         """Activation buffers for `rows` token rows on `a` (the step itself for decode, a _Acts for a
@@ -230,7 +248,8 @@ class B200Step:
             self._layer(l, self)
 
     def _orders_rows(self) -> bool:
-        return any(l.kind == FULL for l in self.layers) and self.batch <= ops.ATTN_ORDER_MAX_ROWS
+        return (any(l.kind == FULL for l in self.layers) and self.batch <= ops.ATTN_ORDER_MAX_ROWS
+                and not self._split_attention(0))
 
     def run_layer(self, i: int) -> None:
         """Layer i alone, eagerly, on self.x and the loaded decode inputs (for layer-by-layer checks)."""
@@ -271,7 +290,11 @@ class B200Step:
             self._gemm(a, a.hq, m.qkv, a.proj)
             heads = dict(num_q_heads=cfg.num_attention_heads // tp, num_kv_heads=cfg.kv_heads_per_rank(tp),
                          head_dim=cfg.head_dim, rot_dim=cfg.rotary_dim, eps=eps)
-            if verify:
+            if chunk is None and self._split_attention(verify):
+                ops.attn_split(a.proj, m.q_norm, m.k_norm, a.cos, a.sin, m.k_cache, m.v_cache, a.position, a.active,
+                               a.mix_attn, batch=self.batch, tokens=max(verify, 1), kv_scales=m.kv_scales,
+                               workspace=self.attn_workspace, **heads)
+            elif verify:
                 ops.attn_verify(a.proj, m.q_norm, m.k_norm, a.cos, a.sin, m.k_cache, m.v_cache, a.position, a.active,
                                 a.mix_attn, batch=self.batch, tokens=verify, **heads)
             elif chunk is None:
@@ -280,11 +303,20 @@ class B200Step:
             else:
                 slot, start, _ = chunk
                 ops.attn_prefill(a.proj, m.q_norm, m.k_norm, a.cos, a.sin, m.k_cache, m.v_cache, a.mix_attn, a.attn_ws,
-                                 slot=slot, start=start, **heads)
+                                 slot=slot, start=start, kv_scales=m.kv_scales, **heads)
             self._row_parallel(a, a.mix_attn, m.o)
         ops.rmsnorm_quant(a.x, l.ln_post, eps, y_e5m2=a.hq)
         ops.fp8_gemm_silu(a.hq, l.gate_up, a.mlp_q)
         self._row_parallel(a, a.mlp_q, l.down)
+
+    # Caches up to these lengths fit the one-CTA-per-(row, KV head) decode and verify kernels, which keep
+    # every score of the row in shared memory; longer caches and the FP8 cache take the split kernels.
+    DECODE_KERNEL_MAX_SEQ = 4096
+    VERIFY_KERNEL_MAX_SEQ = 2048
+
+    def _split_attention(self, verify: int) -> bool:
+        limit = self.VERIFY_KERNEL_MAX_SEQ if verify else self.DECODE_KERNEL_MAX_SEQ
+        return self.kv_fp8 or self.max_seq > limit
 
     # ------------------------------------------------------------------ prefill
     def _chunk_acts(self, tokens: int):
@@ -371,8 +403,9 @@ class B200Step:
     def kernels_per_decode_step(self) -> int:
         """Launches of this library's kernels in one decode step (for the bench's gpu_launches)."""
         n = 1 if self._orders_rows() else 0  # the attention row order
+        attn = 6 if self._split_attention(0) else 4  # rmsnorm, qkv, attention (3 launches when split), o_proj
         for l in self.layers:
-            n += (6 if l.kind == LINEAR else 4) + 3  # GDN: rmsnorm, qkvz, ab, q/k prep, decode, out_proj; MLP: 3
+            n += (6 if l.kind == LINEAR else attn) + 3  # GDN: rmsnorm, qkvz, ab, q/k prep, decode, out_proj; MLP: 3
         return n
 
     def decode_device(self):

@@ -148,6 +148,15 @@ def synthetic_head(cfg: TextConfig, seed: int = 0, device="cpu", std: float = ST
     }
 
 
+def synthetic_kv_scales(cfg: TextConfig, index: int) -> tuple[float, float]:
+    """Static FP8 KV-cache scales (k_scale, v_scale) of attention layer `index` for synthetic weights:
+    powers of two that put normed keys (|k| up to ~5) and the values of N(0, 0.02) projections (|v| up
+    to ~7) inside e4m3's range of +-240, as a checkpoint's calibrated scales would."""
+    if cfg.layer_types[index] != FULL:
+        raise ValueError(f"layer {index} has no KV cache")
+    return 2.0 ** -4, 2.0 ** -5
+
+
 def embedding_rows(cfg: TextConfig, token_ids, seed: int = 0, std: float = STD) -> torch.Tensor:
     """Rows of a seeded N(0, std) embedding table ``[vocab, hidden]``, generated per token, bf16 on CPU."""
     rows = [_normal((cfg.hidden_size,), seed, f"embed.{int(t)}", "cpu", std) for t in token_ids]
