@@ -617,6 +617,50 @@ class OracleStep:
         return x + self.all_reduce(mlp(rms_norm(x, w_post, eps)))
 
 
+class OracleMTP:
+    """MTPStep's CPU branch (model.py:812-860) for one rank: the normed embedding of token t + 1 and the
+    twice-normed hidden state at t, joined and projected by fc, then one full-attention decoder layer in
+    its verify form over its own KV cache (prefill only writes that cache), the layer's norm divided by
+    (1 + the final norm's weight). With TP > 1, rank r takes fc's input columns r * 2H / tp .. (r + 1) *
+    2H / tp of the joined row (the reference's rank_gate split is this at tp = 2), summed by all_reduce."""
+
+    def __init__(self, cfg, weights: dict, max_seq_len: int, batch_size: int, tp_degree: int = 1, rank: int = 0,
+                 all_reduce=None, dtype=torch.bfloat16, kv_scales=None):
+        from dataclasses import replace
+
+        self.cfg, self.tp, self.rank = cfg, tp_degree, rank
+        self.all_reduce = all_reduce or (lambda t: t)
+        self.fc = linear_of(weights["fc"])
+        norm = lambda name: weights[name].cpu().to(dtype)  # noqa: E731
+        self.embedding_norm, self.hidden_norm = norm("embedding_norm_weight"), norm("hidden_norm_weight")
+        self.norm, self.final_norm = norm("norm_weight"), norm("final_norm_weight")
+        layer = {k: v for k, v in weights.items() if k.startswith("layers.")}
+        self.step = OracleStep(replace(cfg, layer_types=(FULL,)), layer, max_seq_len, batch_size, tp_degree, rank,
+                               self.all_reduce, dtype, kv_scales={0: kv_scales} if kv_scales else None)
+
+    @property
+    def attention(self):
+        return self.step.layers[0][1]
+
+    def __call__(self, hidden, inputs_embeds, cos, sin, position=None, active=None, slot=None, start=None, n_valid=None):
+        eps = self.cfg.rms_norm_eps
+        embedded = rms_norm(inputs_embeds, self.embedding_norm, eps)
+        state = rms_norm(rms_norm(hidden, self.final_norm, eps), self.hidden_norm, eps)
+        joined = torch.cat((embedded, state), dim=-1)
+        if self.tp > 1:
+            width = joined.shape[-1] // self.tp
+            joined = joined[..., self.rank * width:(self.rank + 1) * width]
+        x = self.all_reduce(self.fc(joined))
+        if slot is not None:
+            # cache_chunk (model.py:855-856, :795-800): only the layer's keys and values are kept.
+            _, mixer, _, w_in, _ = self.step.layers[0]
+            mixer.prefill(rms_norm(x, w_in, eps), cos, sin, slot, start, n_valid)
+            return x[:, :1]
+        x = self.step.layer(0, x, cos, sin, position, active, accepted=active)
+        out = rms_norm(x, self.norm, eps)
+        return (out.float() / (1.0 + self.final_norm.float())).to(x.dtype)
+
+
 # ---------------------------------------------------------------------------------------------
 # Head (model.py:863-900, generate.py:186-208)
 # ---------------------------------------------------------------------------------------------

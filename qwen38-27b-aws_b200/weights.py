@@ -15,7 +15,7 @@ tensor from its own generator so any one layer can be regenerated alone, on CPU 
 from __future__ import annotations
 
 import hashlib
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 
 import torch
 
@@ -146,6 +146,36 @@ def synthetic_head(cfg: TextConfig, seed: int = 0, device="cpu", std: float = ST
         "norm_weight": _bf16((cfg.hidden_size,), seed, "model.norm", device, std),
         "lm_head": _fp8((cfg.vocab_size, cfg.hidden_size), seed, "lm_head", device, std),
     }
+
+
+MTP_SEED_OFFSET = 7919  # the MTP layer's tensors draw from their own seeds
+
+
+def synthetic_mtp(cfg: TextConfig, seed: int = 0, device="cpu", std: float = STD) -> dict:
+    """The MTP draft layer's weights (MTPStep, qwen38_inf2/model.py:812-860; checkpoint.mtp_weights
+    :363-393 names): fc [hidden, 2 hidden] over [normed embedding | normed hidden state], the four norms
+    (final_norm_weight is the model's final norm, the head's norm_weight) and one full-attention decoder
+    layer under `layers.0.`."""
+    h = cfg.hidden_size
+    layer_cfg = replace(cfg, layer_types=(FULL,))
+    out = {
+        "fc": _fp8((h, 2 * h), seed, "mtp.fc", device, std),
+        "embedding_norm_weight": _bf16((h,), seed, "mtp.pre_fc_norm_embedding", device, std),
+        "hidden_norm_weight": _bf16((h,), seed, "mtp.pre_fc_norm_hidden", device, std),
+        "norm_weight": _bf16((h,), seed, "mtp.norm", device, std),
+        "final_norm_weight": _bf16((h,), seed, "model.norm", device, std),
+    }
+    return out | synthetic_layer(layer_cfg, 0, seed + MTP_SEED_OFFSET, device, std)
+
+
+def shard_mtp(cfg: TextConfig, weights: dict, rank: int, tp: int) -> dict:
+    """One rank's share of the MTP layer: fc by input columns in `tp` equal slices of [embedding | hidden]
+    (any TP degree; the reference's rank_gate split, model.py:835-850, holds only for 2), the decoder layer
+    as any full-attention layer."""
+    layer_cfg = replace(cfg, layer_types=(FULL,))
+    out = {k: v for k, v in weights.items() if not k.startswith("layers.") and k != "fc"}
+    out["fc"] = _cols(weights["fc"], rank, tp) if tp > 1 else weights["fc"]
+    return out | shard_layer(layer_cfg, weights, 0, rank, tp)
 
 
 def synthetic_kv_scales(cfg: TextConfig, index: int) -> tuple[float, float]:

@@ -179,6 +179,51 @@ def fp8_cache_goldens(rconfig, rmodel, rgen, ours, weights):
     return tensors
 
 
+MTP_TOKENS = 4
+
+
+def mtp_goldens(rconfig, rmodel, rgen, ours):
+    """The MTP draft layer (MTPStep, model.py:812-860) with synthetic weights: a prompt chunk into slot 1
+    (which only fills its cache), then two steps of MTP_TOKENS tokens per row from each row's MTP index,
+    the second feeding its own outputs back, into tiny_mtp.safetensors."""
+    ref_cfg = replace(rconfig.tiny_config(num_blocks=1), weight_format="fp8", recurrent_state_format="bf16",
+                      kv_cache_format="bf16")
+    weights = pkg.weights.synthetic_mtp(ours, SEED, "cpu", STD)
+    mtp = rmodel.MTPStep(ref_cfg, 1, MAX_SEQ, torch.bfloat16, rmodel.identity_all_reduce, BATCH).eval()
+    plain = {}
+    for name, t in weights.items():
+        ref_name = ("layer." + name[len("layers.0."):]) if name.startswith("layers.0.") else name
+        if isinstance(t, pkg.weights.FP8Weight):
+            mtp.get_submodule(ref_name)._b200_weight = t.dequant()
+        else:
+            plain[ref_name] = t
+    missing, unexpected = mtp.load_state_dict(plain, strict=False)
+    assert not unexpected, unexpected
+    assert all(n.endswith(("weight_fp8", "_cache")) for n in missing), missing
+    tensors = {}
+    gen = torch.Generator().manual_seed(SEED + 3)
+    with torch.no_grad():
+        hidden = torch.randn(1, CHUNK, ours.hidden_size, generator=gen).to(torch.bfloat16)
+        embeds = torch.randn(1, CHUNK, ours.hidden_size, generator=gen).to(torch.bfloat16)
+        inputs = rgen.mtp_prefill_inputs(ref_cfg, 1, 0, CHUNK, CHUNK, torch.bfloat16)
+        tensors.update({"prefill.hidden": hidden, "prefill.x": embeds} | {f"prefill.{k}": v for k, v in inputs.items()})
+        tensors["prefill.y"] = mtp(hidden=hidden, inputs_embeds=embeds, **inputs)
+        hidden = torch.randn(BATCH, MTP_TOKENS, ours.hidden_size, generator=gen).to(torch.bfloat16)
+        for step, (indices, active) in enumerate([([3, CHUNK, 7], [True, True, False]), ([4, CHUNK + 2, 1], [True, True, True])]):
+            embeds = torch.randn(BATCH, MTP_TOKENS, ours.hidden_size, generator=gen).to(torch.bfloat16)
+            inputs = rgen.mtp_step_inputs(ref_cfg, indices, MTP_TOKENS, MAX_SEQ, torch.bfloat16, active)
+            tensors.update({f"step{step}.hidden": hidden, f"step{step}.x": embeds} | {f"step{step}.{k}": v for k, v in inputs.items()})
+            hidden = mtp(hidden=hidden, inputs_embeds=embeds, **inputs)
+            tensors[f"step{step}.y"] = hidden.clone()
+        tensors["state.k_cache"] = mtp.layer.self_attn.k_cache.clone()
+        tensors["state.v_cache"] = mtp.layer.self_attn.v_cache.clone()
+    meta = {"seed": str(SEED), "std": str(STD), "batch": str(BATCH), "max_seq": str(MAX_SEQ), "chunk": str(CHUNK),
+            "tokens": str(MTP_TOKENS), "steps": "2", "weights_sha256": weights_digest(weights),
+            "generator": "tests/golden/make_golden.py"}
+    save_file({k: v.contiguous() for k, v in tensors.items()}, str(HERE / "tiny_mtp.safetensors"), metadata=meta)
+    print(f"{len(tensors)} tensors, {(HERE / 'tiny_mtp.safetensors').stat().st_size} bytes")
+
+
 FULL_BATCH = 8
 FULL_MAX_SEQ = 512
 FULL_STATE_SEED = 1
@@ -365,6 +410,7 @@ def main():
     print(json.dumps(meta, indent=1))
     print(f"{len(tensors)} tensors, {(HERE / 'tiny_block.safetensors').stat().st_size} bytes")
 
+    mtp_goldens(rconfig, rmodel, rgen, ours)
     ftensors = fp8_cache_goldens(rconfig, rmodel, rgen, ours, weights)
     fmeta = dict(meta, k_scale=str(FP8_SCALES[0]), v_scale=str(FP8_SCALES[1]), verify_tokens=str(VERIFY))
     del fmeta["decode_steps"]

@@ -224,3 +224,33 @@ def test_oracle_reproduces_full_width_reference_steps_and_head(pkg):
         assert tokens == tensors[f"step{s}.tokens_out"].tolist()
         if s + 1 < int(meta["steps"]):
             assert tokens == tensors[f"step{s + 1}.tokens_in"].tolist()
+
+
+MTP_GOLDEN = Path(__file__).resolve().parent / "golden" / "tiny_mtp.safetensors"
+
+
+def _mtp_calls(tensors):
+    return ["prefill"] + [f"step{s}" for s in range(sum(1 for k in tensors if k.startswith("step") and k.endswith(".y")))]
+
+
+def test_oracle_reproduces_reference_mtp_layer(pkg):
+    """The MTP draft layer (MTPStep), made by the reference: a prompt chunk (cache only), then two steps of
+    4 tokens per row (the second on the first's outputs), each output and the layer's final KV cache."""
+    with safe_open(str(MTP_GOLDEN), "pt") as f:
+        tensors, meta = {k: f.get_tensor(k) for k in f.keys()}, f.metadata()
+    cfg = pkg.config.tiny_config(num_blocks=1)
+    weights = pkg.weights.synthetic_mtp(cfg, int(meta["seed"]), "cpu", float(meta["std"]))
+    assert _digest(pkg, weights) == meta["weights_sha256"]
+    mtp = om.OracleMTP(cfg, weights, int(meta["max_seq"]), int(meta["batch"]))
+    for name in _mtp_calls(tensors):
+        keys = ("cos", "sin", "position", "active", "slot", "start", "n_valid")
+        inputs = {k: tensors[f"{name}.{k}"] for k in keys if f"{name}.{k}" in tensors}
+        y = mtp(hidden=tensors[f"{name}.hidden"], inputs_embeds=tensors[f"{name}.x"], **inputs)
+        want = tensors[f"{name}.y"]
+        if "active" in inputs:
+            on = inputs["active"] > 0.5
+            y, want = y[on], want[on]
+        assert torch.equal(y, want), f"{name}: oracle differs from the reference"
+    tail = max(int(meta["tokens"]), int(meta["chunk"]))  # the junk positions of idle rows and of prefill's other rows
+    assert torch.equal(mtp.attention.k_cache[:, :, :-tail], tensors["state.k_cache"][:, :, :-tail])
+    assert torch.equal(mtp.attention.v_cache[:, :, :-tail], tensors["state.v_cache"][:, :, :-tail])
