@@ -120,6 +120,15 @@ int q38_rmsnorm_quant(const void* x, int64_t ldx, const void* w, int64_t rows, i
                       int64_t ldy, void* y_e5m2, int64_t ldq, q38_stream_t stream);
 
 /*
+ * y = bf16(bf16(rms_norm(x) * (1 + w)) / (1 + w_div)) for each of `rows` rows of n values (x, y bf16
+ * with row strides ldx, ldy; w, w_div bf16 [n]): the MTP draft layer's output, its norm divided by the
+ * model's final-norm weight (1 + w_div) so the head's final norm recovers it (MTPStep.forward,
+ * qwen38_inf2/model.py:858-860).
+ */
+int q38_rmsnorm_divide(const void* x, int64_t ldx, const void* w, const void* w_div, int64_t rows, int64_t n, float eps,
+                       void* y, int64_t ldy, q38_stream_t stream);
+
+/*
  * MLP middle: h = e5m2(bf16(bf16(silu(g)) * u)) with g, u the bf16 gate and up projections
  * [rows, n] at gu and gu + n (row stride ld). Replaces silu(gate_proj(x)) * up_proj(x)
  * (qwen38_inf2/model.py:48-51, :259) and the NKI mlp_up epilogue (kernels.py:74-118).

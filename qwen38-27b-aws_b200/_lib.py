@@ -36,6 +36,9 @@ SIGNATURES = {
     "q38_rmsnorm_quant": (
         c_int, [c_void_p, c_int64, c_void_p, c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p, c_int64, c_void_p]
     ),
+    "q38_rmsnorm_divide": (
+        c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p, c_int64, c_void_p]
+    ),
     "q38_silu_mul_quant": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p]),
     "q38_weight_tile_bytes": (c_size_t, [c_int64, c_int64]),
     "q38_bf16_linear": (

@@ -1,5 +1,6 @@
 // Element-wise and row kernels around the FP8 GEMMs, each rounding where the reference rounds:
 //   q38_rmsnorm_quant      rms_norm (model.py:54-57) -> bf16, and e5m2 for the next FP8 linear
+//   q38_rmsnorm_divide     rms_norm, then divided by (1 + w_div): the MTP layer's output (model.py:858-860)
 //   q38_silu_mul_quant     silu(gate) * up in bf16 steps (model.py:48-51, :259) -> e5m2
 // All are HBM-bound; rows are read with 16-byte vector loads.
 #include "q38_common.cuh"
@@ -203,4 +204,50 @@ extern "C" int q38_silu_mul_quant(const void* gu, int64_t ld, int64_t rows, int6
       static_cast<const __nv_bfloat16*>(gu), ld, static_cast<int>(rows), static_cast<int>(n),
       static_cast<uint8_t*>(y_e5m2), ldy);
   return cuda_status(cudaGetLastError(), "silu_mul_quant launch");
+}
+
+// y = bf16(bf16(rms_norm(x) * (1 + w)) / (1 + w_div)) per row: MTPStep's output, its own norm divided by
+// (1 + the final norm's weight) in fp32 (qwen38_inf2/model.py:858-860), so the head's final norm recovers
+// what the layer predicts.
+namespace {
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_divide_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                                      const __nv_bfloat16* __restrict__ w,
+                                                                      const __nv_bfloat16* __restrict__ w_div, int n,
+                                                                      float eps, __nv_bfloat16* __restrict__ y,
+                                                                      int64_t ldy) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t row = blockIdx.x;
+  const __nv_bfloat16* xr = x + row * ldx;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += kNormThreads) {
+    const float f = __bfloat162float(xr[i]);
+    ss += f * f;
+  }
+  __shared__ float red[kNormThreads / 32];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float total = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) total += red[i];
+  const float r = 1.0f / sqrtf(total / static_cast<float>(n) + eps);
+  for (int i = threadIdx.x; i < n; i += kNormThreads) {
+    const float h = bf16r(__fmul_rn(__fmul_rn(__bfloat162float(xr[i]), r), __fadd_rn(1.0f, __bfloat162float(w[i]))));
+    y[row * ldy + i] = __float2bfloat16_rn(__fdiv_rn(h, __fadd_rn(1.0f, __bfloat162float(w_div[i]))));
+  }
+}
+}  // namespace
+
+extern "C" int q38_rmsnorm_divide(const void* x, int64_t ldx, const void* w, const void* w_div, int64_t rows, int64_t n,
+                                  float eps, void* y, int64_t ldy, q38_stream_t stream) {
+  using namespace q38host;
+  if (!x || !w || !w_div || !y) return set_error("q38_rmsnorm_divide: null pointer"), Q38_ERR_ARG;
+  if (rows <= 0 || rows > (1 << 30) || n <= 0 || n > (1 << 20) || ldx < n || ldy < n)
+    return set_error("q38_rmsnorm_divide: bad sizes"), Q38_ERR_ARG;
+  const cudaError_t e = launch_pdl(rmsnorm_divide_kernel, dim3(static_cast<unsigned>(rows)), dim3(kNormThreads), 0,
+                                   static_cast<cudaStream_t>(stream), static_cast<const __nv_bfloat16*>(x), ldx,
+                                   static_cast<const __nv_bfloat16*>(w), static_cast<const __nv_bfloat16*>(w_div),
+                                   static_cast<int>(n), eps, static_cast<__nv_bfloat16*>(y), ldy);
+  return cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "rmsnorm_divide launch");
 }

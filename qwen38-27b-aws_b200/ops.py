@@ -175,6 +175,16 @@ def rmsnorm_quant(x: torch.Tensor, w: torch.Tensor, eps: float, y_bf16: torch.Te
               _stream())
 
 
+def rmsnorm_divide(x: torch.Tensor, w: torch.Tensor, w_div: torch.Tensor, eps: float, y: torch.Tensor) -> None:
+    """y = bf16(bf16(rms_norm(x) * (1 + w)) / (1 + w_div)) per row (the MTP layer's output)."""
+    _cuda(x, w, w_div, y)
+    rows, n = x.shape
+    _need(x.dtype == BF16 and y.dtype == BF16 and w.numel() == n and w_div.numel() == n and x.stride(1) == 1
+          and y.stride(1) == 1, "rmsnorm_divide: bf16 x, y [rows, n], w, w_div [n]")
+    _lib.call("q38_rmsnorm_divide", x.data_ptr(), x.stride(0), w.data_ptr(), w_div.data_ptr(), rows, n, eps, y.data_ptr(),
+              y.stride(0), _stream())
+
+
 def silu_mul_quant(gu: torch.Tensor, n: int, y_e5m2: torch.Tensor) -> None:
     _cuda(gu, y_e5m2)
     rows = gu.shape[0]

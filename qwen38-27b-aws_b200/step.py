@@ -30,7 +30,7 @@ arithmetic is the C-ABI kernels (ops.py) or it fails.
 
 from __future__ import annotations
 
-from dataclasses import dataclass
+from dataclasses import dataclass, replace
 
 import torch
 
@@ -359,6 +359,22 @@ class B200Step:
         a.sin.copy_(sin.reshape(tokens, -1), non_blocking=True)
         return a
 
+    def cache_chunk(self, i: int, x: torch.Tensor, cos, sin, slot: int, start: int) -> None:
+        """FullAttentionStep.cache_chunk (model.py:795-800) for attention layer i: the chunk's keys and
+        values into the slot's cache from the layer input x [C, H] on the device (its norm, qkv projection
+        and rotary; the attention output is computed and dropped)."""
+        l = self.layers[i]
+        if l.kind != FULL:
+            raise ValueError(f"layer {i} has no KV cache")
+        a = self._load_chunk(x.reshape(1, x.shape[0], -1), cos, sin)
+        cfg, m = self.cfg, l.mixer
+        ops.rmsnorm_quant(a.x, l.ln_in, cfg.rms_norm_eps, y_e5m2=a.hq)
+        self._gemm(a, a.hq, m.qkv, a.proj)
+        ops.attn_prefill(a.proj, m.q_norm, m.k_norm, a.cos, a.sin, m.k_cache, m.v_cache, a.mix_attn, a.attn_ws, slot=slot,
+                         start=start, num_q_heads=cfg.num_attention_heads // self.tp,
+                         num_kv_heads=cfg.kv_heads_per_rank(self.tp), head_dim=cfg.head_dim, rot_dim=cfg.rotary_dim,
+                         eps=cfg.rms_norm_eps, kv_scales=m.kv_scales)
+
     def run_prefill_layer(self, i: int, embeds, cos, sin, slot: int, start: int, n_valid: int) -> torch.Tensor:
         """Layer i alone on a prefill chunk whose input is `embeds` [1, C, H] (for layer-by-layer checks)."""
         a = self._load_chunk(embeds, cos, sin)
@@ -532,3 +548,90 @@ class B200Head:
             raise ValueError(f"the head graph takes {self.batch} rows, got {rows}")
         self.hidden.copy_(hidden.reshape(rows, -1), non_blocking=True)
         return _to_host(self.maxima_device())
+
+
+class B200MTP:
+    """The MTP draft layer (MTPStep, qwen38_inf2/model.py:812-860) of one rank, called as the reference's
+    MTP graph: `mtp(hidden=..., inputs_embeds=..., **generate.mtp_step_inputs(...))` for K tokens per row
+    (Scheduler._mtp_drafts, scheduler.py:160-193), or with `generate.mtp_prefill_inputs` for a prompt
+    chunk of one row, which only fills the layer's cache (Scheduler._mtp_prefill, scheduler.py:145-158).
+    Host tensors in, host tensors out.
+
+    fc's input [normed embedding | twice-normed hidden state] is cut by columns into tp equal slices:
+    rank r multiplies its slice, and the partial products are summed across ranks by the fused GEMM +
+    all-reduce (at tp = 2 this is the reference's rank_gate split; it holds for any tp). The decoder layer
+    is a one-layer B200Step in its verify form: each token against the layer's cache before its position
+    and its step's own tokens up to itself. The output is the layer's norm divided by (1 + the final
+    norm's weight), one kernel (q38_rmsnorm_divide)."""
+
+    def __init__(self, cfg: TextConfig, mtp_weights: dict, max_seq_len: int, batch_size: int, tokens: int = 4,
+                 tp_degree: int = 1, rank: int = 0, device=None, process_group=None, fused_allreduce: bool = True,
+                 max_chunk: int = 512, kv_cache_format: str = "bf16", kv_scales=None):
+        self.cfg, self.tp, self.rank, self.batch, self.tokens = cfg, tp_degree, rank, batch_size, tokens
+        self.device = torch.device(device or f"cuda:{torch.cuda.current_device()}")
+        self.group = process_group
+        layer_w = {k: v for k, v in mtp_weights.items() if k.startswith("layers.")}
+        self.layer = B200Step(replace(cfg, layer_types=(FULL,)), layer_w, max_seq_len, batch_size, tp_degree, rank,
+                              self.device, use_graph=False, process_group=process_group, verify_tokens=tokens,
+                              fused_allreduce=fused_allreduce, max_chunk=max_chunk, kv_cache_format=kv_cache_format,
+                              kv_scales={0: kv_scales} if kv_scales else None)
+        shard = W.shard_mtp(cfg, mtp_weights, rank, tp_degree)
+        H = cfg.hidden_size
+        rows = max(batch_size * tokens, max_chunk)
+        dev = self.device
+        with torch.cuda.device(dev):
+            self.fc = ops.DeviceLinear(shard["fc"], dev)
+            vec = lambda name: shard[name].to(dev, BF16).contiguous()  # noqa: E731
+            self.embedding_norm, self.hidden_norm = vec("embedding_norm_weight"), vec("hidden_norm_weight")
+            self.norm, self.final_norm = vec("norm_weight"), vec("final_norm_weight")
+            z = lambda *sh, dt=BF16: torch.zeros(*sh, dtype=dt, device=dev)  # noqa: E731
+            self.emb, self.hid, self.tmp, self.out = z(rows, H), z(rows, H), z(rows, H), z(rows, H)
+            self.x = z(rows, H)
+            self.joined = z(rows, 2 * H, dt=torch.uint8)  # e5m2 of [normed embedding | normed hidden]
+            self.fc_in = z(rows, 2 * H // tp_degree, dt=torch.uint8) if tp_degree > 1 else None
+            self.fc_ws = z(max(256, max(ops.gemm_workspace_bytes(r, H, 8) for r in (batch_size * tokens, max_chunk))),
+                           dt=torch.uint8)
+
+    def _project(self, rows: int) -> torch.Tensor:
+        """x = all_reduce(fc(e5m2([rms(embedding) | rms(rms(hidden, final), hidden)]))) [rows, H] on the device."""
+        cfg, H, eps = self.cfg, self.cfg.hidden_size, self.cfg.rms_norm_eps
+        ops.rmsnorm_quant(self.emb[:rows], self.embedding_norm, eps, y_e5m2=self.joined[:rows, :H])
+        ops.rmsnorm_quant(self.hid[:rows], self.final_norm, eps, y_bf16=self.tmp[:rows])
+        ops.rmsnorm_quant(self.tmp[:rows], self.hidden_norm, eps, y_e5m2=self.joined[:rows, H:])
+        splits = ops.choose_splits(rows, H, self.fc.in_features)
+        if self.tp == 1:
+            ops.fp8_gemm(self.joined[:rows], self.fc, self.x[:rows], splits=splits, workspace=self.fc_ws)
+            return self.x[:rows]
+        width = 2 * H // self.tp
+        self.fc_in[:rows].copy_(self.joined[:rows, self.rank * width:(self.rank + 1) * width])
+        comm = self.layer.comm
+        if comm is not None:
+            comm.x[:rows].zero_()  # the fused projection adds into the residual stream
+            ops.fp8_gemm_allreduce(self.fc_in[:rows], self.fc, comm, splits=min(splits, 8))
+            return comm.x[:rows]
+        ops.fp8_gemm(self.fc_in[:rows], self.fc, self.x[:rows], splits=splits, workspace=self.fc_ws)
+        torch.distributed.all_reduce(self.x[:rows], group=self.group)
+        return self.x[:rows]
+
+    def __call__(self, hidden: torch.Tensor, inputs_embeds: torch.Tensor, cos, sin, position=None, active=None,
+                 slot=None, start=None, n_valid=None) -> torch.Tensor:
+        H = self.cfg.hidden_size
+        rows = inputs_embeds.shape[0] * inputs_embeds.shape[1]
+        with torch.cuda.device(self.device):
+            self.emb[:rows].copy_(inputs_embeds.reshape(rows, H), non_blocking=True)
+            self.hid[:rows].copy_(hidden.reshape(rows, H), non_blocking=True)
+            x = self._project(rows)
+            if slot is not None:
+                # Prefill only fills the layer's cache; the reference returns the projection's first row.
+                scalar = lambda v: int(v.reshape(-1)[0])  # noqa: E731
+                self.layer.cache_chunk(0, x, cos, sin, scalar(slot), scalar(start))
+                return _to_host(x[:1]).reshape(1, 1, H)
+            B, K = inputs_embeds.shape[:2]
+            if (B, K) != (self.batch, self.tokens):
+                raise ValueError(f"MTP steps take [{self.batch}, {self.tokens}, hidden], got {tuple(inputs_embeds.shape)}")
+            y = self.layer.verify(x.reshape(B, K, H), cos, sin, position, active, torch.zeros(B, dtype=torch.int32))
+            ops.rmsnorm_divide(y, self.norm, self.final_norm, self.cfg.rms_norm_eps, self.out[:rows])
+            return _to_host(self.out[:rows]).reshape(B, K, H)
+
+    def close(self) -> None:
+        self.layer.close()
