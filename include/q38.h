@@ -398,6 +398,27 @@ int q38_copy_state_rows(void* const* buffers, const int64_t* row_bytes, const in
 int q38_lm_head_groupmax(const void* x, int64_t rows, int64_t k, const void* w, int64_t vocab, int group,
                          float* maxima, int64_t ld_max, q38_stream_t stream);
 
+/*
+ * The head's exact recheck on the device (ChipHead.next_tokens, qwen38_inf2/generate.py:186-208): for each
+ * of `rows` rows, the `candidates` groups with the largest `maxima` (float [rows, ldm], `groups` groups of
+ * 32 over the whole vocabulary; ties to the lower group), each of their 32 vocabulary rows scored in fp32
+ * against rms_norm(hidden.float(), norm_w) (hidden bf16 [rows, ldh], norm_w bf16 [hidden_size]), and the
+ * best token: the largest logit in a group (its first row on ties), groups taken in candidate order, a
+ * strictly larger logit replacing the best. lm_head is this rank's vocabulary rows [vocab_first,
+ * vocab_first + vocab_rows) in the tiled BF16 layout of q38_lm_head_groupmax; candidate groups outside
+ * them score -inf with token -1. Outputs: tokens int32 [rows] (-1 where no logit is finite), and/or the
+ * per-candidate slot_logits float / slot_tokens int32 [rows, candidates] for combining ranks (a max across
+ * ranks, then q38_lm_head_pick). group must be 32, candidates 1..8.
+ */
+int q38_lm_head_recheck(const void* hidden, int64_t ldh, const void* norm_w, float eps, const float* maxima,
+                        int64_t ldm, int64_t groups, const void* lm_head, int64_t vocab_first, int64_t vocab_rows,
+                        int64_t hidden_size, int group, int candidates, int64_t rows, float* slot_logits,
+                        int32_t* slot_tokens, int32_t* tokens, q38_stream_t stream);
+/* tokens[r] from the per-candidate results of q38_lm_head_recheck (maximised across ranks): the candidate
+ * slots in order, a strictly larger logit replacing the best so far; -1 where none is valid. */
+int q38_lm_head_pick(const float* slot_logits, const int32_t* slot_tokens, int candidates, int64_t rows, int32_t* tokens,
+                     q38_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -106,6 +106,12 @@ SIGNATURES = {
          c_int64, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int, c_float, c_void_p,
          c_size_t, c_void_p],
     ),
+    "q38_lm_head_recheck": (
+        c_int,
+        [c_void_p, c_int64, c_void_p, c_float, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int,
+         c_int, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
+    ),
+    "q38_lm_head_pick": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_void_p, c_void_p]),
     "q38_copy_state_rows": (
         c_int, [ctypes.POINTER(c_void_p), ctypes.POINTER(c_int64), ctypes.POINTER(c_int64), c_int, c_int64, c_int64,
                 c_void_p]

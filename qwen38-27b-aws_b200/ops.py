@@ -424,5 +424,26 @@ class StateRows:
                   _stream())
 
 
+def lm_head_recheck(hidden: torch.Tensor, norm_w: torch.Tensor, eps: float, maxima: torch.Tensor, lin: DeviceBF16Linear,
+                    vocab_first: int, candidates: int, tokens: torch.Tensor | None = None,
+                    slot_logits: torch.Tensor | None = None, slot_tokens: torch.Tensor | None = None) -> None:
+    """ChipHead.next_tokens' exact recheck on the device: tokens int32 [rows], and/or per-candidate slots."""
+    _cuda(hidden, norm_w, maxima, tokens, slot_logits, slot_tokens)
+    rows, h = hidden.shape
+    _need(hidden.dtype == BF16 and hidden.stride(1) == 1 and h == lin.in_features, "hidden bf16 [rows, hidden]")
+    _need(maxima.dtype == torch.float32 and maxima.stride(1) == 1 and maxima.shape[0] >= rows, "maxima fp32 [rows, groups]")
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    _lib.call("q38_lm_head_recheck", hidden.data_ptr(), hidden.stride(0), norm_w.data_ptr(), eps, maxima.data_ptr(),
+              maxima.stride(0), maxima.shape[1], lin.w.data_ptr(), vocab_first, lin.out_features, h, 32, candidates, rows,
+              ptr(slot_logits), ptr(slot_tokens), ptr(tokens), _stream())
+
+
+def lm_head_pick(slot_logits: torch.Tensor, slot_tokens: torch.Tensor, tokens: torch.Tensor) -> None:
+    _cuda(slot_logits, slot_tokens, tokens)
+    rows, candidates = slot_logits.shape
+    _lib.call("q38_lm_head_pick", slot_logits.data_ptr(), slot_tokens.data_ptr(), candidates, rows, tokens.data_ptr(),
+              _stream())
+
+
 def device_status(reset: bool = True) -> int:
     return _lib.load().q38_device_status(1 if reset else 0)

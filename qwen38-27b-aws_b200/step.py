@@ -533,6 +533,7 @@ class B200Head:
         self.maxima = torch.zeros(batch_size, self.vocab_local // 32, dtype=torch.float32, device=self.device)
         self.gathered = (torch.zeros(tp_degree, batch_size, self.vocab_local // 32, dtype=torch.float32, device=self.device)
                          if tp_degree > 1 else None)
+        self._tokens = None  # next_tokens' device buffers, made on first use
 
     def maxima_device(self) -> torch.Tensor:
         ops.rmsnorm_quant(self.hidden, self.norm_w, self.cfg.rms_norm_eps, y_bf16=self.xb)
@@ -541,6 +542,41 @@ class B200Head:
             return self.maxima
         torch.distributed.all_gather_into_tensor(self.gathered, self.maxima, group=self.group)
         return self.gathered.permute(1, 0, 2).reshape(self.batch, -1)
+
+    def next_tokens(self, hidden: torch.Tensor, recheck_groups: int | None = None) -> list[int]:
+        """ChipHead.next_tokens (generate.py:186-208) with its exact recheck on the device: hidden [rows, 1, H]
+        (rows <= batch, padded like the reference) -> the greedy token of each row. The maxima stay on the
+        GPU; only the token ids come back. `recheck_groups` (default 4) is how many of the best groups are
+        rescored, as ChipHead's argument of that name."""
+        rows = hidden.shape[0]
+        if rows > self.batch:
+            raise ValueError(f"the head takes at most {self.batch} rows, got {rows}")
+        k = recheck_groups or 4
+        with torch.cuda.device(self.device):
+            if self._tokens is None:
+                z = lambda *sh, dt: torch.zeros(*sh, dtype=dt, device=self.device)  # noqa: E731
+                self._tokens = z(self.batch, dt=torch.int32)
+                self._slot_logits = z(self.batch, 8, dt=torch.float32)
+                self._slot_tokens = z(self.batch, 8, dt=torch.int32)
+            self.hidden.zero_()
+            self.hidden[:rows].copy_(hidden.reshape(rows, -1), non_blocking=True)
+            maxima = self.maxima_device()
+            eps = self.cfg.rms_norm_eps
+            if self.tp == 1:
+                ops.lm_head_recheck(self.hidden, self.norm_w, eps, maxima, self.lm_head, 0, k, tokens=self._tokens)
+            else:
+                logits, toks = self._slot_logits[:, :k], self._slot_tokens[:, :k]
+                ops.lm_head_recheck(self.hidden, self.norm_w, eps, maxima, self.lm_head, self.rank * self.vocab_local, k,
+                                    slot_logits=logits, slot_tokens=toks)
+                # Each candidate slot is scored on the one rank holding its group; -inf / -1 elsewhere.
+                torch.distributed.all_reduce(logits, op=torch.distributed.ReduceOp.MAX, group=self.group)
+                torch.distributed.all_reduce(toks, op=torch.distributed.ReduceOp.MAX, group=self.group)
+                ops.lm_head_pick(logits, toks, self._tokens)
+            tokens = _to_host(self._tokens[:rows]).tolist()
+        for row, t in enumerate(tokens):
+            if t < 0:
+                raise FloatingPointError(f"row {row}'s logits are not finite, so the graph produced NaN or infinity")
+        return tokens
 
     def run_graph(self, hidden: torch.Tensor) -> torch.Tensor:
         rows = hidden.shape[0]

@@ -14,7 +14,9 @@ ChipHead tokens. Checks per step:
   reference's own arithmetic moves under reordering (every FP8 linear rounds its input to e5m2, so one
   bf16 ulp upstream can move a whole e5m2 step); B200Step must stay within 3x that spread of the
   reference, and within 2e-2 wherever the spread is smaller.
-* Greedy tokens end to end (B200Step, B200Head.run_graph, the reference's recheck): identical to the
+* B200Head.next_tokens (the recheck on the device) gives the same tokens as the host recheck on the
+  same maxima, and the reference's tokens on the reference's hidden state.
+* Greedy tokens end to end (B200Step, B200Head.next_tokens): identical to the
   reference's, except where the reference's best two candidates are a near tie under the measured
   spread (their logit gap below 3x the largest move of either logit under reordering). Step 1 takes the
   reference's tokens (teacher forcing), so one differing row cannot change the others.
@@ -72,6 +74,7 @@ def test_full_width_greedy_tokens_top4_and_hidden_match_reference(pkg, fixture):
         same_values = (want_max.gather(1, top4) - want_max.gather(1, want_top4)).abs() <= 1e-6 * peak
         assert same_values.all(), f"step {s}: top-4 groups {top4.tolist()} vs the reference's {want_top4.tolist()}"
         assert om.recheck_tokens(cfg, y_ref, norm_w, lm_rows, got_max) == want_tokens, f"step {s}: head tokens"
+        assert bhead.next_tokens(y_ref) == want_tokens, f"step {s}: the device recheck's tokens"
 
         # The hidden state, against the measured reordering spread.
         y_gpu = step(inputs_embeds=x, **inputs)
@@ -81,7 +84,8 @@ def test_full_width_greedy_tokens_top4_and_hidden_match_reference(pkg, fixture):
         assert (err <= bound).all(), f"step {s}: relative L2 per row {err.tolist()}, reordering spread {spread.tolist()}"
 
         # Greedy tokens end to end.
-        got_tokens = om.recheck_tokens(cfg, y_gpu, norm_w, lm_rows, bhead.run_graph(y_gpu))
+        got_tokens = bhead.next_tokens(y_gpu)
+        assert got_tokens == om.recheck_tokens(cfg, y_gpu, norm_w, lm_rows, bhead.run_graph(y_gpu)), "device vs host recheck"
         for row, (g, want) in enumerate(zip(got_tokens, want_tokens)):
             if g == want:
                 exact += 1

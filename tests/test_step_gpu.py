@@ -104,6 +104,8 @@ def test_tiny_greedy_tokens_match_oracle(pkg, step_mod, golden):
             if run == "gpu":
                 hidden = step(inputs_embeds=emb, **inputs)
                 maxima = head.run_graph(hidden)
+                # The recheck on the device (B200Head.next_tokens) equals the host recheck on the same maxima.
+                assert head.next_tokens(hidden) == om.recheck_tokens(cfg, hidden, head_w["norm_weight"], lm_rows, maxima)
             else:
                 hidden = oracle(inputs_embeds=emb, **inputs)
                 maxima = om.head_maxima(cfg, hidden, head_w["norm_weight"], head_w["lm_head"].q, head_w["lm_head"].scale)
