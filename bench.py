@@ -11,12 +11,14 @@ heads and vocabulary sliced, row-parallel outputs summed): the total work is fix
 are seeded random values (the bytes moved are the same as a real prompt's).
 
 The JSON line's `value` is tokens/s with the step inputs already on the device; `e2e` is the same
-through the reference-facing calls (B200Step(**host tensors) -> host hidden, B200Head.run_graph ->
-host maxima), host<->device copies included. `step_roofline` sets the algorithmic HBM bytes of one
+through the reference-facing calls (B200Step(**host tensors) -> host hidden, B200Head.next_tokens ->
+host token ids, as ChipHead.next_tokens returns them), host<->device copies included. `step_roofline` sets the algorithmic HBM bytes of one
 whole decode step against the step time; `prefill` is one 512-token chunk of one row through all
-layers, device-timed (the prefill half of the tokens/s metric). `--impl reference` times the CPU oracle (the reference's
-CPU path restated) on this host's cores on a bounded sample: one 4-layer block per step at the same
-batch, scaled to 64 layers.
+layers, device-timed (the prefill half of the tokens/s metric). A step ends with each row's greedy token
+(the exact recheck of the best 4 groups included). `--impl reference` times the reference's own CPU
+branches (its Qwen38Step and HeadStep, copied into oracle/_ref by oracle/build_ref.py; the oracle's
+restatement where that copy is absent) on this host's cores on a bounded sample: one 4-layer block per
+step at the same batch, scaled to 64 layers, plus one head call.
 """
 
 from __future__ import annotations
@@ -148,12 +150,27 @@ def run_ours(args, world, rank, local):
                  active=torch.ones(B).pin_memory()) for s in range(total)]
     dev_inputs = [{k: v.to(device) for k, v in h.items()} for h in host]
 
+    tokens_dev = torch.zeros(B, dtype=torch.int32, device=device)
+    slot_l = torch.zeros(B, 4, dtype=torch.float32, device=device)
+    slot_t = torch.zeros(B, 4, dtype=torch.int32, device=device)
+
     def device_step(s):
+        """One greedy token per row with everything resident: the 64 layers, the lm_head group maxima and
+        the exact recheck of the best 4 groups, tokens left on the device."""
         d = dev_inputs[s]
         step.load_decode_inputs(d["inputs_embeds"], d["cos"], d["sin"], d["position"], d["active"])
         hidden = step.decode_device()
         head.hidden.copy_(hidden)
-        return head.maxima_device()
+        maxima = head.maxima_device()
+        if world == 1:
+            ops.lm_head_recheck(head.hidden, head.norm_w, cfg.rms_norm_eps, maxima, head.lm_head, 0, 4, tokens=tokens_dev)
+        else:
+            ops.lm_head_recheck(head.hidden, head.norm_w, cfg.rms_norm_eps, maxima, head.lm_head, rank * head.vocab_local,
+                                4, slot_logits=slot_l, slot_tokens=slot_t)
+            torch.distributed.all_reduce(slot_l, op=torch.distributed.ReduceOp.MAX)
+            torch.distributed.all_reduce(slot_t, op=torch.distributed.ReduceOp.MAX)
+            ops.lm_head_pick(slot_l, slot_t, tokens_dev)
+        return tokens_dev
 
     # Warm-up (also captures the decode graph).
     for s in range(args.warmup):
@@ -185,14 +202,14 @@ def run_ours(args, world, rank, local):
     w0 = time.perf_counter()
     e_start.record()
     for s in range(args.warmup, total):
-        hidden = step(**host[s])
-        head.run_graph(hidden)
+        hidden = step(**host[s])  # NeuronStep's call: host tensors in, the hidden state back on the host
+        head.next_tokens(hidden)  # ChipHead.next_tokens' call: group maxima and the exact recheck, token ids back
     e_end.record()
     torch.cuda.synchronize()
     wall_e2e = time.perf_counter() - w0
     e2e_ms = max_over_ranks(max(e_start.elapsed_time(e_end), wall_e2e * 1e3), world, device)
     h2d = sum(v.numel() * v.element_size() for v in host[0].values()) + B * cfg.hidden_size * 2
-    d2h = B * cfg.hidden_size * 2 + B * (cfg.vocab_size // 32) * 4
+    d2h = B * cfg.hidden_size * 2 + B * 4
 
     # Roofline of the dominant kernel (gdn_decode): each launch moves the state tiles in and out,
     # the conv state in and out, and reads its qkvz/ab rows and writes the e5m2 output.
@@ -253,9 +270,10 @@ def run_ours(args, world, rank, local):
             "peak_kind": peak_kind,
             "unit": "GB/s",
             "frac": achieved / peak,
-            # DRAM bytes of one gdn_decode_kernel launch at this shape from an ncu capture
-            # (profiles/gdn_decode_b256.md); not captured for other batch sizes or TP degrees.
+            # dram__bytes_read.sum + dram__bytes_write.sum of one gdn_decode_kernel launch from an ncu capture
+            # at batch 256 on one GPU (the shape this line times at N = 1); other shapes were not captured.
             "traffic": GDN_TRAFFIC_B256 if (B == 256 and world == 1) else None,
+            "traffic_source": "ncu capture, batch 256, one GPU" if (B == 256 and world == 1) else None,
             "bytes_per_launch": per_launch,
             "launch_ms": gdn_ms,
         },
@@ -275,7 +293,8 @@ def run_ours(args, world, rank, local):
             "tokens_per_s": C / (prefill_ms / 1e3),
         },
         "clocks": clocks,
-        "gpu_launches": (step.kernels_per_decode_step() + 2) * args.steps,
+        # the step's kernels, then rmsnorm + group maxima + recheck (+ pick with TP > 1)
+        "gpu_launches": (step.kernels_per_decode_step() + 3 + (world > 1)) * args.steps,
         "build_s": round(build_s, 1),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -340,72 +359,112 @@ def rotary(cfg, positions):
 
 # ------------------------------------------------------------------------------------------------
 def cpu_block_step(cfg, pkg, batch: int):
-    """A CPU oracle for one full-width 4-layer block (the bounded sample), and a function running one
-    decode step of it."""
+    """One decode step of one full-width 4-layer block (3 gated-delta + 1 attention layer) on the host's
+    cores, at `batch` rows over seeded cache and state contents, and a function running it. The
+    reference's own Qwen38Step CPU branch when its package is in oracle/_ref (oracle/build_ref.py), else
+    the oracle's restatement of it. Returns (run, kind)."""
+    from oracle import ref_step
+
+    block = pkg.config.block_config(cfg, 4)
+    gen = torch.Generator().manual_seed(5)
+    pos = torch.randint(0, MAX_SEQ - 2, (batch,), generator=gen, dtype=torch.int32)
+    x = (torch.randn(batch, 1, cfg.hidden_size, generator=gen) * 0.02).to(torch.bfloat16)
+    if ref_step.available():
+        model, rcfg, rgen = ref_step.reference_block(block, batch, MAX_SEQ)
+        for layer in model.layers:
+            if hasattr(layer, "linear_attn"):
+                layer.linear_attn.recurrent_state.normal_(0.0, 0.1, generator=gen)
+            else:
+                layer.self_attn.k_cache.normal_(0.0, 1.0, generator=gen)
+                layer.self_attn.v_cache.normal_(0.0, 1.0, generator=gen)
+        inputs = rgen.batch_step_inputs(rcfg, pos.tolist(), MAX_SEQ, torch.bfloat16, [True] * batch)
+
+        def run():
+            with torch.no_grad():
+                return model(inputs_embeds=x, **inputs)
+
+        return run, "reference"
     from oracle import cpu_model as om
 
     w = {}
     for i in range(4):
         w |= pkg.weights.synthetic_layer(cfg, i, seed=0, device="cpu")
-    block = pkg.config.block_config(cfg, 4)
     st = om.OracleStep(block, w, MAX_SEQ, batch)
-    gen = torch.Generator().manual_seed(5)
     for kind, mixer, *_ in st.layers:
         if kind == om.LINEAR:
             mixer.recurrent_state.normal_(0.0, 0.1, generator=gen)
         else:
             mixer.k_cache.normal_(0.0, 1.0, generator=gen)
             mixer.v_cache.normal_(0.0, 1.0, generator=gen)
-    pos = torch.randint(0, MAX_SEQ - 2, (batch,), generator=gen, dtype=torch.int32)
     cos, sin = om.rotary(cfg, pos, torch.bfloat16)
-    x = (torch.randn(batch, 1, cfg.hidden_size, generator=gen) * 0.02).to(torch.bfloat16)
     inputs = dict(cos=cos.unsqueeze(1), sin=sin.unsqueeze(1), position=pos, active=torch.ones(batch))
-    return lambda: st(inputs_embeds=x, **inputs)
+    return (lambda: st(inputs_embeds=x, **inputs)), "port"
+
+
+def cpu_head_seconds(cfg, pkg, batch: int) -> tuple[float, str]:
+    """One call of the head on the host's cores: the reference's HeadStep CPU branch (fp32 logits over the
+    whole vocabulary and their group maxima) when available, else the oracle's restatement."""
+    from oracle import ref_step
+
+    x = (torch.randn(batch, 1, cfg.hidden_size, generator=torch.Generator().manual_seed(6))).to(torch.bfloat16)
+    if ref_step.available():
+        hstep = ref_step.reference_head(cfg, batch)
+        with torch.no_grad():
+            t0 = time.perf_counter()
+            hstep(x)
+            return time.perf_counter() - t0, "reference"
+    from oracle import cpu_model as om
+
+    head = pkg.weights.synthetic_head(cfg, 0, "cpu")
+    t0 = time.perf_counter()
+    om.head_maxima(cfg, x, head["norm_weight"], head["lm_head"].q, head["lm_head"].scale)
+    return time.perf_counter() - t0, "port"
+
+
+def cpu_step(cfg, pkg, batch: int, steps: int, warmup: int) -> dict:
+    """The CPU baseline of one decode step of the 64-layer model at `batch` rows: one 4-layer block timed
+    over `steps` runs (after `warmup`), times 16, plus one timed head call over the whole vocabulary."""
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    run, kind = cpu_block_step(cfg, pkg, batch)
+    for _ in range(max(1, warmup)):
+        run()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        run()
+    per_block = (time.perf_counter() - t0) / steps
+    head_s, _ = cpu_head_seconds(cfg, pkg, batch)
+    step_s = per_block * (LAYERS // 4) + head_s
+    who = "the reference's own Qwen38Step / HeadStep CPU branches" if kind == "reference" else "the oracle's restatement"
+    return {"value": batch / step_s, "unit": "tokens/s", "cores": threads, "kind": kind, "step_s": step_s,
+            "sample": f"{who}: one full-width 4-layer block (3 gated-delta + 1 attention) decoding {batch} rows, "
+                      f"{steps} runs at {per_block:.2f} s, x{LAYERS // 4} for 64 layers, plus one head call over the "
+                      f"whole vocabulary ({head_s:.2f} s); CPU {platform.processor() or platform.machine()}"}
 
 
 def cpu_baseline(cfg, pkg, batch: int, samples: int) -> dict:
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    run = cpu_block_step(cfg, pkg, batch)
-    run()  # dequantises and caches the block's weights
-    times = []
-    for _ in range(samples):
-        t0 = time.perf_counter()
-        run()
-        times.append(time.perf_counter() - t0)
-    per_block = sorted(times)[len(times) // 2]
-    step_s = per_block * (LAYERS // 4)
-    return {"value": batch / step_s, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"one full-width 4-layer block (3 gated-delta + 1 attention) decode at batch {batch}, "
-                      f"{per_block:.2f} s per block, scaled x{LAYERS // 4} to 64 layers; lm_head not included; "
-                      f"CPU {platform.processor() or platform.machine()}"}
+    out = cpu_step(cfg, pkg, batch, samples, 1)
+    out.pop("step_s")
+    return out
 
 
 def run_reference(args, world, rank, local):
-    """The reference arm: the CPU oracle on this host's cores, rank 0 only."""
+    """The reference arm: the reference's own CPU implementation on this host's cores, rank 0 only."""
     if rank != 0:
         return
     pkg = importlib.import_module(PACKAGE)
     cfg = pkg.config.full_config(num_blocks=LAYERS // 4)
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    run = cpu_block_step(cfg, pkg, args.batch)
-    for _ in range(max(1, args.warmup)):
-        run()
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        run()
-    per_block = (time.perf_counter() - t0) / args.steps
-    step_s = per_block * (LAYERS // 4)
-    value = args.batch / step_s
+    base = cpu_step(cfg, pkg, args.batch, args.steps, args.warmup)
+    step_s = base.pop("step_s")
+    value = base["value"]
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "fp8 weights dequantised to bf16 (CPU)", "data": "synthetic", "impl": "reference",
-        "config": {"workload": "BASELINE config 3 decode step, batch %d; per step one 4-layer block timed, scaled x16" % args.batch,
+        "config": {"workload": "BASELINE config 3 decode step, batch %d; per step one 4-layer block timed, x16, plus "
+                               "the head" % args.batch,
                    "global_batch": args.batch, "seq_len": MAX_SEQ, "parallelism": "cpu"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port",
-                         "sample": "one full-width 4-layer block per step at the same batch, scaled to 64 layers"},
+        "cpu_baseline": base,
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
