@@ -51,3 +51,31 @@ def test_decode_step_bytes_counts_weights_state_and_cache():
     want += fp8(48, 32) + fp8(32, 32) + int(kv_positions * 1 * 8 * 2 * 2)  # attention projections, K and V
     assert bench.MAX_SEQ == 512
     assert bench.decode_step_bytes(step, head, "linear_attention", positions) == want
+
+
+def test_input_builders_equal_the_oracles_and_check_positions(pkg):
+    """The host input builders give the rotary tables the oracle (and the reference, generate.py:25-31) uses,
+    the reference's shapes and dtypes, and refuse positions past the cache."""
+    import pytest
+    import torch
+
+    from oracle import cpu_model as om
+
+    inp = __import__(pkg.__name__ + ".inputs", fromlist=["inputs"])
+    cfg = pkg.config.full_config(1)
+    pos = torch.tensor([0, 5, 511, 30000, 32766], dtype=torch.int32)
+    cos, sin = inp.rotary(cfg, pos)
+    ocos, osin = om.rotary(cfg, pos, torch.bfloat16)
+    assert torch.equal(cos, ocos) and torch.equal(sin, osin)
+    d = inp.decode_inputs(cfg, [3, 9], 512, [True, False])
+    assert d["cos"].shape == (2, 1, cfg.rotary_dim) and d["position"].dtype == torch.int32 and d["active"].tolist() == [1.0, 0.0]
+    p = inp.prefill_inputs(cfg, 2, 512, 100, 512)
+    assert p["cos"].shape == (1, 512, cfg.rotary_dim) and int(p["n_valid"]) == 100
+    v = inp.verify_inputs(cfg, [10, 20], 4, 512, [True, True], [0, 3])
+    assert v["cos"].shape == (2, 4, cfg.rotary_dim) and v["accepted"].tolist() == [0, 3]
+    m = inp.mtp_step_inputs(cfg, [10], 4, 512, [True])
+    assert torch.equal(m["cos"][0, 0], inp.rotary(cfg, torch.tensor([11]))[0][0])
+    with pytest.raises(ValueError):
+        inp.decode_inputs(cfg, [511], 512)
+    with pytest.raises(ValueError):
+        inp.verify_inputs(cfg, [509], 4, 512, [True], [0])
