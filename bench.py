@@ -42,6 +42,9 @@ METRIC = "total tokens/s (64-layer decode step incl. lm_head maxima)"
 MAX_SEQ = 512
 GDN_TRAFFIC_B256 = 777.4e6  # dram__bytes per gdn_decode_kernel launch, batch 256, one GPU (ncu)
 LAYERS = 64
+SERVE_PROMPT = (32, 224)  # prompt lengths of the serving sample
+SERVE_CHUNK = 256
+SERVE_NEW = 32
 
 
 def peaks() -> tuple[float, str]:
@@ -239,6 +242,22 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     prefill_ms = max_over_ranks(p_start.elapsed_time(p_end), world, device) / chunks
 
+    # Serving (the prefill half and the decode half of "total tokens/s" together): every slot takes a
+    # seeded prompt, prefilled in chunks through the step's prefill call, then greedy decode steps; the
+    # reference's Scheduler.run without speculation (serve.py), timed on the host clock end to end.
+    serve_mod = importlib.import_module(f"{PACKAGE}.serve")
+    table = pkg.weights.synthetic_embedding_table(cfg, seed=0, device=device)
+    embeddings = serve_mod.Embeddings(table)
+    g_serve = torch.Generator().manual_seed(7)
+    lens = torch.randint(SERVE_PROMPT[0], SERVE_PROMPT[1] + 1, (B,), generator=g_serve).tolist()
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g_serve).tolist() for n in lens]
+    serve_mod.serve(step, head, embeddings, prompts[:2], 2, chunk=SERVE_CHUNK)  # first use of the chunk size
+    if world > 1:
+        torch.distributed.barrier()
+    served = serve_mod.serve(step, head, embeddings, prompts, SERVE_NEW, chunk=SERVE_CHUNK)
+    serve_s = max_over_ranks(served.wall_s, world, device)
+    del table, embeddings
+
     tokens = B * args.steps
     step_bytes = decode_step_bytes(step, head, pkg.config.LINEAR, positions[args.warmup:])
     line = {
@@ -291,6 +310,19 @@ def run_ours(args, world, rank, local):
             "workload": f"one {C}-token chunk of one row through all {LAYERS} layers (device-timed, {chunks} chunks)",
             "ms_per_chunk": prefill_ms,
             "tokens_per_s": C / (prefill_ms / 1e3),
+        },
+        "serve": {
+            "workload": f"{B} prompts of U[{SERVE_PROMPT[0]}, {SERVE_PROMPT[1]}] seeded tokens, prefilled in "
+                        f"{SERVE_CHUNK}-token chunks one row at a time, then {SERVE_NEW} greedy tokens each "
+                        "(prefill-first slots, B200Step + B200Head.next_tokens, host clock)",
+            "total_tokens_per_s": (served.prompt_tokens + served.generated_tokens) / serve_s,
+            "prompt_tokens": served.prompt_tokens,
+            "generated_tokens": served.generated_tokens,
+            "seconds": serve_s,
+            "prefill_seconds": served.prefill_s,
+            "decode_seconds": served.decode_s,
+            "prefill_calls": served.prefill_calls,
+            "decode_steps": served.decode_steps,
         },
         "clocks": clocks,
         # the step's kernels, then rmsnorm + group maxima + recheck (+ pick with TP > 1)

@@ -414,6 +414,11 @@ int q38_lm_head_recheck(const void* hidden, int64_t ldh, const void* norm_w, flo
                         int64_t ldm, int64_t groups, const void* lm_head, int64_t vocab_first, int64_t vocab_rows,
                         int64_t hidden_size, int group, int candidates, int64_t rows, float* slot_logits,
                         int32_t* slot_tokens, int32_t* tokens, q38_stream_t stream);
+/* out[i] = table[ids[i]]: bf16 rows of `hidden` values of the embedding table [vocab, hidden] for n int32
+ * ids, into out [n, ldo] (ChipHead.embed_batch, qwen38_inf2/generate.py:183-184). An id outside the table
+ * gives a zero row and records Q38_ERR_ARG in the device error word. */
+int q38_embed_rows(const void* table, int64_t vocab, int64_t hidden, const int32_t* ids, int64_t n, void* out,
+                   int64_t ldo, q38_stream_t stream);
 /* tokens[r] from the per-candidate results of q38_lm_head_recheck (maximised across ranks): the candidate
  * slots in order, a strictly larger logit replacing the best so far; -1 where none is valid. */
 int q38_lm_head_pick(const float* slot_logits, const int32_t* slot_tokens, int candidates, int64_t rows, int32_t* tokens,

@@ -111,6 +111,7 @@ SIGNATURES = {
         [c_void_p, c_int64, c_void_p, c_float, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int64, c_int64, c_int,
          c_int, c_int64, c_void_p, c_void_p, c_void_p, c_void_p],
     ),
+    "q38_embed_rows": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p]),
     "q38_lm_head_pick": (c_int, [c_void_p, c_void_p, c_int, c_int64, c_void_p, c_void_p]),
     "q38_copy_state_rows": (
         c_int, [ctypes.POINTER(c_void_p), ctypes.POINTER(c_int64), ctypes.POINTER(c_int64), c_int, c_int64, c_int64,

@@ -243,3 +243,38 @@ extern "C" int q38_lm_head_pick(const float* slot_logits, const int32_t* slot_to
                                    slot_logits, slot_tokens, candidates, rows, tokens);
   return cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "lm_head_pick launch");
 }
+
+// ---- embeddings ------------------------------------------------------------------------------------
+// out[i] = table[ids[i]] (bf16 rows of hidden_size), ChipHead.embed_batch (generate.py:183-184) on the
+// device: one 16-byte piece per thread. An id outside the table writes a zero row and records
+// Q38_ERR_ARG in the device error word.
+namespace {
+__global__ void embed_kernel(const __nv_bfloat16* table, int64_t vocab, int64_t hidden, const int32_t* ids, int64_t n,
+                             __nv_bfloat16* out, int64_t ldo) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t i = blockIdx.y;
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;  // 8-value piece
+  if (i >= n || c * 8 >= hidden) return;
+  const int64_t id = ids[i];
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  if (id >= 0 && id < vocab) v = *reinterpret_cast<const uint4*>(table + id * hidden + c * 8);
+  else if (c == 0) record_error(Q38_ERR_ARG);
+  *reinterpret_cast<uint4*>(out + i * ldo + c * 8) = v;
+}
+}  // namespace
+
+extern "C" int q38_embed_rows(const void* table, int64_t vocab, int64_t hidden, const int32_t* ids, int64_t n, void* out,
+                              int64_t ldo, q38_stream_t stream) {
+  using namespace q38host;
+  if (!table || !ids || !out) return set_error("q38_embed_rows: null pointer"), Q38_ERR_ARG;
+  if (vocab <= 0 || hidden <= 0 || hidden % 8 || n <= 0 || n > 65535 || ldo < hidden || ldo % 8)
+    return set_error("q38_embed_rows: bad sizes (hidden a multiple of 8, at most 65535 ids)"), Q38_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(table) | reinterpret_cast<uintptr_t>(out)) & 15u)
+    return set_error("q38_embed_rows: table and out must be 16-byte aligned"), Q38_ERR_ARG;
+  const dim3 grid(static_cast<unsigned>((hidden / 8 + 127) / 128), static_cast<unsigned>(n));
+  const cudaError_t e = launch_pdl(embed_kernel, grid, dim3(128), 0, static_cast<cudaStream_t>(stream),
+                                   static_cast<const __nv_bfloat16*>(table), vocab, hidden, ids, n,
+                                   static_cast<__nv_bfloat16*>(out), ldo);
+  return cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "embed_rows launch");
+}

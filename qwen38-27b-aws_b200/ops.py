@@ -438,6 +438,17 @@ def lm_head_recheck(hidden: torch.Tensor, norm_w: torch.Tensor, eps: float, maxi
               ptr(slot_logits), ptr(slot_tokens), ptr(tokens), _stream())
 
 
+def embed_rows(table: torch.Tensor, ids: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """out[i] = table[ids[i]] (bf16 rows; ids int32 on the device)."""
+    _cuda(table, ids, out)
+    _need(table.dtype == BF16 and table.is_contiguous() and out.dtype == BF16 and out.stride(-1) == 1, "bf16 table and out")
+    _need(ids.dtype == torch.int32 and ids.is_contiguous(), "ids int32")
+    n = ids.numel()
+    _lib.call("q38_embed_rows", table.data_ptr(), table.shape[0], table.shape[1], ids.data_ptr(), n, out.data_ptr(),
+              out.stride(-2) if out.dim() > 1 else table.shape[1], _stream())
+    return out
+
+
 def lm_head_pick(slot_logits: torch.Tensor, slot_tokens: torch.Tensor, tokens: torch.Tensor) -> None:
     _cuda(slot_logits, slot_tokens, tokens)
     rows, candidates = slot_logits.shape

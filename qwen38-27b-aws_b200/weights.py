@@ -187,6 +187,13 @@ def synthetic_kv_scales(cfg: TextConfig, index: int) -> tuple[float, float]:
     return 2.0 ** -4, 2.0 ** -5
 
 
+def synthetic_embedding_table(cfg: TextConfig, seed: int = 0, device="cuda", std: float = STD) -> torch.Tensor:
+    """A seeded N(0, std) embedding table [vocab, hidden] bf16 drawn on `device` in one piece (its values are
+    not embedding_rows', which draws a generator per token on the CPU; serving loops that need every row
+    on the GPU use this one)."""
+    return _bf16((cfg.vocab_size, cfg.hidden_size), seed, "embed.table", device, std)
+
+
 def embedding_rows(cfg: TextConfig, token_ids, seed: int = 0, std: float = STD) -> torch.Tensor:
     """Rows of a seeded N(0, std) embedding table ``[vocab, hidden]``, generated per token, bf16 on CPU."""
     rows = [_normal((cfg.hidden_size,), seed, f"embed.{int(t)}", "cpu", std) for t in token_ids]
