@@ -85,11 +85,12 @@ class B200Step:
     def __init__(self, cfg: TextConfig, layer_weights, max_seq_len: int, batch_size: int, tp_degree: int = 1,
                  rank: int = 0, device: torch.device | str | None = None, saved_states: bool = False,
                  use_graph: bool = True, process_group=None, verify_tokens: int = 0, fused_allreduce: bool = True,
-                 max_chunk: int = 512, kv_cache_format: str = "bf16", kv_scales=None):
+                 max_chunk: int = 512, kv_cache_format: str = "bf16", kv_scales=None, presharded: bool = False):
         """`layer_weights(i)` returns layer i's unsharded weights (weights.synthetic_layer names), or
         `layer_weights` is a dict holding them all. `kv_cache_format` "fp8" keeps the KV cache as FP8 e4m3
         bytes with static per-layer scales (the reference's kv_cache_format, model.py:556-563): `kv_scales`
-        {layer index: (k_scale, v_scale)}, by default weights.synthetic_kv_scales."""
+        {layer index: (k_scale, v_scale)}, by default weights.synthetic_kv_scales. With `presharded`,
+        `layer_weights(i)` already gives this rank's cut (weights.RankShards.layer)."""
         if kv_cache_format not in ("bf16", "fp8"):
             raise ValueError(f"kv_cache_format must be bf16 or fp8, not {kv_cache_format!r}")
         self.kv_fp8 = kv_cache_format == "fp8"
@@ -105,7 +106,8 @@ class B200Step:
         get = layer_weights if callable(layer_weights) else (lambda i: layer_weights)
         self.comm = None
         with torch.cuda.device(self.device):
-            self.layers = [self._prepare(i, W.shard_layer(cfg, get(i), i, rank, tp_degree)) for i in range(cfg.num_hidden_layers)]
+            cut = (lambda i: get(i)) if presharded else (lambda i: W.shard_layer(cfg, get(i), i, rank, tp_degree))  # noqa: E731
+            self.layers = [self._prepare(i, cut(i)) for i in range(cfg.num_hidden_layers)]
             if tp_degree > 1 and fused_allreduce:
                 rows = max(batch_size, batch_size * max(verify_tokens, 1), max_chunk)
                 self.comm = ops.Communicator(rank, tp_degree, rows, cfg.hidden_size, self.device, process_group)
@@ -146,7 +148,10 @@ class B200Step:
             kvh = cfg.kv_heads_per_rank(self.tp)
             scales = None
             if self.kv_fp8:
-                scales = (self.kv_scales or {}).get(i) or W.synthetic_kv_scales(cfg, i)
+                held = (f"{p}.self_attn.k_scale", f"{p}.self_attn.v_scale")  # a checkpoint's calibrated scales
+                scales = ((self.kv_scales or {}).get(i)
+                          or (tuple(float(w[n].reshape(-1)[0]) for n in held) if held[0] in w else None)
+                          or W.synthetic_kv_scales(cfg, i))
                 scales = tuple(float(torch.tensor(float(v), dtype=BF16)) for v in scales)  # the bf16 parameters
             cache_dtype = torch.uint8 if self.kv_fp8 else BF16
             mixer = _Attn(
@@ -517,13 +522,13 @@ class B200Head:
     """Final norm and the lm_head group maxima of one rank's vocab slice (HeadStep, model.py:863-900)."""
 
     def __init__(self, cfg: TextConfig, head_weights: dict, batch_size: int, tp_degree: int = 1, rank: int = 0,
-                 device=None, group_rows: int = 32, process_group=None):
+                 device=None, group_rows: int = 32, process_group=None, presharded: bool = False):
         if group_rows != 32:
             raise ValueError("the lm_head kernel takes groups of 32")
         self.cfg, self.batch, self.tp, self.rank = cfg, batch_size, tp_degree, rank
         self.group = process_group
         self.device = torch.device(device or f"cuda:{torch.cuda.current_device()}")
-        shard = W.shard_head(cfg, head_weights, rank, tp_degree)
+        shard = head_weights if presharded else W.shard_head(cfg, head_weights, rank, tp_degree)
         self.norm_w = shard["norm_weight"].to(self.device, BF16).contiguous()
         # The kernel multiplies BF16 by BF16: the e4m3 * 2^s weights are exact in BF16.
         self.lm_head = ops.DeviceBF16Linear(shard["lm_head"].to(self.device).dequant().to(BF16), self.device)
@@ -602,7 +607,7 @@ class B200MTP:
 
     def __init__(self, cfg: TextConfig, mtp_weights: dict, max_seq_len: int, batch_size: int, tokens: int = 4,
                  tp_degree: int = 1, rank: int = 0, device=None, process_group=None, fused_allreduce: bool = True,
-                 max_chunk: int = 512, kv_cache_format: str = "bf16", kv_scales=None):
+                 max_chunk: int = 512, kv_cache_format: str = "bf16", kv_scales=None, presharded: bool = False):
         self.cfg, self.tp, self.rank, self.batch, self.tokens = cfg, tp_degree, rank, batch_size, tokens
         self.device = torch.device(device or f"cuda:{torch.cuda.current_device()}")
         self.group = process_group

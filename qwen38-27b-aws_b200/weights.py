@@ -243,7 +243,7 @@ def shard_layer(cfg: TextConfig, weights: dict, index: int, rank: int, tp: int) 
         if not name.startswith(p + "."):
             continue
         leaf = name[len(p) + 1 :]
-        if tp == 1 or leaf.endswith("norm_weight"):
+        if tp == 1 or leaf.endswith("norm_weight") or leaf in ("self_attn.k_scale", "self_attn.v_scale"):
             out[name] = t
         elif leaf in ("mlp.gate_proj", "mlp.up_proj", "linear_attn.in_proj_z", "linear_attn.in_proj_b",
                       "linear_attn.in_proj_a", "linear_attn.A_log", "linear_attn.dt_bias", "self_attn.q_proj"):
@@ -262,3 +262,166 @@ def shard_layer(cfg: TextConfig, weights: dict, index: int, rank: int, tp: int) 
 def shard_head(cfg: TextConfig, head: dict, rank: int, tp: int) -> dict:
     a, b = _span(cfg.vocab_size, rank, tp)
     return {"norm_weight": head["norm_weight"], "lm_head": head["lm_head"].rows(a, b)}
+
+
+# ----------------------------------------------------------------------------------------------
+# On-disk weights: this package's per-rank shards, and the reference's own per-rank files
+# ----------------------------------------------------------------------------------------------
+SHARD_BLOCK = 4  # layers per shard file, the model's repeat
+
+
+def _flatten(weights: dict) -> dict:
+    out = {}
+    for name, t in weights.items():
+        if isinstance(t, FP8Weight):
+            out[f"{name}.q"], out[f"{name}.scale"] = t.q.contiguous(), t.scale.contiguous()
+        else:
+            out[name] = t.contiguous()
+    return out
+
+
+def _unflatten(tensors: dict) -> dict:
+    out = {}
+    for name, t in tensors.items():
+        if name.endswith(".q"):
+            base = name[:-2]
+            out[base] = FP8Weight(t, tensors[base + ".scale"])
+        elif not name.endswith(".scale"):
+            out[name] = t
+    return out
+
+
+def shard_file(weights_dir, kind: str, rank: int, block: int | None = None):
+    from pathlib import Path
+
+    stem = f"b200_block{block:02d}_tp{rank}" if kind == "block" else f"b200_{kind}_tp{rank}"
+    return Path(weights_dir) / f"{stem}.safetensors"
+
+
+def write_rank_shards(cfg: TextConfig, layer_weights, head: dict, weights_dir, tp: int, mtp: dict | None = None) -> None:
+    """This package's on-disk format: for every rank r of `tp`, its TP cut (shard_layer, shard_head,
+    shard_mtp: e4m3 bytes [out, in] as <name>.q with fp32 power-of-two scales [out, in / 32] as
+    <name>.scale, bf16 vectors) in b200_block{b}_tp{r} files of SHARD_BLOCK layers, b200_head_tp{r} and
+    b200_mtp_tp{r}, and build_info.json. `layer_weights(i)` gives layer i's unsharded weights. Loading a
+    rank reads only its own files (RankShards)."""
+    import json
+    from pathlib import Path
+
+    from safetensors.torch import save_file
+
+    d = Path(weights_dir)
+    d.mkdir(parents=True, exist_ok=True)
+    L = cfg.num_hidden_layers
+    for b in range(0, L, SHARD_BLOCK):
+        full = {}
+        for i in range(b, min(L, b + SHARD_BLOCK)):
+            full |= layer_weights(i)
+        for r in range(tp):
+            cut = {}
+            for i in range(b, min(L, b + SHARD_BLOCK)):
+                cut |= shard_layer(cfg, full, i, r, tp)
+            save_file(_flatten(cut), str(shard_file(d, "block", r, b // SHARD_BLOCK)))
+    for r in range(tp):
+        save_file(_flatten(shard_head(cfg, head, r, tp)), str(shard_file(d, "head", r)))
+        if mtp is not None:
+            save_file(_flatten(shard_mtp(cfg, mtp, r, tp)), str(shard_file(d, "mtp", r)))
+    (d / "build_info.json").write_text(json.dumps({"format": "b200 e4m3 + fp32 per-32 scales, [out, in]", "tp_degree": tp,
+                                                   "layers": L, "block_layers": SHARD_BLOCK, "mtp": mtp is not None}))
+
+
+class RankShards:
+    """One rank's weights from write_rank_shards' files: `layer(i)` (that rank's cut of layer i, names as
+    synthetic_layer's), `head()`, `mtp()`; pass them to B200Step / B200Head / B200MTP with presharded=True."""
+
+    def __init__(self, weights_dir, rank: int):
+        import json
+        from pathlib import Path
+
+        self.dir, self.rank = Path(weights_dir), rank
+        self.info = json.loads((self.dir / "build_info.json").read_text())
+        if not 0 <= rank < self.info["tp_degree"]:
+            raise ValueError(f"rank {rank} outside the files' {self.info['tp_degree']} ranks")
+        self._block, self._cache = None, {}
+
+    def _load(self, path) -> dict:
+        from safetensors.torch import load_file
+
+        return _unflatten(load_file(str(path)))
+
+    def layer(self, i: int) -> dict:
+        b = i // self.info["block_layers"]
+        if self._block != b:
+            self._cache, self._block = self._load(shard_file(self.dir, "block", self.rank, b)), b
+        p = f"layers.{i}."
+        return {k: v for k, v in self._cache.items() if k.startswith(p)}
+
+    def head(self) -> dict:
+        return self._load(shard_file(self.dir, "head", self.rank))
+
+    def mtp(self) -> dict:
+        return self._load(shard_file(self.dir, "mtp", self.rank))
+
+
+def _e5m2_to_e4m3(weight_fp8: torch.Tensor, name: str) -> FP8Weight:
+    """A reference weight_fp8 matrix (e5m2 bytes [in, out], scale folded in) as e4m3 [out, in] with per-32
+    power-of-two scales, exactly: the reference's weights are MXFP4 values times a power of two per group of
+    32 inputs (checkpoint._fp4_weights, fp4.to_fp8), and a group spanning under 16 binades converts without
+    rounding. A group that would round raises."""
+    w = weight_fp8.view(torch.float8_e5m2).float().transpose(0, 1).contiguous()
+    q, scale = codec.quantize_mx_e4m3(w)
+    back = codec.dequantize_mx_e4m3(q, scale)
+    if not torch.equal(back, w):
+        bad = int((back != w).sum())
+        raise ValueError(f"{name}: {bad} values of the reference's e5m2 weights do not convert to e4m3 exactly")
+    return FP8Weight(q, scale)
+
+
+def reference_rank_files(weights_dir, cfg: TextConfig, block_layers: int, tp_ref: int):
+    """The reference's own per-rank files (checkpoint.write_rank_weights: block{b:02d}_tp{r}.safetensors,
+    checkpoint.py:282-292, :405-413) as layer_weights(i) -> layer i's unsharded weights in this package's
+    form: the ranks' cuts joined again by the reference's rules (rows of column-parallel matrices, columns
+    of row-parallel ones, [q | k | v] block by block, checkpoint.py:165-224), each weight_fp8 converted
+    exactly to e4m3 with per-32 scales; KV-cache scales, when the files hold them, under
+    self_attn.k_scale / v_scale. Re-cut it for any TP degree with shard_layer."""
+    from pathlib import Path
+
+    from safetensors.torch import load_file
+
+    d = Path(weights_dir)
+    cache: dict = {}
+
+    def rank_block(b: int, r: int) -> dict:
+        if (b, r) not in cache:
+            if len(cache) >= 2 * tp_ref:
+                cache.clear()
+            cache[(b, r)] = load_file(str(d / f"block{b:02d}_tp{r}.safetensors"))
+        return cache[(b, r)]
+
+    def layer(i: int) -> dict:
+        b, off = divmod(i, block_layers)
+        parts = [rank_block(b, r) for r in range(tp_ref)]
+        src, dst = f"layers.{off}.", f"layers.{i}."
+        names = sorted({k[len(src):] for k in parts[0] if k.startswith(src)})
+        kd, vd = cfg.linear_key_dim // tp_ref, cfg.linear_value_dim // tp_ref
+        out = {}
+        for leaf in names:
+            ts = [p[src + leaf] for p in parts]
+            base = leaf[: -len(".weight_fp8")] if leaf.endswith(".weight_fp8") else leaf
+            if base in ("mlp.down_proj", "linear_attn.out_proj", "self_attn.o_proj"):
+                full = torch.cat(ts, dim=0)  # [in / t, out] pieces: row-parallel, cut by input
+            elif base == "linear_attn.in_proj_qkv":
+                full = torch.cat([torch.cat([t[:, j * kd:(j + 1) * kd] if j < 2 else t[:, 2 * kd:2 * kd + vd] for t in ts], 1)
+                                  for j in range(3)], dim=1)
+            elif base == "linear_attn.conv_weight":
+                full = torch.cat([torch.cat([t[j * kd:(j + 1) * kd] if j < 2 else t[2 * kd:2 * kd + vd] for t in ts], 0)
+                                  for j in range(3)], dim=0)
+            elif leaf.endswith(".weight_fp8"):
+                full = torch.cat(ts, dim=1)  # [in, out / t] pieces: column-parallel, cut by output
+            elif base in ("linear_attn.in_proj_b", "linear_attn.in_proj_a", "linear_attn.A_log", "linear_attn.dt_bias"):
+                full = torch.cat(ts, dim=0)
+            else:
+                full = ts[0]  # norms and KV-cache scales are the same on every rank
+            out[dst + base] = _e5m2_to_e4m3(full, dst + base) if leaf.endswith(".weight_fp8") else full
+        return out
+
+    return layer
