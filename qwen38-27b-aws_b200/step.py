@@ -559,10 +559,11 @@ class B200Head:
         k = recheck_groups or 4
         with torch.cuda.device(self.device):
             if self._tokens is None:
-                z = lambda *sh, dt: torch.zeros(*sh, dtype=dt, device=self.device)  # noqa: E731
-                self._tokens = z(self.batch, dt=torch.int32)
-                self._slot_logits = z(self.batch, 8, dt=torch.float32)
-                self._slot_tokens = z(self.batch, 8, dt=torch.int32)
+                self._tokens = torch.zeros(self.batch, dtype=torch.int32, device=self.device)
+                self._slots = {}
+            if k not in self._slots:  # contiguous per-candidate buffers, for the cross-rank max
+                self._slots[k] = (torch.zeros(self.batch, k, dtype=torch.float32, device=self.device),
+                                  torch.zeros(self.batch, k, dtype=torch.int32, device=self.device))
             self.hidden.zero_()
             self.hidden[:rows].copy_(hidden.reshape(rows, -1), non_blocking=True)
             maxima = self.maxima_device()
@@ -570,7 +571,7 @@ class B200Head:
             if self.tp == 1:
                 ops.lm_head_recheck(self.hidden, self.norm_w, eps, maxima, self.lm_head, 0, k, tokens=self._tokens)
             else:
-                logits, toks = self._slot_logits[:, :k], self._slot_tokens[:, :k]
+                logits, toks = self._slots[k]
                 ops.lm_head_recheck(self.hidden, self.norm_w, eps, maxima, self.lm_head, self.rank * self.vocab_local, k,
                                     slot_logits=logits, slot_tokens=toks)
                 # Each candidate slot is scored on the one rank holding its group; -inf / -1 elsewhere.

@@ -50,7 +50,10 @@ def _source(rcheckpoint, head, table):
                                    rcheckpoint.EMBED_TOKENS: table})
 
 
-SESSIONS = [[[5, 17, 42, 99, 3, 8, 8, 1], [64, 2, 2, 90]], [[11] * 20 + [7, 3]], [[1, 2, 3]], [[100, 50, 25, 12, 6]]]
+# Multi-turn sessions whose next turn extends the last prompt, as an agent's conversation does: the slot's
+# saved states at the end of a prompt are restored and only the extension is prefilled (scheduler.py:116-135).
+SESSIONS = [[[5, 17, 42, 99, 3, 8, 8, 1], [5, 17, 42, 99, 3, 8, 8, 1, 64, 2, 2, 90]], [[11] * 20 + [7, 3]], [[1, 2, 3]],
+            [[100, 50, 25, 12, 6], [100, 50, 25, 12, 6, 31, 30, 29, 28, 27, 26, 25, 24, 23, 22, 21, 20, 19, 18]]]
 
 
 def test_reference_scheduler_with_mtp_speculation_drives_b200_like_the_oracle(pkg):
