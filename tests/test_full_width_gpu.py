@@ -19,7 +19,8 @@ ChipHead tokens. Checks per step:
   same maxima, and the reference's tokens on the reference's hidden state.
 * Greedy tokens end to end (B200Step, B200Head.next_tokens): identical to the
   reference's, except where the reference's best two candidates are a near tie under the measured
-  spread (their logit gap below 3x the largest move of either logit under reordering). Step 1 takes the
+  spread (their logit gap below 3x the largest move, over the step's rows, of those logits under the
+  reordering). Step 1 takes the
   reference's tokens (teacher forcing), so one differing row cannot change the others.
 """
 
@@ -87,16 +88,21 @@ def test_full_width_greedy_tokens_top4_and_hidden_match_reference(pkg, fixture):
         # Greedy tokens end to end.
         got_tokens = bhead.next_tokens(y_gpu)
         assert got_tokens == om.recheck_tokens(cfg, y_gpu, norm_w, lm_rows, bhead.run_graph(y_gpu)), "device vs host recheck"
+        # How far the reordering moves the logits of the reference's and the GPU's tokens, over all rows of the
+        # step (the same statistic as the hidden-state bound: the spread is a property of the arithmetic).
+        moves = []
+        for row, (g, want) in enumerate(zip(got_tokens, want_tokens)):
+            ref_l = _logits(cfg, y_ref, norm_w, lm_rows, row, (want, g))
+            alt_l = _logits(cfg, y_alt, norm_w, lm_rows, row, (want, g))
+            moves.append(max(abs(a - b) for a, b in zip(ref_l, alt_l)))
         for row, (g, want) in enumerate(zip(got_tokens, want_tokens)):
             if g == want:
                 exact += 1
                 continue
             ref_l = _logits(cfg, y_ref, norm_w, lm_rows, row, (want, g))
-            alt_l = _logits(cfg, y_alt, norm_w, lm_rows, row, (want, g))
             gap = ref_l[0] - ref_l[1]
-            move = max(abs(a - b) for a, b in zip(ref_l, alt_l))
-            near_ties.append((s, row, gap, move))
-            assert gap <= 3 * move, (f"step {s} row {row}: token {g} instead of {want}, logit gap {gap:.4g} against "
-                                     f"a reordering move of {move:.4g}")
+            near_ties.append((s, row, round(gap, 4), round(max(moves), 4)))
+            assert gap <= 3 * max(moves), (f"step {s} row {row}: token {g} instead of {want}, logit gap {gap:.4g} against "
+                                           f"a reordering move of up to {max(moves):.4g}")
     total = int(meta["steps"]) * batch
     print(f"full-width greedy tokens: {exact} of {total} identical; near ties {near_ties}")
