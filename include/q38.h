@@ -351,13 +351,14 @@ int q38_comm_destroy(q38_comm_t comm);
 
 /*
  * x += all_reduce(bf16(e5m2(x_q) @ W^T)) over the communicator's ranks, in one kernel per rank. Each
- * token row of the output has an owner rank (row % world), so every CTA reduces 1/world of the rows of
- * its own tile: the other ranks push their bf16 partial of the row into the owner's `part` slot over
- * NVLink as 64-bit words {two bf16, the call's epoch}, so a word's arrival is its own ready flag (no
- * fences, no separate flags). The owner polls its slots, sums the partials in rank order (fp32, one
- * bf16 rounding), adds the residual (bf16) and pushes the new row the same way into every rank's
- * `result` slot, from which each rank writes its own x. The epoch advances on the device (last CTA of
- * the call), and slots alternate by epoch parity, so calls replay inside CUDA graphs.
+ * token row of the output has an owner rank that sums every rank's bf16 partial of it in rank order
+ * (fp32, one bf16 rounding) and adds the residual (bf16). With 2 ranks both own every row: each pushes
+ * its whole partial into the other's `part` slot over NVLink and both reduce (one crossing, no result
+ * traffic). With more, row t is owned by rank t % world: the others push their partials of it to the
+ * owner, which writes the new row into every rank's x directly. Data moves as plain 16-byte stores; a CTA
+ * publishes each step with a system-scope release of the call's epoch into a per-CTA flag at the
+ * receiver, which acquires it before reading. The epoch advances on the device (last CTA of the call)
+ * and slots alternate by epoch parity, so calls replay inside CUDA graphs.
  * Every rank makes the same sequence of calls. x is the communicator's residual stream (rows 0 .. tokens - 1), so
  * features == hidden. Replaces the row-parallel projection plus all-reduce of o_proj / out_proj /
  * down_proj (qwen38_inf2/model.py:259, :374, :639 with the NxD reduce, neuron.py:9). Needs the whole

@@ -34,14 +34,16 @@ extern "C" int q38_comm_init(int rank, int world, int64_t max_tokens, int64_t hi
     delete c;
     return cuda_status(e, "cudaGetDevice");
   }
-  const size_t words = static_cast<size_t>(max_tokens) * (hidden / 2);  // u64 words of one [tokens][hidden] bf16 slab
+  const size_t slab = 2 * static_cast<size_t>(max_tokens) * hidden;  // bytes of one [tokens][hidden] bf16 slab
   size_t off = 0;
   c->off_x = off;
-  off = align256(off + 2 * static_cast<size_t>(max_tokens) * hidden);
+  off = align256(off + slab);
   c->off_part = off;
-  off = align256(off + 8 * 2 * static_cast<size_t>(world) * words);
-  c->off_result = off;
-  off = align256(off + 8 * 2 * words);
+  off = align256(off + 2 * static_cast<size_t>(world) * slab);
+  c->off_pflag = off;
+  off = align256(off + sizeof(uint32_t) * world * q38::kMaxCtas);
+  c->off_rflag = off;
+  off = align256(off + sizeof(uint32_t) * world * q38::kMaxCtas);
   c->off_epoch = off;
   c->off_done = off + sizeof(uint32_t);
   c->bytes = align256(off + 2 * sizeof(uint32_t));
@@ -51,7 +53,7 @@ extern "C" int q38_comm_init(int rank, int world, int64_t max_tokens, int64_t hi
     return cuda_status(e, "cudaMalloc(comm region)");
   }
   e = cudaMemset(c->base, 0, c->bytes);
-  const uint32_t one = 1;  // epochs start at 1: the zeroed words carry epoch 0
+  const uint32_t one = 1;  // epochs start at 1: the zeroed flags hold epoch 0
   if (e == cudaSuccess) e = cudaMemcpy(c->base + c->off_epoch, &one, sizeof(one), cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
     cudaFree(c->base);

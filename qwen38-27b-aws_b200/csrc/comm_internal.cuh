@@ -2,17 +2,20 @@
 // communicator's C ABI (comm.cu).
 //
 // Each rank allocates one region with cudaMalloc and maps every peer's region through CUDA IPC (over
-// NVLink peer access), so a kernel can store straight into a peer's HBM. Everything that crosses
-// NVLink travels as 64-bit words {two bf16 values, the call's epoch}: an aligned 64-bit store arrives
-// whole, so a receiver polling its own memory sees data and "ready" together, with no fence and no
-// separate flag (a system-scope fence costs ~10 us on B200; this is the low-latency form of NCCL's LL
-// protocol). Layout (same offsets on every rank), by epoch parity so a rank one call ahead never
-// overwrites words still being read:
-//   x       bf16 [max_tokens][hidden]                 the residual stream, replicated on every rank
-//   part    u64  [2][world][max_tokens][hidden / 2]   partials pushed to this rank (the owner) by each source
-//   result  u64  [2][max_tokens][hidden / 2]          reduced rows pushed to this rank by their owners
-//   epoch   u32                                       the call counter, advanced by the last CTA of a call
-//   done    u32                                       CTAs finished in the current call
+// NVLink peer access), so a kernel can store straight into a peer's HBM. Data crosses NVLink as plain
+// bf16 rows (16-byte stores); each CTA that has pushed rows to a rank then publishes the call's epoch in
+// a flag of its own there (a system-scope release after its stores), and the receiving CTA (the same
+// grid position on that rank) acquires it before reading. Layout (same offsets on every rank):
+//   x       bf16 [max_tokens][hidden]               the residual stream; owners write their reduced rows
+//                                                   straight into every rank's x
+//   part    bf16 [2][world][max_tokens][hidden]     partials pushed to this rank by each source, by the
+//                                                   call's parity (a rank runs at most one call ahead)
+//   pflag   u32  [world][kMaxCtas]                  per source rank and CTA: the last call whose partials
+//                                                   it has pushed here
+//   rflag   u32  [world][kMaxCtas]                  per owner rank and CTA: the last call whose reduced
+//                                                   rows it has written into this rank's x
+//   epoch   u32                                     the call counter, advanced by the last CTA of a call
+//   done    u32                                     CTAs finished in the current call
 #pragma once
 
 #include <stdint.h>
@@ -22,14 +25,16 @@
 namespace q38 {
 
 constexpr int kMaxRanks = 8;
+constexpr int kMaxCtas = 16384;  // CTAs of one fused GEMM + all-reduce launch
 
 struct ArArgs {
   int rank, world;
   int ftiles;  // 128-feature tiles of hidden
   int64_t tmax, hidden;
   __nv_bfloat16* x[kMaxRanks];
-  unsigned long long* part[kMaxRanks];
-  unsigned long long* result[kMaxRanks];
+  __nv_bfloat16* part[kMaxRanks];
+  uint32_t* pflag[kMaxRanks];
+  uint32_t* rflag[kMaxRanks];
   uint32_t* epoch;  // this rank's
   uint32_t* done;   // this rank's
 };
@@ -41,7 +46,7 @@ namespace q38host {
 struct Comm {
   int rank = 0, world = 0, device = 0;
   int64_t tmax = 0, hidden = 0;
-  size_t off_x = 0, off_part = 0, off_result = 0, off_epoch = 0, off_done = 0, bytes = 0;
+  size_t off_x = 0, off_part = 0, off_pflag = 0, off_rflag = 0, off_epoch = 0, off_done = 0, bytes = 0;
   uint8_t* base = nullptr;                     // this rank's region
   uint8_t* peer[q38::kMaxRanks] = {nullptr};  // every rank's region as mapped here (peer[rank] == base)
   bool connected = false;
@@ -57,8 +62,9 @@ inline q38::ArArgs ar_args(const Comm& c) {
   a.hidden = c.hidden;
   for (int r = 0; r < c.world; ++r) {
     a.x[r] = reinterpret_cast<__nv_bfloat16*>(c.peer[r] + c.off_x);
-    a.part[r] = reinterpret_cast<unsigned long long*>(c.peer[r] + c.off_part);
-    a.result[r] = reinterpret_cast<unsigned long long*>(c.peer[r] + c.off_result);
+    a.part[r] = reinterpret_cast<__nv_bfloat16*>(c.peer[r] + c.off_part);
+    a.pflag[r] = reinterpret_cast<uint32_t*>(c.peer[r] + c.off_pflag);
+    a.rflag[r] = reinterpret_cast<uint32_t*>(c.peer[r] + c.off_rflag);
   }
   a.epoch = reinterpret_cast<uint32_t*>(c.base + c.off_epoch);
   a.done = reinterpret_cast<uint32_t*>(c.base + c.off_done);

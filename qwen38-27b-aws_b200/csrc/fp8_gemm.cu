@@ -94,38 +94,50 @@ __device__ __forceinline__ bool epi_bar_or(bool pred) {
   return r != 0;
 }
 
-// Peer-memory exchange of the fused all-reduce: 64-bit words {two bf16, epoch}, stored whole over
-// NVLink and polled by the receiver in its own memory (an aligned 64-bit access is single-copy
-// atomic), so nothing needs a fence or a separate flag.
-__device__ __forceinline__ unsigned long long word(uint32_t bits, uint32_t epoch) {
-  return (static_cast<unsigned long long>(epoch) << 32) | bits;
+// Peer-memory exchange of the fused all-reduce: rows go across NVLink as plain bf16 16-byte stores;
+// a CTA publishes "my rows for call `epoch` are there" with a release store of the epoch into a flag at
+// the receiving rank, after a system-scope fence by every thread that stored, and the receiver acquires
+// the flag before it reads. Epochs only grow (a rank runs at most one call ahead), so a flag is ready once
+// it is at least the call's epoch.
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-// Two words (four bf16) in one 16-byte store; each 8-byte element is a single-copy atomic access.
-__device__ __forceinline__ void st_words2(unsigned long long* p, uint2 bits, uint32_t epoch) {
-  asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(word(bits.x, epoch)), "l"(word(bits.y, epoch))
-               : "memory");
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
-__device__ __forceinline__ void ld_words2(const unsigned long long* p, unsigned long long& a, unsigned long long& b) {
-  asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
-}
-// The two words (four bf16) at p once both carry `epoch`; false if that takes longer than the wait limit
-// (recorded in the device error word).
-__device__ __forceinline__ bool poll_words2(const unsigned long long* p, uint32_t epoch, uint2& out) {
-  unsigned long long a, b;
-  ld_words2(p, a, b);
-  if (static_cast<uint32_t>(a >> 32) != epoch || static_cast<uint32_t>(b >> 32) != epoch) {
-    const unsigned long long t0 = global_ns();
-    do {
-      if (global_ns() - t0 > kWaitLimitNs) {
-        record_error(Q38_ERR_TIMEOUT);
-        return false;
-      }
-      __nanosleep(32);
-      ld_words2(p, a, b);
-    } while (static_cast<uint32_t>(a >> 32) != epoch || static_cast<uint32_t>(b >> 32) != epoch);
+// Waits until *flag has reached `epoch`; false if that takes longer than the wait limit (recorded in the
+// device error word).
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch) {
+  if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+  const unsigned long long t0 = global_ns();
+  for (;;) {
+    __nanosleep(64);
+    if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      record_error(Q38_ERR_TIMEOUT);
+      return false;
+    }
   }
-  out = make_uint2(static_cast<uint32_t>(a), static_cast<uint32_t>(b));
-  return true;
+}
+__device__ __forceinline__ uint4 add_rows_bf16(const uint4 (&v)[kMaxRanks], int n, const uint4 xr) {
+  // bf16(x + bf16(sum of the n partials in rank order, fp32)) for 8 values
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int src = 0; src < kMaxRanks; ++src) {
+    if (src >= n) break;
+    const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v[src]);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], __bfloat162float(h[e]));
+  }
+  const __nv_bfloat16* xh = reinterpret_cast<const __nv_bfloat16*>(&xr);
+  uint4 o;
+  __nv_bfloat16* oh = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+  for (int e = 0; e < 8; ++e) oh[e] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(xh[e]), bf16r(acc[e])));
+  return o;
 }
 
 // Applies the bf16 (or bf16 + residual) epilogue to 16 consecutive tokens of one feature row.
@@ -533,110 +545,73 @@ __global__ void __launch_bounds__(192, 1)
         bulk_wait_read0();
       }
     }
-    // Fused all-reduce of the staged bf16 partial. Every token row of the output has an owner rank,
-    // t % world, so every CTA owns 1/world of its own slice and the reduction is spread over all CTAs
-    // of every rank. Warp w of the epilogue takes the slice's rows w, w + 4, ...; lane l their features
-    // 4l .. 4l + 3. A row's owner sums every rank's partial in rank order (fp32, one bf16 rounding),
-    // adds the residual and pushes the new row to every other rank; the other ranks push their partial
-    // of the row to the owner and take the owner's result. Polls are batched: a lane issues the loads of
-    // several rows (and of every source) before it checks any of them, so one round trip covers many.
+    // Fused all-reduce of the staged bf16 partial, over this CTA's slice of rows [tb0, tb1) x its 128
+    // features. Every row has an owner rank that sums every rank's partial of it in rank order (fp32, one
+    // bf16 rounding), adds the residual and writes the new row into every rank's residual stream. With two
+    // ranks every rank owns every row ("one shot": each pushes its whole partial to the other and both
+    // reduce, one crossing of NVLink, no result traffic); with more, row t is owned by rank t % world (each
+    // rank pushes (world - 1) / world of its partial and writes 1 / world of the results to each peer: a
+    // quarter of the one-shot bytes at 8 ranks). Thread i of the 128 takes the 16-byte pieces
+    // (row i / 16 + 8 j, features 8 (i % 16) ..), so a row's 256 bytes go out as one contiguous run.
     if (warp >= 2 && a.epilogue == EPI_ALLREDUCE) {
       const bool failed = epi_bar_or(flags[0] != 0);  // also: the staged partial is complete
       const ArArgs& r = a.ar;
+      const int te = threadIdx.x - 64;
       const uint32_t ep = *reinterpret_cast<volatile uint32_t*>(r.epoch);
       const int64_t par = static_cast<int64_t>(ep & 1u);
+      const int cta = static_cast<int>(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
+      const bool one_shot = r.world == 2;
       const __nv_bfloat16* sbase = reinterpret_cast<const __nv_bfloat16*>(stage);
       const int tb0 = n0 + b0 * TOK_BLOCK;            // first token of the slice
       const int tb1 = min(a.T, n0 + b1 * TOK_BLOCK);  // one past the last
-      const int64_t hw = r.hidden / 2;                // words per row
-      const int f = m0 + lane * 4;                    // this lane's four features
-      const int first = tb0 + (warp - 2);             // this warp's rows: first, first + 4, ...
-      constexpr int RSTEP = 4;
-      bool bad = false;
-      if (live && !failed && f < a.F) {
-        auto partial = [&](int t) { return *reinterpret_cast<const uint2*>(sbase + (t - n0) * BM + (f - m0)); };
-        auto part_word = [&](int owner, int src, int t) {
-          return r.part[owner] + ((par * r.world + src) * r.tmax + t) * hw + f / 2;
-        };
-        // 1. Rows owned elsewhere: this rank's partial to the owner.
-        for (int t = first; t < tb1; t += RSTEP) {
-          const int owner = t % r.world;
-          if (owner != r.rank) st_words2(part_word(owner, r.rank, t), partial(t), ep);
-        }
-        // 2. Owned rows, UB at a time: every source's words loaded before any is checked.
-        constexpr int UB = 2;
-        for (int t = first; t < tb1 && !bad;) {
-          int rows[UB];
-          int n = 0;
-          for (; t < tb1 && n < UB; t += RSTEP)
-            if (t % r.world == r.rank) rows[n++] = t;
-          if (n == 0) break;
-          unsigned long long lo[UB][kMaxRanks], hi[UB][kMaxRanks];
-#pragma unroll
-          for (int j = 0; j < UB; ++j)
-#pragma unroll
-            for (int src = 0; src < kMaxRanks; ++src)
-              if (j < n && src < r.world && src != r.rank) ld_words2(part_word(r.rank, src, rows[j]), lo[j][src], hi[j][src]);
-#pragma unroll
-          for (int j = 0; j < UB; ++j) {
-            if (j >= n || bad) break;
-            const int t = rows[j];
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int src = 0; src < kMaxRanks; ++src) {
-              if (src >= r.world) break;
-              uint2 u;
-              if (src == r.rank) {
-                u = partial(t);
-              } else if (static_cast<uint32_t>(lo[j][src] >> 32) == ep && static_cast<uint32_t>(hi[j][src] >> 32) == ep) {
-                u = make_uint2(static_cast<uint32_t>(lo[j][src]), static_cast<uint32_t>(hi[j][src]));
-              } else if (!poll_words2(part_word(r.rank, src, t), ep, u)) {
-                bad = true;
-                break;
-              }
-              const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) acc[e] = __fadd_rn(acc[e], __bfloat162float(h[e]));
-            }
-            if (bad) break;
-            const int64_t at = static_cast<int64_t>(t) * r.hidden + f;
-            const uint2 xu = *reinterpret_cast<const uint2*>(r.x[r.rank] + at);
-            const __nv_bfloat16* xh = reinterpret_cast<const __nv_bfloat16*>(&xu);
-            uint2 ou;
-            __nv_bfloat16* oh = reinterpret_cast<__nv_bfloat16*>(&ou);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) oh[e] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(xh[e]), bf16r(acc[e])));
-            *reinterpret_cast<uint2*>(r.x[r.rank] + at) = ou;
+      const int f = m0 + (te & 15) * 8;               // this thread's eight features
+      const int first = tb0 + (te >> 4);              // its rows: first, first + 8, ...
+      constexpr int RSTEP = 8;
+      const int64_t H = r.hidden;
+      const bool mine_f = live && f < a.F;
+      auto owns = [&](int rank, int t) { return one_shot || t % r.world == rank; };
+      auto staged = [&](int t) { return *reinterpret_cast<const uint4*>(sbase + (t - n0) * BM + (f - m0)); };
+      auto slot = [&](int owner, int src, int t) {
+        return r.part[owner] + ((par * r.world + src) * r.tmax + t) * H + f;
+      };
+      bool bad = failed || !live;
+      // 1. This rank's partial of every row another rank owns, to that rank; then the flags.
+      if (!bad) {
+        if (mine_f)
+          for (int t = first; t < tb1; t += RSTEP) {
+            const uint4 v = staged(t);
             for (int dq = 0; dq < r.world; ++dq)
-              if (dq != r.rank) st_words2(r.result[dq] + (par * r.tmax + t) * hw + f / 2, ou, ep);
+              if (dq != r.rank && owns(dq, t)) *reinterpret_cast<uint4*>(slot(dq, r.rank, t)) = v;
           }
-        }
-        // 3. Rows owned elsewhere, UC at a time: the owners' results into this rank's residual stream.
-        constexpr int UC = 8;
-        const unsigned long long* res = r.result[r.rank] + par * r.tmax * hw + f / 2;
-        for (int t = first; t < tb1 && !bad;) {
-          int rows[UC];
-          int n = 0;
-          for (; t < tb1 && n < UC; t += RSTEP)
-            if (t % r.world != r.rank) rows[n++] = t;
-          if (n == 0) break;
-          unsigned long long lo[UC], hi[UC];
+        fence_sys();
+      }
+      bad = epi_bar_or(bad);
+      if (!bad && te < r.world && te != r.rank) st_release_sys(r.pflag[te] + r.rank * kMaxCtas + cta, ep);
+      // 2. The rows this rank owns: every source's partial (acquired through its flag), summed in rank
+      //    order, plus the residual; into this rank's x and, for rows others do not own, into theirs.
+      if (!bad && te < r.world && te != r.rank) bad = !wait_flag(r.pflag[r.rank] + te * kMaxCtas + cta, ep);
+      bad = epi_bar_or(bad);
+      if (!bad && mine_f) {
+        for (int t = first; t < tb1; t += RSTEP) {
+          if (!owns(r.rank, t)) continue;
+          uint4 v[kMaxRanks];
 #pragma unroll
-          for (int j = 0; j < UC; ++j)
-            if (j < n) ld_words2(res + static_cast<int64_t>(rows[j]) * hw, lo[j], hi[j]);
-#pragma unroll
-          for (int j = 0; j < UC; ++j) {
-            if (j >= n) break;
-            uint2 u;
-            if (static_cast<uint32_t>(lo[j] >> 32) == ep && static_cast<uint32_t>(hi[j] >> 32) == ep) {
-              u = make_uint2(static_cast<uint32_t>(lo[j]), static_cast<uint32_t>(hi[j]));
-            } else if (!poll_words2(res + static_cast<int64_t>(rows[j]) * hw, ep, u)) {
-              bad = true;
-              break;
-            }
-            *reinterpret_cast<uint2*>(r.x[r.rank] + static_cast<int64_t>(rows[j]) * r.hidden + f) = u;
-          }
+          for (int src = 0; src < kMaxRanks; ++src)
+            if (src < r.world) v[src] = src == r.rank ? staged(t) : __ldcg(reinterpret_cast<const uint4*>(slot(r.rank, src, t)));
+          const int64_t at = static_cast<int64_t>(t) * H + f;
+          const uint4 o = add_rows_bf16(v, r.world, *reinterpret_cast<const uint4*>(r.x[r.rank] + at));
+          *reinterpret_cast<uint4*>(r.x[r.rank] + at) = o;
+          if (!one_shot)
+            for (int dq = 0; dq < r.world; ++dq)
+              if (dq != r.rank) *reinterpret_cast<uint4*>(r.x[dq] + at) = o;
         }
+      }
+      if (!one_shot) {
+        // 3. The other owners' rows of this slice have arrived in this rank's x once their flags have.
+        if (!bad) fence_sys();
+        bad = epi_bar_or(bad);
+        if (!bad && te < r.world && te != r.rank) st_release_sys(r.rflag[te] + r.rank * kMaxCtas + cta, ep);
+        if (!bad && te < r.world && te != r.rank) bad = !wait_flag(r.rflag[r.rank] + te * kMaxCtas + cta, ep);
       }
       epi_bar_or(bad);
     }
@@ -1171,6 +1146,11 @@ int gemm_fp8(const void* x, int64_t tokens, int64_t k, const void* w, const void
   if (st != Q38_OK) return st;
   if (a.cluster == 0) ty = tr = tx;
   const bool resident = ar != nullptr;
+  // The exchange's flags hold one slot per CTA of the launch (the 2-SM form rounds the tiles up to pairs).
+  if (ar && 2 * cdiv(features, 2 * BM) * cdiv(tokens, ntok) * splits > kMaxCtas)
+    return set_error("%s: %lld tokens x %lld features x %d splits need more than %d CTAs", who, (long long)tokens,
+                     (long long)features, splits, kMaxCtas),
+           Q38_ERR_UNSUPPORTED;
   // Unsplit bf16 outputs take the persistent tile loop.
   const bool persistent = ar == nullptr && epilogue == Q38_EPI_BF16 && a.cluster == 1;
   // The 2-SM form for full 256-token tiles whose cluster (2 x splits) stays portable.

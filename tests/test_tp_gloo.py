@@ -55,7 +55,7 @@ def _run(rank, world, port, wide, out_q):
         cos, sin = om.rotary(cfg, torch.tensor([pos, pos + 3]), torch.float32)
         outs.append(step(inputs_embeds=x, cos=cos.unsqueeze(1), sin=sin.unsqueeze(1),
                          position=torch.tensor([pos, pos + 3], dtype=torch.int32), active=torch.ones(2)))
-    out_q.put((rank, torch.stack(outs)))
+    out_q.put((rank, torch.stack(outs).numpy()))  # by value: the worker may exit before the parent reads
     dist.destroy_process_group()
 
 
@@ -81,7 +81,7 @@ def test_tensor_parallel_ranks_match_single_rank(pkg, world, wide):
     procs = [ctx.Process(target=_run, args=(r, world, port, wide, q)) for r in range(world)]
     for p in procs:
         p.start()
-    results = dict(q.get(timeout=300) for _ in range(world))
+    results = {r: torch.from_numpy(a) for r, a in (q.get(timeout=300) for _ in range(world))}
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
