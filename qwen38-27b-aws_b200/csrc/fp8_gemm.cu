@@ -94,12 +94,11 @@ __device__ __forceinline__ bool epi_bar_or(bool pred) {
   return r != 0;
 }
 
-// Peer-memory exchange of the fused all-reduce: rows go across NVLink as plain bf16 16-byte stores;
-// a CTA publishes "my rows for call `epoch` are there" with a release store of the epoch into a flag at
-// the receiving rank, after a system-scope fence by every thread that stored, and the receiver acquires
-// the flag before it reads. Epochs only grow (a rank runs at most one call ahead), so a flag is ready once
-// it is at least the call's epoch.
-__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+// Peer-memory exchange of the fused all-reduce: rows go across NVLink as bulk copies (shared memory ->
+// the peer's HBM, moved by the SM's TMA unit, off its load/store path); a CTA publishes "my rows for call `epoch` are
+// there" once its copies are complete, by a barrier and a system-scope release store of the epoch into a
+// flag at the receiving rank, and the receiver acquires the flag before it reads. Epochs only grow (a
+// rank runs at most one call ahead), so a flag is ready once it is at least the call's epoch.
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
@@ -122,12 +121,12 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch) 
     }
   }
 }
-__device__ __forceinline__ uint4 add_rows_bf16(const uint4 (&v)[kMaxRanks], int n, const uint4 xr) {
-  // bf16(x + bf16(sum of the n partials in rank order, fp32)) for 8 values
+template <int W>
+__device__ __forceinline__ uint4 add_rows_bf16(const uint4 (&v)[W], const uint4 xr) {
+  // bf16(x + bf16(sum of the W partials in rank order, fp32)) for 8 values
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int src = 0; src < kMaxRanks; ++src) {
-    if (src >= n) break;
+  for (int src = 0; src < W; ++src) {
     const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v[src]);
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc[e] = __fadd_rn(acc[e], __bfloat162float(h[e]));
@@ -138,6 +137,60 @@ __device__ __forceinline__ uint4 add_rows_bf16(const uint4 (&v)[kMaxRanks], int 
 #pragma unroll
   for (int e = 0; e < 8; ++e) oh[e] = __float2bfloat16_rn(__fadd_rn(__bfloat162float(xh[e]), bf16r(acc[e])));
   return o;
+}
+
+// Sends this rank's staged bf16 partial of token row t (the tile's 128 features, 256 bytes of shared
+// memory) to every other rank that owns the row (with two ranks: the other one), into its receive
+// slot for this rank at the call's epoch parity, by a bulk copy: the TMA unit moves it over NVLink
+// while the threads go on. The issuing thread completes its copies with bulk_commit + bulk_wait0.
+__device__ __forceinline__ void push_row(const ArArgs& r, int64_t par, int t, int m0, const __nv_bfloat16* row) {
+  for (int dq = 0; dq < r.world; ++dq)
+    if (dq != r.rank && (r.world == 2 || t % r.world == dq))
+      bulk_store(r.part[dq] + ((par * r.world + r.rank) * r.tmax + t) * r.hidden + m0, row, BM * 2);
+}
+
+// Phase 2 of the fused all-reduce for one thread: the rows of [t_begin, t1) that this rank owns (every
+// row with two ranks, t % W == rank above), spread over the 8 row lanes of the 128 threads (this
+// thread: owned rows row_lane, row_lane + 8, ...), features f .. f + 7. Every source's partial (this
+// rank's from the staging tile `sbase`, the others' from this rank's receive slots) is summed in rank
+// order, added to the residual, and written to this rank's x and, above two ranks, back into the
+// staging tile (over this rank's partial of the row), from where bulk copies take it to every peer's
+// x. The loads of U rows are all issued before the first sum: the step is latency-bound otherwise.
+template <int W>
+__device__ __forceinline__ void reduce_owned_rows(const ArArgs& r, __nv_bfloat16* sbase, int n0, int m0, int f,
+                                                  int t_begin, int row_lane, int t1, int64_t par) {
+  constexpr int U = W >= 8 ? 2 : (W >= 4 ? 4 : 8);
+  const int64_t H = r.hidden;
+  const bool one_shot = W == 2;
+  const int stride = one_shot ? 1 : W;                                          // between owned rows
+  const int base = one_shot ? t_begin : t_begin + ((r.rank - t_begin % W) + W) % W;  // first owned row
+  const int t0 = base + row_lane * stride;
+  const int tstep = 8 * stride;
+  for (int tb = t0; tb < t1; tb += U * tstep) {
+    uint4 v[U][W];
+    uint4 xr[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = tb + u * tstep;
+      if (t < t1) {
+#pragma unroll
+        for (int src = 0; src < W; ++src)
+          v[u][src] = src == r.rank ? *reinterpret_cast<const uint4*>(sbase + (t - n0) * BM + (f - m0))
+                                    : __ldcg(reinterpret_cast<const uint4*>(
+                                          r.part[r.rank] + ((par * W + src) * r.tmax + t) * H + f));
+        xr[u] = *reinterpret_cast<const uint4*>(r.x[r.rank] + static_cast<int64_t>(t) * H + f);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int t = tb + u * tstep;
+      if (t >= t1) break;
+      const uint4 o = add_rows_bf16<W>(v[u], xr[u]);
+      const int64_t at = static_cast<int64_t>(t) * H + f;
+      *reinterpret_cast<uint4*>(r.x[r.rank] + at) = o;
+      if (!one_shot) *reinterpret_cast<uint4*>(sbase + (t - n0) * BM + (f - m0)) = o;
+    }
+  }
 }
 
 // Applies the bf16 (or bf16 + residual) epilogue to 16 consecutive tokens of one feature row.
@@ -468,6 +521,10 @@ __global__ void __launch_bounds__(192, 1)
         constexpr int U = 8, NW = 4, SB = 4;
         const int t0 = n0 + b0 * TOK_BLOCK;
         const int t1 = min(a.T, n0 + b1 * TOK_BLOCK);
+        // A fused all-reduce sends each reduced row to the rank that owns it at once, so the NVLink
+        // transfer runs under the rest of the reduction (slots of this call's epoch parity).
+        const int64_t par =
+            a.epilogue == EPI_ALLREDUCE ? static_cast<int64_t>(*reinterpret_cast<volatile uint32_t*>(a.ar.epoch) & 1u) : 0;
         const bool ok = a.epilogue != EPI_RESIDUAL || t0 >= t1 || !live || mbar_wait(resbar, 0);
         if (!ok) flags[0] = 1;
         const uint32_t part0 = smem_u32(smem) + static_cast<uint32_t>(4 * lane * 4);
@@ -531,6 +588,14 @@ __global__ void __launch_bounds__(192, 1)
               o[j] = __float2bfloat16_rn(out);
             }
           }
+          if (a.epilogue == EPI_ALLREDUCE) {
+            // This warp's U rows are complete in the staging tile: lane u sends row tb + 4u.
+            fence_proxy_async_shared();
+            __syncwarp();
+            const int t = tb + NW * lane;
+            if (lane < U && t < t1)
+              push_row(a.ar, par, t, m0, reinterpret_cast<const __nv_bfloat16*>(stage) + (t - n0) * BM);
+          }
         }
       }
     }
@@ -561,30 +626,21 @@ __global__ void __launch_bounds__(192, 1)
       const int64_t par = static_cast<int64_t>(ep & 1u);
       const int cta = static_cast<int>(blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z));
       const bool one_shot = r.world == 2;
-      const __nv_bfloat16* sbase = reinterpret_cast<const __nv_bfloat16*>(stage);
+      __nv_bfloat16* sbase = reinterpret_cast<__nv_bfloat16*>(stage);
       const int tb0 = n0 + b0 * TOK_BLOCK;            // first token of the slice
       const int tb1 = min(a.T, n0 + b1 * TOK_BLOCK);  // one past the last
-      const int f = m0 + (te & 15) * 8;               // this thread's eight features
-      const int first = tb0 + (te >> 4);              // its rows: first, first + 8, ...
-      constexpr int RSTEP = 8;
-      const int64_t H = r.hidden;
+      const int f = m0 + (te & 15) * 8;               // this thread's eight features in phase 2
       const bool mine_f = live && f < a.F;
-      auto owns = [&](int rank, int t) { return one_shot || t % r.world == rank; };
-      auto staged = [&](int t) { return *reinterpret_cast<const uint4*>(sbase + (t - n0) * BM + (f - m0)); };
-      auto slot = [&](int owner, int src, int t) {
-        return r.part[owner] + ((par * r.world + src) * r.tmax + t) * H + f;
-      };
       bool bad = failed || !live;
-      // 1. This rank's partial of every row another rank owns, to that rank; then the flags.
-      if (!bad) {
-        if (mine_f)
-          for (int t = first; t < tb1; t += RSTEP) {
-            const uint4 v = staged(t);
-            for (int dq = 0; dq < r.world; ++dq)
-              if (dq != r.rank && owns(dq, t)) *reinterpret_cast<uint4*>(slot(dq, r.rank, t)) = v;
-          }
-        fence_sys();
-      }
+      // 1. This rank's partial of every row another rank owns, to that rank (with split K the split
+      //    reduction has sent them already, row by row): bulk copies of the staged rows, complete before
+      //    the flags go out (a release after the barrier orders every thread's completed copies).
+      if (!bad && a.cluster == 1) fence_proxy_async_shared();
+      bad = epi_bar_or(bad);
+      if (!bad && a.cluster == 1 && warp == 2)
+        for (int t = tb0 + lane; t < tb1; t += 32) push_row(r, par, t, m0, sbase + (t - n0) * BM);
+      bulk_commit();
+      bulk_wait0();
       bad = epi_bar_or(bad);
       if (!bad && te < r.world && te != r.rank) st_release_sys(r.pflag[te] + r.rank * kMaxCtas + cta, ep);
       // 2. The rows this rank owns: every source's partial (acquired through its flag), summed in rank
@@ -592,23 +648,31 @@ __global__ void __launch_bounds__(192, 1)
       if (!bad && te < r.world && te != r.rank) bad = !wait_flag(r.pflag[r.rank] + te * kMaxCtas + cta, ep);
       bad = epi_bar_or(bad);
       if (!bad && mine_f) {
-        for (int t = first; t < tb1; t += RSTEP) {
-          if (!owns(r.rank, t)) continue;
-          uint4 v[kMaxRanks];
-#pragma unroll
-          for (int src = 0; src < kMaxRanks; ++src)
-            if (src < r.world) v[src] = src == r.rank ? staged(t) : __ldcg(reinterpret_cast<const uint4*>(slot(r.rank, src, t)));
-          const int64_t at = static_cast<int64_t>(t) * H + f;
-          const uint4 o = add_rows_bf16(v, r.world, *reinterpret_cast<const uint4*>(r.x[r.rank] + at));
-          *reinterpret_cast<uint4*>(r.x[r.rank] + at) = o;
-          if (!one_shot)
-            for (int dq = 0; dq < r.world; ++dq)
-              if (dq != r.rank) *reinterpret_cast<uint4*>(r.x[dq] + at) = o;
+        switch (r.world) {
+          case 1: reduce_owned_rows<1>(r, sbase, n0, m0, f, tb0, te >> 4, tb1, par); break;
+          case 2: reduce_owned_rows<2>(r, sbase, n0, m0, f, tb0, te >> 4, tb1, par); break;
+          case 3: reduce_owned_rows<3>(r, sbase, n0, m0, f, tb0, te >> 4, tb1, par); break;
+          case 4: reduce_owned_rows<4>(r, sbase, n0, m0, f, tb0, te >> 4, tb1, par); break;
+          case 5: reduce_owned_rows<5>(r, sbase, n0, m0, f, tb0, te >> 4, tb1, par); break;
+          case 6: reduce_owned_rows<6>(r, sbase, n0, m0, f, tb0, te >> 4, tb1, par); break;
+          case 7: reduce_owned_rows<7>(r, sbase, n0, m0, f, tb0, te >> 4, tb1, par); break;
+          default: reduce_owned_rows<8>(r, sbase, n0, m0, f, tb0, te >> 4, tb1, par); break;
         }
       }
       if (!one_shot) {
-        // 3. The other owners' rows of this slice have arrived in this rank's x once their flags have.
-        if (!bad) fence_sys();
+        // 3. This rank's reduced rows of the slice (now in the staging tile) to every other rank's x by
+        //    bulk copies; the other owners' rows have arrived in this rank's x once their flags have.
+        if (!bad) fence_proxy_async_shared();
+        bad = epi_bar_or(bad);
+        if (!bad && warp == 2) {
+          const int W = r.world;
+          const int base = tb0 + ((r.rank - tb0 % W) + W) % W;  // the slice's first row this rank owns
+          for (int t = base + lane * W; t < tb1; t += 32 * W)
+            for (int dq = 0; dq < W; ++dq)
+              if (dq != r.rank) bulk_store(r.x[dq] + static_cast<int64_t>(t) * r.hidden + m0, sbase + (t - n0) * BM, BM * 2);
+        }
+        bulk_commit();
+        bulk_wait0();
         bad = epi_bar_or(bad);
         if (!bad && te < r.world && te != r.rank) st_release_sys(r.rflag[te] + r.rank * kMaxCtas + cta, ep);
         if (!bad && te < r.world && te != r.rank) bad = !wait_flag(r.rflag[r.rank] + te * kMaxCtas + cta, ep);

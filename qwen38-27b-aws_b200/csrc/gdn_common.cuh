@@ -5,11 +5,6 @@
 
 namespace q38 {
 
-__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
-  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_u32(ssrc)),
-               "r"(bytes)
-               : "memory");
-}
 __device__ __forceinline__ void group_bar(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
 
 // CPL consecutive bf16 of a state row, as one vector access when CPL == 4 (8 bytes, conflict-free
