@@ -38,7 +38,10 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 PACKAGE = "qwen38-27b-aws_b200"
-METRIC = "total tokens/s (64-layer decode step incl. lm_head maxima)"
+# BASELINE.json's metric. `value` is its decode half at config 3 (tokens/s of 64-layer decode steps with the
+# lm_head maxima and each row's greedy token); `serve` is prefill + decode together; at N > 1
+# `fused_allreduce` is config 1 (the fused GEMM + all-reduce against its roofline and against NCCL).
+METRIC = "total tokens/s (prefill+decode) at 1/2/4/8 B200; fused GEMM+AR % of roofline"
 MAX_SEQ = 512
 GDN_TRAFFIC_B256 = 777.4e6  # dram__bytes per gdn_decode_kernel launch, batch 256, one GPU (ncu)
 LAYERS = 64
@@ -258,6 +261,13 @@ def run_ours(args, world, rank, local):
     serve_s = max_over_ranks(served.wall_s, world, device)
     del table, embeddings
 
+    # BASELINE config 1 at TP = N: the fused GEMM + all-reduce against its roofline and against NCCL.
+    fused_ar = None
+    if world > 1:
+        fused_ar = {"workload": "BASELINE config 1: down_proj (17408 / t -> 5120) at M rows: plain GEMM, fused GEMM + "
+                                "all-reduce, GEMM + NCCL all-reduce; CUDA graphs of 20 launches, max over ranks",
+                    "rows": allreduce_rows(world, rank, device, (64, 256, 512), (("down_proj", 17408 // world),), 20)}
+
     tokens = B * args.steps
     step_bytes = decode_step_bytes(step, head, pkg.config.LINEAR, positions[args.warmup:])
     line = {
@@ -274,7 +284,8 @@ def run_ours(args, world, rank, local):
         "dtype": "fp8(e4m3 weights x e5m2 activations)+bf16",
         "data": "synthetic (seeded random FP8 weights of the architecture, random cache/state contents)",
         "config": {
-            "workload": "BASELINE config 3: 64-layer decode step, batch %d, 512-position context, rows at positions spread over [0,511)" % B,
+            "workload": "BASELINE config 3: 64-layer decode steps, batch %d, 512-position context, rows at positions "
+                        "spread over [0,511) (the metric's decode half; `serve` has prefill + decode)" % B,
             "global_batch": B,
             "seq_len": MAX_SEQ,
             "parallelism": f"tp{world}",
@@ -324,6 +335,7 @@ def run_ours(args, world, rank, local):
             "prefill_calls": served.prefill_calls,
             "decode_steps": served.decode_steps,
         },
+        "fused_allreduce": fused_ar,
         "clocks": clocks,
         # the step's kernels, then rmsnorm + group maxima + recheck (+ pick with TP > 1)
         "gpu_launches": (step.kernels_per_decode_step() + 3 + (world > 1)) * args.steps,
@@ -704,30 +716,24 @@ def run_micro(args):
 NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool (the profiling recipe's figure)
 
 
-def run_micro_allreduce(args, world, rank, local):
-    """the row-parallel projection at TP = world, alone, at M in {64, 256, 512} rows
-    (or --batch): the plain GEMM, the fused GEMM + all-reduce, and the GEMM followed by an NCCL all-reduce
-    (the baseline), each timed as a CUDA graph of --steps launches, max over ranks. Shapes: down_proj
-    (17408 / world -> 5120) and o_proj (6144 / world -> 5120). Per shape it reports
-    hidden = 1 - (fused - gemm) / (nccl - gemm), the share of the baseline's communication time the
-    fused kernel hides, and the roofline of the fused call: the slowest of its HBM bytes at the measured
-    HBM peak, its FLOPs at the FP8 tensor peak (twice the measured BF16 peak), and the all-reduce's
-    NVLink bytes (2 (t - 1) / t x M x 5120 x 2 per rank, the reduce-scatter + all-gather minimum) at the
-    measured 770 GB/s per direction."""
+def allreduce_rows(world: int, rank: int, device, batches, shapes, steps: int) -> list[dict]:
+    """the row-parallel projection at TP = world, alone, at M rows: the plain GEMM, the
+    fused GEMM + all-reduce, and the GEMM followed by an NCCL all-reduce (the baseline), each timed as a
+    CUDA graph of `steps` launches, max over ranks. Per shape: hidden = 1 - (fused - gemm) / (nccl - gemm),
+    the share of the baseline's communication time the fused kernel hides, and the roofline of the fused
+    call: the slowest of its HBM bytes at the measured HBM peak, its FLOPs at the FP8 tensor peak (twice
+    the measured BF16 peak), and the all-reduce's NVLink bytes (2 (t - 1) / t x M x 5120 x 2 per rank,
+    the reduce-scatter + all-gather minimum) at the measured 770 GB/s per direction."""
     pkg = importlib.import_module(PACKAGE)
     ops = importlib.import_module(f"{PACKAGE}.ops")
-    device = torch.device(f"cuda:{local}")
-    torch.cuda.set_device(device)
-    torch.distributed.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=120))
     H = 5120
-    batches = [args.batch] if args.batch_given else [64, 256, 512]
     comm = ops.Communicator(rank, world, max(max(batches), 512), H, device)
     hbm, _ = peaks()
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     bf16_tf = float(json.loads(peaks_path.read_text())["bf16_tflops"]) if peaks_path.exists() else 1590.0
     rows = []
     for B in batches:
-        for name, k in (("down_proj", 17408 // world), ("o_proj", 6144 // world)):
+        for name, k in shapes:
             g = torch.Generator().manual_seed(rank)
             lin = ops.DeviceLinear(pkg.weights.FP8Weight.from_float(torch.randn(H, k, generator=g) * 0.02), device)
             xq = pkg.codec.to_e5m2_bytes(torch.randn(B, k, generator=g).to(torch.bfloat16)).to(device)
@@ -748,7 +754,7 @@ def run_micro_allreduce(args, world, rank, local):
                 torch.distributed.barrier()
                 graph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(graph):
-                    for _ in range(args.steps):
+                    for _ in range(steps):
                         fn()
                 graph.replay()
                 torch.cuda.synchronize()
@@ -758,7 +764,7 @@ def run_micro_allreduce(args, world, rank, local):
                 graph.replay()
                 ev1.record()
                 torch.cuda.synchronize()
-                t[vname] = max_over_ranks(ev0.elapsed_time(ev1), world, device) * 1e3 / args.steps
+                t[vname] = max_over_ranks(ev0.elapsed_time(ev1), world, device) * 1e3 / steps
                 del graph
                 torch.distributed.barrier()
             hbm_bytes = H * k * 33 // 32 + B * k + 2 * B * H * 2  # weights + scales, x, residual in and out
@@ -774,12 +780,28 @@ def run_micro_allreduce(args, world, rank, local):
                          "roofline_us": round(target, 2), "roofline_bound": max(bounds, key=bounds.get)[:-3],
                          "roofline_frac": round(target / t["fused"], 3),
                          **{key: round(v, 2) for key, v in bounds.items()}})
-    status = ops.device_status()
+    if ops.device_status() != 0:
+        raise RuntimeError(f"device status {ops.device_status()} after the fused all-reduce sweep")
+    comm.close()
+    return rows
+
+
+def run_micro_allreduce(args, world, rank, local):
+    """The config-1 sweep alone (allreduce_rows) at M in {64, 256, 512} rows (or --batch), down_proj
+    (17408 / world -> 5120) and o_proj (6144 / world -> 5120)."""
+    device = torch.device(f"cuda:{local}")
+    torch.cuda.set_device(device)
+    torch.distributed.init_process_group("nccl", device_id=device, timeout=__import__("datetime").timedelta(seconds=120))
+    batches = [args.batch] if args.batch_given else [64, 256, 512]
+    rows = allreduce_rows(world, rank, device, batches, (("down_proj", 17408 // world), ("o_proj", 6144 // world)),
+                          args.steps)
+    hbm, _ = peaks()
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    bf16_tf = float(json.loads(peaks_path.read_text())["bf16_tflops"]) if peaks_path.exists() else 1590.0
     if rank == 0:
-        print(json.dumps({"micro": "gemm_allreduce", "tp": world, "steps": args.steps, "device_status": status,
+        print(json.dumps({"micro": "gemm_allreduce", "tp": world, "steps": args.steps, "device_status": 0,
                           "peaks": {"hbm_gbs": hbm, "fp8_tflops": 2 * bf16_tf, "nvlink_gbs": NVLINK_GBS},
                           "rows": rows}), flush=True)
-    comm.close()
     torch.distributed.destroy_process_group()
 
 
