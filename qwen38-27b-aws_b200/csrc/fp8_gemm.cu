@@ -77,10 +77,34 @@ struct GemmArgs {
   int64_t ldq;
 };
 
-// Epilogue staging (cluster mode), reusing the pipeline buffers once the accumulator is final:
-// fp32 partial [NTOK tokens][128 rows] at 0, then bf16 [NTOK][128] for the residual in and the
-// output out (the same bytes: each element is read before it is overwritten by its own thread).
+// Epilogue staging (cluster mode), reusing the pipeline buffers once the accumulator is final: bf16
+// [NTOK][128] for the residual in and the output out (the same bytes: each element is read before it
+// is overwritten by its own thread), at NTOK * 128 * 4 with one split, over the send buffers below with
+// split K.
 constexpr int TOK_BLOCK = 32;  // tokens per TMA box of the residual / output
+constexpr int BLOCK_F32_BYTES = TOK_BLOCK * BM * 4;  // one token block of a split's fp32 partial: 16 KB
+
+// Split reduction through the cluster (c K splits of one output tile, one CTA each): token block b of
+// the tile belongs to the split CTA whose slice [s nb / c, (s + 1) nb / c) holds it. Shared memory,
+// reusing the pipeline buffers once the mainloops are done: the receive buffer [c - 1 sources][slice
+// tokens][128 rows] fp32 at 0, then this CTA's fp32 partials of the blocks it sends (compact, in block
+// order), over which the bf16 output staging [NTOK][128] later lies.
+template <int NTOK>
+__host__ __device__ constexpr int split_slice_tokens(int c) {
+  return (NTOK / TOK_BLOCK + c - 1) / c * TOK_BLOCK;
+}
+template <int NTOK>
+__host__ __device__ constexpr size_t split_send_offset(int c) {
+  return c > 1 ? static_cast<size_t>(c - 1) * split_slice_tokens<NTOK>(c) * BM * 4 : 0;
+}
+template <int NTOK>
+__host__ __device__ constexpr size_t split_smem_bytes(int c) {
+  // The fewest blocks a split owns is nb / c (rounded down), so it sends at most nb - nb / c.
+  return split_send_offset<NTOK>(c) +
+         (static_cast<size_t>(NTOK / TOK_BLOCK - NTOK / TOK_BLOCK / c) * BLOCK_F32_BYTES > static_cast<size_t>(NTOK) * BM * 2
+              ? static_cast<size_t>(NTOK / TOK_BLOCK - NTOK / TOK_BLOCK / c) * BLOCK_F32_BYTES
+              : static_cast<size_t>(NTOK) * BM * 2);
+}
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 // The epilogue warps' barrier that also returns, to every one of them, whether any passed `pred`.
@@ -226,7 +250,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* empty = full + C::STAGES;
   uint64_t* accf = empty + C::STAGES;
   uint64_t* resbar = accf + 1;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(resbar + 1);
+  uint64_t* redbar = resbar + 1;  // split reduction: the other splits' blocks of this CTA's slice
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(redbar + 1);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_holder + 1);  // [0] abort, [1] last CTA
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -247,6 +272,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     mbar_init(accf, 1);
     mbar_init(resbar, 1);
+    mbar_init(redbar, 1);
     flags[0] = 0;
     flags[1] = 0;
     fence_mbar_init();
@@ -377,9 +403,10 @@ __global__ void __launch_bounds__(192, 1)
     }
     __syncwarp();
   } else if (a.cluster > 0) {
-    // Epilogue part 1. With one split the accumulator goes straight to its bf16 staging; with a
-    // cluster of splits it goes to shared memory as fp32 [token][row] for part 2. The residual tile of
-    // this CTA's token slice starts loading by TMA meanwhile.
+    // Epilogue part 1. With one split the accumulator goes straight to its bf16 staging (the residual
+    // tile loading by TMA meanwhile); with a cluster of splits this CTA arms its reduction barrier for
+    // the blocks of its slice and drains the blocks it sends to their owners, fp32 [token][row], for
+    // part 2.
     const int q = warp & 3;
     const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
     pdl_wait();
@@ -393,10 +420,9 @@ __global__ void __launch_bounds__(192, 1)
     } else {
       fence_proxy_async_shared();
       uint8_t* stage = smem + NTOK * BM * 4;
-      if (a.epilogue == EPI_RESIDUAL && warp == 2 && lane == 0 && m0 < a.F) {
-        const int rank = srank;
+      if (a.epilogue == EPI_RESIDUAL && a.cluster == 1 && warp == 2 && lane == 0 && m0 < a.F) {
         const int nb = NTOK / TOK_BLOCK;
-        const int b0 = rank * nb / a.cluster, b1 = (rank + 1) * nb / a.cluster;
+        const int b0 = 0, b1 = nb;
         int issued = 0;
         for (int b = b0; b < b1; ++b) issued += n0 + b * TOK_BLOCK < a.T;
         mbar_arrive_expect_tx(resbar, issued * TOK_BLOCK * BM * 2);
@@ -405,13 +431,25 @@ __global__ void __launch_bounds__(192, 1)
       }
       const int r = q * 32 + lane;
       if (a.cluster > 1) {
-        float* part = reinterpret_cast<float*>(smem);
-        for (int c = 0; c < NTOK; c += 64) {
-          if (n0 + c >= a.T) break;
-          float v[64];
-          tmem_ld64(taddr + c, v);
+        if (m0 < a.F) {
+          const int c = a.cluster, nb = NTOK / TOK_BLOCK;
+          const int b0 = srank * nb / c, b1 = (srank + 1) * nb / c;
+          if (warp == 2 && lane == 0) {
+            int mine = 0;
+            for (int b = b0; b < b1; ++b) mine += n0 + b * TOK_BLOCK < a.T;
+            if (mine > 0) mbar_arrive_expect_tx(redbar, static_cast<uint32_t>((c - 1) * mine * BLOCK_F32_BYTES));
+          }
+          float* send = reinterpret_cast<float*>(smem + split_send_offset<NTOK>(c));
+          for (int b = 0; b < nb; ++b) {
+            if (n0 + b * TOK_BLOCK >= a.T) break;
+            if (b >= b0 && b < b1) continue;
+            float v[32];
+            tmem_ld32(taddr + b * TOK_BLOCK, v);
+            float* blk = send + (b < b0 ? b : b - (b1 - b0)) * TOK_BLOCK * BM;
 #pragma unroll
-          for (int j = 0; j < 64; ++j) part[(c + j) * BM + r] = v[j];
+            for (int e = 0; e < 32; ++e) blk[e * BM + r] = v[e];
+          }
+          fence_proxy_async_shared();  // the drained blocks, for the bulk copies
         }
       } else if (m0 < a.F) {
         // Lanes are consecutive rows: a warp's stores of one token fill 64 contiguous bytes.
@@ -513,92 +551,78 @@ __global__ void __launch_bounds__(192, 1)
     const int nb = NTOK / TOK_BLOCK;
     const int b0 = srank * nb / a.cluster, b1 = (srank + 1) * nb / a.cluster;
     const bool live = m0 < a.F;  // the odd CTA of the last pair may lie past the last row
-    uint8_t* stage = smem + NTOK * BM * 4;
+    uint8_t* stage = smem + (a.cluster > 1 ? split_send_offset<NTOK>(a.cluster) : static_cast<size_t>(NTOK) * BM * 4);
     if (a.cluster > 1) {
-      // Every CTA of the cluster has its partial tile in shared memory.
+      const int c = a.cluster;
+      int mine = 0;  // blocks of this CTA's slice that hold tokens
+      for (int b = b0; b < b1; ++b) mine += n0 + b * TOK_BLOCK < a.T;
+      // Every CTA of the cluster is past its mainloop (its receive buffer is free), has armed its
+      // reduction barrier and has drained the blocks it sends.
       cluster_sync();
-      // Epilogue part 2: this CTA's slice of 32-token blocks, summed over the cluster's partials in
-      // rank order (deterministic), then the epilogue; lane l handles rows 4l .. 4l+3 of a token. A
-      // warp issues U tokens' loads from up to SB sources before it adds any of them, so one round
-      // trip of distributed shared memory covers SB x U loads (the reduction is latency-bound).
-      if (warp >= 2 && !flags[0]) {
-        constexpr int U = 8, NW = 4, SB = 4;
-        const int t0 = n0 + b0 * TOK_BLOCK;
-        const int t1 = min(a.T, n0 + b1 * TOK_BLOCK);
-        // A fused all-reduce sends each reduced row to the rank that owns it at once, so the NVLink
-        // transfer runs under the rest of the reduction (slots of this call's epoch parity).
-        const int64_t par =
-            a.epilogue == EPI_ALLREDUCE ? static_cast<int64_t>(*reinterpret_cast<volatile uint32_t*>(a.ar.epoch) & 1u) : 0;
-        const bool ok = a.epilogue != EPI_RESIDUAL || t0 >= t1 || !live || mbar_wait(resbar, 0);
-        if (!ok) flags[0] = 1;
-        const uint32_t part0 = smem_u32(smem) + static_cast<uint32_t>(4 * lane * 4);
-        for (int tb = t0 + (warp - 2); ok && live && tb < t1; tb += NW * U) {
-          float4 acc[U];
+      // Part 2a: the blocks go to their owners by bulk copies, shared memory to the owner's shared
+      // memory, each completing on the owner's reduction barrier (lane b of warp 2 sends block b).
+      if (warp == 2 && live && !flags[0]) {
+        const int b = lane;
+        if (b < nb && !(b >= b0 && b < b1) && n0 + b * TOK_BLOCK < a.T) {
+          int o = 0;
+          while (b >= (o + 1) * nb / c) ++o;  // the split CTA whose slice holds block b
+          const int j = srank < o ? srank : srank - 1;  // this CTA's place among o's sources
+          const int ob0 = o * nb / c;
+          const uint32_t peer = PAIR ? static_cast<uint32_t>(prank + 2 * o) : static_cast<uint32_t>(o);
+          const uint8_t* src = smem + split_send_offset<NTOK>(c) + (b < b0 ? b : b - (b1 - b0)) * BLOCK_F32_BYTES;
+          const uint32_t dst = cluster_map(
+              smem_u32(smem + (static_cast<size_t>(j) * split_slice_tokens<NTOK>(c) + (b - ob0) * TOK_BLOCK) * BM * 4), peer);
+          bulk_copy_cluster(dst, src, BLOCK_F32_BYTES, cluster_map(smem_u32(redbar), peer));
+        }
+      }
+      // Part 2b: the other splits' partials of this CTA's blocks have arrived.
+      if (warp >= 2 && live && !flags[0] && mine > 0 && !mbar_wait(redbar, 0)) flags[0] = 1;
+      // Every copy out of this CTA has landed at its owner: its send buffers may take the staging.
+      cluster_sync();
+      // Part 2c: this CTA's slice, summed in split order (its own partial from TMEM), then the epilogue;
+      // thread = row, 32 tokens per step. The residual slice loads by TMA meanwhile.
+      if (warp >= 2 && !flags[0] && live && mine > 0) {
+        if (a.epilogue == EPI_RESIDUAL && warp == 2 && lane == 0) {
+          mbar_arrive_expect_tx(resbar, static_cast<uint32_t>(mine * TOK_BLOCK * BM * 2));
+          for (int b = b0; b < b1; ++b)
+            if (n0 + b * TOK_BLOCK < a.T) tma_load_2d(stage + b * TOK_BLOCK * BM * 2, &tmap_r, resbar, m0, n0 + b * TOK_BLOCK);
+        }
+        const int q = warp & 3, r = q * 32 + lane;
+        const uint32_t taddr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+        const float* recv = reinterpret_cast<const float*>(smem);
+        const int slice = split_slice_tokens<NTOK>(c);
+        __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stage);
+        bool res_ready = a.epilogue != EPI_RESIDUAL;
+        for (int b = b0; b < b1; ++b) {
+          if (n0 + b * TOK_BLOCK >= a.T) break;
+          float acc[32];
 #pragma unroll
-          for (int u = 0; u < U; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-          // Sources 0 .. SB-1: every load first, then the sums in rank order.
-          {
-            float4 p[SB][U];
+          for (int e = 0; e < 32; ++e) acc[e] = 0.f;
+          for (int src = 0; src < c; ++src) {
+            float v[32];
+            if (src == srank) {
+              tmem_ld32(taddr + b * TOK_BLOCK, v);
+            } else {
+              const float* p = recv + (static_cast<size_t>(src < srank ? src : src - 1) * slice + (b - b0) * TOK_BLOCK) * BM + r;
 #pragma unroll
-            for (int src = 0; src < SB; ++src) {
-              const uint32_t peer = PAIR ? static_cast<uint32_t>(prank + 2 * src) : static_cast<uint32_t>(src);
-#pragma unroll
-              for (int u = 0; u < U; ++u) {
-                const int t = tb + NW * u;
-                p[src][u] = src < a.cluster && t < t1
-                                ? ld_cluster_f4(cluster_map(part0 + static_cast<uint32_t>((t - n0) * BM * 4), peer))
-                                : make_float4(0.f, 0.f, 0.f, 0.f);
-              }
+              for (int e = 0; e < 32; ++e) v[e] = p[e * BM];
             }
 #pragma unroll
-            for (int src = 0; src < SB; ++src) {
-              if (src >= a.cluster) break;
-#pragma unroll
-              for (int u = 0; u < U; ++u) {
-                acc[u].x += p[src][u].x;
-                acc[u].y += p[src][u].y;
-                acc[u].z += p[src][u].z;
-                acc[u].w += p[src][u].w;
-              }
-            }
+            for (int e = 0; e < 32; ++e) acc[e] += v[e];
           }
-          for (int src = SB; src < a.cluster; ++src) {
-            const uint32_t peer = PAIR ? static_cast<uint32_t>(prank + 2 * src) : static_cast<uint32_t>(src);
-            float4 p[U];
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-              const int t = tb + NW * u;
-              p[u] = t < t1 ? ld_cluster_f4(cluster_map(part0 + static_cast<uint32_t>((t - n0) * BM * 4), peer))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
+          if (!res_ready) {
+            if (!mbar_wait(resbar, 0)) {
+              flags[0] = 1;
+              break;
             }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-              acc[u].x += p[u].x;
-              acc[u].y += p[u].y;
-              acc[u].z += p[u].z;
-              acc[u].w += p[u].w;
-            }
+            res_ready = true;
           }
 #pragma unroll
-          for (int u = 0; u < U; ++u) {
-            const int t = tb + NW * u;
-            if (t >= t1) break;
-            const float v[4] = {acc[u].x, acc[u].y, acc[u].z, acc[u].w};
-            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(stage) + (t - n0) * BM + 4 * lane;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              float out = bf16r(v[j]);
-              if (a.epilogue == EPI_RESIDUAL) out = __bfloat162float(o[j]) + out;
-              o[j] = __float2bfloat16_rn(out);
-            }
-          }
-          if (a.epilogue == EPI_ALLREDUCE) {
-            // This warp's U rows are complete in the staging tile: lane u sends row tb + 4u.
-            fence_proxy_async_shared();
-            __syncwarp();
-            const int t = tb + NW * lane;
-            if (lane < U && t < t1)
-              push_row(a.ar, par, t, m0, reinterpret_cast<const __nv_bfloat16*>(stage) + (t - n0) * BM);
+          for (int e = 0; e < 32; ++e) {
+            const int idx = (b * TOK_BLOCK + e) * BM + r;
+            float out = bf16r(acc[e]);
+            if (a.epilogue == EPI_RESIDUAL) out = __bfloat162float(st[idx]) + out;
+            st[idx] = __float2bfloat16_rn(out);
           }
         }
       }
@@ -636,12 +660,11 @@ __global__ void __launch_bounds__(192, 1)
       const int f = m0 + (te & 15) * 8;               // this thread's eight features in phase 2
       const bool mine_f = live && f < a.F;
       bool bad = failed || !live;
-      // 1. This rank's partial of every row another rank owns, to that rank (with split K the split
-      //    reduction has sent them already, row by row): bulk copies of the staged rows, complete before
-      //    the flags go out (a release after the barrier orders every thread's completed copies).
-      if (!bad && a.cluster == 1) fence_proxy_async_shared();
+      // 1. This rank's partial of every row another rank owns, to that rank: bulk copies of the staged
+      //    rows, all complete before the flags go out.
+      if (!bad) fence_proxy_async_shared();
       bad = epi_bar_or(bad);
-      if (!bad && a.cluster == 1 && warp == 2)
+      if (!bad && warp == 2)
         for (int t = tb0 + lane; t < tb1; t += 32) push_row(r, par, t, m0, sbase + (t - n0) * BM);
       bulk_commit();
       bulk_wait0();
@@ -683,9 +706,9 @@ __global__ void __launch_bounds__(192, 1)
       }
       epi_bar_or(bad);
     }
-    // No CTA leaves while a peer may still read its shared memory (and a pair frees its tensor memory
-    // together).
-    if (a.cluster > 1 || PAIR) cluster_sync();
+    // A pair frees its tensor memory together (after the split reduction's second barrier no CTA
+    // touches another's shared memory).
+    if (PAIR) cluster_sync();
   }
 
   tc_fence_before();
@@ -1062,6 +1085,10 @@ int launch_gemm(const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap&
                 cudaStream_t stream, const CUtensorMap* tw = nullptr, const CUtensorMap* tsf = nullptr,
                 bool resident = false, bool pair_place = false) {
   using C = Cfg<NTOK, MX, PAIR>;
+  // The split reduction's buffers live in the pipeline buffers.
+  if (a.cluster > 1 && split_smem_bytes<NTOK>(a.cluster) > C::PIPE)
+    return q38host::set_error("fp8 gemm: the %d-split reduction of %d-token tiles does not fit shared memory", a.cluster, NTOK),
+           Q38_ERR_UNSUPPORTED;
   // The shared-memory opt-in is per device; remember which devices have it.
   static unsigned long long done_mask = 0;
   int dev = 0;
@@ -1102,6 +1129,14 @@ int launch_gemm(const CUtensorMap& tx, const CUtensorMap& ty, const CUtensorMap&
 }
 
 int token_tile(int64_t tokens) { return tokens > 128 ? 256 : 128; }
+
+// The token tile for a split reduction over `cluster` K splits in the 1-SM form: a 256-token tile keeps
+// its receive and send buffers inside the pipeline buffers only up to 4 splits; above, 128 tokens.
+template <bool MX>
+int cluster_token_tile(int ntok, int cluster) {
+  if (ntok != 256 || cluster <= 1) return ntok;
+  return split_smem_bytes<256>(cluster) <= Cfg<256, MX, false>::PIPE ? 256 : 128;
+}
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
@@ -1187,7 +1222,7 @@ int gemm_fp8(const void* x, int64_t tokens, int64_t k, const void* w, const void
              void* y, int64_t ldy, const void* residual, int64_t ldr, int splits, void* workspace,
              size_t workspace_bytes, const ArArgs* ar, cudaStream_t s, const char* who) {
   using namespace q38host;
-  const int ntok = token_tile(tokens);
+  int ntok = token_tile(tokens);
   const int nkc = static_cast<int>(cdiv(k, BK_BYTES));
   splits = effective_splits(k, splits);
   GemmArgs a{};
@@ -1210,6 +1245,7 @@ int gemm_fp8(const void* x, int64_t tokens, int64_t k, const void* w, const void
   if (st != Q38_OK) return st;
   if (ar && a.cluster == 0)
     return set_error("%s: the fused all-reduce takes at most %d K splits", who, kMaxClusterSplits), Q38_ERR_UNSUPPORTED;
+  if (!(ntok == 256 && 2 * a.cluster <= kMaxClusterSplits && features > BM)) ntok = cluster_token_tile<true>(ntok, a.cluster);
   st = encode_tmap_2d(&tx, x, tokens, k, 1, ntok, BK_BYTES);
   if (st != Q38_OK) return st;
   if (a.cluster == 0) ty = tr = tx;
@@ -1357,7 +1393,7 @@ extern "C" int q38_bf16_linear(const void* x, int64_t ldx, int64_t rows, int64_t
     return set_error("q38_bf16_linear: x and w must be 16-byte aligned, splits >= 1"), Q38_ERR_ARG;
   // A thin output (one 128-row tile, e.g. in_proj_b/a's 96) gets 128-token tiles: twice the CTAs,
   // each streaming half the activations.
-  const int ntok = n_out <= BM ? 128 : token_tile(rows);
+  int ntok = n_out <= BM ? 128 : token_tile(rows);
   const int nkc = static_cast<int>(cdiv(k, BK_BYTES / 2));
   const int kc_per = static_cast<int>(cdiv(nkc, std::min(splits, nkc)));
   splits = static_cast<int>(cdiv(nkc, kc_per));
@@ -1381,6 +1417,7 @@ extern "C" int q38_bf16_linear(const void* x, int64_t ldx, int64_t rows, int64_t
   int st = setup_epilogue(a, splits, rows, n_out, y, ldy, nullptr, 0, workspace, workspace_bytes, &ty, &tr,
                           "q38_bf16_linear", !via_workspace);
   if (st != Q38_OK) return st;
+  ntok = cluster_token_tile<false>(ntok, a.cluster);
   st = encode_tmap_2d(&tx, x, rows, k, 2, ntok, BK_BYTES / 2);
   if (st != Q38_OK) return st;
   if (a.cluster == 0) ty = tr = tx;
