@@ -14,7 +14,8 @@ the baseline and to compare ranks). Checks, per rank:
   before the GPU ranks start. Every rank's residual stream must equal rank 0's bit for bit. TP is not
   compared with TP = 1 end to end: rounding each rank's partial to bf16 moves later e5m2 roundings, as
   the reference's own TP test avoids by running in float32 (tests/test_model_parity.py:141-170).
-* the same layer checks with the NCCL baseline instead of the fused all-reduce;
+* the same layer checks with the NCCL baseline instead of the fused all-reduce (within 1e-1 above two
+  ranks, where NCCL's ring rounds every hop's partial sum to bf16);
 * two whole steps back to back, as one CUDA graph and as eager launches: the same bits (the exchange
   has no host synchronisation between layers there).
 Each worker bounds its collectives (a short process-group timeout) and the parent kills workers that
@@ -135,7 +136,11 @@ def _worker(rank, world, port, queue, oracle_path):
                 peak = want.abs().amax(-1, keepdim=True)
                 worst = ((got - want).abs() / peak).max().item()
                 rel = ((got - want).norm(dim=-1) / want.norm(dim=-1)).max().item()
-                results.append((f"TP={world} {name} layer {i} vs TP={world} oracle", worst <= 2e-2 and rel <= 2e-2,
+                # The NCCL baseline sums bf16 partials on a ring: above two ranks every hop rounds to bf16,
+                # which the oracle's rank-order fp32 sum does not, and the layer's e5m2 roundings amplify
+                # those ulps; it is the comparison baseline, held to 1e-1 there.
+                bound = 1e-1 if (name == "nccl" and world > 2) else 2e-2
+                results.append((f"TP={world} {name} layer {i} vs TP={world} oracle", worst <= bound and rel <= bound,
                                 f"max {worst:.3g} of the row peak, relative L2 {rel:.3g}"))
             step.close()
             torch.distributed.barrier()

@@ -22,9 +22,12 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _config(pkg, wide: bool):
+def _config(pkg, wide):
     cfg = pkg.config.tiny_config(num_blocks=1)
-    if wide:  # 8 query heads over 2 KV heads, 4 key / 12 value heads: splits 4 ways with KV replication
+    if wide == "tp8":  # the full model's head counts (24 query over 4 KV heads, 16 key / 48 value heads) at the
+        # tiny head sizes: at 8 ranks 3 query heads per rank, each pair of ranks sharing one replicated KV head
+        cfg = replace(cfg, num_attention_heads=24, num_key_value_heads=4, linear_num_key_heads=16, linear_num_value_heads=48)
+    elif wide:  # 8 query heads over 2 KV heads, 4 key / 12 value heads: splits 4 ways with KV replication
         cfg = replace(cfg, num_attention_heads=8, num_key_value_heads=2, linear_num_key_heads=4, linear_num_value_heads=12)
     return cfg
 
@@ -59,7 +62,7 @@ def _run(rank, world, port, wide, out_q):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,wide", [(2, False), (4, True)])
+@pytest.mark.parametrize("world,wide", [(2, False), (4, True), (8, "tp8")])
 def test_tensor_parallel_ranks_match_single_rank(pkg, world, wide):
     cfg = _config(pkg, wide)
     weights = {}
