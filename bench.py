@@ -353,9 +353,11 @@ def run_ours(args, world, rank, local):
 
 
 def decode_step_bytes(step, head, linear_kind: str, positions: torch.Tensor) -> int:
-    """HBM bytes one decode step must move on this rank, averaged over the timed steps' positions."""
+    """HBM bytes one decode step must move on this rank, averaged over the timed steps' positions. The
+    lm_head counts as FP8 with its scales (the checkpoint's format and the algorithmic figure), although
+    the kernel streams it as BF16 (twice the bytes: at 256 rows it is bound by the BF16 tensor rate)."""
     fp8 = lambda lin: lin.out_features * lin.in_features * 33 // 32  # e4m3 bytes + UE8M0 per 32  # noqa: E731
-    total = head.lm_head.out_features * head.lm_head.in_features * 2
+    total = fp8(head.lm_head)
     kv_positions = positions.clamp(max=MAX_SEQ).long().sum(dim=1).float().mean().item()
     for l in step.layers:
         total += fp8(l.gate_up) + fp8(l.down)
