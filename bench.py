@@ -571,12 +571,18 @@ def run_micro(args):
         lins = [ops.DeviceLinear(pkg.weights.FP8Weight.from_float(torch.randn(n, k, device=dev, generator=gen) * 0.02), dev)
                 for _ in range(args.copies)]
         x = pkg.codec.to_e5m2_bytes(bf(B, k))
-        y = torch.empty(B, n, dtype=torch.bfloat16, device=dev)
+        y = torch.zeros(B, n, dtype=torch.bfloat16, device=dev)
         splits = args.splits or ops.choose_splits(B, n, k)
-        ws = torch.zeros(max(256, ops.gemm_workspace_bytes(B, n, splits)), dtype=torch.uint8, device=dev)
+        if args.streamk:  # the row-parallel form at TP = 1: stream-K with the residual epilogue
+            ws = torch.zeros(ops.streamk_workspace_bytes(B, n, k), dtype=torch.uint8, device=dev)
 
-        def launch(i):
-            ops.fp8_gemm(x, lins[i % len(lins)], y, splits=splits, workspace=ws)
+            def launch(i):
+                ops.fp8_gemm_streamk(x, lins[i % len(lins)], y, ws, residual=y)
+        else:
+            ws = torch.zeros(max(256, ops.gemm_workspace_bytes(B, n, splits)), dtype=torch.uint8, device=dev)
+
+            def launch(i):
+                ops.fp8_gemm(x, lins[i % len(lins)], y, splits=splits, workspace=ws)
         per = n * k + n * (k // 32) + B * k + B * n * 2
         unit, bound = "GB/s", "hbm"
     elif args.micro == "gemm_silu":
@@ -815,6 +821,7 @@ def main():
     ap.add_argument("--tp", type=int, default=1, help="--micro gemm: K = 17408 / tp")
     ap.add_argument("--shape", help="--micro gemm: 'features,k' instead of the down_proj shape")
     ap.add_argument("--splits", type=int, default=0, help="--micro gemm/ab: K splits instead of the default choice")
+    ap.add_argument("--streamk", action="store_true", help="--micro gemm: the stream-K form with the residual epilogue")
     ap.add_argument("--eager", action="store_true", help="--micro: launch one by one instead of one CUDA graph")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)

@@ -104,6 +104,24 @@ int q38_fp8_gemm_static_scratch(const void* x, int64_t tokens, int64_t k, const 
                                 int64_t features, int epilogue, void* y, int64_t ldy, const void* residual,
                                 int64_t ldr, int splits, q38_stream_t stream);
 
+/*
+ * The same GEMM and epilogues (Q38_EPI_BF16, Q38_EPI_RESIDUAL) divided stream-K: one persistent CTA per
+ * SM (2-SM pairs for 256-token tiles) and the K steps of all output tiles split evenly between them, so
+ * every SM works for the whole launch whatever the tile count. A tile that one CTA computes whole takes
+ * its epilogue from tensor memory; a tile split between CTAs leaves each part's fp32 partial in the
+ * workspace and the last part to finish sums them in K order (deterministic) and applies the epilogue.
+ * No CTA waits for another. Same FP8 formats as q38_fp8_gemm; the sum order over K differs from the
+ * split-K form's (fp32 partial sums over other K ranges). The workspace (q38_fp8_gemm_streamk_workspace_bytes
+ * for the shape on the current device, 0 on a bad shape or without a device) must be 16-byte aligned and
+ * zero when first used; each call leaves its counters at zero again. Calls on one workspace must not
+ * overlap. Replaces the row-parallel projections at TP = 1 (qwen38_inf2/model.py:259, :374, :639 with the
+ * residual add of DecoderLayer.forward, model.py:918-930).
+ */
+size_t q38_fp8_gemm_streamk_workspace_bytes(int64_t tokens, int64_t features, int64_t k);
+int q38_fp8_gemm_streamk(const void* x_q, int64_t tokens, int64_t k, const void* w, const void* w_sf,
+                         int64_t features, int epilogue, void* y, int64_t ldy, const void* residual, int64_t ldr,
+                         void* workspace, size_t workspace_bytes, q38_stream_t stream);
+
 /* Bytes of the pre-tiled scale array of a [features, k] weight. */
 size_t q38_sf_tile_bytes(int64_t features, int64_t k);
 

@@ -27,6 +27,12 @@ SIGNATURES = {
         [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int,
          c_void_p, c_size_t, c_void_p],
     ),
+    "q38_fp8_gemm_streamk_workspace_bytes": (c_size_t, [c_int64, c_int64, c_int64]),
+    "q38_fp8_gemm_streamk": (
+        c_int,
+        [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_int64, c_void_p, c_int64, c_void_p,
+         c_size_t, c_void_p],
+    ),
     "q38_fp8_gemm_static_scratch": (
         c_int,
         [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int,

@@ -75,6 +75,11 @@ struct GemmArgs {
   ArArgs ar;              // EPI_ALLREDUCE: the ranks' exchange regions
   uint8_t* yq;            // EPI_SILU: e5m2 [T, ldq] of SiLU(gate) * up
   int64_t ldq;
+  // Stream-K (persistent kernel, sk_groups > 0): group g of sk_groups owns the linear K steps
+  // [g W / G, (g + 1) W / G) of W = tiles x nkc; a tile split between groups sums its fp32 partials
+  // from ws ([128-row tile][sk_max_seg slots][128 x NTOK]) in K order, by the last group to finish.
+  int sk_groups;
+  int sk_max_seg;
 };
 
 // Epilogue staging (cluster mode), reusing the pipeline buffers once the accumulator is final: bf16
@@ -222,14 +227,49 @@ __device__ __forceinline__ void reduce_owned_rows(const ArArgs& r, __nv_bfloat16
 }
 
 // Applies the bf16 (or bf16 + residual) epilogue to 16 consecutive tokens of one feature row.
+// v[j] = sum over slots s < n of p[s * stride + j], j < 16, in slot order from zero (the split-K and
+// stream-K partial sums, fp32): the loads of four slots are in flight before the first add, so a chunk
+// costs one memory round trip per four slots instead of one per slot.
+__device__ __forceinline__ void sum_slots16(const float* p, size_t stride, int n, float (&v)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = 0.f;
+  for (int s0 = 0; s0 < n; s0 += 4) {
+    float4 q[4][4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (s0 + u < n)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) q[u][j] = __ldcg(reinterpret_cast<const float4*>(p + (s0 + u) * stride) + j);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (s0 + u >= n) break;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        v[4 * j] += q[u][j].x;
+        v[4 * j + 1] += q[u][j].y;
+        v[4 * j + 2] += q[u][j].z;
+        v[4 * j + 3] += q[u][j].w;
+      }
+    }
+  }
+}
+
+// The residual rows are all loaded before the first store: y and the residual may be the same buffer
+// (the residual stream updated in place), so a load after a store could not be moved ahead of it and
+// each token would cost a dependent round trip to memory.
 __device__ __forceinline__ void epilogue16(const GemmArgs& a, int row, int t0, const float (&v)[16], int lane) {
   if (row >= a.F) return;
+  float res[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+    res[j] = (a.epilogue == EPI_RESIDUAL && t0 + j < a.T) ? __bfloat162float(a.res[static_cast<int64_t>(t0 + j) * a.ldr + row])
+                                                           : 0.f;
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
     const int t = t0 + j;
     if (t < a.T) {
       float out = bf16r(v[j]);
-      if (a.epilogue == EPI_RESIDUAL) out = __bfloat162float(a.res[static_cast<int64_t>(t) * a.ldr + row]) + out;
+      if (a.epilogue == EPI_RESIDUAL) out = res[j] + out;
       a.y[static_cast<int64_t>(t) * a.ldy + row] = __float2bfloat16_rn(out);
     }
   }
@@ -526,19 +566,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int c = 0; c < NTOK; c += 16) {
           if (n0 + c >= a.T) break;
           float v[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0.f;
-          for (int s = 0; s < a.splits; ++s) {
-            const float* p = base + s * split_stride + static_cast<size_t>(c / 16) * BM * 16;
-#pragma unroll
-            for (int j = 0; j < 16; j += 4) {
-              const float4 f = __ldcg(reinterpret_cast<const float4*>(p + j));
-              v[j] += f.x;
-              v[j + 1] += f.y;
-              v[j + 2] += f.z;
-              v[j + 3] += f.w;
-            }
-          }
+          sum_slots16(base + static_cast<size_t>(c / 16) * BM * 16, split_stride, a.splits, v);
           epilogue16(a, row, n0 + c, v, lane);
         }
         if (warp == 2 && lane == 0) a.counters[tile] = 0u;
@@ -729,6 +757,43 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// The group holding linear K step i of W over G groups (group g holds [floor(g W / G), floor((g+1) W / G))).
+__host__ __device__ __forceinline__ int sk_group_of(long long i, long long W, int G) {
+  return static_cast<int>(((i + 1) * G + W - 1) / W) - 1;
+}
+// Segment `idx` of group `group`'s work: tile u, K steps [k0, k1). Without stream-K a segment is a whole
+// tile (u = group + idx x ngroups); with it, the group's contiguous range cut at tile boundaries.
+__device__ __forceinline__ bool seg_at(const GemmArgs& a, int group, int ngroups, int units, int nk, int idx, int& u,
+                                       int& k0, int& k1) {
+  if (a.sk_groups == 0) {
+    u = group + idx * ngroups;
+    k0 = 0;
+    k1 = nk;
+    return u < units;
+  }
+  const long long W = static_cast<long long>(units) * nk;
+  long long i = group * W / a.sk_groups;
+  const long long i1 = (group + 1) * W / a.sk_groups;
+  for (int s = 0; i < i1; ++s) {
+    u = static_cast<int>(i / nk);
+    k0 = static_cast<int>(i % nk);
+    k1 = static_cast<int>(k0 + (i1 - i < nk - k0 ? i1 - i : nk - k0));
+    if (s == idx) return true;
+    i += k1 - k0;
+  }
+  return false;
+}
+// The groups sharing tile u under stream-K: the first one, and how many (1: the tile is whole).
+__device__ __forceinline__ int sk_tile_split(const GemmArgs& a, int u, int units, int nk, int& first) {
+  if (a.sk_groups == 0) {
+    first = 0;
+    return 1;
+  }
+  const long long W = static_cast<long long>(units) * nk;
+  first = sk_group_of(static_cast<long long>(u) * nk, W, a.sk_groups);
+  return sk_group_of(static_cast<long long>(u + 1) * nk - 1, W, a.sk_groups) - first + 1;
+}
+
 // ---------------------------------------------------------------------------------------------
 // Persistent form for unsplit GEMMs (EPI_BF16, EPI_SILU): each CTA (or 2-SM pair) walks output
 // tiles, unit u = (weight rows u / n_tiles, token tile u % n_tiles): the token tiles of one weight tile
@@ -776,7 +841,7 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* accf = empty + C::STAGES;
   uint64_t* tmem_empty = accf + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_empty + 1);
-  volatile int* flags = reinterpret_cast<volatile int*>(tmem_holder + 1);  // [0] abort
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_holder + 1);  // [0] abort, [1] last group (stream-K)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t crank = PAIR ? cluster_rank() : 0u;
@@ -843,20 +908,24 @@ __global__ void __launch_bounds__(192, 1)
         if constexpr (PAIR) tma_load_2d_pair(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0 + prank * C::B_ROWS);
         else tma_load_2d(sB + s * C::B_BYTES, &tmap_x, &full[s], kx, n0);
       };
-      // The first pass over the ring needs no slot to drain: the first tile's weights go first.
+      // The first pass over the ring needs no slot to drain: the first segment's weights go first.
       int pre = 0;
-      if (group < units) {
-        const int mt = PAIR ? 2 * (group / n_tiles) + prank : group / n_tiles;
-        pre = min(nk, C::STAGES);
-        for (int i = 0; i < pre; ++i) load_w(i, mt, i);
+      {
+        int u, k0, k1;
+        if (seg_at(a, group, ngroups, units, nk, 0, u, k0, k1)) {
+          const int mt = PAIR ? 2 * (u / n_tiles) + prank : u / n_tiles;
+          pre = min(k1 - k0, C::STAGES);
+          for (int i = 0; i < pre; ++i) load_w(i, mt, k0 + i);
+        }
       }
       pdl_wait();
       int it = 0;
-      for (int u = group; u < units && !flags[0]; u += ngroups) {
+      int u, k0, k1;
+      for (int si = 0; !flags[0] && seg_at(a, group, ngroups, units, nk, si, u, k0, k1); ++si) {
         const int mp = u / n_tiles, nt = u % n_tiles;
         const int mt = PAIR ? 2 * mp + prank : mp;
         const int n0 = nt * NTOK;
-        for (int i = 0; i < nk; ++i, ++it) {
+        for (int i = k0; i < k1; ++i, ++it) {
           if (it < pre) {
             load_x(it, n0, i);
             continue;
@@ -886,14 +955,15 @@ __global__ void __launch_bounds__(192, 1)
                 (static_cast<uint32_t>(BM >> 4) << 24);
       }
       int it = 0, tc = 0;
-      for (int u = group; u < units && !flags[0]; u += ngroups, ++tc) {
-        // The epilogue has drained the previous tile's accumulator.
+      int u, k0, k1;
+      for (int si = 0; !flags[0] && seg_at(a, group, ngroups, units, nk, si, u, k0, k1); ++si, ++tc) {
+        // The epilogue has drained the previous segment's accumulator.
         if (!mbar_wait(tmem_empty, (tc & 1) ^ 1)) {
           flags[0] = 1;
           break;
         }
         tc_fence_after();
-        for (int i = 0; i < nk; ++i, ++it) {
+        for (int i = k0; i < k1; ++i, ++it) {
           const int s = it % C::STAGES;
           const uint32_t ph = (it / C::STAGES) & 1;
           if (flags[0] || !mbar_wait(&full[s], ph)) {
@@ -911,7 +981,7 @@ __global__ void __launch_bounds__(192, 1)
               const uint32_t id = idesc | (static_cast<uint32_t>(kk) << 29) | (static_cast<uint32_t>(kk) << 4);
               mma_mxf8_pair(tmem, sdesc_sw128(a_addr + kk * 32), sdesc_sw128(b_addr + kk * 32), id,
                             sfa | (static_cast<uint32_t>(kk) << 30), (tmem + C::SFB_COL) | (static_cast<uint32_t>(kk) << 30),
-                            (i | kk) != 0);
+                            ((i - k0) | kk) != 0);
             }
             tc_commit_pair(&empty[s], pair_mask);
           } else if (MX) {
@@ -922,13 +992,13 @@ __global__ void __launch_bounds__(192, 1)
               const uint32_t id = idesc | (static_cast<uint32_t>(kk) << 29) | (static_cast<uint32_t>(kk) << 4);
               mma_mxf8(tmem, sdesc_sw128(a_addr + kk * 32), sdesc_sw128(b_addr + kk * 32), id,
                        sfa | (static_cast<uint32_t>(kk) << 30), (tmem + C::SFB_COL) | (static_cast<uint32_t>(kk) << 30),
-                       (i | kk) != 0);
+                       ((i - k0) | kk) != 0);
             }
             tc_commit(&empty[s]);
           } else {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)
-              mma_f16(tmem, sdesc_sw128(a_addr + kk * 32), sdesc_sw128(b_addr + kk * 32), idesc, (i | kk) != 0);
+              mma_f16(tmem, sdesc_sw128(a_addr + kk * 32), sdesc_sw128(b_addr + kk * 32), idesc, ((i - k0) | kk) != 0);
             tc_commit(&empty[s]);
           }
         }
@@ -946,7 +1016,8 @@ __global__ void __launch_bounds__(192, 1)
     __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(sOut);
     pdl_wait();
     int tc = 0;
-    for (int u = group; u < units; u += ngroups, ++tc) {
+    int u, k0, k1;
+    for (int si = 0; seg_at(a, group, ngroups, units, nk, si, u, k0, k1); ++si, ++tc) {
       const int mp = u / n_tiles, nt = u % n_tiles;
       const int mt = PAIR ? 2 * mp + prank : mp;
       const int m0 = mt * BM, n0 = nt * NTOK;
@@ -955,8 +1026,82 @@ __global__ void __launch_bounds__(192, 1)
         if (threadIdx.x == 64) flags[0] = 1;
         break;
       }
-      if (u + ngroups >= units) pdl_trigger();  // this CTA's last mainloop is done
+      {
+        int nu, nk0, nk1;
+        if (!seg_at(a, group, ngroups, units, nk, si + 1, nu, nk0, nk1)) pdl_trigger();  // this CTA's last mainloop
+      }
       tc_fence_after();
+      if (a.sk_groups > 0) {
+        // Stream-K: a whole tile takes its epilogue straight from TMEM; a tile split between groups
+        // leaves this group's fp32 partial in its slot of the workspace ([16-token chunk][128 rows][16]:
+        // a warp's 32 rows of one chunk are 2 KB contiguous), and the last group to finish the tile sums
+        // every slot in K order and applies the epilogue.
+        int first;
+        const int nseg = sk_tile_split(a, u, units, nk, first);
+        const int ctile = nt * (PAIR ? 2 * m_units : m_units) + mt;
+        const size_t tile_f = static_cast<size_t>(BM) * NTOK;
+        if (nseg == 1) {
+          for (int c = 0; c < NTOK; c += 64) {
+            if (n0 + c >= a.T) break;
+            float v[64];
+            tmem_ld64(taddr + c, v);
+#pragma unroll
+            for (int k = 0; k < 64; k += 16) {
+              float w[16];
+#pragma unroll
+              for (int j = 0; j < 16; ++j) w[j] = v[k + j];
+              epilogue16(a, m0 + r, n0 + c + k, w, lane);
+            }
+          }
+          tc_fence_before();
+          epi_bar();
+          if (threadIdx.x == 64) {
+            if constexpr (PAIR) mbar_arrive_cluster(tmem_empty, crank & ~1u);
+            else mbar_arrive(tmem_empty);
+          }
+          continue;
+        }
+        float* part = a.ws + (static_cast<size_t>(ctile) * a.sk_max_seg + (group - first)) * tile_f + static_cast<size_t>(r) * 16;
+        for (int c = 0; c < NTOK; c += 64) {
+          if (n0 + c >= a.T) break;
+          float v[64];
+          tmem_ld64(taddr + c, v);
+#pragma unroll
+          for (int k = 0; k < 64; k += 16) {
+            if (n0 + c + k >= a.T) break;
+            float* dst = part + static_cast<size_t>((c + k) / 16) * BM * 16;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4)
+              __stcg(reinterpret_cast<float4*>(dst + j), make_float4(v[k + j], v[k + j + 1], v[k + j + 2], v[k + j + 3]));
+          }
+        }
+        // TMEM back to the MMA warp at once; the partial is published, then counted.
+        tc_fence_before();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          if constexpr (PAIR) mbar_arrive_cluster(tmem_empty, crank & ~1u);
+          else mbar_arrive(tmem_empty);
+        }
+        __threadfence();
+        epi_bar();
+        if (threadIdx.x == 64) {
+          const unsigned prev = atomicAdd(&a.counters[ctile], 1u);
+          flags[1] = prev == static_cast<unsigned>(nseg - 1);
+        }
+        epi_bar();
+        if (flags[1]) {
+          __threadfence();
+          const float* base = a.ws + static_cast<size_t>(ctile) * a.sk_max_seg * tile_f + static_cast<size_t>(r) * 16;
+          for (int c = 0; c < NTOK; c += 16) {
+            if (n0 + c >= a.T) break;
+            float v[16];
+            sum_slots16(base + static_cast<size_t>(c / 16) * BM * 16, tile_f, nseg, v);
+            epilogue16(a, m0 + r, n0 + c, v, lane);
+          }
+          if (threadIdx.x == 64) a.counters[ctile] = 0u;
+        }
+        continue;
+      }
       // The previous tile's store has finished reading the staging buffer.
       if (threadIdx.x == 64) bulk_wait_read0();
       epi_bar();
@@ -1061,7 +1206,7 @@ int launch_persistent(const CUtensorMap& tx, const CUtensorMap& ty, const CUtens
   }
   const int rows_per_unit = PAIR ? 2 * BM : BM;
   const int units = static_cast<int>(((a.F + rows_per_unit - 1) / rows_per_unit) * ((a.T + NTOK - 1) / NTOK));
-  const int groups = std::min(units, PAIR ? sms[dev] / 2 : sms[dev]);
+  const int groups = a.sk_groups > 0 ? a.sk_groups : std::min(units, PAIR ? sms[dev] / 2 : sms[dev]);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(PAIR ? 2 * groups : groups), 1, 1);
   cfg.blockDim = dim3(192, 1, 1);
@@ -1425,6 +1570,104 @@ extern "C" int q38_bf16_linear(const void* x, int64_t ldx, int64_t rows, int64_t
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return ntok == 256 ? launch_gemm<256, false>(tx, ty, tr, a, grid, s, nullptr, nullptr, false, via_workspace)
                      : launch_gemm<128, false>(tx, ty, tr, a, grid, s, nullptr, nullptr, false, via_workspace);
+}
+
+// ------------------------------------------------------------------------------------------------
+// q38_fp8_gemm_streamk: the persistent kernel with stream-K work division.
+// ------------------------------------------------------------------------------------------------
+namespace {
+
+struct StreamKPlan {
+  int ntok = 0;
+  bool pair = false;
+  int units = 0, nk = 0, groups = 0, ctiles = 0, max_seg = 0;
+  size_t counter_bytes = 0, bytes = 0;
+};
+
+// The same plan for the size query and the launch: tiles of 128 (256 as a 2-SM pair) weight rows x
+// 128 or 256 tokens, the K steps of all tiles divided evenly over one group per SM (pair); `max_seg`
+// is the most groups any tile is split between, the workspace's slots per 128-row tile.
+int streamk_plan(int64_t tokens, int64_t features, int64_t k, StreamKPlan* p) {
+  using namespace q38host;
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_status(e, "stream-K plan: SM count");
+  p->ntok = token_tile(tokens);
+  p->pair = p->ntok == 256 && features > BM;
+  const int64_t rows = p->pair ? 2 * BM : BM;
+  const int64_t m_units = cdiv(features, rows), n_tiles = cdiv(tokens, p->ntok);
+  p->units = static_cast<int>(m_units * n_tiles);
+  p->nk = static_cast<int>(cdiv(k, BK_BYTES));
+  const long long W = static_cast<long long>(p->units) * p->nk;
+  p->groups = static_cast<int>(std::min<long long>(W, p->pair ? sms / 2 : sms));
+  p->ctiles = static_cast<int>((p->pair ? 2 * m_units : m_units) * n_tiles);
+  p->max_seg = 1;
+  for (int u = 0; u < p->units; ++u) {
+    const int first = sk_group_of(static_cast<long long>(u) * p->nk, W, p->groups);
+    const int last = sk_group_of(static_cast<long long>(u + 1) * p->nk - 1, W, p->groups);
+    p->max_seg = std::max(p->max_seg, last - first + 1);
+  }
+  p->counter_bytes = (static_cast<size_t>(p->ctiles) * 4 + 255) / 256 * 256;
+  p->bytes = p->counter_bytes + static_cast<size_t>(p->ctiles) * p->max_seg * BM * p->ntok * sizeof(float);
+  return Q38_OK;
+}
+
+}  // namespace
+
+extern "C" size_t q38_fp8_gemm_streamk_workspace_bytes(int64_t tokens, int64_t features, int64_t k) {
+  if (tokens <= 0 || features <= 0 || k <= 0 || tokens > (1 << 24) || features > (1 << 30) || k > (1 << 30)) return 0;
+  StreamKPlan p;
+  return streamk_plan(tokens, features, k, &p) == Q38_OK ? p.bytes : 0;
+}
+
+extern "C" int q38_fp8_gemm_streamk(const void* x, int64_t tokens, int64_t k, const void* w, const void* w_sf,
+                                    int64_t features, int epilogue, void* y, int64_t ldy, const void* residual,
+                                    int64_t ldr, void* workspace, size_t workspace_bytes, q38_stream_t stream) {
+  using namespace q38host;
+  const char* who = "q38_fp8_gemm_streamk";
+  int st = check_fp8_gemm_call(x, tokens, k, w, w_sf, features, epilogue, y, ldy, residual, ldr, 1, who);
+  if (st != Q38_OK) return st;
+  StreamKPlan p;
+  st = streamk_plan(tokens, features, k, &p);
+  if (st != Q38_OK) return st;
+  if (!workspace || workspace_bytes < p.bytes || !aligned16(workspace))
+    return set_error("%s: needs a 16-byte aligned, zero-initialised workspace of %zu bytes", who, p.bytes), Q38_ERR_ARG;
+  GemmArgs a{};
+  a.w = static_cast<const uint8_t*>(w);
+  a.sf = static_cast<const uint8_t*>(w_sf);
+  a.T = static_cast<int>(tokens);
+  a.F = static_cast<int>(features);
+  a.nkc = p.nk;
+  a.splits = 1;
+  a.kc_per_split = p.nk;
+  a.epilogue = epilogue;
+  a.y = static_cast<__nv_bfloat16*>(y);
+  a.ldy = ldy;
+  a.res = static_cast<const __nv_bfloat16*>(residual);
+  a.ldr = ldr;
+  a.cluster = 1;
+  a.counters = static_cast<unsigned int*>(workspace);
+  a.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + p.counter_bytes);
+  a.sk_groups = p.groups;
+  a.sk_max_seg = p.max_seg;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap tx;
+  if (p.pair) {
+    st = encode_tmap_2d(&tx, x, tokens, k, 1, PCfg<256, true, true>::B_ROWS, BK_BYTES);
+    if (st != Q38_OK) return st;
+    CUtensorMap tw, tsf;
+    const int64_t tiles = cdiv(features, BM) * a.nkc;
+    st = encode_tmap_2d(&tw, w, tiles * BM, BK_BYTES, 1, BM, BK_BYTES, false);
+    if (st != Q38_OK) return st;
+    st = encode_tmap_2d(&tsf, w_sf, tiles * 32, 16, 1, 32, 16, false);
+    if (st != Q38_OK) return st;
+    return launch_persistent<256, true, true>(tx, tx, tw, tsf, a, s);
+  }
+  st = encode_tmap_2d(&tx, x, tokens, k, 1, p.ntok, BK_BYTES);
+  if (st != Q38_OK) return st;
+  return p.ntok == 256 ? launch_persistent<256, true, false>(tx, tx, tx, tx, a, s)
+                       : launch_persistent<128, true, false>(tx, tx, tx, tx, a, s);
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -99,6 +99,33 @@ def fp8_gemm(x_e5m2: torch.Tensor, lin: DeviceLinear, y: torch.Tensor, residual:
     return y
 
 
+def streamk_workspace_bytes(tokens: int, features: int, k: int) -> int:
+    """Workspace bytes of fp8_gemm_streamk for this shape on the current device."""
+    n = _lib.load().q38_fp8_gemm_streamk_workspace_bytes(tokens, features, k)
+    _need(n > 0, f"no stream-K plan for {tokens} x {features} x {k} (bad shape or no device)")
+    return n
+
+
+def fp8_gemm_streamk(x_e5m2: torch.Tensor, lin: DeviceLinear, y: torch.Tensor, workspace: torch.Tensor,
+                     residual: torch.Tensor | None = None) -> torch.Tensor:
+    """y[:, :out] = bf16(e5m2(x) @ W^T) (+ residual, in bf16), the K steps of all tiles divided evenly over
+    one CTA (pair) per SM; `workspace` zero-initialised, streamk_workspace_bytes long."""
+    _cuda(x_e5m2, y, residual, workspace)
+    _need(x_e5m2.dtype == U8 and x_e5m2.dim() == 2 and x_e5m2.stride(1) == 1 and x_e5m2.stride(0) == x_e5m2.shape[1],
+          "x must be contiguous uint8 e5m2 [tokens, k]")
+    tokens, k = x_e5m2.shape
+    _need(k == lin.in_features, f"x has {k} columns, the weight {lin.in_features}")
+    _need(y.dtype == BF16 and y.dim() == 2 and y.stride(1) == 1 and y.shape[0] >= tokens, "y must be bf16 [tokens, >= out]")
+    epi, ldr = 0, 0
+    if residual is not None:
+        _need(residual.dtype == BF16 and residual.stride(1) == 1, "residual must be bf16 with unit column stride")
+        epi, ldr = 1, residual.stride(0)
+    _lib.call("q38_fp8_gemm_streamk", x_e5m2.data_ptr(), tokens, k, lin.q.data_ptr(), lin.sf.data_ptr(),
+              lin.out_features, epi, y.data_ptr(), y.stride(0), residual.data_ptr() if residual is not None else None,
+              ldr, workspace.data_ptr(), workspace.numel() * workspace.element_size(), _stream())
+    return y
+
+
 class _DeviceArray:
     """A raw device allocation seen by torch through __cuda_array_interface__ (no copy)."""
 

@@ -85,12 +85,15 @@ class B200Step:
     def __init__(self, cfg: TextConfig, layer_weights, max_seq_len: int, batch_size: int, tp_degree: int = 1,
                  rank: int = 0, device: torch.device | str | None = None, saved_states: bool = False,
                  use_graph: bool = True, process_group=None, verify_tokens: int = 0, fused_allreduce: bool = True,
-                 max_chunk: int = 512, kv_cache_format: str = "bf16", kv_scales=None, presharded: bool = False):
+                 max_chunk: int = 512, kv_cache_format: str = "bf16", kv_scales=None, presharded: bool = False,
+                 streamk: bool = False):
         """`layer_weights(i)` returns layer i's unsharded weights (weights.synthetic_layer names), or
         `layer_weights` is a dict holding them all. `kv_cache_format` "fp8" keeps the KV cache as FP8 e4m3
         bytes with static per-layer scales (the reference's kv_cache_format, model.py:556-563): `kv_scales`
         {layer index: (k_scale, v_scale)}, by default weights.synthetic_kv_scales. With `presharded`,
-        `layer_weights(i)` already gives this rank's cut (weights.RankShards.layer)."""
+        `layer_weights(i)` already gives this rank's cut (weights.RankShards.layer). At TP = 1 the
+        row-parallel projections (out_proj, o_proj, down_proj with the residual add) run as split-K
+        clusters, or stream-K (q38_fp8_gemm_streamk) with `streamk=True`."""
         if kv_cache_format not in ("bf16", "fp8"):
             raise ValueError(f"kv_cache_format must be bf16 or fp8, not {kv_cache_format!r}")
         self.kv_fp8 = kv_cache_format == "fp8"
@@ -101,6 +104,7 @@ class B200Step:
         self.device = torch.device(device or f"cuda:{torch.cuda.current_device()}")
         self.group = process_group
         self.use_graph = use_graph
+        self.streamk = streamk
         self.saved = saved_states
         self.verify_tokens = verify_tokens
         get = layer_weights if callable(layer_weights) else (lambda i: layer_weights)
@@ -228,6 +232,11 @@ class B200Step:
         a.ab_splits = ops.bf16_linear_splits(rows, hv2, H)
         a.ab_workspace = z(max(ops.gemm_workspace_bytes(rows, hv2, a.ab_splits), 256), dt=torch.uint8)
         a.workspace = z(max(need, 256), dt=torch.uint8)
+        a.sk_workspace = None
+        if tp == 1 and self.streamk:
+            rowpar = [lin for l in self.layers for lin in (l.mixer.out if l.kind == LINEAR else l.mixer.o, l.down)]
+            a.sk_workspace = z(max(ops.streamk_workspace_bytes(rows, lin.out_features, lin.in_features) for lin in rowpar),
+                               dt=torch.uint8)
 
     # ------------------------------------------------------------------ kernels of one decode step
     def _gemm(self, a, x_q, lin: ops.DeviceLinear, y, residual=None):
@@ -236,7 +245,10 @@ class B200Step:
     def _row_parallel(self, a, x_q, lin: ops.DeviceLinear):
         """x += all_reduce(bf16(x_q @ W^T)) (the reference's `x + all_reduce(proj(...))`)."""
         if self.tp == 1:
-            self._gemm(a, x_q, lin, a.x, residual=a.x)
+            if a.sk_workspace is not None:
+                ops.fp8_gemm_streamk(x_q, lin, a.x, a.sk_workspace, residual=a.x)
+            else:
+                self._gemm(a, x_q, lin, a.x, residual=a.x)
             return
         if self.comm is not None:
             ops.fp8_gemm_allreduce(x_q, lin, self.comm, splits=a.splits.get(id(lin), 1))

@@ -59,6 +59,26 @@ def test_static_scratch_gemm_checks_arguments_before_any_device_call(pkg):
     assert status == -1 and "scratch" in lib_mod.last_error()
 
 
+def test_streamk_gemm_checks_arguments_on_the_host(pkg):
+    """q38_fp8_gemm_streamk refuses bad sizes, null pointers and a missing residual before any device call,
+    and its workspace query answers 0 for a bad shape."""
+    import ctypes
+
+    lib_mod = __import__(pkg.__name__ + "._lib", fromlist=["_lib"])
+    lib = lib_mod.load()
+    dummy = ctypes.c_void_p(16)
+    for tokens, features in ((0, 1024), (64, -128)):
+        status = lib.q38_fp8_gemm_streamk(dummy, tokens, 4096, dummy, dummy, features, 0, dummy, 1024, None, 0, dummy,
+                                          1 << 20, None)
+        assert status == -1 and "bad sizes" in lib_mod.last_error(), (tokens, features, lib_mod.last_error())
+    assert lib.q38_fp8_gemm_streamk(dummy, 64, 4096, dummy, dummy, 1024, 0, None, 1024, None, 0, dummy, 1 << 20, None) == -1
+    assert "null pointer" in lib_mod.last_error()
+    assert lib.q38_fp8_gemm_streamk(dummy, 64, 4096, dummy, dummy, 1024, 1, dummy, 1024, None, 0, dummy, 1 << 20, None) == -1
+    assert "residual" in lib_mod.last_error()
+    assert lib.q38_fp8_gemm_streamk_workspace_bytes(0, 5120, 17408) == 0
+    assert lib.q38_fp8_gemm_streamk_workspace_bytes(256, 5120, -1) == 0
+
+
 def test_copy_state_rows_checks_rows_on_the_host(pkg):
     """Rows outside a buffer, null buffers and empty rows are refused before any CUDA call."""
     import ctypes

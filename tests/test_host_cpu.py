@@ -43,7 +43,7 @@ def test_decode_step_bytes_counts_weights_state_and_cache():
     head = SimpleNamespace(lm_head=lin(320, 32))
     positions = torch.tensor([[3, 600], [4, 20]], dtype=torch.int32)  # two steps; 600 counts as MAX_SEQ (512)
     fp8 = lambda o, i: o * i * 33 // 32  # noqa: E731
-    want = 320 * 32 * 2                                                    # BF16 lm_head
+    want = fp8(320, 32)                                                    # lm_head at its FP8 size
     want += 2 * (fp8(64, 32) + fp8(32, 32))                                # MLPs
     want += fp8(96, 32) + fp8(32, 64) + 4 * 32 * 2                         # GDN projections, BF16 in_proj_b/a
     want += (2 * 4 * 8 * 8 + 2 * 10 * 3) * 2 * 2                           # state and conv state in and out

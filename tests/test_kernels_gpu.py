@@ -129,6 +129,61 @@ def test_fp8_gemm_matches_float64(pkg, ops, tokens, k, features, splits):
         assert torch.equal(y, y2), "split-K result must not depend on which CTA finishes last"
 
 
+STREAMK_CASES = [
+    # tokens, k, features, residual
+    (256, 17408, 5120, True),  # down_proj at TP = 1: every tile split between ~4 CTA pairs
+    (256, 6144, 5120, True),  # out_proj / o_proj
+    (64, 17408, 5120, False),  # 128-token tiles, one CTA per SM
+    (8, 6144, 5120, True),
+    (200, 3072, 1024, False),
+    (512, 8704, 5120, True),  # two token tiles
+    (37, 512, 384, True),  # fewer K steps than CTAs: some tiles whole
+    (300, 640, 520, False),  # ragged features and tokens
+]
+
+
+@pytest.mark.parametrize("tokens,k,features,residual", STREAMK_CASES)
+def test_fp8_gemm_streamk_matches_float64(pkg, ops, tokens, k, features, residual):
+    """q38_fp8_gemm_streamk: within the GEMM tolerance of the float64 product; with the residual epilogue
+    within 1 bf16 ulp of the split-K form's; the same bits on a second call (the last-arriver sum is in K
+    order, and the counters are back at zero)."""
+    gen = torch.Generator().manual_seed(tokens * 5 + k + features)
+    w = scaled_weight(pkg, features, k, gen)
+    x = torch.randn(tokens, k, generator=gen).to(torch.bfloat16)
+    xq = pkg.codec.to_e5m2_bytes(x).to(DEV)
+    lin = ops.DeviceLinear(w, DEV)
+    res = (torch.randn(tokens, features, generator=gen) * 4).to(torch.bfloat16).to(DEV) if residual else None
+    ws = torch.zeros(ops.streamk_workspace_bytes(tokens, features, k), dtype=torch.uint8, device=DEV)
+    y = torch.full((tokens, features), float("nan"), dtype=torch.bfloat16, device=DEV)
+    ops.fp8_gemm_streamk(xq, lin, y, ws, residual=res)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    xf, wf = pkg.codec.e5m2_bytes_to_float(xq.cpu()).double().to(DEV), w.dequant().double().to(DEV)
+    exact = xf @ wf.T
+    magnitude = xf.abs() @ wf.abs().T
+    if residual:
+        # bf16(residual + bf16(acc)) against the split-K form's residual epilogue on the same inputs: the
+        # fp32 sums run in another order, so the two accumulators differ by up to twice the fp32 rounding
+        # of the running sum (2^-19 of sum |x w| each, as assert_gemm_close allows) and bf16(acc) by up to
+        # one more ulp; the sum with the residual then adds one ulp of the result.
+        splits = ops.choose_splits(tokens, features, k)
+        wsk = torch.zeros(max(256, ops.gemm_workspace_bytes(tokens, features, splits)), dtype=torch.uint8, device=DEV)
+        ref = res.clone()
+        ops.fp8_gemm(xq, lin, ref, residual=ref, splits=splits, workspace=wsk)
+        torch.cuda.synchronize()
+        got, want = y.double().cpu(), ref.double().cpu()
+        diff = (got - want).abs()
+        bound = bf16_ulp(want).double() + bf16_ulp(exact.cpu()).double() + 2 * magnitude.cpu() * 2.0**-19
+        assert torch.isfinite(got).all() and (diff <= bound * 1.01).all(), f"streamk {tokens}x{k}x{features} + residual"
+        assert (diff > 0).float().mean().item() <= 0.02, f"streamk {tokens}x{k}x{features}: too many elements differ"
+    else:
+        assert_gemm_close(y, exact, magnitude, what=f"streamk {tokens}x{k}x{features}")
+    y2 = torch.empty_like(y)
+    ops.fp8_gemm_streamk(xq, lin, y2, ws, residual=res)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y2), "stream-K result must not depend on which CTA finishes a tile last"
+
+
 def test_fp8_gemm_residual_epilogue_and_oracle_linear(pkg, ops):
     gen = torch.Generator().manual_seed(3)
     tokens, k, features = 37, 512, 384
