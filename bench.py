@@ -65,30 +65,64 @@ def dist_env():
 
 
 class ClockSampler:
-    """nvidia-smi samples during the timed region (clocks and throttle reasons)."""
+    """nvidia-smi samples during the timed region (clocks and throttle reasons). The sampler starts
+    before the region and is waited for until its first sample arrives (nvidia-smi takes a few hundred
+    ms to start); samples are read by a thread with their arrival time, and those that arrive between
+    `begin()` and `end()` (plus one sampling interval) are the region's."""
 
     FIELDS = "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    INTERVAL_MS = 20
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.lines = []
+        self.t0 = self.t1 = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.monotonic(), line))
 
     def start(self):
+        import threading
+
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", str(self.INTERVAL_MS)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+        deadline = time.monotonic() + 10.0
+        while not self.lines and time.monotonic() < deadline and self.proc.poll() is None:
+            time.sleep(0.01)
+
+    def begin(self):
+        self.t0 = time.monotonic()
+
+    def end(self):
+        self.t1 = time.monotonic()
 
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(2 * self.INTERVAL_MS / 1e3)  # the region's last sample arrives after it is taken
         self.proc.terminate()
-        out, _ = self.proc.communicate(timeout=10)
+        try:
+            self.proc.wait(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.reader.join(timeout=10)
+        t0 = self.t0 if self.t0 is not None else float("-inf")
+        t1 = (self.t1 if self.t1 is not None else float("inf")) + 2 * self.INTERVAL_MS / 1e3
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in out.strip().splitlines():
+        for when, line in self.lines:
+            if not t0 <= when <= t1:
+                continue
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -190,11 +224,13 @@ def run_ours(args, world, rank, local):
         torch.distributed.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler.begin()
     start.record()
     for s in range(args.warmup, total):
         device_step(s)
     end.record()
     torch.cuda.synchronize()
+    sampler.end()
     if world > 1:
         torch.distributed.barrier()
     dev_ms = max_over_ranks(start.elapsed_time(end), world, device)
