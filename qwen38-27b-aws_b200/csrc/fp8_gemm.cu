@@ -20,9 +20,16 @@
 // (exact dequantisation: the reference's weights are e4m3 * 2^s), B = e5m2 activations with scale
 // 1.0. BF16 path (in_proj_b/a): kind::f16 with BF16 A and B. The lm_head has its own kernel (lm_head.cu).
 //
-// Split K: with splits > 1 each CTA stores its fp32 partial tile in the workspace; the last CTA of
-// a tile (by an atomic counter) sums the partials in split order 0..S-1, so results do not depend
-// on which CTA finishes last, then resets the counter.
+// Split K: up to 8 K splits of a tile form one thread-block cluster; each split sends the 32-token
+// blocks of its fp32 partial that other splits own to them by bulk shared-memory copies, and each
+// owner sums its blocks in split order 0..S-1 (the own partial straight from TMEM) and applies the
+// epilogue. With more splits (or an output that cannot be tensor-mapped) each CTA stores its partial
+// in a workspace and the last CTA of a tile (by an atomic counter) sums them in split order, then
+// resets the counter. Either way results do not depend on which CTA finishes last.
+//
+// Epilogues: bf16, bf16 + residual, SiLU(gate) * up to e5m2 (persistent kernel), and the fused
+// tensor-parallel all-reduce (EPI_ALLREDUCE: rows to their owner ranks over NVLink, see below). The
+// persistent kernel also runs stream-K (q38_fp8_gemm_streamk).
 #include <algorithm>
 #include <cmath>
 #include <cstdio>

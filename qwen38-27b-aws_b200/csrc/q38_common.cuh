@@ -120,8 +120,8 @@ __device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_
 }
 __device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
-// Thread-block clusters: rank, barrier over every thread of every CTA, and loads from a peer CTA's
-// shared memory (distributed shared memory).
+// Thread-block clusters: rank, barrier over every thread of every CTA, a peer CTA's shared-memory
+// address, and bulk copies into a peer CTA's shared memory (distributed shared memory).
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
