@@ -600,6 +600,34 @@ def run_micro(args):
                             head_dim=hd, rot_dim=cfg.rotary_dim, eps=1e-6, row_order=order)
         per = int(pos.sum().item()) * kvh * hd * 2 * 2 + B * qkv.shape[1] * 2 + B * heads * hd + B * kvh * hd * 2 * 2
         unit, bound = "GB/s", "hbm"
+    elif args.micro == "attn_long":
+        # BASELINE config 4's attention decode (or K-token verify): 4 rows (--batch) at positions U[30000, 32000) of a
+        # 32,768-position cache (the long-context agent workload), one layer at TP = --tp head counts,
+        # split along the cache (q38_attn_split); --kv fp8 reads the FP8 e4m3 cache. Bytes: the K and V
+        # rows below each position, plus the row's inputs and outputs.
+        B = args.batch if args.batch_given else 4
+        max_seq = 32768
+        heads, kvh, hd = cfg.num_attention_heads // args.tp, cfg.kv_heads_per_rank(args.tp), cfg.head_dim
+        fp8 = args.kv == "fp8"
+        mk = (lambda: bf(B, kvh, max_seq, hd).float().to(torch.float8_e4m3fn).view(torch.uint8)) if fp8 else (
+            lambda: bf(B, kvh, max_seq, hd))
+        caches = [(mk(), mk()) for _ in range(args.copies)]
+        K = args.verify_tokens
+        qkv = bf(B * K, heads * 2 * hd + 2 * kvh * hd)
+        qn, kn = bf(hd) * 0.1, bf(hd) * 0.1
+        pos = torch.randint(30000, 32000, (B,), device=dev, dtype=torch.int32, generator=gen)
+        cs, sn = bf(B * K, cfg.rotary_dim), bf(B * K, cfg.rotary_dim)
+        act = torch.ones(B, device=dev)
+        out = torch.empty(B * K, heads * hd, dtype=torch.uint8, device=dev)
+        ws = torch.empty(ops.attn_split_workspace_bytes(B, heads, kvh, K, max_seq, hd), dtype=torch.uint8, device=dev)
+        scales = (2.0 ** -4, 2.0 ** -5) if fp8 else None
+
+        def launch(i):
+            kc, vc = caches[i % len(caches)]
+            ops.attn_split(qkv, qn, kn, cs, sn, kc, vc, pos, act, out, batch=B, tokens=K, num_q_heads=heads,
+                           num_kv_heads=kvh, head_dim=hd, rot_dim=cfg.rotary_dim, eps=1e-6, kv_scales=scales, workspace=ws)
+        per = int(pos.sum().item()) * kvh * hd * (1 if fp8 else 2) * 2 + B * K * (qkv.shape[1] * 2 + heads * hd)
+        unit, bound = "GB/s", "hbm"
     elif args.micro == "gemm":
         k, n = cfg.intermediate_size // args.tp, cfg.hidden_size
         if args.shape:
@@ -851,7 +879,9 @@ def run_micro_allreduce(args, world, rank, local):
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
-    ap.add_argument("--micro", choices=["gdn", "gemm", "gemm_silu", "head", "attn", "ab", "gdn_prefill", "attn_prefill", "verify", "gemm_ar"],
+    ap.add_argument("--kv", choices=["bf16", "fp8"], default="bf16", help="--micro attn_long: the KV cache format")
+    ap.add_argument("--verify-tokens", type=int, default=1, help="--micro attn_long: query tokens per row (4: verify)")
+    ap.add_argument("--micro", choices=["gdn", "gemm", "gemm_silu", "head", "attn", "attn_long", "ab", "gdn_prefill", "attn_prefill", "verify", "gemm_ar"],
                     help="time one kernel alone (profiling) instead of the step; gemm_ar: the fused all-reduce under torchrun")
     ap.add_argument("--copies", type=int, default=4, help="--micro: distinct weight/state copies cycled (defeat L2)")
     ap.add_argument("--tp", type=int, default=1, help="--micro gemm: K = 17408 / tp")
