@@ -34,6 +34,8 @@ constexpr int kStages = 4;                     // tiles in flight per CTA
 constexpr int kMaxRows = 32;                   // query rows per (row, KV head): groups x tokens
 constexpr int kMaxTokens = 8;                  // verify tokens
 constexpr int kMaxChunk = 512;                 // cache positions per chunk
+constexpr int kFinishThreads = 512;            // threads of a finishing CTA
+constexpr int kFinishSlices = 4;               // finishing CTAs per (row, KV head)
 
 __host__ __device__ constexpr size_t al16(size_t x) { return (x + 15) & ~size_t(15); }
 
@@ -127,7 +129,8 @@ template <int HD, bool FP8>
 struct Layout {
   size_t ring, work, q, qf, prm, sc, kown, bars, total;
   int rowp, scw;
-  __host__ __device__ Layout(int rows, int tokens, int chunk, int rot) {
+  // mrows: the query rows the MMA tiles cover (16 x MT), which the query and score buffers hold.
+  __host__ __device__ Layout(int rows, int tokens, int chunk, int rot, int mrows) {
     rowp = HD + 8;
     scw = chunk + 8;
     size_t off = 0;
@@ -138,10 +141,10 @@ struct Layout {
     };
     ring = take(static_cast<size_t>(kStages) * (FP8 ? Geom<HD>::kRawBytes : Geom<HD>::kTileBytes));
     work = FP8 ? take(2 * static_cast<size_t>(Geom<HD>::kTileBytes)) : 0;  // decoded tiles (double buffered)
-    q = take(static_cast<size_t>(kMaxRows) * rowp * 2);                  // queries bf16 (scores kernel)
+    q = take(static_cast<size_t>(mrows) * rowp * 2);                     // queries bf16 (scores kernel)
     qf = take(static_cast<size_t>(rows) * HD * 4);                        // query staging fp32
     prm = take(static_cast<size_t>(2) * HD * 2 + static_cast<size_t>(2) * tokens * (rot > 0 ? rot : 1) * 2);
-    sc = take(static_cast<size_t>(kMaxRows) * scw * 2);                   // scores / weights bf16
+    sc = take(static_cast<size_t>(mrows) * scw * 2);                      // scores / weights bf16
     kown = take(static_cast<size_t>(tokens) * HD * 4);                    // own keys fp32
     bars = take(2 * kStages * 8);
     total = off + 1024;
@@ -213,7 +216,7 @@ __device__ __forceinline__ uint32_t tile_for(uint8_t* ring, uint8_t* work, uint6
 // Queries of the pair's rows (r = t * groups + h) normed and rotated into `qs` (bf16, rows past `rows`
 // zero), with the fp32 copies in `qf`; with `keys`, the step's own keys too (as the cache holds them).
 template <int HD, bool FP8>
-__device__ void stage_queries(const SplitArgs& a, const Pair& p, __nv_bfloat16* qs, int rowp, float* qf,
+__device__ void stage_queries(const SplitArgs& a, const Pair& p, __nv_bfloat16* qs, int rowp, int mrows, float* qf,
                               __nv_bfloat16* prm, float* kown, bool keys, int tid, int warp, int lane) {
   const int G = a.groups, K = a.tokens, rot = a.rot > 0 ? a.rot : 1;
   __nv_bfloat16* wq = prm;
@@ -254,7 +257,7 @@ __device__ void stage_queries(const SplitArgs& a, const Pair& p, __nv_bfloat16* 
     }
   }
   compute_bar();
-  for (int i = tid; i < kMaxRows * HD; i += kWarps * 32) {
+  for (int i = tid; i < mrows * HD; i += kWarps * 32) {
     const int r = i / HD, d = i % HD;
     qs[r * rowp + d] = __float2bfloat16_rn(r < a.rows ? qf[i] : 0.f);
   }
@@ -268,7 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1) split_scores_kernel(const __grid_
   constexpr int KSTEPS = HD / 16;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Layout<HD, FP8> L(a.rows, a.tokens, a.chunk, a.rot);
+  const Layout<HD, FP8> L(a.rows, a.tokens, a.chunk, a.rot, MT * 16);
   uint8_t* ring = smem + L.ring;
   uint8_t* work = smem + L.work;
   __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(smem + L.q);
@@ -301,7 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1) split_scores_kernel(const __grid_
     if (lane == 0 && p0 < p1) copy_tiles<HD, FP8>(&tmap_k, a.k_cache, row0, p0, p1, ring, full, empty);
     return;
   }
-  stage_queries<HD, FP8>(a, p, qs, L.rowp, qf, prm, kown, c == 0, tid, warp, lane);
+  stage_queries<HD, FP8>(a, p, qs, L.rowp, MT * 16, qf, prm, kown, c == 0, tid, warp, lane);
   if (c == 0) {
     // Own-key scores: bf16(q . k_own) for the visible own keys (token t sees own tokens 0 .. t).
     for (int i = warp; i < a.rows * a.tokens; i += kWarps) {
@@ -383,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1) split_values_kernel(const __grid_
   constexpr int NT2 = HD / 8 / kWarps;  // 8-dim output tiles per warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Layout<HD, FP8> L(a.rows, a.tokens, a.chunk, a.rot);
+  const Layout<HD, FP8> L(a.rows, a.tokens, a.chunk, a.rot, MT * 16);
   uint8_t* ring = smem + L.ring;
   uint8_t* work = smem + L.work;
   __nv_bfloat16* wt = reinterpret_cast<__nv_bfloat16*>(smem + L.sc);
@@ -424,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1) split_values_kernel(const __grid_
   compute_bar();
   // bf16 weights of the chunk's positions; rows past `rows` and positions past p1 are zero.
   const int n = p1 - p0, ntiles = (n + KT - 1) / KT;
-  for (int i = tid; i < kMaxRows * ntiles * KT; i += kWarps * 32) {
+  for (int i = tid; i < MT * 16 * ntiles * KT; i += kWarps * 32) {
     const int r = i / (ntiles * KT), q = i % (ntiles * KT);
     float w = 0.f;
     if (r < a.rows && q < n) {
@@ -493,8 +496,12 @@ __global__ void __launch_bounds__(kThreads, 1) split_values_kernel(const __grid_
 }
 
 // ---- launch 3: the output rows and the cache writes ----------------------------------------------
+// One CTA of kFinishThreads per (row, KV head, slice of the rows x HD outputs): the softmax statistics
+// and the step's own keys and values are recomputed by every slice (a few hundred values), the
+// chunks' partial sums are read for the slice's outputs only, eight chunks' loads in flight at a time
+// and added in chunk order; slice 0 writes the step's keys and values into the cache.
 template <int HD, bool FP8>
-__global__ void __launch_bounds__(kWarps * 32) split_finish_kernel(SplitArgs a) {
+__global__ void __launch_bounds__(kFinishThreads) split_finish_kernel(SplitArgs a) {
   extern __shared__ uint8_t smem_raw[];
   float* rs = reinterpret_cast<float*>(smem_raw);   // [rows][2]
   float* wown = rs + 2 * kMaxRows;                  // [rows][tokens] own weights (bf16 values)
@@ -506,10 +513,11 @@ __global__ void __launch_bounds__(kWarps * 32) split_finish_kernel(SplitArgs a) 
   pdl_trigger();
   const Pair p = pair_of(a, blockIdx.x, blockIdx.y);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int NT = kFinishThreads, NW = kFinishThreads / 32;
   const int K = a.tokens, G = a.groups, rot = a.rot > 0 ? a.rot : 1;
   const int live = (p.n_read + a.chunk - 1) / a.chunk;
   const float scale = static_cast<float>(1.0 / sqrt(static_cast<double>(HD)));
-  for (int r = warp; r < a.rows; r += kWarps) {
+  for (int r = warp; r < a.rows; r += NW) {
     float m, s;
     row_stats(a, p.pair, r, live, scale, lane, m, s);
     if (lane < K) {
@@ -521,13 +529,13 @@ __global__ void __launch_bounds__(kWarps * 32) split_finish_kernel(SplitArgs a) 
   __nv_bfloat16* wk = prm;
   __nv_bfloat16* cs = wk + HD;
   __nv_bfloat16* sn = cs + K * rot;
-  for (int i = tid; i < HD; i += kWarps * 32) wk[i] = a.k_norm_w[i];
-  for (int i = tid; i < K * a.rot; i += kWarps * 32) {
+  for (int i = tid; i < HD; i += NT) wk[i] = a.k_norm_w[i];
+  for (int i = tid; i < K * a.rot; i += NT) {
     const int t = i / a.rot, d = i % a.rot;
     cs[t * rot + d] = a.cos[(static_cast<int64_t>(p.b) * K + t) * a.rot + d];
     sn[t * rot + d] = a.sin[(static_cast<int64_t>(p.b) * K + t) * a.rot + d];
   }
-  for (int i = tid; i < K * HD; i += kWarps * 32) {
+  for (int i = tid; i < K * HD; i += NT) {
     const int t = i / HD, d = i % HD;
     const __nv_bfloat16* row = a.qkv + (static_cast<int64_t>(p.b) * K + t) * a.ld_qkv +
                                static_cast<int64_t>(a.num_q_heads) * 2 * HD + static_cast<int64_t>(p.g) * HD + d;
@@ -536,15 +544,27 @@ __global__ void __launch_bounds__(kWarps * 32) split_finish_kernel(SplitArgs a) 
     vown[i] = FP8 ? fp8_load(fp8_store(v, a.v_scale), a.v_scale) : v;
   }
   __syncthreads();
-  for (int t = warp; t < K; t += kWarps) norm_rope_head<HD>(kown + t * HD, wk, cs + t * rot, sn + t * rot, a.rot, a.eps, lane);
+  for (int t = warp; t < K; t += NW) norm_rope_head<HD>(kown + t * HD, wk, cs + t * rot, sn + t * rot, a.rot, a.eps, lane);
   __syncthreads();
 
   // out = bf16(bf16(sum over chunks of W V) + bf16(W_own V_own)) * bf16(sigmoid(gate)), to e5m2.
   const float* part = a.part + (static_cast<int64_t>(p.pair) * a.nchunks) * a.rows * HD;
-  for (int i = tid; i < a.rows * HD; i += kWarps * 32) {
+  const int64_t cstride = static_cast<int64_t>(a.rows) * HD;
+  const int n_out = a.rows * HD;
+  const int lo = static_cast<int>(static_cast<int64_t>(blockIdx.z) * n_out / gridDim.z);
+  const int hi = static_cast<int>(static_cast<int64_t>(blockIdx.z + 1) * n_out / gridDim.z);
+  for (int i = lo + tid; i < hi; i += NT) {
     const int r = i / HD, d = i % HD, t = r / G, h = r % G;
     float cache_part = 0.f;
-    for (int c = 0; c < live; ++c) cache_part += part[static_cast<int64_t>(c) * a.rows * HD + i];
+    int c = 0;
+    for (; c + 8 <= live; c += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = part[(c + u) * cstride + i];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) cache_part += v[u];
+    }
+    for (; c < live; ++c) cache_part += part[c * cstride + i];
     float own_part = 0.f;
     for (int t2 = 0; t2 < K; ++t2) own_part = __fmaf_rn(wown[r * kMaxTokens + t2], vown[t2 * HD + d], own_part);
     const float o = bf16r(__fadd_rn(bf16r(cache_part), bf16r(own_part)));
@@ -554,7 +574,8 @@ __global__ void __launch_bounds__(kWarps * 32) split_finish_kernel(SplitArgs a) 
     a.out[qrow * a.ld_out + static_cast<int64_t>(qh) * HD + d] = f32_to_e5m2(bf16r(__fmul_rn(o, bf16r(sigmoidf_(gv)))));
   }
   // The step's keys and values into the cache: every read of it this step is in the earlier launches.
-  for (int i = tid; i < K * HD; i += kWarps * 32) {
+  if (blockIdx.z != 0) return;
+  for (int i = tid; i < K * HD; i += NT) {
     const int t = i / HD, d = i % HD;
     const int64_t at = (static_cast<int64_t>(p.pair) * a.max_seq + write_position(a, p, t)) * HD + d;
     const float k = kown[i];
@@ -613,7 +634,7 @@ int launch_split(SplitArgs a, int64_t batch, cudaStream_t stream) {
     if (st == Q38_OK) st = q38host::encode_tmap_2d(&tv, a.v_cache, cache_rows, HD, 2, KT, T::kBoxCols, T::kSwizzle);
     if (st != Q38_OK) return st;
   }
-  const size_t smem = Layout<HD, FP8>(a.rows, a.tokens, a.chunk, a.rot).total;
+  const size_t smem = Layout<HD, FP8>(a.rows, a.tokens, a.chunk, a.rot, MT * 16).total;
   cudaError_t e = cudaFuncSetAttribute(split_scores_kernel<HD, MT, FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e == cudaSuccess)
@@ -626,8 +647,8 @@ int launch_split(SplitArgs a, int64_t batch, cudaStream_t stream) {
   const size_t fsmem = (2 * kMaxRows + kMaxRows * kMaxTokens + 2 * kMaxTokens * HD) * 4 +
                        (HD + 2 * kMaxTokens * (a.rot > 0 ? a.rot : 1)) * 2;
   if (e == cudaSuccess)
-    e = q38host::launch_pdl(split_finish_kernel<HD, FP8>, dim3(a.num_kv_heads, static_cast<unsigned>(batch)),
-                            dim3(kWarps * 32), fsmem, stream, a);
+    e = q38host::launch_pdl(split_finish_kernel<HD, FP8>, dim3(a.num_kv_heads, static_cast<unsigned>(batch), kFinishSlices),
+                            dim3(kFinishThreads), fsmem, stream, a);
   return q38host::cuda_status(e != cudaSuccess ? e : cudaGetLastError(), "attn_split launch");
 }
 
