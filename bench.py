@@ -409,27 +409,38 @@ def decode_step_bytes(step, head, linear_kind: str, positions: torch.Tensor) -> 
 
 
 def time_gdn_launches(step, ops, pkg, repeats: int) -> float:
-    """Average duration of the step's gdn_decode launches, each bracketed by CUDA events on the
-    launching stream, replayed eagerly over the 48 layers' own states right after the timed region."""
+    """Average duration of one layer's gated-delta decode (its q/k prep + decode launches) right after the
+    timed region: the 48 layers' launches over their own states, captured as one CUDA graph as in the
+    step (no host launch gaps between them), replayed `repeats` times between CUDA events on the
+    launching stream."""
     cfg, tp = step.cfg, step.tp
-    durations = []
     stream = torch.cuda.current_stream()
-    for _ in range(repeats):
-        for l in step.layers:
-            if l.kind != pkg.config.LINEAR:
-                continue
+    layers = [l for l in step.layers if l.kind == pkg.config.LINEAR]
+
+    def run():
+        for l in layers:
             m = l.mixer
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
             ops.gdn_decode(step.proj, step.ab, m.conv_state, m.conv_w, m.a_log, m.dt_bias, m.norm_w, m.state,
                            step.position, step.active, step.mix_gdn, batch=step.batch,
                            num_k_heads=cfg.linear_num_key_heads // tp, num_v_heads=cfg.linear_num_value_heads // tp,
-                           head_k=cfg.linear_key_head_dim, head_v=cfg.linear_value_head_dim, eps=cfg.rms_norm_eps)
-            b.record(stream)
-            durations.append((a, b))
+                           head_k=cfg.linear_key_head_dim, head_v=cfg.linear_value_head_dim, eps=cfg.rms_norm_eps,
+                           workspace=step.gdn_workspace)
+
+    run()  # outside capture first (module loading, attributes)
     torch.cuda.synchronize()
-    times = [a.elapsed_time(b) for a, b in durations]
-    return sum(times) / len(times)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run()
+    graph.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(repeats):
+        graph.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    del graph
+    return a.elapsed_time(b) / (repeats * len(layers))
 
 
 def rotary(cfg, positions):
